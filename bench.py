@@ -1,0 +1,451 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 sparse-MoE layer (BASELINE config 2 at N=1).
+
+Workload: one Qwen3-30B-A3B-shaped MoE layer (hidden 2048, 128 experts,
+top-8 renormalised, intermediate 768, SwiGLU, int4 group-64 experts, bf16
+activations N(0,1), router weight N(0, 0.02^2), seed 1), decode batch of
+``--tokens`` tokens (default 64) per GPU. A step is one layer forward. Eight
+distinct layers' weights (seeds 1..8, 2.6 GB) are cycled step by step, so
+every step streams its experts from HBM (the working set is ~20x the 126 MB
+L2); no explicit flush is needed.
+
+* ``value``: tokens/s over K steps replayed from CUDA graphs, inputs resident
+  in HBM, timed with CUDA events; max over ranks for N > 1.
+* ``e2e``: the same through the public API ``phantom_moe.moe_layer`` per
+  step, with the step's activations copied host->device from pinned memory
+  and the output copied back and synchronised, timed with CUDA events.
+* ``roofline``: the dominant kernel (FFN gate/up) timed by CUDA events the
+  library records between its stages; algorithmic bytes = packed int4
+  weights + fp16 scales of every expert hit + activations in + h out.
+* ``cpu_baseline``: transformers' Qwen3MoeSparseMoeBlock (the MoE code
+  PHANTOM runs) in fp32 on the host cores, same layer and batch.
+
+With N > 1 (torchrun), experts are sharded expert-parallel (128/N per
+rank), each rank routes its own ``--tokens`` tokens, and dispatch/combine
+are NCCL all-to-alls (weak scaling).
+
+``--impl reference`` times the reference's CPU path alone (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "solution-is-all-you-need_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+H, E, K_TOP, I, G = 2048, 128, 8, 768, 64
+SWEEP = (1, 4, 16, 64, 256)
+METRIC = "MoE-layer tokens/s (Qwen3-30B-A3B-shaped layer, int4 g64, bf16 decode)"
+EXPERT_BYTES = (2 * I * H // 2 + 2 * I * (H // G) * 2) + (H * I // 2 + H * (I // G) * 2)  # 2,506,752
+W13_BYTES = 2 * I * H // 2 + 2 * I * (H // G) * 2  # 1,671,168 per expert
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def dist_info():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------------------
+# weights
+# ---------------------------------------------------------------------------
+
+def make_layer(seed: int, device, expert_range=None):
+    """Router weight (bf16 [E, H]) and packed experts of one layer, drawn
+    N(0, 0.02^2) from ``seed``. ``expert_range`` keeps only those experts
+    (expert-parallel shard); the full draw is made so shards agree."""
+    import phantom_moe as pm
+    g = torch.Generator(device=device).manual_seed(seed)
+    wr = (torch.randn(E, H, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    w13 = torch.randn(E, 2 * I, H, device=device, generator=g) * 0.02
+    lo, hi = expert_range if expert_range else (0, E)
+    p13 = pm.quantize_int4(w13[lo:hi].contiguous(), G)
+    del w13
+    w2 = torch.randn(E, H, I, device=device, generator=g) * 0.02
+    p2 = pm.quantize_int4(w2[lo:hi].contiguous(), G)
+    del w2
+    return wr, pm.PackedExperts(p13[0], p13[1], p2[0], p2[1], G)
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"phmoe_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = [r.split(", ") for r in self.path.read_text().strip().splitlines() if r.count(",") >= 8]
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        loaded = sorted(sm)[len(sm) // 2:] if sm else []
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons, "samples": len(rows),
+                "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()), default=None)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_single_gpu(args, device):
+    import phantom_moe as pm
+    from phantom_moe import _lib
+    lib = pm.load_library()
+    L = args.layers
+    t0 = time.time()
+    layers = [make_layer(1 + l, device) for l in range(L)]
+    torch.cuda.synchronize()
+    log(f"[bench] built {L} layers in {time.time() - t0:.1f}s")
+    stream = torch.cuda.Stream(device)
+    results = {}
+    headline = None
+    Ts = sorted(set(SWEEP) | {args.tokens}) if args.sweep else [args.tokens]
+    for T in Ts:
+        g = torch.Generator(device=device).manual_seed(1000 + T)
+        xs = [torch.randn(T, H, device=device, generator=g).to(torch.bfloat16) for _ in range(L)]
+        outs = [torch.empty(T, H, device=device, dtype=torch.bfloat16) for _ in range(L)]
+        # unique experts hit per layer (algorithmic bytes)
+        U = []
+        for l in range(L):
+            _, idx, _ = pm.moe_layer(xs[l], layers[l][0], *_pk(layers[l][1]), K_TOP, return_routing=True)
+            U.append(int(torch.unique(idx).numel()))
+        torch.cuda.synchronize()
+        # capture one graph per layer
+        graphs = []
+        with torch.cuda.stream(stream):
+            for l in range(L):  # warm the workspace for this stream
+                pm.moe_layer(xs[l], layers[l][0], *_pk(layers[l][1]), K_TOP, out=outs[l])
+            stream.synchronize()
+            n0 = lib.phmoe_kernel_launch_count()
+            for l in range(L):
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=stream):
+                    pm.moe_layer(xs[l], layers[l][0], *_pk(layers[l][1]), K_TOP, out=outs[l])
+                graphs.append(gr)
+            launches_per_step = (lib.phmoe_kernel_launch_count() - n0) / L
+        K, W = args.steps, args.warmup
+        with torch.cuda.stream(stream):
+            for i in range(W):
+                graphs[i % L].replay()
+            stream.synchronize()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+            for i in range(K):
+                graphs[i % L].replay()
+            ev1.record(stream)
+            ev1.synchronize()
+        ms = ev0.elapsed_time(ev1) / K
+        # per-stage device time (eager calls queued behind a sleep so launch gaps do not count)
+        stage = profile_stages(pm, lib, layers, xs, outs, stream, n_calls=min(64, max(8, K)))
+        mean_u = float(np.mean(U))
+        R = T * K_TOP
+        gateup_bytes = mean_u * W13_BYTES + R * H * 2 + R * I * 4
+        ffn_bytes = mean_u * EXPERT_BYTES + R * H * 2 + 2 * R * I * 4 + R * H * 4
+        layer_bytes = mean_u * EXPERT_BYTES + E * H * 2 + 2 * T * H * 2
+        res = {"tokens": T, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
+               "unique_experts_mean": mean_u, "layer_GBps": layer_bytes / (ms / 1e3) / 1e9,
+               "stage_ms": stage, "gateup_GBps": gateup_bytes / (stage["ffn_gateup"] / 1e3) / 1e9,
+               "ffn_GBps": ffn_bytes / ((stage["ffn_gateup"] + stage["ffn_down"]) / 1e3) / 1e9,
+               "launches_per_step": launches_per_step}
+        results[T] = res
+        log(f"[bench] T={T:4d} {ms * 1e3:8.1f} us/step {res['tokens_per_s'] / 1e6:7.3f} Mtok/s "
+            f"layer {res['layer_GBps']:7.0f} GB/s gateup {res['gateup_GBps']:7.0f} GB/s U={mean_u:.1f} "
+            f"stages(us) " + " ".join(f"{k}={v * 1e3:.1f}" for k, v in stage.items()))
+        if T == args.tokens:
+            headline = dict(res, graphs=graphs, xs=xs, outs=outs, gateup_bytes=gateup_bytes)
+        else:
+            del graphs
+    return layers, results, headline
+
+
+def _pk(p):
+    return p.w13_q, p.w13_scales, p.w2_q, p.w2_scales
+
+
+def profile_stages(pm, lib, layers, xs, outs, stream, n_calls):
+    from phantom_moe import _lib
+    import ctypes
+    L = len(layers)
+    with torch.cuda.stream(stream):
+        _lib.call("phmoe_profile_begin", n_calls)
+        torch.cuda._sleep(50_000_000)  # ~25 ms: the CPU queues every call before the GPU starts
+        for i in range(n_calls):
+            l = i % L
+            pm.moe_layer(xs[l], layers[l][0], *_pk(layers[l][1]), K_TOP, out=outs[l])
+        arr = (ctypes.c_float * _lib.NUM_STAGES)()
+        n = ctypes.c_int(0)
+        _lib.call("phmoe_profile_end", arr, _lib.NUM_STAGES, ctypes.byref(n))
+    return {name: arr[i] / max(n.value, 1) for i, name in enumerate(_lib.STAGE_NAMES)}
+
+
+def e2e_single(args, device, layers, T):
+    """Public-API path with host<->device copies inside the timed region."""
+    import phantom_moe as pm
+    L = len(layers)
+    g = torch.Generator().manual_seed(2000 + T)
+    xh = [torch.randn(T, H, generator=g).to(torch.bfloat16).pin_memory() for _ in range(L)]
+    oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty(T, H, dtype=torch.bfloat16, device=device)
+    st = torch.cuda.current_stream(device)
+    for i in range(args.warmup):
+        xd.copy_(xh[i % L], non_blocking=True)
+        out = pm.moe_layer(xd, layers[i % L][0], *_pk(layers[i % L][1]), K_TOP)
+        oh.copy_(out, non_blocking=True)
+        st.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(st)
+    for i in range(args.steps):
+        xd.copy_(xh[i % L], non_blocking=True)
+        out = pm.moe_layer(xd, layers[i % L][0], *_pk(layers[i % L][1]), K_TOP)
+        oh.copy_(out, non_blocking=True)
+        st.synchronize()
+    ev1.record(st)
+    ev1.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    return {"value": T / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+            "d2h_bytes_per_step": T * H * 2, "ms_per_step": ms}
+
+
+def cpu_baseline(layers_host_fn, T, budget_s):
+    """transformers' Qwen3MoeSparseMoeBlock, fp32, all host threads."""
+    from oracle import tf_ref
+    threads = tf_ref.host_threads()
+    torch.set_num_threads(threads)
+    wr, w13_q, w13_s, w2_q, w2_s = layers_host_fn()
+    blk = tf_ref.build_block("qwen3", wr, w13_q, w13_s, w2_q, w2_s, K_TOP, G)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(3000 + T)).to(torch.bfloat16).float().numpy()
+    tf_ref.forward(blk, x)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        tf_ref.forward(blk, x)
+        n += 1
+        el = time.perf_counter() - t0
+        if (el >= budget_s and n >= 3) or n >= 1000:
+            break
+    return {"value": n * T / el, "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": f"transformers 5.5.0 Qwen3MoeSparseMoeBlock fp32 (eager experts loop), layer seed 1, "
+                      f"T={T}, {n} forwards in {el:.1f}s, torch threads={threads}, cpu={tf_ref.cpu_model()}"}
+
+
+def host_layer0():
+    """Layer-0 weights (seed 1) on the host, packed by the CUDA quantiser when
+    a GPU is present (identical bytes to the oracle's quantiser)."""
+    if torch.cuda.is_available():
+        wr, pk = make_layer(1, torch.device("cuda", torch.cuda.current_device()))
+        return (wr.float().cpu().numpy(), pk.w13_q.cpu().numpy(), pk.w13_scales.cpu().numpy(),
+                pk.w2_q.cpu().numpy(), pk.w2_scales.cpu().numpy())
+    from oracle import moe_oracle as O
+    g = torch.Generator().manual_seed(1)
+    wr = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
+    w13 = torch.randn(E, 2 * I, H, generator=g) * 0.02
+    parts13 = [O.quantize_int4(w13[e].numpy(), G) for e in range(E)]
+    del w13
+    w2 = torch.randn(E, H, I, generator=g) * 0.02
+    parts2 = [O.quantize_int4(w2[e].numpy(), G) for e in range(E)]
+    return (wr, np.stack([p for p, _ in parts13]), np.stack([s for _, s in parts13]),
+            np.stack([p for p, _ in parts2]), np.stack([s for _, s in parts2]))
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic(T):
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        v = d.get(f"ffn_gateup_T{T}")
+        if v is not None:
+            return float(v)
+    return None
+
+
+def run_ours(args):
+    ws, rank, local = dist_info()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if ws > 1:
+        return run_ep(args, ws, rank, device)
+    with ClockSampler(local) as clk:
+        layers, results, hl = run_single_gpu(args, device)
+        # sustained replay of the headline step while the sampler runs
+        t_end = time.time() + args.clock_soak
+        st = torch.cuda.current_stream(device)
+        while time.time() < t_end:
+            for i in range(200):
+                hl["graphs"][i % len(hl["graphs"])].replay()
+            st.synchronize()
+    clocks = clk.summary()
+    e2e = e2e_single(args, device, layers, args.tokens)
+    T = args.tokens
+    res = results[T]
+    peak, peak_kind = load_peaks()
+    achieved = hl["gateup_bytes"] / (res["stage_ms"]["ffn_gateup"] / 1e3) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        del layers, hl
+        torch.cuda.empty_cache()
+        cpu = cpu_baseline(host_layer0, T, args.cpu_budget)
+    line = {
+        "metric": METRIC, "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights, int4 g64)",
+        "config": {"workload": f"qwen3-30b-a3b moe layer decode T={T}", "hidden": H, "experts": E,
+                   "top_k": K_TOP, "intermediate": I, "group_size": G, "tokens_per_gpu": T,
+                   "global_batch": T, "parallelism": "single-gpu",
+                   "l2": f"inputs larger than L2: {args.layers} layers' weights cycled per step",
+                   "graph": "CUDA graph per layer", "sweep": {str(k): _sweep_entry(v) for k, v in results.items()}},
+        "roofline": {"kernel": "ffn_gateup", "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": load_traffic(T), "algorithmic_bytes_per_launch": hl["gateup_bytes"],
+                     "ffn_achieved": res["ffn_GBps"], "ffn_frac": res["ffn_GBps"] / peak},
+        "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+        "gpu_launches": int(round(res["launches_per_step"] * args.steps)),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _sweep_entry(v):
+    return {"tokens_per_s": round(v["tokens_per_s"], 1), "us_per_step": round(v["ms_per_step"] * 1e3, 2),
+            "layer_GBps": round(v["layer_GBps"], 1), "gateup_GBps": round(v["gateup_GBps"], 1),
+            "unique_experts": v["unique_experts_mean"],
+            "stage_us": {k: round(s * 1e3, 2) for k, s in v["stage_ms"].items()}}
+
+
+def run_ep(args, ws, rank, device):
+    import torch.distributed as dist
+    from phantom_moe import ep
+    res = ep.bench_ep(args, ws, rank, device, make_layer, ClockSampler, H=H, E=E, k=K_TOP, I=I, G=G)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+
+def run_reference(args):
+    ws, rank, local = dist_info()
+    if rank != 0:
+        return
+    from oracle import tf_ref
+    T = args.tokens
+    threads = tf_ref.host_threads()
+    torch.set_num_threads(threads)
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    wr, w13_q, w13_s, w2_q, w2_s = host_layer0()
+    blk = tf_ref.build_block("qwen3", wr, w13_q, w13_s, w2_q, w2_s, K_TOP, G)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(3000 + T)).to(torch.bfloat16).float().numpy()
+    for _ in range(max(1, args.warmup)):
+        tf_ref.forward(blk, x)
+    steps = max(1, args.steps)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        tf_ref.forward(blk, x)
+    el = time.perf_counter() - t0
+    v = steps * T / el
+    sample = (f"transformers 5.5.0 Qwen3MoeSparseMoeBlock fp32 on the host (the MoE code PHANTOM runs), "
+              f"T={T}, {steps} forwards, torch threads={threads}, cpu={tf_ref.cpu_model()}")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": ws,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": el / steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"qwen3-30b-a3b moe layer decode T={T}", "hidden": H, "experts": E,
+                   "top_k": K_TOP, "intermediate": I, "group_size": G, "tokens_per_gpu": T},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "reference", "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=64, help="decode tokens per GPU (headline)")
+    ap.add_argument("--layers", type=int, default=8, help="distinct layers cycled (L2 defeat)")
+    ap.add_argument("--no-sweep", dest="sweep", action="store_false")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
+    ap.add_argument("--clock-soak", type=float, default=2.0, help="seconds of sustained replay for clocks")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    ws, rank, local = dist_info()
+    if ws > 1 and args.impl == "ours":
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,174 @@
+/*
+ * phmoe.h - C ABI of the B200 (sm_100a) sparse-MoE layer.
+ *
+ * The reference (FreakyAdy/Solution-is-all-You-need, "PHANTOM") runs MoE
+ * layers through transformers' Qwen3MoeSparseMoeBlock / MixtralSparseMoeBlock
+ * (transformers 5.5.0 models/qwen3_moe/modeling_qwen3_moe.py:275-286, reached
+ * from python/phantom/phantom_cli.py:1393-1430). Its own native kernels use
+ * the convention `extern "C" float fn(device pointers, dims, cudaStream_t)`
+ * (kernels/sparse_moe/sparse_matmul.cu:240-254, gate_predict.cu:200-214).
+ * This ABI keeps that shape - raw device pointers, plain integer dims and a
+ * stream - with three changes: every entry returns a status code instead of
+ * calling exit() (kernels/common/cuda_utils.h:31-52); scratch memory is a
+ * caller-provided workspace instead of cudaMalloc per call
+ * (sparse_matmul.cu:264-273); and nothing synchronises the stream.
+ *
+ * All pointers are device pointers unless stated. `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream). Entries are
+ * reentrant as long as concurrent calls use distinct workspaces.
+ *
+ * Packed int4 layout (build-defined, generalising GGUF Q4_0,
+ * python/phantom/loader/gguf_loader.py:362-381): a weight row of K elements
+ * is K/2 bytes; group g of G elements (G = 32 or 64) is bytes
+ * [g*G/2, (g+1)*G/2); byte j of a group holds element j in its low nibble
+ * and element j+G/2 in its high nibble; value = (nibble - 8) * scale, with
+ * one fp16 scale per (row, group) in a separate [rows, K/G] array.
+ */
+#ifndef PHMOE_H_
+#define PHMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define PHMOE_OK 0
+#define PHMOE_ERR_INVALID_ARG (-1)  /* a size, pointer or flag is out of range */
+#define PHMOE_ERR_UNSUPPORTED (-2)  /* shape/dtype combination not built */
+#define PHMOE_ERR_WORKSPACE (-3)    /* workspace too small or misaligned */
+#define PHMOE_ERR_CUDA (-4)         /* a CUDA runtime call failed */
+#define PHMOE_ERR_ALIGNMENT (-5)    /* a pointer is not 16-byte aligned */
+
+/* ---- element types ---- */
+#define PHMOE_DTYPE_F32 0
+#define PHMOE_DTYPE_BF16 1
+
+/* ---- FFN path selection for phmoe_moe_layer ---- */
+#define PHMOE_PATH_AUTO 0    /* decode kernel for small batches, prefill kernel above */
+#define PHMOE_PATH_DECODE 1  /* register-dequant grouped GEMV (mma.sync) */
+#define PHMOE_PATH_PREFILL 2 /* TMA + tcgen05/TMEM grouped GEMM */
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int phmoe_version(void);
+
+/* Human-readable text for a status code. Never returns NULL. */
+const char* phmoe_status_string(int status);
+
+/* Detail text of the last failing call on this host thread ("" if none). */
+const char* phmoe_last_error(void);
+
+/*
+ * Bytes of workspace phmoe_moe_layer needs for T tokens (256-byte aligned
+ * sub-buffers). Returns 0 on invalid arguments.
+ */
+size_t phmoe_workspace_size(int T, int H, int E, int top_k, int I, int path);
+
+/*
+ * Router: logits = x . Wr^T (fp32, fixed reduction order), fp32 softmax,
+ * top-k with ties to the lower expert index, optional renormalisation.
+ * Replaces Qwen3MoeTopKRouter.forward (modeling_qwen3_moe.py:263-272) and
+ * PhantomTopKRouter.forward (tests/test_moe_routing.py:56-72).
+ *   x         [T, H]  x_dtype         router_w [E, H] w_dtype
+ *   logits    [T, E]  fp32 (required: also the softmax staging buffer)
+ *   probs     [T, E]  fp32 (may be NULL)
+ *   topk_idx  [T, k]  int32           topk_w   [T, k] fp32
+ * Limits: H % 8 == 0, 1 <= E <= 1024, 1 <= top_k <= min(E, 32).
+ */
+int phmoe_router(const void* x, int x_dtype, const void* router_w, int w_dtype, int T, int H,
+                 int E, int top_k, int renormalize, float* logits, float* probs,
+                 int32_t* topk_idx, float* topk_w, void* stream);
+
+/*
+ * Dispatch: group the T*k (token, slot) assignments by expert, ordered by
+ * token index inside each expert (replaces the one_hot/where loop,
+ * modeling_qwen3_moe.py:234-244).
+ *   expert_offsets [E+1]  exclusive scan of per-expert counts
+ *   row_token      [T*k]  token of each permuted row
+ *   inv            [T*k]  permuted row of assignment t*k+j
+ *   active         [E+1]  active[0] = number of experts hit, active[1..] their ids ascending
+ * `scratch` needs phmoe_dispatch_scratch_size(T, k, E) bytes.
+ */
+size_t phmoe_dispatch_scratch_size(int T, int top_k, int E);
+int phmoe_dispatch(const int32_t* topk_idx, int T, int top_k, int E, int32_t* expert_offsets,
+                   int32_t* row_token, int32_t* inv, int32_t* active, void* scratch,
+                   size_t scratch_bytes, void* stream);
+
+/*
+ * Grouped SwiGLU expert FFN over dispatched rows, decode form: int4 weights
+ * are dequantised in registers straight into mma.sync A fragments (weights
+ * never pass through shared memory). Replaces Qwen3MoeExperts.forward's
+ * per-expert loop body (modeling_qwen3_moe.py:245-247).
+ *   x        [T, H] x_dtype, gathered through row_token
+ *   w13_q    [E, 2I, H/2] uint8 (gate rows 0..I-1, up rows I..2I-1)
+ *   w13_s    [E, 2I, H/G] fp16        w2_q [E, H, I/2] uint8   w2_s [E, H, I/G] fp16
+ *   h        scratch of T*k*I*4 bytes (bf16 hi and lo planes of the SwiGLU output)
+ *   y        [T*k, H] fp32 output (permuted rows)
+ * Limits: H % 64 == 0, I % 64 == 0 (G = 64) or % 32 (G = 32).
+ */
+int phmoe_expert_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
+                            const int32_t* expert_offsets, const int32_t* active,
+                            const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
+                            const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
+                            int group_size, float* h, float* y, void* stream);
+
+/*
+ * Combine: out[t] = sum_j topk_w[t,j] * y[inv[t,j]] in slot order j = 0..k-1
+ * (deterministic; replaces the weight multiply + index_add_,
+ * modeling_qwen3_moe.py:248-249). out is [T, H] in out_dtype.
+ */
+int phmoe_combine(const float* y, const int32_t* inv, const float* topk_w, int T, int top_k,
+                  int H, void* out, int out_dtype, void* stream);
+
+/*
+ * The whole layer (Qwen3MoeSparseMoeBlock.forward, modeling_qwen3_moe.py:281-286,
+ * on [T, H] rows): router -> dispatch -> grouped FFN -> combine, all
+ * stream-ordered, no host synchronisation, no allocation.
+ *   out           [T, H] same dtype as x
+ *   topk_idx_out  [T, k] int32 (may be NULL)   topk_w_out [T, k] fp32 (may be NULL)
+ *   workspace     >= phmoe_workspace_size(T, H, E, k, I, path) bytes, 256-byte aligned
+ */
+int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtype,
+                    const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
+                    const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
+                    int group_size, int renormalize, int path, void* out, int32_t* topk_idx_out,
+                    float* topk_w_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Symmetric int4 group quantiser on the GPU (load-time utility; the
+ * reference has no quantiser and reads pre-quantised GGUF files):
+ * scale = fp16(absmax(group)/7), q = clamp(rint(w/scale), -8, 7).
+ *   w [rows, K] fp32 or bf16 -> packed [rows, K/2] uint8, scales [rows, K/G] fp16.
+ */
+int phmoe_quantize_int4(const void* w, int w_dtype, long long rows, int K, int group_size,
+                        uint8_t* packed, uint16_t* scales, void* stream);
+
+/*
+ * Instrumentation for benchmarks (no counterpart in the reference, whose
+ * entries return their own elapsed ms from a CudaTimer,
+ * kernels/common/cuda_utils.h:341-357, sparse_matmul.cu:256-257).
+ *
+ * phmoe_kernel_launch_count: number of kernels this library has enqueued in
+ * this process (host-side counter; replays of a captured CUDA graph are not
+ * counted again).
+ *
+ * phmoe_profile_begin(max_calls): the next max_calls phmoe_moe_layer calls
+ * record CUDA events between their stages on the caller's stream
+ * (stages: 0 router, 1 dispatch, 2 FFN gate/up, 3 FFN down, 4 combine).
+ * phmoe_profile_end waits for the last recorded event, writes the summed
+ * device time per stage (ms) into stage_ms[0..n_stages-1], the number of
+ * calls recorded into *calls, and releases the events. Process-global and
+ * not thread-safe; do not profile inside stream capture.
+ */
+#define PHMOE_NUM_STAGES 5
+unsigned long long phmoe_kernel_launch_count(void);
+int phmoe_profile_begin(int max_calls);
+int phmoe_profile_end(float* stage_ms, int n_stages, int* calls);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PHMOE_H_ */

@@ -1,0 +1,384 @@
+"""CPU oracle for the sparse-MoE layer (test infrastructure, not product code).
+
+This module is the parity checker for the CUDA path. Only ``tests/``,
+``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` may import
+it. The product path (``phantom_moe``) never calls into it.
+
+It restates, in NumPy, the reference's MoE-layer arithmetic:
+
+* router: logits = x . Wr^T, softmax in fp32, top-k, renormalise
+  (reference: tests/test_moe_routing.py:56-72 ``PhantomTopKRouter.forward``;
+  executed form transformers 5.5.0 models/qwen3_moe/modeling_qwen3_moe.py:263-272
+  ``Qwen3MoeTopKRouter.forward``; Mixtral models/mixtral/modeling_mixtral.py:109-117);
+* dispatch: one_hot + where grouping of (token, slot) pairs per expert
+  (modeling_qwen3_moe.py:234-244);
+* expert SwiGLU FFN: gate = first half of ``gate_up_proj``, silu(gate) * up,
+  then ``down_proj`` (modeling_qwen3_moe.py:245-247);
+* combine: multiply by the routing weight and ``index_add_`` per token
+  (modeling_qwen3_moe.py:248-249);
+* int4 dequant: GGUF Q4_0 nibble order and the -8 offset
+  (python/phantom/loader/gguf_loader.py:362-381 on CPU, 588-596 on GPU).
+
+Two router forms live here. ``route_reference`` is the plain fp32 semantics
+(what transformers computes, up to summation order). ``route_fixed_order``
+replays, operation by operation, the fixed reduction order and the exp
+routine of the CUDA router, so its logits, probabilities and top-k indices
+are bit-identical to the kernel's. Both are pinned against the reference: the
+golden fixtures under ``tests/golden`` were produced by running transformers'
+``Qwen3MoeSparseMoeBlock`` / ``MixtralSparseMoeBlock``, the reference's own
+``PhantomTopKRouter`` and the reference's ``GGUFLoader.dequantize_tensor``.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+F32 = np.float32
+
+# ---------------------------------------------------------------------------
+# int4 symmetric group quantisation (build-defined format)
+# ---------------------------------------------------------------------------
+#
+# Layout of one row of K weights, group size G (32 or 64), K % G == 0:
+#   packed row = K/2 bytes; group g occupies bytes [g*G/2, (g+1)*G/2).
+#   Inside a group, byte j holds element j in its low nibble and element
+#   j + G/2 in its high nibble: the GGUF Q4_0 block order
+#   (gguf_loader.py:372-378: low nibbles -> elements 0..15, high -> 16..31),
+#   with the fp16 scale moved out of the block into a separate
+#   [rows, K/G] fp16 array. With G = 32 the nibble bytes are exactly Q4_0's.
+#   value = (nibble - 8) * scale.
+# Quantiser (the reference has none; it consumes GGUF files):
+#   scale = fp16(absmax(group) / 7), q = clamp(rint(w / scale), -8, 7).
+
+
+def quantize_int4(w: np.ndarray, group: int = 64):
+    """Quantise ``w[..., K]`` (fp32) to packed int4 + fp16 scales.
+
+    Returns ``(packed uint8[..., K/2], scales fp16[..., K/group])``.
+    """
+    w = np.ascontiguousarray(w, dtype=F32)
+    K = w.shape[-1]
+    assert K % group == 0 and group in (32, 64)
+    lead = w.shape[:-1]
+    wg = w.reshape(*lead, K // group, group)
+    absmax = np.max(np.abs(wg), axis=-1)
+    scale16 = (absmax / F32(7.0)).astype(np.float16)
+    s = scale16.astype(F32)[..., None]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = np.where(s > 0, np.rint(wg / np.where(s > 0, s, F32(1.0))), F32(0.0))
+    q = np.clip(q, -8, 7).astype(np.int16) + 8
+    half = group // 2
+    lo = q[..., :half].astype(np.uint8)
+    hi = q[..., half:].astype(np.uint8)
+    packed = (lo | (hi << 4)).astype(np.uint8).reshape(*lead, K // 2)
+    return packed, scale16
+
+
+def dequantize_int4(packed: np.ndarray, scales: np.ndarray, group: int = 64) -> np.ndarray:
+    """Inverse of :func:`quantize_int4` (fp32 output).
+
+    Follows gguf_loader.py:372-378 (low nibble = first half of the block,
+    high nibble = second half, value = (nibble - 8) * d), generalised to a
+    group of 64 with the scale held in a separate array.
+    """
+    lead = packed.shape[:-1]
+    K = packed.shape[-1] * 2
+    half = group // 2
+    pg = packed.reshape(*lead, K // group, half)
+    lo = (pg & 0x0F).astype(np.int16) - 8
+    hi = ((pg >> 4) & 0x0F).astype(np.int16) - 8
+    q = np.concatenate([lo, hi], axis=-1).astype(F32)
+    s = scales.astype(F32)[..., None]
+    return (q * s).reshape(*lead, K)
+
+
+def dequantize_q4_0(raw: bytes, n_elems: int) -> np.ndarray:
+    """GGUF Q4_0 blocks -> fp32 (restates gguf_loader.py:362-381).
+
+    The reference returns bf16 (gguf_loader.py:380); this returns the fp32
+    values before that rounding.
+    """
+    n_blocks = n_elems // 32
+    blk = np.frombuffer(raw[: n_blocks * 18], dtype=np.uint8).reshape(n_blocks, 18)
+    d = blk[:, :2].copy().view(np.float16).astype(F32)
+    qs = blk[:, 2:]
+    low = (qs & 0x0F).astype(np.int8) - 8
+    high = ((qs >> 4) & 0x0F).astype(np.int8) - 8
+    out = np.empty((n_blocks, 32), dtype=F32)
+    out[:, :16] = low * d
+    out[:, 16:] = high * d
+    return out.reshape(-1)[:n_elems]
+
+
+def q4_0_to_packed(raw: bytes, rows: int, K: int):
+    """Split GGUF Q4_0 blocks of a [rows, K] tensor into (packed, scales).
+
+    Lossless: the 16 nibble bytes of each 18-byte block are kept as they are
+    and the fp16 ``d`` goes to the scales array (group size 32).
+    """
+    nb = K // 32
+    blk = np.frombuffer(raw[: rows * nb * 18], dtype=np.uint8).reshape(rows, nb, 18)
+    scales = blk[:, :, :2].copy().view(np.float16).reshape(rows, nb)
+    packed = np.ascontiguousarray(blk[:, :, 2:]).reshape(rows, K // 2)
+    return packed, scales
+
+
+# ---------------------------------------------------------------------------
+# fixed-order fp32 arithmetic shared with the CUDA router
+# ---------------------------------------------------------------------------
+
+def _bits(u: int) -> np.float32:
+    return np.array(u, dtype=np.uint32).view(F32)[()]
+
+
+# Constants as exact fp32 bit patterns (the CUDA router uses the same bits).
+LOG2E = _bits(0x3FB8AA3B)   # log2(e)
+LN2_HI = _bits(0x3F318000)  # 0.693359375, 9 significant bits: n * LN2_HI is exact
+LN2_LO = _bits(0xB95E8083)  # ln(2) - LN2_HI
+EXP_C = [_bits(u) for u in (0x3F800000, 0x3F800000, 0x3F000000, 0x3E2AAAAB,
+                            0x3D2AAAAB, 0x3C088889, 0x3AB60B61, 0x39500D01)]  # 1/i!
+
+
+def fixed_exp(x: np.ndarray) -> np.ndarray:
+    """exp(x) for x <= 0 by Cody-Waite range reduction + degree-7 Taylor.
+
+    Every step is one correctly rounded fp32 operation (no fused multiply-add),
+    in the same order as ``phm_exp_fixed`` in the CUDA router, so both produce
+    identical bits. x < -87 returns 0.
+    """
+    x = np.asarray(x, dtype=F32)
+    n = np.rint((x * LOG2E).astype(F32)).astype(F32)
+    r = (x - (n * LN2_HI).astype(F32)).astype(F32)
+    r = (r - (n * LN2_LO).astype(F32)).astype(F32)
+    p = EXP_C[7]
+    for c in (EXP_C[6], EXP_C[5], EXP_C[4], EXP_C[3], EXP_C[2], EXP_C[1], EXP_C[0]):
+        p = ((p * r).astype(F32) + c).astype(F32)
+    ni = np.clip(n, -126, 127).astype(np.int32)
+    two_n = ((ni + 127).astype(np.uint32) << np.uint32(23)).view(F32)
+    out = (p * two_n).astype(F32)
+    return np.where(x < F32(-87.0), F32(0.0), out).astype(F32)
+
+
+LANES = 32
+VEC = 8  # elements per lane per chunk (one 16-byte load of bf16)
+
+
+def logits_fixed_order(x: np.ndarray, wr: np.ndarray, products_exact: bool) -> np.ndarray:
+    """Router logits in the CUDA router's reduction order.
+
+    Element h of the hidden dimension goes to lane (h // 8) % 32 of a warp;
+    each lane accumulates its elements in increasing h with a rounded multiply
+    then a rounded add; the 32 lane sums are combined by an xor butterfly
+    (offsets 16, 8, 4, 2, 1). H is zero-padded to a multiple of 256.
+    ``products_exact`` is informational (bf16 inputs give exact fp32
+    products); the arithmetic is identical either way.
+    """
+    x = np.asarray(x, dtype=F32)
+    wr = np.asarray(wr, dtype=F32)
+    T, H = x.shape
+    E = wr.shape[0]
+    Hp = ((H + LANES * VEC - 1) // (LANES * VEC)) * LANES * VEC
+    if Hp != H:
+        x = np.pad(x, ((0, 0), (0, Hp - H)))
+        wr = np.pad(wr, ((0, 0), (0, Hp - H)))
+    nchunk = Hp // (LANES * VEC)
+    xr = x.reshape(T, nchunk, LANES, VEC)
+    wrr = wr.reshape(E, nchunk, LANES, VEC)
+    acc = np.zeros((T, E, LANES), dtype=F32)
+    for c in range(nchunk):
+        for v in range(VEC):
+            prod = (xr[:, None, c, :, v] * wrr[None, :, c, :, v]).astype(F32)
+            acc = (acc + prod).astype(F32)
+    for off in (16, 8, 4, 2, 1):
+        perm = np.arange(LANES) ^ off
+        acc = (acc + acc[:, :, perm]).astype(F32)
+    return acc[:, :, 0].copy()
+
+
+def softmax_fixed(logits: np.ndarray) -> np.ndarray:
+    """Softmax in the CUDA router's order: max, exp(l - max), lane sums
+    (expert e on lane e % 32, ascending e), xor butterfly, then a rounded
+    division."""
+    l = np.asarray(logits, dtype=F32)
+    T, E = l.shape
+    m = l.max(axis=1, keepdims=True)
+    e = fixed_exp((l - m).astype(F32))
+    Ep = ((E + LANES - 1) // LANES) * LANES
+    ep = np.pad(e, ((0, 0), (0, Ep - E))).reshape(T, Ep // LANES, LANES)
+    acc = np.zeros((T, LANES), dtype=F32)
+    for i in range(Ep // LANES):
+        acc = (acc + ep[:, i, :]).astype(F32)
+    for off in (16, 8, 4, 2, 1):
+        perm = np.arange(LANES) ^ off
+        acc = (acc + acc[:, perm]).astype(F32)
+    s = acc[:, :1]
+    return (e / s).astype(F32)
+
+
+def topk_stable(p: np.ndarray, k: int):
+    """Top-k by descending value; equal values -> lower expert index first.
+
+    The reference uses ``torch.topk`` whose tie order is unspecified
+    (modeling_qwen3_moe.py:267); this build pins 'lower index wins'.
+    """
+    T, E = p.shape
+    order = np.lexsort((np.broadcast_to(np.arange(E), (T, E)), -p), axis=1)[:, :k]
+    return order.astype(np.int32), np.take_along_axis(p, order, axis=1).astype(F32)
+
+
+def renormalise_fixed(vals: np.ndarray, renormalize: bool) -> np.ndarray:
+    """Sum of the k picked probabilities in pick order, then divide
+    (modeling_qwen3_moe.py:268-269)."""
+    if not renormalize:
+        return vals.astype(F32)
+    s = np.zeros((vals.shape[0], 1), dtype=F32)
+    for j in range(vals.shape[1]):
+        s = (s + vals[:, j : j + 1]).astype(F32)
+    return (vals / s).astype(F32)
+
+
+def route_fixed_order(x, wr, top_k: int, renormalize: bool = True):
+    """Router exactly as the CUDA kernel computes it.
+
+    Returns (logits fp32[T,E], probs fp32[T,E], idx int32[T,k], w fp32[T,k]).
+    """
+    logits = logits_fixed_order(x, wr, products_exact=True)
+    probs = softmax_fixed(logits)
+    idx, vals = topk_stable(probs, top_k)
+    return logits, probs, idx, renormalise_fixed(vals, renormalize)
+
+
+def route_reference(x, wr, top_k: int, renormalize: bool = True):
+    """Plain fp32 router semantics (modeling_qwen3_moe.py:263-272): logits by
+    float64 dot then rounded to fp32, fp32 softmax, stable top-k, renorm."""
+    x = np.asarray(x, dtype=np.float64)
+    wr = np.asarray(wr, dtype=np.float64)
+    logits = (x @ wr.T).astype(F32)
+    l64 = logits.astype(np.float64)
+    e = np.exp(l64 - l64.max(axis=1, keepdims=True))
+    probs = (e / e.sum(axis=1, keepdims=True)).astype(F32)
+    idx, vals = topk_stable(probs, top_k)
+    if renormalize:
+        vals = (vals / vals.sum(axis=1, keepdims=True, dtype=np.float64)).astype(F32)
+    return logits, probs, idx, vals
+
+
+def topk_margin(probs: np.ndarray, k: int) -> np.ndarray:
+    """Per-token gap between the k-th and (k+1)-th largest probability."""
+    s = -np.sort(-probs, axis=1)
+    if probs.shape[1] <= k:
+        return np.full(probs.shape[0], np.inf, dtype=F32)
+    return (s[:, k - 1] - s[:, k]).astype(F32)
+
+
+# ---------------------------------------------------------------------------
+# dispatch / FFN / combine
+# ---------------------------------------------------------------------------
+
+
+def dispatch(idx: np.ndarray, num_experts: int):
+    """Group (token, slot) assignments by expert, ordered by token index.
+
+    Returns ``counts[E]``, ``offsets[E+1]`` (exclusive scan), ``row_token[R]``
+    (token of each permuted row), ``row_slot[R]`` (its k slot) and
+    ``inv[T,k]`` (permuted row of each assignment); R = T*k.
+
+    The reference groups with one_hot + where (modeling_qwen3_moe.py:234-244);
+    within one expert each token appears at most once, so 'by token index' is
+    a total order. This is the permutation the CUDA dispatch must reproduce
+    bit for bit.
+    """
+    idx = np.asarray(idx, dtype=np.int64)
+    T, k = idx.shape
+    flat = idx.reshape(-1)
+    counts = np.bincount(flat, minlength=num_experts).astype(np.int32)
+    offsets = np.zeros(num_experts + 1, dtype=np.int32)
+    offsets[1:] = np.cumsum(counts)
+    tok = np.repeat(np.arange(T), k)
+    slot = np.tile(np.arange(k), T)
+    order = np.lexsort((tok, flat))  # by expert, then token
+    row_token = tok[order].astype(np.int32)
+    row_slot = slot[order].astype(np.int32)
+    inv = np.empty(T * k, dtype=np.int32)
+    inv[order] = np.arange(T * k, dtype=np.int32)
+    return counts, offsets, row_token, row_slot, inv.reshape(T, k)
+
+
+def silu(x):
+    x = np.asarray(x, dtype=F32)
+    return (x / (F32(1.0) + np.exp(-x))).astype(F32)
+
+
+def expert_ffn(x_rows: np.ndarray, w13: np.ndarray, w2: np.ndarray) -> np.ndarray:
+    """SwiGLU FFN of one expert in fp32 (modeling_qwen3_moe.py:245-247).
+
+    ``w13`` is [2I, H] with the gate rows first (``chunk(2)`` order);
+    ``w2`` is [H, I].
+    """
+    I = w13.shape[0] // 2
+    gu = x_rows.astype(F32) @ w13.T.astype(F32)
+    h = silu(gu[:, :I]) * gu[:, I:]
+    return (h.astype(F32) @ w2.T.astype(F32)).astype(F32)
+
+
+def moe_layer_reference(x, wr, w13_deq, w2_deq, top_k: int, renormalize: bool = True,
+                        router: str = "fixed"):
+    """Whole layer in fp32 on dequantized weights.
+
+    ``router='fixed'`` uses the kernel-order router (so the expert choice is the
+    kernel's), ``'reference'`` the plain fp32 router. Experts are visited in
+    ascending index and their rows accumulated into each token in that order,
+    as ``index_add_`` does (modeling_qwen3_moe.py:239-249).
+    Returns (out fp32[T,H], idx, w).
+    """
+    x = np.asarray(x, dtype=F32)
+    T, H = x.shape
+    E = w13_deq.shape[0]
+    if router == "fixed":
+        _, _, idx, w = route_fixed_order(x, wr, top_k, renormalize)
+    else:
+        _, _, idx, w = route_reference(x, wr, top_k, renormalize)
+    out = np.zeros((T, H), dtype=F32)
+    for e in range(E):
+        tok, slot = np.nonzero(idx == e)
+        if tok.size == 0:
+            continue
+        y = expert_ffn(x[tok], w13_deq[e], w2_deq[e])
+        out[tok] += (y * w[tok, slot][:, None]).astype(F32)
+    return out, idx, w
+
+
+def moe_layer_reference_packed(x, wr, w13_q, w13_s, w2_q, w2_s, top_k: int, group: int = 64,
+                               renormalize: bool = True, router: str = "fixed", idx=None, w=None):
+    """:func:`moe_layer_reference` on packed weights, dequantising one expert
+    at a time (full-size layers would need ~2.4 GB of fp32 weights at once).
+    ``idx``/``w`` may be given to reuse a routing computed elsewhere."""
+    x = np.asarray(x, dtype=F32)
+    T, H = x.shape
+    E = w13_q.shape[0]
+    if idx is None:
+        route = route_fixed_order if router == "fixed" else route_reference
+        _, _, idx, w = route(x, wr, top_k, renormalize)
+    out = np.zeros((T, H), dtype=F32)
+    for e in range(E):
+        tok, slot = np.nonzero(idx == e)
+        if tok.size == 0:
+            continue
+        d13 = dequantize_int4(w13_q[e], w13_s[e], group)
+        d2 = dequantize_int4(w2_q[e], w2_s[e], group)
+        y = expert_ffn(x[tok], d13, d2)
+        out[tok] += (y * w[tok, slot][:, None]).astype(F32)
+    return out, idx, w
+
+
+def parity_stats(got: np.ndarray, ref: np.ndarray):
+    """(max-abs error, mean-relative error) as the north star defines them:
+    max |got - ref| and mean|got - ref| / mean|ref|."""
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    d = np.abs(got - ref)
+    return float(d.max(initial=0.0)), float(d.mean() / max(np.abs(ref).mean(), 1e-30))
+
+
+MAX_ABS_TOL = 2e-2
+MEAN_REL_TOL = 5e-3

@@ -1,0 +1,332 @@
+// C ABI of the phantom-moe layer (declared in include/phmoe.h).
+//
+// Every entry validates its arguments, launches stream-ordered work and
+// returns a status code; nothing allocates, synchronises or exits. The
+// reference's native entries instead cudaMalloc/cudaFree and create a cuBLAS
+// handle per call and exit() on error (kernels/sparse_moe/sparse_matmul.cu:
+// 264-314, kernels/common/cuda_utils.h:31-52).
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace phmoe {
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess)
+    return fail(PHMOE_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(err), cudaGetErrorString(err));
+  return PHMOE_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+bool dtype_ok(int d) { return d == PHMOE_DTYPE_F32 || d == PHMOE_DTYPE_BF16; }
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+constexpr size_t kAlign = 256;
+
+// Workspace carve-up shared by phmoe_workspace_size and phmoe_moe_layer.
+struct Layout {
+  size_t logits, idx, w, offsets, active, row_token, inv, disp, h, y, total;
+};
+
+Layout make_layout(int T, int H, int E, int k, int I) {
+  Layout L{};
+  const size_t R = (size_t)T * k;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { const size_t o = off; off = round_up(off + bytes, kAlign); return o; };
+  L.logits = take((size_t)T * E * 4);
+  L.idx = take(R * 4);
+  L.w = take(R * 4);
+  L.offsets = take((size_t)(E + 1) * 4);
+  L.active = take((size_t)(E + 1) * 4);
+  L.row_token = take(R * 4);
+  L.inv = take(R * 4);
+  L.disp = take(dispatch_scratch_bytes(T, k, E));
+  L.h = take(R * (size_t)I * 4);
+  L.y = take(R * (size_t)H * 4);
+  L.total = off;
+  return L;
+}
+
+int check_router_dims(int T, int H, int E, int top_k) {
+  if (T < 0) return fail(PHMOE_ERR_INVALID_ARG, "T must be >= 0 (got %d)", T);
+  if (H <= 0 || H % 8) return fail(PHMOE_ERR_INVALID_ARG, "H must be a positive multiple of 8 (got %d)", H);
+  if (E < 1 || E > 1024) return fail(PHMOE_ERR_INVALID_ARG, "E must be in [1, 1024] (got %d)", E);
+  if (top_k < 1 || top_k > E || top_k > 32)
+    return fail(PHMOE_ERR_INVALID_ARG, "top_k must be in [1, min(E, 32)] (got %d, E=%d)", top_k, E);
+  return PHMOE_OK;
+}
+
+int check_ffn_dims(int H, int I, int G) {
+  if (G != 32 && G != 64) return fail(PHMOE_ERR_UNSUPPORTED, "group_size must be 32 or 64 (got %d)", G);
+  if (H % 64) return fail(PHMOE_ERR_UNSUPPORTED, "H must be a multiple of 64 (got %d)", H);
+  if (I <= 0 || I % 16 || I % G)
+    return fail(PHMOE_ERR_UNSUPPORTED, "I must be a positive multiple of 16 and of group_size (got %d)", I);
+  return PHMOE_OK;
+}
+
+}  // namespace
+
+namespace {
+std::atomic<unsigned long long> g_launches{0};
+
+// Stage-timing events for phmoe_profile_begin/end (process-global).
+struct Profile {
+  int max_calls = 0;
+  int calls = 0;
+  std::vector<cudaEvent_t> ev;  // max_calls * (PHMOE_NUM_STAGES + 1)
+};
+Profile g_prof;
+
+cudaEvent_t prof_event(int call, int boundary) {
+  return g_prof.ev[(size_t)call * (PHMOE_NUM_STAGES + 1) + boundary];
+}
+}  // namespace
+
+void note_launches(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+
+int device_sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+}  // namespace phmoe
+
+using namespace phmoe;
+
+extern "C" {
+
+int phmoe_version(void) { return 100; }
+
+const char* phmoe_status_string(int status) {
+  switch (status) {
+    case PHMOE_OK: return "ok";
+    case PHMOE_ERR_INVALID_ARG: return "invalid argument";
+    case PHMOE_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+    case PHMOE_ERR_WORKSPACE: return "workspace too small or misaligned";
+    case PHMOE_ERR_CUDA: return "CUDA error";
+    case PHMOE_ERR_ALIGNMENT: return "pointer not 16-byte aligned";
+    default: return "unknown status";
+  }
+}
+
+const char* phmoe_last_error(void) { return g_last_error.c_str(); }
+
+size_t phmoe_workspace_size(int T, int H, int E, int top_k, int I, int path) {
+  if (T < 0 || H <= 0 || E < 1 || top_k < 1 || I <= 0) return 0;
+  if (path < PHMOE_PATH_AUTO || path > PHMOE_PATH_PREFILL) return 0;
+  return make_layout(T, H, E, top_k, I).total;
+}
+
+int phmoe_router(const void* x, int x_dtype, const void* router_w, int w_dtype, int T, int H,
+                 int E, int top_k, int renormalize, float* logits, float* probs,
+                 int32_t* topk_idx, float* topk_w, void* stream) {
+  g_last_error.clear();
+  if (int s = check_router_dims(T, H, E, top_k)) return s;
+  if (!dtype_ok(x_dtype) || !dtype_ok(w_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  if (T == 0) return PHMOE_OK;
+  if (!x || !router_w || !logits || !topk_idx || !topk_w)
+    return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned(x, 16) || !aligned(router_w, 16))
+    return fail(PHMOE_ERR_ALIGNMENT, "x and router_w must be 16-byte aligned");
+  launch_router(x, x_dtype, router_w, w_dtype, T, H, E, top_k, renormalize, logits, probs, topk_idx,
+                topk_w, static_cast<cudaStream_t>(stream));
+  return check_launch("phmoe_router");
+}
+
+size_t phmoe_dispatch_scratch_size(int T, int top_k, int E) {
+  if (T < 0 || top_k < 1 || E < 1) return 0;
+  return dispatch_scratch_bytes(T, top_k, E);
+}
+
+int phmoe_dispatch(const int32_t* topk_idx, int T, int top_k, int E, int32_t* expert_offsets,
+                   int32_t* row_token, int32_t* inv, int32_t* active, void* scratch,
+                   size_t scratch_bytes, void* stream) {
+  g_last_error.clear();
+  if (T < 0 || top_k < 1 || top_k > 32 || E < 1 || E > 1024)
+    return fail(PHMOE_ERR_INVALID_ARG, "bad dispatch dims T=%d k=%d E=%d", T, top_k, E);
+  if (!expert_offsets || !active) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (T > 0 && (!topk_idx || !row_token || !inv)) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  const size_t need = dispatch_scratch_bytes(T, top_k, E);
+  if (scratch_bytes < need || (need && !scratch))
+    return fail(PHMOE_ERR_WORKSPACE, "dispatch scratch needs %zu bytes", need);
+  launch_dispatch(topk_idx, T, top_k, E, expert_offsets, row_token, inv, active, scratch,
+                  static_cast<cudaStream_t>(stream));
+  return check_launch("phmoe_dispatch");
+}
+
+int phmoe_expert_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
+                            const int32_t* expert_offsets, const int32_t* active,
+                            const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
+                            const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
+                            int group_size, float* h, float* y, void* stream) {
+  g_last_error.clear();
+  if (int s = check_router_dims(T, H, E, top_k)) return s;
+  if (int s = check_ffn_dims(H, I, group_size)) return s;
+  if (!dtype_ok(x_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  if (T == 0) return PHMOE_OK;
+  if (!x || !row_token || !expert_offsets || !active || !w13_q || !w13_s || !w2_q || !w2_s || !h || !y)
+    return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned(x, 16) || !aligned(w13_q, 16) || !aligned(w2_q, 16) || !aligned(h, 16) || !aligned(y, 16))
+    return fail(PHMOE_ERR_ALIGNMENT, "x, weights, h and y must be 16-byte aligned");
+  if (!aligned(w13_s, 2) || !aligned(w2_s, 2)) return fail(PHMOE_ERR_ALIGNMENT, "scales must be 2-byte aligned");
+  const int s = launch_ffn_decode(x, x_dtype, row_token, expert_offsets, active, w13_q, w13_s, w2_q,
+                                  w2_s, T, H, E, top_k, I, group_size, h, y,
+                                  static_cast<cudaStream_t>(stream));
+  if (s) return fail(s, "no decode kernel for group_size=%d", group_size);
+  return check_launch("phmoe_expert_ffn_decode");
+}
+
+int phmoe_combine(const float* y, const int32_t* inv, const float* topk_w, int T, int top_k,
+                  int H, void* out, int out_dtype, void* stream) {
+  g_last_error.clear();
+  if (T < 0 || top_k < 1 || top_k > 32 || H <= 0 || H % 4)
+    return fail(PHMOE_ERR_INVALID_ARG, "bad combine dims T=%d k=%d H=%d", T, top_k, H);
+  if (!dtype_ok(out_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  if (T == 0) return PHMOE_OK;
+  if (!y || !inv || !topk_w || !out) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned(y, 16) || !aligned(out, 16)) return fail(PHMOE_ERR_ALIGNMENT, "y and out must be 16-byte aligned");
+  launch_combine(y, inv, topk_w, T, top_k, H, out, out_dtype, static_cast<cudaStream_t>(stream));
+  return check_launch("phmoe_combine");
+}
+
+int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtype,
+                    const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
+                    const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
+                    int group_size, int renormalize, int path, void* out, int32_t* topk_idx_out,
+                    float* topk_w_out, void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (int s = check_router_dims(T, H, E, top_k)) return s;
+  if (int s = check_ffn_dims(H, I, group_size)) return s;
+  if (!dtype_ok(x_dtype) || !dtype_ok(w_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  if (path < PHMOE_PATH_AUTO || path > PHMOE_PATH_PREFILL)
+    return fail(PHMOE_ERR_INVALID_ARG, "bad path code %d", path);
+  if (path == PHMOE_PATH_PREFILL)
+    return fail(PHMOE_ERR_UNSUPPORTED, "prefill path is not built in this library");
+  if (T == 0) return PHMOE_OK;
+  if (!x || !router_w || !w13_q || !w13_s || !w2_q || !w2_s || !out || !workspace)
+    return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned(x, 16) || !aligned(router_w, 16) || !aligned(w13_q, 16) || !aligned(w2_q, 16) || !aligned(out, 16))
+    return fail(PHMOE_ERR_ALIGNMENT, "x, router_w, packed weights and out must be 16-byte aligned");
+  if (!aligned(w13_s, 2) || !aligned(w2_s, 2)) return fail(PHMOE_ERR_ALIGNMENT, "scales must be 2-byte aligned");
+  const Layout L = make_layout(T, H, E, top_k, I);
+  if (!aligned(workspace, kAlign)) return fail(PHMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  if (workspace_bytes < L.total)
+    return fail(PHMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", L.total, workspace_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  float* logits = reinterpret_cast<float*>(ws + L.logits);
+  int32_t* idx = topk_idx_out ? topk_idx_out : reinterpret_cast<int32_t*>(ws + L.idx);
+  float* wts = topk_w_out ? topk_w_out : reinterpret_cast<float*>(ws + L.w);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  int32_t* active = reinterpret_cast<int32_t*>(ws + L.active);
+  int32_t* row_token = reinterpret_cast<int32_t*>(ws + L.row_token);
+  int32_t* inv = reinterpret_cast<int32_t*>(ws + L.inv);
+  float* h = reinterpret_cast<float*>(ws + L.h);
+  float* y = reinterpret_cast<float*>(ws + L.y);
+
+  const bool prof = g_prof.calls < g_prof.max_calls;
+  const int pc = g_prof.calls;
+  auto mark = [&](int b) { if (prof) cudaEventRecord(prof_event(pc, b), st); };
+
+  mark(0);
+  launch_router(x, x_dtype, router_w, w_dtype, T, H, E, top_k, renormalize, logits, nullptr, idx, wts, st);
+  if (int s = check_launch("router")) return s;
+  mark(1);
+  launch_dispatch(idx, T, top_k, E, offsets, row_token, inv, active, ws + L.disp, st);
+  if (int s = check_launch("dispatch")) return s;
+  mark(2);
+  if (int s = launch_ffn_decode(x, x_dtype, row_token, offsets, active, w13_q, w13_s, w2_q, w2_s, T, H,
+                                E, top_k, I, group_size, h, y, st, prof ? prof_event(pc, 3) : nullptr))
+    return fail(s, "no decode kernel for group_size=%d", group_size);
+  if (int s = check_launch("expert_ffn")) return s;
+  mark(4);
+  launch_combine(y, inv, wts, T, top_k, H, out, x_dtype, st);
+  mark(5);
+  if (prof) g_prof.calls++;
+  return check_launch("combine");
+}
+
+int phmoe_quantize_int4(const void* w, int w_dtype, long long rows, int K, int group_size,
+                        uint8_t* packed, uint16_t* scales, void* stream) {
+  g_last_error.clear();
+  if (!dtype_ok(w_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  if (group_size != 32 && group_size != 64) return fail(PHMOE_ERR_UNSUPPORTED, "group_size must be 32 or 64");
+  if (rows < 0 || K <= 0 || K % group_size) return fail(PHMOE_ERR_INVALID_ARG, "K must be a positive multiple of group_size");
+  if (rows == 0) return PHMOE_OK;
+  if (!w || !packed || !scales) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  launch_quantize(w, w_dtype, rows, K, group_size, packed, scales, static_cast<cudaStream_t>(stream));
+  return check_launch("phmoe_quantize_int4");
+}
+
+unsigned long long phmoe_kernel_launch_count(void) { return g_launches.load(); }
+
+int phmoe_profile_begin(int max_calls) {
+  g_last_error.clear();
+  if (max_calls < 0 || max_calls > (1 << 20)) return fail(PHMOE_ERR_INVALID_ARG, "bad max_calls %d", max_calls);
+  for (cudaEvent_t e : g_prof.ev) cudaEventDestroy(e);
+  g_prof = Profile{};
+  g_prof.ev.resize((size_t)max_calls * (PHMOE_NUM_STAGES + 1));
+  for (auto& e : g_prof.ev) {
+    const cudaError_t err = cudaEventCreate(&e);
+    if (err != cudaSuccess) {
+      g_prof.ev.clear();
+      return fail(PHMOE_ERR_CUDA, "cudaEventCreate: %s", cudaGetErrorString(err));
+    }
+  }
+  g_prof.max_calls = max_calls;
+  return PHMOE_OK;
+}
+
+int phmoe_profile_end(float* stage_ms, int n_stages, int* calls) {
+  g_last_error.clear();
+  int status = PHMOE_OK;
+  if (stage_ms)
+    for (int s = 0; s < n_stages; ++s) stage_ms[s] = 0.f;
+  const int n = g_prof.calls;
+  if (n > 0) {
+    const cudaError_t err = cudaEventSynchronize(prof_event(n - 1, PHMOE_NUM_STAGES));
+    if (err != cudaSuccess) status = fail(PHMOE_ERR_CUDA, "cudaEventSynchronize: %s", cudaGetErrorString(err));
+  }
+  for (int c = 0; c < n && status == PHMOE_OK; ++c)
+    for (int s = 0; s < PHMOE_NUM_STAGES && s < n_stages; ++s) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, prof_event(c, s), prof_event(c, s + 1)) == cudaSuccess && stage_ms)
+        stage_ms[s] += ms;
+    }
+  if (calls) *calls = n;
+  for (cudaEvent_t e : g_prof.ev) cudaEventDestroy(e);
+  g_prof = Profile{};
+  return status;
+}
+
+}  // extern "C"

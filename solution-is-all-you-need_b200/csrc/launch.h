@@ -1,0 +1,38 @@
+// Internal launchers shared between the kernel files and the C ABI layer.
+// Arguments are validated by the ABI layer (api.cu) before these run.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace phmoe {
+
+int launch_router(const void* x, int x_dtype, const void* wr, int w_dtype, int T, int H, int E,
+                  int top_k, int renormalize, float* logits, float* probs, int32_t* topk_idx,
+                  float* topk_w, cudaStream_t st);
+
+size_t dispatch_scratch_bytes(int T, int top_k, int E);
+int launch_dispatch(const int32_t* topk_idx, int T, int top_k, int E, int32_t* offsets,
+                    int32_t* row_token, int32_t* inv, int32_t* active, void* scratch,
+                    cudaStream_t st);
+
+// mid_event (may be null) is recorded between the gate/up and down kernels.
+int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
+                      const int32_t* offsets, const int32_t* active, const uint8_t* w13_q,
+                      const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T,
+                      int H, int E, int top_k, int I, int G, float* h, float* y,
+                      cudaStream_t st, cudaEvent_t mid_event = nullptr);
+
+int launch_combine(const float* y, const int32_t* inv, const float* topk_w, int T, int top_k,
+                   int H, void* out, int out_dtype, cudaStream_t st);
+
+int launch_quantize(const void* w, int w_dtype, long long rows, int K, int G, uint8_t* packed,
+                    uint16_t* scales, cudaStream_t st);
+
+int device_sm_count();
+
+// Host-side count of kernels enqueued by this library (see phmoe.h).
+void note_launches(int n);
+
+}  // namespace phmoe

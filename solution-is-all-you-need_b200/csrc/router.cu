@@ -1,0 +1,218 @@
+// Fused MoE router: logits GEMV (fixed fp32 reduction order), fp32 softmax
+// with a bit-reproducible exp, warp-shuffle top-k (ties -> lower expert
+// index) and renormalisation.
+//
+// Reference semantics: Qwen3MoeTopKRouter.forward (transformers 5.5.0
+// models/qwen3_moe/modeling_qwen3_moe.py:263-272): linear -> softmax(fp32) ->
+// topk -> divide by the sum of the picked values; PhantomTopKRouter.forward
+// (tests/test_moe_routing.py:56-72) computes the same weights as
+// softmax over the k largest logits.
+//
+// Every fp32 operation below is an explicitly rounded __fmul_rn/__fadd_rn/
+// __fdiv_rn so that the CPU restatement can replay it bit for bit:
+//   logit(t,e): element h goes to lane (h/8)%32; each lane adds its products
+//   in increasing h; lanes are combined by an xor butterfly 16,8,4,2,1.
+//   softmax: expert e on lane e%32, lane sums in increasing e, xor butterfly.
+#include "common.cuh"
+#include "launch.h"
+
+namespace phmoe {
+
+namespace {
+
+constexpr int kRouterWarps = 8;     // experts per CTA (one warp each)
+constexpr int kRouterTokens = 8;    // tokens per CTA
+
+template <typename T>
+struct Vec8;
+
+template <>
+struct Vec8<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, bool ok, float (&v)[8]) {
+    uint4 u = ok ? __ldg(reinterpret_cast<const uint4*>(p)) : make_uint4(0, 0, 0, 0);
+    v[0] = bf16_lo_to_f32(u.x); v[1] = bf16_hi_to_f32(u.x);
+    v[2] = bf16_lo_to_f32(u.y); v[3] = bf16_hi_to_f32(u.y);
+    v[4] = bf16_lo_to_f32(u.z); v[5] = bf16_hi_to_f32(u.z);
+    v[6] = bf16_lo_to_f32(u.w); v[7] = bf16_hi_to_f32(u.w);
+  }
+};
+
+template <>
+struct Vec8<float> {
+  static __device__ __forceinline__ void load(const float* p, bool ok, float (&v)[8]) {
+    float4 a = ok ? __ldg(reinterpret_cast<const float4*>(p)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 b = ok ? __ldg(reinterpret_cast<const float4*>(p) + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+};
+
+template <typename XT, typename WT>
+__global__ void __launch_bounds__(kRouterWarps * 32)
+router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T, int H, int E,
+                     float* __restrict__ logits) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * kRouterWarps + warp;
+  const int t0 = blockIdx.y * kRouterTokens;
+  if (e >= E) return;
+  const int nt = min(kRouterTokens, T - t0);
+  float acc[kRouterTokens];
+#pragma unroll
+  for (int t = 0; t < kRouterTokens; ++t) acc[t] = 0.f;
+  const int nchunk = (H + 255) / 256;
+  const WT* wrow = wr + (size_t)e * H;
+  for (int c = 0; c < nchunk; ++c) {
+    const int h0 = c * 256 + lane * 8;
+    const bool ok = h0 < H;
+    float w[8];
+    Vec8<WT>::load(wrow + h0, ok, w);
+#pragma unroll
+    for (int t = 0; t < kRouterTokens; ++t) {
+      if (t < nt) {
+        float xv[8];
+        Vec8<XT>::load(x + (size_t)(t0 + t) * H + h0, ok, xv);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) acc[t] = __fadd_rn(acc[t], __fmul_rn(xv[v], w[v]));
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kRouterTokens; ++t) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1)
+      acc[t] = __fadd_rn(acc[t], __shfl_xor_sync(0xffffffffu, acc[t], off));
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int t = 0; t < kRouterTokens; ++t)
+      if (t < nt) logits[(size_t)(t0 + t) * E + e] = acc[t];
+  }
+}
+
+// exp(x) for x <= 0: Cody-Waite reduction with a two-part ln2, then the
+// degree-7 Taylor polynomial of e^r in Horner form, then scaling by 2^n.
+// Constants are fp32 bit patterns shared with the CPU restatement.
+__device__ __forceinline__ float exp_fixed(float x) {
+  const float kLog2e = __uint_as_float(0x3FB8AA3Bu);
+  const float kLn2Hi = __uint_as_float(0x3F318000u);
+  const float kLn2Lo = __uint_as_float(0xB95E8083u);
+  const float c[8] = {__uint_as_float(0x3F800000u), __uint_as_float(0x3F800000u),
+                      __uint_as_float(0x3F000000u), __uint_as_float(0x3E2AAAABu),
+                      __uint_as_float(0x3D2AAAABu), __uint_as_float(0x3C088889u),
+                      __uint_as_float(0x3AB60B61u), __uint_as_float(0x39500D01u)};
+  const float n = rintf(__fmul_rn(x, kLog2e));
+  float r = __fsub_rn(x, __fmul_rn(n, kLn2Hi));
+  r = __fsub_rn(r, __fmul_rn(n, kLn2Lo));
+  float p = c[7];
+#pragma unroll
+  for (int i = 6; i >= 0; --i) p = __fadd_rn(__fmul_rn(p, r), c[i]);
+  int ni = (int)n;
+  ni = ni < -126 ? -126 : (ni > 127 ? 127 : ni);
+  const float two_n = __uint_as_float((uint32_t)(ni + 127) << 23);
+  const float out = __fmul_rn(p, two_n);
+  return x < -87.0f ? 0.0f : out;
+}
+
+// One warp per token. EPL = experts held per lane (E <= 32*EPL).
+template <int EPL>
+__global__ void __launch_bounds__(256)
+router_topk_kernel(const float* __restrict__ logits, int T, int E, int top_k, int renormalize,
+                   float* __restrict__ probs, int32_t* __restrict__ topk_idx,
+                   float* __restrict__ topk_w) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t >= T) return;
+  const float* lrow = logits + (size_t)t * E;
+  float v[EPL];
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? lrow[e] : -INFINITY;
+    m = fmaxf(m, v[i]);
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? exp_fixed(__fsub_rn(v[i], m)) : 0.f;
+    s = __fadd_rn(s, v[i]);
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    if (e < E) {
+      v[i] = __fdiv_rn(v[i], s);
+      if (probs) probs[(size_t)t * E + e] = v[i];
+    } else {
+      v[i] = -1.0f;  // below every probability: never picked
+    }
+  }
+  // k rounds of warp argmax; larger value wins, equal values -> lower index.
+  uint32_t taken = 0;
+  float my_val = 0.f;
+  int my_idx = 0;
+  float sum_sel = 0.f;
+  for (int j = 0; j < top_k; ++j) {
+    float bv = -2.0f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = lane + 32 * i;
+      const bool free_slot = !((taken >> i) & 1u);
+      if (free_slot && (v[i] > bv || (v[i] == bv && e < bi))) { bv = v[i]; bi = e; }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    sum_sel = __fadd_rn(sum_sel, bv);
+    if (lane == j) { my_val = bv; my_idx = bi; }
+  }
+  if (lane < top_k) {
+    topk_idx[(size_t)t * top_k + lane] = my_idx;
+    topk_w[(size_t)t * top_k + lane] = renormalize ? __fdiv_rn(my_val, sum_sel) : my_val;
+  }
+}
+
+template <typename XT, typename WT>
+void launch_logits(const void* x, const void* wr, int T, int H, int E, float* logits,
+                   cudaStream_t st) {
+  dim3 grid((E + kRouterWarps - 1) / kRouterWarps, (T + kRouterTokens - 1) / kRouterTokens);
+  router_logits_kernel<XT, WT><<<grid, kRouterWarps * 32, 0, st>>>(
+      static_cast<const XT*>(x), static_cast<const WT*>(wr), T, H, E, logits);
+}
+
+}  // namespace
+
+int launch_router(const void* x, int x_dtype, const void* wr, int w_dtype, int T, int H, int E,
+                  int top_k, int renormalize, float* logits, float* probs, int32_t* topk_idx,
+                  float* topk_w, cudaStream_t st) {
+  if (T == 0) return PHMOE_OK;
+  if (x_dtype == PHMOE_DTYPE_BF16 && w_dtype == PHMOE_DTYPE_BF16)
+    launch_logits<__nv_bfloat16, __nv_bfloat16>(x, wr, T, H, E, logits, st);
+  else if (x_dtype == PHMOE_DTYPE_BF16 && w_dtype == PHMOE_DTYPE_F32)
+    launch_logits<__nv_bfloat16, float>(x, wr, T, H, E, logits, st);
+  else if (x_dtype == PHMOE_DTYPE_F32 && w_dtype == PHMOE_DTYPE_BF16)
+    launch_logits<float, __nv_bfloat16>(x, wr, T, H, E, logits, st);
+  else
+    launch_logits<float, float>(x, wr, T, H, E, logits, st);
+  const int grid = (T + 7) / 8;
+  if (E <= 128)
+    router_topk_kernel<4><<<grid, 256, 0, st>>>(logits, T, E, top_k, renormalize, probs, topk_idx, topk_w);
+  else if (E <= 256)
+    router_topk_kernel<8><<<grid, 256, 0, st>>>(logits, T, E, top_k, renormalize, probs, topk_idx, topk_w);
+  else
+    router_topk_kernel<32><<<grid, 256, 0, st>>>(logits, T, E, top_k, renormalize, probs, topk_idx, topk_w);
+  note_launches(2);
+  return PHMOE_OK;
+}
+
+}  // namespace phmoe

@@ -1,0 +1,38 @@
+"""phantom_moe - B200-native (sm_100a) sparse-MoE layer.
+
+Drop-in for the MoE block that PHANTOM (FreakyAdy/Solution-is-all-You-need)
+runs through transformers (python/phantom/phantom_cli.py:1393-1430 ->
+Qwen3MoeSparseMoeBlock.forward, transformers 5.5.0
+models/qwen3_moe/modeling_qwen3_moe.py:281-286), with int4 group-quantised
+experts. The compute is hand-written CUDA in ``libphmoe.so`` behind the C ABI
+of ``include/phmoe.h``; this package validates tensors and calls it.
+"""
+
+from ._lib import PhmoeError, load as load_library
+from .layer import (
+    PackedExperts,
+    check_expert_weights,
+    combine,
+    dispatch,
+    expert_ffn_decode,
+    moe_layer,
+    pack_experts,
+    quantize_int4,
+    router,
+)
+
+__all__ = [
+    "PhmoeError",
+    "PackedExperts",
+    "check_expert_weights",
+    "combine",
+    "dispatch",
+    "expert_ffn_decode",
+    "load_library",
+    "moe_layer",
+    "pack_experts",
+    "quantize_int4",
+    "router",
+]
+
+__version__ = "0.1.0"

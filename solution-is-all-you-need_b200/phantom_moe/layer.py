@@ -1,0 +1,296 @@
+"""Host side of the MoE layer: tensor validation + calls into the C ABI.
+
+``moe_layer`` is the drop-in for ``Qwen3MoeSparseMoeBlock.forward`` /
+``MixtralSparseMoeBlock.forward`` (transformers 5.5.0
+models/qwen3_moe/modeling_qwen3_moe.py:281-286, models/mixtral/modeling_mixtral.py:119-137),
+the MoE path PHANTOM executes (python/phantom/phantom_cli.py:1393-1430), with
+the weights in packed int4 form. The stage functions (``router``,
+``dispatch``, ``expert_ffn_decode``, ``combine``, ``quantize_int4``) expose
+each kernel on its own for tests and for the expert-parallel path.
+
+All work is enqueued on ``torch.cuda.current_stream()``; nothing here
+synchronises the device. There is no CPU path: CPU tensors are rejected.
+"""
+
+from __future__ import annotations
+
+import threading
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}
+_PATHS = {"auto": _lib.PATH_AUTO, "decode": _lib.PATH_DECODE, "prefill": _lib.PATH_PREFILL}
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need_cuda(name: str, t: torch.Tensor) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (got {t.device}); phantom_moe has no CPU path")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _need_dtype(name: str, t: torch.Tensor, dtypes) -> None:
+    if t.dtype not in dtypes:
+        raise TypeError(f"{name} must have dtype in {[str(d) for d in dtypes]} (got {t.dtype})")
+
+
+def _need_shape(name: str, t: torch.Tensor, shape) -> None:
+    if tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} must have shape {tuple(shape)} (got {tuple(t.shape)})")
+
+
+class _Workspace:
+    """Per-(device, stream) scratch buffer, grown on demand through torch's
+    caching allocator. Calls on one stream are ordered, so they may share it."""
+
+    def __init__(self):
+        self._bufs: dict[tuple[int, int], torch.Tensor] = {}
+        self._lock = threading.Lock()
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        key = (device.index if device.index is not None else torch.cuda.current_device(), _stream())
+        with self._lock:
+            buf = self._bufs.get(key)
+            if buf is None or buf.numel() < nbytes:
+                buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+                self._bufs[key] = buf
+            return buf
+
+    def clear(self) -> None:
+        with self._lock:
+            self._bufs.clear()
+
+
+WORKSPACE = _Workspace()
+
+
+@dataclass
+class PackedExperts:
+    """Packed int4 expert weights for one layer.
+
+    w13_q [E, 2I, H/2] uint8 (gate rows 0..I-1, up rows I..2I-1, as
+    ``gate_up_proj`` is split by ``chunk(2)``, modeling_qwen3_moe.py:245),
+    w13_scales [E, 2I, H/G] fp16, w2_q [E, H, I/2] uint8, w2_scales [E, H, I/G] fp16.
+    """
+
+    w13_q: torch.Tensor
+    w13_scales: torch.Tensor
+    w2_q: torch.Tensor
+    w2_scales: torch.Tensor
+    group_size: int = 64
+
+    @property
+    def num_experts(self) -> int:
+        return self.w13_q.shape[0]
+
+    @property
+    def hidden_size(self) -> int:
+        return self.w2_q.shape[1]
+
+    @property
+    def intermediate_size(self) -> int:
+        return self.w13_q.shape[1] // 2
+
+
+def check_expert_weights(w13_q, w13_scales, w2_q, w2_scales, H: int, group_size: int):
+    """Validate packed expert tensors; returns (E, I)."""
+    for n, t in (("w13_q", w13_q), ("w13_scales", w13_scales), ("w2_q", w2_q), ("w2_scales", w2_scales)):
+        _need_cuda(n, t)
+    _need_dtype("w13_q", w13_q, (torch.uint8,))
+    _need_dtype("w2_q", w2_q, (torch.uint8,))
+    _need_dtype("w13_scales", w13_scales, (torch.float16,))
+    _need_dtype("w2_scales", w2_scales, (torch.float16,))
+    if group_size not in (32, 64):
+        raise ValueError(f"group_size must be 32 or 64 (got {group_size})")
+    if w13_q.dim() != 3:
+        raise ValueError("w13_q must be [E, 2I, H/2]")
+    E, I2, Hh = w13_q.shape
+    if I2 % 2:
+        raise ValueError("w13_q dim 1 must be 2*I")
+    I = I2 // 2
+    _need_shape("w13_q", w13_q, (E, 2 * I, H // 2))
+    _need_shape("w13_scales", w13_scales, (E, 2 * I, H // group_size))
+    _need_shape("w2_q", w2_q, (E, H, I // 2))
+    _need_shape("w2_scales", w2_scales, (E, H, I // group_size))
+    return E, I
+
+
+# ---------------------------------------------------------------------------
+# stage entry points
+# ---------------------------------------------------------------------------
+
+def router(x: torch.Tensor, router_weight: torch.Tensor, top_k: int, renormalize: bool = True,
+           return_probs: bool = False):
+    """Fused router (Qwen3MoeTopKRouter.forward, modeling_qwen3_moe.py:263-272).
+
+    Returns ``(topk_idx int32[T,k], topk_w fp32[T,k], logits fp32[T,E])`` and
+    ``probs fp32[T,E]`` when ``return_probs``.
+    """
+    _need_cuda("x", x)
+    _need_cuda("router_weight", router_weight)
+    _need_dtype("x", x, _DT)
+    _need_dtype("router_weight", router_weight, _DT)
+    T, H = x.shape
+    E = router_weight.shape[0]
+    _need_shape("router_weight", router_weight, (E, H))
+    dev = x.device
+    logits = torch.empty(T, E, dtype=torch.float32, device=dev)
+    probs = torch.empty(T, E, dtype=torch.float32, device=dev) if return_probs else None
+    idx = torch.empty(T, top_k, dtype=torch.int32, device=dev)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    _lib.call("phmoe_router", _ptr(x), _DT[x.dtype], _ptr(router_weight), _DT[router_weight.dtype],
+              T, H, E, top_k, int(bool(renormalize)), _ptr(logits), _ptr(probs), _ptr(idx), _ptr(w),
+              _stream())
+    if return_probs:
+        return idx, w, logits, probs
+    return idx, w, logits
+
+
+def dispatch(topk_idx: torch.Tensor, num_experts: int):
+    """Expert grouping ordered by token (modeling_qwen3_moe.py:234-244).
+
+    Returns ``(offsets int32[E+1], row_token int32[T*k], inv int32[T,k],
+    active int32[E+1])``; ``active[0]`` = experts hit, ``active[1:1+n]`` their ids.
+    """
+    _need_cuda("topk_idx", topk_idx)
+    _need_dtype("topk_idx", topk_idx, (torch.int32,))
+    T, k = topk_idx.shape
+    dev = topk_idx.device
+    E = int(num_experts)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    active = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    row_token = torch.empty(T * k, dtype=torch.int32, device=dev)
+    inv = torch.empty(T, k, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    nscr = lib.phmoe_dispatch_scratch_size(T, k, E)
+    scratch = torch.empty(max(nscr, 1), dtype=torch.uint8, device=dev)
+    _lib.call("phmoe_dispatch", _ptr(topk_idx), T, k, E, _ptr(offsets), _ptr(row_token), _ptr(inv),
+              _ptr(active), _ptr(scratch), nscr, _stream())
+    return offsets, row_token, inv, active
+
+
+def expert_ffn_decode(x: torch.Tensor, row_token, offsets, active, w13_q, w13_scales, w2_q,
+                      w2_scales, top_k: int, group_size: int = 64):
+    """Grouped SwiGLU FFN over dispatched rows (modeling_qwen3_moe.py:245-247).
+
+    ``row_token`` holds R rows (the token each row reads); returns y fp32[R, H]
+    in permuted-row order.
+    """
+    _need_cuda("x", x)
+    _need_dtype("x", x, _DT)
+    T, H = x.shape
+    E, I = check_expert_weights(w13_q, w13_scales, w2_q, w2_scales, H, group_size)
+    R = row_token.numel()
+    if R != T * top_k:
+        raise ValueError(f"row_token must have T*top_k = {T * top_k} rows (got {R})")
+    dev = x.device
+    h = torch.empty(max(R * I, 1), dtype=torch.float32, device=dev)
+    y = torch.empty(R, H, dtype=torch.float32, device=dev)
+    _lib.call("phmoe_expert_ffn_decode", _ptr(x), _DT[x.dtype], _ptr(row_token), _ptr(offsets),
+              _ptr(active), _ptr(w13_q), _ptr(w13_scales), _ptr(w2_q), _ptr(w2_scales), T, H, E,
+              top_k, I, group_size, _ptr(h), _ptr(y), _stream())
+    return y
+
+
+def combine(y: torch.Tensor, inv: torch.Tensor, topk_w: torch.Tensor, out_dtype=torch.bfloat16):
+    """out[t] = sum_j w[t,j] * y[inv[t,j]] (modeling_qwen3_moe.py:248-249)."""
+    _need_cuda("y", y)
+    T, k = inv.shape
+    H = y.shape[1]
+    out = torch.empty(T, H, dtype=out_dtype, device=y.device)
+    _lib.call("phmoe_combine", _ptr(y), _ptr(inv), _ptr(topk_w), T, k, H, _ptr(out), _DT[out_dtype],
+              _stream())
+    return out
+
+
+def quantize_int4(w: torch.Tensor, group_size: int = 64):
+    """GPU symmetric int4 group quantiser: ``w[..., K]`` (fp32/bf16, CUDA) ->
+    ``(packed uint8[..., K/2], scales fp16[..., K/G])``."""
+    _need_cuda("w", w)
+    _need_dtype("w", w, _DT)
+    K = w.shape[-1]
+    rows = w.numel() // K if K else 0
+    packed = torch.empty(*w.shape[:-1], K // 2, dtype=torch.uint8, device=w.device)
+    scales = torch.empty(*w.shape[:-1], K // group_size, dtype=torch.float16, device=w.device)
+    _lib.call("phmoe_quantize_int4", _ptr(w), _DT[w.dtype], rows, K, group_size, _ptr(packed),
+              _ptr(scales), _stream())
+    return packed, scales
+
+
+def pack_experts(gate_up_proj: torch.Tensor, down_proj: torch.Tensor, group_size: int = 64) -> PackedExperts:
+    """Quantise dense expert weights in transformers' layout
+    (``gate_up_proj [E, 2I, H]``, ``down_proj [E, H, I]``,
+    modeling_qwen3_moe.py:221-222) into :class:`PackedExperts` on the GPU."""
+    w13_q, w13_s = quantize_int4(gate_up_proj.contiguous(), group_size)
+    w2_q, w2_s = quantize_int4(down_proj.contiguous(), group_size)
+    return PackedExperts(w13_q, w13_s, w2_q, w2_s, group_size)
+
+
+# ---------------------------------------------------------------------------
+# the layer
+# ---------------------------------------------------------------------------
+
+def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: torch.Tensor,
+              w13_scales: torch.Tensor, w2_q: torch.Tensor, w2_scales: torch.Tensor, top_k: int,
+              renormalize: bool = True, group_size: int = 64, ep_group=None, *,
+              path: str = "auto", return_routing: bool = False, out: torch.Tensor | None = None):
+    """Sparse-MoE layer: router -> dispatch -> grouped int4 SwiGLU FFN -> combine.
+
+    ``hidden_states`` is ``[T, H]`` or ``[B, S, H]`` (bf16 or fp32); the result
+    has the same shape and dtype. ``router_weight`` is ``[E, H]`` (bf16/fp32).
+    With ``ep_group`` (a ``torch.distributed`` group of P > 1 ranks) the expert
+    tensors hold this rank's E/P experts and tokens are exchanged with NCCL
+    all-to-all (see :mod:`phantom_moe.ep`).
+
+    ``return_routing`` adds ``(topk_idx int32[T,k], topk_w fp32[T,k])``.
+    """
+    if ep_group is not None:
+        from . import ep as _ep
+        if _ep.group_size(ep_group) > 1:
+            return _ep.moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scales,
+                                    top_k, renormalize, group_size, ep_group, return_routing=return_routing)
+    _need_cuda("hidden_states", hidden_states)
+    _need_cuda("router_weight", router_weight)
+    _need_dtype("hidden_states", hidden_states, _DT)
+    _need_dtype("router_weight", router_weight, _DT)
+    shape = hidden_states.shape
+    H = shape[-1]
+    x = hidden_states.reshape(-1, H)
+    T = x.shape[0]
+    E, I = check_expert_weights(w13_q, w13_scales, w2_q, w2_scales, H, group_size)
+    _need_shape("router_weight", router_weight, (E, H))
+    if path not in _PATHS:
+        raise ValueError(f"path must be one of {list(_PATHS)}")
+    dev = x.device
+    if out is None:
+        out = torch.empty(T, H, dtype=x.dtype, device=dev)
+    else:
+        _need_cuda("out", out)
+        if out.dtype != x.dtype or out.numel() != T * H:
+            raise ValueError("out must match hidden_states in dtype and size")
+    idx = torch.empty(T, top_k, dtype=torch.int32, device=dev) if return_routing else None
+    wts = torch.empty(T, top_k, dtype=torch.float32, device=dev) if return_routing else None
+    lib = _lib.load()
+    need = lib.phmoe_workspace_size(T, H, E, top_k, I, _PATHS[path])
+    ws = WORKSPACE.get(dev, need)
+    _lib.call("phmoe_moe_layer", _ptr(x), _DT[x.dtype], _ptr(router_weight), _DT[router_weight.dtype],
+              _ptr(w13_q), _ptr(w13_scales), _ptr(w2_q), _ptr(w2_scales), T, H, E, top_k, I, group_size,
+              int(bool(renormalize)), _PATHS[path], _ptr(out), _ptr(idx), _ptr(wts), _ptr(ws), ws.numel(),
+              _stream())
+    out = out.reshape(shape)
+    if return_routing:
+        return out, idx, wts
+    return out

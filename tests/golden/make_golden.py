@@ -1,0 +1,188 @@
+"""Generate the golden fixtures under tests/golden/ from the REFERENCE code.
+
+Run from the repo root, in a container where the reference checkout and
+transformers 5.5.0 are importable:
+
+    python tests/golden/make_golden.py --reference /path/to/reference
+
+What each fixture pins, and which reference code produced it:
+
+* ``q4_0_kat.npz`` - GGUF Q4_0 dequantisation by the reference's own
+  ``GGUFLoader.dequantize_tensor`` (python/phantom/loader/gguf_loader.py:362-381,
+  CPU branch), on the known-answer block of tests/audit_suite.py:36-41
+  (nibbles 0x88, d = 1.5 -> zeros) and on 64 seeded random blocks.
+* ``router_phantom.npz`` - the reference's ``PhantomTopKRouter``
+  (tests/test_moe_routing.py:43-72) on the shapes of its own
+  ``test_router_correctness`` (x [2,4,256], 8 experts, top-2).
+* ``qwen3_block_small.npz`` / ``mixtral_block_small.npz`` - transformers'
+  ``Qwen3MoeSparseMoeBlock`` / ``MixtralSparseMoeBlock`` (the MoE code PHANTOM
+  executes, python/phantom/phantom_cli.py:1393-1430) in fp32 on CPU, with
+  expert weights set to the dequantised int4 values whose packed bytes are
+  stored alongside.
+* ``qwen3_cfg1.npz`` - the same Qwen3 block at BASELINE config 1 (H=2048,
+  128 experts, top-8, I=768, T=16, fp32 inputs drawn from
+  ``torch.Generator().manual_seed(0)``). The 320 MB of packed weights are
+  not stored: the fixture keeps sha256 digests of the regenerated inputs and
+  packed bytes, the block output, and the top-k indices/weights.
+
+Only this generator touches the reference; the tests read the .npz files.
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import logging
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(REPO))
+from oracle import moe_oracle as O  # noqa: E402
+
+OUT = Path(__file__).resolve().parent
+
+
+def sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def import_reference(ref: Path):
+    # python/phantom/loader/safetensors_loader.py imports structlog unguarded;
+    # a logging-backed stand-in lets the package import.
+    sys.modules.setdefault("structlog", types.SimpleNamespace(
+        get_logger=lambda *a, **k: logging.getLogger("phantom")))
+    sys.path.insert(0, str(ref / "python"))
+    sys.path.insert(0, str(ref / "tests"))
+    from phantom.loader.gguf_loader import GGUFLoader, GGUFQuantType  # noqa: E402
+    import test_moe_routing  # noqa: E402
+    return GGUFLoader, GGUFQuantType, test_moe_routing
+
+
+def make_q4_0(GGUFLoader, GGUFQuantType):
+    loader = GGUFLoader.__new__(GGUFLoader)
+    # audit_suite.py:36-41 known answer
+    kat_raw = np.array([1.5], dtype=np.float16).tobytes() + bytes([0x88] * 16)
+    kat_out = loader.dequantize_tensor(kat_raw, GGUFQuantType.Q4_0, (32,)).float().numpy()
+    rng = np.random.default_rng(1234)
+    n_blocks = 64
+    d = (rng.standard_normal(n_blocks) * 0.01).astype(np.float16)
+    qs = rng.integers(0, 256, size=(n_blocks, 16), dtype=np.uint8)
+    raw = b"".join(d[i:i + 1].tobytes() + qs[i].tobytes() for i in range(n_blocks))
+    out = loader.dequantize_tensor(raw, GGUFQuantType.Q4_0, (n_blocks * 32,)).float().numpy()
+    np.savez_compressed(OUT / "q4_0_kat.npz",
+                        kat_raw=np.frombuffer(kat_raw, dtype=np.uint8), kat_out=kat_out,
+                        raw=np.frombuffer(raw, dtype=np.uint8), out_bf16=out)
+
+
+def make_router_phantom(tmr):
+    torch.manual_seed(7)
+    router = tmr.PhantomTopKRouter(256, 8, 2)
+    x = torch.randn(2, 4, 256)
+    with torch.no_grad():
+        w, idx = router(x)
+    np.savez_compressed(OUT / "router_phantom.npz", x=x.numpy(), gate=router.gate.weight.detach().numpy(),
+                        weights=w.numpy(), indices=idx.numpy().astype(np.int32))
+
+
+def _tf_block(kind: str, H, E, k, I, renorm=True):
+    if kind == "qwen3":
+        from transformers.models.qwen3_moe.configuration_qwen3_moe import Qwen3MoeConfig
+        from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeSparseMoeBlock
+        cfg = Qwen3MoeConfig(hidden_size=H, num_experts=E, num_experts_per_tok=k,
+                             moe_intermediate_size=I, norm_topk_prob=renorm)
+        cfg._experts_implementation = "eager"
+        return Qwen3MoeSparseMoeBlock(cfg).eval()
+    from transformers.models.mixtral.configuration_mixtral import MixtralConfig
+    from transformers.models.mixtral.modeling_mixtral import MixtralSparseMoeBlock
+    cfg = MixtralConfig(hidden_size=H, num_local_experts=E, num_experts_per_tok=k, intermediate_size=I)
+    cfg._experts_implementation = "eager"
+    return MixtralSparseMoeBlock(cfg).eval()
+
+
+def run_tf_block(kind, x, wr, d13, d2, k, renorm=True):
+    E, I2, H = d13.shape
+    blk = _tf_block(kind, H, E, k, I2 // 2, renorm)
+    with torch.no_grad():
+        blk.gate.weight.copy_(torch.from_numpy(wr))
+        blk.experts.gate_up_proj.copy_(torch.from_numpy(d13))
+        blk.experts.down_proj.copy_(torch.from_numpy(d2))
+        xt = torch.from_numpy(x)
+        probs, scores, idx = blk.gate(xt)
+        out = blk(xt[None])
+        if isinstance(out, tuple):
+            out = out[0]
+    return (out[0].numpy().astype(np.float32), probs.numpy().astype(np.float32),
+            idx.numpy().astype(np.int32), scores.numpy().astype(np.float32))
+
+
+def make_small_block(kind, name, T, H, E, k, I, group, seed, keep_dense=False):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, H, generator=g).numpy()
+    wr = (torch.randn(E, H, generator=g) * 0.02).numpy()
+    w13 = (torch.randn(E, 2 * I, H, generator=g) * 0.02).numpy()
+    w2 = (torch.randn(E, H, I, generator=g) * 0.02).numpy()
+    p13, s13 = O.quantize_int4(w13, group)
+    p2, s2 = O.quantize_int4(w2, group)
+    d13 = O.dequantize_int4(p13, s13, group)
+    d2 = O.dequantize_int4(p2, s2, group)
+    out, probs, idx, scores = run_tf_block(kind, x, wr, d13, d2, k)
+    dense = dict(w13=w13, w2=w2) if keep_dense else {}
+    np.savez_compressed(OUT / name, x=x, wr=wr, w13_q=p13, w13_s=s13, w2_q=p2, w2_s=s2, **dense,
+                        group=np.int32(group), top_k=np.int32(k), out=out, probs=probs, idx=idx, scores=scores)
+
+
+def gen_cfg1_inputs():
+    """BASELINE config 1 inputs (documented procedure; the GPU tests repeat it)."""
+    g = torch.Generator().manual_seed(0)
+    T, H, E, I = 16, 2048, 128, 768
+    x = torch.randn(T, H, generator=g)
+    wr = torch.randn(E, H, generator=g) * 0.02
+    w13 = torch.randn(E, 2 * I, H, generator=g) * 0.02
+    w2 = torch.randn(E, H, I, generator=g) * 0.02
+    return x, wr, w13, w2
+
+
+def make_cfg1():
+    x, wr, w13, w2 = gen_cfg1_inputs()
+    E = w13.shape[0]
+    p13 = np.empty((E, w13.shape[1], w13.shape[2] // 2), np.uint8)
+    s13 = np.empty((E, w13.shape[1], w13.shape[2] // 64), np.float16)
+    p2 = np.empty((E, w2.shape[1], w2.shape[2] // 2), np.uint8)
+    s2 = np.empty((E, w2.shape[1], w2.shape[2] // 64), np.float16)
+    for e in range(E):
+        p13[e], s13[e] = O.quantize_int4(w13[e].numpy(), 64)
+        p2[e], s2[e] = O.quantize_int4(w2[e].numpy(), 64)
+    d13 = np.stack([O.dequantize_int4(p13[e], s13[e]) for e in range(E)])
+    d2 = np.stack([O.dequantize_int4(p2[e], s2[e]) for e in range(E)])
+    out, probs, idx, scores = run_tf_block("qwen3", x.numpy(), wr.numpy(), d13, d2, 8)
+    np.savez_compressed(
+        OUT / "qwen3_cfg1.npz", out=out, probs=probs, idx=idx, scores=scores,
+        sha_x=sha(x.numpy()), sha_wr=sha(wr.numpy()), sha_w13_q=sha(p13), sha_w13_s=sha(s13),
+        sha_w2_q=sha(p2), sha_w2_s=sha(s2))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--skip-cfg1", action="store_true", help="keep the existing qwen3_cfg1.npz")
+    args = ap.parse_args()
+    GGUFLoader, QT, tmr = import_reference(Path(args.reference))
+    make_q4_0(GGUFLoader, QT)
+    make_router_phantom(tmr)
+    make_small_block("qwen3", "qwen3_block_small.npz", T=12, H=128, E=16, k=4, I=64, group=64, seed=11,
+                     keep_dense=True)
+    make_small_block("qwen3", "qwen3_block_small_g32.npz", T=9, H=128, E=8, k=2, I=64, group=32, seed=12)
+    make_small_block("mixtral", "mixtral_block_small.npz", T=10, H=128, E=8, k=2, I=128, group=64, seed=13)
+    if not args.skip_cfg1:
+        make_cfg1()
+    for p in sorted(OUT.glob("*.npz")):
+        print(p.name, p.stat().st_size)
+
+
+if __name__ == "__main__":
+    main()

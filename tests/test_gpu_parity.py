@@ -1,0 +1,354 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle and the
+reference's golden outputs.
+
+Bars (from the north star): top-k indices and the dispatch permutation are
+bit-exact; layer outputs are within max-abs 2e-2 and mean-rel 5e-3 of the fp32
+CPU computation on the same dequantised weights. The router is additionally
+bit-exact in logits, probabilities and weights against the oracle's replay of
+its fixed reduction order.
+"""
+
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from oracle import moe_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = O.MAX_ABS_TOL   # 2e-2
+MEAN_REL = O.MEAN_REL_TOL  # 5e-3
+
+
+def cu(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t.to(dtype) if dtype is not None else t
+
+
+def f32_bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy().view(np.uint32)
+
+
+def np_bits(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+
+
+def bf16_np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy()
+
+
+# ---------------------------------------------------------------------------
+# router
+# ---------------------------------------------------------------------------
+
+def _check_router(x_t, wr_t, k, renorm=True):
+    import phantom_moe as pm
+    idx, w, logits, probs = pm.router(x_t, wr_t, k, renorm, return_probs=True)
+    torch.cuda.synchronize()
+    x = bf16_np(x_t)
+    wr = bf16_np(wr_t)
+    l_ref, p_ref, i_ref, w_ref = O.route_fixed_order(x, wr, k, renorm)
+    assert np.array_equal(f32_bits(logits), np_bits(l_ref)), "logits differ from fixed-order replay"
+    assert np.array_equal(f32_bits(probs), np_bits(p_ref)), "probs differ"
+    assert np.array_equal(idx.cpu().numpy(), i_ref), "top-k indices differ"
+    assert np.array_equal(f32_bits(w), np_bits(w_ref)), "routing weights differ"
+    return idx.cpu().numpy(), p_ref
+
+
+@pytest.mark.parametrize("T", [1, 4, 16, 64, 256])
+def test_router_cfg2_bf16_bitexact(cuda_device, T):
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(T, 2048, device="cuda", generator=g).to(torch.bfloat16)
+    wr = (torch.randn(128, 2048, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    idx, probs = _check_router(x, wr, 8)
+    # same experts as the plain fp32 semantics wherever the k-th/k+1-th gap is resolvable
+    _, _, i_plain, _ = O.route_reference(bf16_np(x), bf16_np(wr), 8)
+    safe = O.topk_margin(probs, 8) > 1e-5
+    assert np.array_equal(np.sort(idx[safe], 1), np.sort(i_plain[safe], 1))
+
+
+def test_router_cfg1_fp32_matches_transformers(cuda_device):
+    g = load_golden("qwen3_cfg1.npz")
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(16, 2048, generator=gen)
+    wr = torch.randn(128, 2048, generator=gen) * 0.02
+    idx, _ = _check_router(x.cuda(), wr.cuda(), 8)
+    assert np.array_equal(idx, g["idx"]), "indices differ from transformers' Qwen3MoeTopKRouter"
+
+
+@pytest.mark.parametrize("E,k,H,T,renorm", [(8, 2, 4096, 64, True), (256, 8, 512, 33, True),
+                                            (1000, 4, 256, 9, False), (8, 2, 256, 8, True),
+                                            (1, 1, 64, 5, True), (128, 8, 2056, 17, True)])
+def test_router_shapes(cuda_device, E, k, H, T, renorm):
+    g = torch.Generator(device="cuda").manual_seed(E * 7 + k)
+    x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
+    wr = (torch.randn(E, H, device="cuda", generator=g) * 0.02).float()
+    _check_router(x, wr, k, renorm)
+
+
+def test_router_phantom_golden(cuda_device):
+    g = load_golden("router_phantom.npz")
+    x = cu(g["x"].reshape(-1, 256))
+    idx, w, _ = __import__("phantom_moe").router(x, cu(g["gate"]), 2, True)
+    assert np.array_equal(idx.cpu().numpy(), g["indices"].reshape(-1, 2))
+    np.testing.assert_allclose(w.cpu().numpy(), g["weights"].reshape(-1, 2), atol=2e-6, rtol=0)
+
+
+def test_router_ties_prefer_lower_index(cuda_device):
+    """Duplicate router rows give bit-equal probabilities; the lower expert
+    index must win (torch.topk leaves this unspecified)."""
+    import phantom_moe as pm
+    E, H, T, k = 16, 256, 32, 3
+    g = torch.Generator(device="cuda").manual_seed(5)
+    wr = torch.randn(E, H, device="cuda", generator=g) * 0.02
+    wr[9] = wr[5]
+    wr[12] = wr[5]
+    wr[3] = wr[14]
+    x = torch.randn(T, H, device="cuda", generator=g)
+    x[:8] = wr[5] * 50.0  # these tokens strongly prefer the tied experts 5/9/12
+    idx, _, logits = pm.router(x, wr, k)
+    idx = idx.cpu().numpy()
+    assert np.array_equal(idx[:8], np.tile([5, 9, 12], (8, 1)))
+    _check_router(x, wr, k)
+    _check_router(x, wr, 1)
+
+
+# ---------------------------------------------------------------------------
+# dispatch
+# ---------------------------------------------------------------------------
+
+def _rand_idx(T, E, k, seed, zipf=None):
+    rng = np.random.default_rng(seed)
+    if zipf is None:
+        return np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32) if T else \
+            np.zeros((0, k), np.int32)
+    p = np.arange(1, E + 1, dtype=np.float64) ** (-zipf)
+    p /= p.sum()
+    return np.stack([rng.choice(E, size=k, replace=False, p=p) for _ in range(T)]).astype(np.int32)
+
+
+@pytest.mark.parametrize("T,E,k,zipf", [(1, 128, 8, None), (7, 16, 4, None), (256, 128, 8, None),
+                                        (2048, 128, 8, None), (2049, 128, 8, None),
+                                        (8192, 128, 8, 1.2), (4096, 8, 2, None), (300, 1024, 1, None),
+                                        (64, 1, 1, None), (3000, 64, 6, 2.0)])
+def test_dispatch_exact(cuda_device, T, E, k, zipf):
+    import phantom_moe as pm
+    idx = _rand_idx(T, E, k, seed=T + E, zipf=zipf)
+    offsets, row_token, inv, active = pm.dispatch(cu(idx), E)
+    counts_r, off_r, tok_r, slot_r, inv_r = O.dispatch(idx, E)
+    assert np.array_equal(offsets.cpu().numpy(), off_r)
+    assert np.array_equal(row_token.cpu().numpy(), tok_r)
+    assert np.array_equal(inv.cpu().numpy(), inv_r)
+    act = active.cpu().numpy()
+    hit = np.nonzero(counts_r)[0]
+    assert act[0] == hit.size and np.array_equal(act[1:1 + hit.size], hit)
+
+
+def test_dispatch_all_tokens_one_expert_set(cuda_device):
+    import phantom_moe as pm
+    T, E, k = 5000, 128, 8
+    idx = np.tile(np.array([3, 77, 5, 100, 0, 127, 64, 9], np.int32), (T, 1))
+    offsets, row_token, inv, active = pm.dispatch(cu(idx), E)
+    _, off_r, tok_r, _, inv_r = O.dispatch(idx, E)
+    assert np.array_equal(offsets.cpu().numpy(), off_r)
+    assert np.array_equal(row_token.cpu().numpy(), tok_r)
+    assert np.array_equal(inv.cpu().numpy(), inv_r)
+    assert active.cpu().numpy()[0] == 8
+
+
+# ---------------------------------------------------------------------------
+# quantiser
+# ---------------------------------------------------------------------------
+
+def test_quantizer_bytes_match_oracle(cuda_device):
+    import phantom_moe as pm
+    g = load_golden("qwen3_block_small.npz")
+    for G in (64, 32):
+        p, s = pm.quantize_int4(cu(g["w13"]), G)
+        p_ref, s_ref = O.quantize_int4(g["w13"], G)
+        assert np.array_equal(p.cpu().numpy(), p_ref)
+        assert np.array_equal(s.cpu().numpy(), s_ref)
+    wb = cu(g["w2"]).to(torch.bfloat16)
+    p, s = pm.quantize_int4(wb, 64)
+    p_ref, s_ref = O.quantize_int4(bf16_np(wb), 64)
+    assert np.array_equal(p.cpu().numpy(), p_ref) and np.array_equal(s.cpu().numpy(), s_ref)
+    z = torch.zeros(3, 128, device="cuda")
+    p, s = pm.quantize_int4(z, 64)
+    assert bool((p == 0x88).all()) and bool((s == 0).all())
+
+
+# ---------------------------------------------------------------------------
+# whole layer
+# ---------------------------------------------------------------------------
+
+def _packed_to_cuda(g):
+    return (cu(g["w13_q"]), cu(g["w13_s"]), cu(g["w2_q"]), cu(g["w2_s"]))
+
+
+@pytest.mark.parametrize("name", ["qwen3_block_small.npz", "qwen3_block_small_g32.npz",
+                                  "mixtral_block_small.npz"])
+@pytest.mark.parametrize("xdtype", [torch.float32, torch.bfloat16])
+def test_layer_small_golden(cuda_device, name, xdtype):
+    import phantom_moe as pm
+    g = load_golden(name)
+    G, k = int(g["group"]), int(g["top_k"])
+    x = cu(g["x"]).to(xdtype)
+    wr = cu(g["wr"])
+    out, idx, w = pm.moe_layer(x, wr, *_packed_to_cuda(g), k, True, G, return_routing=True)
+    torch.cuda.synchronize()
+    out = bf16_np(out)
+    if xdtype == torch.float32:
+        ref = g["out"]  # transformers' block output
+        assert np.array_equal(idx.cpu().numpy(), g["idx"])
+        mx, mr = O.parity_stats(out, ref)
+        assert mx < 1e-4 and mr < 1e-4, (mx, mr)
+    else:
+        ref, i_ref, _ = O.moe_layer_reference_packed(bf16_np(x), g["wr"], g["w13_q"], g["w13_s"],
+                                                     g["w2_q"], g["w2_s"], k, G)
+        assert np.array_equal(idx.cpu().numpy(), i_ref)
+    mx, mr = O.parity_stats(out, ref)
+    assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
+
+
+def _sha(t: torch.Tensor) -> str:
+    return hashlib.sha256(t.contiguous().cpu().numpy().tobytes()).hexdigest()
+
+
+@pytest.fixture(scope="module")
+def cfg1_layer(cuda_device):
+    """BASELINE config 1 on the GPU: inputs regenerated from seed 0 on the CPU,
+    experts quantised by the CUDA quantiser (digests pinned by the fixture)."""
+    import phantom_moe as pm
+    g = load_golden("qwen3_cfg1.npz")
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(16, 2048, generator=gen)
+    wr = torch.randn(128, 2048, generator=gen) * 0.02
+    w13 = torch.randn(128, 1536, 2048, generator=gen) * 0.02
+    w2 = torch.randn(128, 2048, 768, generator=gen) * 0.02
+    pk = pm.pack_experts(w13.cuda(), w2.cuda(), 64)
+    del w13, w2
+    return g, x, wr, pk
+
+
+def test_cfg1_quantiser_digests(cfg1_layer):
+    g, x, wr, pk = cfg1_layer
+    assert _sha(pk.w13_q) == str(g["sha_w13_q"])
+    assert _sha(pk.w13_scales) == str(g["sha_w13_s"])
+    assert _sha(pk.w2_q) == str(g["sha_w2_q"])
+    assert _sha(pk.w2_scales) == str(g["sha_w2_s"])
+
+
+def test_cfg1_layer_matches_transformers(cfg1_layer):
+    import phantom_moe as pm
+    g, x, wr, pk = cfg1_layer
+    out, idx, w = pm.moe_layer(x.cuda(), wr.cuda(), pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, 8,
+                               return_routing=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(idx.cpu().numpy(), g["idx"])
+    np.testing.assert_allclose(w.cpu().numpy(), g["scores"], atol=2e-6, rtol=0)
+    mx, mr = O.parity_stats(out.cpu().numpy(), g["out"])
+    assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
+    assert mx < 1e-3 and mr < 1e-4, (mx, mr)  # fp32 input: hi/lo split keeps ~16 bits
+
+
+@pytest.fixture(scope="module")
+def qwen3_bf16_weights(cuda_device):
+    """Config 2 weights: N(0, 0.02^2) experts, seed 1, int4 g64."""
+    import phantom_moe as pm
+    g = torch.Generator(device="cuda").manual_seed(1)
+    wr = (torch.randn(128, 2048, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    w13 = torch.randn(128, 1536, 2048, device="cuda", generator=g) * 0.02
+    pk13 = pm.quantize_int4(w13, 64)
+    del w13
+    w2 = torch.randn(128, 2048, 768, device="cuda", generator=g) * 0.02
+    pk2 = pm.quantize_int4(w2, 64)
+    del w2
+    pk = pm.PackedExperts(pk13[0], pk13[1], pk2[0], pk2[1], 64)
+    host = tuple(t.cpu().numpy() for t in (pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales))
+    return wr, pk, host
+
+
+@pytest.mark.parametrize("T", [1, 4, 16, 64, 256])
+def test_cfg2_layer_bf16_sweep(qwen3_bf16_weights, T):
+    import phantom_moe as pm
+    wr, pk, host = qwen3_bf16_weights
+    g = torch.Generator(device="cuda").manual_seed(100 + T)
+    x = torch.randn(T, 2048, device="cuda", generator=g).to(torch.bfloat16)
+    out, idx, w = pm.moe_layer(x, wr, pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, 8, return_routing=True)
+    torch.cuda.synchronize()
+    ref, i_ref, w_ref = O.moe_layer_reference_packed(bf16_np(x), bf16_np(wr), *host, 8, 64)
+    assert np.array_equal(idx.cpu().numpy(), i_ref)
+    assert np.array_equal(f32_bits(w), np_bits(w_ref))
+    mx, mr = O.parity_stats(bf16_np(out), ref)
+    assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
+
+
+def test_cfg5_zipf_skew_large_T(qwen3_bf16_weights):
+    """Config-5 shape: 8192 tokens with Zipf(1.2)-biased routing (hot experts
+    get hundreds of rows: the multi-pass token loop and the multi-CTA
+    dispatch). Checked on every token against the fp32 oracle."""
+    import phantom_moe as pm
+    wr, pk, host = qwen3_bf16_weights
+    T = 8192
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(T, 2048, device="cuda", generator=g).to(torch.bfloat16)
+    # bias the router: add log Zipf prior through an extra hidden direction
+    prior = torch.log(torch.arange(1, 129, device="cuda", dtype=torch.float32) ** -1.2)
+    x[:, 0] = 1.0
+    wr2 = wr.clone().float()
+    wr2[:, 0] = prior
+    wr2 = wr2.to(torch.bfloat16)
+    out, idx, w = pm.moe_layer(x, wr2, pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, 8, return_routing=True)
+    torch.cuda.synchronize()
+    counts = np.bincount(idx.cpu().numpy().reshape(-1), minlength=128)
+    assert counts.max() / counts.mean() > 8.0  # strongly skewed
+    ref, i_ref, _ = O.moe_layer_reference_packed(bf16_np(x), bf16_np(wr2), *host, 8, 64)
+    assert np.array_equal(idx.cpu().numpy(), i_ref)
+    mx, mr = O.parity_stats(bf16_np(out), ref)
+    assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
+
+
+def test_layer_deterministic_and_edge_cases(qwen3_bf16_weights):
+    import phantom_moe as pm
+    wr, pk, host = qwen3_bf16_weights
+    args = (pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, 8)
+    x = torch.randn(64, 2048, device="cuda").to(torch.bfloat16)
+    a = pm.moe_layer(x, wr, *args)
+    b = pm.moe_layer(x, wr, *args)
+    assert torch.equal(a, b)
+    # [B, S, H] input keeps its shape
+    y = pm.moe_layer(x.view(4, 16, 2048), wr, *args)
+    assert y.shape == (4, 16, 2048) and torch.equal(y.view(64, 2048), a)
+    # T = 0
+    e = pm.moe_layer(x[:0], wr, *args)
+    assert e.shape == (0, 2048)
+    # every token routed to the same 8 experts (one dominant direction)
+    wr3 = torch.zeros_like(wr)
+    wr3[[3, 17, 40, 41, 42, 90, 100, 127], :] = 0.05
+    xs = torch.rand(40, 2048, device="cuda").to(torch.bfloat16)
+    out, idx, w = pm.moe_layer(xs, wr3, *args, return_routing=True)
+    torch.cuda.synchronize()
+    assert set(np.unique(idx.cpu().numpy())) == {3, 17, 40, 41, 42, 90, 100, 127}
+    ref, i_ref, _ = O.moe_layer_reference_packed(bf16_np(xs), bf16_np(wr3), *host, 8, 64)
+    assert np.array_equal(idx.cpu().numpy(), i_ref)
+    mx, mr = O.parity_stats(bf16_np(out), ref)
+    assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
+
+
+def test_stage_functions_compose(qwen3_bf16_weights):
+    """router -> dispatch -> expert_ffn_decode -> combine equals moe_layer."""
+    import phantom_moe as pm
+    wr, pk, host = qwen3_bf16_weights
+    x = torch.randn(24, 2048, device="cuda").to(torch.bfloat16)
+    idx, w, _ = pm.router(x, wr, 8)
+    offsets, row_token, inv, active = pm.dispatch(idx, 128)
+    y = pm.expert_ffn_decode(x, row_token, offsets, active, pk.w13_q, pk.w13_scales, pk.w2_q,
+                             pk.w2_scales, 8)
+    out = pm.combine(y, inv, w, torch.bfloat16)
+    ref = pm.moe_layer(x, wr, pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, 8)
+    assert torch.equal(out, ref)
