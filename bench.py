@@ -158,6 +158,7 @@ def run_single_gpu(args, device):
         g = torch.Generator(device=device).manual_seed(1000 + T)
         xs = [torch.randn(T, H, device=device, generator=g).to(torch.bfloat16) for _ in range(L)]
         outs = [torch.empty(T, H, device=device, dtype=torch.bfloat16) for _ in range(L)]
+        wsp = torch.empty(pm.workspace_bytes(T, H, E, K_TOP, I), dtype=torch.uint8, device=device)
         # unique experts hit per layer (algorithmic bytes)
         U = []
         for l in range(L):
@@ -167,14 +168,14 @@ def run_single_gpu(args, device):
         # capture one graph per layer
         graphs = []
         with torch.cuda.stream(stream):
-            for l in range(L):  # warm the workspace for this stream
-                pm.moe_layer(xs[l], layers[l][0], *_pk(layers[l][1]), K_TOP, out=outs[l])
+            for l in range(L):  # warm-up outside capture
+                pm.moe_layer(xs[l], layers[l][0], *_pk(layers[l][1]), K_TOP, out=outs[l], workspace=wsp)
             stream.synchronize()
             n0 = lib.phmoe_kernel_launch_count()
             for l in range(L):
                 gr = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(gr, stream=stream):
-                    pm.moe_layer(xs[l], layers[l][0], *_pk(layers[l][1]), K_TOP, out=outs[l])
+                    pm.moe_layer(xs[l], layers[l][0], *_pk(layers[l][1]), K_TOP, out=outs[l], workspace=wsp)
                 graphs.append(gr)
             launches_per_step = (lib.phmoe_kernel_launch_count() - n0) / L
         K, W = args.steps, args.warmup
@@ -206,7 +207,7 @@ def run_single_gpu(args, device):
             f"layer {res['layer_GBps']:7.0f} GB/s gateup {res['gateup_GBps']:7.0f} GB/s U={mean_u:.1f} "
             f"stages(us) " + " ".join(f"{k}={v * 1e3:.1f}" for k, v in stage.items()))
         if T == args.tokens:
-            headline = dict(res, graphs=graphs, xs=xs, outs=outs, gateup_bytes=gateup_bytes)
+            headline = dict(res, graphs=graphs, xs=xs, outs=outs, wsp=wsp, gateup_bytes=gateup_bytes)
         else:
             del graphs
     return layers, results, headline

@@ -79,11 +79,22 @@ int check_router_dims(int T, int H, int E, int top_k) {
   return PHMOE_OK;
 }
 
+// The router stages an 8-token tile of x in shared memory (227 KB per CTA).
+int check_router_smem(int H, int x_dtype) {
+  const size_t bytes = (size_t)8 * H * (x_dtype == PHMOE_DTYPE_F32 ? 4 : 2);
+  if (bytes > 227 * 1024)
+    return fail(PHMOE_ERR_UNSUPPORTED, "H=%d too large for the router's token tile", H);
+  return PHMOE_OK;
+}
+
+// The FFN kernels copy scales in pairs of groups (4-byte async copies) and
+// tile the down projection in 128-row blocks.
 int check_ffn_dims(int H, int I, int G) {
   if (G != 32 && G != 64) return fail(PHMOE_ERR_UNSUPPORTED, "group_size must be 32 or 64 (got %d)", G);
-  if (H % 64) return fail(PHMOE_ERR_UNSUPPORTED, "H must be a multiple of 64 (got %d)", H);
-  if (I <= 0 || I % 16 || I % G)
-    return fail(PHMOE_ERR_UNSUPPORTED, "I must be a positive multiple of 16 and of group_size (got %d)", I);
+  if (H <= 0 || H % 128 || H % (2 * G))
+    return fail(PHMOE_ERR_UNSUPPORTED, "H must be a positive multiple of 128 and of 2*group_size (got %d)", H);
+  if (I <= 0 || I % 16 || I % (2 * G))
+    return fail(PHMOE_ERR_UNSUPPORTED, "I must be a positive multiple of 16 and of 2*group_size (got %d)", I);
   return PHMOE_OK;
 }
 
@@ -153,6 +164,7 @@ int phmoe_router(const void* x, int x_dtype, const void* router_w, int w_dtype, 
   g_last_error.clear();
   if (int s = check_router_dims(T, H, E, top_k)) return s;
   if (!dtype_ok(x_dtype) || !dtype_ok(w_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  if (int s = check_router_smem(H, x_dtype)) return s;
   if (T == 0) return PHMOE_OK;
   if (!x || !router_w || !logits || !topk_idx || !topk_w)
     return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
@@ -198,7 +210,7 @@ int phmoe_expert_ffn_decode(const void* x, int x_dtype, const int32_t* row_token
     return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
   if (!aligned(x, 16) || !aligned(w13_q, 16) || !aligned(w2_q, 16) || !aligned(h, 16) || !aligned(y, 16))
     return fail(PHMOE_ERR_ALIGNMENT, "x, weights, h and y must be 16-byte aligned");
-  if (!aligned(w13_s, 2) || !aligned(w2_s, 2)) return fail(PHMOE_ERR_ALIGNMENT, "scales must be 2-byte aligned");
+  if (!aligned(w13_s, 4) || !aligned(w2_s, 4)) return fail(PHMOE_ERR_ALIGNMENT, "scales must be 4-byte aligned");
   const int s = launch_ffn_decode(x, x_dtype, row_token, expert_offsets, active, w13_q, w13_s, w2_q,
                                   w2_s, T, H, E, top_k, I, group_size, h, y,
                                   static_cast<cudaStream_t>(stream));
@@ -228,6 +240,7 @@ int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtyp
   if (int s = check_router_dims(T, H, E, top_k)) return s;
   if (int s = check_ffn_dims(H, I, group_size)) return s;
   if (!dtype_ok(x_dtype) || !dtype_ok(w_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  if (int s = check_router_smem(H, x_dtype)) return s;
   if (path < PHMOE_PATH_AUTO || path > PHMOE_PATH_PREFILL)
     return fail(PHMOE_ERR_INVALID_ARG, "bad path code %d", path);
   if (path == PHMOE_PATH_PREFILL)
@@ -237,7 +250,7 @@ int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtyp
     return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
   if (!aligned(x, 16) || !aligned(router_w, 16) || !aligned(w13_q, 16) || !aligned(w2_q, 16) || !aligned(out, 16))
     return fail(PHMOE_ERR_ALIGNMENT, "x, router_w, packed weights and out must be 16-byte aligned");
-  if (!aligned(w13_s, 2) || !aligned(w2_s, 2)) return fail(PHMOE_ERR_ALIGNMENT, "scales must be 2-byte aligned");
+  if (!aligned(w13_s, 4) || !aligned(w2_s, 4)) return fail(PHMOE_ERR_ALIGNMENT, "scales must be 4-byte aligned");
   const Layout L = make_layout(T, H, E, top_k, I);
   if (!aligned(workspace, kAlign)) return fail(PHMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   if (workspace_bytes < L.total)

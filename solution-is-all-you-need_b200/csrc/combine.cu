@@ -36,15 +36,33 @@ combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv,
   const int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
   if (h >= H) return;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int j = 0; j < top_k; ++j) {
-    const int row = __ldg(inv + (size_t)t * top_k + j);
-    if (row < 0) continue;  // assignment dropped by dispatch (expert id out of range)
-    const float w = __ldg(topk_w + (size_t)t * top_k + j);
-    const float4 v = __ldg(reinterpret_cast<const float4*>(y + (size_t)row * H + h));
-    acc.x = fmaf(w, v.x, acc.x);
-    acc.y = fmaf(w, v.y, acc.y);
-    acc.z = fmaf(w, v.z, acc.z);
-    acc.w = fmaf(w, v.w, acc.w);
+  const int32_t* inv_t = inv + (size_t)t * top_k;
+  const float* w_t = topk_w + (size_t)t * top_k;
+  // Slots in batches of 8: all loads of a batch are issued before the sums,
+  // which then run in slot order.
+  for (int j0 = 0; j0 < top_k; j0 += 8) {
+    int row[8];
+    float w[8];
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const bool ok = j0 + u < top_k;
+      row[u] = ok ? __ldg(inv_t + j0 + u) : -1;  // -1 also marks a dropped assignment
+      w[u] = ok ? __ldg(w_t + j0 + u) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      v[u] = row[u] >= 0 ? __ldg(reinterpret_cast<const float4*>(y + (size_t)row[u] * H + h))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (row[u] >= 0) {
+        acc.x = fmaf(w[u], v[u].x, acc.x);
+        acc.y = fmaf(w[u], v[u].y, acc.y);
+        acc.z = fmaf(w[u], v[u].z, acc.z);
+        acc.w = fmaf(w[u], v[u].w, acc.w);
+      }
+    }
   }
   store4<OT>(out + (size_t)t * H + h, acc);
 }

@@ -19,6 +19,7 @@ from .layer import (
     pack_experts,
     quantize_int4,
     router,
+    workspace_bytes,
 )
 
 __all__ = [
@@ -33,6 +34,7 @@ __all__ = [
     "pack_experts",
     "quantize_int4",
     "router",
+    "workspace_bytes",
 ]
 
 __version__ = "0.1.0"

@@ -54,10 +54,17 @@ def _need_shape(name: str, t: torch.Tensor, shape) -> None:
 
 class _Workspace:
     """Per-(device, stream) scratch buffer, grown on demand through torch's
-    caching allocator. Calls on one stream are ordered, so they may share it."""
+    caching allocator. Calls on one stream are ordered, so they may share it.
+
+    A CUDA graph captured around ``moe_layer`` bakes the workspace address in,
+    so a buffer is never released once handed out: when a larger one is
+    needed the old one is kept in ``_retired`` for the life of the process
+    (or until :meth:`clear`, which the caller may only use when no captured
+    graph that used the workspace will be replayed again)."""
 
     def __init__(self):
         self._bufs: dict[tuple[int, int], torch.Tensor] = {}
+        self._retired: list[torch.Tensor] = []
         self._lock = threading.Lock()
 
     def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
@@ -65,6 +72,8 @@ class _Workspace:
         with self._lock:
             buf = self._bufs.get(key)
             if buf is None or buf.numel() < nbytes:
+                if buf is not None:
+                    self._retired.append(buf)
                 buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
                 self._bufs[key] = buf
             return buf
@@ -72,6 +81,7 @@ class _Workspace:
     def clear(self) -> None:
         with self._lock:
             self._bufs.clear()
+            self._retired.clear()
 
 
 WORKSPACE = _Workspace()
@@ -243,10 +253,19 @@ def pack_experts(gate_up_proj: torch.Tensor, down_proj: torch.Tensor, group_size
 # the layer
 # ---------------------------------------------------------------------------
 
+def workspace_bytes(T: int, H: int, E: int, top_k: int, I: int, path: str = "auto") -> int:
+    """Scratch bytes ``moe_layer`` needs for T tokens (``phmoe_workspace_size``)."""
+    n = _lib.load().phmoe_workspace_size(T, H, E, top_k, I, _PATHS[path])
+    if n == 0:
+        raise ValueError("invalid layer dimensions")
+    return int(n)
+
+
 def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: torch.Tensor,
               w13_scales: torch.Tensor, w2_q: torch.Tensor, w2_scales: torch.Tensor, top_k: int,
               renormalize: bool = True, group_size: int = 64, ep_group=None, *,
-              path: str = "auto", return_routing: bool = False, out: torch.Tensor | None = None):
+              path: str = "auto", return_routing: bool = False, out: torch.Tensor | None = None,
+              workspace: torch.Tensor | None = None):
     """Sparse-MoE layer: router -> dispatch -> grouped int4 SwiGLU FFN -> combine.
 
     ``hidden_states`` is ``[T, H]`` or ``[B, S, H]`` (bf16 or fp32); the result
@@ -256,6 +275,8 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
     all-to-all (see :mod:`phantom_moe.ep`).
 
     ``return_routing`` adds ``(topk_idx int32[T,k], topk_w fp32[T,k])``.
+    ``workspace`` (uint8 CUDA tensor of at least ``workspace_bytes(...)``)
+    overrides the per-stream cached scratch buffer.
     """
     if ep_group is not None:
         from . import ep as _ep
@@ -285,7 +306,14 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
     wts = torch.empty(T, top_k, dtype=torch.float32, device=dev) if return_routing else None
     lib = _lib.load()
     need = lib.phmoe_workspace_size(T, H, E, top_k, I, _PATHS[path])
-    ws = WORKSPACE.get(dev, need)
+    if workspace is None:
+        ws = WORKSPACE.get(dev, need)
+    else:
+        _need_cuda("workspace", workspace)
+        _need_dtype("workspace", workspace, (torch.uint8,))
+        if workspace.numel() < need:
+            raise ValueError(f"workspace needs {need} bytes (got {workspace.numel()})")
+        ws = workspace
     _lib.call("phmoe_moe_layer", _ptr(x), _DT[x.dtype], _ptr(router_weight), _DT[router_weight.dtype],
               _ptr(w13_q), _ptr(w13_scales), _ptr(w2_q), _ptr(w2_scales), T, H, E, top_k, I, group_size,
               int(bool(renormalize)), _PATHS[path], _ptr(out), _ptr(idx), _ptr(wts), _ptr(ws), ws.numel(),

@@ -131,7 +131,7 @@ def make_small_block(kind, name, T, H, E, k, I, group, seed, keep_dense=False):
     d13 = O.dequantize_int4(p13, s13, group)
     d2 = O.dequantize_int4(p2, s2, group)
     out, probs, idx, scores = run_tf_block(kind, x, wr, d13, d2, k)
-    dense = dict(w13=w13, w2=w2) if keep_dense else {}
+    dense = dict(w13=w13) if keep_dense else {}
     np.savez_compressed(OUT / name, x=x, wr=wr, w13_q=p13, w13_s=s13, w2_q=p2, w2_s=s2, **dense,
                         group=np.int32(group), top_k=np.int32(k), out=out, probs=probs, idx=idx, scores=scores)
 
@@ -174,7 +174,7 @@ def main():
     GGUFLoader, QT, tmr = import_reference(Path(args.reference))
     make_q4_0(GGUFLoader, QT)
     make_router_phantom(tmr)
-    make_small_block("qwen3", "qwen3_block_small.npz", T=12, H=128, E=16, k=4, I=64, group=64, seed=11,
+    make_small_block("qwen3", "qwen3_block_small.npz", T=12, H=128, E=16, k=4, I=128, group=64, seed=11,
                      keep_dense=True)
     make_small_block("qwen3", "qwen3_block_small_g32.npz", T=9, H=128, E=8, k=2, I=64, group=32, seed=12)
     make_small_block("mixtral", "mixtral_block_small.npz", T=10, H=128, E=8, k=2, I=128, group=64, seed=13)
