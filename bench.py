@@ -339,10 +339,12 @@ def run_ours(args):
     T = args.tokens
     res = results[T]
     peak, peak_kind = load_peaks()
-    achieved = hl["gateup_bytes"] / (res["stage_ms"]["ffn_gateup"] / 1e3) / 1e9
+    gateup_bytes = hl["gateup_bytes"]
+    achieved = gateup_bytes / (res["stage_ms"]["ffn_gateup"] / 1e3) / 1e9
     cpu = None
     if not args.no_cpu_baseline:
         del layers, hl
+        torch.cuda.synchronize()
         torch.cuda.empty_cache()
         cpu = cpu_baseline(host_layer0, T, args.cpu_budget)
     line = {
@@ -357,7 +359,7 @@ def run_ours(args):
                    "graph": "CUDA graph per layer", "sweep": {str(k): _sweep_entry(v) for k, v in results.items()}},
         "roofline": {"kernel": "ffn_gateup", "bound": "hbm", "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": load_traffic(T), "algorithmic_bytes_per_launch": hl["gateup_bytes"],
+                     "traffic": load_traffic(T), "algorithmic_bytes_per_launch": gateup_bytes,
                      "ffn_achieved": res["ffn_GBps"], "ffn_frac": res["ffn_GBps"] / peak},
         "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
         "gpu_launches": int(round(res["launches_per_step"] * args.steps)),

@@ -8,36 +8,37 @@
 //
 // Design. At decode sizes the layer streams ~2.5 MB of packed weights per
 // expert hit and does a few FMAs per weight: the bound is HBM. Both kernels
-// are persistent (one 256-thread CTA per SM) and run a 4-stage cp.async
-// pipeline: while the 8 warps compute task t, the packed int4 weights and
-// fp16 scales of tasks t+1..t+3 are in flight from HBM into shared memory
-// (~100 KB per SM), so memory latency is covered by the pipeline rather than
-// by occupancy. Weight rows are stored with a 32-byte (G=64) / 16-byte (G=32)
-// pad so that the fragment reads below are bank-conflict free.
+// are persistent (one 256-thread CTA per SM, a contiguous range of work items
+// each) and run a multi-stage cp.async pipeline over "tasks" (a work item's
+// K-chunk). A stage holds everything a task reads: the packed int4 weight
+// rows, their fp16 scales and the K-chunk of the activation rows (B). While
+// the 8 warps compute task t, tasks t+1.. are in flight from HBM/L2, so the
+// compute loop issues no global loads at all. Rows are padded so that every
+// fragment read below is bank-conflict free.
 //
 // From shared memory each lane reads the int4 bytes of its A fragments, turns
 // them into bf16 (nibble - 8) in registers (exact) and issues mma.sync
-// m16n8k16 with tokens as the N=8 side. The dequantised weights are never
-// written back to shared memory (bf16 would be 4x the int4 bytes). The fp16
-// group scale multiplies the fp32 partial of each group (exact factorisation).
-// Activations (B) are prefetched into registers one group ahead.
+// m16n8k16 with the 8 tokens of a pass as the N side. Dequantised weights are
+// never written back to shared memory (bf16 would be 4x the int4 bytes). The
+// fp16 group scale multiplies the fp32 partial of each group (exact).
 //
 // The K order inside a group is permuted identically for A and B (a dot
 // product does not depend on the order): for G=64 lane c of a quad holds
 // elements 8c..8c+7 (low nibbles) and 32+8c..32+8c+7 (high nibbles), exactly
-// the activations it loads with two 16-byte loads.
+// the activations it reads with two 16-byte loads.
 //
 // Precision: bf16 activations enter the MMA exactly; fp32 activations and the
 // intermediate h are split into bf16 hi + lo parts (two MMAs each), keeping
 // ~16 significant bits.
 //
-// gate/up kernel: item = (expert, token pass, 16 intermediate rows) -> 32
-//   weight rows (16 gate + 16 up); the 8 warps split K and are reduced through
-//   shared memory in warp order (deterministic); SwiGLU in the epilogue.
-// down kernel: item = (expert, token pass, 128 output rows); warp w owns rows
-//   16w..16w+15 over all of K.
-// A token pass covers up to 8*NCH of the expert's rows; experts with more
-// rows get more passes (more items).
+// gate/up kernel: item = (expert, 16 intermediate rows, pass of 8 tokens) ->
+//   32 weight rows (16 gate + 16 up); the 8 warps split each K-chunk and are
+//   reduced through shared memory in warp order (deterministic); SwiGLU in
+//   the epilogue, h stored as bf16 hi/lo planes.
+// down kernel: item = (expert, 128 output rows, pass); warp w owns rows
+//   16w..16w+15.
+// Items are ordered (expert, tile, pass) so the extra passes of an expert
+// with more than 8 rows re-read weights that are still in L2.
 #include "common.cuh"
 #include "launch.h"
 
@@ -47,7 +48,7 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 4;
+constexpr int kTok = 8;  // tokens per pass (the MMA N dimension)
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -68,9 +69,8 @@ __device__ __forceinline__ void cp_async_wait() {
 // fragments
 // ---------------------------------------------------------------------------
 
-// B fragments for one group and one 8-token chunk: per MMA step (2 per
-// 32-bit weight word: low then high nibbles) the two b registers, for the
-// "hi" part and (split inputs) the "lo" part.
+// B fragments of one group: per MMA step (2 per 32-bit weight word: low then
+// high nibbles) two b registers, for the "hi" part and (split inputs) "lo".
 template <int G>
 struct GroupB {
   static constexpr int kSteps = 2 * (G / 32);
@@ -78,28 +78,22 @@ struct GroupB {
   uint32_t lo[kSteps][2];
 };
 
-// Activations of one group (global group index g). Step order: word 0 low,
-// word 0 high, word 1 low, word 1 high. G=64: word w low covers elements
-// 8c+4w..+3, high covers 32+8c+4w..+3. G=32: low 4c..4c+3, high 16+4c..+3.
+// bf16 activations of one group from shared memory (p = row + group start).
+// Step order: word 0 low, word 0 high, word 1 low, word 1 high. G=64: word w
+// low covers elements 8c+4w..+3, high 32+8c+4w..+3. G=32: low 4c..4c+3,
+// high 16+4c..16+4c+3.
 template <int G>
-__device__ __forceinline__ void load_b_bf16(const __nv_bfloat16* row, int g, int c, bool ok,
-                                            uint32_t (&d)[GroupB<G>::kSteps][2]) {
+__device__ __forceinline__ void lds_b_bf16(const uint8_t* p, int c, uint32_t (&d)[GroupB<G>::kSteps][2]) {
   if constexpr (G == 64) {
-    uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
-    if (ok) {
-      x0 = __ldg(reinterpret_cast<const uint4*>(row + g * 64 + 8 * c));
-      x1 = __ldg(reinterpret_cast<const uint4*>(row + g * 64 + 32 + 8 * c));
-    }
+    const uint4 x0 = *reinterpret_cast<const uint4*>(p + 16 * c);
+    const uint4 x1 = *reinterpret_cast<const uint4*>(p + 64 + 16 * c);
     d[0][0] = x0.x; d[0][1] = x0.y;
     d[1][0] = x1.x; d[1][1] = x1.y;
     d[2][0] = x0.z; d[2][1] = x0.w;
     d[3][0] = x1.z; d[3][1] = x1.w;
   } else {
-    uint2 x0 = make_uint2(0, 0), x1 = make_uint2(0, 0);
-    if (ok) {
-      x0 = __ldg(reinterpret_cast<const uint2*>(row + g * 32 + 4 * c));
-      x1 = __ldg(reinterpret_cast<const uint2*>(row + g * 32 + 16 + 4 * c));
-    }
+    const uint2 x0 = *reinterpret_cast<const uint2*>(p + 8 * c);
+    const uint2 x1 = *reinterpret_cast<const uint2*>(p + 32 + 8 * c);
     d[0][0] = x0.x; d[0][1] = x0.y;
     d[1][0] = x1.x; d[1][1] = x1.y;
   }
@@ -111,37 +105,22 @@ __device__ __forceinline__ void split4(const float4 v, uint32_t& h0, uint32_t& h
   split_bf16x2(v.z, v.w, h1, l1);
 }
 
+// fp32 activations of one group from shared memory, split into hi/lo bf16.
 template <int G>
-__device__ __forceinline__ void load_b_f32(const float* row, int g, int c, bool ok, GroupB<G>& b) {
-  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+__device__ __forceinline__ void lds_b_f32(const uint8_t* p, int c, GroupB<G>& b) {
   if constexpr (G == 64) {
-    const float4* p0 = reinterpret_cast<const float4*>(row + g * 64 + 8 * c);
-    const float4* p1 = reinterpret_cast<const float4*>(row + g * 64 + 32 + 8 * c);
-    const float4 a0 = ok ? __ldg(p0) : z, a1 = ok ? __ldg(p0 + 1) : z;
-    const float4 c0 = ok ? __ldg(p1) : z, c1 = ok ? __ldg(p1 + 1) : z;
-    split4(a0, b.hi[0][0], b.hi[0][1], b.lo[0][0], b.lo[0][1]);
-    split4(c0, b.hi[1][0], b.hi[1][1], b.lo[1][0], b.lo[1][1]);
-    split4(a1, b.hi[2][0], b.hi[2][1], b.lo[2][0], b.lo[2][1]);
-    split4(c1, b.hi[3][0], b.hi[3][1], b.lo[3][0], b.lo[3][1]);
+    const float4* q0 = reinterpret_cast<const float4*>(p + 32 * c);
+    const float4* q1 = reinterpret_cast<const float4*>(p + 128 + 32 * c);
+    split4(q0[0], b.hi[0][0], b.hi[0][1], b.lo[0][0], b.lo[0][1]);
+    split4(q1[0], b.hi[1][0], b.hi[1][1], b.lo[1][0], b.lo[1][1]);
+    split4(q0[1], b.hi[2][0], b.hi[2][1], b.lo[2][0], b.lo[2][1]);
+    split4(q1[1], b.hi[3][0], b.hi[3][1], b.lo[3][0], b.lo[3][1]);
   } else {
-    const float4 a0 = ok ? __ldg(reinterpret_cast<const float4*>(row + g * 32 + 4 * c)) : z;
-    const float4 c0 = ok ? __ldg(reinterpret_cast<const float4*>(row + g * 32 + 16 + 4 * c)) : z;
+    const float4 a0 = *reinterpret_cast<const float4*>(p + 16 * c);
+    const float4 c0 = *reinterpret_cast<const float4*>(p + 64 + 16 * c);
     split4(a0, b.hi[0][0], b.hi[0][1], b.lo[0][0], b.lo[0][1]);
     split4(c0, b.hi[1][0], b.hi[1][1], b.lo[1][0], b.lo[1][1]);
   }
-}
-
-template <int G, typename XT>
-__device__ __forceinline__ void load_b_x(const XT* row, int g, int c, bool ok, GroupB<G>& b) {
-  if constexpr (std::is_same<XT, float>::value) load_b_f32<G>(row, g, c, ok, b);
-  else load_b_bf16<G>(row, g, c, ok, b.hi);
-}
-
-template <int G>
-__device__ __forceinline__ void load_b_planes(const __nv_bfloat16* hi_row, const __nv_bfloat16* lo_row,
-                                              int g, int c, bool ok, GroupB<G>& b) {
-  load_b_bf16<G>(hi_row, g, c, ok, b.hi);
-  load_b_bf16<G>(lo_row, g, c, ok, b.lo);
 }
 
 // Packed words of one row of one group for this lane, from shared memory.
@@ -162,7 +141,7 @@ __device__ __forceinline__ RowWords<G> lds_row(const uint8_t* p) {
   return r;
 }
 
-// tmp += A(rows r, r+8 of one group) * B(chunk), all MMA steps of the group.
+// tmp += A(rows r, r+8 of one group) * B, all MMA steps of the group.
 template <int G, bool kTwoParts>
 __device__ __forceinline__ void mma_group(float (&tmp)[4], const RowWords<G>& r0,
                                           const RowWords<G>& r8, const GroupB<G>& b) {
@@ -186,239 +165,234 @@ __device__ __forceinline__ void mma_group(float (&tmp)[4], const RowWords<G>& r0
 // work items
 // ---------------------------------------------------------------------------
 
-// table[s] = items of the active experts before slot s (s = 0..na); an
-// expert with n rows has ceil(n / tok_per_pass) passes of `tiles` items.
-// Every CTA builds the same table. Returns the total item count.
-__device__ int build_item_table(const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
-                                int tok_per_pass, int tiles, int* table) {
+// Per active slot s: expert id, first row, row count, and the prefix
+// table[s] of items before slot s (an expert with n rows has
+// tiles * ceil(n / 8) items). Every CTA builds the same copy in shared memory.
+struct Meta {
+  int* e;
+  int* row0;
+  int* n;
+  int* table;  // [na + 1]
+};
+
+__device__ int build_meta(const int32_t* __restrict__ offsets, const int32_t* __restrict__ active, int tiles,
+                          Meta m) {
   const int na = active[0];
+  for (int s = threadIdx.x; s < na; s += blockDim.x) {
+    const int e = active[1 + s];
+    const int r0 = offsets[e];
+    m.e[s] = e;
+    m.row0[s] = r0;
+    m.n[s] = offsets[e + 1] - r0;
+  }
+  __syncthreads();
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     int carry = 0;
     for (int s0 = 0; s0 < na; s0 += 32) {
       const int s = s0 + lane;
-      int v = 0;
-      if (s < na) {
-        const int e = active[1 + s];
-        const int n = offsets[e + 1] - offsets[e];
-        v = ((n + tok_per_pass - 1) / tok_per_pass) * tiles;
-      }
+      const int v = s < na ? ((m.n[s] + kTok - 1) / kTok) * tiles : 0;
       int incl = v;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const int t = __shfl_up_sync(0xffffffffu, incl, off);
         if (lane >= off) incl += t;
       }
-      if (s < na) table[s + 1] = carry + incl;
+      if (s < na) m.table[s + 1] = carry + incl;
       carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    if (lane == 0) table[0] = 0;
+    if (lane == 0) m.table[0] = 0;
   }
   __syncthreads();
-  return table[na];
+  return m.table[na];
 }
 
 struct Item {
   int e, row0, n, p0, tile;
 };
 
-__device__ __forceinline__ Item decode_item(int q, const int* table, const int32_t* __restrict__ offsets,
-                                            const int32_t* __restrict__ active, int tiles, int tok_per_pass) {
-  int lo = 0, hi = active[0];  // table[lo] <= q < table[hi]
+// Item q -> (slot, tile, pass); items of one slot are ordered tile-major so
+// the passes of a tile follow each other.
+__device__ __forceinline__ Item decode_item(int q, int na, int tiles, const Meta& m) {
+  int lo = 0, hi = na;  // table[lo] <= q < table[hi]
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (table[mid] <= q) lo = mid;
+    if (m.table[mid] <= q) lo = mid;
     else hi = mid;
   }
-  const int local = q - table[lo];
-  const int pass = local / tiles;
+  const int local = q - m.table[lo];
   Item it;
-  it.e = active[1 + lo];
-  it.row0 = offsets[it.e];
-  it.n = offsets[it.e + 1] - it.row0;
-  it.p0 = pass * tok_per_pass;
-  it.tile = local - pass * tiles;
+  it.e = m.e[lo];
+  it.row0 = m.row0[lo];
+  it.n = m.n[lo];
+  const int passes = (it.n + kTok - 1) / kTok;
+  it.tile = local / passes;
+  it.p0 = (local - it.tile * passes) * kTok;
   return it;
+}
+
+__device__ __forceinline__ void cta_range(int total, int& q0, int& q1) {
+  q0 = (int)((long long)total * blockIdx.x / gridDim.x);
+  q1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
 }
 
 // ---------------------------------------------------------------------------
 // gate/up + SwiGLU
 // ---------------------------------------------------------------------------
-template <int G>
+template <int G, typename XT>
 struct GateUpCfg {
+  static constexpr bool kF32 = std::is_same<XT, float>::value;
+  static constexpr int kStages = 5;
   static constexpr int kRows = 32;
-  static constexpr int kKch = 2048;  // K elements per task
-  static constexpr int kStride = kKch / 2 + (G == 64 ? 32 : 16);
-  static constexpr int kScaleRow = kKch / G * 2;  // scale bytes per row per task
-  static constexpr int kWBytes = kRows * kStride;
-  static constexpr int kStage = kWBytes + kRows * kScaleRow;
+  static constexpr int kKch = kF32 ? 512 : 1024;                   // K elements per task
+  static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);  // conflict-free A reads
+  static constexpr int kScaleRow = kKch / G * 2;
+  static constexpr int kBRowBytes = kKch * (int)sizeof(XT);
+  static constexpr int kBPad = kF32 ? (G == 64 ? 16 : 64) : (G == 64 ? 64 : 32);
+  static constexpr int kBStride = kBRowBytes + kBPad;              // conflict-free B reads
+  static constexpr int kW = 0;
+  static constexpr int kS = kRows * kWStride;
+  static constexpr int kB = kS + kRows * kScaleRow;
+  static constexpr int kStage = (kB + kTok * kBStride + 127) / 128 * 128;
+  static constexpr int kRed = kWarps * 8 * 32 * 4;
 };
 
-template <int G, typename XT, int NCH>
+template <int G, typename XT>
 __global__ void __launch_bounds__(kThreads, 1)
 ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_token,
                   const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                   const uint8_t* __restrict__ w13_q, const uint16_t* __restrict__ w13_s, int H, int I,
-                  __nv_bfloat16* __restrict__ h_hi, __nv_bfloat16* __restrict__ h_lo) {
-  using C = GateUpCfg<G>;
-  constexpr bool kTwo = std::is_same<XT, float>::value;
-  constexpr int kTok = 8 * NCH;
+                  int E, __nv_bfloat16* __restrict__ h_hi, __nv_bfloat16* __restrict__ h_lo) {
+  using C = GateUpCfg<G, XT>;
+  constexpr int S = C::kStages;
   extern __shared__ __align__(128) uint8_t smem[];
-  float* red = reinterpret_cast<float*>(smem + kStages * C::kStage);  // [kWarps][NCH*8][32]
-  int* table = reinterpret_cast<int*>(red + kWarps * NCH * 8 * 32);
+  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [kWarps][8][32]
+  int* mbase = reinterpret_cast<int*>(smem + S * C::kStage + C::kRed);
+  const Meta meta{mbase, mbase + E, mbase + 2 * E, mbase + 3 * E};
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
   const int tiles = I / 16;
   const int NG = H / G;
   const int nkc = (H + C::kKch - 1) / C::kKch;
   const size_t row_bytes = (size_t)H / 2;
+  const int na = active[0];
 
-  const int total = build_item_table(offsets, active, kTok, tiles, table);
-  const int my_items = blockIdx.x < total ? (total - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-  const int my_tasks = my_items * nkc;
+  const int total = build_meta(offsets, active, tiles, meta);
+  int q0, q1;
+  cta_range(total, q0, q1);
+  const int ntask = (q1 - q0) * nkc;
 
-  auto issue = [&](int task) {
-    const int j = task / nkc, kc = task - j * nkc;
-    const Item it = decode_item(blockIdx.x + j * gridDim.x, table, offsets, active, tiles, kTok);
-    uint8_t* st = smem + (task % kStages) * C::kStage;
+  // B-copy assignment of this thread: token bn, 16-byte chunks bc, bc+32, ...
+  const int bn = threadIdx.x >> 5;
+  const int bc = threadIdx.x & 31;
+  auto token_of = [&](int task) -> int {
+    if (task >= ntask) return -1;
+    const Item it = decode_item(q0 + task / nkc, na, tiles, meta);
+    const int rr = it.p0 + bn;
+    return rr < it.n ? __ldg(row_token + it.row0 + rr) : -1;
+  };
+  auto issue = [&](int task, int tok) {
+    const int kc = task % nkc;
+    const Item it = decode_item(q0 + task / nkc, na, tiles, meta);
+    uint8_t* st = smem + (task % S) * C::kStage;
     const int k0 = kc * C::kKch;
     const int kel = min(C::kKch, H - k0);
-    const int nch16 = kel / 32;  // 16-byte chunks per row
     const size_t erow = (size_t)it.e * 2 * I;
     const int i0 = it.tile * 16;
-    for (int q = threadIdx.x; q < C::kRows * nch16; q += kThreads) {
-      const int rr = q / nch16, cc = q - rr * nch16;
+    const int wch = kel / 32;  // 16-byte chunks of packed weights per row
+    for (int q = threadIdx.x; q < C::kRows * wch; q += kThreads) {
+      const int rr = q / wch, cc = q - rr * wch;
       const size_t grow = erow + (rr < 16 ? i0 + rr : I + i0 + rr - 16);
-      cp_async16(smem_u32(st + rr * C::kStride + cc * 16), w13_q + grow * row_bytes + k0 / 2 + cc * 16);
+      cp_async16(smem_u32(st + C::kW + rr * C::kWStride + cc * 16), w13_q + grow * row_bytes + k0 / 2 + cc * 16);
     }
     const int npair = kel / G / 2;
-    uint8_t* sc = st + C::kWBytes;
     for (int q = threadIdx.x; q < C::kRows * npair; q += kThreads) {
       const int rr = q / npair, pp = q - rr * npair;
       const size_t grow = erow + (rr < 16 ? i0 + rr : I + i0 + rr - 16);
-      cp_async4(smem_u32(sc + rr * C::kScaleRow + pp * 4), w13_s + grow * NG + k0 / G + 2 * pp);
+      cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + grow * NG + k0 / G + 2 * pp);
+    }
+    if (tok >= 0) {
+      const int bch = kel * (int)sizeof(XT) / 16;
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(x + (size_t)tok * H + k0);
+      for (int cc = bc; cc < bch; cc += 32)
+        cp_async16(smem_u32(st + C::kB + bn * C::kBStride + cc * 16), src + cc * 16);
     }
   };
 
-#pragma unroll
-  for (int s = 0; s < kStages - 1; ++s) {
-    if (s < my_tasks) issue(s);
+  for (int s = 0; s < S - 1; ++s) {
+    if (s < ntask) issue(s, token_of(s));
     cp_async_commit();
   }
+  int next_tok = token_of(S - 1);
 
-  float acc[NCH][2][4];
-  for (int task = 0; task < my_tasks; ++task) {
-    if (task + kStages - 1 < my_tasks) issue(task + kStages - 1);
+  float acc[2][4];
+  for (int task = 0; task < ntask; ++task) {
+    if (task + S - 1 < ntask) issue(task + S - 1, next_tok);
     cp_async_commit();
-    const int j = task / nkc, kc = task - j * nkc;
-    const Item it = decode_item(blockIdx.x + j * gridDim.x, table, offsets, active, tiles, kTok);
+    next_tok = token_of(task + S);  // consumed by the next iteration's issue
+    const int kc = task % nkc;
+    const Item it = decode_item(q0 + task / nkc, na, tiles, meta);
     if (kc == 0) {
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) { acc[ch][0][q] = 0.f; acc[ch][1][q] = 0.f; }
+      for (int q = 0; q < 4; ++q) { acc[0][q] = 0.f; acc[1][q] = 0.f; }
     }
-    const int nvch = min(NCH, (it.n - it.p0 + 7) / 8);  // chunks holding tokens
-    const XT* xrow[NCH];
-    bool xok[NCH];
-#pragma unroll
-    for (int ch = 0; ch < NCH; ++ch) {
-      const int rr = it.p0 + ch * 8 + r;
-      xok[ch] = rr < it.n;
-      xrow[ch] = x + (size_t)(xok[ch] ? row_token[it.row0 + rr] : 0) * H;
-    }
-    const int k0 = kc * C::kKch;
-    const int ngt = min(C::kKch, H - k0) / G;
-    const int kg0 = k0 / G;
-    GroupB<G> b0[NCH], b1[NCH];
-    if (warp < ngt) {
-#pragma unroll
-      for (int ch = 0; ch < NCH; ++ch)
-        if (ch < nvch) load_b_x<G, XT>(xrow[ch], kg0 + warp, c, xok[ch], b0[ch]);
-    }
-    cp_async_wait<kStages - 1>();
+    const int ngt = min(C::kKch, H - kc * C::kKch) / G;
+    cp_async_wait<S - 1>();
     __syncthreads();
-    const uint8_t* st = smem + (task % kStages) * C::kStage;
-    const __half* sc = reinterpret_cast<const __half*>(st + C::kWBytes);
+    const uint8_t* st = smem + (task % S) * C::kStage;
+    const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
     constexpr int kScH = C::kScaleRow / 2;
-    const int lane_off = (G == 64) ? 8 * c : 4 * c;
-
-    auto compute = [&](int g, const GroupB<G> (&b)[NCH]) {
-      const uint8_t* base = st + g * (G / 2) + lane_off;
-      const RowWords<G> ag0 = lds_row<G>(base + r * C::kStride);
-      const RowWords<G> ag8 = lds_row<G>(base + (r + 8) * C::kStride);
-      const RowWords<G> au0 = lds_row<G>(base + (16 + r) * C::kStride);
-      const RowWords<G> au8 = lds_row<G>(base + (24 + r) * C::kStride);
+    const int a_off = (G == 64) ? 8 * c : 4 * c;
+    for (int g = warp; g < ngt; g += kWarps) {
+      const uint8_t* ab = st + C::kW + g * (G / 2) + a_off;
+      const RowWords<G> ag0 = lds_row<G>(ab + r * C::kWStride);
+      const RowWords<G> ag8 = lds_row<G>(ab + (r + 8) * C::kWStride);
+      const RowWords<G> au0 = lds_row<G>(ab + (16 + r) * C::kWStride);
+      const RowWords<G> au8 = lds_row<G>(ab + (24 + r) * C::kWStride);
+      GroupB<G> b;
+      const uint8_t* bb = st + C::kB + r * C::kBStride + g * G * (int)sizeof(XT);
+      if constexpr (C::kF32) lds_b_f32<G>(bb, c, b);
+      else lds_b_bf16<G>(bb, c, b.hi);
+      float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_group<G, C::kF32>(tg, ag0, ag8, b);
+      mma_group<G, C::kF32>(tu, au0, au8, b);
       const float sg0 = __half2float(sc[r * kScH + g]);
       const float sg8 = __half2float(sc[(r + 8) * kScH + g]);
       const float su0 = __half2float(sc[(16 + r) * kScH + g]);
       const float su8 = __half2float(sc[(24 + r) * kScH + g]);
-#pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) {
-        if (ch < nvch) {
-          float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f};
-          mma_group<G, kTwo>(tg, ag0, ag8, b[ch]);
-          mma_group<G, kTwo>(tu, au0, au8, b[ch]);
-          acc[ch][0][0] = fmaf(sg0, tg[0], acc[ch][0][0]);
-          acc[ch][0][1] = fmaf(sg0, tg[1], acc[ch][0][1]);
-          acc[ch][0][2] = fmaf(sg8, tg[2], acc[ch][0][2]);
-          acc[ch][0][3] = fmaf(sg8, tg[3], acc[ch][0][3]);
-          acc[ch][1][0] = fmaf(su0, tu[0], acc[ch][1][0]);
-          acc[ch][1][1] = fmaf(su0, tu[1], acc[ch][1][1]);
-          acc[ch][1][2] = fmaf(su8, tu[2], acc[ch][1][2]);
-          acc[ch][1][3] = fmaf(su8, tu[3], acc[ch][1][3]);
-        }
-      }
-    };
-
-    // groups g = warp, warp+8, ...; B for the next group is in flight while
-    // the current one computes.
-    for (int g = warp; g < ngt; g += 2 * kWarps) {
-      const int g1 = g + kWarps, g2 = g + 2 * kWarps;
-      if (g1 < ngt) {
-#pragma unroll
-        for (int ch = 0; ch < NCH; ++ch)
-          if (ch < nvch) load_b_x<G, XT>(xrow[ch], kg0 + g1, c, xok[ch], b1[ch]);
-      }
-      compute(g, b0);
-      if (g1 < ngt) {
-        if (g2 < ngt) {
-#pragma unroll
-          for (int ch = 0; ch < NCH; ++ch)
-            if (ch < nvch) load_b_x<G, XT>(xrow[ch], kg0 + g2, c, xok[ch], b0[ch]);
-        }
-        compute(g1, b1);
-      }
+      acc[0][0] = fmaf(sg0, tg[0], acc[0][0]);
+      acc[0][1] = fmaf(sg0, tg[1], acc[0][1]);
+      acc[0][2] = fmaf(sg8, tg[2], acc[0][2]);
+      acc[0][3] = fmaf(sg8, tg[3], acc[0][3]);
+      acc[1][0] = fmaf(su0, tu[0], acc[1][0]);
+      acc[1][1] = fmaf(su0, tu[1], acc[1][1]);
+      acc[1][2] = fmaf(su8, tu[2], acc[1][2]);
+      acc[1][3] = fmaf(su8, tu[3], acc[1][3]);
     }
-
     if (kc == nkc - 1) {
       // reduce the 8 K-slices in warp order, then SwiGLU
-      float* mine = red + (size_t)warp * NCH * 8 * 32;
+      float* mine = red + warp * 8 * 32;
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          mine[(ch * 8 + q) * 32 + lane] = acc[ch][0][q];
-          mine[(ch * 8 + 4 + q) * 32 + lane] = acc[ch][1][q];
-        }
+      for (int q = 0; q < 4; ++q) {
+        mine[q * 32 + lane] = acc[0][q];
+        mine[(4 + q) * 32 + lane] = acc[1][q];
+      }
       __syncthreads();
-      if (warp < nvch) {
-        const int ch = warp;
+      if (warp == 0) {
         float gs[4] = {0.f, 0.f, 0.f, 0.f}, us[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) {
-          const float* src = red + (size_t)w * NCH * 8 * 32;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            gs[q] += src[(ch * 8 + q) * 32 + lane];
-            us[q] += src[(ch * 8 + 4 + q) * 32 + lane];
+            gs[q] += red[w * 256 + q * 32 + lane];
+            us[q] += red[w * 256 + (4 + q) * 32 + lane];
           }
         }
         const int i0 = it.tile * 16;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int i = i0 + r + (q >= 2 ? 8 : 0);
-          const int rr = it.p0 + ch * 8 + 2 * c + (q & 1);
+          const int rr = it.p0 + 2 * c + (q & 1);
           if (rr < it.n) {
             const float hv = silu_f32(gs[q]) * us[q];
             const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
@@ -430,7 +404,7 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
         }
       }
     }
-    __syncthreads();  // stage (task % kStages) and `red` are free again
+    __syncthreads();  // stage (task % S) and `red` are free again
   }
   cp_async_wait<0>();
 }
@@ -440,196 +414,160 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
 // ---------------------------------------------------------------------------
 template <int G>
 struct DownCfg {
+  static constexpr int kStages = 3;
   static constexpr int kRows = 128;
   static constexpr int kKch = 512;
-  static constexpr int kStride = kKch / 2 + (G == 64 ? 32 : 16);
+  static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);
   static constexpr int kScaleRow = kKch / G * 2;
-  static constexpr int kWBytes = kRows * kStride;
-  static constexpr int kStage = kWBytes + kRows * kScaleRow;
+  static constexpr int kBRowBytes = kKch * 2;  // one bf16 plane
+  static constexpr int kBStride = kBRowBytes + (G == 64 ? 64 : 32);
+  static constexpr int kW = 0;
+  static constexpr int kS = kRows * kWStride;
+  static constexpr int kB = kS + kRows * kScaleRow;             // [2 planes][kTok][kBStride]
+  static constexpr int kStage = (kB + 2 * kTok * kBStride + 127) / 128 * 128;
 };
 
-template <int G, int NCH>
+template <int G>
 __global__ void __launch_bounds__(kThreads, 1)
 ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __restrict__ h_lo,
                 const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
-                const uint8_t* __restrict__ w2_q, const uint16_t* __restrict__ w2_s, int H, int I,
+                const uint8_t* __restrict__ w2_q, const uint16_t* __restrict__ w2_s, int H, int I, int E,
                 float* __restrict__ y) {
   using C = DownCfg<G>;
-  constexpr int kTok = 8 * NCH;
+  constexpr int S = C::kStages;
   extern __shared__ __align__(128) uint8_t smem[];
-  int* table = reinterpret_cast<int*>(smem + kStages * C::kStage);
+  int* mbase = reinterpret_cast<int*>(smem + S * C::kStage);
+  const Meta meta{mbase, mbase + E, mbase + 2 * E, mbase + 3 * E};
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
   const int tiles = H / C::kRows;
   const int NG = I / G;
   const int nkc = (I + C::kKch - 1) / C::kKch;
   const size_t row_bytes = (size_t)I / 2;
+  const int na = active[0];
 
-  const int total = build_item_table(offsets, active, kTok, tiles, table);
-  const int my_items = blockIdx.x < total ? (total - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-  const int my_tasks = my_items * nkc;
+  const int total = build_meta(offsets, active, tiles, meta);
+  int q0, q1;
+  cta_range(total, q0, q1);
+  const int ntask = (q1 - q0) * nkc;
 
   auto issue = [&](int task) {
-    const int j = task / nkc, kc = task - j * nkc;
-    const Item it = decode_item(blockIdx.x + j * gridDim.x, table, offsets, active, tiles, kTok);
-    uint8_t* st = smem + (task % kStages) * C::kStage;
+    const int kc = task % nkc;
+    const Item it = decode_item(q0 + task / nkc, na, tiles, meta);
+    uint8_t* st = smem + (task % S) * C::kStage;
     const int k0 = kc * C::kKch;
     const int kel = min(C::kKch, I - k0);
-    const int nch16 = kel / 32;
     const size_t rbase = (size_t)it.e * H + (size_t)it.tile * C::kRows;
-    for (int q = threadIdx.x; q < C::kRows * nch16; q += kThreads) {
-      const int rr = q / nch16, cc = q - rr * nch16;
-      cp_async16(smem_u32(st + rr * C::kStride + cc * 16), w2_q + (rbase + rr) * row_bytes + k0 / 2 + cc * 16);
+    const int wch = kel / 32;
+    for (int q = threadIdx.x; q < C::kRows * wch; q += kThreads) {
+      const int rr = q / wch, cc = q - rr * wch;
+      cp_async16(smem_u32(st + C::kW + rr * C::kWStride + cc * 16), w2_q + (rbase + rr) * row_bytes + k0 / 2 + cc * 16);
     }
     const int npair = kel / G / 2;
-    uint8_t* sc = st + C::kWBytes;
     for (int q = threadIdx.x; q < C::kRows * npair; q += kThreads) {
       const int rr = q / npair, pp = q - rr * npair;
-      cp_async4(smem_u32(sc + rr * C::kScaleRow + pp * 4), w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
+      cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
+    }
+    // h rows of the pass (both planes), this K-chunk
+    const int nt = min(kTok, it.n - it.p0);
+    const int bch = kel * 2 / 16;
+    for (int q = threadIdx.x; q < 2 * nt * bch; q += kThreads) {
+      const int pl = q / (nt * bch);
+      const int rem = q - pl * nt * bch;
+      const int n = rem / bch, cc = rem - n * bch;
+      const __nv_bfloat16* src = (pl ? h_lo : h_hi) + (size_t)(it.row0 + it.p0 + n) * I + k0;
+      cp_async16(smem_u32(st + C::kB + (pl * kTok + n) * C::kBStride + cc * 16),
+                 reinterpret_cast<const uint8_t*>(src) + cc * 16);
     }
   };
 
-#pragma unroll
-  for (int s = 0; s < kStages - 1; ++s) {
-    if (s < my_tasks) issue(s);
+  for (int s = 0; s < S - 1; ++s) {
+    if (s < ntask) issue(s);
     cp_async_commit();
   }
 
-  float acc[NCH][4];
+  float acc[4];
   const int lr0 = warp * 16 + r;
-  for (int task = 0; task < my_tasks; ++task) {
-    if (task + kStages - 1 < my_tasks) issue(task + kStages - 1);
+  for (int task = 0; task < ntask; ++task) {
+    if (task + S - 1 < ntask) issue(task + S - 1);
     cp_async_commit();
-    const int j = task / nkc, kc = task - j * nkc;
-    const Item it = decode_item(blockIdx.x + j * gridDim.x, table, offsets, active, tiles, kTok);
+    const int kc = task % nkc;
+    const Item it = decode_item(q0 + task / nkc, na, tiles, meta);
     if (kc == 0) {
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) acc[ch][q] = 0.f;
+      for (int q = 0; q < 4; ++q) acc[q] = 0.f;
     }
-    const int nvch = min(NCH, (it.n - it.p0 + 7) / 8);
-    const __nv_bfloat16* hr[NCH];
-    const __nv_bfloat16* lr[NCH];
-    bool ok[NCH];
-#pragma unroll
-    for (int ch = 0; ch < NCH; ++ch) {
-      const int rr = it.p0 + ch * 8 + r;
-      ok[ch] = rr < it.n;
-      const size_t off = (size_t)(it.row0 + (ok[ch] ? rr : 0)) * I;
-      hr[ch] = h_hi + off;
-      lr[ch] = h_lo + off;
-    }
-    const int k0 = kc * C::kKch;
-    const int ngt = min(C::kKch, I - k0) / G;
-    const int kg0 = k0 / G;
-    GroupB<G> b0[NCH], b1[NCH];
-#pragma unroll
-    for (int ch = 0; ch < NCH; ++ch)
-      if (ch < nvch) load_b_planes<G>(hr[ch], lr[ch], kg0, c, ok[ch], b0[ch]);
-    cp_async_wait<kStages - 1>();
+    const int ngt = min(C::kKch, I - kc * C::kKch) / G;
+    const bool tok_ok = it.p0 + r < it.n;  // rows beyond the pass read zeros
+    cp_async_wait<S - 1>();
     __syncthreads();
-    const uint8_t* st = smem + (task % kStages) * C::kStage;
-    const __half* sc = reinterpret_cast<const __half*>(st + C::kWBytes);
+    const uint8_t* st = smem + (task % S) * C::kStage;
+    const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
     constexpr int kScH = C::kScaleRow / 2;
-    const int lane_off = (G == 64) ? 8 * c : 4 * c;
-
-    auto compute = [&](int g, const GroupB<G> (&b)[NCH]) {
-      const uint8_t* base = st + g * (G / 2) + lane_off;
-      const RowWords<G> a0 = lds_row<G>(base + lr0 * C::kStride);
-      const RowWords<G> a8 = lds_row<G>(base + (lr0 + 8) * C::kStride);
+    const int a_off = (G == 64) ? 8 * c : 4 * c;
+#pragma unroll 2
+    for (int g = 0; g < ngt; ++g) {
+      const uint8_t* ab = st + C::kW + g * (G / 2) + a_off;
+      const RowWords<G> a0 = lds_row<G>(ab + lr0 * C::kWStride);
+      const RowWords<G> a8 = lds_row<G>(ab + (lr0 + 8) * C::kWStride);
+      GroupB<G> b;
+      if (tok_ok) {
+        lds_b_bf16<G>(st + C::kB + r * C::kBStride + g * G * 2, c, b.hi);
+        lds_b_bf16<G>(st + C::kB + (kTok + r) * C::kBStride + g * G * 2, c, b.lo);
+      } else {
+#pragma unroll
+        for (int s2 = 0; s2 < GroupB<G>::kSteps; ++s2) {
+          b.hi[s2][0] = b.hi[s2][1] = 0u;
+          b.lo[s2][0] = b.lo[s2][1] = 0u;
+        }
+      }
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_group<G, true>(t, a0, a8, b);
       const float s0 = __half2float(sc[lr0 * kScH + g]);
       const float s8 = __half2float(sc[(lr0 + 8) * kScH + g]);
-#pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) {
-        if (ch < nvch) {
-          float t[4] = {0.f, 0.f, 0.f, 0.f};
-          mma_group<G, true>(t, a0, a8, b[ch]);
-          acc[ch][0] = fmaf(s0, t[0], acc[ch][0]);
-          acc[ch][1] = fmaf(s0, t[1], acc[ch][1]);
-          acc[ch][2] = fmaf(s8, t[2], acc[ch][2]);
-          acc[ch][3] = fmaf(s8, t[3], acc[ch][3]);
-        }
-      }
-    };
-
-    for (int g = 0; g < ngt; g += 2) {
-      if (g + 1 < ngt) {
-#pragma unroll
-        for (int ch = 0; ch < NCH; ++ch)
-          if (ch < nvch) load_b_planes<G>(hr[ch], lr[ch], kg0 + g + 1, c, ok[ch], b1[ch]);
-      }
-      compute(g, b0);
-      if (g + 1 < ngt) {
-        if (g + 2 < ngt) {
-#pragma unroll
-          for (int ch = 0; ch < NCH; ++ch)
-            if (ch < nvch) load_b_planes<G>(hr[ch], lr[ch], kg0 + g + 2, c, ok[ch], b0[ch]);
-        }
-        compute(g + 1, b1);
-      }
+      acc[0] = fmaf(s0, t[0], acc[0]);
+      acc[1] = fmaf(s0, t[1], acc[1]);
+      acc[2] = fmaf(s8, t[2], acc[2]);
+      acc[3] = fmaf(s8, t[3], acc[3]);
     }
-
     if (kc == nkc - 1) {
 #pragma unroll
-      for (int ch = 0; ch < NCH; ++ch) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int hrow = it.tile * C::kRows + lr0 + (q >= 2 ? 8 : 0);
-          const int rr = it.p0 + ch * 8 + 2 * c + (q & 1);
-          if (rr < it.n) y[(size_t)(it.row0 + rr) * H + hrow] = acc[ch][q];
-        }
+      for (int q = 0; q < 4; ++q) {
+        const int hrow = it.tile * C::kRows + lr0 + (q >= 2 ? 8 : 0);
+        const int rr = it.p0 + 2 * c + (q & 1);
+        if (rr < it.n) y[(size_t)(it.row0 + rr) * H + hrow] = acc[q];
       }
     }
-    __syncthreads();  // stage (task % kStages) is free again
+    __syncthreads();  // stage (task % S) is free again
   }
   cp_async_wait<0>();
 }
 
-template <int G, typename XT, int NCH>
-void launch_gateup(const void* x, const int32_t* row_token, const int32_t* offsets,
-                   const int32_t* active, const uint8_t* w13_q, const uint16_t* w13_s, int H, int I,
-                   int E, __nv_bfloat16* h_hi, __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
-  const size_t smem = (size_t)kStages * GateUpCfg<G>::kStage + (size_t)kWarps * NCH * 8 * 32 * 4 +
-                      (size_t)(E + 2) * 4;
-  auto kern = ffn_gateup_kernel<G, XT, NCH>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kern<<<grid, kThreads, smem, st>>>(static_cast<const XT*>(x), row_token, offsets, active, w13_q, w13_s,
-                                      H, I, h_hi, h_lo);
-}
-
-template <int G, int NCH>
-void launch_down(const __nv_bfloat16* h_hi, const __nv_bfloat16* h_lo, const int32_t* offsets,
-                 const int32_t* active, const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E,
-                 float* y, int grid, cudaStream_t st) {
-  const size_t smem = (size_t)kStages * DownCfg<G>::kStage + (size_t)(E + 2) * 4;
-  auto kern = ffn_down_kernel<G, NCH>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kern<<<grid, kThreads, smem, st>>>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, y);
-}
-
-template <int G, int NCH>
-void launch_all(const void* x, int x_dtype, const int32_t* row_token, const int32_t* offsets,
-                const int32_t* active, const uint8_t* w13_q, const uint16_t* w13_s,
-                const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, int R,
-                __nv_bfloat16* h_hi, __nv_bfloat16* h_lo, float* y, cudaStream_t st,
-                cudaEvent_t mid_event) {
-  const int sms = device_sm_count();
-  // upper bounds on the item counts (every row its own pass at worst)
-  const long long max_active = std::min<long long>(E, R);
-  const long long passes = max_active + R / (8 * NCH);
-  const int g1 = (int)std::max<long long>(1, std::min<long long>(sms, passes * (I / 16)));
-  const int g2 = (int)std::max<long long>(1, std::min<long long>(sms, passes * (H / 128)));
-  if (x_dtype == PHMOE_DTYPE_BF16)
-    launch_gateup<G, __nv_bfloat16, NCH>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, g1, st);
-  else
-    launch_gateup<G, float, 1>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, g1, st);
-  if (mid_event) cudaEventRecord(mid_event, st);
-  launch_down<G, NCH>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, g2, st);
-  note_launches(2);
+template <typename K>
+void set_smem(K kern, size_t bytes) {
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
 }  // namespace
+
+size_t ffn_decode_gateup_smem(int G, int x_dtype, int E) {
+  const size_t meta = (size_t)(4 * E + 4) * 4;
+  if (G == 64)
+    return x_dtype == PHMOE_DTYPE_F32
+               ? GateUpCfg<64, float>::kStages * GateUpCfg<64, float>::kStage + GateUpCfg<64, float>::kRed + meta
+               : GateUpCfg<64, __nv_bfloat16>::kStages * GateUpCfg<64, __nv_bfloat16>::kStage +
+                     GateUpCfg<64, __nv_bfloat16>::kRed + meta;
+  return x_dtype == PHMOE_DTYPE_F32
+             ? GateUpCfg<32, float>::kStages * GateUpCfg<32, float>::kStage + GateUpCfg<32, float>::kRed + meta
+             : GateUpCfg<32, __nv_bfloat16>::kStages * GateUpCfg<32, __nv_bfloat16>::kStage +
+                   GateUpCfg<32, __nv_bfloat16>::kRed + meta;
+}
+
+size_t ffn_decode_down_smem(int G, int E) {
+  const size_t meta = (size_t)(4 * E + 4) * 4;
+  return G == 64 ? DownCfg<64>::kStages * DownCfg<64>::kStage + meta
+                 : DownCfg<32>::kStages * DownCfg<32>::kStage + meta;
+}
 
 int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       const int32_t* offsets, const int32_t* active, const uint8_t* w13_q,
@@ -638,22 +576,37 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       cudaStream_t st, cudaEvent_t mid_event) {
   const long long R = (long long)T * top_k;
   if (R == 0) return PHMOE_OK;
+  if (G != 32 && G != 64) return PHMOE_ERR_UNSUPPORTED;
   __nv_bfloat16* h_hi = reinterpret_cast<__nv_bfloat16*>(h);
   __nv_bfloat16* h_lo = h_hi + (size_t)R * I;
-  const long long mean = (R + E - 1) / E;
-  const int nch = (mean <= 2 || x_dtype == PHMOE_DTYPE_F32) ? 1 : 2;
-#define PHMOE_FFN_CASE(GG, NN)                                                                  \
-  if (G == GG && nch == NN) {                                                                   \
-    launch_all<GG, NN>(x, x_dtype, row_token, offsets, active, w13_q, w13_s, w2_q, w2_s, H, I, E, \
-                       (int)R, h_hi, h_lo, y, st, mid_event);                                  \
-    return PHMOE_OK;                                                                            \
+  const int grid = device_sm_count();
+  const size_t s1 = ffn_decode_gateup_smem(G, x_dtype, E);
+  const size_t s2 = ffn_decode_down_smem(G, E);
+#define PHMOE_GATEUP(GG, XT)                                                                        \
+  {                                                                                                 \
+    auto k = ffn_gateup_kernel<GG, XT>;                                                             \
+    set_smem(k, s1);                                                                                \
+    k<<<grid, kThreads, s1, st>>>(static_cast<const XT*>(x), row_token, offsets, active, w13_q,     \
+                                  w13_s, H, I, E, h_hi, h_lo);                                      \
   }
-  PHMOE_FFN_CASE(64, 1)
-  PHMOE_FFN_CASE(64, 2)
-  PHMOE_FFN_CASE(32, 1)
-  PHMOE_FFN_CASE(32, 2)
-#undef PHMOE_FFN_CASE
-  return PHMOE_ERR_UNSUPPORTED;
+  if (G == 64) {
+    if (x_dtype == PHMOE_DTYPE_BF16) PHMOE_GATEUP(64, __nv_bfloat16) else PHMOE_GATEUP(64, float)
+  } else {
+    if (x_dtype == PHMOE_DTYPE_BF16) PHMOE_GATEUP(32, __nv_bfloat16) else PHMOE_GATEUP(32, float)
+  }
+#undef PHMOE_GATEUP
+  if (mid_event) cudaEventRecord(mid_event, st);
+  if (G == 64) {
+    auto k = ffn_down_kernel<64>;
+    set_smem(k, s2);
+    k<<<grid, kThreads, s2, st>>>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
+  } else {
+    auto k = ffn_down_kernel<32>;
+    set_smem(k, s2);
+    k<<<grid, kThreads, s2, st>>>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
+  }
+  note_launches(2);
+  return PHMOE_OK;
 }
 
 }  // namespace phmoe
