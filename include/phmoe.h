@@ -19,10 +19,12 @@
  *
  * Packed int4 layout (build-defined, generalising GGUF Q4_0,
  * python/phantom/loader/gguf_loader.py:362-381): a weight row of K elements
- * is K/2 bytes; group g of G elements (G = 32 or 64) is bytes
- * [g*G/2, (g+1)*G/2); byte j of a group holds element j in its low nibble
- * and element j+G/2 in its high nibble; value = (nibble - 8) * scale, with
- * one fp16 scale per (row, group) in a separate [rows, K/G] array.
+ * is K/2 bytes; value = (nibble - 8) * scale, with one fp16 scale per G
+ * consecutive elements (G = 32 or 64) in a separate [rows, K/G] array.
+ * Every 8 consecutive elements e0..e7 form one little-endian 32-bit word
+ * holding e_{2i} in bits [4i, 4i+4) and e_{2i+1} in bits [16+4i, 16+4i+4):
+ * bytes (e0|e2<<4, e4|e6<<4, e1|e3<<4, e5|e7<<4). GGUF Q4_0 blocks map to it
+ * losslessly with G = 32 (a nibble shuffle; the block's d becomes the scale).
  */
 #ifndef PHMOE_H_
 #define PHMOE_H_

@@ -40,15 +40,43 @@ F32 = np.float32
 # ---------------------------------------------------------------------------
 #
 # Layout of one row of K weights, group size G (32 or 64), K % G == 0:
-#   packed row = K/2 bytes; group g occupies bytes [g*G/2, (g+1)*G/2).
-#   Inside a group, byte j holds element j in its low nibble and element
-#   j + G/2 in its high nibble: the GGUF Q4_0 block order
-#   (gguf_loader.py:372-378: low nibbles -> elements 0..15, high -> 16..31),
-#   with the fp16 scale moved out of the block into a separate
-#   [rows, K/G] fp16 array. With G = 32 the nibble bytes are exactly Q4_0's.
-#   value = (nibble - 8) * scale.
+#   value = (nibble - 8) * scale, one fp16 scale per G consecutive elements in
+#   a separate [rows, K/G] array (GGUF Q4_0 semantics, gguf_loader.py:362-381,
+#   with the block's fp16 `d` moved out and the group generalised to 64).
+#   Nibble order (build-defined, chosen for the GPU dequantiser): every 8
+#   consecutive elements e0..e7 form one little-endian 32-bit word with
+#   element e_{2i} in bits [4i, 4i+4) and e_{2i+1} in bits [16+4i, 16+4i+4),
+#   i = 0..3; i.e. bytes (e0|e2<<4, e4|e6<<4, e1|e3<<4, e5|e7<<4). Shifting the
+#   word right by 4i and masking 0x000F000F yields the pair (e_{2i}, e_{2i+1})
+#   in the two 16-bit halves - one bf16x2 register per instruction.
+#   GGUF Q4_0 blocks convert to this layout losslessly (a nibble shuffle,
+#   :func:`q4_0_to_packed`).
 # Quantiser (the reference has none; it consumes GGUF files):
 #   scale = fp16(absmax(group) / 7), q = clamp(rint(w / scale), -8, 7).
+
+# element (within its 8-element word) held by the low / high nibble of byte p
+_LO_ELEM = np.array([0, 4, 1, 5])
+_HI_ELEM = _LO_ELEM + 2
+
+
+def pack_nibbles(q: np.ndarray) -> np.ndarray:
+    """Nibble values ``q[..., K]`` (0..15, K % 8 == 0) -> packed ``[..., K/2]``."""
+    q = np.asarray(q, dtype=np.uint8)
+    lead, K = q.shape[:-1], q.shape[-1]
+    qw = q.reshape(*lead, K // 8, 8)
+    packed = qw[..., _LO_ELEM] | (qw[..., _HI_ELEM] << 4)
+    return packed.astype(np.uint8).reshape(*lead, K // 2)
+
+
+def unpack_nibbles(packed: np.ndarray) -> np.ndarray:
+    """Inverse of :func:`pack_nibbles`: ``[..., K/2]`` -> nibble values ``[..., K]``."""
+    packed = np.asarray(packed, dtype=np.uint8)
+    lead, K = packed.shape[:-1], packed.shape[-1] * 2
+    pw = packed.reshape(*lead, K // 8, 4)
+    q = np.empty((*lead, K // 8, 8), dtype=np.uint8)
+    q[..., _LO_ELEM] = pw & 0x0F
+    q[..., _HI_ELEM] = pw >> 4
+    return q.reshape(*lead, K)
 
 
 def quantize_int4(w: np.ndarray, group: int = 64):
@@ -66,30 +94,17 @@ def quantize_int4(w: np.ndarray, group: int = 64):
     s = scale16.astype(F32)[..., None]
     with np.errstate(divide="ignore", invalid="ignore"):
         q = np.where(s > 0, np.rint(wg / np.where(s > 0, s, F32(1.0))), F32(0.0))
-    q = np.clip(q, -8, 7).astype(np.int16) + 8
-    half = group // 2
-    lo = q[..., :half].astype(np.uint8)
-    hi = q[..., half:].astype(np.uint8)
-    packed = (lo | (hi << 4)).astype(np.uint8).reshape(*lead, K // 2)
-    return packed, scale16
+    q = (np.clip(q, -8, 7).astype(np.int16) + 8).astype(np.uint8).reshape(*lead, K)
+    return pack_nibbles(q), scale16
 
 
 def dequantize_int4(packed: np.ndarray, scales: np.ndarray, group: int = 64) -> np.ndarray:
-    """Inverse of :func:`quantize_int4` (fp32 output).
-
-    Follows gguf_loader.py:372-378 (low nibble = first half of the block,
-    high nibble = second half, value = (nibble - 8) * d), generalised to a
-    group of 64 with the scale held in a separate array.
-    """
-    lead = packed.shape[:-1]
-    K = packed.shape[-1] * 2
-    half = group // 2
-    pg = packed.reshape(*lead, K // group, half)
-    lo = (pg & 0x0F).astype(np.int16) - 8
-    hi = ((pg >> 4) & 0x0F).astype(np.int16) - 8
-    q = np.concatenate([lo, hi], axis=-1).astype(F32)
+    """Inverse of :func:`quantize_int4` (fp32 output): (nibble - 8) * scale,
+    as gguf_loader.py:372-378 dequantises Q4_0 with a per-block ``d``."""
+    q = unpack_nibbles(packed).astype(np.int16) - 8
+    lead, K = q.shape[:-1], q.shape[-1]
     s = scales.astype(F32)[..., None]
-    return (q * s).reshape(*lead, K)
+    return (q.reshape(*lead, K // group, group).astype(F32) * s).reshape(*lead, K)
 
 
 def dequantize_q4_0(raw: bytes, n_elems: int) -> np.ndarray:
@@ -111,16 +126,18 @@ def dequantize_q4_0(raw: bytes, n_elems: int) -> np.ndarray:
 
 
 def q4_0_to_packed(raw: bytes, rows: int, K: int):
-    """Split GGUF Q4_0 blocks of a [rows, K] tensor into (packed, scales).
+    """Convert GGUF Q4_0 blocks of a [rows, K] tensor into (packed, scales).
 
-    Lossless: the 16 nibble bytes of each 18-byte block are kept as they are
-    and the fp16 ``d`` goes to the scales array (group size 32).
+    Lossless: each 18-byte block's fp16 ``d`` goes to the scales array (group
+    size 32) and its 32 nibbles (byte j: element j low, element j+16 high,
+    gguf_loader.py:372-378) are re-ordered into the packed nibble layout.
     """
     nb = K // 32
     blk = np.frombuffer(raw[: rows * nb * 18], dtype=np.uint8).reshape(rows, nb, 18)
     scales = blk[:, :, :2].copy().view(np.float16).reshape(rows, nb)
-    packed = np.ascontiguousarray(blk[:, :, 2:]).reshape(rows, K // 2)
-    return packed, scales
+    qs = blk[:, :, 2:]
+    q = np.concatenate([qs & 0x0F, qs >> 4], axis=-1).reshape(rows, K)
+    return pack_nibbles(q), scales
 
 
 # ---------------------------------------------------------------------------

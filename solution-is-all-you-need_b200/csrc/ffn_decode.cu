@@ -8,35 +8,40 @@
 //
 // Design. At decode sizes the layer streams ~2.5 MB of packed weights per
 // expert hit and does a few FMAs per weight: the bound is HBM. Both kernels
-// are persistent (one 256-thread CTA per SM, a contiguous range of work items
+// are persistent (one 512-thread CTA per SM, a contiguous range of work items
 // each) and run a multi-stage cp.async pipeline over "tasks" (a work item's
 // K-chunk). A stage holds everything a task reads: the packed int4 weight
 // rows, their fp16 scales and the K-chunk of the activation rows (B). While
-// the 8 warps compute task t, tasks t+1.. are in flight from HBM/L2, so the
-// compute loop issues no global loads at all. Rows are padded so that every
-// fragment read below is bank-conflict free.
+// the 16 warps compute task t, tasks t+1.. are in flight from HBM/L2, so the
+// compute loop issues no global loads. Rows are padded so that every
+// fragment read is bank-conflict free (fp32 activations excepted).
 //
-// From shared memory each lane reads the int4 bytes of its A fragments, turns
-// them into bf16 (nibble - 8) in registers (exact) and issues mma.sync
-// m16n8k16 with the 8 tokens of a pass as the N side. Dequantised weights are
-// never written back to shared memory (bf16 would be 4x the int4 bytes). The
-// fp16 group scale multiplies the fp32 partial of each group (exact).
+// From shared memory each lane reads the int4 words of its A fragments and
+// turns each 32-bit word (8 consecutive weights) into four bf16x2 pairs with
+// one lop3 each (see the packed layout in phmoe.h); the pairs feed mma.sync
+// m16n8k16 directly, with the 8 tokens of a pass as the N side. Dequantised
+// weights are never written back to shared memory (bf16 would be 4x the int4
+// bytes). In gate/up the unpacked values are 128 + nibble and the +136
+// offset is removed after the MMA with one extra MMA per K step against an
+// all-ones A (it yields sum_k x_k); the fp16 group scale multiplies the fp32
+// partial of each group. Both steps are exact factorisations.
 //
-// The K order inside a group is permuted identically for A and B (a dot
-// product does not depend on the order): for G=64 lane c of a quad holds
-// elements 8c..8c+7 (low nibbles) and 32+8c..32+8c+7 (high nibbles), exactly
-// the activations it reads with two 16-byte loads.
+// Lane c of a quad holds K elements 16c..16c+15 of a 64-group (8c..8c+7 of a
+// 32-group) for A and reads the same activations for B; inside one MMA the K
+// order is a permutation applied to both operands, which a dot product does
+// not see.
 //
 // Precision: bf16 activations enter the MMA exactly; fp32 activations and the
 // intermediate h are split into bf16 hi + lo parts (two MMAs each), keeping
 // ~16 significant bits.
 //
 // gate/up kernel: item = (expert, 16 intermediate rows, pass of 8 tokens) ->
-//   32 weight rows (16 gate + 16 up); the 8 warps split each K-chunk and are
+//   32 weight rows (16 gate + 16 up); the 16 warps split each K-chunk and are
 //   reduced through shared memory in warp order (deterministic); SwiGLU in
 //   the epilogue, h stored as bf16 hi/lo planes.
 // down kernel: item = (expert, 128 output rows, pass); warp w owns rows
-//   16w..16w+15.
+//   16(w%8)..+15 and half of each K-chunk (w/8); the halves are added in a
+//   fixed order.
 // Items are ordered (expert, tile, pass) so the extra passes of an expert
 // with more than 8 rows re-read weights that are still in L2.
 #include "common.cuh"
@@ -46,7 +51,7 @@ namespace phmoe {
 
 namespace {
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kTok = 8;  // tokens per pass (the MMA N dimension)
 
@@ -69,61 +74,7 @@ __device__ __forceinline__ void cp_async_wait() {
 // fragments
 // ---------------------------------------------------------------------------
 
-// B fragments of one group: per MMA step (2 per 32-bit weight word: low then
-// high nibbles) two b registers, for the "hi" part and (split inputs) "lo".
-template <int G>
-struct GroupB {
-  static constexpr int kSteps = 2 * (G / 32);
-  uint32_t hi[kSteps][2];
-  uint32_t lo[kSteps][2];
-};
-
-// bf16 activations of one group from shared memory (p = row + group start).
-// Step order: word 0 low, word 0 high, word 1 low, word 1 high. G=64: word w
-// low covers elements 8c+4w..+3, high 32+8c+4w..+3. G=32: low 4c..4c+3,
-// high 16+4c..16+4c+3.
-template <int G>
-__device__ __forceinline__ void lds_b_bf16(const uint8_t* p, int c, uint32_t (&d)[GroupB<G>::kSteps][2]) {
-  if constexpr (G == 64) {
-    const uint4 x0 = *reinterpret_cast<const uint4*>(p + 16 * c);
-    const uint4 x1 = *reinterpret_cast<const uint4*>(p + 64 + 16 * c);
-    d[0][0] = x0.x; d[0][1] = x0.y;
-    d[1][0] = x1.x; d[1][1] = x1.y;
-    d[2][0] = x0.z; d[2][1] = x0.w;
-    d[3][0] = x1.z; d[3][1] = x1.w;
-  } else {
-    const uint2 x0 = *reinterpret_cast<const uint2*>(p + 8 * c);
-    const uint2 x1 = *reinterpret_cast<const uint2*>(p + 32 + 8 * c);
-    d[0][0] = x0.x; d[0][1] = x0.y;
-    d[1][0] = x1.x; d[1][1] = x1.y;
-  }
-}
-
-__device__ __forceinline__ void split4(const float4 v, uint32_t& h0, uint32_t& h1, uint32_t& l0,
-                                       uint32_t& l1) {
-  split_bf16x2(v.x, v.y, h0, l0);
-  split_bf16x2(v.z, v.w, h1, l1);
-}
-
-// fp32 activations of one group from shared memory, split into hi/lo bf16.
-template <int G>
-__device__ __forceinline__ void lds_b_f32(const uint8_t* p, int c, GroupB<G>& b) {
-  if constexpr (G == 64) {
-    const float4* q0 = reinterpret_cast<const float4*>(p + 32 * c);
-    const float4* q1 = reinterpret_cast<const float4*>(p + 128 + 32 * c);
-    split4(q0[0], b.hi[0][0], b.hi[0][1], b.lo[0][0], b.lo[0][1]);
-    split4(q1[0], b.hi[1][0], b.hi[1][1], b.lo[1][0], b.lo[1][1]);
-    split4(q0[1], b.hi[2][0], b.hi[2][1], b.lo[2][0], b.lo[2][1]);
-    split4(q1[1], b.hi[3][0], b.hi[3][1], b.lo[3][0], b.lo[3][1]);
-  } else {
-    const float4 a0 = *reinterpret_cast<const float4*>(p + 16 * c);
-    const float4 c0 = *reinterpret_cast<const float4*>(p + 64 + 16 * c);
-    split4(a0, b.hi[0][0], b.hi[0][1], b.lo[0][0], b.lo[0][1]);
-    split4(c0, b.hi[1][0], b.hi[1][1], b.lo[1][0], b.lo[1][1]);
-  }
-}
-
-// Packed words of one row of one group for this lane, from shared memory.
+// A words of one row and one group for this lane (G/32 words).
 template <int G>
 struct RowWords {
   uint32_t w[G / 32];
@@ -141,24 +92,98 @@ __device__ __forceinline__ RowWords<G> lds_row(const uint8_t* p) {
   return r;
 }
 
-// tmp += A(rows r, r+8 of one group) * B, all MMA steps of the group.
-template <int G, bool kTwoParts>
-__device__ __forceinline__ void mma_group(float (&tmp)[4], const RowWords<G>& r0,
-                                          const RowWords<G>& r8, const GroupB<G>& b) {
+// B words of one group for this lane: bf16 pairs of its G/4 elements.
+template <int G>
+struct BWords {
+  uint32_t hi[G / 8];
+  uint32_t lo[G / 8];
+};
+
+template <int G>
+__device__ __forceinline__ void lds_b_plane(const uint8_t* p, uint32_t (&d)[G / 8]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(p);
+  d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w;
+  if constexpr (G == 64) {
+    const uint4 b = *reinterpret_cast<const uint4*>(p + 16);
+    d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
+  }
+}
+
+__device__ __forceinline__ void split4(const float4 v, uint32_t& h0, uint32_t& h1, uint32_t& l0,
+                                       uint32_t& l1) {
+  split_bf16x2(v.x, v.y, h0, l0);
+  split_bf16x2(v.z, v.w, h1, l1);
+}
+
+template <int G>
+__device__ __forceinline__ void lds_b_f32(const uint8_t* p, BWords<G>& b) {
+#pragma unroll
+  for (int i = 0; i < G / 16; ++i)
+    split4(reinterpret_cast<const float4*>(p)[i], b.hi[2 * i], b.hi[2 * i + 1], b.lo[2 * i], b.lo[2 * i + 1]);
+}
+
+// gate/up partial of one group: acc_g/acc_u += s * (A.B - 136 * sum(B)) for
+// rows (r, r+8) of the gate and up tiles. A is unpacked biased (128 + n).
+template <int G, bool kTwo>
+__device__ __forceinline__ void gateup_group(const RowWords<G>& g0, const RowWords<G>& g8,
+                                             const RowWords<G>& u0, const RowWords<G>& u8,
+                                             const BWords<G>& b, float sg0, float sg8, float su0,
+                                             float su8, float (&acc_g)[4], float (&acc_u)[4]) {
+  float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f}, td[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint32_t ones[4] = {kBf16x2One, kBf16x2One, kBf16x2One, kBf16x2One};
 #pragma unroll
   for (int w = 0; w < G / 32; ++w) {
-    uint32_t lo01a, lo23a, hi01a, hi23a, lo01b, lo23b, hi01b, hi23b;
-    dequant_word(r0.w[w], lo01a, lo23a, hi01a, hi23a);
-    dequant_word(r8.w[w], lo01b, lo23b, hi01b, hi23b);
-    const uint32_t alo[4] = {lo01a, lo01b, lo23a, lo23b};
-    const uint32_t ahi[4] = {hi01a, hi01b, hi23a, hi23b};
-    mma_bf16_16816(tmp, alo, b.hi[2 * w][0], b.hi[2 * w][1], tmp);
-    mma_bf16_16816(tmp, ahi, b.hi[2 * w + 1][0], b.hi[2 * w + 1][1], tmp);
-    if constexpr (kTwoParts) {
-      mma_bf16_16816(tmp, alo, b.lo[2 * w][0], b.lo[2 * w][1], tmp);
-      mma_bf16_16816(tmp, ahi, b.lo[2 * w + 1][0], b.lo[2 * w + 1][1], tmp);
+    uint32_t pg0[4], pg8[4], pu0[4], pu8[4];
+    unpack_word_biased(g0.w[w], pg0);
+    unpack_word_biased(g8.w[w], pg8);
+    unpack_word_biased(u0.w[w], pu0);
+    unpack_word_biased(u8.w[w], pu8);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {  // two MMA steps per word
+      const int s = 2 * w + h;
+      const uint32_t ag[4] = {pg0[2 * h], pg8[2 * h], pg0[2 * h + 1], pg8[2 * h + 1]};
+      const uint32_t au[4] = {pu0[2 * h], pu8[2 * h], pu0[2 * h + 1], pu8[2 * h + 1]};
+      mma_bf16_16816(tg, ag, b.hi[2 * s], b.hi[2 * s + 1], tg);
+      mma_bf16_16816(tu, au, b.hi[2 * s], b.hi[2 * s + 1], tu);
+      mma_bf16_16816(td, ones, b.hi[2 * s], b.hi[2 * s + 1], td);
+      if constexpr (kTwo) {
+        mma_bf16_16816(tg, ag, b.lo[2 * s], b.lo[2 * s + 1], tg);
+        mma_bf16_16816(tu, au, b.lo[2 * s], b.lo[2 * s + 1], tu);
+        mma_bf16_16816(td, ones, b.lo[2 * s], b.lo[2 * s + 1], td);
+      }
     }
   }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float d = -136.0f * td[q];  // td = sum of this group's activations (per token)
+    const float sg = q < 2 ? sg0 : sg8, su = q < 2 ? su0 : su8;
+    acc_g[q] = fmaf(sg, tg[q] + d, acc_g[q]);
+    acc_u[q] = fmaf(su, tu[q] + d, acc_u[q]);
+  }
+}
+
+// down partial of one group: acc += s * A.(B_hi + B_lo), A unpacked exactly.
+template <int G>
+__device__ __forceinline__ void down_group(const RowWords<G>& a0, const RowWords<G>& a8,
+                                           const BWords<G>& b, float s0, float s8, float (&acc)[4]) {
+  float t[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int w = 0; w < G / 32; ++w) {
+    uint32_t p0[4], p8[4];
+    unpack_word(a0.w[w], p0);
+    unpack_word(a8.w[w], p8);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int s = 2 * w + h;
+      const uint32_t a[4] = {p0[2 * h], p8[2 * h], p0[2 * h + 1], p8[2 * h + 1]};
+      mma_bf16_16816(t, a, b.hi[2 * s], b.hi[2 * s + 1], t);
+      mma_bf16_16816(t, a, b.lo[2 * s], b.lo[2 * s + 1], t);
+    }
+  }
+  acc[0] = fmaf(s0, t[0], acc[0]);
+  acc[1] = fmaf(s0, t[1], acc[1]);
+  acc[2] = fmaf(s8, t[2], acc[2]);
+  acc[3] = fmaf(s8, t[3], acc[3]);
 }
 
 // ---------------------------------------------------------------------------
@@ -242,19 +267,20 @@ __device__ __forceinline__ void cta_range(int total, int& q0, int& q1) {
 template <int G, typename XT>
 struct GateUpCfg {
   static constexpr bool kF32 = std::is_same<XT, float>::value;
-  static constexpr int kStages = 5;
+  static constexpr int kStages = kF32 ? 3 : 5;
   static constexpr int kRows = 32;
-  static constexpr int kKch = kF32 ? 512 : 1024;                   // K elements per task
-  static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);  // conflict-free A reads
+  static constexpr int kKch = 1024;                                  // K elements per task
+  static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);    // conflict-free A reads
   static constexpr int kScaleRow = kKch / G * 2;
   static constexpr int kBRowBytes = kKch * (int)sizeof(XT);
-  static constexpr int kBPad = kF32 ? (G == 64 ? 16 : 64) : (G == 64 ? 64 : 32);
-  static constexpr int kBStride = kBRowBytes + kBPad;              // conflict-free B reads
+  static constexpr int kBPad = (G == 32 && !kF32) ? 64 : 16;         // conflict-free B reads
+  static constexpr int kBStride = kBRowBytes + kBPad;
   static constexpr int kW = 0;
   static constexpr int kS = kRows * kWStride;
   static constexpr int kB = kS + kRows * kScaleRow;
   static constexpr int kStage = (kB + kTok * kBStride + 127) / 128 * 128;
   static constexpr int kRed = kWarps * 8 * 32 * 4;
+  static constexpr int kBChunks = kBRowBytes / 16;                   // per token row
 };
 
 template <int G, typename XT>
@@ -282,9 +308,9 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
   cta_range(total, q0, q1);
   const int ntask = (q1 - q0) * nkc;
 
-  // B-copy assignment of this thread: token bn, 16-byte chunks bc, bc+32, ...
-  const int bn = threadIdx.x >> 5;
-  const int bc = threadIdx.x & 31;
+  // B-copy assignment of this thread: token bn, 16-byte chunks bc, bc+64, ...
+  const int bn = threadIdx.x >> 6;
+  const int bc = threadIdx.x & 63;
   auto token_of = [&](int task) -> int {
     if (task >= ntask) return -1;
     const Item it = decode_item(q0 + task / nkc, na, tiles, meta);
@@ -314,7 +340,7 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
     if (tok >= 0) {
       const int bch = kel * (int)sizeof(XT) / 16;
       const uint8_t* src = reinterpret_cast<const uint8_t*>(x + (size_t)tok * H + k0);
-      for (int cc = bc; cc < bch; cc += 32)
+      for (int cc = bc; cc < bch; cc += 64)
         cp_async16(smem_u32(st + C::kB + bn * C::kBStride + cc * 16), src + cc * 16);
     }
   };
@@ -325,7 +351,9 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
   }
   int next_tok = token_of(S - 1);
 
-  float acc[2][4];
+  float acc_g[4], acc_u[4];
+  const int a_off = (G == 64) ? 8 * c : 4 * c;
+  const int b_off = (G == 64 ? 16 : 8) * c * (int)sizeof(XT);
   for (int task = 0; task < ntask; ++task) {
     if (task + S - 1 < ntask) issue(task + S - 1, next_tok);
     cp_async_commit();
@@ -334,7 +362,7 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
     const Item it = decode_item(q0 + task / nkc, na, tiles, meta);
     if (kc == 0) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) { acc[0][q] = 0.f; acc[1][q] = 0.f; }
+      for (int q = 0; q < 4; ++q) { acc_g[q] = 0.f; acc_u[q] = 0.f; }
     }
     const int ngt = min(C::kKch, H - kc * C::kKch) / G;
     cp_async_wait<S - 1>();
@@ -342,40 +370,28 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
     const uint8_t* st = smem + (task % S) * C::kStage;
     const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
     constexpr int kScH = C::kScaleRow / 2;
-    const int a_off = (G == 64) ? 8 * c : 4 * c;
+#pragma unroll 2
     for (int g = warp; g < ngt; g += kWarps) {
       const uint8_t* ab = st + C::kW + g * (G / 2) + a_off;
       const RowWords<G> ag0 = lds_row<G>(ab + r * C::kWStride);
       const RowWords<G> ag8 = lds_row<G>(ab + (r + 8) * C::kWStride);
       const RowWords<G> au0 = lds_row<G>(ab + (16 + r) * C::kWStride);
       const RowWords<G> au8 = lds_row<G>(ab + (24 + r) * C::kWStride);
-      GroupB<G> b;
-      const uint8_t* bb = st + C::kB + r * C::kBStride + g * G * (int)sizeof(XT);
-      if constexpr (C::kF32) lds_b_f32<G>(bb, c, b);
-      else lds_b_bf16<G>(bb, c, b.hi);
-      float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f};
-      mma_group<G, C::kF32>(tg, ag0, ag8, b);
-      mma_group<G, C::kF32>(tu, au0, au8, b);
-      const float sg0 = __half2float(sc[r * kScH + g]);
-      const float sg8 = __half2float(sc[(r + 8) * kScH + g]);
-      const float su0 = __half2float(sc[(16 + r) * kScH + g]);
-      const float su8 = __half2float(sc[(24 + r) * kScH + g]);
-      acc[0][0] = fmaf(sg0, tg[0], acc[0][0]);
-      acc[0][1] = fmaf(sg0, tg[1], acc[0][1]);
-      acc[0][2] = fmaf(sg8, tg[2], acc[0][2]);
-      acc[0][3] = fmaf(sg8, tg[3], acc[0][3]);
-      acc[1][0] = fmaf(su0, tu[0], acc[1][0]);
-      acc[1][1] = fmaf(su0, tu[1], acc[1][1]);
-      acc[1][2] = fmaf(su8, tu[2], acc[1][2]);
-      acc[1][3] = fmaf(su8, tu[3], acc[1][3]);
+      BWords<G> b;
+      const uint8_t* bb = st + C::kB + r * C::kBStride + g * G * (int)sizeof(XT) + b_off;
+      if constexpr (C::kF32) lds_b_f32<G>(bb, b);
+      else lds_b_plane<G>(bb, b.hi);
+      gateup_group<G, C::kF32>(ag0, ag8, au0, au8, b, __half2float(sc[r * kScH + g]),
+                               __half2float(sc[(r + 8) * kScH + g]), __half2float(sc[(16 + r) * kScH + g]),
+                               __half2float(sc[(24 + r) * kScH + g]), acc_g, acc_u);
     }
     if (kc == nkc - 1) {
-      // reduce the 8 K-slices in warp order, then SwiGLU
+      // reduce the K-slices in warp order, then SwiGLU
       float* mine = red + warp * 8 * 32;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        mine[q * 32 + lane] = acc[0][q];
-        mine[(4 + q) * 32 + lane] = acc[1][q];
+        mine[q * 32 + lane] = acc_g[q];
+        mine[(4 + q) * 32 + lane] = acc_u[q];
       }
       __syncthreads();
       if (warp == 0) {
@@ -420,11 +436,12 @@ struct DownCfg {
   static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);
   static constexpr int kScaleRow = kKch / G * 2;
   static constexpr int kBRowBytes = kKch * 2;  // one bf16 plane
-  static constexpr int kBStride = kBRowBytes + (G == 64 ? 64 : 32);
+  static constexpr int kBStride = kBRowBytes + (G == 64 ? 16 : 64);
   static constexpr int kW = 0;
   static constexpr int kS = kRows * kWStride;
   static constexpr int kB = kS + kRows * kScaleRow;             // [2 planes][kTok][kBStride]
   static constexpr int kStage = (kB + 2 * kTok * kBStride + 127) / 128 * 128;
+  static constexpr int kRed = 8 * 4 * 32 * 4;
 };
 
 template <int G>
@@ -436,10 +453,12 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
   using C = DownCfg<G>;
   constexpr int S = C::kStages;
   extern __shared__ __align__(128) uint8_t smem[];
-  int* mbase = reinterpret_cast<int*>(smem + S * C::kStage);
+  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [8][4][32]
+  int* mbase = reinterpret_cast<int*>(smem + S * C::kStage + C::kRed);
   const Meta meta{mbase, mbase + E, mbase + 2 * E, mbase + 3 * E};
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
+  const int rb = warp & 7, kh = warp >> 3;  // row block, K half
   const int tiles = H / C::kRows;
   const int NG = I / G;
   const int nkc = (I + C::kKch - 1) / C::kKch;
@@ -487,7 +506,9 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
   }
 
   float acc[4];
-  const int lr0 = warp * 16 + r;
+  const int lr0 = rb * 16 + r;
+  const int a_off = (G == 64) ? 8 * c : 4 * c;
+  const int b_off = (G == 64 ? 32 : 16) * c;
   for (int task = 0; task < ntask; ++task) {
     if (task + S - 1 < ntask) issue(task + S - 1);
     cp_async_commit();
@@ -498,47 +519,45 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
       for (int q = 0; q < 4; ++q) acc[q] = 0.f;
     }
     const int ngt = min(C::kKch, I - kc * C::kKch) / G;
-    const bool tok_ok = it.p0 + r < it.n;  // rows beyond the pass read zeros
+    const bool tok_ok = it.p0 + r < it.n;  // B rows beyond the pass hold stale data: use zeros
     cp_async_wait<S - 1>();
     __syncthreads();
     const uint8_t* st = smem + (task % S) * C::kStage;
     const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
     constexpr int kScH = C::kScaleRow / 2;
-    const int a_off = (G == 64) ? 8 * c : 4 * c;
 #pragma unroll 2
-    for (int g = 0; g < ngt; ++g) {
+    for (int g = kh; g < ngt; g += 2) {
       const uint8_t* ab = st + C::kW + g * (G / 2) + a_off;
       const RowWords<G> a0 = lds_row<G>(ab + lr0 * C::kWStride);
       const RowWords<G> a8 = lds_row<G>(ab + (lr0 + 8) * C::kWStride);
-      GroupB<G> b;
+      BWords<G> b;
       if (tok_ok) {
-        lds_b_bf16<G>(st + C::kB + r * C::kBStride + g * G * 2, c, b.hi);
-        lds_b_bf16<G>(st + C::kB + (kTok + r) * C::kBStride + g * G * 2, c, b.lo);
+        const uint8_t* bb = st + C::kB + r * C::kBStride + g * G * 2 + b_off;
+        lds_b_plane<G>(bb, b.hi);
+        lds_b_plane<G>(bb + kTok * C::kBStride, b.lo);
       } else {
 #pragma unroll
-        for (int s2 = 0; s2 < GroupB<G>::kSteps; ++s2) {
-          b.hi[s2][0] = b.hi[s2][1] = 0u;
-          b.lo[s2][0] = b.lo[s2][1] = 0u;
-        }
+        for (int i = 0; i < G / 8; ++i) b.hi[i] = b.lo[i] = 0u;
       }
-      float t[4] = {0.f, 0.f, 0.f, 0.f};
-      mma_group<G, true>(t, a0, a8, b);
-      const float s0 = __half2float(sc[lr0 * kScH + g]);
-      const float s8 = __half2float(sc[(lr0 + 8) * kScH + g]);
-      acc[0] = fmaf(s0, t[0], acc[0]);
-      acc[1] = fmaf(s0, t[1], acc[1]);
-      acc[2] = fmaf(s8, t[2], acc[2]);
-      acc[3] = fmaf(s8, t[3], acc[3]);
+      down_group<G>(a0, a8, b, __half2float(sc[lr0 * kScH + g]), __half2float(sc[(lr0 + 8) * kScH + g]), acc);
     }
     if (kc == nkc - 1) {
+      if (kh == 1) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int hrow = it.tile * C::kRows + lr0 + (q >= 2 ? 8 : 0);
-        const int rr = it.p0 + 2 * c + (q & 1);
-        if (rr < it.n) y[(size_t)(it.row0 + rr) * H + hrow] = acc[q];
+        for (int q = 0; q < 4; ++q) red[(rb * 4 + q) * 32 + lane] = acc[q];
+      }
+      __syncthreads();
+      if (kh == 0) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float v = acc[q] + red[(rb * 4 + q) * 32 + lane];
+          const int hrow = it.tile * C::kRows + lr0 + (q >= 2 ? 8 : 0);
+          const int rr = it.p0 + 2 * c + (q & 1);
+          if (rr < it.n) y[(size_t)(it.row0 + rr) * H + hrow] = v;
+        }
       }
     }
-    __syncthreads();  // stage (task % S) is free again
+    __syncthreads();  // stage (task % S) and `red` are free again
   }
   cp_async_wait<0>();
 }
@@ -548,26 +567,40 @@ void set_smem(K kern, size_t bytes) {
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
+template <int G, typename XT>
+size_t gateup_smem(int E) {
+  using C = GateUpCfg<G, XT>;
+  return (size_t)C::kStages * C::kStage + C::kRed + (size_t)(4 * E + 4) * 4;
+}
+
+template <int G>
+size_t down_smem(int E) {
+  using C = DownCfg<G>;
+  return (size_t)C::kStages * C::kStage + C::kRed + (size_t)(4 * E + 4) * 4;
+}
+
+template <int G, typename XT>
+void launch_gateup(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
+                   const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
+                   __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
+  const size_t smem = gateup_smem<G, XT>(E);
+  auto k = ffn_gateup_kernel<G, XT>;
+  set_smem(k, smem);
+  k<<<grid, kThreads, smem, st>>>(static_cast<const XT*>(x), row_token, offsets, active, w13_q, w13_s, H, I,
+                                  E, h_hi, h_lo);
+}
+
+template <int G>
+void launch_down(const __nv_bfloat16* h_hi, const __nv_bfloat16* h_lo, const int32_t* offsets,
+                 const int32_t* active, const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, float* y,
+                 int grid, cudaStream_t st) {
+  const size_t smem = down_smem<G>(E);
+  auto k = ffn_down_kernel<G>;
+  set_smem(k, smem);
+  k<<<grid, kThreads, smem, st>>>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
+}
+
 }  // namespace
-
-size_t ffn_decode_gateup_smem(int G, int x_dtype, int E) {
-  const size_t meta = (size_t)(4 * E + 4) * 4;
-  if (G == 64)
-    return x_dtype == PHMOE_DTYPE_F32
-               ? GateUpCfg<64, float>::kStages * GateUpCfg<64, float>::kStage + GateUpCfg<64, float>::kRed + meta
-               : GateUpCfg<64, __nv_bfloat16>::kStages * GateUpCfg<64, __nv_bfloat16>::kStage +
-                     GateUpCfg<64, __nv_bfloat16>::kRed + meta;
-  return x_dtype == PHMOE_DTYPE_F32
-             ? GateUpCfg<32, float>::kStages * GateUpCfg<32, float>::kStage + GateUpCfg<32, float>::kRed + meta
-             : GateUpCfg<32, __nv_bfloat16>::kStages * GateUpCfg<32, __nv_bfloat16>::kStage +
-                   GateUpCfg<32, __nv_bfloat16>::kRed + meta;
-}
-
-size_t ffn_decode_down_smem(int G, int E) {
-  const size_t meta = (size_t)(4 * E + 4) * 4;
-  return G == 64 ? DownCfg<64>::kStages * DownCfg<64>::kStage + meta
-                 : DownCfg<32>::kStages * DownCfg<32>::kStage + meta;
-}
 
 int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       const int32_t* offsets, const int32_t* active, const uint8_t* w13_q,
@@ -580,31 +613,17 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
   __nv_bfloat16* h_hi = reinterpret_cast<__nv_bfloat16*>(h);
   __nv_bfloat16* h_lo = h_hi + (size_t)R * I;
   const int grid = device_sm_count();
-  const size_t s1 = ffn_decode_gateup_smem(G, x_dtype, E);
-  const size_t s2 = ffn_decode_down_smem(G, E);
-#define PHMOE_GATEUP(GG, XT)                                                                        \
-  {                                                                                                 \
-    auto k = ffn_gateup_kernel<GG, XT>;                                                             \
-    set_smem(k, s1);                                                                                \
-    k<<<grid, kThreads, s1, st>>>(static_cast<const XT*>(x), row_token, offsets, active, w13_q,     \
-                                  w13_s, H, I, E, h_hi, h_lo);                                      \
-  }
+  const bool f32 = x_dtype == PHMOE_DTYPE_F32;
   if (G == 64) {
-    if (x_dtype == PHMOE_DTYPE_BF16) PHMOE_GATEUP(64, __nv_bfloat16) else PHMOE_GATEUP(64, float)
+    if (f32) launch_gateup<64, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
+    else launch_gateup<64, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
   } else {
-    if (x_dtype == PHMOE_DTYPE_BF16) PHMOE_GATEUP(32, __nv_bfloat16) else PHMOE_GATEUP(32, float)
+    if (f32) launch_gateup<32, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
+    else launch_gateup<32, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
   }
-#undef PHMOE_GATEUP
   if (mid_event) cudaEventRecord(mid_event, st);
-  if (G == 64) {
-    auto k = ffn_down_kernel<64>;
-    set_smem(k, s2);
-    k<<<grid, kThreads, s2, st>>>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
-  } else {
-    auto k = ffn_down_kernel<32>;
-    set_smem(k, s2);
-    k<<<grid, kThreads, s2, st>>>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
-  }
+  if (G == 64) launch_down<64>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+  else launch_down<32>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
   note_launches(2);
   return PHMOE_OK;
 }

@@ -5,7 +5,8 @@
 // This kernel produces the packed layout the FFN kernels read:
 //   scale = fp16_rn(absmax(group) / 7)          (IEEE fp32 division)
 //   q     = clamp(rint(w / scale), -8, 7) + 8   (0 when scale == 0)
-//   byte j of a group = q[j] | q[j + G/2] << 4  (GGUF Q4_0 nibble order)
+//   every 8 consecutive elements e0..e7 form one little-endian 32-bit word:
+//   bytes (e0|e2<<4, e4|e6<<4, e1|e3<<4, e5|e7<<4)
 // One warp per (row, group); every operation is IEEE-rounded so the CPU
 // restatement reproduces the bytes exactly.
 #include "common.cuh"
@@ -55,15 +56,18 @@ quantize_kernel(const WT* __restrict__ w, long long rows, int K, uint8_t* __rest
   const __half sh = __float2half_rn(__fdiv_rn(m, 7.0f));
   const float s = __half2float(sh);
   uint8_t* dst = packed + row * (K / 2) + (long long)g * (G / 2);
-  if constexpr (G == 64) {
-    // lane holds elements lane (low nibble of byte lane) and lane+32 (high).
-    const int lo = quant_one(v[0], s), hi = quant_one(v[1], s);
-    dst[lane] = (uint8_t)(lo | (hi << 4));
-  } else {
-    const int q = quant_one(v[0], s);
-    const int qhi = __shfl_down_sync(0xffffffffu, q, 16);
-    if (lane < 16) dst[lane] = (uint8_t)(q | (qhi << 4));
-  }
+  // Lane holds the nibbles of elements lane and (G=64) lane+32. Byte b of
+  // the group belongs to 8-element word m = b/4; its low nibble is element
+  // 8m + 4(b&1) + ((b&3)>>1) and its high nibble that element + 2.
+  const int q0 = quant_one(v[0], s);
+  const int q1 = kPer > 1 ? quant_one(v[kPer - 1], s) : 8;
+  const int wm = lane >> 2, p = lane & 3;
+  const int elo = 8 * wm + 4 * (p & 1) + (p >> 1), ehi = elo + 2;
+  const int lo_a = __shfl_sync(0xffffffffu, q0, elo & 31), lo_b = __shfl_sync(0xffffffffu, q1, elo & 31);
+  const int hi_a = __shfl_sync(0xffffffffu, q0, ehi & 31), hi_b = __shfl_sync(0xffffffffu, q1, ehi & 31);
+  const int qlo = elo < 32 ? lo_a : lo_b;
+  const int qhi = ehi < 32 ? hi_a : hi_b;
+  if (lane < G / 2) dst[lane] = (uint8_t)(qlo | (qhi << 4));
   if (lane == 0) scales[row * ng + g] = __half_as_ushort(sh);
 }
 
