@@ -232,28 +232,42 @@ __device__ int build_meta(const int32_t* __restrict__ offsets, const int32_t* __
   return m.table[na];
 }
 
-struct Item {
-  int e, row0, n, p0, tile;
+// Position of a CTA in its task sequence: (active slot, tile, pass, K-chunk).
+// Tasks are visited in order, so a cursor only ever advances by one; no
+// integer division happens in the loops (a runtime division costs several
+// instructions on the SM's narrow XU pipe).
+struct Cursor {
+  int slot, tile, pass, kc, passes;
 };
 
-// Item q -> (slot, tile, pass); items of one slot are ordered tile-major so
-// the passes of a tile follow each other.
-__device__ __forceinline__ Item decode_item(int q, int na, int tiles, const Meta& m) {
+__device__ __forceinline__ int passes_of(int n) { return (n + kTok - 1) / kTok; }
+
+__device__ Cursor cursor_at(int q, int na, int tiles, const Meta& m) {
   int lo = 0, hi = na;  // table[lo] <= q < table[hi]
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (m.table[mid] <= q) lo = mid;
     else hi = mid;
   }
+  Cursor c;
+  c.slot = lo;
+  c.passes = passes_of(m.n[lo]);
   const int local = q - m.table[lo];
-  Item it;
-  it.e = m.e[lo];
-  it.row0 = m.row0[lo];
-  it.n = m.n[lo];
-  const int passes = (it.n + kTok - 1) / kTok;
-  it.tile = local / passes;
-  it.p0 = (local - it.tile * passes) * kTok;
-  return it;
+  c.tile = local / c.passes;
+  c.pass = local - c.tile * c.passes;
+  c.kc = 0;
+  return c;
+}
+
+__device__ __forceinline__ void cursor_next(Cursor& c, int tiles, int nkc, const Meta& m) {
+  if (++c.kc < nkc) return;
+  c.kc = 0;
+  if (++c.pass < c.passes) return;
+  c.pass = 0;
+  if (++c.tile < tiles) return;
+  c.tile = 0;
+  ++c.slot;                          // may step one past the last slot: arrays hold E + 1 entries
+  c.passes = passes_of(m.n[c.slot]);
 }
 
 __device__ __forceinline__ void cta_range(int total, int& q0, int& q1) {
@@ -270,9 +284,12 @@ struct GateUpCfg {
   static constexpr int kStages = kF32 ? 3 : 5;
   static constexpr int kRows = 32;
   static constexpr int kKch = 1024;                                  // K elements per task
+  static constexpr int kWch = kKch / 32;                             // 16-byte weight chunks per row
+  static constexpr int kPairs = kKch / G / 2;                        // 4-byte scale pairs per row
   static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);    // conflict-free A reads
   static constexpr int kScaleRow = kKch / G * 2;
   static constexpr int kBRowBytes = kKch * (int)sizeof(XT);
+  static constexpr int kBch = kBRowBytes / 16;                       // 16-byte B chunks per token
   static constexpr int kBPad = (G == 32 && !kF32) ? 64 : 16;         // conflict-free B reads
   static constexpr int kBStride = kBRowBytes + kBPad;
   static constexpr int kW = 0;
@@ -280,7 +297,6 @@ struct GateUpCfg {
   static constexpr int kB = kS + kRows * kScaleRow;
   static constexpr int kStage = (kB + kTok * kBStride + 127) / 128 * 128;
   static constexpr int kRed = kWarps * 8 * 32 * 4;
-  static constexpr int kBChunks = kBRowBytes / 16;                   // per token row
 };
 
 template <int G, typename XT>
@@ -294,7 +310,7 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
   extern __shared__ __align__(128) uint8_t smem[];
   float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [kWarps][8][32]
   int* mbase = reinterpret_cast<int*>(smem + S * C::kStage + C::kRed);
-  const Meta meta{mbase, mbase + E, mbase + 2 * E, mbase + 3 * E};
+  const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
   const int tiles = I / 16;
@@ -307,64 +323,71 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
   int q0, q1;
   cta_range(total, q0, q1);
   const int ntask = (q1 - q0) * nkc;
+  if (ntask == 0) return;
 
   // B-copy assignment of this thread: token bn, 16-byte chunks bc, bc+64, ...
   const int bn = threadIdx.x >> 6;
   const int bc = threadIdx.x & 63;
-  auto token_of = [&](int task) -> int {
-    if (task >= ntask) return -1;
-    const Item it = decode_item(q0 + task / nkc, na, tiles, meta);
-    const int rr = it.p0 + bn;
-    return rr < it.n ? __ldg(row_token + it.row0 + rr) : -1;
+  auto token_of = [&](const Cursor& cu) -> int {
+    const int rr = cu.pass * kTok + bn;
+    return rr < meta.n[cu.slot] ? __ldg(row_token + meta.row0[cu.slot] + rr) : -1;
   };
-  auto issue = [&](int task, int tok) {
-    const int kc = task % nkc;
-    const Item it = decode_item(q0 + task / nkc, na, tiles, meta);
+  auto issue = [&](const Cursor& cu, int task, int tok) {
     uint8_t* st = smem + (task % S) * C::kStage;
-    const int k0 = kc * C::kKch;
+    const int k0 = cu.kc * C::kKch;
     const int kel = min(C::kKch, H - k0);
-    const size_t erow = (size_t)it.e * 2 * I;
-    const int i0 = it.tile * 16;
-    const int wch = kel / 32;  // 16-byte chunks of packed weights per row
-    for (int q = threadIdx.x; q < C::kRows * wch; q += kThreads) {
-      const int rr = q / wch, cc = q - rr * wch;
-      const size_t grow = erow + (rr < 16 ? i0 + rr : I + i0 + rr - 16);
-      cp_async16(smem_u32(st + C::kW + rr * C::kWStride + cc * 16), w13_q + grow * row_bytes + k0 / 2 + cc * 16);
+    const size_t erow = (size_t)meta.e[cu.slot] * 2 * I;
+    const int i0 = cu.tile * 16;
+#pragma unroll
+    for (int q = threadIdx.x; q < C::kRows * C::kWch; q += kThreads) {
+      const int rr = q / C::kWch, cc = q % C::kWch;
+      if (cc * 32 < kel) {
+        const size_t grow = erow + (rr < 16 ? i0 + rr : I + i0 + rr - 16);
+        cp_async16(smem_u32(st + C::kW + rr * C::kWStride + cc * 16), w13_q + grow * row_bytes + k0 / 2 + cc * 16);
+      }
     }
-    const int npair = kel / G / 2;
-    for (int q = threadIdx.x; q < C::kRows * npair; q += kThreads) {
-      const int rr = q / npair, pp = q - rr * npair;
-      const size_t grow = erow + (rr < 16 ? i0 + rr : I + i0 + rr - 16);
-      cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + grow * NG + k0 / G + 2 * pp);
+#pragma unroll
+    for (int q = threadIdx.x; q < C::kRows * C::kPairs; q += kThreads) {
+      const int rr = q / C::kPairs, pp = q % C::kPairs;
+      if (pp * 2 * G < kel) {
+        const size_t grow = erow + (rr < 16 ? i0 + rr : I + i0 + rr - 16);
+        cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + grow * NG + k0 / G + 2 * pp);
+      }
     }
     if (tok >= 0) {
-      const int bch = kel * (int)sizeof(XT) / 16;
       const uint8_t* src = reinterpret_cast<const uint8_t*>(x + (size_t)tok * H + k0);
-      for (int cc = bc; cc < bch; cc += 64)
-        cp_async16(smem_u32(st + C::kB + bn * C::kBStride + cc * 16), src + cc * 16);
+      const int bch = kel * (int)sizeof(XT) / 16;
+#pragma unroll
+      for (int cc = bc; cc < C::kBch; cc += 64)
+        if (cc < bch) cp_async16(smem_u32(st + C::kB + bn * C::kBStride + cc * 16), src + cc * 16);
     }
   };
 
+  Cursor ci = cursor_at(q0, na, tiles, meta);  // next task to issue
   for (int s = 0; s < S - 1; ++s) {
-    if (s < ntask) issue(s, token_of(s));
+    if (s < ntask) issue(ci, s, token_of(ci));
     cp_async_commit();
+    cursor_next(ci, tiles, nkc, meta);
   }
-  int next_tok = token_of(S - 1);
+  Cursor ct = ci;  // task S-1: its token id is loaded one iteration ahead
+  int next_tok = (S - 1 < ntask) ? token_of(ct) : -1;
+  cursor_next(ct, tiles, nkc, meta);
+  Cursor cm = cursor_at(q0, na, tiles, meta);  // task being computed
 
   float acc_g[4], acc_u[4];
   const int a_off = (G == 64) ? 8 * c : 4 * c;
   const int b_off = (G == 64 ? 16 : 8) * c * (int)sizeof(XT);
   for (int task = 0; task < ntask; ++task) {
-    if (task + S - 1 < ntask) issue(task + S - 1, next_tok);
+    if (task + S - 1 < ntask) issue(ci, task + S - 1, next_tok);
     cp_async_commit();
-    next_tok = token_of(task + S);  // consumed by the next iteration's issue
-    const int kc = task % nkc;
-    const Item it = decode_item(q0 + task / nkc, na, tiles, meta);
-    if (kc == 0) {
+    cursor_next(ci, tiles, nkc, meta);
+    next_tok = (task + S < ntask) ? token_of(ct) : -1;  // consumed by the next iteration's issue
+    cursor_next(ct, tiles, nkc, meta);
+    if (cm.kc == 0) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) { acc_g[q] = 0.f; acc_u[q] = 0.f; }
     }
-    const int ngt = min(C::kKch, H - kc * C::kKch) / G;
+    const int ngt = min(C::kKch, H - cm.kc * C::kKch) / G;
     cp_async_wait<S - 1>();
     __syncthreads();
     const uint8_t* st = smem + (task % S) * C::kStage;
@@ -385,7 +408,7 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
                                __half2float(sc[(r + 8) * kScH + g]), __half2float(sc[(16 + r) * kScH + g]),
                                __half2float(sc[(24 + r) * kScH + g]), acc_g, acc_u);
     }
-    if (kc == nkc - 1) {
+    if (cm.kc == nkc - 1) {
       // reduce the K-slices in warp order, then SwiGLU
       float* mine = red + warp * 8 * 32;
 #pragma unroll
@@ -404,22 +427,24 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
             us[q] += red[w * 256 + (4 + q) * 32 + lane];
           }
         }
-        const int i0 = it.tile * 16;
+        const int n = meta.n[cm.slot], row0 = meta.row0[cm.slot];
+        const int i0 = cm.tile * 16, p0 = cm.pass * kTok;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int i = i0 + r + (q >= 2 ? 8 : 0);
-          const int rr = it.p0 + 2 * c + (q & 1);
-          if (rr < it.n) {
+          const int rr = p0 + 2 * c + (q & 1);
+          if (rr < n) {
             const float hv = silu_f32(gs[q]) * us[q];
             const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
             const __nv_bfloat16 lb = __float2bfloat16_rn(hv - __bfloat162float(hb));
-            const size_t o = (size_t)(it.row0 + rr) * I + i;
+            const size_t o = (size_t)(row0 + rr) * I + i;
             h_hi[o] = hb;
             h_lo[o] = lb;
           }
         }
       }
     }
+    cursor_next(cm, tiles, nkc, meta);
     __syncthreads();  // stage (task % S) and `red` are free again
   }
   cp_async_wait<0>();
@@ -433,9 +458,12 @@ struct DownCfg {
   static constexpr int kStages = 3;
   static constexpr int kRows = 128;
   static constexpr int kKch = 512;
+  static constexpr int kWch = kKch / 32;
+  static constexpr int kPairs = kKch / G / 2;
   static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);
   static constexpr int kScaleRow = kKch / G * 2;
   static constexpr int kBRowBytes = kKch * 2;  // one bf16 plane
+  static constexpr int kBch = kBRowBytes / 16;
   static constexpr int kBStride = kBRowBytes + (G == 64 ? 16 : 64);
   static constexpr int kW = 0;
   static constexpr int kS = kRows * kWStride;
@@ -455,7 +483,7 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
   extern __shared__ __align__(128) uint8_t smem[];
   float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [8][4][32]
   int* mbase = reinterpret_cast<int*>(smem + S * C::kStage + C::kRed);
-  const Meta meta{mbase, mbase + E, mbase + 2 * E, mbase + 3 * E};
+  const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
   const int rb = warp & 7, kh = warp >> 3;  // row block, K half
@@ -469,57 +497,63 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
   int q0, q1;
   cta_range(total, q0, q1);
   const int ntask = (q1 - q0) * nkc;
+  if (ntask == 0) return;
 
-  auto issue = [&](int task) {
-    const int kc = task % nkc;
-    const Item it = decode_item(q0 + task / nkc, na, tiles, meta);
+  auto issue = [&](const Cursor& cu, int task) {
     uint8_t* st = smem + (task % S) * C::kStage;
-    const int k0 = kc * C::kKch;
+    const int k0 = cu.kc * C::kKch;
     const int kel = min(C::kKch, I - k0);
-    const size_t rbase = (size_t)it.e * H + (size_t)it.tile * C::kRows;
-    const int wch = kel / 32;
-    for (int q = threadIdx.x; q < C::kRows * wch; q += kThreads) {
-      const int rr = q / wch, cc = q - rr * wch;
-      cp_async16(smem_u32(st + C::kW + rr * C::kWStride + cc * 16), w2_q + (rbase + rr) * row_bytes + k0 / 2 + cc * 16);
+    const size_t rbase = (size_t)meta.e[cu.slot] * H + (size_t)cu.tile * C::kRows;
+#pragma unroll
+    for (int q = threadIdx.x; q < C::kRows * C::kWch; q += kThreads) {
+      const int rr = q / C::kWch, cc = q % C::kWch;
+      if (cc * 32 < kel)
+        cp_async16(smem_u32(st + C::kW + rr * C::kWStride + cc * 16), w2_q + (rbase + rr) * row_bytes + k0 / 2 + cc * 16);
     }
-    const int npair = kel / G / 2;
-    for (int q = threadIdx.x; q < C::kRows * npair; q += kThreads) {
-      const int rr = q / npair, pp = q - rr * npair;
-      cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
+#pragma unroll
+    for (int q = threadIdx.x; q < C::kRows * C::kPairs; q += kThreads) {
+      const int rr = q / C::kPairs, pp = q % C::kPairs;
+      if (pp * 2 * G < kel)
+        cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
     }
     // h rows of the pass (both planes), this K-chunk
-    const int nt = min(kTok, it.n - it.p0);
-    const int bch = kel * 2 / 16;
-    for (int q = threadIdx.x; q < 2 * nt * bch; q += kThreads) {
-      const int pl = q / (nt * bch);
-      const int rem = q - pl * nt * bch;
-      const int n = rem / bch, cc = rem - n * bch;
-      const __nv_bfloat16* src = (pl ? h_lo : h_hi) + (size_t)(it.row0 + it.p0 + n) * I + k0;
-      cp_async16(smem_u32(st + C::kB + (pl * kTok + n) * C::kBStride + cc * 16),
-                 reinterpret_cast<const uint8_t*>(src) + cc * 16);
+    const int row_p = meta.row0[cu.slot] + cu.pass * kTok;
+    const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
+#pragma unroll
+    for (int q = threadIdx.x; q < 2 * kTok * C::kBch; q += kThreads) {
+      const int pl = q / (kTok * C::kBch);
+      const int n = (q / C::kBch) % kTok, cc = q % C::kBch;
+      if (n < nt && cc * 8 < kel) {
+        const __nv_bfloat16* src = (pl ? h_lo : h_hi) + (size_t)(row_p + n) * I + k0;
+        cp_async16(smem_u32(st + C::kB + (pl * kTok + n) * C::kBStride + cc * 16),
+                   reinterpret_cast<const uint8_t*>(src) + cc * 16);
+      }
     }
   };
 
+  Cursor ci = cursor_at(q0, na, tiles, meta);
   for (int s = 0; s < S - 1; ++s) {
-    if (s < ntask) issue(s);
+    if (s < ntask) issue(ci, s);
     cp_async_commit();
+    cursor_next(ci, tiles, nkc, meta);
   }
+  Cursor cm = cursor_at(q0, na, tiles, meta);
 
   float acc[4];
   const int lr0 = rb * 16 + r;
   const int a_off = (G == 64) ? 8 * c : 4 * c;
   const int b_off = (G == 64 ? 32 : 16) * c;
   for (int task = 0; task < ntask; ++task) {
-    if (task + S - 1 < ntask) issue(task + S - 1);
+    if (task + S - 1 < ntask) issue(ci, task + S - 1);
     cp_async_commit();
-    const int kc = task % nkc;
-    const Item it = decode_item(q0 + task / nkc, na, tiles, meta);
-    if (kc == 0) {
+    cursor_next(ci, tiles, nkc, meta);
+    if (cm.kc == 0) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[q] = 0.f;
     }
-    const int ngt = min(C::kKch, I - kc * C::kKch) / G;
-    const bool tok_ok = it.p0 + r < it.n;  // B rows beyond the pass hold stale data: use zeros
+    const int ngt = min(C::kKch, I - cm.kc * C::kKch) / G;
+    const int n = meta.n[cm.slot], p0 = cm.pass * kTok;
+    const bool tok_ok = p0 + r < n;  // B rows beyond the pass hold stale data: use zeros
     cp_async_wait<S - 1>();
     __syncthreads();
     const uint8_t* st = smem + (task % S) * C::kStage;
@@ -541,22 +575,24 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
       }
       down_group<G>(a0, a8, b, __half2float(sc[lr0 * kScH + g]), __half2float(sc[(lr0 + 8) * kScH + g]), acc);
     }
-    if (kc == nkc - 1) {
+    if (cm.kc == nkc - 1) {
       if (kh == 1) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) red[(rb * 4 + q) * 32 + lane] = acc[q];
       }
       __syncthreads();
       if (kh == 0) {
+        const int row0 = meta.row0[cm.slot];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const float v = acc[q] + red[(rb * 4 + q) * 32 + lane];
-          const int hrow = it.tile * C::kRows + lr0 + (q >= 2 ? 8 : 0);
-          const int rr = it.p0 + 2 * c + (q & 1);
-          if (rr < it.n) y[(size_t)(it.row0 + rr) * H + hrow] = v;
+          const int hrow = cm.tile * C::kRows + lr0 + (q >= 2 ? 8 : 0);
+          const int rr = p0 + 2 * c + (q & 1);
+          if (rr < n) y[(size_t)(row0 + rr) * H + hrow] = v;
         }
       }
     }
+    cursor_next(cm, tiles, nkc, meta);
     __syncthreads();  // stage (task % S) and `red` are free again
   }
   cp_async_wait<0>();
