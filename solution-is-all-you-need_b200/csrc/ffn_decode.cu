@@ -278,12 +278,14 @@ __device__ __forceinline__ void cta_range(int total, int& q0, int& q1) {
 // ---------------------------------------------------------------------------
 // gate/up + SwiGLU
 // ---------------------------------------------------------------------------
-template <int G, typename XT>
+// KCH = K elements per task: 2048 (3 stages) amortises the per-task barriers
+// over twice the bytes; 1024 (5 stages, 3 for fp32) when 2048 does not fit.
+template <int G, typename XT, int KCH>
 struct GateUpCfg {
   static constexpr bool kF32 = std::is_same<XT, float>::value;
-  static constexpr int kStages = kF32 ? 3 : 5;
+  static constexpr int kStages = KCH == 2048 ? 3 : (kF32 ? 3 : 5);
   static constexpr int kRows = 32;
-  static constexpr int kKch = 1024;                                  // K elements per task
+  static constexpr int kKch = KCH;
   static constexpr int kWch = kKch / 32;                             // 16-byte weight chunks per row
   static constexpr int kPairs = kKch / G / 2;                        // 4-byte scale pairs per row
   static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);    // conflict-free A reads
@@ -299,13 +301,13 @@ struct GateUpCfg {
   static constexpr int kRed = kWarps * 8 * 32 * 4;
 };
 
-template <int G, typename XT>
+template <int G, typename XT, int KCH>
 __global__ void __launch_bounds__(kThreads, 1)
 ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_token,
                   const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                   const uint8_t* __restrict__ w13_q, const uint16_t* __restrict__ w13_s, int H, int I,
                   int E, __nv_bfloat16* __restrict__ h_hi, __nv_bfloat16* __restrict__ h_lo) {
-  using C = GateUpCfg<G, XT>;
+  using C = GateUpCfg<G, XT, KCH>;
   constexpr int S = C::kStages;
   extern __shared__ __align__(128) uint8_t smem[];
   float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [kWarps][8][32]
@@ -417,30 +419,26 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
         mine[(4 + q) * 32 + lane] = acc_u[q];
       }
       __syncthreads();
-      if (warp == 0) {
-        float gs[4] = {0.f, 0.f, 0.f, 0.f}, us[4] = {0.f, 0.f, 0.f, 0.f};
+      // 128 threads finish the 4 x 32 fragment slots: thread (q, ln) sums
+      // slot q of lane ln over the warps in order 0..15.
+      if (threadIdx.x < 128) {
+        const int q = threadIdx.x >> 5, ln = threadIdx.x & 31;
+        float gs = 0.f, us = 0.f;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            gs[q] += red[w * 256 + q * 32 + lane];
-            us[q] += red[w * 256 + (4 + q) * 32 + lane];
-          }
+          gs += red[w * 256 + q * 32 + ln];
+          us += red[w * 256 + (4 + q) * 32 + ln];
         }
         const int n = meta.n[cm.slot], row0 = meta.row0[cm.slot];
-        const int i0 = cm.tile * 16, p0 = cm.pass * kTok;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int i = i0 + r + (q >= 2 ? 8 : 0);
-          const int rr = p0 + 2 * c + (q & 1);
-          if (rr < n) {
-            const float hv = silu_f32(gs[q]) * us[q];
-            const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
-            const __nv_bfloat16 lb = __float2bfloat16_rn(hv - __bfloat162float(hb));
-            const size_t o = (size_t)(row0 + rr) * I + i;
-            h_hi[o] = hb;
-            h_lo[o] = lb;
-          }
+        const int i = cm.tile * 16 + (ln >> 2) + (q >= 2 ? 8 : 0);
+        const int rr = cm.pass * kTok + 2 * (ln & 3) + (q & 1);
+        if (rr < n) {
+          const float hv = silu_f32(gs) * us;
+          const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
+          const __nv_bfloat16 lb = __float2bfloat16_rn(hv - __bfloat162float(hb));
+          const size_t o = (size_t)(row0 + rr) * I + i;
+          h_hi[o] = hb;
+          h_lo[o] = lb;
         }
       }
     }
@@ -603,9 +601,11 @@ void set_smem(K kern, size_t bytes) {
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
-template <int G, typename XT>
+constexpr size_t kMaxSmem = 227 * 1024;
+
+template <int G, typename XT, int KCH>
 size_t gateup_smem(int E) {
-  using C = GateUpCfg<G, XT>;
+  using C = GateUpCfg<G, XT, KCH>;
   return (size_t)C::kStages * C::kStage + C::kRed + (size_t)(4 * E + 4) * 4;
 }
 
@@ -615,15 +615,29 @@ size_t down_smem(int E) {
   return (size_t)C::kStages * C::kStage + C::kRed + (size_t)(4 * E + 4) * 4;
 }
 
+template <int G, typename XT, int KCH>
+void launch_gateup_k(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
+                     const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
+                     __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
+  const size_t smem = gateup_smem<G, XT, KCH>(E);
+  auto k = ffn_gateup_kernel<G, XT, KCH>;
+  set_smem(k, smem);
+  k<<<grid, kThreads, smem, st>>>(static_cast<const XT*>(x), row_token, offsets, active, w13_q, w13_s, H, I,
+                                  E, h_hi, h_lo);
+}
+
+// 2048-element tasks for bf16 activations when H needs them and they fit.
 template <int G, typename XT>
 void launch_gateup(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
                    const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
                    __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
-  const size_t smem = gateup_smem<G, XT>(E);
-  auto k = ffn_gateup_kernel<G, XT>;
-  set_smem(k, smem);
-  k<<<grid, kThreads, smem, st>>>(static_cast<const XT*>(x), row_token, offsets, active, w13_q, w13_s, H, I,
-                                  E, h_hi, h_lo);
+  if constexpr (!std::is_same<XT, float>::value) {
+    if (H > 1024 && gateup_smem<G, XT, 2048>(E) <= kMaxSmem) {
+      launch_gateup_k<G, XT, 2048>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
+      return;
+    }
+  }
+  launch_gateup_k<G, XT, 1024>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
 }
 
 template <int G>
