@@ -165,6 +165,14 @@ int phmoe_quantize_int4(const void* w, int w_dtype, long long rows, int K, int g
  * not thread-safe; do not profile inside stream capture.
  */
 #define PHMOE_NUM_STAGES 5
+
+/*
+ * Device-side error word of the current device: 0 when every pipeline wait
+ * of the FFN kernels completed; 1 when one timed out (its CTA abandoned its
+ * work after a bounded wait instead of hanging). Synchronous; reset != 0
+ * clears it. Not part of the hot path.
+ */
+int phmoe_device_error(int reset);
 unsigned long long phmoe_kernel_launch_count(void);
 int phmoe_profile_begin(int max_calls);
 int phmoe_profile_end(float* stage_ms, int n_stages, int* calls);

@@ -303,6 +303,8 @@ int phmoe_quantize_int4(const void* w, int w_dtype, long long rows, int K, int g
 
 unsigned long long phmoe_kernel_launch_count(void) { return g_launches.load(); }
 
+int phmoe_device_error(int reset) { return ffn_device_error(reset != 0); }
+
 int phmoe_profile_begin(int max_calls) {
   g_last_error.clear();
   if (max_calls < 0 || max_calls > (1 << 20)) return fail(PHMOE_ERR_INVALID_ARG, "bad max_calls %d", max_calls);

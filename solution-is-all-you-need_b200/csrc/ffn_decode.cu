@@ -8,23 +8,24 @@
 //
 // Design. At decode sizes the layer streams ~2.5 MB of packed weights per
 // expert hit and does a few FMAs per weight: the bound is HBM. Both kernels
-// are persistent (one 512-thread CTA per SM, a contiguous range of work items
-// each) and run a multi-stage cp.async pipeline over "tasks" (a work item's
-// K-chunk). A stage holds everything a task reads: the packed int4 weight
-// rows, their fp16 scales and the K-chunk of the activation rows (B). While
-// the 16 warps compute task t, tasks t+1.. are in flight from HBM/L2, so the
-// compute loop issues no global loads. Rows are padded so that every
-// fragment read is bank-conflict free (fp32 activations excepted).
-//
+// are persistent (one CTA per SM, a contiguous range of work items each) and
+// warp-specialised:
+//  * one producer warp streams "tasks" (a work item's K-chunk) into a ring of
+//    shared-memory stages: each packed weight row and each activation row is
+//    ONE cp.async.bulk (TMA bulk copy) whose completion is counted in bytes on
+//    the stage's "full" mbarrier; the fp16 scale slices arrive by 4-byte
+//    cp.async tracked on the same barrier (cp.async.mbarrier.arrive.noinc);
+//  * 16 consumer warps wait on "full", compute, and release the stage on its
+//    "empty" mbarrier. No CTA-wide barrier is ever taken.
 // From shared memory each lane reads the int4 words of its A fragments and
 // turns each 32-bit word (8 consecutive weights) into four bf16x2 pairs with
-// one lop3 each (see the packed layout in phmoe.h); the pairs feed mma.sync
-// m16n8k16 directly, with the 8 tokens of a pass as the N side. Dequantised
-// weights are never written back to shared memory (bf16 would be 4x the int4
-// bytes). In gate/up the unpacked values are 128 + nibble and the +136
-// offset is removed after the MMA with one extra MMA per K step against an
-// all-ones A (it yields sum_k x_k); the fp16 group scale multiplies the fp32
-// partial of each group. Both steps are exact factorisations.
+// one lop3 each (packed layout in phmoe.h); the pairs feed mma.sync m16n8k16
+// directly, with the 8 tokens of a pass as the N side. Dequantised weights
+// are never written back to shared memory (bf16 would be 4x the int4 bytes).
+// In gate/up the unpacked values are 128 + nibble and the +136 offset is
+// removed after the MMA with one extra MMA per K step against an all-ones A
+// (it yields sum_k x_k); the fp16 group scale multiplies the fp32 partial of
+// each group. Both are exact factorisations.
 //
 // Lane c of a quad holds K elements 16c..16c+15 of a 64-group (8c..8c+7 of a
 // 32-group) for A and reads the same activations for B; inside one MMA the K
@@ -36,39 +37,88 @@
 // ~16 significant bits.
 //
 // gate/up kernel: item = (expert, 16 intermediate rows, pass of 8 tokens) ->
-//   32 weight rows (16 gate + 16 up); the 16 warps split each K-chunk and are
-//   reduced through shared memory in warp order (deterministic); SwiGLU in
-//   the epilogue, h stored as bf16 hi/lo planes.
-// down kernel: item = (expert, 128 output rows, pass); warp w owns rows
-//   16(w%8)..+15 and half of each K-chunk (w/8); the halves are added in a
-//   fixed order.
+//   32 weight rows (16 gate + 16 up); the consumer warps split each K-chunk
+//   and their partials are summed in warp order (deterministic) by 4 warps
+//   that apply SwiGLU and store h as bf16 hi/lo planes.
+// down kernel: item = (expert, 128 output rows, pass); consumer warp w owns
+//   rows 16(w%8)..+15 and half of each K-chunk (w/8); the halves are added in
+//   a fixed order.
 // Items are ordered (expert, tile, pass) so the extra passes of an expert
 // with more than 8 rows re-read weights that are still in L2.
+//
+// Every wait is bounded: after kSpinLimit polls a warp raises the CTA's abort
+// flag and the device error word (read by phmoe_ffn_device_error), and all
+// warps leave; the producer first waits (bounded) for its copies in flight.
 #include "common.cuh"
 #include "launch.h"
 
 namespace phmoe {
 
+__device__ int g_ffn_error;  // 0 = ok, 1 = a pipeline wait timed out
+
 namespace {
 
-constexpr int kWarps = 16;
-constexpr int kThreads = kWarps * 32;
-constexpr int kTok = 8;  // tokens per pass (the MMA N dimension)
+constexpr int kConsumers = 16;                  // consumer warps
+constexpr int kThreads = (kConsumers + 1) * 32; // + 1 producer warp
+constexpr int kTok = 8;                         // tokens per pass (the MMA N dimension)
+constexpr uint32_t kSpinLimit = 1u << 22;       // try_wait polls before giving up
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(g) : "memory");
-}
 __device__ __forceinline__ void cp_async4(uint32_t saddr, const void* g) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(saddr), "l"(g) : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
 }
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+// One poll; the thread may be suspended up to ~1 us inside it.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(done) : "r"(bar), "r"(parity), "r"(1000u) : "memory");
+  return done != 0;
+}
+// Arrive on `bar` once every cp.async this thread issued so far has landed.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
+}
+// One bulk (TMA) copy global -> shared, completion counted on `bar` in bytes.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+               ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+
+// Bounded wait on a barrier phase. Returns false when this CTA aborts.
+__device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort_flag) return false;
+  }
+  *abort_flag = 1;
+  atomicExch(&g_ffn_error, 1);
+  return false;
+}
+
+// Shared-memory control block of a CTA: stage barriers, reduction-buffer
+// barriers, abort flag.
+template <int S>
+struct Ctl {
+  uint64_t full[S];
+  uint64_t empty[S];
+  uint64_t red_full[2];
+  uint64_t red_empty[2];
+  int abort_flag;
+};
 
 // ---------------------------------------------------------------------------
 // fragments
@@ -278,125 +328,132 @@ __device__ __forceinline__ void cta_range(int total, int& q0, int& q1) {
 // ---------------------------------------------------------------------------
 // gate/up + SwiGLU
 // ---------------------------------------------------------------------------
-// KCH = K elements per task: 2048 (3 stages) amortises the per-task barriers
-// over twice the bytes; 1024 (5 stages, 3 for fp32) when 2048 does not fit.
-template <int G, typename XT, int KCH>
+template <int G, typename XT>
 struct GateUpCfg {
   static constexpr bool kF32 = std::is_same<XT, float>::value;
-  static constexpr int kStages = KCH == 2048 ? 3 : (kF32 ? 3 : 5);
+  static constexpr int kStages = kF32 ? 3 : 5;
   static constexpr int kRows = 32;
-  static constexpr int kKch = KCH;
-  static constexpr int kWch = kKch / 32;                             // 16-byte weight chunks per row
+  static constexpr int kKch = 1024;                                  // K elements per task
   static constexpr int kPairs = kKch / G / 2;                        // 4-byte scale pairs per row
   static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);    // conflict-free A reads
   static constexpr int kScaleRow = kKch / G * 2;
   static constexpr int kBRowBytes = kKch * (int)sizeof(XT);
-  static constexpr int kBch = kBRowBytes / 16;                       // 16-byte B chunks per token
   static constexpr int kBPad = (G == 32 && !kF32) ? 64 : 16;         // conflict-free B reads
   static constexpr int kBStride = kBRowBytes + kBPad;
   static constexpr int kW = 0;
   static constexpr int kS = kRows * kWStride;
   static constexpr int kB = kS + kRows * kScaleRow;
   static constexpr int kStage = (kB + kTok * kBStride + 127) / 128 * 128;
-  static constexpr int kRed = kWarps * 8 * 32 * 4;
+  static constexpr int kRedBuf = kConsumers * 8 * 32 * 4;            // one partial-sum buffer
+  static constexpr size_t smem(int E) {
+    return (size_t)kStages * kStage + 2 * kRedBuf + sizeof(Ctl<kStages>) + (size_t)(4 * E + 4) * 4;
+  }
 };
 
-template <int G, typename XT, int KCH>
+template <int G, typename XT>
 __global__ void __launch_bounds__(kThreads, 1)
 ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_token,
                   const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                   const uint8_t* __restrict__ w13_q, const uint16_t* __restrict__ w13_s, int H, int I,
                   int E, __nv_bfloat16* __restrict__ h_hi, __nv_bfloat16* __restrict__ h_lo) {
-  using C = GateUpCfg<G, XT, KCH>;
+  using C = GateUpCfg<G, XT>;
   constexpr int S = C::kStages;
   extern __shared__ __align__(128) uint8_t smem[];
-  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [kWarps][8][32]
-  int* mbase = reinterpret_cast<int*>(smem + S * C::kStage + C::kRed);
+  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [2][kConsumers][8][32]
+  Ctl<S>* ctl = reinterpret_cast<Ctl<S>*>(smem + S * C::kStage + 2 * C::kRedBuf);
+  int* mbase = reinterpret_cast<int*>(ctl + 1);
   const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
+  volatile int* abort_flag = &ctl->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = lane >> 2, c = lane & 3;
   const int tiles = I / 16;
   const int NG = H / G;
   const int nkc = (H + C::kKch - 1) / C::kKch;
   const size_t row_bytes = (size_t)H / 2;
   const int na = active[0];
 
-  const int total = build_meta(offsets, active, tiles, meta);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(&ctl->full[s]), 1 + 32);  // expect_tx arrive + 32 cp.async arrivals
+      mbar_init(smem_u32(&ctl->empty[s]), kConsumers * 32);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&ctl->red_full[b]), kConsumers * 32);
+      mbar_init(smem_u32(&ctl->red_empty[b]), 4 * 32);
+    }
+    ctl->abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  const int total = build_meta(offsets, active, tiles, meta);  // its barriers publish the init too
   int q0, q1;
   cta_range(total, q0, q1);
   const int ntask = (q1 - q0) * nkc;
   if (ntask == 0) return;
 
-  // B-copy assignment of this thread: token bn, 16-byte chunks bc, bc+64, ...
-  const int bn = threadIdx.x >> 6;
-  const int bc = threadIdx.x & 63;
-  auto token_of = [&](const Cursor& cu) -> int {
-    const int rr = cu.pass * kTok + bn;
-    return rr < meta.n[cu.slot] ? __ldg(row_token + meta.row0[cu.slot] + rr) : -1;
-  };
-  auto issue = [&](const Cursor& cu, int task, int tok) {
-    uint8_t* st = smem + (task % S) * C::kStage;
-    const int k0 = cu.kc * C::kKch;
-    const int kel = min(C::kKch, H - k0);
-    const size_t erow = (size_t)meta.e[cu.slot] * 2 * I;
-    const int i0 = cu.tile * 16;
+  if (warp == kConsumers) {
+    // ---------------- producer warp ----------------
+    Cursor cu = cursor_at(q0, na, tiles, meta);
+    auto token = [&](const Cursor& k) -> int {
+      const int rr = k.pass * kTok + lane;
+      return (lane < kTok && rr < meta.n[k.slot]) ? __ldg(row_token + meta.row0[k.slot] + rr) : -1;
+    };
+    int tok = token(cu);
+    int issued = 0;
+    for (int t = 0; t < ntask; ++t) {
+      const int s = t % S;
+      if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
+      Cursor nx = cu;
+      cursor_next(nx, tiles, nkc, meta);
+      const int tok_next = t + 1 < ntask ? token(nx) : -1;  // hidden behind this task's issue
+      const int k0 = cu.kc * C::kKch;
+      const int kel = min(C::kKch, H - k0);
+      const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
+      const uint32_t full = smem_u32(&ctl->full[s]);
+      uint8_t* st = smem + s * C::kStage;
+      if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(C::kRows * (kel / 2) + nt * kel * (int)sizeof(XT)));
+      __syncwarp();
+      const int i0 = cu.tile * 16;
+      const size_t grow = (size_t)meta.e[cu.slot] * 2 * I + (lane < 16 ? i0 + lane : I + i0 + lane - 16);
+      bulk_g2s(smem_u32(st + C::kW + lane * C::kWStride), w13_q + grow * row_bytes + k0 / 2, kel / 2, full);
+      if (lane < nt)
+        bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), x + (size_t)tok * H + k0, kel * (int)sizeof(XT), full);
 #pragma unroll
-    for (int q = threadIdx.x; q < C::kRows * C::kWch; q += kThreads) {
-      const int rr = q / C::kWch, cc = q % C::kWch;
-      if (cc * 32 < kel) {
-        const size_t grow = erow + (rr < 16 ? i0 + rr : I + i0 + rr - 16);
-        cp_async16(smem_u32(st + C::kW + rr * C::kWStride + cc * 16), w13_q + grow * row_bytes + k0 / 2 + cc * 16);
+      for (int pp = 0; pp < C::kPairs; ++pp)
+        if (pp * 2 * G < kel)
+          cp_async4(smem_u32(st + C::kS + lane * C::kScaleRow + pp * 4), w13_s + grow * NG + k0 / G + 2 * pp);
+      cp_async_arrive_noinc(full);
+      ++issued;
+      tok = tok_next;
+      cu = nx;
+    }
+    // leave only when every copy issued into this CTA's shared memory has landed
+    for (int t = max(0, issued - S); t < issued; ++t) {
+      const uint32_t full = smem_u32(&ctl->full[t % S]);
+      for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(full, (t / S) & 1); ++i) {
       }
     }
-#pragma unroll
-    for (int q = threadIdx.x; q < C::kRows * C::kPairs; q += kThreads) {
-      const int rr = q / C::kPairs, pp = q % C::kPairs;
-      if (pp * 2 * G < kel) {
-        const size_t grow = erow + (rr < 16 ? i0 + rr : I + i0 + rr - 16);
-        cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + grow * NG + k0 / G + 2 * pp);
-      }
-    }
-    if (tok >= 0) {
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(x + (size_t)tok * H + k0);
-      const int bch = kel * (int)sizeof(XT) / 16;
-#pragma unroll
-      for (int cc = bc; cc < C::kBch; cc += 64)
-        if (cc < bch) cp_async16(smem_u32(st + C::kB + bn * C::kBStride + cc * 16), src + cc * 16);
-    }
-  };
-
-  Cursor ci = cursor_at(q0, na, tiles, meta);  // next task to issue
-  for (int s = 0; s < S - 1; ++s) {
-    if (s < ntask) issue(ci, s, token_of(ci));
-    cp_async_commit();
-    cursor_next(ci, tiles, nkc, meta);
+    return;
   }
-  Cursor ct = ci;  // task S-1: its token id is loaded one iteration ahead
-  int next_tok = (S - 1 < ntask) ? token_of(ct) : -1;
-  cursor_next(ct, tiles, nkc, meta);
-  Cursor cm = cursor_at(q0, na, tiles, meta);  // task being computed
 
-  float acc_g[4], acc_u[4];
+  // ---------------- consumer warps ----------------
+  const int r = lane >> 2, c = lane & 3;
   const int a_off = (G == 64) ? 8 * c : 4 * c;
   const int b_off = (G == 64 ? 16 : 8) * c * (int)sizeof(XT);
-  for (int task = 0; task < ntask; ++task) {
-    if (task + S - 1 < ntask) issue(ci, task + S - 1, next_tok);
-    cp_async_commit();
-    cursor_next(ci, tiles, nkc, meta);
-    next_tok = (task + S < ntask) ? token_of(ct) : -1;  // consumed by the next iteration's issue
-    cursor_next(ct, tiles, nkc, meta);
-    if (cm.kc == 0) {
+  constexpr int kScH = C::kScaleRow / 2;
+  Cursor cu = cursor_at(q0, na, tiles, meta);
+  float acc_g[4] = {0.f, 0.f, 0.f, 0.f}, acc_u[4] = {0.f, 0.f, 0.f, 0.f};
+  int item = 0;
+  for (int t = 0; t < ntask; ++t) {
+    const int s = t % S;
+    if (cu.kc == 0) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) { acc_g[q] = 0.f; acc_u[q] = 0.f; }
     }
-    const int ngt = min(C::kKch, H - cm.kc * C::kKch) / G;
-    cp_async_wait<S - 1>();
-    __syncthreads();
-    const uint8_t* st = smem + (task % S) * C::kStage;
+    const int ngt = min(C::kKch, H - cu.kc * C::kKch) / G;
+    if (!wait_phase(smem_u32(&ctl->full[s]), (t / S) & 1, abort_flag)) return;
+    const uint8_t* st = smem + s * C::kStage;
     const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
-    constexpr int kScH = C::kScaleRow / 2;
 #pragma unroll 2
-    for (int g = warp; g < ngt; g += kWarps) {
+    for (int g = warp; g < ngt; g += kConsumers) {
       const uint8_t* ab = st + C::kW + g * (G / 2) + a_off;
       const RowWords<G> ag0 = lds_row<G>(ab + r * C::kWStride);
       const RowWords<G> ag8 = lds_row<G>(ab + (r + 8) * C::kWStride);
@@ -410,28 +467,33 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
                                __half2float(sc[(r + 8) * kScH + g]), __half2float(sc[(16 + r) * kScH + g]),
                                __half2float(sc[(24 + r) * kScH + g]), acc_g, acc_u);
     }
-    if (cm.kc == nkc - 1) {
-      // reduce the K-slices in warp order, then SwiGLU
-      float* mine = red + warp * 8 * 32;
+    mbar_arrive(smem_u32(&ctl->empty[s]));  // this thread is done with the stage
+    if (cu.kc == nkc - 1) {
+      const int buf = item & 1;
+      const int use = item >> 1;
+      float* rb = red + buf * (C::kRedBuf / 4);
+      if (use > 0 && !wait_phase(smem_u32(&ctl->red_empty[buf]), (use - 1) & 1, abort_flag)) return;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        mine[q * 32 + lane] = acc_g[q];
-        mine[(4 + q) * 32 + lane] = acc_u[q];
+        rb[warp * 256 + q * 32 + lane] = acc_g[q];
+        rb[warp * 256 + (4 + q) * 32 + lane] = acc_u[q];
       }
-      __syncthreads();
-      // 128 threads finish the 4 x 32 fragment slots: thread (q, ln) sums
-      // slot q of lane ln over the warps in order 0..15.
-      if (threadIdx.x < 128) {
-        const int q = threadIdx.x >> 5, ln = threadIdx.x & 31;
+      mbar_arrive(smem_u32(&ctl->red_full[buf]));
+      if (warp < 4) {
+        // thread (q = warp, ln = lane) finishes fragment slot q of lane ln,
+        // summing the consumer warps' partials in order 0..15, then SwiGLU
+        if (!wait_phase(smem_u32(&ctl->red_full[buf]), use & 1, abort_flag)) return;
+        const int q = warp, ln = lane;
         float gs = 0.f, us = 0.f;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-          gs += red[w * 256 + q * 32 + ln];
-          us += red[w * 256 + (4 + q) * 32 + ln];
+        for (int w = 0; w < kConsumers; ++w) {
+          gs += rb[w * 256 + q * 32 + ln];
+          us += rb[w * 256 + (4 + q) * 32 + ln];
         }
-        const int n = meta.n[cm.slot], row0 = meta.row0[cm.slot];
-        const int i = cm.tile * 16 + (ln >> 2) + (q >= 2 ? 8 : 0);
-        const int rr = cm.pass * kTok + 2 * (ln & 3) + (q & 1);
+        mbar_arrive(smem_u32(&ctl->red_empty[buf]));
+        const int n = meta.n[cu.slot], row0 = meta.row0[cu.slot];
+        const int i = cu.tile * 16 + (ln >> 2) + (q >= 2 ? 8 : 0);
+        const int rr = cu.pass * kTok + 2 * (ln & 3) + (q & 1);
         if (rr < n) {
           const float hv = silu_f32(gs) * us;
           const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
@@ -441,11 +503,10 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
           h_lo[o] = lb;
         }
       }
+      ++item;
     }
-    cursor_next(cm, tiles, nkc, meta);
-    __syncthreads();  // stage (task % S) and `red` are free again
+    cursor_next(cu, tiles, nkc, meta);
   }
-  cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------------------
@@ -456,18 +517,19 @@ struct DownCfg {
   static constexpr int kStages = 3;
   static constexpr int kRows = 128;
   static constexpr int kKch = 512;
-  static constexpr int kWch = kKch / 32;
   static constexpr int kPairs = kKch / G / 2;
   static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);
   static constexpr int kScaleRow = kKch / G * 2;
   static constexpr int kBRowBytes = kKch * 2;  // one bf16 plane
-  static constexpr int kBch = kBRowBytes / 16;
   static constexpr int kBStride = kBRowBytes + (G == 64 ? 16 : 64);
   static constexpr int kW = 0;
   static constexpr int kS = kRows * kWStride;
   static constexpr int kB = kS + kRows * kScaleRow;             // [2 planes][kTok][kBStride]
   static constexpr int kStage = (kB + 2 * kTok * kBStride + 127) / 128 * 128;
-  static constexpr int kRed = 8 * 4 * 32 * 4;
+  static constexpr int kRedBuf = 8 * 4 * 32 * 4;
+  static constexpr size_t smem(int E) {
+    return (size_t)kStages * kStage + 2 * kRedBuf + sizeof(Ctl<kStages>) + (size_t)(4 * E + 4) * 4;
+  }
 };
 
 template <int G>
@@ -479,84 +541,106 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
   using C = DownCfg<G>;
   constexpr int S = C::kStages;
   extern __shared__ __align__(128) uint8_t smem[];
-  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [8][4][32]
-  int* mbase = reinterpret_cast<int*>(smem + S * C::kStage + C::kRed);
+  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [2][8][4][32]
+  Ctl<S>* ctl = reinterpret_cast<Ctl<S>*>(smem + S * C::kStage + 2 * C::kRedBuf);
+  int* mbase = reinterpret_cast<int*>(ctl + 1);
   const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
+  volatile int* abort_flag = &ctl->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = lane >> 2, c = lane & 3;
-  const int rb = warp & 7, kh = warp >> 3;  // row block, K half
   const int tiles = H / C::kRows;
   const int NG = I / G;
   const int nkc = (I + C::kKch - 1) / C::kKch;
   const size_t row_bytes = (size_t)I / 2;
   const int na = active[0];
 
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(&ctl->full[s]), 1 + 32);
+      mbar_init(smem_u32(&ctl->empty[s]), kConsumers * 32);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&ctl->red_full[b]), 8 * 32);
+      mbar_init(smem_u32(&ctl->red_empty[b]), 8 * 32);
+    }
+    ctl->abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
   const int total = build_meta(offsets, active, tiles, meta);
   int q0, q1;
   cta_range(total, q0, q1);
   const int ntask = (q1 - q0) * nkc;
   if (ntask == 0) return;
 
-  auto issue = [&](const Cursor& cu, int task) {
-    uint8_t* st = smem + (task % S) * C::kStage;
-    const int k0 = cu.kc * C::kKch;
-    const int kel = min(C::kKch, I - k0);
-    const size_t rbase = (size_t)meta.e[cu.slot] * H + (size_t)cu.tile * C::kRows;
+  if (warp == kConsumers) {
+    // ---------------- producer warp ----------------
+    Cursor cu = cursor_at(q0, na, tiles, meta);
+    int issued = 0;
+    for (int t = 0; t < ntask; ++t) {
+      const int s = t % S;
+      if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
+      const int k0 = cu.kc * C::kKch;
+      const int kel = min(C::kKch, I - k0);
+      const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
+      const uint32_t full = smem_u32(&ctl->full[s]);
+      uint8_t* st = smem + s * C::kStage;
+      if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(C::kRows * (kel / 2) + 2 * nt * kel * 2));
+      __syncwarp();
+      const size_t rbase = (size_t)meta.e[cu.slot] * H + (size_t)cu.tile * C::kRows;
 #pragma unroll
-    for (int q = threadIdx.x; q < C::kRows * C::kWch; q += kThreads) {
-      const int rr = q / C::kWch, cc = q % C::kWch;
-      if (cc * 32 < kel)
-        cp_async16(smem_u32(st + C::kW + rr * C::kWStride + cc * 16), w2_q + (rbase + rr) * row_bytes + k0 / 2 + cc * 16);
+      for (int j = 0; j < C::kRows / 32; ++j) {
+        const int rr = lane + 32 * j;
+        bulk_g2s(smem_u32(st + C::kW + rr * C::kWStride), w2_q + (rbase + rr) * row_bytes + k0 / 2, kel / 2, full);
+      }
+      if (lane < 2 * kTok) {
+        const int pl = lane >> 3, n = lane & 7;
+        if (n < nt) {
+          const __nv_bfloat16* src =
+              (pl ? h_lo : h_hi) + (size_t)(meta.row0[cu.slot] + cu.pass * kTok + n) * I + k0;
+          bulk_g2s(smem_u32(st + C::kB + (pl * kTok + n) * C::kBStride), src, kel * 2, full);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < C::kRows / 32; ++j) {
+        const int rr = lane + 32 * j;
+#pragma unroll
+        for (int pp = 0; pp < C::kPairs; ++pp)
+          if (pp * 2 * G < kel)
+            cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
+      }
+      cp_async_arrive_noinc(full);
+      ++issued;
+      cursor_next(cu, tiles, nkc, meta);
     }
-#pragma unroll
-    for (int q = threadIdx.x; q < C::kRows * C::kPairs; q += kThreads) {
-      const int rr = q / C::kPairs, pp = q % C::kPairs;
-      if (pp * 2 * G < kel)
-        cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
-    }
-    // h rows of the pass (both planes), this K-chunk
-    const int row_p = meta.row0[cu.slot] + cu.pass * kTok;
-    const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
-#pragma unroll
-    for (int q = threadIdx.x; q < 2 * kTok * C::kBch; q += kThreads) {
-      const int pl = q / (kTok * C::kBch);
-      const int n = (q / C::kBch) % kTok, cc = q % C::kBch;
-      if (n < nt && cc * 8 < kel) {
-        const __nv_bfloat16* src = (pl ? h_lo : h_hi) + (size_t)(row_p + n) * I + k0;
-        cp_async16(smem_u32(st + C::kB + (pl * kTok + n) * C::kBStride + cc * 16),
-                   reinterpret_cast<const uint8_t*>(src) + cc * 16);
+    for (int t = max(0, issued - S); t < issued; ++t) {
+      const uint32_t full = smem_u32(&ctl->full[t % S]);
+      for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(full, (t / S) & 1); ++i) {
       }
     }
-  };
-
-  Cursor ci = cursor_at(q0, na, tiles, meta);
-  for (int s = 0; s < S - 1; ++s) {
-    if (s < ntask) issue(ci, s);
-    cp_async_commit();
-    cursor_next(ci, tiles, nkc, meta);
+    return;
   }
-  Cursor cm = cursor_at(q0, na, tiles, meta);
 
-  float acc[4];
-  const int lr0 = rb * 16 + r;
+  // ---------------- consumer warps ----------------
+  const int r = lane >> 2, c = lane & 3;
+  const int rbk = warp & 7, kh = warp >> 3;  // row block, K half
+  const int lr0 = rbk * 16 + r;
   const int a_off = (G == 64) ? 8 * c : 4 * c;
   const int b_off = (G == 64 ? 32 : 16) * c;
-  for (int task = 0; task < ntask; ++task) {
-    if (task + S - 1 < ntask) issue(ci, task + S - 1);
-    cp_async_commit();
-    cursor_next(ci, tiles, nkc, meta);
-    if (cm.kc == 0) {
+  constexpr int kScH = C::kScaleRow / 2;
+  Cursor cu = cursor_at(q0, na, tiles, meta);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  int item = 0;
+  for (int t = 0; t < ntask; ++t) {
+    const int s = t % S;
+    if (cu.kc == 0) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[q] = 0.f;
     }
-    const int ngt = min(C::kKch, I - cm.kc * C::kKch) / G;
-    const int n = meta.n[cm.slot], p0 = cm.pass * kTok;
+    const int ngt = min(C::kKch, I - cu.kc * C::kKch) / G;
+    const int n = meta.n[cu.slot], p0 = cu.pass * kTok;
     const bool tok_ok = p0 + r < n;  // B rows beyond the pass hold stale data: use zeros
-    cp_async_wait<S - 1>();
-    __syncthreads();
-    const uint8_t* st = smem + (task % S) * C::kStage;
+    if (!wait_phase(smem_u32(&ctl->full[s]), (t / S) & 1, abort_flag)) return;
+    const uint8_t* st = smem + s * C::kStage;
     const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
-    constexpr int kScH = C::kScaleRow / 2;
 #pragma unroll 2
     for (int g = kh; g < ngt; g += 2) {
       const uint8_t* ab = st + C::kW + g * (G / 2) + a_off;
@@ -573,27 +657,34 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
       }
       down_group<G>(a0, a8, b, __half2float(sc[lr0 * kScH + g]), __half2float(sc[(lr0 + 8) * kScH + g]), acc);
     }
-    if (cm.kc == nkc - 1) {
+    mbar_arrive(smem_u32(&ctl->empty[s]));
+    if (cu.kc == nkc - 1) {
+      const int buf = item & 1;
+      const int use = item >> 1;
+      float* rb = red + buf * (C::kRedBuf / 4);
       if (kh == 1) {
+        if (use > 0 && !wait_phase(smem_u32(&ctl->red_empty[buf]), (use - 1) & 1, abort_flag)) return;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) red[(rb * 4 + q) * 32 + lane] = acc[q];
-      }
-      __syncthreads();
-      if (kh == 0) {
-        const int row0 = meta.row0[cm.slot];
+        for (int q = 0; q < 4; ++q) rb[(rbk * 4 + q) * 32 + lane] = acc[q];
+        mbar_arrive(smem_u32(&ctl->red_full[buf]));
+      } else {
+        if (!wait_phase(smem_u32(&ctl->red_full[buf]), use & 1, abort_flag)) return;
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] = acc[q] + rb[(rbk * 4 + q) * 32 + lane];
+        mbar_arrive(smem_u32(&ctl->red_empty[buf]));
+        const int row0 = meta.row0[cu.slot];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const float v = acc[q] + red[(rb * 4 + q) * 32 + lane];
-          const int hrow = cm.tile * C::kRows + lr0 + (q >= 2 ? 8 : 0);
+          const int hrow = cu.tile * C::kRows + lr0 + (q >= 2 ? 8 : 0);
           const int rr = p0 + 2 * c + (q & 1);
-          if (rr < n) y[(size_t)(row0 + rr) * H + hrow] = v;
+          if (rr < n) y[(size_t)(row0 + rr) * H + hrow] = v[q];
         }
       }
+      ++item;
     }
-    cursor_next(cm, tiles, nkc, meta);
-    __syncthreads();  // stage (task % S) and `red` are free again
+    cursor_next(cu, tiles, nkc, meta);
   }
-  cp_async_wait<0>();
 }
 
 template <typename K>
@@ -601,56 +692,38 @@ void set_smem(K kern, size_t bytes) {
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
-constexpr size_t kMaxSmem = 227 * 1024;
-
-template <int G, typename XT, int KCH>
-size_t gateup_smem(int E) {
-  using C = GateUpCfg<G, XT, KCH>;
-  return (size_t)C::kStages * C::kStage + C::kRed + (size_t)(4 * E + 4) * 4;
-}
-
-template <int G>
-size_t down_smem(int E) {
-  using C = DownCfg<G>;
-  return (size_t)C::kStages * C::kStage + C::kRed + (size_t)(4 * E + 4) * 4;
-}
-
-template <int G, typename XT, int KCH>
-void launch_gateup_k(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
-                     const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
-                     __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
-  const size_t smem = gateup_smem<G, XT, KCH>(E);
-  auto k = ffn_gateup_kernel<G, XT, KCH>;
-  set_smem(k, smem);
-  k<<<grid, kThreads, smem, st>>>(static_cast<const XT*>(x), row_token, offsets, active, w13_q, w13_s, H, I,
-                                  E, h_hi, h_lo);
-}
-
-// 2048-element tasks for bf16 activations when H needs them and they fit.
 template <int G, typename XT>
 void launch_gateup(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
                    const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
                    __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
-  if constexpr (!std::is_same<XT, float>::value) {
-    if (H > 1024 && gateup_smem<G, XT, 2048>(E) <= kMaxSmem) {
-      launch_gateup_k<G, XT, 2048>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
-      return;
-    }
-  }
-  launch_gateup_k<G, XT, 1024>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
+  const size_t smem = GateUpCfg<G, XT>::smem(E);
+  auto k = ffn_gateup_kernel<G, XT>;
+  set_smem(k, smem);
+  k<<<grid, kThreads, smem, st>>>(static_cast<const XT*>(x), row_token, offsets, active, w13_q, w13_s, H, I,
+                                  E, h_hi, h_lo);
 }
 
 template <int G>
 void launch_down(const __nv_bfloat16* h_hi, const __nv_bfloat16* h_lo, const int32_t* offsets,
                  const int32_t* active, const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, float* y,
                  int grid, cudaStream_t st) {
-  const size_t smem = down_smem<G>(E);
+  const size_t smem = DownCfg<G>::smem(E);
   auto k = ffn_down_kernel<G>;
   set_smem(k, smem);
   k<<<grid, kThreads, smem, st>>>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
 }
 
 }  // namespace
+
+int ffn_device_error(bool reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_ffn_error, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_ffn_error, &zero, sizeof(int));
+  }
+  return v;
+}
 
 int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       const int32_t* offsets, const int32_t* active, const uint8_t* w13_q,

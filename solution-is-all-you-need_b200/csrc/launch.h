@@ -32,6 +32,9 @@ int launch_quantize(const void* w, int w_dtype, long long rows, int K, int G, ui
 
 int device_sm_count();
 
+// Error word the FFN kernels raise when a pipeline wait times out (0 = ok).
+int ffn_device_error(bool reset);
+
 // Host-side count of kernels enqueued by this library (see phmoe.h).
 void note_launches(int n);
 

@@ -50,6 +50,7 @@ SIGNATURES = {
     "phmoe_kernel_launch_count": (ctypes.c_ulonglong, []),
     "phmoe_profile_begin": (_I, [_I]),
     "phmoe_profile_end": (_I, [_P, _I, _P]),
+    "phmoe_device_error": (_I, [_I]),
 }
 
 NUM_STAGES = 5

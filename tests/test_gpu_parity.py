@@ -321,6 +321,8 @@ def test_layer_deterministic_and_edge_cases(qwen3_bf16_weights):
     a = pm.moe_layer(x, wr, *args)
     b = pm.moe_layer(x, wr, *args)
     assert torch.equal(a, b)
+    torch.cuda.synchronize()
+    assert pm.load_library().phmoe_device_error(1) == 0  # no pipeline wait timed out
     # [B, S, H] input keeps its shape
     y = pm.moe_layer(x.view(4, 16, 2048), wr, *args)
     assert y.shape == (4, 16, 2048) and torch.equal(y.view(64, 2048), a)
