@@ -10,13 +10,16 @@
 // expert hit and does a few FMAs per weight: the bound is HBM. Both kernels
 // are persistent (one CTA per SM, a contiguous range of work items each) and
 // warp-specialised:
-//  * one producer warp streams "tasks" (a work item's K-chunk) into a ring of
-//    shared-memory stages: each packed weight row and each activation row is
-//    ONE cp.async.bulk (TMA bulk copy) whose completion is counted in bytes on
-//    the stage's "full" mbarrier; the fp16 scale slices arrive by 4-byte
-//    cp.async tracked on the same barrier (cp.async.mbarrier.arrive.noinc);
+//  * two producer warps stream "tasks" (a work item's K-chunk) into a ring of
+//    shared-memory stages with 16-byte cp.async (512 B per warp instruction:
+//    weight rows, activation rows, fp16 scale slices), each lane signalling
+//    the stage's "full" mbarrier when its copies land
+//    (cp.async.mbarrier.arrive.noinc). Rows land padded, so every fragment
+//    read below is bank-conflict free. (One TMA bulk copy per row was tried
+//    and measured slower: rows here are 256 B - 2 KB, and each bulk copy has
+//    a fixed cost comparable to moving ~2 KB.)
 //  * 16 consumer warps wait on "full", compute, and release the stage on its
-//    "empty" mbarrier. No CTA-wide barrier is ever taken.
+//    "empty" mbarrier (one arrival per warp). No CTA-wide barrier is taken.
 // From shared memory each lane reads the int4 words of its A fragments and
 // turns each 32-bit word (8 consecutive weights) into four bf16x2 pairs with
 // one lop3 each (packed layout in phmoe.h); the pairs feed mma.sync m16n8k16
@@ -59,7 +62,8 @@ __device__ int g_ffn_error;  // 0 = ok, 1 = a pipeline wait timed out
 namespace {
 
 constexpr int kConsumers = 16;                  // consumer warps
-constexpr int kThreads = (kConsumers + 1) * 32; // + 1 producer warp
+constexpr int kProducers = 2;                   // producer warps
+constexpr int kThreads = (kConsumers + kProducers) * 32;
 constexpr int kTok = 8;                         // tokens per pass (the MMA N dimension)
 constexpr uint32_t kSpinLimit = 1u << 22;       // try_wait polls before giving up
 
@@ -75,9 +79,6 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
-}
 // One poll; the thread may be suspended up to ~1 us inside it.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;
@@ -92,10 +93,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
 }
-// One bulk (TMA) copy global -> shared, completion counted on `bar` in bytes.
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
-               ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(g) : "memory");
+}
+
+// Copy `bytes` (a multiple of 16) from global to shared memory with the 32
+// lanes of a producer warp: lane j moves 16-byte chunks j, j+32, ...
+__device__ __forceinline__ void warp_copy(uint32_t dst, const uint8_t* src, int bytes, int lane) {
+  for (int o = lane * 16; o < bytes; o += 32 * 16) cp_async16(dst + o, src + o);
+}
+
+// Release a stage / buffer: every lane's shared-memory reads or writes are
+// ordered before lane 0's arrive by the warp barrier.
+__device__ __forceinline__ void warp_arrive(uint32_t bar, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
 }
 
 // Bounded wait on a barrier phase. Returns false when this CTA aborts.
@@ -373,12 +385,12 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&ctl->full[s]), 1 + 32);  // expect_tx arrive + 32 cp.async arrivals
-      mbar_init(smem_u32(&ctl->empty[s]), kConsumers * 32);
+      mbar_init(smem_u32(&ctl->full[s]), kProducers * 32);  // one cp.async arrival per producer lane
+      mbar_init(smem_u32(&ctl->empty[s]), kConsumers);      // one arrival per consumer warp
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&ctl->red_full[b]), kConsumers * 32);
-      mbar_init(smem_u32(&ctl->red_empty[b]), 4 * 32);
+      mbar_init(smem_u32(&ctl->red_full[b]), kConsumers);
+      mbar_init(smem_u32(&ctl->red_empty[b]), 4);
     }
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -389,12 +401,15 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
   const int ntask = (q1 - q0) * nkc;
   if (ntask == 0) return;
 
-  if (warp == kConsumers) {
-    // ---------------- producer warp ----------------
+  if (warp >= kConsumers) {
+    // ---------------- producer warps ----------------
+    // Warp pw copies the weight rows and activation rows of parity pw, and
+    // the scale slices of the gate (pw = 0) or up (pw = 1) rows.
+    const int pw = warp - kConsumers;
     Cursor cu = cursor_at(q0, na, tiles, meta);
-    auto token = [&](const Cursor& k) -> int {
-      const int rr = k.pass * kTok + lane;
-      return (lane < kTok && rr < meta.n[k.slot]) ? __ldg(row_token + meta.row0[k.slot] + rr) : -1;
+    auto token = [&](const Cursor& k) -> int {  // lane holds the token id of row lane % 8
+      const int rr = k.pass * kTok + (lane & (kTok - 1));
+      return rr < meta.n[k.slot] ? __ldg(row_token + meta.row0[k.slot] + rr) : -1;
     };
     int tok = token(cu);
     int issued = 0;
@@ -403,23 +418,30 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
       if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
       Cursor nx = cu;
       cursor_next(nx, tiles, nkc, meta);
-      const int tok_next = t + 1 < ntask ? token(nx) : -1;  // hidden behind this task's issue
+      const int tok_next = t + 1 < ntask ? token(nx) : -1;  // hidden behind this task's copies
       const int k0 = cu.kc * C::kKch;
       const int kel = min(C::kKch, H - k0);
       const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
       const uint32_t full = smem_u32(&ctl->full[s]);
-      uint8_t* st = smem + s * C::kStage;
-      if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(C::kRows * (kel / 2) + nt * kel * (int)sizeof(XT)));
-      __syncwarp();
+      const uint32_t st = smem_u32(smem + s * C::kStage);
       const int i0 = cu.tile * 16;
-      const size_t grow = (size_t)meta.e[cu.slot] * 2 * I + (lane < 16 ? i0 + lane : I + i0 + lane - 16);
-      bulk_g2s(smem_u32(st + C::kW + lane * C::kWStride), w13_q + grow * row_bytes + k0 / 2, kel / 2, full);
-      if (lane < nt)
-        bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), x + (size_t)tok * H + k0, kel * (int)sizeof(XT), full);
-#pragma unroll
-      for (int pp = 0; pp < C::kPairs; ++pp)
-        if (pp * 2 * G < kel)
-          cp_async4(smem_u32(st + C::kS + lane * C::kScaleRow + pp * 4), w13_s + grow * NG + k0 / G + 2 * pp);
+      const size_t erow = (size_t)meta.e[cu.slot] * 2 * I;
+      for (int rr = pw; rr < C::kRows; rr += kProducers) {
+        const size_t grow = erow + (rr < 16 ? i0 + rr : I + i0 + rr - 16);
+        warp_copy(st + C::kW + rr * C::kWStride, w13_q + grow * row_bytes + k0 / 2, kel / 2, lane);
+      }
+      for (int n = pw; n < nt; n += kProducers) {
+        const int tk = __shfl_sync(0xffffffffu, tok, n);
+        warp_copy(st + C::kB + n * C::kBStride, reinterpret_cast<const uint8_t*>(x + (size_t)tk * H + k0),
+                  kel * (int)sizeof(XT), lane);
+      }
+      {
+        const int rr = pw * 16 + (lane & 15);
+        const size_t grow = erow + (rr < 16 ? i0 + rr : I + i0 + rr - 16);
+        for (int pp = lane >> 4; pp < C::kPairs; pp += 2)
+          if (pp * 2 * G < kel)
+            cp_async4(st + C::kS + rr * C::kScaleRow + pp * 4, w13_s + grow * NG + k0 / G + 2 * pp);
+      }
       cp_async_arrive_noinc(full);
       ++issued;
       tok = tok_next;
@@ -467,7 +489,7 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
                                __half2float(sc[(r + 8) * kScH + g]), __half2float(sc[(16 + r) * kScH + g]),
                                __half2float(sc[(24 + r) * kScH + g]), acc_g, acc_u);
     }
-    mbar_arrive(smem_u32(&ctl->empty[s]));  // this thread is done with the stage
+    warp_arrive(smem_u32(&ctl->empty[s]), lane);  // this warp is done with the stage
     if (cu.kc == nkc - 1) {
       const int buf = item & 1;
       const int use = item >> 1;
@@ -478,7 +500,7 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
         rb[warp * 256 + q * 32 + lane] = acc_g[q];
         rb[warp * 256 + (4 + q) * 32 + lane] = acc_u[q];
       }
-      mbar_arrive(smem_u32(&ctl->red_full[buf]));
+      warp_arrive(smem_u32(&ctl->red_full[buf]), lane);
       if (warp < 4) {
         // thread (q = warp, ln = lane) finishes fragment slot q of lane ln,
         // summing the consumer warps' partials in order 0..15, then SwiGLU
@@ -490,7 +512,7 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
           gs += rb[w * 256 + q * 32 + ln];
           us += rb[w * 256 + (4 + q) * 32 + ln];
         }
-        mbar_arrive(smem_u32(&ctl->red_empty[buf]));
+        warp_arrive(smem_u32(&ctl->red_empty[buf]), lane);
         const int n = meta.n[cu.slot], row0 = meta.row0[cu.slot];
         const int i = cu.tile * 16 + (ln >> 2) + (q >= 2 ? 8 : 0);
         const int rr = cu.pass * kTok + 2 * (ln & 3) + (q & 1);
@@ -555,12 +577,12 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&ctl->full[s]), 1 + 32);
-      mbar_init(smem_u32(&ctl->empty[s]), kConsumers * 32);
+      mbar_init(smem_u32(&ctl->full[s]), kProducers * 32);  // one cp.async arrival per producer lane
+      mbar_init(smem_u32(&ctl->empty[s]), kConsumers);      // one arrival per consumer warp
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&ctl->red_full[b]), 8 * 32);
-      mbar_init(smem_u32(&ctl->red_empty[b]), 8 * 32);
+      mbar_init(smem_u32(&ctl->red_full[b]), 8);
+      mbar_init(smem_u32(&ctl->red_empty[b]), 8);
     }
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -571,8 +593,13 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
   const int ntask = (q1 - q0) * nkc;
   if (ntask == 0) return;
 
-  if (warp == kConsumers) {
-    // ---------------- producer warp ----------------
+  if (warp >= kConsumers) {
+    // ---------------- producer warps ----------------
+    // The 64 producer lanes split the weight and scale copies evenly; the
+    // h rows go to the warp of their parity.
+    const int pw = warp - kConsumers;
+    const int pl_lane = pw * 32 + lane;
+    constexpr int kWch = C::kKch / 32;  // 16-byte weight chunks per row (full chunk)
     Cursor cu = cursor_at(q0, na, tiles, meta);
     int issued = 0;
     for (int t = 0; t < ntask; ++t) {
@@ -582,30 +609,25 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
       const int kel = min(C::kKch, I - k0);
       const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
       const uint32_t full = smem_u32(&ctl->full[s]);
-      uint8_t* st = smem + s * C::kStage;
-      if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(C::kRows * (kel / 2) + 2 * nt * kel * 2));
-      __syncwarp();
+      const uint32_t st = smem_u32(smem + s * C::kStage);
       const size_t rbase = (size_t)meta.e[cu.slot] * H + (size_t)cu.tile * C::kRows;
-#pragma unroll
-      for (int j = 0; j < C::kRows / 32; ++j) {
-        const int rr = lane + 32 * j;
-        bulk_g2s(smem_u32(st + C::kW + rr * C::kWStride), w2_q + (rbase + rr) * row_bytes + k0 / 2, kel / 2, full);
+#pragma unroll 4
+      for (int q = pl_lane; q < C::kRows * kWch; q += kProducers * 32) {
+        const int rr = q / kWch, cc = q % kWch;
+        if (cc * 32 < kel)
+          cp_async16(st + C::kW + rr * C::kWStride + cc * 16, w2_q + (rbase + rr) * row_bytes + k0 / 2 + cc * 16);
       }
-      if (lane < 2 * kTok) {
-        const int pl = lane >> 3, n = lane & 7;
-        if (n < nt) {
-          const __nv_bfloat16* src =
-              (pl ? h_lo : h_hi) + (size_t)(meta.row0[cu.slot] + cu.pass * kTok + n) * I + k0;
-          bulk_g2s(smem_u32(st + C::kB + (pl * kTok + n) * C::kBStride), src, kel * 2, full);
-        }
+      const int row_p = meta.row0[cu.slot] + cu.pass * kTok;
+      for (int b = pw; b < 2 * nt; b += kProducers) {
+        const int pl = b / nt, n = b - pl * nt;
+        const __nv_bfloat16* src = (pl ? h_lo : h_hi) + (size_t)(row_p + n) * I + k0;
+        warp_copy(st + C::kB + (pl * kTok + n) * C::kBStride, reinterpret_cast<const uint8_t*>(src), kel * 2, lane);
       }
-#pragma unroll
-      for (int j = 0; j < C::kRows / 32; ++j) {
-        const int rr = lane + 32 * j;
-#pragma unroll
-        for (int pp = 0; pp < C::kPairs; ++pp)
-          if (pp * 2 * G < kel)
-            cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
+#pragma unroll 4
+      for (int q = pl_lane; q < C::kRows * C::kPairs; q += kProducers * 32) {
+        const int rr = q / C::kPairs, pp = q % C::kPairs;
+        if (pp * 2 * G < kel)
+          cp_async4(st + C::kS + rr * C::kScaleRow + pp * 4, w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
       }
       cp_async_arrive_noinc(full);
       ++issued;
@@ -657,7 +679,7 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
       }
       down_group<G>(a0, a8, b, __half2float(sc[lr0 * kScH + g]), __half2float(sc[(lr0 + 8) * kScH + g]), acc);
     }
-    mbar_arrive(smem_u32(&ctl->empty[s]));
+    warp_arrive(smem_u32(&ctl->empty[s]), lane);
     if (cu.kc == nkc - 1) {
       const int buf = item & 1;
       const int use = item >> 1;
@@ -666,13 +688,13 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
         if (use > 0 && !wait_phase(smem_u32(&ctl->red_empty[buf]), (use - 1) & 1, abort_flag)) return;
 #pragma unroll
         for (int q = 0; q < 4; ++q) rb[(rbk * 4 + q) * 32 + lane] = acc[q];
-        mbar_arrive(smem_u32(&ctl->red_full[buf]));
+        warp_arrive(smem_u32(&ctl->red_full[buf]), lane);
       } else {
         if (!wait_phase(smem_u32(&ctl->red_full[buf]), use & 1, abort_flag)) return;
         float v[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) v[q] = acc[q] + rb[(rbk * 4 + q) * 32 + lane];
-        mbar_arrive(smem_u32(&ctl->red_empty[buf]));
+        warp_arrive(smem_u32(&ctl->red_empty[buf]), lane);
         const int row0 = meta.row0[cu.slot];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
