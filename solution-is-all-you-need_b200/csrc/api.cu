@@ -87,12 +87,13 @@ int check_router_smem(int H, int x_dtype) {
   return PHMOE_OK;
 }
 
-// The FFN kernels copy scales in pairs of groups (4-byte async copies) and
-// tile the down projection in 128-row blocks.
+// The FFN kernels copy scales in pairs of groups (4-byte async copies), load
+// gate/up weights as TMA boxes of 128-byte K-chunks (H % 256) and tile the
+// down projection in 128-row blocks.
 int check_ffn_dims(int H, int I, int G) {
   if (G != 32 && G != 64) return fail(PHMOE_ERR_UNSUPPORTED, "group_size must be 32 or 64 (got %d)", G);
-  if (H <= 0 || H % 128 || H % (2 * G))
-    return fail(PHMOE_ERR_UNSUPPORTED, "H must be a positive multiple of 128 and of 2*group_size (got %d)", H);
+  if (H <= 0 || H % 256)
+    return fail(PHMOE_ERR_UNSUPPORTED, "H must be a positive multiple of 256 (got %d)", H);
   if (I <= 0 || I % 16 || I % (2 * G))
     return fail(PHMOE_ERR_UNSUPPORTED, "I must be a positive multiple of 16 and of 2*group_size (got %d)", I);
   return PHMOE_OK;

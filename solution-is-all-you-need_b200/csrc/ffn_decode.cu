@@ -6,29 +6,35 @@
 //   y_e = linear(h, down_proj[e])
 // on weights dequantised as (nibble - 8) * scale (gguf_loader.py:372-378).
 //
-// Design. At decode sizes the layer streams ~2.5 MB of packed weights per
-// expert hit and does a few FMAs per weight: the bound is HBM. Both kernels
-// are persistent (one CTA per SM, a contiguous range of work items each) and
-// warp-specialised:
-//  * two producer warps stream "tasks" (a work item's K-chunk) into a ring of
-//    shared-memory stages with 16-byte cp.async (512 B per warp instruction:
-//    weight rows, activation rows, fp16 scale slices), each lane signalling
-//    the stage's "full" mbarrier when its copies land
-//    (cp.async.mbarrier.arrive.noinc). Rows land padded, so every fragment
-//    read below is bank-conflict free. (One TMA bulk copy per row was tried
-//    and measured slower: rows here are 256 B - 2 KB, and each bulk copy has
-//    a fixed cost comparable to moving ~2 KB.)
-//  * 16 consumer warps wait on "full", compute, and release the stage on its
-//    "empty" mbarrier (one arrival per warp). No CTA-wide barrier is taken.
-// From shared memory each lane reads the int4 words of its A fragments and
-// turns each 32-bit word (8 consecutive weights) into four bf16x2 pairs with
-// one lop3 each (packed layout in phmoe.h); the pairs feed mma.sync m16n8k16
-// directly, with the 8 tokens of a pass as the N side. Dequantised weights
-// are never written back to shared memory (bf16 would be 4x the int4 bytes).
-// In gate/up the unpacked values are 128 + nibble and the +136 offset is
-// removed after the MMA with one extra MMA per K step against an all-ones A
-// (it yields sum_k x_k); the fp16 group scale multiplies the fp32 partial of
-// each group. Both are exact factorisations.
+// At decode sizes the layer streams ~2.5 MB of packed weights per expert hit
+// and does a few FMAs per weight: the bound is HBM. Both kernels are
+// persistent (one CTA per SM, a contiguous range of work items each) and
+// stream "tasks" (a work item's K-chunk) through a ring of shared-memory
+// stages; from shared memory each lane reads the int4 words of its A
+// fragments and turns each 32-bit word (8 consecutive weights) into four
+// bf16x2 pairs with one lop3 each (packed layout in phmoe.h); the pairs feed
+// mma.sync m16n8k16 directly, with the 8 tokens of a pass as the N side.
+// Dequantised weights are never written back to shared memory (bf16 would
+// be 4x the int4 bytes).
+//
+// gate/up kernel (the larger half of the bytes): warp-specialised.
+//  * A producer warp issues, per task, two TMA tensor copies (one 16-row x
+//    512-byte box of gate rows and one of up rows, 128-byte swizzled so the
+//    fragment reads are nearly conflict free), one bulk copy per activation
+//    row, and the fp16 scale slices as 4-byte cp.async; all complete on the
+//    stage's "full" mbarrier (bytes for TMA, cp.async.mbarrier.arrive.noinc).
+//  * 16 consumer warps split each task's K, wait on "full", compute and
+//    release "empty" (one arrival per warp); at an item's last task their
+//    partials are summed in warp order (deterministic) by 4 warps that apply
+//    SwiGLU and store h as bf16 hi/lo planes. The unpacked weights are
+//    128 + nibble: the +136 offset is removed after the MMA with one extra MMA
+//    per K step against an all-ones A (it yields sum_k x_k), and the fp16
+//    group scale multiplies the fp32 partial of each group.
+//  * item = (expert, 16 intermediate rows, pass of 8 tokens); items are
+//    ordered (expert, tile, pass) so extra passes re-read weights still in L2.
+// down kernel: 16 warps copy each task (128 rows x 512 K) with 16-byte
+//  cp.async into padded rows and compute it between two CTA barriers; warp w
+//  owns rows 16(w%8)..+15 and half of each K-chunk (w/8).
 //
 // Lane c of a quad holds K elements 16c..16c+15 of a 64-group (8c..8c+7 of a
 // 32-group) for A and reads the same activations for B; inside one MMA the K
@@ -39,19 +45,11 @@
 // intermediate h are split into bf16 hi + lo parts (two MMAs each), keeping
 // ~16 significant bits.
 //
-// gate/up kernel: item = (expert, 16 intermediate rows, pass of 8 tokens) ->
-//   32 weight rows (16 gate + 16 up); the consumer warps split each K-chunk
-//   and their partials are summed in warp order (deterministic) by 4 warps
-//   that apply SwiGLU and store h as bf16 hi/lo planes.
-// down kernel: item = (expert, 128 output rows, pass); consumer warp w owns
-//   rows 16(w%8)..+15 and half of each K-chunk (w/8); the halves are added in
-//   a fixed order.
-// Items are ordered (expert, tile, pass) so the extra passes of an expert
-// with more than 8 rows re-read weights that are still in L2.
-//
-// Every wait is bounded: after kSpinLimit polls a warp raises the CTA's abort
-// flag and the device error word (read by phmoe_ffn_device_error), and all
+// Every mbarrier wait is bounded: after kSpinLimit polls a warp raises the
+// CTA's abort flag and the device error word (phmoe_device_error) and all
 // warps leave; the producer first waits (bounded) for its copies in flight.
+#include <cuda.h>  // CUtensorMap (types only; the encoder is fetched from the driver at run time)
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -61,11 +59,11 @@ __device__ int g_ffn_error;  // 0 = ok, 1 = a pipeline wait timed out
 
 namespace {
 
-constexpr int kConsumers = 16;                  // consumer warps
-constexpr int kProducers = 2;                   // producer warps
-constexpr int kThreads = (kConsumers + kProducers) * 32;
+constexpr int kConsumers = 16;                  // gate/up consumer warps
+constexpr int kGuThreads = (kConsumers + 1) * 32;  // + 1 producer warp
+constexpr int kDownThreads = 16 * 32;
 constexpr int kTok = 8;                         // tokens per pass (the MMA N dimension)
-constexpr uint32_t kSpinLimit = 1u << 22;       // try_wait polls before giving up
+constexpr uint32_t kSpinLimit = 1u << 24;       // try_wait polls before giving up
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -73,41 +71,52 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ void cp_async4(uint32_t saddr, const void* g) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(saddr), "l"(g) : "memory");
 }
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
-// One poll; the thread may be suspended up to ~1 us inside it.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(done) : "r"(bar), "r"(parity), "r"(1000u) : "memory");
+      : "=r"(done) : "r"(bar), "r"(parity) : "memory");
   return done != 0;
 }
 // Arrive on `bar` once every cp.async this thread issued so far has landed.
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(g) : "memory");
+// One bulk copy global -> shared (16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+               ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
-
-// Copy `bytes` (a multiple of 16) from global to shared memory with the 32
-// lanes of a producer warp: lane j moves 16-byte chunks j, j+32, ...
-__device__ __forceinline__ void warp_copy(uint32_t dst, const uint8_t* src, int bytes, int lane) {
-  for (int o = lane * 16; o < bytes; o += 32 * 16) cp_async16(dst + o, src + o);
+// TMA tensor tile loads (innermost coordinate is always 0 or a multiple of 128 bytes).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar) : "memory");
 }
-
-// Release a stage / buffer: every lane's shared-memory reads or writes are
-// ordered before lane 0's arrive by the warp barrier.
-__device__ __forceinline__ void warp_arrive(uint32_t bar, int lane) {
-  __syncwarp();
-  if (lane == 0) mbar_arrive(bar);
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar) : "memory");
 }
 
 // Bounded wait on a barrier phase. Returns false when this CTA aborts.
@@ -121,8 +130,11 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volati
   return false;
 }
 
-// Shared-memory control block of a CTA: stage barriers, reduction-buffer
-// barriers, abort flag.
+__device__ __forceinline__ void warp_arrive(uint32_t bar, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
+
 template <int S>
 struct Ctl {
   uint64_t full[S];
@@ -338,39 +350,50 @@ __device__ __forceinline__ void cta_range(int total, int& q0, int& q1) {
 }
 
 // ---------------------------------------------------------------------------
-// gate/up + SwiGLU
+// gate/up + SwiGLU (TMA-fed, warp-specialised)
 // ---------------------------------------------------------------------------
 template <int G, typename XT>
 struct GateUpCfg {
   static constexpr bool kF32 = std::is_same<XT, float>::value;
   static constexpr int kStages = kF32 ? 3 : 5;
   static constexpr int kRows = 32;
-  static constexpr int kKch = 1024;                                  // K elements per task
-  static constexpr int kPairs = kKch / G / 2;                        // 4-byte scale pairs per row
-  static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);    // conflict-free A reads
+  static constexpr int kKch = 1024;                          // K elements per task
+  static constexpr int kBlock = 16 * (kKch / 2);             // one 16-row box: 8 KB
   static constexpr int kScaleRow = kKch / G * 2;
+  static constexpr int kPairs = kKch / G / 2;
   static constexpr int kBRowBytes = kKch * (int)sizeof(XT);
-  static constexpr int kBPad = (G == 32 && !kF32) ? 64 : 16;         // conflict-free B reads
+  static constexpr int kBPad = (G == 32 && !kF32) ? 64 : 16;  // conflict-free B reads
   static constexpr int kBStride = kBRowBytes + kBPad;
-  static constexpr int kW = 0;
-  static constexpr int kS = kRows * kWStride;
+  static constexpr int kW = 0;                               // [gate box][up box], 1024-aligned
+  static constexpr int kS = 2 * kBlock;
   static constexpr int kB = kS + kRows * kScaleRow;
-  static constexpr int kStage = (kB + kTok * kBStride + 127) / 128 * 128;
-  static constexpr int kRedBuf = kConsumers * 8 * 32 * 4;            // one partial-sum buffer
+  static constexpr int kStage = (kB + kTok * kBStride + 1023) / 1024 * 1024;
+  static constexpr int kRedBuf = kConsumers * 8 * 32 * 4;
   static constexpr size_t smem(int E) {
-    return (size_t)kStages * kStage + 2 * kRedBuf + sizeof(Ctl<kStages>) + (size_t)(4 * E + 4) * 4;
+    return 1024 + (size_t)kStages * kStage + 2 * kRedBuf + sizeof(Ctl<kStages>) + (size_t)(4 * E + 4) * 4;
   }
 };
 
+// Byte offset of (row R of a 16-row box, byte kb of the task's K slice) in a
+// box written by TMA with 128-byte swizzle: 128-byte lines ordered (K-chunk,
+// row); the 16-byte unit inside a line is XORed with the row (mod 8).
+__device__ __forceinline__ int swz_off(int Rb, int kb) {
+  const int c0 = kb & 127;
+  return ((kb >> 7) * 16 + Rb) * 128 + ((((c0 >> 4) ^ (Rb & 7)) << 4) | (c0 & 15));
+}
+
 template <int G, typename XT>
-__global__ void __launch_bounds__(kThreads, 1)
-ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_token,
+__global__ void __launch_bounds__(kGuThreads, 1)
+ffn_gateup_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int box_chunks,
+                  const XT* __restrict__ x, const int32_t* __restrict__ row_token,
                   const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
-                  const uint8_t* __restrict__ w13_q, const uint16_t* __restrict__ w13_s, int H, int I,
-                  int E, __nv_bfloat16* __restrict__ h_hi, __nv_bfloat16* __restrict__ h_lo) {
+                  const uint16_t* __restrict__ w13_s, int H, int I, int E,
+                  __nv_bfloat16* __restrict__ h_hi, __nv_bfloat16* __restrict__ h_lo) {
   using C = GateUpCfg<G, XT>;
   constexpr int S = C::kStages;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte swizzled TMA destinations must be 1024-byte aligned
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [2][kConsumers][8][32]
   Ctl<S>* ctl = reinterpret_cast<Ctl<S>*>(smem + S * C::kStage + 2 * C::kRedBuf);
   int* mbase = reinterpret_cast<int*>(ctl + 1);
@@ -380,13 +403,12 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
   const int tiles = I / 16;
   const int NG = H / G;
   const int nkc = (H + C::kKch - 1) / C::kKch;
-  const size_t row_bytes = (size_t)H / 2;
   const int na = active[0];
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&ctl->full[s]), kProducers * 32);  // one cp.async arrival per producer lane
-      mbar_init(smem_u32(&ctl->empty[s]), kConsumers);      // one arrival per consumer warp
+      mbar_init(smem_u32(&ctl->full[s]), 1 + 32);  // expect_tx arrival + one cp.async arrival per lane
+      mbar_init(smem_u32(&ctl->empty[s]), kConsumers);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&ctl->red_full[b]), kConsumers);
@@ -401,18 +423,16 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
   const int ntask = (q1 - q0) * nkc;
   if (ntask == 0) return;
 
-  if (warp >= kConsumers) {
-    // ---------------- producer warps ----------------
-    // Warp pw copies the weight rows and activation rows of parity pw, and
-    // the scale slices of the gate (pw = 0) or up (pw = 1) rows.
-    const int pw = warp - kConsumers;
+  if (warp == kConsumers) {
+    // ---------------- producer warp ----------------
     Cursor cu = cursor_at(q0, na, tiles, meta);
-    auto token = [&](const Cursor& k) -> int {  // lane holds the token id of row lane % 8
+    auto token = [&](const Cursor& k) -> int {  // lane holds the token id of pass row lane % 8
       const int rr = k.pass * kTok + (lane & (kTok - 1));
       return rr < meta.n[k.slot] ? __ldg(row_token + meta.row0[k.slot] + rr) : -1;
     };
     int tok = token(cu);
     int issued = 0;
+    const uint32_t box_bytes = 16u * 128u * (uint32_t)box_chunks;
     for (int t = 0; t < ntask; ++t) {
       const int s = t % S;
       if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
@@ -423,24 +443,28 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
       const int kel = min(C::kKch, H - k0);
       const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
       const uint32_t full = smem_u32(&ctl->full[s]);
-      const uint32_t st = smem_u32(smem + s * C::kStage);
-      const int i0 = cu.tile * 16;
-      const size_t erow = (size_t)meta.e[cu.slot] * 2 * I;
-      for (int rr = pw; rr < C::kRows; rr += kProducers) {
-        const size_t grow = erow + (rr < 16 ? i0 + rr : I + i0 + rr - 16);
-        warp_copy(st + C::kW + rr * C::kWStride, w13_q + grow * row_bytes + k0 / 2, kel / 2, lane);
+      uint8_t* st = smem + s * C::kStage;
+      if (lane == 0)
+        mbar_arrive_expect_tx(full, 2 * box_bytes + (uint32_t)(nt * kel * (int)sizeof(XT)));
+      __syncwarp();
+      const int grow = meta.e[cu.slot] * 2 * I + cu.tile * 16;  // first gate row; up rows are I further
+      if (lane < 2) {
+        const uint32_t dst = smem_u32(st + C::kW + lane * C::kBlock);
+        const int row = grow + lane * I;
+        if (map3d) {
+          tma_load_3d(dst, &w13_map, 0, row, k0 / 256, full);
+        } else {
+          for (int ch = 0; ch < box_chunks; ++ch)
+            tma_load_2d(dst + ch * 16 * 128, &w13_map, k0 / 2 + ch * 128, row, full);
+        }
       }
-      for (int n = pw; n < nt; n += kProducers) {
-        const int tk = __shfl_sync(0xffffffffu, tok, n);
-        warp_copy(st + C::kB + n * C::kBStride, reinterpret_cast<const uint8_t*>(x + (size_t)tk * H + k0),
-                  kel * (int)sizeof(XT), lane);
-      }
+      if (lane < nt)  // lane n < 8 holds the token id of pass row n
+        bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), x + (size_t)tok * H + k0, kel * (int)sizeof(XT), full);
       {
-        const int rr = pw * 16 + (lane & 15);
-        const size_t grow = erow + (rr < 16 ? i0 + rr : I + i0 + rr - 16);
-        for (int pp = lane >> 4; pp < C::kPairs; pp += 2)
+        const size_t srow = (size_t)(lane < 16 ? grow + lane : grow + I + lane - 16);
+        for (int pp = 0; pp < C::kPairs; ++pp)
           if (pp * 2 * G < kel)
-            cp_async4(st + C::kS + rr * C::kScaleRow + pp * 4, w13_s + grow * NG + k0 / G + 2 * pp);
+            cp_async4(smem_u32(st + C::kS + lane * C::kScaleRow + pp * 4), w13_s + srow * NG + k0 / G + 2 * pp);
       }
       cp_async_arrive_noinc(full);
       ++issued;
@@ -458,7 +482,6 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
 
   // ---------------- consumer warps ----------------
   const int r = lane >> 2, c = lane & 3;
-  const int a_off = (G == 64) ? 8 * c : 4 * c;
   const int b_off = (G == 64 ? 16 : 8) * c * (int)sizeof(XT);
   constexpr int kScH = C::kScaleRow / 2;
   Cursor cu = cursor_at(q0, na, tiles, meta);
@@ -473,14 +496,17 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
     const int ngt = min(C::kKch, H - cu.kc * C::kKch) / G;
     if (!wait_phase(smem_u32(&ctl->full[s]), (t / S) & 1, abort_flag)) return;
     const uint8_t* st = smem + s * C::kStage;
+    const uint8_t* wg = st + C::kW;
+    const uint8_t* wu = st + C::kW + C::kBlock;
     const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
 #pragma unroll 2
     for (int g = warp; g < ngt; g += kConsumers) {
-      const uint8_t* ab = st + C::kW + g * (G / 2) + a_off;
-      const RowWords<G> ag0 = lds_row<G>(ab + r * C::kWStride);
-      const RowWords<G> ag8 = lds_row<G>(ab + (r + 8) * C::kWStride);
-      const RowWords<G> au0 = lds_row<G>(ab + (16 + r) * C::kWStride);
-      const RowWords<G> au8 = lds_row<G>(ab + (24 + r) * C::kWStride);
+      const int kb = (G == 64) ? g * 32 + 8 * c : g * 16 + 4 * c;
+      const int o0 = swz_off(r, kb), o8 = swz_off(r + 8, kb);
+      const RowWords<G> ag0 = lds_row<G>(wg + o0);
+      const RowWords<G> ag8 = lds_row<G>(wg + o8);
+      const RowWords<G> au0 = lds_row<G>(wu + o0);
+      const RowWords<G> au8 = lds_row<G>(wu + o8);
       BWords<G> b;
       const uint8_t* bb = st + C::kB + r * C::kBStride + g * G * (int)sizeof(XT) + b_off;
       if constexpr (C::kF32) lds_b_f32<G>(bb, b);
@@ -531,7 +557,6 @@ ffn_gateup_kernel(const XT* __restrict__ x, const int32_t* __restrict__ row_toke
   }
 }
 
-// ---------------------------------------------------------------------------
 // down projection
 // ---------------------------------------------------------------------------
 template <int G>
@@ -539,23 +564,22 @@ struct DownCfg {
   static constexpr int kStages = 3;
   static constexpr int kRows = 128;
   static constexpr int kKch = 512;
+  static constexpr int kWch = kKch / 32;
   static constexpr int kPairs = kKch / G / 2;
   static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);
   static constexpr int kScaleRow = kKch / G * 2;
   static constexpr int kBRowBytes = kKch * 2;  // one bf16 plane
+  static constexpr int kBch = kBRowBytes / 16;
   static constexpr int kBStride = kBRowBytes + (G == 64 ? 16 : 64);
   static constexpr int kW = 0;
   static constexpr int kS = kRows * kWStride;
   static constexpr int kB = kS + kRows * kScaleRow;             // [2 planes][kTok][kBStride]
   static constexpr int kStage = (kB + 2 * kTok * kBStride + 127) / 128 * 128;
-  static constexpr int kRedBuf = 8 * 4 * 32 * 4;
-  static constexpr size_t smem(int E) {
-    return (size_t)kStages * kStage + 2 * kRedBuf + sizeof(Ctl<kStages>) + (size_t)(4 * E + 4) * 4;
-  }
+  static constexpr int kRed = 8 * 4 * 32 * 4;
 };
 
 template <int G>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kDownThreads, 1)
 ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __restrict__ h_lo,
                 const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                 const uint8_t* __restrict__ w2_q, const uint16_t* __restrict__ w2_s, int H, int I, int E,
@@ -563,106 +587,84 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
   using C = DownCfg<G>;
   constexpr int S = C::kStages;
   extern __shared__ __align__(128) uint8_t smem[];
-  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [2][8][4][32]
-  Ctl<S>* ctl = reinterpret_cast<Ctl<S>*>(smem + S * C::kStage + 2 * C::kRedBuf);
-  int* mbase = reinterpret_cast<int*>(ctl + 1);
+  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [8][4][32]
+  int* mbase = reinterpret_cast<int*>(smem + S * C::kStage + C::kRed);
   const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
-  volatile int* abort_flag = &ctl->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, c = lane & 3;
+  const int rb = warp & 7, kh = warp >> 3;  // row block, K half
   const int tiles = H / C::kRows;
   const int NG = I / G;
   const int nkc = (I + C::kKch - 1) / C::kKch;
   const size_t row_bytes = (size_t)I / 2;
   const int na = active[0];
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&ctl->full[s]), kProducers * 32);  // one cp.async arrival per producer lane
-      mbar_init(smem_u32(&ctl->empty[s]), kConsumers);      // one arrival per consumer warp
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&ctl->red_full[b]), 8);
-      mbar_init(smem_u32(&ctl->red_empty[b]), 8);
-    }
-    ctl->abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-  }
   const int total = build_meta(offsets, active, tiles, meta);
   int q0, q1;
   cta_range(total, q0, q1);
   const int ntask = (q1 - q0) * nkc;
   if (ntask == 0) return;
 
-  if (warp >= kConsumers) {
-    // ---------------- producer warps ----------------
-    // The 64 producer lanes split the weight and scale copies evenly; the
-    // h rows go to the warp of their parity.
-    const int pw = warp - kConsumers;
-    const int pl_lane = pw * 32 + lane;
-    constexpr int kWch = C::kKch / 32;  // 16-byte weight chunks per row (full chunk)
-    Cursor cu = cursor_at(q0, na, tiles, meta);
-    int issued = 0;
-    for (int t = 0; t < ntask; ++t) {
-      const int s = t % S;
-      if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
-      const int k0 = cu.kc * C::kKch;
-      const int kel = min(C::kKch, I - k0);
-      const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
-      const uint32_t full = smem_u32(&ctl->full[s]);
-      const uint32_t st = smem_u32(smem + s * C::kStage);
-      const size_t rbase = (size_t)meta.e[cu.slot] * H + (size_t)cu.tile * C::kRows;
-#pragma unroll 4
-      for (int q = pl_lane; q < C::kRows * kWch; q += kProducers * 32) {
-        const int rr = q / kWch, cc = q % kWch;
-        if (cc * 32 < kel)
-          cp_async16(st + C::kW + rr * C::kWStride + cc * 16, w2_q + (rbase + rr) * row_bytes + k0 / 2 + cc * 16);
-      }
-      const int row_p = meta.row0[cu.slot] + cu.pass * kTok;
-      for (int b = pw; b < 2 * nt; b += kProducers) {
-        const int pl = b / nt, n = b - pl * nt;
+  auto issue = [&](const Cursor& cu, int task) {
+    uint8_t* st = smem + (task % S) * C::kStage;
+    const int k0 = cu.kc * C::kKch;
+    const int kel = min(C::kKch, I - k0);
+    const size_t rbase = (size_t)meta.e[cu.slot] * H + (size_t)cu.tile * C::kRows;
+#pragma unroll
+    for (int q = threadIdx.x; q < C::kRows * C::kWch; q += kDownThreads) {
+      const int rr = q / C::kWch, cc = q % C::kWch;
+      if (cc * 32 < kel)
+        cp_async16(smem_u32(st + C::kW + rr * C::kWStride + cc * 16), w2_q + (rbase + rr) * row_bytes + k0 / 2 + cc * 16);
+    }
+#pragma unroll
+    for (int q = threadIdx.x; q < C::kRows * C::kPairs; q += kDownThreads) {
+      const int rr = q / C::kPairs, pp = q % C::kPairs;
+      if (pp * 2 * G < kel)
+        cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
+    }
+    // h rows of the pass (both planes), this K-chunk
+    const int row_p = meta.row0[cu.slot] + cu.pass * kTok;
+    const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
+#pragma unroll
+    for (int q = threadIdx.x; q < 2 * kTok * C::kBch; q += kDownThreads) {
+      const int pl = q / (kTok * C::kBch);
+      const int n = (q / C::kBch) % kTok, cc = q % C::kBch;
+      if (n < nt && cc * 8 < kel) {
         const __nv_bfloat16* src = (pl ? h_lo : h_hi) + (size_t)(row_p + n) * I + k0;
-        warp_copy(st + C::kB + (pl * kTok + n) * C::kBStride, reinterpret_cast<const uint8_t*>(src), kel * 2, lane);
-      }
-#pragma unroll 4
-      for (int q = pl_lane; q < C::kRows * C::kPairs; q += kProducers * 32) {
-        const int rr = q / C::kPairs, pp = q % C::kPairs;
-        if (pp * 2 * G < kel)
-          cp_async4(st + C::kS + rr * C::kScaleRow + pp * 4, w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
-      }
-      cp_async_arrive_noinc(full);
-      ++issued;
-      cursor_next(cu, tiles, nkc, meta);
-    }
-    for (int t = max(0, issued - S); t < issued; ++t) {
-      const uint32_t full = smem_u32(&ctl->full[t % S]);
-      for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(full, (t / S) & 1); ++i) {
+        cp_async16(smem_u32(st + C::kB + (pl * kTok + n) * C::kBStride + cc * 16),
+                   reinterpret_cast<const uint8_t*>(src) + cc * 16);
       }
     }
-    return;
-  }
+  };
 
-  // ---------------- consumer warps ----------------
-  const int r = lane >> 2, c = lane & 3;
-  const int rbk = warp & 7, kh = warp >> 3;  // row block, K half
-  const int lr0 = rbk * 16 + r;
+  Cursor ci = cursor_at(q0, na, tiles, meta);
+  for (int s = 0; s < S - 1; ++s) {
+    if (s < ntask) issue(ci, s);
+    cp_async_commit();
+    cursor_next(ci, tiles, nkc, meta);
+  }
+  Cursor cm = cursor_at(q0, na, tiles, meta);
+
+  float acc[4];
+  const int lr0 = rb * 16 + r;
   const int a_off = (G == 64) ? 8 * c : 4 * c;
   const int b_off = (G == 64 ? 32 : 16) * c;
-  constexpr int kScH = C::kScaleRow / 2;
-  Cursor cu = cursor_at(q0, na, tiles, meta);
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  int item = 0;
-  for (int t = 0; t < ntask; ++t) {
-    const int s = t % S;
-    if (cu.kc == 0) {
+  for (int task = 0; task < ntask; ++task) {
+    if (task + S - 1 < ntask) issue(ci, task + S - 1);
+    cp_async_commit();
+    cursor_next(ci, tiles, nkc, meta);
+    if (cm.kc == 0) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[q] = 0.f;
     }
-    const int ngt = min(C::kKch, I - cu.kc * C::kKch) / G;
-    const int n = meta.n[cu.slot], p0 = cu.pass * kTok;
+    const int ngt = min(C::kKch, I - cm.kc * C::kKch) / G;
+    const int n = meta.n[cm.slot], p0 = cm.pass * kTok;
     const bool tok_ok = p0 + r < n;  // B rows beyond the pass hold stale data: use zeros
-    if (!wait_phase(smem_u32(&ctl->full[s]), (t / S) & 1, abort_flag)) return;
-    const uint8_t* st = smem + s * C::kStage;
+    cp_async_wait<S - 1>();
+    __syncthreads();
+    const uint8_t* st = smem + (task % S) * C::kStage;
     const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
+    constexpr int kScH = C::kScaleRow / 2;
 #pragma unroll 2
     for (int g = kh; g < ngt; g += 2) {
       const uint8_t* ab = st + C::kW + g * (G / 2) + a_off;
@@ -679,34 +681,27 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
       }
       down_group<G>(a0, a8, b, __half2float(sc[lr0 * kScH + g]), __half2float(sc[(lr0 + 8) * kScH + g]), acc);
     }
-    warp_arrive(smem_u32(&ctl->empty[s]), lane);
-    if (cu.kc == nkc - 1) {
-      const int buf = item & 1;
-      const int use = item >> 1;
-      float* rb = red + buf * (C::kRedBuf / 4);
+    if (cm.kc == nkc - 1) {
       if (kh == 1) {
-        if (use > 0 && !wait_phase(smem_u32(&ctl->red_empty[buf]), (use - 1) & 1, abort_flag)) return;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) rb[(rbk * 4 + q) * 32 + lane] = acc[q];
-        warp_arrive(smem_u32(&ctl->red_full[buf]), lane);
-      } else {
-        if (!wait_phase(smem_u32(&ctl->red_full[buf]), use & 1, abort_flag)) return;
-        float v[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) v[q] = acc[q] + rb[(rbk * 4 + q) * 32 + lane];
-        warp_arrive(smem_u32(&ctl->red_empty[buf]), lane);
-        const int row0 = meta.row0[cu.slot];
+        for (int q = 0; q < 4; ++q) red[(rb * 4 + q) * 32 + lane] = acc[q];
+      }
+      __syncthreads();
+      if (kh == 0) {
+        const int row0 = meta.row0[cm.slot];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const int hrow = cu.tile * C::kRows + lr0 + (q >= 2 ? 8 : 0);
+          const float v = acc[q] + red[(rb * 4 + q) * 32 + lane];
+          const int hrow = cm.tile * C::kRows + lr0 + (q >= 2 ? 8 : 0);
           const int rr = p0 + 2 * c + (q & 1);
-          if (rr < n) y[(size_t)(row0 + rr) * H + hrow] = v[q];
+          if (rr < n) y[(size_t)(row0 + rr) * H + hrow] = v;
         }
       }
-      ++item;
     }
-    cursor_next(cu, tiles, nkc, meta);
+    cursor_next(cm, tiles, nkc, meta);
+    __syncthreads();  // stage (task % S) and `red` are free again
   }
+  cp_async_wait<0>();
 }
 
 template <typename K>
@@ -714,25 +709,81 @@ void set_smem(K kern, size_t bytes) {
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// Tensor map over w13_q viewed as [rows = E*2I][K bytes = H/2], for 16-row
+// boxes of `box_chunks` 128-byte K-chunks with 128-byte swizzle. First choice:
+// a 3-D view (128 B, rows, K-chunks) so one copy moves the whole box; if the
+// driver rejects it, a 2-D view copied one 128-byte chunk at a time (same
+// shared-memory layout). Returns 0 (2-D), 1 (3-D) or -1 (no map).
+int make_w13_map(CUtensorMap* map, const uint8_t* w13_q, long long rows, int H, int box_chunks) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return -1;
+  {
+    const cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)(H / 256)};
+    const cuuint64_t strides[2] = {(cuuint64_t)(H / 2), 128};
+    const cuuint32_t box[3] = {128, 16, (cuuint32_t)box_chunks};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(w13_q), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+      return 1;
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)(H / 2), (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(H / 2)};
+  const cuuint32_t box[2] = {128, 16};
+  const cuuint32_t estr[2] = {1, 1};
+  if (enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w13_q), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+    return 0;
+  return -1;
+}
+
 template <int G, typename XT>
-void launch_gateup(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
-                   const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
-                   __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
+int launch_gateup(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
+                  const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
+                  __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
+  const int box_chunks = std::min(H, GateUpCfg<G, XT>::kKch) / 256;
+  alignas(64) CUtensorMap map;
+  const int mode = make_w13_map(&map, w13_q, (long long)E * 2 * I, H, box_chunks);
+  if (mode < 0) return PHMOE_ERR_CUDA;
   const size_t smem = GateUpCfg<G, XT>::smem(E);
   auto k = ffn_gateup_kernel<G, XT>;
   set_smem(k, smem);
-  k<<<grid, kThreads, smem, st>>>(static_cast<const XT*>(x), row_token, offsets, active, w13_q, w13_s, H, I,
-                                  E, h_hi, h_lo);
+  k<<<grid, kGuThreads, smem, st>>>(map, mode, box_chunks, static_cast<const XT*>(x), row_token, offsets, active,
+                                    w13_s, H, I, E, h_hi, h_lo);
+  return PHMOE_OK;
+}
+
+template <int G>
+size_t down_smem(int E) {
+  using C = DownCfg<G>;
+  return (size_t)C::kStages * C::kStage + C::kRed + (size_t)(4 * E + 4) * 4;
 }
 
 template <int G>
 void launch_down(const __nv_bfloat16* h_hi, const __nv_bfloat16* h_lo, const int32_t* offsets,
                  const int32_t* active, const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, float* y,
                  int grid, cudaStream_t st) {
-  const size_t smem = DownCfg<G>::smem(E);
+  const size_t smem = down_smem<G>(E);
   auto k = ffn_down_kernel<G>;
   set_smem(k, smem);
-  k<<<grid, kThreads, smem, st>>>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
+  k<<<grid, kDownThreads, smem, st>>>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
 }
 
 }  // namespace
@@ -759,13 +810,14 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
   __nv_bfloat16* h_lo = h_hi + (size_t)R * I;
   const int grid = device_sm_count();
   const bool f32 = x_dtype == PHMOE_DTYPE_F32;
-  if (G == 64) {
-    if (f32) launch_gateup<64, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
-    else launch_gateup<64, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
-  } else {
-    if (f32) launch_gateup<32, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
-    else launch_gateup<32, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
-  }
+  int s;
+  if (G == 64)
+    s = f32 ? launch_gateup<64, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
+            : launch_gateup<64, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
+  else
+    s = f32 ? launch_gateup<32, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
+            : launch_gateup<32, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
+  if (s) return s;
   if (mid_event) cudaEventRecord(mid_event, st);
   if (G == 64) launch_down<64>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
   else launch_down<32>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);

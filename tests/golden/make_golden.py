@@ -120,20 +120,27 @@ def run_tf_block(kind, x, wr, d13, d2, k, renorm=True):
             idx.numpy().astype(np.int32), scores.numpy().astype(np.float32))
 
 
-def make_small_block(kind, name, T, H, E, k, I, group, seed, keep_dense=False):
+def small_block_inputs(T, H, E, I, seed):
+    """Seeded inputs of a small-block fixture (tests regenerate the dense
+    expert weights this way instead of storing them)."""
     g = torch.Generator().manual_seed(seed)
     x = torch.randn(T, H, generator=g).numpy()
     wr = (torch.randn(E, H, generator=g) * 0.02).numpy()
     w13 = (torch.randn(E, 2 * I, H, generator=g) * 0.02).numpy()
     w2 = (torch.randn(E, H, I, generator=g) * 0.02).numpy()
+    return x, wr, w13, w2
+
+
+def make_small_block(kind, name, T, H, E, k, I, group, seed):
+    x, wr, w13, w2 = small_block_inputs(T, H, E, I, seed)
     p13, s13 = O.quantize_int4(w13, group)
     p2, s2 = O.quantize_int4(w2, group)
     d13 = O.dequantize_int4(p13, s13, group)
     d2 = O.dequantize_int4(p2, s2, group)
     out, probs, idx, scores = run_tf_block(kind, x, wr, d13, d2, k)
-    dense = dict(w13=w13) if keep_dense else {}
-    np.savez_compressed(OUT / name, x=x, wr=wr, w13_q=p13, w13_s=s13, w2_q=p2, w2_s=s2, **dense,
-                        group=np.int32(group), top_k=np.int32(k), out=out, probs=probs, idx=idx, scores=scores)
+    np.savez_compressed(OUT / name, x=x, wr=wr, w13_q=p13, w13_s=s13, w2_q=p2, w2_s=s2,
+                        dims=np.array([T, H, E, I, seed], np.int32), group=np.int32(group),
+                        top_k=np.int32(k), out=out, probs=probs, idx=idx, scores=scores)
 
 
 def gen_cfg1_inputs():
@@ -174,10 +181,9 @@ def main():
     GGUFLoader, QT, tmr = import_reference(Path(args.reference))
     make_q4_0(GGUFLoader, QT)
     make_router_phantom(tmr)
-    make_small_block("qwen3", "qwen3_block_small.npz", T=12, H=128, E=16, k=4, I=128, group=64, seed=11,
-                     keep_dense=True)
-    make_small_block("qwen3", "qwen3_block_small_g32.npz", T=9, H=128, E=8, k=2, I=64, group=32, seed=12)
-    make_small_block("mixtral", "mixtral_block_small.npz", T=10, H=128, E=8, k=2, I=128, group=64, seed=13)
+    make_small_block("qwen3", "qwen3_block_small.npz", T=12, H=256, E=16, k=4, I=128, group=64, seed=11)
+    make_small_block("qwen3", "qwen3_block_small_g32.npz", T=9, H=256, E=8, k=2, I=64, group=32, seed=12)
+    make_small_block("mixtral", "mixtral_block_small.npz", T=10, H=256, E=8, k=2, I=128, group=64, seed=13)
     if not args.skip_cfg1:
         make_cfg1()
     for p in sorted(OUT.glob("*.npz")):

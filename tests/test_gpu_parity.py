@@ -167,13 +167,16 @@ def test_dispatch_all_tokens_one_expert_set(cuda_device):
 
 def test_quantizer_bytes_match_oracle(cuda_device):
     import phantom_moe as pm
+    from test_oracle_golden import small_block_dense
     g = load_golden("qwen3_block_small.npz")
+    w13, _ = small_block_dense(g)
+    assert np.array_equal(O.quantize_int4(w13, 64)[0], g["w13_q"])
     for G in (64, 32):
-        p, s = pm.quantize_int4(cu(g["w13"]), G)
-        p_ref, s_ref = O.quantize_int4(g["w13"], G)
+        p, s = pm.quantize_int4(cu(w13), G)
+        p_ref, s_ref = O.quantize_int4(w13, G)
         assert np.array_equal(p.cpu().numpy(), p_ref)
         assert np.array_equal(s.cpu().numpy(), s_ref)
-    wb = cu(g["w13"][:, :64]).to(torch.bfloat16).contiguous()
+    wb = cu(w13[:, :64]).to(torch.bfloat16).contiguous()
     p, s = pm.quantize_int4(wb, 64)
     p_ref, s_ref = O.quantize_int4(bf16_np(wb), 64)
     assert np.array_equal(p.cpu().numpy(), p_ref) and np.array_equal(s.cpu().numpy(), s_ref)

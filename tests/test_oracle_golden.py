@@ -61,10 +61,27 @@ def test_quantizer_roundtrip_bounds():
     assert np.all(p == 0x88) and np.all(s == 0)
 
 
+def small_block_dense(g):
+    """Dense expert weights of a small-block fixture, regenerated from its seed
+    (tests/golden/make_golden.py:small_block_inputs)."""
+    T, H, E, I, seed = (int(v) for v in g["dims"])
+    gen = torch.Generator().manual_seed(seed)
+    torch.randn(T, H, generator=gen)
+    torch.randn(E, H, generator=gen)
+    w13 = (torch.randn(E, 2 * I, H, generator=gen) * 0.02).numpy()
+    w2 = (torch.randn(E, H, I, generator=gen) * 0.02).numpy()
+    return w13, w2
+
+
 def test_quantizer_matches_fixture_bytes():
-    g = load_golden("qwen3_block_small.npz")
-    p13, s13 = O.quantize_int4(g["w13"], 64)
-    assert np.array_equal(p13, g["w13_q"]) and np.array_equal(s13, g["w13_s"])
+    for name in ("qwen3_block_small.npz", "qwen3_block_small_g32.npz", "mixtral_block_small.npz"):
+        g = load_golden(name)
+        w13, w2 = small_block_dense(g)
+        G = int(g["group"])
+        p13, s13 = O.quantize_int4(w13, G)
+        p2, s2 = O.quantize_int4(w2, G)
+        assert np.array_equal(p13, g["w13_q"]) and np.array_equal(s13, g["w13_s"])
+        assert np.array_equal(p2, g["w2_q"]) and np.array_equal(s2, g["w2_s"])
 
 
 # ---- exp / router --------------------------------------------------------
