@@ -352,13 +352,19 @@ __device__ __forceinline__ void cta_range(int total, int& q0, int& q1) {
 // ---------------------------------------------------------------------------
 // gate/up + SwiGLU (TMA-fed, warp-specialised)
 // ---------------------------------------------------------------------------
-template <int G, typename XT>
+// KCH = K elements per task. 2048 (3 stages, one reduction buffer) gives each
+// consumer warp 2 (G=64) or 4 (G=32) groups per task, amortising the per-task
+// work; 1024 (5 stages, 3 for fp32; two reduction buffers) is used when that
+// does not fit in shared memory.
+template <int G, typename XT, int KCH>
 struct GateUpCfg {
   static constexpr bool kF32 = std::is_same<XT, float>::value;
-  static constexpr int kStages = kF32 ? 3 : 5;
+  static constexpr int kStages = KCH == 2048 ? 3 : (kF32 ? 3 : 5);
+  static constexpr int kRedBufs = KCH == 2048 ? 1 : 2;
   static constexpr int kRows = 32;
-  static constexpr int kKch = 1024;                          // K elements per task
-  static constexpr int kBlock = 16 * (kKch / 2);             // one 16-row box: 8 KB
+  static constexpr int kKch = KCH;
+  static constexpr int kGpw = kKch / G / kConsumers;         // groups per consumer warp per task
+  static constexpr int kBlock = 16 * (kKch / 2);             // one 16-row box
   static constexpr int kScaleRow = kKch / G * 2;
   static constexpr int kPairs = kKch / G / 2;
   static constexpr int kBRowBytes = kKch * (int)sizeof(XT);
@@ -370,7 +376,8 @@ struct GateUpCfg {
   static constexpr int kStage = (kB + kTok * kBStride + 1023) / 1024 * 1024;
   static constexpr int kRedBuf = kConsumers * 8 * 32 * 4;
   static constexpr size_t smem(int E) {
-    return 1024 + (size_t)kStages * kStage + 2 * kRedBuf + sizeof(Ctl<kStages>) + (size_t)(4 * E + 4) * 4;
+    return 1024 + (size_t)kStages * kStage + kRedBufs * kRedBuf + sizeof(Ctl<kStages>) +
+           (size_t)(4 * E + 4) * 4;
   }
 };
 
@@ -382,20 +389,20 @@ __device__ __forceinline__ int swz_off(int Rb, int kb) {
   return ((kb >> 7) * 16 + Rb) * 128 + ((((c0 >> 4) ^ (Rb & 7)) << 4) | (c0 & 15));
 }
 
-template <int G, typename XT>
+template <int G, typename XT, int KCH>
 __global__ void __launch_bounds__(kGuThreads, 1)
 ffn_gateup_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int box_chunks,
                   const XT* __restrict__ x, const int32_t* __restrict__ row_token,
                   const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                   const uint16_t* __restrict__ w13_s, int H, int I, int E,
                   __nv_bfloat16* __restrict__ h_hi, __nv_bfloat16* __restrict__ h_lo) {
-  using C = GateUpCfg<G, XT>;
+  using C = GateUpCfg<G, XT, KCH>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   // 128-byte swizzled TMA destinations must be 1024-byte aligned
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [2][kConsumers][8][32]
-  Ctl<S>* ctl = reinterpret_cast<Ctl<S>*>(smem + S * C::kStage + 2 * C::kRedBuf);
+  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [kRedBufs][kConsumers][8][32]
+  Ctl<S>* ctl = reinterpret_cast<Ctl<S>*>(smem + S * C::kStage + C::kRedBufs * C::kRedBuf);
   int* mbase = reinterpret_cast<int*>(ctl + 1);
   const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
   volatile int* abort_flag = &ctl->abort_flag;
@@ -481,9 +488,21 @@ ffn_gateup_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int bo
   }
 
   // ---------------- consumer warps ----------------
+  // Warp w computes groups g_j = w + 16 j (j < kGpw) of every task; their
+  // shared-memory offsets inside a stage are fixed, so they are computed once.
   const int r = lane >> 2, c = lane & 3;
-  const int b_off = (G == 64 ? 16 : 8) * c * (int)sizeof(XT);
+  constexpr int kGpw = C::kGpw;
   constexpr int kScH = C::kScaleRow / 2;
+  int o0[kGpw], o8[kGpw], ob[kGpw], os[kGpw];
+#pragma unroll
+  for (int j = 0; j < kGpw; ++j) {
+    const int g = warp + kConsumers * j;
+    const int kb = (G == 64) ? g * 32 + 8 * c : g * 16 + 4 * c;
+    o0[j] = C::kW + swz_off(r, kb);
+    o8[j] = C::kW + swz_off(r + 8, kb);
+    ob[j] = C::kB + r * C::kBStride + g * G * (int)sizeof(XT) + (G == 64 ? 16 : 8) * c * (int)sizeof(XT);
+    os[j] = C::kS + (r * kScH + g) * 2;
+  }
   Cursor cu = cursor_at(q0, na, tiles, meta);
   float acc_g[4] = {0.f, 0.f, 0.f, 0.f}, acc_u[4] = {0.f, 0.f, 0.f, 0.f};
   int item = 0;
@@ -496,29 +515,25 @@ ffn_gateup_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int bo
     const int ngt = min(C::kKch, H - cu.kc * C::kKch) / G;
     if (!wait_phase(smem_u32(&ctl->full[s]), (t / S) & 1, abort_flag)) return;
     const uint8_t* st = smem + s * C::kStage;
-    const uint8_t* wg = st + C::kW;
-    const uint8_t* wu = st + C::kW + C::kBlock;
-    const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
-#pragma unroll 2
-    for (int g = warp; g < ngt; g += kConsumers) {
-      const int kb = (G == 64) ? g * 32 + 8 * c : g * 16 + 4 * c;
-      const int o0 = swz_off(r, kb), o8 = swz_off(r + 8, kb);
-      const RowWords<G> ag0 = lds_row<G>(wg + o0);
-      const RowWords<G> ag8 = lds_row<G>(wg + o8);
-      const RowWords<G> au0 = lds_row<G>(wu + o0);
-      const RowWords<G> au8 = lds_row<G>(wu + o8);
-      BWords<G> b;
-      const uint8_t* bb = st + C::kB + r * C::kBStride + g * G * (int)sizeof(XT) + b_off;
-      if constexpr (C::kF32) lds_b_f32<G>(bb, b);
-      else lds_b_plane<G>(bb, b.hi);
-      gateup_group<G, C::kF32>(ag0, ag8, au0, au8, b, __half2float(sc[r * kScH + g]),
-                               __half2float(sc[(r + 8) * kScH + g]), __half2float(sc[(16 + r) * kScH + g]),
-                               __half2float(sc[(24 + r) * kScH + g]), acc_g, acc_u);
+#pragma unroll
+    for (int j = 0; j < kGpw; ++j) {
+      if (warp + kConsumers * j < ngt) {
+        const RowWords<G> ag0 = lds_row<G>(st + o0[j]);
+        const RowWords<G> ag8 = lds_row<G>(st + o8[j]);
+        const RowWords<G> au0 = lds_row<G>(st + o0[j] + C::kBlock);
+        const RowWords<G> au8 = lds_row<G>(st + o8[j] + C::kBlock);
+        BWords<G> b;
+        if constexpr (C::kF32) lds_b_f32<G>(st + ob[j], b);
+        else lds_b_plane<G>(st + ob[j], b.hi);
+        const __half* sc = reinterpret_cast<const __half*>(st + os[j]);
+        gateup_group<G, C::kF32>(ag0, ag8, au0, au8, b, __half2float(sc[0]), __half2float(sc[8 * kScH]),
+                                 __half2float(sc[16 * kScH]), __half2float(sc[24 * kScH]), acc_g, acc_u);
+      }
     }
     warp_arrive(smem_u32(&ctl->empty[s]), lane);  // this warp is done with the stage
     if (cu.kc == nkc - 1) {
-      const int buf = item & 1;
-      const int use = item >> 1;
+      const int buf = C::kRedBufs == 2 ? (item & 1) : 0;
+      const int use = C::kRedBufs == 2 ? (item >> 1) : item;
       float* rb = red + buf * (C::kRedBuf / 4);
       if (use > 0 && !wait_phase(smem_u32(&ctl->red_empty[buf]), (use - 1) & 1, abort_flag)) return;
 #pragma unroll
@@ -754,20 +769,34 @@ int make_w13_map(CUtensorMap* map, const uint8_t* w13_q, long long rows, int H, 
   return -1;
 }
 
-template <int G, typename XT>
-int launch_gateup(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
-                  const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
-                  __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
-  const int box_chunks = std::min(H, GateUpCfg<G, XT>::kKch) / 256;
+constexpr size_t kMaxSmem = 227 * 1024;
+
+template <int G, typename XT, int KCH>
+int launch_gateup_k(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
+                    const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
+                    __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
+  const int box_chunks = std::min(H, KCH) / 256;
   alignas(64) CUtensorMap map;
   const int mode = make_w13_map(&map, w13_q, (long long)E * 2 * I, H, box_chunks);
   if (mode < 0) return PHMOE_ERR_CUDA;
-  const size_t smem = GateUpCfg<G, XT>::smem(E);
-  auto k = ffn_gateup_kernel<G, XT>;
+  const size_t smem = GateUpCfg<G, XT, KCH>::smem(E);
+  auto k = ffn_gateup_kernel<G, XT, KCH>;
   set_smem(k, smem);
   k<<<grid, kGuThreads, smem, st>>>(map, mode, box_chunks, static_cast<const XT*>(x), row_token, offsets, active,
                                     w13_s, H, I, E, h_hi, h_lo);
   return PHMOE_OK;
+}
+
+// 2048-element tasks for bf16 activations when H needs them and they fit.
+template <int G, typename XT>
+int launch_gateup(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
+                  const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
+                  __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
+  if constexpr (!std::is_same<XT, float>::value) {
+    if (H >= 2048 && GateUpCfg<G, XT, 2048>::smem(E) <= kMaxSmem)
+      return launch_gateup_k<G, XT, 2048>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
+  }
+  return launch_gateup_k<G, XT, 1024>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
 }
 
 template <int G>
