@@ -108,7 +108,9 @@ int phmoe_dispatch(const int32_t* topk_idx, int T, int top_k, int E, int32_t* ex
  *   w13_s    [E, 2I, H/G] fp16        w2_q [E, H, I/2] uint8   w2_s [E, H, I/G] fp16
  *   h        scratch of T*k*I*4 bytes (bf16 hi and lo planes of the SwiGLU output)
  *   y        [T*k, H] fp32 output (permuted rows)
- * Limits: H % 64 == 0, I % 64 == 0 (G = 64) or % 32 (G = 32).
+ * Limits: G in {32, 64}; H % 256 == 0 (gate/up weight tiles are copied by TMA
+ * in 128-byte rows); I % 16 == 0 and I % (2G) == 0; w13_s and w2_s 4-byte
+ * aligned; w13_q 16-byte aligned.
  */
 int phmoe_expert_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                             const int32_t* expert_offsets, const int32_t* active,
