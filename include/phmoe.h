@@ -141,6 +141,32 @@ int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtyp
                     float* topk_w_out, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * phmoe_moe_layer without a workspace argument, for callers that cannot
+ * allocate device memory: hosts handed buffers by another framework whose
+ * allocator already holds the GPU's free memory, hosts that forbid device
+ * allocation after load (cudaFree synchronises the device, cudaMalloc may),
+ * and foreign-language bindings with no allocator to call. No counterpart in
+ * the reference (its kernels cudaMalloc scratch per call).
+ *
+ * Scratch comes from a fixed array of PHMOE_STATIC_SCRATCH_BYTES inside the
+ * library, held on every GPU that loads the library until the process exits.
+ * Calls needing more (phmoe_workspace_size(...) > PHMOE_STATIC_SCRATCH_BYTES;
+ * at H 2048, E 128, top-8, I 768 that is beyond 184 tokens) return
+ * PHMOE_ERR_WORKSPACE without launching anything. All calls on a device share
+ * the array, which keeps the last call's contents (nothing in it has to start
+ * at zero); calls that overlap on the GPU race on it, so order them on one
+ * stream. The first call on each device looks up the array's address
+ * (cudaGetSymbolAddress); make it before any stream capture on that device.
+ * Allocates nothing. Same arguments and results as phmoe_moe_layer.
+ */
+#define PHMOE_STATIC_SCRATCH_BYTES ((size_t)16 << 20)
+int phmoe_moe_layer_noalloc(const void* x, int x_dtype, const void* router_w, int w_dtype,
+                            const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
+                            const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
+                            int group_size, int renormalize, int path, void* out,
+                            int32_t* topk_idx_out, float* topk_w_out, void* stream);
+
+/*
  * Symmetric int4 group quantiser on the GPU (load-time utility; the
  * reference has no quantiser and reads pre-quantised GGUF files):
  * scale = fp16(absmax(group)/7), q = clamp(rint(w/scale), -8, 7).

@@ -131,6 +131,8 @@ int device_sm_count() {
   return cache[dev];
 }
 
+int record_error(int status, const char* msg) { return fail(status, "%s", msg); }
+
 }  // namespace phmoe
 
 using namespace phmoe;

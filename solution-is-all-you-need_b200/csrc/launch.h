@@ -38,4 +38,7 @@ int ffn_device_error(bool reset);
 // Host-side count of kernels enqueued by this library (see phmoe.h).
 void note_launches(int n);
 
+// Sets the text phmoe_last_error returns on this host thread; returns status.
+int record_error(int status, const char* msg);
+
 }  // namespace phmoe

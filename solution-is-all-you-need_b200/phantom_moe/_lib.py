@@ -46,6 +46,8 @@ SIGNATURES = {
     "phmoe_combine": (_I, [_P, _P, _P, _I, _I, _I, _P, _I, _P]),
     "phmoe_moe_layer": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
                              _P, _P, _P, _P, _SZ, _P]),
+    "phmoe_moe_layer_noalloc": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
+                                     _P, _P, _P, _P]),
     "phmoe_quantize_int4": (_I, [_P, _I, _LL, _I, _I, _P, _P, _P]),
     "phmoe_kernel_launch_count": (ctypes.c_ulonglong, []),
     "phmoe_profile_begin": (_I, [_I]),
