@@ -375,11 +375,102 @@ def _sweep_entry(v):
 
 
 def run_ep(args, ws, rank, device):
+    """N > 1: experts sharded E/N per rank, each rank routes its own
+    ``--tokens`` tokens (weak scaling), NCCL all-to-all dispatch and return.
+    Every rank runs the same collectives in the same order."""
     import torch.distributed as dist
+    import phantom_moe as pm
     from phantom_moe import ep
-    res = ep.bench_ep(args, ws, rank, device, make_layer, ClockSampler, H=H, E=E, k=K_TOP, I=I, G=G)
-    if rank == 0 and res is not None:
-        print(json.dumps(res), flush=True)
+    lib = pm.load_library()
+    L, T = args.layers, args.tokens
+    lo, hi = ep.shard_range(E, ws, rank)
+    layers = [make_layer(1 + l, device, expert_range=(lo, hi)) for l in range(L)]
+    g = torch.Generator(device=device).manual_seed(1000 + T + 7919 * rank)
+    xs = [torch.randn(T, H, device=device, generator=g).to(torch.bfloat16) for _ in range(L)]
+    torch.cuda.synchronize()
+
+    def step(i, x=None, stats=None):
+        l = i % L
+        return ep.moe_layer_ep(xs[l] if x is None else x, layers[l][0], *_pk(layers[l][1]), K_TOP, True, G,
+                               None, stats=stats)
+
+    # imbalance and local experts hit, per layer (outside the timed region)
+    hit, recv = [], []
+    for l in range(L):
+        st = {}
+        step(l, stats=st)
+        hit.append(st["local_experts_hit"])
+        recv.append(sum(st["recv_rows"]))
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn, K, W):
+        for i in range(W):
+            fn(i)
+        dist.barrier()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for i in range(K):
+            fn(i)
+        ev1.record(stream)
+        ev1.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        t = torch.tensor([ev0.elapsed_time(ev1) / K], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    n0 = lib.phmoe_kernel_launch_count()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ms = timed(step, args.steps, args.warmup)
+    launches = lib.phmoe_kernel_launch_count() - n0
+    clocks = clk.summary()
+    # end to end: pinned host tokens in, output back to the host, every step
+    gh = torch.Generator().manual_seed(2000 + T + 7919 * rank)
+    xh = [torch.randn(T, H, generator=gh).to(torch.bfloat16).pin_memory() for _ in range(L)]
+    oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty(T, H, dtype=torch.bfloat16, device=device)
+
+    def e2e_step(i):
+        xd.copy_(xh[i % L], non_blocking=True)
+        out = step(i, x=xd)
+        oh.copy_(out, non_blocking=True)
+        stream.synchronize()
+
+    ms_e2e = timed(e2e_step, args.steps, args.warmup)
+    # per-GPU weight bytes streamed per step (mean over layers and ranks)
+    stats = torch.tensor([float(np.mean(hit)), float(max(recv)), float(np.mean(recv))], device=device)
+    gathered = [torch.empty_like(stats) for _ in range(ws)]
+    dist.all_gather(gathered, stats)
+    if rank == 0:
+        g_hit = float(np.mean([s[0].item() for s in gathered]))
+        recv_all = [s[1].item() for s in gathered]
+        recv_mean = float(np.mean([s[2].item() for s in gathered]))
+        peak, peak_kind = load_peaks()
+        bytes_gpu = g_hit * EXPERT_BYTES
+        achieved = bytes_gpu / (ms / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": ws * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights, int4 g64)",
+            "config": {"workload": f"qwen3-30b-a3b moe layer decode T={T} per GPU, expert-parallel",
+                       "hidden": H, "experts": E, "top_k": K_TOP, "intermediate": I, "group_size": G,
+                       "tokens_per_gpu": T, "global_batch": ws * T, "parallelism": f"ep{ws}",
+                       "experts_per_gpu": E // ws,
+                       "l2": f"inputs larger than L2: {L} layers' weights cycled per step",
+                       "exchange": "NCCL all_to_all_single: counts, bf16 rows out, fp32 rows back",
+                       "local_experts_hit_mean": g_hit, "recv_rows_max_over_ranks": max(recv_all),
+                       "recv_rows_mean": recv_mean},
+            "roofline": {"kernel": "layer (per GPU)", "bound": "hbm", "achieved": achieved, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                         "algorithmic_bytes_per_launch": bytes_gpu},
+            "cpu_baseline": None,
+            "e2e": {"value": ws * T / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                    "d2h_bytes_per_step": T * H * 2, "ms_per_step": ms_e2e},
+            "clocks": clocks, "gpu_launches": int(launches * args.steps // (args.steps + args.warmup)),
+        }
+        print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -441,6 +532,9 @@ def main():
     if ws > 1 and args.impl == "ours":
         import datetime
         import torch.distributed as dist
+        # keep stdout to the one JSON line (NCCL's version banner goes to stdout)
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))

@@ -127,6 +127,17 @@ int phmoe_combine(const float* y, const int32_t* inv, const float* topk_w, int T
                   int H, void* out, int out_dtype, void* stream);
 
 /*
+ * Row gather: dst[i] = src[index[i]] for i < n_rows, rows of row_bytes bytes;
+ * a row whose index is outside [0, src_rows) is zero-filled. Used by the
+ * expert-parallel layer to pack rows in expert order before the dispatch
+ * all-to-all and to restore arrival order before the return all-to-all. No
+ * counterpart in the reference (PHANTOM has no expert parallelism).
+ * Limits: row_bytes % 16 == 0; src and dst 16-byte aligned.
+ */
+int phmoe_gather_rows(const void* src, long long src_rows, const int32_t* index, int n_rows,
+                      long long row_bytes, void* dst, void* stream);
+
+/*
  * The whole layer (Qwen3MoeSparseMoeBlock.forward, modeling_qwen3_moe.py:281-286,
  * on [T, H] rows): router -> dispatch -> grouped FFN -> combine, all
  * stream-ordered, no host synchronisation, no allocation.

@@ -234,6 +234,19 @@ int phmoe_combine(const float* y, const int32_t* inv, const float* topk_w, int T
   return check_launch("phmoe_combine");
 }
 
+int phmoe_gather_rows(const void* src, long long src_rows, const int32_t* index, int n_rows,
+                      long long row_bytes, void* dst, void* stream) {
+  g_last_error.clear();
+  if (n_rows < 0 || src_rows < 0 || row_bytes <= 0 || row_bytes % 16 || row_bytes / 16 > (1LL << 30))
+    return fail(PHMOE_ERR_INVALID_ARG, "bad gather dims n_rows=%d src_rows=%lld row_bytes=%lld", n_rows,
+                src_rows, row_bytes);
+  if (n_rows == 0) return PHMOE_OK;
+  if (!index || !dst || (src_rows > 0 && !src)) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned(src, 16) || !aligned(dst, 16)) return fail(PHMOE_ERR_ALIGNMENT, "src and dst must be 16-byte aligned");
+  launch_gather_rows(src, src_rows, index, n_rows, row_bytes, dst, static_cast<cudaStream_t>(stream));
+  return check_launch("phmoe_gather_rows");
+}
+
 int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtype,
                     const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
                     const uint16_t* w2_s, int T, int H, int E, int top_k, int I,

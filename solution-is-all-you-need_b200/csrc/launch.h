@@ -27,6 +27,9 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
 int launch_combine(const float* y, const int32_t* inv, const float* topk_w, int T, int top_k,
                    int H, void* out, int out_dtype, cudaStream_t st);
 
+void launch_gather_rows(const void* src, long long src_rows, const int32_t* index, int n_rows,
+                        long long row_bytes, void* dst, cudaStream_t st);
+
 int launch_quantize(const void* w, int w_dtype, long long rows, int K, int G, uint8_t* packed,
                     uint16_t* scales, cudaStream_t st);
 

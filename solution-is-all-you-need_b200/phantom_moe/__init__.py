@@ -15,6 +15,7 @@ from .layer import (
     combine,
     dispatch,
     expert_ffn_decode,
+    gather_rows,
     moe_layer,
     pack_experts,
     quantize_int4,
@@ -29,6 +30,7 @@ __all__ = [
     "combine",
     "dispatch",
     "expert_ffn_decode",
+    "gather_rows",
     "load_library",
     "moe_layer",
     "pack_experts",

@@ -1,0 +1,203 @@
+"""Expert-parallel sparse-MoE layer: experts sharded over the ranks of a
+``torch.distributed`` group, tokens exchanged with all-to-all (NCCL over
+NVLink on B200s).
+
+PHANTOM has no expert parallelism; this follows the layer semantics of
+transformers' ``Qwen3MoeSparseMoeBlock.forward`` (modeling_qwen3_moe.py:
+281-286) with the experts spread over P GPUs.
+
+Sharding: with E experts and P ranks (E % P == 0) rank r holds experts
+``[r*E/P, (r+1)*E/P)`` (see :func:`shard_range`); the router weight is
+replicated and every rank routes its own tokens (data parallel). One layer
+call on each rank:
+
+1. router + dispatch of the rank's own T tokens. Rows come out expert-major
+   (token order inside an expert); since a rank's experts are contiguous,
+   that order is also destination-rank-major.
+2. all-to-all of the per-expert row counts ``[P, E/P]`` int32, then one
+   device-to-host copy of the send and receive counts: the split sizes the
+   row all-to-alls need (the only host synchronisation of the layer).
+3. rows packed in that order (:func:`phantom_moe.gather_rows`) and sent with
+   an all-to-all.
+4. the receiver labels arrived rows with their local expert (from the
+   counts), dispatches them by expert (stable in arrival order), runs the
+   grouped FFN and gathers its fp32 rows back into arrival order.
+5. the reverse all-to-all returns the fp32 rows to their source, which
+   combines them with its own routing weights in slot order.
+
+Per row the FFN result does not depend on which other rows share the batch,
+and the return path carries fp32, so the output equals the single-GPU layer's
+bit for bit.
+
+Every rank issues the same collectives in the same order whatever its token
+count (zero included). The compute steps go through an ``ops`` object
+(:class:`CudaOps` for the product path), so the exchange logic can be tested
+on CPU ranks with a checker's ops.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import layer as _layer
+
+
+def ep_world_size(group) -> int:
+    import torch.distributed as dist
+    if group is None or not dist.is_available() or not dist.is_initialized():
+        return 1
+    return dist.get_world_size(group)
+
+
+def shard_range(num_experts: int, world: int, rank: int) -> tuple[int, int]:
+    """Experts ``[lo, hi)`` held by ``rank`` of ``world`` ranks."""
+    if world < 1 or num_experts % world:
+        raise ValueError(f"{num_experts} experts do not split evenly over {world} ranks")
+    per = num_experts // world
+    return rank * per, (rank + 1) * per
+
+
+class CudaOps:
+    """The product's compute steps: the libphmoe CUDA kernels."""
+
+    def router(self, x, router_weight, top_k, renormalize):
+        idx, w, _ = _layer.router(x, router_weight, top_k, renormalize)
+        return idx, w
+
+    def dispatch(self, idx, num_experts):
+        return _layer.dispatch(idx, num_experts)
+
+    def gather(self, src, index):
+        return _layer.gather_rows(src, index)
+
+    def ffn(self, x, row_token, offsets, active, w13_q, w13_scales, w2_q, w2_scales, group_size):
+        return _layer.expert_ffn_decode(x, row_token, offsets, active, w13_q, w13_scales, w2_q, w2_scales,
+                                        top_k=1, group_size=group_size)
+
+    def combine(self, y, inv, topk_w, out_dtype):
+        return _layer.combine(y, inv, topk_w, out_dtype)
+
+
+_CUDA_OPS = CudaOps()
+
+
+@dataclass
+class Routed:
+    """A rank's routing of its own tokens."""
+    idx: torch.Tensor        # int32 [T, k]
+    w: torch.Tensor          # fp32 [T, k]
+    offsets: torch.Tensor    # int32 [E + 1], rows per expert (expert-major)
+    row_token: torch.Tensor  # int32 [T*k]
+    inv: torch.Tensor        # int32 [T, k], row of each (token, slot)
+    counts: torch.Tensor     # int32 [E], rows per expert = per (destination rank, local expert)
+
+
+def route_local(x, router_weight, top_k, renormalize, ops) -> Routed:
+    E = router_weight.shape[0]
+    idx, w = ops.router(x, router_weight, top_k, renormalize)
+    offsets, row_token, inv, _ = ops.dispatch(idx, E)
+    counts = (offsets[1:] - offsets[:-1]).to(torch.int32)
+    return Routed(idx, w, offsets, row_token, inv, counts)
+
+
+def rows_per_rank(counts_host: torch.Tensor, world: int) -> list[int]:
+    """Per-rank row totals from per-(rank, local expert) counts."""
+    return counts_host.view(world, -1).sum(1).tolist()
+
+
+def arrived_expert_ids(recv_counts: torch.Tensor, world: int, total: int) -> torch.Tensor:
+    """Local expert of each arrived row: source-major blocks, each expert-major."""
+    per = recv_counts.numel() // world
+    ids = torch.arange(per, dtype=torch.int32, device=recv_counts.device).repeat(world)
+    return torch.repeat_interleave(ids, recv_counts.to(torch.int64), output_size=total).to(torch.int32)
+
+
+def expert_compute(recv_x, recv_counts, world, w13_q, w13_scales, w2_q, w2_scales, group_size, ops):
+    """Grouped FFN over rows that arrived from all ranks; fp32 rows back in
+    arrival order."""
+    total = recv_x.shape[0]
+    per = w13_q.shape[0]
+    if total == 0:
+        return torch.empty(0, recv_x.shape[1], dtype=torch.float32, device=recv_x.device)
+    eid = arrived_expert_ids(recv_counts, world, total)
+    offsets, row_token, inv, active = ops.dispatch(eid.view(total, 1), per)
+    y = ops.ffn(recv_x, row_token, offsets, active, w13_q, w13_scales, w2_q, w2_scales, group_size)
+    return ops.gather(y, inv.view(-1))
+
+
+def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scales, top_k: int,
+                 renormalize: bool = True, group_size: int = 64, ep_group=None, *,
+                 return_routing: bool = False, ops=None, stats: dict | None = None):
+    """The MoE layer with this rank's expert shard (``w13_q`` etc. hold
+    ``E/P`` experts, ``router_weight`` all ``E``). Same result as
+    :func:`phantom_moe.moe_layer` on the full layer for this rank's tokens.
+
+    ``stats`` (a dict) receives ``send_rows`` / ``recv_rows``: the rows this
+    rank sent to / received from each rank (load-imbalance reporting), and
+    ``local_experts_hit``: how many of this rank's experts received rows.
+    """
+    import torch.distributed as dist
+    ops = _CUDA_OPS if ops is None else ops
+    world = dist.get_world_size(ep_group)  # None: the default group
+    shape = hidden_states.shape
+    H = shape[-1]
+    x = hidden_states.reshape(-1, H)
+    E = router_weight.shape[0]
+    if w13_q.shape[0] * world != E:
+        raise ValueError(f"this rank holds {w13_q.shape[0]} experts; {E} experts over {world} ranks "
+                         f"needs {E // max(world, 1)} per rank")
+    rt = route_local(x, router_weight, top_k, renormalize, ops)
+    recv_counts = torch.empty_like(rt.counts)
+    dist.all_to_all_single(recv_counts, rt.counts, group=ep_group)
+    both = torch.cat([rt.counts, recv_counts]).cpu()
+    send_rows = rows_per_rank(both[:E], world)
+    recv_rows = rows_per_rank(both[E:], world)
+    send_x = ops.gather(x, rt.row_token)
+    recv_x = x.new_empty((sum(recv_rows), H))
+    dist.all_to_all_single(recv_x, send_x, recv_rows, send_rows, group=ep_group)
+    y_arrived = expert_compute(recv_x, recv_counts, world, w13_q, w13_scales, w2_q, w2_scales, group_size, ops)
+    y_back = y_arrived.new_empty((rt.row_token.numel(), H))
+    dist.all_to_all_single(y_back, y_arrived, send_rows, recv_rows, group=ep_group)
+    out = ops.combine(y_back, rt.inv, rt.w, x.dtype).reshape(shape)
+    if stats is not None:
+        stats["send_rows"] = send_rows
+        stats["recv_rows"] = recv_rows
+        stats["local_experts_hit"] = int((both[E:].view(world, -1).sum(0) > 0).sum())
+    if return_routing:
+        return out, rt.idx, rt.w
+    return out
+
+
+def moe_layer_ep_emulated(xs, router_weight, shards, top_k: int, renormalize: bool = True,
+                          group_size: int = 64, ops=None):
+    """Expert-parallel layer for P ranks emulated in one process (one device):
+    ``xs[r]`` are rank r's tokens and ``shards[r]`` its ``(w13_q, w13_scales,
+    w2_q, w2_scales)``. The all-to-alls become concatenations, so the steps
+    and data movement of :func:`moe_layer_ep` can be checked on one GPU.
+    Returns each rank's output."""
+    ops = _CUDA_OPS if ops is None else ops
+    world = len(xs)
+    E = router_weight.shape[0]
+    per = E // world
+    rts = [route_local(x, router_weight, top_k, renormalize, ops) for x in xs]
+    counts = [rt.counts.cpu() for rt in rts]
+    send_rows = [rows_per_rank(c, world) for c in counts]              # [src][dst]
+    packed = [ops.gather(x, rt.row_token) for x, rt in zip(xs, rts)]
+    starts = [[sum(send_rows[s][:d]) for d in range(world)] for s in range(world)]
+    y_arrived = []
+    for d in range(world):
+        parts = [packed[s][starts[s][d]:starts[s][d] + send_rows[s][d]] for s in range(world)]
+        recv_x = torch.cat(parts)
+        recv_counts = torch.cat([rts[s].counts[d * per:(d + 1) * per] for s in range(world)])
+        y_arrived.append(expert_compute(recv_x, recv_counts, world, *shards[d], group_size, ops))
+    outs = []
+    for s in range(world):
+        parts = []
+        for d in range(world):
+            first = sum(send_rows[q][d] for q in range(s))
+            parts.append(y_arrived[d][first:first + send_rows[s][d]])
+        y_back = torch.cat(parts).contiguous()
+        outs.append(ops.combine(y_back, rts[s].inv, rts[s].w, xs[s].dtype))
+    return outs

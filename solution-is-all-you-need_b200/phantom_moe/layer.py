@@ -226,6 +226,24 @@ def combine(y: torch.Tensor, inv: torch.Tensor, topk_w: torch.Tensor, out_dtype=
     return out
 
 
+def gather_rows(src: torch.Tensor, index: torch.Tensor, out: torch.Tensor | None = None):
+    """``out[i] = src[index[i]]`` for a 2-D CUDA tensor (rows of a multiple of
+    16 bytes); rows whose index is out of range come back zero."""
+    _need_cuda("src", src)
+    _need_cuda("index", index)
+    _need_dtype("index", index, (torch.int32,))
+    if src.dim() != 2 or not src.is_contiguous():
+        raise ValueError("src must be a contiguous 2-D tensor")
+    n = index.numel()
+    if out is None:
+        out = torch.empty(n, src.shape[1], dtype=src.dtype, device=src.device)
+    elif out.shape != (n, src.shape[1]) or out.dtype != src.dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous [len(index), src.shape[1]] tensor of src's dtype")
+    _lib.call("phmoe_gather_rows", _ptr(src), src.shape[0], _ptr(index), n,
+              src.shape[1] * src.element_size(), _ptr(out), _stream())
+    return out
+
+
 def quantize_int4(w: torch.Tensor, group_size: int = 64):
     """GPU symmetric int4 group quantiser: ``w[..., K]`` (fp32/bf16, CUDA) ->
     ``(packed uint8[..., K/2], scales fp16[..., K/G])``."""
@@ -280,7 +298,7 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
     """
     if ep_group is not None:
         from . import ep as _ep
-        if _ep.group_size(ep_group) > 1:
+        if _ep.ep_world_size(ep_group) > 1:
             return _ep.moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scales,
                                     top_k, renormalize, group_size, ep_group, return_routing=return_routing)
     _need_cuda("hidden_states", hidden_states)
