@@ -119,6 +119,27 @@ int phmoe_expert_ffn_decode(const void* x, int x_dtype, const int32_t* row_token
                             int group_size, float* h, float* y, void* stream);
 
 /*
+ * Grouped SwiGLU expert FFN, prefill form: the dispatched rows are gathered
+ * into expert order, then two persistent grouped GEMMs run on the tcgen05
+ * tensor cores (TMA-fed, accumulators in tensor memory) with fp16 operands:
+ * the bf16 rows convert to fp16 exactly, the int4 weights are dequantised per
+ * tile in shared memory to fp16_rn((nibble - 8) * scale) (the semantics of
+ * gguf_loader.py:362-381 with 11 significant bits), and the SwiGLU output h
+ * is rounded to fp16 between the two GEMMs. Values beyond the fp16 range
+ * are clamped and reported by phmoe_device_error (bit 1). Replaces the same
+ * loop as phmoe_expert_ffn_decode, for batches where every expert sees many
+ * rows. Same arguments; x must be bf16; h is scratch of T*k*I*4 bytes (the
+ * fp16 h uses half); y doubles as the gathered rows until the down GEMM.
+ * Limits: G in {32, 64}; H % 256 == 0; I % 128 == 0; E such that the tile
+ * table fits in shared memory (E <= 1024).
+ */
+int phmoe_expert_ffn_prefill(const void* x, int x_dtype, const int32_t* row_token,
+                             const int32_t* expert_offsets, const int32_t* active,
+                             const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
+                             const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
+                             int group_size, float* h, float* y, void* stream);
+
+/*
  * Combine: out[t] = sum_j topk_w[t,j] * y[inv[t,j]] in slot order j = 0..k-1
  * (deterministic; replaces the weight multiply + index_add_,
  * modeling_qwen3_moe.py:248-249). out is [T, H] in out_dtype.
@@ -206,10 +227,11 @@ int phmoe_quantize_int4(const void* w, int w_dtype, long long rows, int K, int g
 #define PHMOE_NUM_STAGES 5
 
 /*
- * Device-side error word of the current device: 0 when every pipeline wait
- * of the FFN kernels completed; 1 when one timed out (its CTA abandoned its
- * work after a bounded wait instead of hanging). Synchronous; reset != 0
- * clears it. Not part of the hot path.
+ * Device-side error bits of the current device: 0 when all is well; bit 0
+ * (1) when a pipeline wait of an FFN kernel timed out (its CTA abandoned its
+ * work after a bounded wait instead of hanging); bit 1 (2) when the prefill
+ * path clamped an activation or SwiGLU value to the fp16 range (+-65504).
+ * Synchronous; reset != 0 clears it. Not part of the hot path.
  */
 int phmoe_device_error(int reset);
 unsigned long long phmoe_kernel_launch_count(void);

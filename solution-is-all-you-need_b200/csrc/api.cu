@@ -99,6 +99,36 @@ int check_ffn_dims(int H, int I, int G) {
   return PHMOE_OK;
 }
 
+// The prefill GEMMs take bf16 activations, tile output columns by 256 (down)
+// and 128 (gate/up, with the 128 matching up rows) and K by 64.
+int check_prefill_dims(int x_dtype, int H, int I, int G, int E) {
+  if (x_dtype != PHMOE_DTYPE_BF16) return fail(PHMOE_ERR_UNSUPPORTED, "the prefill path takes bf16 activations");
+  if (G != 32 && G != 64) return fail(PHMOE_ERR_UNSUPPORTED, "group_size must be 32 or 64 (got %d)", G);
+  if (H <= 0 || H % 256) return fail(PHMOE_ERR_UNSUPPORTED, "prefill needs H %% 256 == 0 (got %d)", H);
+  if (I <= 0 || I % 128) return fail(PHMOE_ERR_UNSUPPORTED, "prefill needs I %% 128 == 0 (got %d)", I);
+  if (!prefill_supported(H, I, G, E)) return fail(PHMOE_ERR_UNSUPPORTED, "prefill not built for E=%d", E);
+  return PHMOE_OK;
+}
+
+// Average rows per expert from which PHMOE_PATH_AUTO takes the prefill GEMMs.
+constexpr int kPrefillRowsPerExpert = 64;
+
+// Resolves PHMOE_PATH_AUTO and checks the chosen path's limits.
+int resolve_path(int path, int x_dtype, int T, int top_k, int H, int I, int G, int E, int* chosen) {
+  if (path < PHMOE_PATH_AUTO || path > PHMOE_PATH_PREFILL)
+    return fail(PHMOE_ERR_INVALID_ARG, "bad path code %d", path);
+  if (path == PHMOE_PATH_AUTO) {
+    const bool g_ok = G == 32 || G == 64;
+    const bool prefill_ok = g_ok && x_dtype == PHMOE_DTYPE_BF16 && H % 256 == 0 && I % 128 == 0 &&
+                            prefill_supported(H, I, G, E);
+    const bool decode_ok = g_ok && H % 256 == 0 && I % 16 == 0 && I % (2 * G) == 0;
+    const bool big = (long long)T * top_k >= (long long)kPrefillRowsPerExpert * E;
+    path = (prefill_ok && (big || !decode_ok)) ? PHMOE_PATH_PREFILL : PHMOE_PATH_DECODE;
+  }
+  *chosen = path;
+  return path == PHMOE_PATH_PREFILL ? check_prefill_dims(x_dtype, H, I, G, E) : check_ffn_dims(H, I, G);
+}
+
 }  // namespace
 
 namespace {
@@ -221,6 +251,26 @@ int phmoe_expert_ffn_decode(const void* x, int x_dtype, const int32_t* row_token
   return check_launch("phmoe_expert_ffn_decode");
 }
 
+int phmoe_expert_ffn_prefill(const void* x, int x_dtype, const int32_t* row_token,
+                             const int32_t* expert_offsets, const int32_t* active,
+                             const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
+                             const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
+                             int group_size, float* h, float* y, void* stream) {
+  g_last_error.clear();
+  if (int s = check_router_dims(T, H, E, top_k)) return s;
+  if (int s = check_prefill_dims(x_dtype, H, I, group_size, E)) return s;
+  if (T == 0) return PHMOE_OK;
+  if (!x || !row_token || !expert_offsets || !active || !w13_q || !w13_s || !w2_q || !w2_s || !h || !y)
+    return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned(x, 16) || !aligned(w13_q, 16) || !aligned(w2_q, 16) || !aligned(h, 16) || !aligned(y, 16))
+    return fail(PHMOE_ERR_ALIGNMENT, "x, weights, h and y must be 16-byte aligned");
+  if (!aligned(w13_s, 2) || !aligned(w2_s, 2)) return fail(PHMOE_ERR_ALIGNMENT, "scales must be 2-byte aligned");
+  const int s = launch_ffn_prefill(x, row_token, expert_offsets, active, w13_q, w13_s, w2_q, w2_s, T, H, E,
+                                   top_k, I, group_size, h, y, static_cast<cudaStream_t>(stream));
+  if (s) return fail(s, "prefill launch failed (tensor map or kernel attribute)");
+  return check_launch("phmoe_expert_ffn_prefill");
+}
+
 int phmoe_combine(const float* y, const int32_t* inv, const float* topk_w, int T, int top_k,
                   int H, void* out, int out_dtype, void* stream) {
   g_last_error.clear();
@@ -254,13 +304,10 @@ int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtyp
                     float* topk_w_out, void* workspace, size_t workspace_bytes, void* stream) {
   g_last_error.clear();
   if (int s = check_router_dims(T, H, E, top_k)) return s;
-  if (int s = check_ffn_dims(H, I, group_size)) return s;
   if (!dtype_ok(x_dtype) || !dtype_ok(w_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  int chosen = PHMOE_PATH_DECODE;
+  if (int s = resolve_path(path, x_dtype, T, top_k, H, I, group_size, E, &chosen)) return s;
   if (int s = check_router_smem(H, x_dtype)) return s;
-  if (path < PHMOE_PATH_AUTO || path > PHMOE_PATH_PREFILL)
-    return fail(PHMOE_ERR_INVALID_ARG, "bad path code %d", path);
-  if (path == PHMOE_PATH_PREFILL)
-    return fail(PHMOE_ERR_UNSUPPORTED, "prefill path is not built in this library");
   if (T == 0) return PHMOE_OK;
   if (!x || !router_w || !w13_q || !w13_s || !w2_q || !w2_s || !out || !workspace)
     return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
@@ -294,9 +341,14 @@ int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtyp
   launch_dispatch(idx, T, top_k, E, offsets, row_token, inv, active, ws + L.disp, st);
   if (int s = check_launch("dispatch")) return s;
   mark(2);
-  if (int s = launch_ffn_decode(x, x_dtype, row_token, offsets, active, w13_q, w13_s, w2_q, w2_s, T, H,
-                                E, top_k, I, group_size, h, y, st, prof ? prof_event(pc, 3) : nullptr))
+  if (chosen == PHMOE_PATH_PREFILL) {
+    if (int s = launch_ffn_prefill(x, row_token, offsets, active, w13_q, w13_s, w2_q, w2_s, T, H, E, top_k, I,
+                                   group_size, h, y, st, prof ? prof_event(pc, 3) : nullptr))
+      return fail(s, "prefill launch failed (tensor map or kernel attribute)");
+  } else if (int s = launch_ffn_decode(x, x_dtype, row_token, offsets, active, w13_q, w13_s, w2_q, w2_s, T, H,
+                                       E, top_k, I, group_size, h, y, st, prof ? prof_event(pc, 3) : nullptr)) {
     return fail(s, "no decode kernel for group_size=%d", group_size);
+  }
   if (int s = check_launch("expert_ffn")) return s;
   mark(4);
   launch_combine(y, inv, wts, T, top_k, H, out, x_dtype, st);
@@ -319,7 +371,12 @@ int phmoe_quantize_int4(const void* w, int w_dtype, long long rows, int K, int g
 
 unsigned long long phmoe_kernel_launch_count(void) { return g_launches.load(); }
 
-int phmoe_device_error(int reset) { return ffn_device_error(reset != 0); }
+int phmoe_device_error(int reset) {
+  const int a = ffn_device_error(reset != 0);
+  const int b = prefill_device_error(reset != 0);
+  if (a < 0 || b < 0) return -1;
+  return a | b;
+}
 
 int phmoe_profile_begin(int max_calls) {
   g_last_error.clear();

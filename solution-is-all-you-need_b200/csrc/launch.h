@@ -24,6 +24,15 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       int H, int E, int top_k, int I, int G, float* h, float* y,
                       cudaStream_t st, cudaEvent_t mid_event = nullptr);
 
+// Prefill form (tcgen05 grouped GEMMs): bf16 x only; h is R*I*4 bytes of
+// scratch and y doubles as the gathered activations until the down GEMM.
+bool prefill_supported(int H, int I, int G, int E);
+int launch_ffn_prefill(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
+                       const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s,
+                       int T, int H, int E, int top_k, int I, int G, float* h, float* y, cudaStream_t st,
+                       cudaEvent_t mid_event = nullptr);
+int prefill_device_error(bool reset);
+
 int launch_combine(const float* y, const int32_t* inv, const float* topk_w, int T, int top_k,
                    int H, void* out, int out_dtype, cudaStream_t st);
 

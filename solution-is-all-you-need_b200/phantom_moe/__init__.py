@@ -15,6 +15,7 @@ from .layer import (
     combine,
     dispatch,
     expert_ffn_decode,
+    expert_ffn_prefill,
     gather_rows,
     moe_layer,
     pack_experts,
@@ -30,6 +31,7 @@ __all__ = [
     "combine",
     "dispatch",
     "expert_ffn_decode",
+    "expert_ffn_prefill",
     "gather_rows",
     "load_library",
     "moe_layer",

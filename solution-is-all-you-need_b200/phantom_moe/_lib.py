@@ -43,6 +43,8 @@ SIGNATURES = {
     "phmoe_dispatch": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _SZ, _P]),
     "phmoe_expert_ffn_decode": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _P,
                                      _I, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "phmoe_expert_ffn_prefill": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _P,
+                                      _I, _I, _I, _I, _I, _I, _P, _P, _P]),
     "phmoe_combine": (_I, [_P, _P, _P, _I, _I, _I, _P, _I, _P]),
     "phmoe_gather_rows": (_I, [_P, _LL, _P, _I, _LL, _P, _P]),
     "phmoe_moe_layer": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,

@@ -215,6 +215,26 @@ def expert_ffn_decode(x: torch.Tensor, row_token, offsets, active, w13_q, w13_sc
     return y
 
 
+def expert_ffn_prefill(x: torch.Tensor, row_token, offsets, active, w13_q, w13_scales, w2_q,
+                       w2_scales, top_k: int, group_size: int = 64):
+    """Grouped SwiGLU FFN as two tcgen05 grouped GEMMs (large batches; bf16
+    ``x``). Same inputs and result layout as :func:`expert_ffn_decode`."""
+    _need_cuda("x", x)
+    _need_dtype("x", x, (torch.bfloat16,))
+    T, H = x.shape
+    E, I = check_expert_weights(w13_q, w13_scales, w2_q, w2_scales, H, group_size)
+    R = row_token.numel()
+    if R != T * top_k:
+        raise ValueError(f"row_token must have T*top_k = {T * top_k} rows (got {R})")
+    dev = x.device
+    h = torch.empty(max(R * I, 1), dtype=torch.float32, device=dev)
+    y = torch.empty(R, H, dtype=torch.float32, device=dev)
+    _lib.call("phmoe_expert_ffn_prefill", _ptr(x), _DT[x.dtype], _ptr(row_token), _ptr(offsets),
+              _ptr(active), _ptr(w13_q), _ptr(w13_scales), _ptr(w2_q), _ptr(w2_scales), T, H, E,
+              top_k, I, group_size, _ptr(h), _ptr(y), _stream())
+    return y
+
+
 def combine(y: torch.Tensor, inv: torch.Tensor, topk_w: torch.Tensor, out_dtype=torch.bfloat16):
     """out[t] = sum_j w[t,j] * y[inv[t,j]] (modeling_qwen3_moe.py:248-249)."""
     _need_cuda("y", y)

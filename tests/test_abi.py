@@ -114,3 +114,14 @@ def test_python_layer_rejects_cpu_tensors():
         phantom_moe.moe_layer(x, x[:8], x, x, x, x, 2)
     with pytest.raises(ValueError, match="CUDA"):
         phantom_moe.router(x, x[:8], 2)
+
+
+def test_prefill_rejects_fp32_and_bad_dims(lib):
+    args = [None, None, None, None, None, None, None, 4, 4096, 8, 2]
+    assert lib.phmoe_expert_ffn_prefill(None, 0, *args, 14336, 64, None, None, None) == _lib.PHMOE_ERR_UNSUPPORTED
+    assert lib.phmoe_expert_ffn_prefill(None, 1, *args, 14272, 64, None, None, None) == _lib.PHMOE_ERR_UNSUPPORTED
+    assert lib.phmoe_expert_ffn_prefill(None, 1, *args, 14336, 16, None, None, None) == _lib.PHMOE_ERR_UNSUPPORTED
+    # the layer with an explicit prefill path and fp32 activations
+    rc = lib.phmoe_moe_layer(None, 0, None, 0, None, None, None, None, 4, 4096, 8, 2, 14336, 64, 1, 2,
+                             None, None, None, None, 0, None)
+    assert rc == _lib.PHMOE_ERR_UNSUPPORTED

@@ -165,3 +165,14 @@ def test_dispatch_oracle_invariants():
         for j in range(k):
             r = inv[t, j]
             assert row_token[r] == t and row_slot[r] == j
+
+
+def test_torch_reference_nibble_order():
+    """The GPU-side fp32 reference helpers read the same packed layout."""
+    from torch_ref import dequant_torch
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal((6, 256)) * 0.02).astype(np.float32)
+    for G in (32, 64):
+        p, s = O.quantize_int4(w, G)
+        got = dequant_torch(torch.from_numpy(p), torch.from_numpy(s), G).numpy()
+        assert np.array_equal(got, O.dequantize_int4(p, s, G))
