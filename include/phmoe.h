@@ -69,6 +69,14 @@ const char* phmoe_last_error(void);
 size_t phmoe_workspace_size(int T, int H, int E, int top_k, int I, int path);
 
 /*
+ * The FFN path phmoe_moe_layer takes for these arguments: PHMOE_PATH_DECODE
+ * or PHMOE_PATH_PREFILL (PHMOE_PATH_AUTO picks the prefill GEMMs for bf16
+ * activations from 64 rows per expert on average, where the shapes allow),
+ * or a negative status when the requested path cannot run them. Host-only.
+ */
+int phmoe_select_path(int path, int x_dtype, int T, int top_k, int H, int E, int I, int group_size);
+
+/*
  * Router: logits = x . Wr^T (fp32, fixed reduction order), fp32 softmax,
  * top-k with ties to the lower expert index, optional renormalisation.
  * Replaces Qwen3MoeTopKRouter.forward (modeling_qwen3_moe.py:263-272) and

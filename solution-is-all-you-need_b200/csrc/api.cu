@@ -185,6 +185,15 @@ const char* phmoe_status_string(int status) {
 
 const char* phmoe_last_error(void) { return g_last_error.c_str(); }
 
+int phmoe_select_path(int path, int x_dtype, int T, int top_k, int H, int E, int I, int group_size) {
+  g_last_error.clear();
+  if (int s = check_router_dims(T, H, E, top_k)) return s;
+  if (!dtype_ok(x_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  int chosen = PHMOE_PATH_DECODE;
+  if (int s = resolve_path(path, x_dtype, T, top_k, H, I, group_size, E, &chosen)) return s;
+  return chosen;
+}
+
 size_t phmoe_workspace_size(int T, int H, int E, int top_k, int I, int path) {
   if (T < 0 || H <= 0 || E < 1 || top_k < 1 || I <= 0) return 0;
   if (path < PHMOE_PATH_AUTO || path > PHMOE_PATH_PREFILL) return 0;

@@ -22,6 +22,7 @@ namespace {
 
 constexpr int kRouterWarps = 8;     // experts per CTA (one warp each)
 constexpr int kRouterTokens = 8;    // tokens per CTA
+constexpr int kBlockRouterMinTokens = 256;  // from here the register-blocked kernel is used
 
 template <typename T>
 struct Vec8;
@@ -139,6 +140,75 @@ router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T,
     for (int t = 0; t < TT; ++t)
       if (t < nt) logits[(size_t)(t0 + t) * E + e] = acc[t];
   }
+}
+
+// Large-batch form for bf16 x and router weight: each warp computes an
+// 8-token x 8-expert block of logits in registers, reading x and the weight
+// rows straight from global memory (16-byte loads, coalesced across the
+// warp). Lane L still owns exactly the elements h with (h/8) % 32 == L, adds
+// its exact bf16 x bf16 products in increasing h, and the 32 lane sums are
+// combined by the same xor butterfly, so every logit is bit-identical to
+// router_logits_kernel's. CTA: 4 token blocks x 2 expert blocks of warps.
+constexpr int kBlkT = 8, kBlkE = 8, kBlkWarpsT = 4, kBlkWarpsE = 2;
+
+__global__ void __launch_bounds__(kBlkWarpsT * kBlkWarpsE * 32)
+router_logits_block_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wr, int T,
+                           int H, int E, float* __restrict__ logits) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = (blockIdx.y * kBlkWarpsT + warp % kBlkWarpsT) * kBlkT;
+  const int e0 = (blockIdx.x * kBlkWarpsE + warp / kBlkWarpsT) * kBlkE;
+  if (t0 >= T || e0 >= E) return;
+  float acc[kBlkT][kBlkE];
+#pragma unroll
+  for (int t = 0; t < kBlkT; ++t)
+#pragma unroll
+    for (int e = 0; e < kBlkE; ++e) acc[t][e] = 0.f;
+  const int nchunk = (H + 255) / 256;
+  for (int c = 0; c < nchunk; ++c) {
+    const int h0 = c * 256 + lane * 8;
+    const bool hok = h0 < H;
+    uint4 xv[kBlkT], wv[kBlkE];
+#pragma unroll
+    for (int t = 0; t < kBlkT; ++t)
+      xv[t] = (hok && t0 + t < T) ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)(t0 + t) * H + h0))
+                                  : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int e = 0; e < kBlkE; ++e)
+      wv[e] = (hok && e0 + e < E) ? __ldg(reinterpret_cast<const uint4*>(wr + (size_t)(e0 + e) * H + h0))
+                                  : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {  // element h0 + v, in increasing h
+      float xf[kBlkT], wf[kBlkE];
+#pragma unroll
+      for (int t = 0; t < kBlkT; ++t) {
+        const uint32_t u = (v < 2) ? xv[t].x : (v < 4) ? xv[t].y : (v < 6) ? xv[t].z : xv[t].w;
+        xf[t] = (v & 1) ? bf16_hi_to_f32(u) : bf16_lo_to_f32(u);
+      }
+#pragma unroll
+      for (int e = 0; e < kBlkE; ++e) {
+        const uint32_t u = (v < 2) ? wv[e].x : (v < 4) ? wv[e].y : (v < 6) ? wv[e].z : wv[e].w;
+        wf[e] = (v & 1) ? bf16_hi_to_f32(u) : bf16_lo_to_f32(u);
+      }
+#pragma unroll
+      for (int t = 0; t < kBlkT; ++t)
+#pragma unroll
+        for (int e = 0; e < kBlkE; ++e) acc[t][e] = __fmaf_rn(xf[t], wf[e], acc[t][e]);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kBlkT; ++t)
+#pragma unroll
+    for (int e = 0; e < kBlkE; ++e)
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1)
+        acc[t][e] = __fadd_rn(acc[t][e], __shfl_xor_sync(0xffffffffu, acc[t][e], off));
+  // lane (t * 8 + e) % 32 writes two of the 64 results
+#pragma unroll
+  for (int t = 0; t < kBlkT; ++t)
+#pragma unroll
+    for (int e = 0; e < kBlkE; ++e)
+      if (lane == ((t * kBlkE + e) & 31) && t0 + t < T && e0 + e < E)
+        logits[(size_t)(t0 + t) * E + e0 + e] = acc[t][e];
 }
 
 // exp(x) for x <= 0: Cody-Waite reduction with a two-part ln2, then the
@@ -262,7 +332,11 @@ int launch_router(const void* x, int x_dtype, const void* wr, int w_dtype, int T
                   int top_k, int renormalize, float* logits, float* probs, int32_t* topk_idx,
                   float* topk_w, cudaStream_t st) {
   if (T == 0) return PHMOE_OK;
-  if (x_dtype == PHMOE_DTYPE_BF16 && w_dtype == PHMOE_DTYPE_BF16)
+  if (x_dtype == PHMOE_DTYPE_BF16 && w_dtype == PHMOE_DTYPE_BF16 && T >= kBlockRouterMinTokens) {
+    dim3 grid((E + kBlkE * kBlkWarpsE - 1) / (kBlkE * kBlkWarpsE), (T + kBlkT * kBlkWarpsT - 1) / (kBlkT * kBlkWarpsT));
+    router_logits_block_kernel<<<grid, kBlkWarpsT * kBlkWarpsE * 32, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(wr), T, H, E, logits);
+  } else if (x_dtype == PHMOE_DTYPE_BF16 && w_dtype == PHMOE_DTYPE_BF16)
     launch_logits<__nv_bfloat16, __nv_bfloat16>(x, wr, T, H, E, logits, st);
   else if (x_dtype == PHMOE_DTYPE_BF16 && w_dtype == PHMOE_DTYPE_F32)
     launch_logits<__nv_bfloat16, float>(x, wr, T, H, E, logits, st);

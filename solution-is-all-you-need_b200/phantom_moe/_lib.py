@@ -38,6 +38,7 @@ SIGNATURES = {
     "phmoe_status_string": (ctypes.c_char_p, [_I]),
     "phmoe_last_error": (ctypes.c_char_p, []),
     "phmoe_workspace_size": (_SZ, [_I, _I, _I, _I, _I, _I]),
+    "phmoe_select_path": (_I, [_I, _I, _I, _I, _I, _I, _I, _I]),
     "phmoe_router": (_I, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
     "phmoe_dispatch_scratch_size": (_SZ, [_I, _I, _I]),
     "phmoe_dispatch": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _SZ, _P]),

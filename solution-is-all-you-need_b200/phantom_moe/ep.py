@@ -72,9 +72,14 @@ class CudaOps:
     def gather(self, src, index):
         return _layer.gather_rows(src, index)
 
-    def ffn(self, x, row_token, offsets, active, w13_q, w13_scales, w2_q, w2_scales, group_size):
-        return _layer.expert_ffn_decode(x, row_token, offsets, active, w13_q, w13_scales, w2_q, w2_scales,
-                                        top_k=1, group_size=group_size)
+    def ffn(self, x, row_token, offsets, active, w13_q, w13_scales, w2_q, w2_scales, group_size, path="auto"):
+        """Grouped FFN over this rank's arrived rows; ``path`` as in
+        :func:`phantom_moe.moe_layer`, 'auto' deciding on the local batch."""
+        E, I = w13_q.shape[0], w13_q.shape[1] // 2
+        chosen = _layer.select_path(path, x.dtype, x.shape[0], 1, x.shape[1], E, I, group_size)
+        ffn = _layer.expert_ffn_prefill if chosen == "prefill" else _layer.expert_ffn_decode
+        return ffn(x, row_token, offsets, active, w13_q, w13_scales, w2_q, w2_scales, top_k=1,
+                   group_size=group_size)
 
     def combine(self, y, inv, topk_w, out_dtype):
         return _layer.combine(y, inv, topk_w, out_dtype)
@@ -114,7 +119,7 @@ def arrived_expert_ids(recv_counts: torch.Tensor, world: int, total: int) -> tor
     return torch.repeat_interleave(ids, recv_counts.to(torch.int64), output_size=total).to(torch.int32)
 
 
-def expert_compute(recv_x, recv_counts, world, w13_q, w13_scales, w2_q, w2_scales, group_size, ops):
+def expert_compute(recv_x, recv_counts, world, w13_q, w13_scales, w2_q, w2_scales, group_size, ops, path="auto"):
     """Grouped FFN over rows that arrived from all ranks; fp32 rows back in
     arrival order."""
     total = recv_x.shape[0]
@@ -123,18 +128,19 @@ def expert_compute(recv_x, recv_counts, world, w13_q, w13_scales, w2_q, w2_scale
         return torch.empty(0, recv_x.shape[1], dtype=torch.float32, device=recv_x.device)
     eid = arrived_expert_ids(recv_counts, world, total)
     offsets, row_token, inv, active = ops.dispatch(eid.view(total, 1), per)
-    y = ops.ffn(recv_x, row_token, offsets, active, w13_q, w13_scales, w2_q, w2_scales, group_size)
+    y = ops.ffn(recv_x, row_token, offsets, active, w13_q, w13_scales, w2_q, w2_scales, group_size, path)
     return ops.gather(y, inv.view(-1))
 
 
 def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scales, top_k: int,
-                 renormalize: bool = True, group_size: int = 64, ep_group=None, *,
+                 renormalize: bool = True, group_size: int = 64, ep_group=None, *, path: str = "auto",
                  return_routing: bool = False, ops=None, stats: dict | None = None):
     """The MoE layer with this rank's expert shard (``w13_q`` etc. hold
     ``E/P`` experts, ``router_weight`` all ``E``). Same result as
     :func:`phantom_moe.moe_layer` on the full layer for this rank's tokens.
 
-    ``stats`` (a dict) receives ``send_rows`` / ``recv_rows``: the rows this
+    ``path`` selects the FFN kernels on each rank ('auto' decides on the
+    rank's arrived rows). ``stats`` (a dict) receives ``send_rows`` / ``recv_rows``: the rows this
     rank sent to / received from each rank (load-imbalance reporting), and
     ``local_experts_hit``: how many of this rank's experts received rows.
     """
@@ -157,7 +163,8 @@ def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scale
     send_x = ops.gather(x, rt.row_token)
     recv_x = x.new_empty((sum(recv_rows), H))
     dist.all_to_all_single(recv_x, send_x, recv_rows, send_rows, group=ep_group)
-    y_arrived = expert_compute(recv_x, recv_counts, world, w13_q, w13_scales, w2_q, w2_scales, group_size, ops)
+    y_arrived = expert_compute(recv_x, recv_counts, world, w13_q, w13_scales, w2_q, w2_scales, group_size, ops,
+                               path)
     y_back = y_arrived.new_empty((rt.row_token.numel(), H))
     dist.all_to_all_single(y_back, y_arrived, send_rows, recv_rows, group=ep_group)
     out = ops.combine(y_back, rt.inv, rt.w, x.dtype).reshape(shape)
@@ -171,7 +178,7 @@ def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scale
 
 
 def moe_layer_ep_emulated(xs, router_weight, shards, top_k: int, renormalize: bool = True,
-                          group_size: int = 64, ops=None):
+                          group_size: int = 64, ops=None, path: str = "auto"):
     """Expert-parallel layer for P ranks emulated in one process (one device):
     ``xs[r]`` are rank r's tokens and ``shards[r]`` its ``(w13_q, w13_scales,
     w2_q, w2_scales)``. The all-to-alls become concatenations, so the steps
@@ -191,7 +198,7 @@ def moe_layer_ep_emulated(xs, router_weight, shards, top_k: int, renormalize: bo
         parts = [packed[s][starts[s][d]:starts[s][d] + send_rows[s][d]] for s in range(world)]
         recv_x = torch.cat(parts)
         recv_counts = torch.cat([rts[s].counts[d * per:(d + 1) * per] for s in range(world)])
-        y_arrived.append(expert_compute(recv_x, recv_counts, world, *shards[d], group_size, ops))
+        y_arrived.append(expert_compute(recv_x, recv_counts, world, *shards[d], group_size, ops, path))
     outs = []
     for s in range(world):
         parts = []

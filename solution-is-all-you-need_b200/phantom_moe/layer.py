@@ -291,6 +291,19 @@ def pack_experts(gate_up_proj: torch.Tensor, down_proj: torch.Tensor, group_size
 # the layer
 # ---------------------------------------------------------------------------
 
+def select_path(path: str, dtype: torch.dtype, T: int, top_k: int, H: int, E: int, I: int,
+                group_size: int = 64) -> str:
+    """The FFN path ('decode' or 'prefill') the layer takes for these
+    arguments (``phmoe_select_path``); raises when ``path`` cannot run."""
+    if path not in _PATHS:
+        raise ValueError(f"path must be one of {list(_PATHS)}")
+    if dtype not in _DT:
+        raise ValueError(f"unsupported dtype {dtype}")
+    rc = _lib.load().phmoe_select_path(_PATHS[path], _DT[dtype], T, top_k, H, E, I, group_size)
+    _lib.check("phmoe_select_path", rc if rc < 0 else 0)
+    return "prefill" if rc == _lib.PATH_PREFILL else "decode"
+
+
 def workspace_bytes(T: int, H: int, E: int, top_k: int, I: int, path: str = "auto") -> int:
     """Scratch bytes ``moe_layer`` needs for T tokens (``phmoe_workspace_size``)."""
     n = _lib.load().phmoe_workspace_size(T, H, E, top_k, I, _PATHS[path])
@@ -320,7 +333,8 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
         from . import ep as _ep
         if _ep.ep_world_size(ep_group) > 1:
             return _ep.moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scales,
-                                    top_k, renormalize, group_size, ep_group, return_routing=return_routing)
+                                    top_k, renormalize, group_size, ep_group, path=path,
+                                    return_routing=return_routing)
     _need_cuda("hidden_states", hidden_states)
     _need_cuda("router_weight", router_weight)
     _need_dtype("hidden_states", hidden_states, _DT)

@@ -43,7 +43,7 @@ class OracleOps:
         out[ok] = src[index[ok].long()]
         return out
 
-    def ffn(self, x, row_token, offsets, active, w13_q, w13_scales, w2_q, w2_scales, group_size):
+    def ffn(self, x, row_token, offsets, active, w13_q, w13_scales, w2_q, w2_scales, group_size, path="auto"):
         xs = x.numpy()
         off = offsets.numpy()
         rt = row_token.numpy()

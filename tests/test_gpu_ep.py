@@ -81,10 +81,11 @@ def test_ep_emulated_zipf_skew(cuda_device):
     wr[:, 0] = prior
     x, wr = x.to(torch.bfloat16), wr.to(torch.bfloat16)
     xs = list(x.split(T // 4))
-    outs = ep.moe_layer_ep_emulated(xs, wr, _shards(packed, 4), K, True, G)
-    ref, idx, _ = pm.moe_layer(x, wr, *packed, K, return_routing=True)
-    torch.cuda.synchronize()
-    assert torch.equal(torch.cat(outs), ref)
+    for path in ("decode", "prefill"):  # each rank runs the same kernels as the single GPU
+        outs = ep.moe_layer_ep_emulated(xs, wr, _shards(packed, 4), K, True, G, path=path)
+        ref, idx, _ = pm.moe_layer(x, wr, *packed, K, path=path, return_routing=True)
+        torch.cuda.synchronize()
+        assert torch.equal(torch.cat(outs), ref), path
     load = torch.bincount(idx.view(-1).long(), minlength=E).float()
     assert load.max() / load.mean() > 5.0  # the skew is real
 
