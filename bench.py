@@ -319,12 +319,82 @@ def load_traffic(T):
     return None
 
 
+def run_prefill(args, device):
+    """Mixtral-8x7B-shaped layer (H 4096, 8 experts, top-2,
+    I 14336, int4 g64), bf16 prefill batch of 4096 tokens (seed 2), through
+    the tcgen05 prefill GEMMs. Timed with CUDA events over back-to-back layer
+    calls (3 ms each; the 750 MB of packed weights and 64 MB of activations
+    stream from HBM every step). Roofline: tensor, 2*3*H*I*k*T FLOPs per step."""
+    import phantom_moe as pm
+    from phantom_moe import _lib
+    import ctypes
+    Hm, Em, km, Im, Tm = 4096, 8, 2, 14336, args.prefill_tokens
+    g = torch.Generator(device=device).manual_seed(2)
+    x = torch.randn(Tm, Hm, device=device, generator=g).to(torch.bfloat16)
+    wr = (torch.randn(Em, Hm, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    w13 = torch.randn(Em, 2 * Im, Hm, device=device, generator=g) * 0.02
+    p13 = pm.quantize_int4(w13, G)
+    del w13
+    w2 = torch.randn(Em, Hm, Im, device=device, generator=g) * 0.02
+    p2 = pm.quantize_int4(w2, G)
+    del w2
+    torch.cuda.empty_cache()
+    wts = (p13[0], p13[1], p2[0], p2[1])
+    out = torch.empty_like(x)
+    wsp = torch.empty(pm.workspace_bytes(Tm, Hm, Em, km, Im, "prefill"), dtype=torch.uint8, device=device)
+    st = torch.cuda.current_stream(device)
+    for _ in range(max(3, args.warmup // 4)):
+        pm.moe_layer(x, wr, *wts, km, path="prefill", out=out, workspace=wsp)
+    steps = max(5, min(args.steps, 30))
+    n0 = pm.load_library().phmoe_kernel_launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.synchronize()
+    ev0.record(st)
+    for _ in range(steps):
+        pm.moe_layer(x, wr, *wts, km, path="prefill", out=out, workspace=wsp)
+    ev1.record(st)
+    ev1.synchronize()
+    ms = ev0.elapsed_time(ev1) / steps
+    launches = (pm.load_library().phmoe_kernel_launch_count() - n0) / steps
+    _lib.call("phmoe_profile_begin", steps)
+    torch.cuda._sleep(20_000_000)
+    for _ in range(steps):
+        pm.moe_layer(x, wr, *wts, km, path="prefill", out=out, workspace=wsp)
+    arr = (ctypes.c_float * _lib.NUM_STAGES)()
+    n = ctypes.c_int(0)
+    _lib.call("phmoe_profile_end", arr, _lib.NUM_STAGES, ctypes.byref(n))
+    stage = {name: arr[i] / max(n.value, 1) for i, name in enumerate(_lib.STAGE_NAMES)}
+    flops = 2.0 * 3 * Hm * Im * km * Tm
+    ffn_ms = stage["ffn_gateup"] + stage["ffn_down"]
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    burst = float(peaks.get("bf16_tflops", 1590.0))
+    sustained = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    layer_tf = flops / (ms / 1e3) / 1e12
+    ffn_tf = flops / (ffn_ms / 1e3) / 1e12
+    res = {"workload": f"mixtral-8x7b moe layer prefill T={Tm} (BASELINE config 3), 1 GPU",
+           "tokens_per_s": Tm / (ms / 1e3), "ms_per_step": ms, "steps": steps, "dtype": "fp16 MMA operands, fp32 accumulate",
+           "stage_us": {k: round(v * 1e3, 1) for k, v in stage.items()},
+           "roofline": {"kernel": "ffn (gate/up + down GEMMs)", "bound": "tensor", "achieved": ffn_tf,
+                        "peak": burst, "unit": "TFLOP/s", "frac": ffn_tf / burst,
+                        "frac_of_sustained": ffn_tf / sustained, "layer_tflops": layer_tf,
+                        "peak_kind": "measured" if peaks else "fallback"},
+           "gpu_launches_per_step": launches}
+    log(f"[bench] prefill config 3: {ms * 1e3:.0f} us/layer {Tm / ms / 1e3:.3f} Mtok/s layer {layer_tf:.0f} TF/s "
+        f"ffn {ffn_tf:.0f} TF/s ({ffn_tf / burst:.2f} of burst, {ffn_tf / sustained:.2f} of sustained)")
+    del x, wr, wts, p13, p2, out, wsp
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args):
     ws, rank, local = dist_info()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if ws > 1:
         return run_ep(args, ws, rank, device)
+    if args.prefill_only:
+        print(json.dumps({"prefill": run_prefill(args, device)}), flush=True)
+        return
     with ClockSampler(local) as clk:
         layers, results, hl = run_single_gpu(args, device)
         # sustained replay of the headline step while the sampler runs
@@ -341,11 +411,12 @@ def run_ours(args):
     peak, peak_kind = load_peaks()
     gateup_bytes = hl["gateup_bytes"]
     achieved = gateup_bytes / (res["stage_ms"]["ffn_gateup"] / 1e3) / 1e9
+    del layers, hl
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    prefill = run_prefill(args, device) if args.prefill else None
     cpu = None
     if not args.no_cpu_baseline:
-        del layers, hl
-        torch.cuda.synchronize()
-        torch.cuda.empty_cache()
         cpu = cpu_baseline(host_layer0, T, args.cpu_budget)
     line = {
         "metric": METRIC, "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1,
@@ -363,6 +434,7 @@ def run_ours(args):
                      "ffn_achieved": res["ffn_GBps"], "ffn_frac": res["ffn_GBps"] / peak},
         "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
         "gpu_launches": int(round(res["launches_per_step"] * args.steps)),
+        "prefill": prefill,
     }
     print(json.dumps(line), flush=True)
 
@@ -522,6 +594,11 @@ def main():
     ap.add_argument("--tokens", type=int, default=64, help="decode tokens per GPU (headline)")
     ap.add_argument("--layers", type=int, default=8, help="distinct layers cycled (L2 defeat)")
     ap.add_argument("--no-sweep", dest="sweep", action="store_false")
+    ap.add_argument("--no-prefill", dest="prefill", action="store_false",
+                    help="skip the config-3 (Mixtral prefill) measurement")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="run only the config-3 prefill measurement (profiling)")
+    ap.add_argument("--prefill-tokens", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
     ap.add_argument("--clock-soak", type=float, default=2.0, help="seconds of sustained replay for clocks")
