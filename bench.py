@@ -21,8 +21,9 @@ L2); no explicit flush is needed.
   PHANTOM runs) in fp32 on the host cores, same layer and batch.
 
 With N > 1 (torchrun), experts are sharded expert-parallel (128/N per
-rank), each rank routes its own ``--tokens`` tokens, and dispatch/combine
-are NCCL all-to-alls (weak scaling).
+rank), each rank routes its own ``--tokens`` tokens (weak scaling), and the
+rows and expert outputs move through peer memory over NVLink inside one
+library call per layer (``--ep-exchange nccl``: NCCL all-to-alls instead).
 
 ``--impl reference`` times the reference's CPU path alone (rank 0).
 """
@@ -461,10 +462,12 @@ def run_ep(args, ws, rank, device):
     xs = [torch.randn(T, H, device=device, generator=g).to(torch.bfloat16) for _ in range(L)]
     torch.cuda.synchronize()
 
+    exchange = ep.PeerExchange(None, T, K_TOP, H, E) if args.ep_exchange == "peer" else None
+
     def step(i, x=None, stats=None):
         l = i % L
         return ep.moe_layer_ep(xs[l] if x is None else x, layers[l][0], *_pk(layers[l][1]), K_TOP, True, G,
-                               None, stats=stats)
+                               None, stats=stats, exchange=None if stats is not None else exchange)
 
     # imbalance and local experts hit, per layer (outside the timed region)
     hit, recv = [], []
@@ -495,7 +498,14 @@ def run_ep(args, ws, rank, device):
     n0 = lib.phmoe_kernel_launch_count()
     with ClockSampler(torch.cuda.current_device()) as clk:
         ms = timed(step, args.steps, args.warmup)
-    launches = lib.phmoe_kernel_launch_count() - n0
+        launches = lib.phmoe_kernel_launch_count() - n0
+        # sustained steps while the sampler runs (same count on every rank)
+        n_soak = int(args.clock_soak / max(ms / 1e3, 1e-6))
+        n_soak = torch.tensor([n_soak], device=device)
+        dist.all_reduce(n_soak, op=dist.ReduceOp.MIN)
+        for i in range(int(n_soak.item())):
+            step(i)
+        torch.cuda.synchronize()
     clocks = clk.summary()
     # end to end: pinned host tokens in, output back to the host, every step
     gh = torch.Generator().manual_seed(2000 + T + 7919 * rank)
@@ -531,7 +541,9 @@ def run_ep(args, ws, rank, device):
                        "tokens_per_gpu": T, "global_batch": ws * T, "parallelism": f"ep{ws}",
                        "experts_per_gpu": E // ws,
                        "l2": f"inputs larger than L2: {L} layers' weights cycled per step",
-                       "exchange": "NCCL all_to_all_single: counts, bf16 rows out, fp32 rows back",
+                       "exchange": ("peer-memory stores over NVLink with epoch flags (phmoe_ep_layer)"
+                                    if exchange is not None else
+                                    "NCCL all_to_all_single: counts, bf16 rows out, fp32 rows back"),
                        "local_experts_hit_mean": g_hit, "recv_rows_max_over_ranks": max(recv_all),
                        "recv_rows_mean": recv_mean},
             "roofline": {"kernel": "layer (per GPU)", "bound": "hbm", "achieved": achieved, "peak": peak,
@@ -543,6 +555,8 @@ def run_ep(args, ws, rank, device):
             "clocks": clocks, "gpu_launches": int(launches * args.steps // (args.steps + args.warmup)),
         }
         print(json.dumps(line), flush=True)
+    if exchange is not None:
+        exchange.close()
     dist.barrier()
     dist.destroy_process_group()
 
@@ -599,6 +613,8 @@ def main():
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the config-3 prefill measurement (profiling)")
     ap.add_argument("--prefill-tokens", type=int, default=4096)
+    ap.add_argument("--ep-exchange", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: token exchange through peer memory (default) or NCCL all-to-all")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
     ap.add_argument("--clock-soak", type=float, default=2.0, help="seconds of sustained replay for clocks")

@@ -167,6 +167,48 @@ int phmoe_gather_rows(const void* src, long long src_rows, const int32_t* index,
                       long long row_bytes, void* dst, void* stream);
 
 /*
+ * Expert parallelism with the token exchange in peer memory (NVLink /
+ * NVSwitch). No counterpart in the reference (PHANTOM has no expert
+ * parallelism). E experts split evenly over `world` ranks (one process per
+ * GPU, all on one node): rank r holds experts [r*E/world, (r+1)*E/world).
+ *
+ * Set-up (once per group, outside any stream capture):
+ *   phmoe_ep_create   allocates this rank's exchange region (flags, counts,
+ *                     received rows, returned rows; sized for max_tokens
+ *                     tokens per rank) and writes its CUDA IPC handle
+ *                     (PHMOE_EP_HANDLE_BYTES) to ipc_handle_out;
+ *   the caller gathers every rank's handle, in rank order, and passes the
+ *   world * PHMOE_EP_HANDLE_BYTES bytes to phmoe_ep_connect on every rank;
+ *   phmoe_ep_destroy after all ranks have stopped calling the layer.
+ * Per layer, on every rank in the same order (the call takes an epoch from a
+ * host counter, so all ranks must make the same number of calls):
+ *   phmoe_ep_layer    router and dispatch over all E experts; the rows for
+ *                     each rank's experts are stored into that rank's region;
+ *                     grouped FFN over the rows that arrived (w13_q etc. are
+ *                     this rank's E/world experts); fp32 results stored back
+ *                     into each source's region; combine. Completion is
+ *                     signalled by epoch flags; a wait that exceeds 2 s sets
+ *                     phmoe_device_error bit 2 and the layer continues with
+ *                     the rows that did arrive instead of hanging.
+ *   T (0..max_tokens) may differ between ranks. `path` as for
+ *   phmoe_moe_layer, chosen for the T*k rows a rank expects over its E/world
+ *   experts. workspace >= phmoe_ep_workspace_size(ctx, I) bytes, 256-byte
+ *   aligned. The result equals phmoe_moe_layer on the full layer for this
+ *   rank's tokens when both take the same FFN path.
+ */
+#define PHMOE_EP_MAX_WORLD 8
+#define PHMOE_EP_HANDLE_BYTES 64
+int phmoe_ep_create(int rank, int world, int max_tokens, int top_k, int H, int E, int x_dtype, void** ctx,
+                    void* ipc_handle_out);
+int phmoe_ep_connect(void* ctx, const void* ipc_handles);
+int phmoe_ep_destroy(void* ctx);
+size_t phmoe_ep_workspace_size(const void* ctx, int I);
+int phmoe_ep_layer(void* ctx, const void* x, int x_dtype, const void* router_w, int w_dtype, const uint8_t* w13_q,
+                   const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T, int I, int group_size,
+                   int renormalize, int path, void* out, int32_t* topk_idx_out, float* topk_w_out, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/*
  * The whole layer (Qwen3MoeSparseMoeBlock.forward, modeling_qwen3_moe.py:281-286,
  * on [T, H] rows): router -> dispatch -> grouped FFN -> combine, all
  * stream-ordered, no host synchronisation, no allocation.
@@ -238,7 +280,8 @@ int phmoe_quantize_int4(const void* w, int w_dtype, long long rows, int K, int g
  * Device-side error bits of the current device: 0 when all is well; bit 0
  * (1) when a pipeline wait of an FFN kernel timed out (its CTA abandoned its
  * work after a bounded wait instead of hanging); bit 1 (2) when the prefill
- * path clamped an activation or SwiGLU value to the fp16 range (+-65504).
+ * path clamped an activation or SwiGLU value to the fp16 range (+-65504);
+ * bit 2 (4) when an expert-parallel peer flag did not arrive within 2 s.
  * Synchronous; reset != 0 clears it. Not part of the hot path.
  */
 int phmoe_device_error(int reset);

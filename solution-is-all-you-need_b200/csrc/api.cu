@@ -383,8 +383,78 @@ unsigned long long phmoe_kernel_launch_count(void) { return g_launches.load(); }
 int phmoe_device_error(int reset) {
   const int a = ffn_device_error(reset != 0);
   const int b = prefill_device_error(reset != 0);
-  if (a < 0 || b < 0) return -1;
-  return a | b;
+  const int c = ep_device_error(reset != 0);
+  if (a < 0 || b < 0 || c < 0) return -1;
+  return a | b | c;
+}
+
+// ---- expert parallelism in peer memory ----
+
+int phmoe_ep_create(int rank, int world, int max_tokens, int top_k, int H, int E, int x_dtype, void** ctx,
+                    void* ipc_handle_out) {
+  g_last_error.clear();
+  if (!ctx || !ipc_handle_out) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  *ctx = nullptr;
+  if (!dtype_ok(x_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  if (world < 1 || world > PHMOE_EP_MAX_WORLD || rank < 0 || rank >= world)
+    return fail(PHMOE_ERR_INVALID_ARG, "rank %d of world %d (world must be 1..%d)", rank, world, PHMOE_EP_MAX_WORLD);
+  if (E < 1 || E > 1024 || E % world) return fail(PHMOE_ERR_INVALID_ARG, "E=%d must split evenly over %d ranks", E, world);
+  if (max_tokens < 1 || top_k < 1 || top_k > E || top_k > 32 || H <= 0 || H % 8)
+    return fail(PHMOE_ERR_INVALID_ARG, "bad dims max_tokens=%d top_k=%d H=%d", max_tokens, top_k, H);
+  EpContext* c = nullptr;
+  const int s = ep_create(rank, world, max_tokens, top_k, H, E, x_dtype == PHMOE_DTYPE_F32 ? 4 : 2, &c,
+                          ipc_handle_out);
+  if (s) return fail(s, "could not allocate or export the exchange region (%s)", cudaGetErrorString(cudaGetLastError()));
+  *ctx = c;
+  return PHMOE_OK;
+}
+
+int phmoe_ep_connect(void* ctx, const void* ipc_handles) {
+  g_last_error.clear();
+  if (!ctx || !ipc_handles) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (int s = ep_connect(static_cast<EpContext*>(ctx), ipc_handles))
+    return fail(s, "could not open a peer's exchange region (%s)", cudaGetErrorString(cudaGetLastError()));
+  return PHMOE_OK;
+}
+
+int phmoe_ep_destroy(void* ctx) {
+  g_last_error.clear();
+  ep_destroy(static_cast<EpContext*>(ctx));
+  return PHMOE_OK;
+}
+
+size_t phmoe_ep_workspace_size(const void* ctx, int I) {
+  if (!ctx || I <= 0) return 0;
+  return ep_workspace_bytes(static_cast<const EpContext*>(ctx), I);
+}
+
+int phmoe_ep_layer(void* ctx, const void* x, int x_dtype, const void* router_w, int w_dtype, const uint8_t* w13_q,
+                   const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T, int I, int group_size,
+                   int renormalize, int path, void* out, int32_t* topk_idx_out, float* topk_w_out, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (!ctx) return fail(PHMOE_ERR_INVALID_ARG, "null context");
+  EpContext* c = static_cast<EpContext*>(ctx);
+  int rank, world, max_tokens, top_k, H, E;
+  if (!ep_info(c, &rank, &world, &max_tokens, &top_k, &H, &E))
+    return fail(PHMOE_ERR_INVALID_ARG, "context not connected (phmoe_ep_connect)");
+  if (T < 0 || T > max_tokens) return fail(PHMOE_ERR_INVALID_ARG, "T=%d outside [0, %d]", T, max_tokens);
+  if (!dtype_ok(x_dtype) || !dtype_ok(w_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  if (int s = check_router_smem(H, x_dtype)) return s;
+  // the path is chosen for the rows a rank expects (T*k over E/world experts)
+  int chosen = PHMOE_PATH_DECODE;
+  if (int s = resolve_path(path, x_dtype, T > 0 ? T : 1, top_k, H, I, group_size, E / world, &chosen)) return s;
+  if ((T > 0 && (!x || !router_w || !out)) || !w13_q || !w13_s || !w2_q || !w2_s || !workspace)
+    return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned(x, 16) || !aligned(router_w, 16) || !aligned(w13_q, 16) || !aligned(w2_q, 16) || !aligned(out, 16))
+    return fail(PHMOE_ERR_ALIGNMENT, "x, router_w, packed weights and out must be 16-byte aligned");
+  if (!aligned(workspace, kAlign)) return fail(PHMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  const size_t need = ep_workspace_bytes(c, I);
+  if (workspace_bytes < need) return fail(PHMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", need, workspace_bytes);
+  const int s = ep_layer(c, x, x_dtype, router_w, w_dtype, w13_q, w13_s, w2_q, w2_s, T, I, group_size, renormalize,
+                         chosen, out, topk_idx_out, topk_w_out, workspace, static_cast<cudaStream_t>(stream));
+  if (s) return fail(s, "expert FFN launch failed");
+  return check_launch("phmoe_ep_layer");
 }
 
 int phmoe_profile_begin(int max_calls) {

@@ -1,0 +1,408 @@
+// Expert-parallel MoE layer with the token exchange done in peer memory over
+// NVLink / NVSwitch: each rank writes the rows it routes to another rank's
+// experts straight into that rank's receive buffer, and the expert outputs
+// come back the same way. No host synchronisation and no collective library
+// on the data path; completion is signalled with per-source epoch flags
+// (system-scope release stores, acquire loads). PHANTOM has no expert
+// parallelism; the layer semantics are those of phmoe_moe_layer (transformers'
+// Qwen3MoeSparseMoeBlock.forward, modeling_qwen3_moe.py:281-286) with the
+// E experts split evenly over the ranks (rank r holds [r*E/P, (r+1)*E/P)).
+//
+// Per layer on rank `me` (one stream, in order):
+//   router + dispatch over all E experts (rows come out expert-major, hence
+//     destination-major);
+//   ep_send_kernel   - row r goes to rank d = owner of its expert, slot
+//     i = r - offsets[d*Epr] of d's receive block for `me`; the last CTA to
+//     finish (after a system fence by every CTA) stores `me`'s per-expert
+//     counts for d and then d's arrival flag for `me` = epoch;
+//   ep_prepare_kernel - waits (bounded) for every source's flag, then builds
+//     the local expert grouping of the arrived rows (per local expert: source
+//     by source, each source's rows in its own order) and, per local row, the
+//     source rank and its row in the source's dispatch order;
+//   grouped FFN (decode or prefill kernels) over the arrived rows;
+//   ep_return_kernel - each fp32 expert-output row goes back to its source's
+//     return buffer at that row; the last CTA raises the return flags;
+//   ep_wait_kernel   - waits (bounded) for every destination's return flag;
+//   combine over the returned rows in slot order.
+// Reusing the single receive/return buffers is safe without further
+// handshakes: a source writes epoch e+1 rows only after its combine of epoch
+// e, which waited for this rank's return of epoch e, which came after this
+// rank's FFN finished reading the epoch-e rows.
+//
+// Waits give up after kWaitNs (2 s) of %globaltimer time, set the device error word
+// (phmoe_device_error bit 2) and continue with empty data instead of hanging.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace phmoe {
+
+__device__ int g_ep_error;  // 0 = ok, 4 = a peer flag did not arrive in time
+
+namespace {
+
+constexpr int kMaxWorld = 8;
+constexpr int kCopyThreads = 256;
+constexpr unsigned long long kWaitNs = 2000000000ull;
+
+struct Peers {
+  char* base[kMaxWorld];  // every rank's region, as mapped in this process (own one included)
+};
+
+// Byte offsets inside a rank's region (identical on every rank).
+struct Region {
+  size_t flags_in, flags_back, counts_in, recv_x, y_back, done, total;
+};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+Region region_layout(int world, int cap, int epr, int H, int elt) {
+  Region L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) { const size_t o = off; off = align_up(off + bytes, 256); return o; };
+  L.flags_in = take(kMaxWorld * 4);
+  L.flags_back = take(kMaxWorld * 4);
+  L.counts_in = take((size_t)kMaxWorld * (epr + 1) * 4);  // per source: epr counts, then its base row
+  L.done = take(2 * 4);                                     // last-CTA counters (send, return)
+  L.recv_x = take((size_t)world * cap * H * elt);
+  L.y_back = take((size_t)cap * H * 4);
+  L.total = off;
+  return L;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait for *flag == epoch; false (and the error bit) on timeout.
+__device__ bool wait_flag(const uint32_t* flag, uint32_t epoch) {
+  if (ld_acquire_sys(flag) == epoch) return true;
+  const unsigned long long t0 = global_ns();
+  while (ld_acquire_sys(flag) != epoch) {
+    if (global_ns() - t0 > kWaitNs) {
+      atomicOr(&g_ep_error, 4);
+      return false;
+    }
+    __nanosleep(200);
+  }
+  return true;
+}
+
+__device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int chunks) {
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = __ldg(src + c);
+}
+
+// True for the one CTA that finishes last (every CTA fences its writes to
+// system scope first); that CTA resets the counter for the next layer.
+__device__ bool last_cta(int* counter) {
+  __shared__ bool last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    last = atomicAdd(counter, 1) == (int)(gridDim.x - 1);
+    if (last) *counter = 0;
+  }
+  __syncthreads();
+  if (last) __threadfence_system();
+  return last;
+}
+
+__global__ void __launch_bounds__(kCopyThreads)
+ep_send_kernel(const char* __restrict__ x, const int32_t* __restrict__ row_token, const int32_t* __restrict__ offsets,
+               int R, int T, int epr, int world, int me, int cap, int row_bytes, Peers peers, Region L, uint32_t epoch) {
+  const int chunks = row_bytes / 16;
+  const int nvalid = R > 0 ? __ldg(offsets + epr * world) : 0;
+  for (int r = blockIdx.x; r < nvalid; r += gridDim.x) {
+    int d = 0;
+    while (d + 1 < world && __ldg(offsets + (d + 1) * epr) <= r) ++d;
+    const int i = r - __ldg(offsets + d * epr);
+    const int t = __ldg(row_token + r);
+    if (i < cap && t >= 0 && t < T) {
+      uint4* dst = reinterpret_cast<uint4*>(peers.base[d] + L.recv_x + ((size_t)me * cap + i) * row_bytes);
+      copy_row(dst, reinterpret_cast<const uint4*>(x + (size_t)t * row_bytes), chunks);
+    }
+  }
+  int* done = reinterpret_cast<int*>(peers.base[me] + L.done);
+  if (!last_cta(done)) return;
+  // counts and base row for each destination, then its flag
+  for (int d = 0; d < world; ++d) {
+    int32_t* cnt = reinterpret_cast<int32_t*>(peers.base[d] + L.counts_in) + (size_t)me * (epr + 1);
+    for (int l = threadIdx.x; l <= epr; l += blockDim.x) {
+      int32_t v = 0;
+      if (R > 0) v = l < epr ? __ldg(offsets + d * epr + l + 1) - __ldg(offsets + d * epr + l) : __ldg(offsets + d * epr);
+      cnt[l] = v;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < world)
+    st_release_sys(reinterpret_cast<uint32_t*>(peers.base[threadIdx.x] + L.flags_in) + me, epoch);
+}
+
+constexpr int kPrepThreads = 1024;
+
+// One CTA. Local grouping of the arrived rows: for local expert l, the rows of
+// source 0, then source 1, ... each in the source's order. Outputs:
+// off[epr+1], active[epr+1], row_token (index into the receive buffer),
+// ret_src / ret_row (where each local row goes back).
+__global__ void __launch_bounds__(kPrepThreads)
+ep_prepare_kernel(const char* __restrict__ local, Region L, int world, int cap, int epr, uint32_t epoch,
+                  int32_t* __restrict__ off, int32_t* __restrict__ active, int32_t* __restrict__ row_token,
+                  int32_t* __restrict__ ret_src, int32_t* __restrict__ ret_row) {
+  __shared__ int s_ok[kMaxWorld];
+  extern __shared__ int sm[];
+  int* cnt = sm;                           // [world][epr]
+  int* base = cnt + world * epr;           // [world]
+  int* seg = base + world;                 // [world][epr] exclusive scan over l per source
+  int* loff = seg + world * epr;           // [epr + 1]
+  if (threadIdx.x < world)
+    s_ok[threadIdx.x] = wait_flag(reinterpret_cast<const uint32_t*>(local + L.flags_in) + threadIdx.x, epoch);
+  __syncthreads();
+  const int32_t* cin = reinterpret_cast<const int32_t*>(local + L.counts_in);
+  for (int q = threadIdx.x; q < world * (epr + 1); q += blockDim.x) {
+    const int s = q / (epr + 1), l = q % (epr + 1);
+    int v = s_ok[s] ? cin[(size_t)s * (epr + 1) + l] : 0;
+    if (l < epr) {
+      cnt[s * epr + l] = v < 0 ? 0 : (v > cap ? cap : v);
+    } else {
+      base[s] = v;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < world) {  // per-source scan over local experts
+    const int s = threadIdx.x;
+    int run = 0;
+    for (int l = 0; l < epr; ++l) {
+      seg[s * epr + l] = run;
+      run += cnt[s * epr + l];
+    }
+  }
+  if (threadIdx.x == 32) {  // scan over local experts of the per-expert totals, and the active list
+    int run = 0, na = 0;
+    for (int l = 0; l < epr; ++l) {
+      loff[l] = run;
+      int n = 0;
+      for (int s = 0; s < world; ++s) n += cnt[s * epr + l];
+      run += n;
+      if (n) active[1 + na++] = l;
+    }
+    loff[epr] = run;
+    active[0] = na;
+  }
+  __syncthreads();
+  for (int l = threadIdx.x; l <= epr; l += blockDim.x) off[l] = loff[l];
+  // rows: one warp per (expert, source) segment
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  for (int q = warp; q < epr * world; q += nwarps) {
+    const int l = q / world, s = q % world;
+    int p = loff[l];
+    for (int s2 = 0; s2 < s; ++s2) p += cnt[s2 * epr + l];
+    const int n = cnt[s * epr + l], st = seg[s * epr + l];
+    for (int j = lane; j < n; j += 32) {
+      row_token[p + j] = s * cap + st + j;
+      ret_src[p + j] = s;
+      ret_row[p + j] = base[s] + st + j;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kCopyThreads)
+ep_return_kernel(const float* __restrict__ y, const int32_t* __restrict__ off, int epr,
+                 const int32_t* __restrict__ ret_src, const int32_t* __restrict__ ret_row, int world, int me, int cap,
+                 int H, Peers peers, Region L, uint32_t epoch) {
+  const int nrows = __ldg(off + epr);
+  const int chunks = H * 4 / 16;
+  for (int r = blockIdx.x; r < nrows; r += gridDim.x) {
+    const int s = __ldg(ret_src + r), row = __ldg(ret_row + r);
+    if (s >= 0 && s < world && row >= 0 && row < cap) {
+      uint4* dst = reinterpret_cast<uint4*>(peers.base[s] + L.y_back + (size_t)row * H * 4);
+      copy_row(dst, reinterpret_cast<const uint4*>(y + (size_t)r * H), chunks);
+    }
+  }
+  int* done = reinterpret_cast<int*>(peers.base[me] + L.done) + 1;
+  if (!last_cta(done)) return;
+  if (threadIdx.x < world)
+    st_release_sys(reinterpret_cast<uint32_t*>(peers.base[threadIdx.x] + L.flags_back) + me, epoch);
+}
+
+__global__ void ep_wait_kernel(const char* __restrict__ local, Region L, int world, uint32_t epoch) {
+  if (threadIdx.x < world) wait_flag(reinterpret_cast<const uint32_t*>(local + L.flags_back) + threadIdx.x, epoch);
+}
+
+}  // namespace
+
+struct EpContext {
+  int rank = 0, world = 1, max_tokens = 0, top_k = 1, H = 0, E = 0, epr = 0, elt = 2, cap = 0, device = 0;
+  Region L{};
+  char* local = nullptr;
+  Peers peers{};
+  bool opened[kMaxWorld] = {};
+  bool connected = false;
+  uint32_t epoch = 0;
+};
+
+int ep_device_error(bool reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_ep_error, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_ep_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+int ep_create(int rank, int world, int max_tokens, int top_k, int H, int E, int x_elt, EpContext** out,
+              void* handle_out) {
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || E % world || max_tokens < 1 || top_k < 1 ||
+      H <= 0 || (H * x_elt) % 16)
+    return PHMOE_ERR_INVALID_ARG;
+  EpContext* c = new EpContext();
+  c->rank = rank;
+  c->world = world;
+  c->max_tokens = max_tokens;
+  c->top_k = top_k;
+  c->H = H;
+  c->E = E;
+  c->epr = E / world;
+  c->elt = x_elt;
+  c->cap = max_tokens * top_k;
+  c->L = region_layout(world, c->cap, c->epr, H, x_elt);
+  if (cudaGetDevice(&c->device) != cudaSuccess || cudaMalloc(&c->local, c->L.total) != cudaSuccess ||
+      cudaMemset(c->local, 0, c->L.total) != cudaSuccess) {
+    if (c->local) cudaFree(c->local);
+    delete c;
+    return PHMOE_ERR_CUDA;
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, c->local) != cudaSuccess) {
+    cudaFree(c->local);
+    delete c;
+    return PHMOE_ERR_CUDA;
+  }
+  memcpy(handle_out, &h, sizeof(h));
+  c->peers.base[rank] = c->local;
+  *out = c;
+  return PHMOE_OK;
+}
+
+int ep_connect(EpContext* c, const void* handles) {
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const char*>(handles) + (size_t)r * sizeof(h), sizeof(h));
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return PHMOE_ERR_CUDA;
+    c->peers.base[r] = static_cast<char*>(p);
+    c->opened[r] = true;
+  }
+  c->connected = true;
+  return PHMOE_OK;
+}
+
+void ep_destroy(EpContext* c) {
+  if (!c) return;
+  for (int r = 0; r < c->world; ++r)
+    if (c->opened[r]) cudaIpcCloseMemHandle(c->peers.base[r]);
+  if (c->local) cudaFree(c->local);
+  delete c;
+}
+
+size_t ep_workspace_bytes(const EpContext* c, int I) {
+  const size_t capr = (size_t)c->world * c->cap;  // rows this rank may receive
+  size_t off = 0;
+  auto take = [&](size_t b) { off = align_up(off + b, 256); };
+  take((size_t)c->max_tokens * c->E * 4);               // logits
+  take((size_t)c->cap * 4);                             // idx
+  take((size_t)c->cap * 4);                             // w
+  take((size_t)(c->E + 1) * 4);                         // offsets
+  take((size_t)(c->E + 1) * 4);                         // active
+  take((size_t)c->cap * 4);                             // row_token
+  take((size_t)c->cap * 4);                             // inv
+  take(dispatch_scratch_bytes(c->max_tokens, c->top_k, c->E));
+  take((size_t)(c->epr + 1) * 4 * 2);                   // local offsets, active
+  take(capr * 4 * 3);                                   // local row_token, ret_src, ret_row
+  take(capr * (size_t)I * 4);                           // h
+  take(capr * (size_t)c->H * 4);                        // y (local expert order)
+  return off;
+}
+
+int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int w_dtype, const uint8_t* w13_q,
+             const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T, int I, int G, int renormalize,
+             int path, void* out, int32_t* topk_idx_out, float* topk_w_out, void* workspace, cudaStream_t st) {
+  const int E = c->E, k = c->top_k, epr = c->epr, world = c->world;
+  const size_t capr = (size_t)world * c->cap;
+  char* ws = static_cast<char*>(workspace);
+  size_t off = 0;
+  auto take = [&](size_t b) { char* p = ws + off; off = align_up(off + b, 256); return p; };
+  float* logits = reinterpret_cast<float*>(take((size_t)c->max_tokens * E * 4));
+  int32_t* idx = reinterpret_cast<int32_t*>(take((size_t)c->cap * 4));
+  float* wts = reinterpret_cast<float*>(take((size_t)c->cap * 4));
+  int32_t* offsets = reinterpret_cast<int32_t*>(take((size_t)(E + 1) * 4));
+  int32_t* active = reinterpret_cast<int32_t*>(take((size_t)(E + 1) * 4));
+  int32_t* row_token = reinterpret_cast<int32_t*>(take((size_t)c->cap * 4));
+  int32_t* inv = reinterpret_cast<int32_t*>(take((size_t)c->cap * 4));
+  void* disp = take(dispatch_scratch_bytes(c->max_tokens, k, E));
+  int32_t* loff = reinterpret_cast<int32_t*>(take((size_t)(epr + 1) * 4 * 2));
+  int32_t* lact = loff + (epr + 1);
+  int32_t* lrow = reinterpret_cast<int32_t*>(take(capr * 4 * 3));
+  int32_t* ret_src = lrow + capr;
+  int32_t* ret_row = ret_src + capr;
+  float* h = reinterpret_cast<float*>(take(capr * (size_t)I * 4));
+  float* y = reinterpret_cast<float*>(take(capr * (size_t)c->H * 4));
+  if (topk_idx_out) idx = topk_idx_out;
+  if (topk_w_out) wts = topk_w_out;
+
+  const uint32_t epoch = ++c->epoch;
+  const int R = T * k;
+  const int row_bytes = c->H * c->elt;
+  if (T > 0) {
+    launch_router(x, x_dtype, router_w, w_dtype, T, c->H, E, k, renormalize, logits, nullptr, idx, wts, st);
+    launch_dispatch(idx, T, k, E, offsets, row_token, inv, active, disp, st);
+  }
+  const int sms = device_sm_count();
+  ep_send_kernel<<<R > 0 ? (R < sms * 4 ? R : sms * 4) : 1, kCopyThreads, 0, st>>>(
+      static_cast<const char*>(x), row_token, offsets, R, T, epr, world, c->rank, c->cap, row_bytes, c->peers, c->L,
+      epoch);
+  const size_t psmem = (size_t)(2 * world * epr + world + epr + 1) * sizeof(int);
+  ep_prepare_kernel<<<1, kPrepThreads, psmem, st>>>(c->local, c->L, world, c->cap, epr, epoch, loff, lact, lrow,
+                                                    ret_src, ret_row);
+  const char* recv = c->local + c->L.recv_x;
+  int s;
+  if (path == PHMOE_PATH_PREFILL)
+    s = launch_ffn_prefill(recv, lrow, loff, lact, w13_q, w13_s, w2_q, w2_s, (int)capr, c->H, epr, 1, I, G, h, y, st);
+  else
+    s = launch_ffn_decode(recv, x_dtype, lrow, loff, lact, w13_q, w13_s, w2_q, w2_s, (int)capr, c->H, epr, 1, I, G, h,
+                          y, st);
+  if (s) return s;
+  ep_return_kernel<<<sms * 4, kCopyThreads, 0, st>>>(y, loff, epr, ret_src, ret_row, world, c->rank, c->cap, c->H,
+                                                    c->peers, c->L, epoch);
+  ep_wait_kernel<<<1, 32, 0, st>>>(c->local, c->L, world, epoch);
+  if (T > 0)
+    launch_combine(reinterpret_cast<const float*>(c->local + c->L.y_back), inv, wts, T, k, c->H, out, x_dtype, st);
+  note_launches(4 + (T > 0 ? 3 : 0));
+  return PHMOE_OK;
+}
+
+int ep_info(const EpContext* c, int* rank, int* world, int* max_tokens, int* top_k, int* H, int* E) {
+  *rank = c->rank;
+  *world = c->world;
+  *max_tokens = c->max_tokens;
+  *top_k = c->top_k;
+  *H = c->H;
+  *E = c->E;
+  return c->connected ? 1 : 0;
+}
+
+}  // namespace phmoe

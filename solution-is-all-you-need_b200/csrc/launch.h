@@ -53,4 +53,17 @@ void note_launches(int n);
 // Sets the text phmoe_last_error returns on this host thread; returns status.
 int record_error(int status, const char* msg);
 
+// Expert-parallel exchange in peer memory (ep_p2p.cu).
+struct EpContext;
+int ep_create(int rank, int world, int max_tokens, int top_k, int H, int E, int x_elt, EpContext** out,
+              void* handle_out);
+int ep_connect(EpContext* c, const void* handles);
+void ep_destroy(EpContext* c);
+size_t ep_workspace_bytes(const EpContext* c, int I);
+int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int w_dtype, const uint8_t* w13_q,
+             const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T, int I, int G, int renormalize,
+             int path, void* out, int32_t* topk_idx_out, float* topk_w_out, void* workspace, cudaStream_t st);
+int ep_info(const EpContext* c, int* rank, int* world, int* max_tokens, int* top_k, int* H, int* E);
+int ep_device_error(bool reset);
+
 }  // namespace phmoe

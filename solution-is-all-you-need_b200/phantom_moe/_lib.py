@@ -26,6 +26,7 @@ DTYPE_BF16 = 1
 PATH_AUTO = 0
 PATH_DECODE = 1
 PATH_PREFILL = 2
+EP_HANDLE_BYTES = 64  # PHMOE_EP_HANDLE_BYTES
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -48,6 +49,11 @@ SIGNATURES = {
                                       _I, _I, _I, _I, _I, _I, _P, _P, _P]),
     "phmoe_combine": (_I, [_P, _P, _P, _I, _I, _I, _P, _I, _P]),
     "phmoe_gather_rows": (_I, [_P, _LL, _P, _I, _LL, _P, _P]),
+    "phmoe_ep_create": (_I, [_I, _I, _I, _I, _I, _I, _I, _P, _P]),
+    "phmoe_ep_connect": (_I, [_P, _P]),
+    "phmoe_ep_destroy": (_I, [_P]),
+    "phmoe_ep_workspace_size": (_SZ, [_P, _I]),
+    "phmoe_ep_layer": (_I, [_P, _P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P]),
     "phmoe_moe_layer": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
                              _P, _P, _P, _P, _SZ, _P]),
     "phmoe_moe_layer_noalloc": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,

@@ -37,10 +37,12 @@ on CPU ranks with a checker's ops.
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
 
+from . import _lib
 from . import layer as _layer
 
 
@@ -132,9 +134,72 @@ def expert_compute(recv_x, recv_counts, world, w13_q, w13_scales, w2_q, w2_scale
     return ops.gather(y, inv.view(-1))
 
 
+class PeerExchange:
+    """Token exchange in peer memory for :func:`moe_layer_ep` (the
+    ``phmoe_ep_*`` entries): every rank of ``group`` allocates one exchange
+    region sized for ``max_tokens`` tokens per call, the CUDA IPC handles are
+    gathered over ``group``, and each rank maps its peers' regions. Layer calls
+    then move rows and results with direct stores over NVLink and epoch flags:
+    no host synchronisation and no collective on the data path.
+
+    All ranks must create it together, call the layer the same number of
+    times, and :meth:`close` it together (the group is used for the handle
+    exchange and for barriers only, so gloo or NCCL both work)."""
+
+    def __init__(self, group, max_tokens: int, top_k: int, hidden_size: int, num_experts: int,
+                 dtype: torch.dtype = torch.bfloat16):
+        import torch.distributed as dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.max_tokens, self.top_k, self.hidden_size, self.num_experts = max_tokens, top_k, hidden_size, num_experts
+        self.dtype = dtype
+        self._ctx = ctypes.c_void_p()
+        handle = (ctypes.c_char * _lib.EP_HANDLE_BYTES)()
+        _lib.call("phmoe_ep_create", self.rank, self.world, max_tokens, top_k, hidden_size, num_experts,
+                  _layer._DT[dtype], ctypes.byref(self._ctx), handle)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        _lib.call("phmoe_ep_connect", self._ctx, b"".join(handles))
+        dist.barrier(group=group)
+        self._ws = {}
+
+    def workspace(self, device, intermediate_size: int) -> torch.Tensor:
+        key = (device.index, intermediate_size)
+        if key not in self._ws:
+            n = _lib.load().phmoe_ep_workspace_size(self._ctx, intermediate_size)
+            self._ws[key] = torch.empty(n, dtype=torch.uint8, device=device)
+        return self._ws[key]
+
+    def layer(self, x, router_weight, w13_q, w13_scales, w2_q, w2_scales, renormalize=True, group_size=64,
+              path="auto", return_routing=False):
+        T, H = x.shape
+        I = w13_q.shape[1] // 2
+        out = torch.empty_like(x)
+        idx = torch.empty(T, self.top_k, dtype=torch.int32, device=x.device) if return_routing else None
+        w = torch.empty(T, self.top_k, dtype=torch.float32, device=x.device) if return_routing else None
+        ws = self.workspace(x.device, I)
+        _lib.call("phmoe_ep_layer", self._ctx, _layer._ptr(x), _layer._DT[x.dtype], _layer._ptr(router_weight),
+                  _layer._DT[router_weight.dtype], _layer._ptr(w13_q), _layer._ptr(w13_scales), _layer._ptr(w2_q),
+                  _layer._ptr(w2_scales), T, I, group_size, int(bool(renormalize)), _layer._PATHS[path],
+                  _layer._ptr(out), _layer._ptr(idx), _layer._ptr(w), _layer._ptr(ws), ws.numel(),
+                  _layer._stream())
+        return (out, idx, w) if return_routing else out
+
+    def close(self):
+        import torch.distributed as dist
+        if self._ctx:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            _lib.call("phmoe_ep_destroy", self._ctx)
+            self._ctx = ctypes.c_void_p()
+            dist.barrier(group=self.group)
+
+
 def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scales, top_k: int,
                  renormalize: bool = True, group_size: int = 64, ep_group=None, *, path: str = "auto",
-                 return_routing: bool = False, ops=None, stats: dict | None = None):
+                 return_routing: bool = False, ops=None, stats: dict | None = None,
+                 exchange: PeerExchange | None = None):
     """The MoE layer with this rank's expert shard (``w13_q`` etc. hold
     ``E/P`` experts, ``router_weight`` all ``E``). Same result as
     :func:`phantom_moe.moe_layer` on the full layer for this rank's tokens.
@@ -143,8 +208,22 @@ def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scale
     rank's arrived rows). ``stats`` (a dict) receives ``send_rows`` / ``recv_rows``: the rows this
     rank sent to / received from each rank (load-imbalance reporting), and
     ``local_experts_hit``: how many of this rank's experts received rows.
+
+    With ``exchange`` (a :class:`PeerExchange` over ``ep_group``) the rows
+    move through peer memory inside one library call; otherwise through
+    ``torch.distributed.all_to_all_single`` (any backend, the checker's
+    ``ops`` included; one device-to-host copy of the counts per call).
     """
     import torch.distributed as dist
+    if exchange is not None:
+        _layer._need_cuda("hidden_states", hidden_states)
+        shape = hidden_states.shape
+        x = hidden_states.reshape(-1, shape[-1])
+        res = exchange.layer(x, router_weight, w13_q, w13_scales, w2_q, w2_scales, renormalize, group_size, path,
+                             return_routing)
+        if return_routing:
+            return res[0].reshape(shape), res[1], res[2]
+        return res.reshape(shape)
     ops = _CUDA_OPS if ops is None else ops
     world = dist.get_world_size(ep_group)  # None: the default group
     shape = hidden_states.shape

@@ -132,3 +132,83 @@ def test_ep_nccl_ranks_equal_single_gpu(cuda_device, tmp_path):
     res = [np.load(tmp_path / f"ok{r}.npy") for r in range(world)]
     assert all(bool(r[0]) for r in res)
     assert sum(int(r[1]) for r in res) == sum([64, 3, 0, 40, 64, 1, 17, 9][:world]) * K
+
+
+def _peer_worker(rank, world, port, out_dir, case):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    lib = pm.load_library()
+    result = {}
+    try:
+        wr, packed = _layer(61, dev)
+        lo, hi = ep.shard_range(E, world, rank)
+        shard = tuple(t[lo:hi] for t in packed)
+        if case == "layer":
+            ok = True
+            ex = ep.PeerExchange(None, max_tokens=64, top_k=K, hidden_size=H, num_experts=E)
+            tokens = [64, 3, 0, 40, 64, 1, 17, 9][:world]
+            t0 = sum(tokens[:rank])
+            for it in range(3):  # consecutive calls reuse the exchange buffers
+                g = torch.Generator(device=dev).manual_seed(70 + it)
+                xs = [torch.randn(t, H, device=dev, generator=g).to(torch.bfloat16) for t in tokens]
+                out = ep.moe_layer_ep(xs[rank], wr, *shard, K, True, G, None, path="decode", exchange=ex)
+                ref = pm.moe_layer(torch.cat(xs), wr, *packed, K, path="decode")
+                torch.cuda.synchronize()
+                ok = ok and torch.equal(out, ref[t0:t0 + tokens[rank]])
+            ex.close()
+            ex2 = ep.PeerExchange(None, max_tokens=1024, top_k=K, hidden_size=H, num_experts=E)
+            tokens = [1024, 512, 0, 1000, 1024, 7, 300, 64][:world]
+            t0 = sum(tokens[:rank])
+            g = torch.Generator(device=dev).manual_seed(80)
+            xs = [torch.randn(t, H, device=dev, generator=g).to(torch.bfloat16) for t in tokens]
+            out = ep.moe_layer_ep(xs[rank], wr, *shard, K, True, G, None, path="prefill", exchange=ex2)
+            ref = pm.moe_layer(torch.cat(xs), wr, *packed, K, path="prefill")
+            torch.cuda.synchronize()
+            ok = ok and torch.equal(out, ref[t0:t0 + tokens[rank]])
+            ex2.close()
+            result = {"ok": ok, "err": lib.phmoe_device_error(1)}
+        else:  # "timeout": rank 1 never calls the layer, so rank 0's flags never arrive
+            ex = ep.PeerExchange(None, max_tokens=8, top_k=K, hidden_size=H, num_experts=E)
+            if rank == 0:
+                x = torch.randn(8, H, device=dev).to(torch.bfloat16)
+                ep.moe_layer_ep(x, wr, *shard, K, True, G, None, path="decode", exchange=ex)
+                torch.cuda.synchronize()
+            result = {"err": lib.phmoe_device_error(1), "alive": int(torch.ones(1, device=dev).sum().item())}
+            ex.close()
+        np.save(os.path.join(out_dir, f"peer{rank}.npy"), np.array([result.get("ok", True), result["err"],
+                                                                     result.get("alive", 1)]))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_peer(case, tmp_path):
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    torch.multiprocessing.start_processes(_peer_worker, args=(world, _free_port(), str(tmp_path), case),
+                                          nprocs=world, join=True, start_method="spawn")
+    return [np.load(tmp_path / f"peer{r}.npy") for r in range(world)]
+
+
+@pytest.mark.gpu
+def test_ep_peer_exchange_equals_single_gpu(cuda_device, tmp_path):
+    """Rows and results moved through peer memory (no collective on the data
+    path): three consecutive decode calls with ragged and empty ranks, then a
+    prefill call, each equal to the single-GPU layer bit for bit."""
+    res = _run_peer("layer", tmp_path)
+    assert all(bool(r[0]) for r in res)
+    assert all(int(r[1]) == 0 for r in res)
+
+
+@pytest.mark.gpu
+def test_ep_peer_wait_times_out_without_hanging(cuda_device, tmp_path):
+    """A rank that never calls the layer: the other rank's bounded flag waits
+    run out (2 s each), set device error bit 2 and return; its GPU context
+    stays usable."""
+    res = _run_peer("timeout", tmp_path)
+    assert int(res[0][1]) & 4
+    assert int(res[0][2]) == 1
+    assert all(int(r[1]) == 0 for r in res[1:])
