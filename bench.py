@@ -520,6 +520,19 @@ def run_ep(args, ws, rank, device):
         stream.synchronize()
 
     ms_e2e = timed(e2e_step, args.steps, args.warmup)
+    # per-stage device time on this rank (events the library records inside the layer)
+    from phantom_moe import _lib
+    import ctypes
+    nprof = 32
+    dist.barrier()
+    _lib.call("phmoe_profile_begin", nprof)
+    for i in range(nprof):
+        step(i)
+    arr = (ctypes.c_float * _lib.NUM_STAGES)()
+    ncalls = ctypes.c_int(0)
+    _lib.call("phmoe_profile_end", arr, _lib.NUM_STAGES, ctypes.byref(ncalls))
+    ep_stage_names = ["router", "dispatch+send+prepare", "ffn_gateup", "ffn_down", "return+wait+combine"]
+    stage_us = {nm: round(arr[i] / max(ncalls.value, 1) * 1e3, 1) for i, nm in enumerate(ep_stage_names)}
     # per-GPU weight bytes streamed per step (mean over layers and ranks)
     stats = torch.tensor([float(np.mean(hit)), float(max(recv)), float(np.mean(recv))], device=device)
     gathered = [torch.empty_like(stats) for _ in range(ws)]
@@ -545,7 +558,7 @@ def run_ep(args, ws, rank, device):
                                     if exchange is not None else
                                     "NCCL all_to_all_single: counts, bf16 rows out, fp32 rows back"),
                        "local_experts_hit_mean": g_hit, "recv_rows_max_over_ranks": max(recv_all),
-                       "recv_rows_mean": recv_mean},
+                       "recv_rows_mean": recv_mean, "stage_us_rank0": stage_us},
             "roofline": {"kernel": "layer (per GPU)", "bound": "hbm", "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
                          "algorithmic_bytes_per_launch": bytes_gpu},

@@ -451,8 +451,16 @@ int phmoe_ep_layer(void* ctx, const void* x, int x_dtype, const void* router_w, 
   if (!aligned(workspace, kAlign)) return fail(PHMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   const size_t need = ep_workspace_bytes(c, I);
   if (workspace_bytes < need) return fail(PHMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", need, workspace_bytes);
+  // stage events as phmoe_moe_layer records them; here stage 1 also holds the
+  // row exchange out, stage 4 the return of the results
+  const bool prof = g_prof.calls < g_prof.max_calls;
+  cudaEvent_t marks[PHMOE_NUM_STAGES + 1] = {};
+  if (prof)
+    for (int b = 0; b <= PHMOE_NUM_STAGES; ++b) marks[b] = prof_event(g_prof.calls, b);
   const int s = ep_layer(c, x, x_dtype, router_w, w_dtype, w13_q, w13_s, w2_q, w2_s, T, I, group_size, renormalize,
-                         chosen, out, topk_idx_out, topk_w_out, workspace, static_cast<cudaStream_t>(stream));
+                         chosen, out, topk_idx_out, topk_w_out, workspace, static_cast<cudaStream_t>(stream),
+                         prof ? marks : nullptr);
+  if (prof) g_prof.calls++;
   if (s) return fail(s, "expert FFN launch failed");
   return check_launch("phmoe_ep_layer");
 }

@@ -340,8 +340,10 @@ size_t ep_workspace_bytes(const EpContext* c, int I) {
 
 int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int w_dtype, const uint8_t* w13_q,
              const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T, int I, int G, int renormalize,
-             int path, void* out, int32_t* topk_idx_out, float* topk_w_out, void* workspace, cudaStream_t st) {
+             int path, void* out, int32_t* topk_idx_out, float* topk_w_out, void* workspace, cudaStream_t st,
+             const cudaEvent_t* marks) {
   const int E = c->E, k = c->top_k, epr = c->epr, world = c->world;
+  auto mark = [&](int b) { if (marks) cudaEventRecord(marks[b], st); };
   const size_t capr = (size_t)world * c->cap;
   char* ws = static_cast<char*>(workspace);
   size_t off = 0;
@@ -367,10 +369,10 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
   const uint32_t epoch = ++c->epoch;
   const int R = T * k;
   const int row_bytes = c->H * c->elt;
-  if (T > 0) {
-    launch_router(x, x_dtype, router_w, w_dtype, T, c->H, E, k, renormalize, logits, nullptr, idx, wts, st);
-    launch_dispatch(idx, T, k, E, offsets, row_token, inv, active, disp, st);
-  }
+  mark(0);
+  if (T > 0) launch_router(x, x_dtype, router_w, w_dtype, T, c->H, E, k, renormalize, logits, nullptr, idx, wts, st);
+  mark(1);
+  if (T > 0) launch_dispatch(idx, T, k, E, offsets, row_token, inv, active, disp, st);
   const int sms = device_sm_count();
   ep_send_kernel<<<R > 0 ? (R < sms * 4 ? R : sms * 4) : 1, kCopyThreads, 0, st>>>(
       static_cast<const char*>(x), row_token, offsets, R, T, epr, world, c->rank, c->cap, row_bytes, c->peers, c->L,
@@ -379,18 +381,23 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
   ep_prepare_kernel<<<1, kPrepThreads, psmem, st>>>(c->local, c->L, world, c->cap, epr, epoch, loff, lact, lrow,
                                                     ret_src, ret_row);
   const char* recv = c->local + c->L.recv_x;
+  mark(2);
+  const cudaEvent_t mid = marks ? marks[3] : nullptr;
   int s;
   if (path == PHMOE_PATH_PREFILL)
-    s = launch_ffn_prefill(recv, lrow, loff, lact, w13_q, w13_s, w2_q, w2_s, (int)capr, c->H, epr, 1, I, G, h, y, st);
+    s = launch_ffn_prefill(recv, lrow, loff, lact, w13_q, w13_s, w2_q, w2_s, (int)capr, c->H, epr, 1, I, G, h, y, st,
+                           mid);
   else
     s = launch_ffn_decode(recv, x_dtype, lrow, loff, lact, w13_q, w13_s, w2_q, w2_s, (int)capr, c->H, epr, 1, I, G, h,
-                          y, st);
+                          y, st, mid);
   if (s) return s;
+  mark(4);
   ep_return_kernel<<<sms * 4, kCopyThreads, 0, st>>>(y, loff, epr, ret_src, ret_row, world, c->rank, c->cap, c->H,
                                                     c->peers, c->L, epoch);
   ep_wait_kernel<<<1, 32, 0, st>>>(c->local, c->L, world, epoch);
   if (T > 0)
     launch_combine(reinterpret_cast<const float*>(c->local + c->L.y_back), inv, wts, T, k, c->H, out, x_dtype, st);
+  mark(5);
   note_launches(4 + (T > 0 ? 3 : 0));
   return PHMOE_OK;
 }

@@ -62,7 +62,8 @@ void ep_destroy(EpContext* c);
 size_t ep_workspace_bytes(const EpContext* c, int I);
 int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int w_dtype, const uint8_t* w13_q,
              const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T, int I, int G, int renormalize,
-             int path, void* out, int32_t* topk_idx_out, float* topk_w_out, void* workspace, cudaStream_t st);
+             int path, void* out, int32_t* topk_idx_out, float* topk_w_out, void* workspace, cudaStream_t st,
+             const cudaEvent_t* marks);  // marks: PHMOE_NUM_STAGES + 1 events, or null
 int ep_info(const EpContext* c, int* rank, int* world, int* max_tokens, int* top_k, int* H, int* E);
 int ep_device_error(bool reset);
 
