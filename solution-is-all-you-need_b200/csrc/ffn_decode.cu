@@ -18,20 +18,24 @@
 // be 4x the int4 bytes).
 //
 // gate/up kernel (the larger half of the bytes): warp-specialised.
-//  * A producer warp issues, per task, two TMA tensor copies (one 16-row x
-//    512-byte box of gate rows and one of up rows, 128-byte swizzled so the
-//    fragment reads are nearly conflict free), one bulk copy per activation
-//    row, and the fp16 scale slices as 4-byte cp.async; all complete on the
-//    stage's "full" mbarrier (bytes for TMA, cp.async.mbarrier.arrive.noinc).
-//  * 16 consumer warps split each task's K, wait on "full", compute and
-//    release "empty" (one arrival per warp); at an item's last task their
-//    partials are summed in warp order (deterministic) by 4 warps that apply
-//    SwiGLU and store h as bf16 hi/lo planes. The unpacked weights are
-//    128 + nibble: the +136 offset is removed after the MMA with one extra MMA
-//    per K step against an all-ones A (it yields sum_k x_k), and the fp16
-//    group scale multiplies the fp32 partial of each group.
-//  * item = (expert, 16 intermediate rows, pass of 8 tokens); items are
-//    ordered (expert, tile, pass) so extra passes re-read weights still in L2.
+//  * item = (expert, 64 gate rows and the 64 matching up rows, pass of 8
+//    tokens); task = one 512-element K chunk of an item (32 KB of weights).
+//    Items are ordered (expert, row block, pass) so extra passes re-read
+//    weights still in L2.
+//  * A producer warp issues, per task, two TMA tensor copies of weights (a
+//    64-row x 2 x 128-byte box of gate rows and one of up rows, 128-byte
+//    swizzled so the fragment reads are nearly conflict free), two TMA copies
+//    of the matching fp16 scale slices, and one bulk copy per activation row;
+//    all complete on the stage's "full" mbarrier.
+//  * Consumer warp w owns 16-row group w%4 and K quarter w/4 of every task,
+//    waits on "full", computes and releases "empty" (one arrival per warp);
+//    its accumulators cover the item's whole K, so the only cross-warp step
+//    is a 4-way sum (fixed order) at the item's end, after which the
+//    quarter-0 warp applies SwiGLU and stores h as bf16 hi/lo planes. The
+//    unpacked weights are 128 + nibble: the +136 offset is removed after the
+//    MMA with one extra MMA per K step against an all-ones A (it yields
+//    sum_k x_k), and the fp16 group scale multiplies the fp32 partial of
+//    each group.
 // down kernel: 16 warps copy each task (128 rows x 512 K) with 16-byte
 //  cp.async into padded rows and compute it between two CTA barriers; warp w
 //  owns rows 16(w%8)..+15 and half of each K-chunk (w/8).
@@ -49,6 +53,7 @@
 // CTA's abort flag and the device error word (phmoe_device_error) and all
 // warps leave; the producer first waits (bounded) for its copies in flight.
 #include <cuda.h>  // CUtensorMap (types only; the encoder is fetched from the driver at run time)
+#include <string.h>
 
 #include "common.cuh"
 #include "launch.h"
@@ -135,14 +140,17 @@ __device__ __forceinline__ void warp_arrive(uint32_t bar, int lane) {
   if (lane == 0) mbar_arrive(bar);
 }
 
+// Control block of the row-block gate/up kernel: stage ring plus
+// double-buffered reduction barriers for each of the four row groups.
 template <int S>
-struct Ctl {
+struct RbCtl {
   uint64_t full[S];
   uint64_t empty[S];
-  uint64_t red_full[2];
-  uint64_t red_empty[2];
+  uint64_t red_full[8];   // [buf][rg]: the three kq > 0 warps have written
+  uint64_t red_empty[8];  // [buf][rg]: the kq = 0 warp has read
   int abort_flag;
 };
+
 
 // ---------------------------------------------------------------------------
 // fragments
@@ -350,66 +358,65 @@ __device__ __forceinline__ void cta_range(int total, int& q0, int& q1) {
 }
 
 // ---------------------------------------------------------------------------
-// gate/up + SwiGLU (TMA-fed, warp-specialised)
+// gate/up + SwiGLU, row-block form
 // ---------------------------------------------------------------------------
-// KCH = K elements per task. 2048 (3 stages, one reduction buffer) gives each
-// consumer warp 2 (G=64) or 4 (G=32) groups per task, amortising the per-task
-// work; 1024 (5 stages, 3 for fp32; two reduction buffers) is used when that
-// does not fit in shared memory.
-template <int G, typename XT, int KCH>
-struct GateUpCfg {
+// Item = (expert, 64-row block of gate rows and the matching up rows, pass of
+// 8 tokens); task = one 512-element K chunk of the item (32 KB of weights).
+// Consumer warp w owns 16-row group rg = w % 4 and K quarter kq = w / 4 of
+// every task, so its accumulators run over the whole K range of the item and
+// the only cross-warp step is a 4-way sum (fixed order kq 0, 1, 2, 3) at the
+// end of each item, after which the kq = 0 warp applies SwiGLU. Scales arrive
+// with the weights (4-byte async copies) and are read as fp16 pairs.
+constexpr int kRbRows = 64;   // gate rows per item (and as many up rows)
+constexpr int kRbKc = 512;    // K elements per task
+
+template <int G, typename XT>
+struct RbCfg {
   static constexpr bool kF32 = std::is_same<XT, float>::value;
-  static constexpr int kStages = KCH == 2048 ? 3 : (kF32 ? 3 : 5);
-  static constexpr int kRedBufs = KCH == 2048 ? 1 : 2;
-  static constexpr int kRows = 32;
-  static constexpr int kKch = KCH;
-  static constexpr int kGpw = kKch / G / kConsumers;         // groups per consumer warp per task
-  static constexpr int kBlock = 16 * (kKch / 2);             // one 16-row box
-  static constexpr int kScaleRow = kKch / G * 2;
-  static constexpr int kPairs = kKch / G / 2;
-  static constexpr int kBRowBytes = kKch * (int)sizeof(XT);
-  static constexpr int kBPad = (G == 32 && !kF32) ? 64 : 16;  // conflict-free B reads
+  static constexpr int kGpq = 128 / G;                       // groups per consumer warp per task
+  static constexpr int kBlock = 2 * kRbRows * 128;           // one 64-row box of 2 K-chunks (16 KB)
+  static constexpr int kScaleRow = kRbKc / G * 2;            // bytes of scales per row per task
+  static constexpr int kPairs = kRbKc / G / 2;
+  static constexpr int kBRowBytes = kRbKc * (int)sizeof(XT);
+  static constexpr int kBPad = (G == 32 && !kF32) ? 64 : 16;
   static constexpr int kBStride = kBRowBytes + kBPad;
-  static constexpr int kW = 0;                               // [gate box][up box], 1024-aligned
-  static constexpr int kS = 2 * kBlock;
-  static constexpr int kB = kS + kRows * kScaleRow;
+  static constexpr int kW = 0;                                // [gate box][up box]
+  static constexpr int kS = 2 * kBlock;                       // [128 rows][kScaleRow]
+  static constexpr int kB = kS + 2 * kRbRows * kScaleRow;     // [8 tokens][kBStride]
   static constexpr int kStage = (kB + kTok * kBStride + 1023) / 1024 * 1024;
-  static constexpr int kRedBuf = kConsumers * 8 * 32 * 4;
+  static constexpr int kStages = kF32 ? 3 : 4;
+  static constexpr int kRed = 4 * 3 * 32 * 8 * 4;             // [rg][kq-1][lane][8] floats
   static constexpr size_t smem(int E) {
-    return 1024 + (size_t)kStages * kStage + kRedBufs * kRedBuf + sizeof(Ctl<kStages>) +
-           (size_t)(4 * E + 4) * 4;
+    return 1024 + (size_t)kStages * kStage + 2 * kRed + sizeof(RbCtl<kStages>) + (size_t)(4 * E + 4) * 4;
   }
 };
 
-// Byte offset of (row R of a 16-row box, byte kb of the task's K slice) in a
-// box written by TMA with 128-byte swizzle: 128-byte lines ordered (K-chunk,
-// row); the 16-byte unit inside a line is XORed with the row (mod 8).
-__device__ __forceinline__ int swz_off(int Rb, int kb) {
+// Byte offset of (row R of a 64-row box, byte kb of the task's K slice).
+__device__ __forceinline__ int swz_off64(int R, int kb) {
   const int c0 = kb & 127;
-  return ((kb >> 7) * 16 + Rb) * 128 + ((((c0 >> 4) ^ (Rb & 7)) << 4) | (c0 & 15));
+  return ((kb >> 7) * kRbRows + R) * 128 + ((((c0 >> 4) ^ (R & 7)) << 4) | (c0 & 15));
 }
 
-template <int G, typename XT, int KCH>
+template <int G, typename XT>
 __global__ void __launch_bounds__(kGuThreads, 1)
-ffn_gateup_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int box_chunks,
-                  const XT* __restrict__ x, const int32_t* __restrict__ row_token,
-                  const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
-                  const uint16_t* __restrict__ w13_s, int H, int I, int E,
-                  __nv_bfloat16* __restrict__ h_hi, __nv_bfloat16* __restrict__ h_lo) {
-  using C = GateUpCfg<G, XT, KCH>;
+ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int box_chunks,
+                     const __grid_constant__ CUtensorMap s_map, int s_tma, const XT* __restrict__ x,
+                     const int32_t* __restrict__ row_token, const int32_t* __restrict__ offsets,
+                     const int32_t* __restrict__ active, const uint16_t* __restrict__ w13_s, int H, int I, int E,
+                     __nv_bfloat16* __restrict__ h_hi, __nv_bfloat16* __restrict__ h_lo) {
+  using C = RbCfg<G, XT>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
-  // 128-byte swizzled TMA destinations must be 1024-byte aligned
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [kRedBufs][kConsumers][8][32]
-  Ctl<S>* ctl = reinterpret_cast<Ctl<S>*>(smem + S * C::kStage + C::kRedBufs * C::kRedBuf);
+  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [2][rg][kq-1][lane][8]
+  RbCtl<S>* ctl = reinterpret_cast<RbCtl<S>*>(smem + S * C::kStage + 2 * C::kRed);
   int* mbase = reinterpret_cast<int*>(ctl + 1);
   const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
   volatile int* abort_flag = &ctl->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles = I / 16;
+  const int tiles = (I + kRbRows - 1) / kRbRows;
   const int NG = H / G;
-  const int nkc = (H + C::kKch - 1) / C::kKch;
+  const int nkc = (H + kRbKc - 1) / kRbKc;
   const int na = active[0];
 
   if (threadIdx.x == 0) {
@@ -417,9 +424,9 @@ ffn_gateup_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int bo
       mbar_init(smem_u32(&ctl->full[s]), 1 + 32);  // expect_tx arrival + one cp.async arrival per lane
       mbar_init(smem_u32(&ctl->empty[s]), kConsumers);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&ctl->red_full[b]), kConsumers);
-      mbar_init(smem_u32(&ctl->red_empty[b]), 4);
+    for (int i = 0; i < 8; ++i) {
+      mbar_init(smem_u32(&ctl->red_full[i]), 3);
+      mbar_init(smem_u32(&ctl->red_empty[i]), 1);
     }
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -439,22 +446,22 @@ ffn_gateup_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int bo
     };
     int tok = token(cu);
     int issued = 0;
-    const uint32_t box_bytes = 16u * 128u * (uint32_t)box_chunks;
     for (int t = 0; t < ntask; ++t) {
       const int s = t % S;
       if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
       Cursor nx = cu;
       cursor_next(nx, tiles, nkc, meta);
-      const int tok_next = t + 1 < ntask ? token(nx) : -1;  // hidden behind this task's copies
-      const int k0 = cu.kc * C::kKch;
-      const int kel = min(C::kKch, H - k0);
+      const int tok_next = (t + 1 < ntask && nx.kc == 0) ? token(nx) : tok;
+      const int k0 = cu.kc * kRbKc;
+      const int kel = min(kRbKc, H - k0);
       const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
       const uint32_t full = smem_u32(&ctl->full[s]);
       uint8_t* st = smem + s * C::kStage;
       if (lane == 0)
-        mbar_arrive_expect_tx(full, 2 * box_bytes + (uint32_t)(nt * kel * (int)sizeof(XT)));
+        mbar_arrive_expect_tx(full, 2u * (uint32_t)(box_chunks * kRbRows * 128) + (uint32_t)(nt * kel * (int)sizeof(XT)) +
+                                        (s_tma ? 2u * kRbRows * C::kScaleRow : 0u));
       __syncwarp();
-      const int grow = meta.e[cu.slot] * 2 * I + cu.tile * 16;  // first gate row; up rows are I further
+      const int grow = meta.e[cu.slot] * 2 * I + cu.tile * kRbRows;  // first gate row; up rows are I further
       if (lane < 2) {
         const uint32_t dst = smem_u32(st + C::kW + lane * C::kBlock);
         const int row = grow + lane * I;
@@ -462,23 +469,31 @@ ffn_gateup_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int bo
           tma_load_3d(dst, &w13_map, 0, row, k0 / 256, full);
         } else {
           for (int ch = 0; ch < box_chunks; ++ch)
-            tma_load_2d(dst + ch * 16 * 128, &w13_map, k0 / 2 + ch * 128, row, full);
+            tma_load_2d(dst + ch * kRbRows * 128, &w13_map, k0 / 2 + ch * 128, row, full);
         }
       }
       if (lane < nt)  // lane n < 8 holds the token id of pass row n
         bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), x + (size_t)tok * H + k0, kel * (int)sizeof(XT), full);
-      {
-        const size_t srow = (size_t)(lane < 16 ? grow + lane : grow + I + lane - 16);
-        for (int pp = 0; pp < C::kPairs; ++pp)
-          if (pp * 2 * G < kel)
-            cp_async4(smem_u32(st + C::kS + lane * C::kScaleRow + pp * 4), w13_s + srow * NG + k0 / G + 2 * pp);
+      // scales: 64 gate rows then 64 up rows, kel/G groups each: two TMA boxes
+      // when the scale rows are 16-byte aligned, else pairs of groups by
+      // 4-byte async copies
+      if (s_tma) {
+        if (lane == 2 || lane == 3)
+          tma_load_2d(smem_u32(st + C::kS + (lane - 2) * kRbRows * C::kScaleRow), &s_map, k0 / G,
+                      grow + (lane - 2) * I, full);
+      } else for (int q = lane; q < 2 * kRbRows * C::kPairs; q += 32) {
+        const int rr = q / C::kPairs, pp = q - rr * C::kPairs;
+        const int i = cu.tile * kRbRows + (rr & (kRbRows - 1));
+        if (pp * 2 * G < kel && i < I) {
+          const size_t srow = (size_t)grow + (rr >= kRbRows ? I : 0) + (rr & (kRbRows - 1));
+          cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + srow * NG + k0 / G + 2 * pp);
+        }
       }
       cp_async_arrive_noinc(full);
       ++issued;
       tok = tok_next;
       cu = nx;
     }
-    // leave only when every copy issued into this CTA's shared memory has landed
     for (int t = max(0, issued - S); t < issued; ++t) {
       const uint32_t full = smem_u32(&ctl->full[t % S]);
       for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(full, (t / S) & 1); ++i) {
@@ -488,21 +503,24 @@ ffn_gateup_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int bo
   }
 
   // ---------------- consumer warps ----------------
-  // Warp w computes groups g_j = w + 16 j (j < kGpw) of every task; their
-  // shared-memory offsets inside a stage are fixed, so they are computed once.
+  const int rg = warp & 3, kq = warp >> 2;
   const int r = lane >> 2, c = lane & 3;
-  constexpr int kGpw = C::kGpw;
-  constexpr int kScH = C::kScaleRow / 2;
-  int o0[kGpw], o8[kGpw], ob[kGpw], os[kGpw];
+  constexpr int kGpq = C::kGpq;
+  const int R0 = rg * 16 + r;
+  int o0[kGpq], o8[kGpq], ob[kGpq];
 #pragma unroll
-  for (int j = 0; j < kGpw; ++j) {
-    const int g = warp + kConsumers * j;
+  for (int j = 0; j < kGpq; ++j) {
+    const int g = kq * kGpq + j;  // group within the task
     const int kb = (G == 64) ? g * 32 + 8 * c : g * 16 + 4 * c;
-    o0[j] = C::kW + swz_off(r, kb);
-    o8[j] = C::kW + swz_off(r + 8, kb);
+    o0[j] = C::kW + swz_off64(R0, kb);
+    o8[j] = C::kW + swz_off64(R0 + 8, kb);
     ob[j] = C::kB + r * C::kBStride + g * G * (int)sizeof(XT) + (G == 64 ? 16 : 8) * c * (int)sizeof(XT);
-    os[j] = C::kS + (r * kScH + g) * 2;
   }
+  // scales of this warp's groups for gate rows R0, R0+8 and up rows R0, R0+8
+  const int osg0 = C::kS + R0 * C::kScaleRow + kq * kGpq * 2;
+  const int osg8 = osg0 + 8 * C::kScaleRow;
+  const int osu0 = osg0 + kRbRows * C::kScaleRow;
+  const int osu8 = osu0 + 8 * C::kScaleRow;
   Cursor cu = cursor_at(q0, na, tiles, meta);
   float acc_g[4] = {0.f, 0.f, 0.f, 0.f}, acc_u[4] = {0.f, 0.f, 0.f, 0.f};
   int item = 0;
@@ -512,12 +530,21 @@ ffn_gateup_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int bo
 #pragma unroll
       for (int q = 0; q < 4; ++q) { acc_g[q] = 0.f; acc_u[q] = 0.f; }
     }
-    const int ngt = min(C::kKch, H - cu.kc * C::kKch) / G;
+    const int ngt = min(kRbKc, H - cu.kc * kRbKc) / G;
     if (!wait_phase(smem_u32(&ctl->full[s]), (t / S) & 1, abort_flag)) return;
     const uint8_t* st = smem + s * C::kStage;
+    __half2 sg0[kGpq / 2 > 0 ? kGpq / 2 : 1], sg8[kGpq / 2 > 0 ? kGpq / 2 : 1];
+    __half2 su0[kGpq / 2 > 0 ? kGpq / 2 : 1], su8[kGpq / 2 > 0 ? kGpq / 2 : 1];
 #pragma unroll
-    for (int j = 0; j < kGpw; ++j) {
-      if (warp + kConsumers * j < ngt) {
+    for (int p = 0; p < kGpq / 2; ++p) {
+      sg0[p] = *reinterpret_cast<const __half2*>(st + osg0 + 4 * p);
+      sg8[p] = *reinterpret_cast<const __half2*>(st + osg8 + 4 * p);
+      su0[p] = *reinterpret_cast<const __half2*>(st + osu0 + 4 * p);
+      su8[p] = *reinterpret_cast<const __half2*>(st + osu8 + 4 * p);
+    }
+#pragma unroll
+    for (int j = 0; j < kGpq; ++j) {
+      if (kq * kGpq + j < ngt) {
         const RowWords<G> ag0 = lds_row<G>(st + o0[j]);
         const RowWords<G> ag8 = lds_row<G>(st + o8[j]);
         const RowWords<G> au0 = lds_row<G>(st + o0[j] + C::kBlock);
@@ -525,45 +552,51 @@ ffn_gateup_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int bo
         BWords<G> b;
         if constexpr (C::kF32) lds_b_f32<G>(st + ob[j], b);
         else lds_b_plane<G>(st + ob[j], b.hi);
-        const __half* sc = reinterpret_cast<const __half*>(st + os[j]);
-        gateup_group<G, C::kF32>(ag0, ag8, au0, au8, b, __half2float(sc[0]), __half2float(sc[8 * kScH]),
-                                 __half2float(sc[16 * kScH]), __half2float(sc[24 * kScH]), acc_g, acc_u);
+        const int p = j >> 1;
+        const bool hi = j & 1;
+        gateup_group<G, C::kF32>(ag0, ag8, au0, au8, b,
+                                 hi ? __high2float(sg0[p]) : __low2float(sg0[p]),
+                                 hi ? __high2float(sg8[p]) : __low2float(sg8[p]),
+                                 hi ? __high2float(su0[p]) : __low2float(su0[p]),
+                                 hi ? __high2float(su8[p]) : __low2float(su8[p]), acc_g, acc_u);
       }
     }
     warp_arrive(smem_u32(&ctl->empty[s]), lane);  // this warp is done with the stage
     if (cu.kc == nkc - 1) {
-      const int buf = C::kRedBufs == 2 ? (item & 1) : 0;
-      const int use = C::kRedBufs == 2 ? (item >> 1) : item;
-      float* rb = red + buf * (C::kRedBuf / 4);
-      if (use > 0 && !wait_phase(smem_u32(&ctl->red_empty[buf]), (use - 1) & 1, abort_flag)) return;
+      const int buf = item & 1, use = item >> 1;
+      const int bi = buf * 4 + rg;  // barrier index
+      float* rb = red + (size_t)buf * (C::kRed / 4) + (size_t)rg * 3 * 32 * 8;
+      if (kq > 0) {
+        if (use > 0 && !wait_phase(smem_u32(&ctl->red_empty[bi]), (use - 1) & 1, abort_flag)) return;
+        float4* dst = reinterpret_cast<float4*>(rb + ((kq - 1) * 32 + lane) * 8);
+        dst[0] = make_float4(acc_g[0], acc_g[1], acc_g[2], acc_g[3]);
+        dst[1] = make_float4(acc_u[0], acc_u[1], acc_u[2], acc_u[3]);
+        warp_arrive(smem_u32(&ctl->red_full[bi]), lane);
+      } else {
+        if (!wait_phase(smem_u32(&ctl->red_full[bi]), use & 1, abort_flag)) return;
+        float gs[4] = {acc_g[0], acc_g[1], acc_g[2], acc_g[3]};
+        float us[4] = {acc_u[0], acc_u[1], acc_u[2], acc_u[3]};
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        rb[warp * 256 + q * 32 + lane] = acc_g[q];
-        rb[warp * 256 + (4 + q) * 32 + lane] = acc_u[q];
-      }
-      warp_arrive(smem_u32(&ctl->red_full[buf]), lane);
-      if (warp < 4) {
-        // thread (q = warp, ln = lane) finishes fragment slot q of lane ln,
-        // summing the consumer warps' partials in order 0..15, then SwiGLU
-        if (!wait_phase(smem_u32(&ctl->red_full[buf]), use & 1, abort_flag)) return;
-        const int q = warp, ln = lane;
-        float gs = 0.f, us = 0.f;
-#pragma unroll
-        for (int w = 0; w < kConsumers; ++w) {
-          gs += rb[w * 256 + q * 32 + ln];
-          us += rb[w * 256 + (4 + q) * 32 + ln];
+        for (int w = 0; w < 3; ++w) {
+          const float4* src = reinterpret_cast<const float4*>(rb + (w * 32 + lane) * 8);
+          const float4 a = src[0], b = src[1];
+          gs[0] += a.x; gs[1] += a.y; gs[2] += a.z; gs[3] += a.w;
+          us[0] += b.x; us[1] += b.y; us[2] += b.z; us[3] += b.w;
         }
-        warp_arrive(smem_u32(&ctl->red_empty[buf]), lane);
+        warp_arrive(smem_u32(&ctl->red_empty[bi]), lane);
         const int n = meta.n[cu.slot], row0 = meta.row0[cu.slot];
-        const int i = cu.tile * 16 + (ln >> 2) + (q >= 2 ? 8 : 0);
-        const int rr = cu.pass * kTok + 2 * (ln & 3) + (q & 1);
-        if (rr < n) {
-          const float hv = silu_f32(gs) * us;
-          const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
-          const __nv_bfloat16 lb = __float2bfloat16_rn(hv - __bfloat162float(hb));
-          const size_t o = (size_t)(row0 + rr) * I + i;
-          h_hi[o] = hb;
-          h_lo[o] = lb;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int i = cu.tile * kRbRows + R0 + (q >= 2 ? 8 : 0);
+          const int rr = cu.pass * kTok + 2 * c + (q & 1);
+          if (rr < n && i < I) {
+            const float hv = silu_f32(gs[q]) * us[q];
+            const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
+            const __nv_bfloat16 lb = __float2bfloat16_rn(hv - __bfloat162float(hb));
+            const size_t o = (size_t)(row0 + rr) * I + i;
+            h_hi[o] = hb;
+            h_lo[o] = lb;
+          }
         }
       }
       ++item;
@@ -745,13 +778,13 @@ EncodeTiledFn encode_fn() {
 // a 3-D view (128 B, rows, K-chunks) so one copy moves the whole box; if the
 // driver rejects it, a 2-D view copied one 128-byte chunk at a time (same
 // shared-memory layout). Returns 0 (2-D), 1 (3-D) or -1 (no map).
-int make_w13_map(CUtensorMap* map, const uint8_t* w13_q, long long rows, int H, int box_chunks) {
+int make_w13_map(CUtensorMap* map, const uint8_t* w13_q, long long rows, int H, int box_chunks, int box_rows = 16) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return -1;
   {
     const cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)(H / 256)};
     const cuuint64_t strides[2] = {(cuuint64_t)(H / 2), 128};
-    const cuuint32_t box[3] = {128, 16, (cuuint32_t)box_chunks};
+    const cuuint32_t box[3] = {128, (cuuint32_t)box_rows, (cuuint32_t)box_chunks};
     const cuuint32_t estr[3] = {1, 1, 1};
     if (enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(w13_q), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -760,7 +793,7 @@ int make_w13_map(CUtensorMap* map, const uint8_t* w13_q, long long rows, int H, 
   }
   const cuuint64_t dims[2] = {(cuuint64_t)(H / 2), (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)(H / 2)};
-  const cuuint32_t box[2] = {128, 16};
+  const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   if (enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w13_q), dims, strides, box, estr,
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -771,32 +804,34 @@ int make_w13_map(CUtensorMap* map, const uint8_t* w13_q, long long rows, int H, 
 
 constexpr size_t kMaxSmem = 227 * 1024;
 
-template <int G, typename XT, int KCH>
-int launch_gateup_k(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
-                    const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
-                    __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
-  const int box_chunks = std::min(H, KCH) / 256;
-  alignas(64) CUtensorMap map;
-  const int mode = make_w13_map(&map, w13_q, (long long)E * 2 * I, H, box_chunks);
-  if (mode < 0) return PHMOE_ERR_CUDA;
-  const size_t smem = GateUpCfg<G, XT, KCH>::smem(E);
-  auto k = ffn_gateup_kernel<G, XT, KCH>;
-  set_smem(k, smem);
-  k<<<grid, kGuThreads, smem, st>>>(map, mode, box_chunks, static_cast<const XT*>(x), row_token, offsets, active,
-                                    w13_s, H, I, E, h_hi, h_lo);
-  return PHMOE_OK;
-}
-
-// 2048-element tasks for bf16 activations when H needs them and they fit.
 template <int G, typename XT>
-int launch_gateup(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
-                  const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
-                  __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
-  if constexpr (!std::is_same<XT, float>::value) {
-    if (H >= 2048 && GateUpCfg<G, XT, 2048>::smem(E) <= kMaxSmem)
-      return launch_gateup_k<G, XT, 2048>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
+int launch_gateup_rb(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
+                     const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
+                     __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
+  const int box_chunks = std::min(H, kRbKc) / 256;
+  alignas(64) CUtensorMap map, smap;
+  const int mode = make_w13_map(&map, w13_q, (long long)E * 2 * I, H, box_chunks, kRbRows);
+  if (mode < 0) return PHMOE_ERR_CUDA;
+  // scales as a 2-D fp16 tensor [E*2I rows][H/G]: boxes of one task's groups x 64 rows
+  int s_tma = 0;
+  if (((H / G) * 2) % 16 == 0) {
+    EncodeTiledFn enc = encode_fn();
+    const cuuint64_t dims[2] = {(cuuint64_t)(H / G), (cuuint64_t)E * 2 * I};
+    const cuuint64_t strides[1] = {(cuuint64_t)(H / G) * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)(kRbKc / G), (cuuint32_t)kRbRows};
+    const cuuint32_t estr[2] = {1, 1};
+    s_tma = enc && enc(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(w13_s), dims, strides, box,
+                       estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
   }
-  return launch_gateup_k<G, XT, 1024>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
+  if (!s_tma) memset(&smap, 0, sizeof(smap));
+  const size_t smem = RbCfg<G, XT>::smem(E);
+  if (smem > kMaxSmem) return PHMOE_ERR_UNSUPPORTED;
+  auto k = ffn_gateup_rb_kernel<G, XT>;
+  set_smem(k, smem);
+  k<<<grid, kGuThreads, smem, st>>>(map, mode, box_chunks, smap, s_tma, static_cast<const XT*>(x), row_token,
+                                    offsets, active, w13_s, H, I, E, h_hi, h_lo);
+  return PHMOE_OK;
 }
 
 template <int G>
@@ -841,11 +876,13 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
   const bool f32 = x_dtype == PHMOE_DTYPE_F32;
   int s;
   if (G == 64)
-    s = f32 ? launch_gateup<64, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
-            : launch_gateup<64, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
+    s = f32 ? launch_gateup_rb<64, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
+            : launch_gateup_rb<64, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid,
+                                                  st);
   else
-    s = f32 ? launch_gateup<32, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
-            : launch_gateup<32, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st);
+    s = f32 ? launch_gateup_rb<32, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
+            : launch_gateup_rb<32, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid,
+                                                  st);
   if (s) return s;
   if (mid_event) cudaEventRecord(mid_event, st);
   if (G == 64) launch_down<64>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
