@@ -752,6 +752,214 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
   cp_async_wait<0>();
 }
 
+// ---------------------------------------------------------------------------
+// down projection, TMA-fed form (I % 256 == 0)
+// ---------------------------------------------------------------------------
+// Item = (expert, 128 output rows, pass of 8 tokens); task = one 512-element
+// K chunk. A producer warp copies per task one TMA box of weights (128 rows x
+// 2 x 128 bytes, 128-byte swizzle), the matching scales (a TMA box when the
+// scale rows are 16-byte aligned, else one bulk copy of the block's
+// contiguous scale rows, else 4-byte async copies) and the two h planes of
+// the pass (one TMA box each: 8 groups x 8 rows x 64 elements, 128-byte
+// swizzle). Consumer warp w owns 16-row group w%8 and K half w/8; the two
+// halves are summed (fixed order) at the item's end.
+constexpr int kDnRows = 128;
+constexpr int kDnKc = 512;
+constexpr int kDnScaleBytes = 4096;  // scale region of a stage
+
+template <int S>
+struct DnCtl {
+  uint64_t full[S];
+  uint64_t empty[S];
+  uint64_t red_full[16];   // [buf][rg]
+  uint64_t red_empty[16];
+  int abort_flag;
+};
+
+template <int G>
+struct DnCfg {
+  static constexpr int kGph = 256 / G;                 // groups per consumer warp per task
+  static constexpr int kW = 0;                         // [2 chunks][128 rows][128 B]
+  static constexpr int kS = 2 * kDnRows * 128;         // scales
+  static constexpr int kB = kS + kDnScaleBytes;        // [2 planes][8 groups][8 rows][128 B]
+  static constexpr int kPlane = 8 * kTok * 128;
+  static constexpr int kStage = kB + 2 * kPlane;
+  static constexpr int kStages = 4;
+  static constexpr int kRed = 8 * 32 * 16;             // [rg][lane][4 floats]
+  static constexpr size_t smem(int E) {
+    return 1024 + (size_t)kStages * kStage + 2 * kRed + sizeof(DnCtl<kStages>) + (size_t)(4 * E + 4) * 4;
+  }
+};
+
+__device__ __forceinline__ int swz_off_rows(int R, int kb, int rows) {
+  const int c0 = kb & 127;
+  return ((kb >> 7) * rows + R) * 128 + ((((c0 >> 4) ^ (R & 7)) << 4) | (c0 & 15));
+}
+
+// B words of group g (within a task) for token row r from one h plane laid
+// out [64-element block][8 rows][128 B] with 128-byte swizzle.
+template <int G>
+__device__ __forceinline__ void lds_b_swz(const uint8_t* plane, int g, int r, int c, uint32_t (&d)[G / 8]) {
+  if constexpr (G == 64) {
+    const uint8_t* row = plane + g * (kTok * 128) + r * 128;
+    const uint4 a = *reinterpret_cast<const uint4*>(row + (((2 * c) ^ (r & 7)) << 4));
+    const uint4 b = *reinterpret_cast<const uint4*>(row + (((2 * c + 1) ^ (r & 7)) << 4));
+    d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w;
+    d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
+  } else {
+    const uint8_t* row = plane + (g >> 1) * (kTok * 128) + r * 128;
+    const uint4 a = *reinterpret_cast<const uint4*>(row + ((((g & 1) * 4 + c) ^ (r & 7)) << 4));
+    d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w;
+  }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kGuThreads, 1)
+ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap s_map,
+                    const __grid_constant__ CUtensorMap hi_map, const __grid_constant__ CUtensorMap lo_map,
+                    int s_mode, const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
+                    const uint16_t* __restrict__ w2_s, int H, int I, int E, float* __restrict__ y) {
+  using C = DnCfg<G>;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [2][rg][lane][4]
+  DnCtl<S>* ctl = reinterpret_cast<DnCtl<S>*>(smem + S * C::kStage + 2 * C::kRed);
+  int* mbase = reinterpret_cast<int*>(ctl + 1);
+  const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
+  volatile int* abort_flag = &ctl->abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = H / kDnRows;
+  const int NG = I / G;
+  const int nkc = (I + kDnKc - 1) / kDnKc;
+  const int na = active[0];
+  // scale rows in shared memory: s_mode 0 = TMA box / async copies of the
+  // task's groups; 1 = every group of the block (one bulk copy)
+  const int srow = s_mode == 1 ? NG * 2 : (kDnKc / G) * 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(&ctl->full[s]), 1 + 32);
+      mbar_init(smem_u32(&ctl->empty[s]), kConsumers);
+    }
+    for (int i = 0; i < 16; ++i) {
+      mbar_init(smem_u32(&ctl->red_full[i]), 1);
+      mbar_init(smem_u32(&ctl->red_empty[i]), 1);
+    }
+    ctl->abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  const int total = build_meta(offsets, active, tiles, meta);
+  int q0, q1;
+  cta_range(total, q0, q1);
+  const int ntask = (q1 - q0) * nkc;
+  if (ntask == 0) return;
+
+  if (warp == kConsumers) {
+    // ---------------- producer warp ----------------
+    Cursor cu = cursor_at(q0, na, tiles, meta);
+    int issued = 0;
+    const uint32_t sbytes_block = (uint32_t)kDnRows * (uint32_t)NG * 2;
+    for (int t = 0; t < ntask; ++t) {
+      const int s = t % S;
+      if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
+      const int k0 = cu.kc * kDnKc;
+      const int kel = min(kDnKc, I - k0);
+      const uint32_t full = smem_u32(&ctl->full[s]);
+      uint8_t* st = smem + s * C::kStage;
+      const int wrow = meta.e[cu.slot] * H + cu.tile * kDnRows;
+      const int hrow = meta.row0[cu.slot] + cu.pass * kTok;
+      const uint32_t sbytes = s_mode == 0 ? (uint32_t)kDnRows * (kDnKc / G) * 2 : (s_mode == 1 ? sbytes_block : 0u);
+      if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(2 * kDnRows * 128) + sbytes + 2u * C::kPlane);
+      __syncwarp();
+      if (lane == 0) tma_load_3d(smem_u32(st + C::kW), &w_map, 0, wrow, k0 / 256, full);
+      if (lane == 1) tma_load_3d(smem_u32(st + C::kB), &hi_map, 0, hrow, k0 / 64, full);
+      if (lane == 2) tma_load_3d(smem_u32(st + C::kB + C::kPlane), &lo_map, 0, hrow, k0 / 64, full);
+      if (s_mode == 0) {
+        if (lane == 3) tma_load_2d(smem_u32(st + C::kS), &s_map, k0 / G, wrow, full);
+      } else if (s_mode == 1) {
+        if (lane == 3) bulk_g2s(smem_u32(st + C::kS), w2_s + (size_t)wrow * NG, sbytes_block, full);
+      } else {
+        constexpr int kPairs = kDnKc / G / 2;
+        for (int q = lane; q < kDnRows * kPairs; q += 32) {
+          const int rr = q / kPairs, pp = q - rr * kPairs;
+          if (pp * 2 * G < kel)
+            cp_async4(smem_u32(st + C::kS + rr * srow + pp * 4), w2_s + (size_t)(wrow + rr) * NG + k0 / G + 2 * pp);
+        }
+      }
+      cp_async_arrive_noinc(full);
+      ++issued;
+      cursor_next(cu, tiles, nkc, meta);
+    }
+    for (int t = max(0, issued - S); t < issued; ++t) {
+      const uint32_t full = smem_u32(&ctl->full[t % S]);
+      for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(full, (t / S) & 1); ++i) {
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumer warps ----------------
+  const int rg = warp & 7, kh = warp >> 3;
+  const int r = lane >> 2, c = lane & 3;
+  const int lr0 = rg * 16 + r;
+  const int a_off = (G == 64) ? 8 * c : 4 * c;
+  Cursor cu = cursor_at(q0, na, tiles, meta);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  int item = 0;
+  for (int t = 0; t < ntask; ++t) {
+    const int s = t % S;
+    if (cu.kc == 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] = 0.f;
+    }
+    const int ngt = min(kDnKc, I - cu.kc * kDnKc) / G;
+    if (!wait_phase(smem_u32(&ctl->full[s]), (t / S) & 1, abort_flag)) return;
+    const uint8_t* st = smem + s * C::kStage;
+    const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
+    const int goff = s_mode == 1 ? cu.kc * (kDnKc / G) : 0;
+#pragma unroll
+    for (int j = 0; j < C::kGph; ++j) {
+      const int g = kh * C::kGph + j;
+      if (g < ngt) {
+        const int kb = g * (G / 2) + a_off;
+        const RowWords<G> a0 = lds_row<G>(st + C::kW + swz_off_rows(lr0, kb, kDnRows));
+        const RowWords<G> a8 = lds_row<G>(st + C::kW + swz_off_rows(lr0 + 8, kb, kDnRows));
+        BWords<G> b;
+        lds_b_swz<G>(st + C::kB, g, r, c, b.hi);
+        lds_b_swz<G>(st + C::kB + C::kPlane, g, r, c, b.lo);
+        down_group<G>(a0, a8, b, __half2float(sc[(lr0 * srow) / 2 + goff + g]),
+                      __half2float(sc[((lr0 + 8) * srow) / 2 + goff + g]), acc);
+      }
+    }
+    warp_arrive(smem_u32(&ctl->empty[s]), lane);
+    if (cu.kc == nkc - 1) {
+      const int buf = item & 1, use = item >> 1;
+      const int bi = buf * 8 + rg;
+      float4* rb = reinterpret_cast<float4*>(red + (size_t)buf * (C::kRed / 4)) + rg * 32 + lane;
+      if (kh == 1) {
+        if (use > 0 && !wait_phase(smem_u32(&ctl->red_empty[bi]), (use - 1) & 1, abort_flag)) return;
+        *rb = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        warp_arrive(smem_u32(&ctl->red_full[bi]), lane);
+      } else {
+        if (!wait_phase(smem_u32(&ctl->red_full[bi]), use & 1, abort_flag)) return;
+        const float4 o = *rb;
+        warp_arrive(smem_u32(&ctl->red_empty[bi]), lane);
+        const float v[4] = {acc[0] + o.x, acc[1] + o.y, acc[2] + o.z, acc[3] + o.w};
+        const int n = meta.n[cu.slot], row0 = meta.row0[cu.slot];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int hr = cu.tile * kDnRows + lr0 + (q >= 2 ? 8 : 0);
+          const int rr = cu.pass * kTok + 2 * c + (q & 1);
+          if (rr < n) y[(size_t)(row0 + rr) * H + hr] = v[q];
+        }
+      }
+      ++item;
+    }
+    cursor_next(cu, tiles, nkc, meta);
+  }
+}
+
 template <typename K>
 void set_smem(K kern, size_t bytes) {
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
@@ -850,6 +1058,60 @@ void launch_down(const __nv_bfloat16* h_hi, const __nv_bfloat16* h_lo, const int
   k<<<grid, kDownThreads, smem, st>>>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
 }
 
+// TMA-fed down projection; returns false (nothing launched) when the shape
+// or the tensor maps do not allow it.
+template <int G>
+bool launch_down_tma(const __nv_bfloat16* h_hi, const __nv_bfloat16* h_lo, long long R, const int32_t* offsets,
+                     const int32_t* active, const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, float* y,
+                     int grid, cudaStream_t st) {
+  if (I % 256 || H % kDnRows || R <= 0) return false;
+  const size_t smem = DnCfg<G>::smem(E);
+  if (smem > kMaxSmem) return false;
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  alignas(64) CUtensorMap wm, sm, hm, lm;
+  const cuuint32_t e3[3] = {1, 1, 1}, e2[2] = {1, 1};
+  {
+    const cuuint64_t dims[3] = {128, (cuuint64_t)E * H, (cuuint64_t)(I / 256)};
+    const cuuint64_t strides[2] = {(cuuint64_t)(I / 2), 128};
+    const cuuint32_t box[3] = {128, (cuuint32_t)kDnRows, 2};
+    if (enc(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(w2_q), dims, strides, box, e3,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  const __nv_bfloat16* planes[2] = {h_hi, h_lo};
+  CUtensorMap* pm[2] = {&hm, &lm};
+  for (int p = 0; p < 2; ++p) {
+    const cuuint64_t dims[3] = {64, (cuuint64_t)R, (cuuint64_t)(I / 64)};
+    const cuuint64_t strides[2] = {(cuuint64_t)I * 2, 128};
+    const cuuint32_t box[3] = {64, (cuuint32_t)kTok, 8};
+    if (enc(pm[p], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<__nv_bfloat16*>(planes[p]), dims, strides, box, e3,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  const int NG = I / G;
+  int s_mode = 2;
+  memset(&sm, 0, sizeof(sm));
+  if ((NG * 2) % 16 == 0) {
+    const cuuint64_t dims[2] = {(cuuint64_t)NG, (cuuint64_t)E * H};
+    const cuuint64_t strides[1] = {(cuuint64_t)NG * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)(kDnKc / G), (cuuint32_t)kDnRows};
+    if (enc(&sm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(w2_s), dims, strides, box, e2,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+      s_mode = 0;
+  }
+  if (s_mode == 2 && (size_t)kDnRows * NG * 2 <= (size_t)kDnScaleBytes &&
+      (reinterpret_cast<uintptr_t>(w2_s) & 15) == 0)
+    s_mode = 1;
+  auto k = ffn_down_tma_kernel<G>;
+  set_smem(k, smem);
+  k<<<grid, kGuThreads, smem, st>>>(wm, sm, hm, lm, s_mode, offsets, active, w2_s, H, I, E, y);
+  return true;
+}
+
 }  // namespace
 
 int ffn_device_error(bool reset) {
@@ -885,8 +1147,12 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                                                   st);
   if (s) return s;
   if (mid_event) cudaEventRecord(mid_event, st);
-  if (G == 64) launch_down<64>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
-  else launch_down<32>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+  const bool tma = G == 64 ? launch_down_tma<64>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st)
+                           : launch_down_tma<32>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+  if (!tma) {
+    if (G == 64) launch_down<64>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+    else launch_down<32>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+  }
   note_launches(2);
   return PHMOE_OK;
 }
