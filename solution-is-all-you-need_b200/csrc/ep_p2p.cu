@@ -389,7 +389,7 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
                            mid);
   else
     s = launch_ffn_decode(recv, x_dtype, lrow, loff, lact, w13_q, w13_s, w2_q, w2_s, (int)capr, c->H, epr, 1, I, G, h,
-                          y, st, mid);
+                          y, st, mid, (long long)T * k);  // a rank receives about the T*k rows it sends
   if (s) return s;
   mark(4);
   ep_return_kernel<<<sms * 4, kCopyThreads, 0, st>>>(y, loff, epr, ret_src, ret_row, world, c->rank, c->cap, c->H,

@@ -244,6 +244,58 @@ __device__ __forceinline__ void gateup_group(const RowWords<G>& g0, const RowWor
   }
 }
 
+// gateup_group for up to NB 8-token column blocks: the A fragments are
+// unpacked once and reused for every block b < nb (B of block b at
+// b_base + b * b_stride).
+template <int G, bool kTwo, int NB>
+__device__ __forceinline__ void gateup_group_mt(const RowWords<G>& g0, const RowWords<G>& g8,
+                                                const RowWords<G>& u0, const RowWords<G>& u8,
+                                                const uint8_t* b_base, int b_stride, int nb, float sg0, float sg8,
+                                                float su0, float su8, float (&acc_g)[NB][4], float (&acc_u)[NB][4]) {
+  uint32_t pg0[G / 32][4], pg8[G / 32][4], pu0[G / 32][4], pu8[G / 32][4];
+#pragma unroll
+  for (int w = 0; w < G / 32; ++w) {
+    unpack_word_biased(g0.w[w], pg0[w]);
+    unpack_word_biased(g8.w[w], pg8[w]);
+    unpack_word_biased(u0.w[w], pu0[w]);
+    unpack_word_biased(u8.w[w], pu8[w]);
+  }
+  const uint32_t ones[4] = {kBf16x2One, kBf16x2One, kBf16x2One, kBf16x2One};
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    if (b < nb) {
+      BWords<G> bw;
+      if constexpr (kTwo) lds_b_f32<G>(b_base + b * b_stride, bw);
+      else lds_b_plane<G>(b_base + b * b_stride, bw.hi);
+      float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f}, td[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int w = 0; w < G / 32; ++w) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int s = 2 * w + h;
+          const uint32_t ag[4] = {pg0[w][2 * h], pg8[w][2 * h], pg0[w][2 * h + 1], pg8[w][2 * h + 1]};
+          const uint32_t au[4] = {pu0[w][2 * h], pu8[w][2 * h], pu0[w][2 * h + 1], pu8[w][2 * h + 1]};
+          mma_bf16_16816(tg, ag, bw.hi[2 * s], bw.hi[2 * s + 1], tg);
+          mma_bf16_16816(tu, au, bw.hi[2 * s], bw.hi[2 * s + 1], tu);
+          mma_bf16_16816(td, ones, bw.hi[2 * s], bw.hi[2 * s + 1], td);
+          if constexpr (kTwo) {
+            mma_bf16_16816(tg, ag, bw.lo[2 * s], bw.lo[2 * s + 1], tg);
+            mma_bf16_16816(tu, au, bw.lo[2 * s], bw.lo[2 * s + 1], tu);
+            mma_bf16_16816(td, ones, bw.lo[2 * s], bw.lo[2 * s + 1], td);
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float d = -136.0f * td[q];
+        const float sg = q < 2 ? sg0 : sg8, su = q < 2 ? su0 : su8;
+        acc_g[b][q] = fmaf(sg, tg[q] + d, acc_g[b][q]);
+        acc_u[b][q] = fmaf(su, tu[q] + d, acc_u[b][q]);
+      }
+    }
+  }
+}
+
 // down partial of one group: acc += s * A.(B_hi + B_lo), A unpacked exactly.
 template <int G>
 __device__ __forceinline__ void down_group(const RowWords<G>& a0, const RowWords<G>& a8,
@@ -282,6 +334,7 @@ struct Meta {
   int* table;  // [na + 1]
 };
 
+template <int TB = kTok>  // tokens per item
 __device__ int build_meta(const int32_t* __restrict__ offsets, const int32_t* __restrict__ active, int tiles,
                           Meta m) {
   const int na = active[0];
@@ -298,7 +351,7 @@ __device__ int build_meta(const int32_t* __restrict__ offsets, const int32_t* __
     int carry = 0;
     for (int s0 = 0; s0 < na; s0 += 32) {
       const int s = s0 + lane;
-      const int v = s < na ? ((m.n[s] + kTok - 1) / kTok) * tiles : 0;
+      const int v = s < na ? ((m.n[s] + TB - 1) / TB) * tiles : 0;
       int incl = v;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
@@ -322,8 +375,10 @@ struct Cursor {
   int slot, tile, pass, kc, passes;
 };
 
-__device__ __forceinline__ int passes_of(int n) { return (n + kTok - 1) / kTok; }
+template <int TB = kTok>
+__device__ __forceinline__ int passes_of(int n) { return (n + TB - 1) / TB; }
 
+template <int TB = kTok>
 __device__ Cursor cursor_at(int q, int na, int tiles, const Meta& m) {
   int lo = 0, hi = na;  // table[lo] <= q < table[hi]
   while (hi - lo > 1) {
@@ -333,7 +388,7 @@ __device__ Cursor cursor_at(int q, int na, int tiles, const Meta& m) {
   }
   Cursor c;
   c.slot = lo;
-  c.passes = passes_of(m.n[lo]);
+  c.passes = passes_of<TB>(m.n[lo]);
   const int local = q - m.table[lo];
   c.tile = local / c.passes;
   c.pass = local - c.tile * c.passes;
@@ -341,6 +396,7 @@ __device__ Cursor cursor_at(int q, int na, int tiles, const Meta& m) {
   return c;
 }
 
+template <int TB = kTok>
 __device__ __forceinline__ void cursor_next(Cursor& c, int tiles, int nkc, const Meta& m) {
   if (++c.kc < nkc) return;
   c.kc = 0;
@@ -349,7 +405,7 @@ __device__ __forceinline__ void cursor_next(Cursor& c, int tiles, int nkc, const
   if (++c.tile < tiles) return;
   c.tile = 0;
   ++c.slot;                          // may step one past the last slot: arrays hold E + 1 entries
-  c.passes = passes_of(m.n[c.slot]);
+  c.passes = passes_of<TB>(m.n[c.slot]);
 }
 
 __device__ __forceinline__ void cta_range(int total, int& q0, int& q1) {
@@ -390,6 +446,13 @@ struct RbCfg {
     return 1024 + (size_t)kStages * kStage + 2 * kRed + sizeof(RbCtl<kStages>) + (size_t)(4 * E + 4) * 4;
   }
 };
+
+// Byte offset of (row R of a `rows`-row box of 128-byte K-chunks, byte kb of
+// the task's K slice) as TMA writes it with the 128-byte swizzle.
+__device__ __forceinline__ int swz_off_rows(int R, int kb, int rows) {
+  const int c0 = kb & 127;
+  return ((kb >> 7) * rows + R) * 128 + ((((c0 >> 4) ^ (R & 7)) << 4) | (c0 & 15));
+}
 
 // Byte offset of (row R of a 64-row box, byte kb of the task's K slice).
 __device__ __forceinline__ int swz_off64(int R, int kb) {
@@ -753,6 +816,260 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
 }
 
 // ---------------------------------------------------------------------------
+// gate/up + SwiGLU, multi-token form (batches with >= ~12 rows per expert)
+// ---------------------------------------------------------------------------
+// As the row-block form, but an item covers up to 32 tokens of one expert:
+// each lane unpacks its A fragments once per group and applies them to every
+// 8-token column block of the item (up to four mma.sync per fragment and row
+// pair), so the unpack cost is shared by up to 32 tokens. Item = (expert, 64
+// gate rows + the 64 matching up rows, block of up to 32 tokens); task = one
+// 512-element K chunk. Eight consumer warps = 4 row groups x 2 K halves (288
+// threads leave registers for the accumulators). Each warp keeps one
+// accumulator per 128-element K quarter of the task, and the item's end sum
+// is ((q0 + q1) + q2) + q3 like the row-block form's, so both forms give
+// bit-identical h for every row: which one runs never changes the result.
+constexpr int kMtConsumers = 8;
+constexpr int kMtThreads = (kMtConsumers + 1) * 32;
+constexpr int kMtRows = 64;
+constexpr int kMtKc = 512;
+constexpr int kMtTok = 32;
+constexpr int kMtNb = kMtTok / kTok;  // 8-token column blocks per item
+// expected rows per expert from which a launch takes the multi-token form
+#ifndef PHMOE_DECODE_MT_MIN_ROWS
+#define PHMOE_DECODE_MT_MIN_ROWS 20
+#endif
+constexpr int kMtMinRowsPerExpert = PHMOE_DECODE_MT_MIN_ROWS;
+
+template <int S>
+struct MtCtl {
+  uint64_t full[S];
+  uint64_t empty[S];
+  uint64_t red_full[4];   // [rg]: the K-half-1 warp has written its partials
+  uint64_t red_empty[4];  // [rg]: the K-half-0 warp has read them
+  int abort_flag;
+};
+
+template <int G, typename XT>
+struct MtCfg {
+  static constexpr bool kF32 = std::is_same<XT, float>::value;
+  static constexpr int kGpq = 128 / G;                        // groups per K quarter per task
+  static constexpr int kBlock = 2 * kMtRows * 128;            // one 64-row box of 2 K-chunks (16 KB)
+  static constexpr int kScaleRow = kMtKc / G * 2;
+  static constexpr int kPairs = kMtKc / G / 2;
+  static constexpr int kBRowBytes = kMtKc * (int)sizeof(XT);
+  static constexpr int kBPad = (G == 32 && !kF32) ? 64 : 16;
+  static constexpr int kBStride = kBRowBytes + kBPad;
+  static constexpr int kW = 0;                                // [gate box][up box]
+  static constexpr int kS = 2 * kBlock;                       // [128 rows][kScaleRow]
+  static constexpr int kB = kS + 2 * kMtRows * kScaleRow;     // [32 tokens][kBStride]
+  static constexpr int kStage = (kB + kMtTok * kBStride + 1023) / 1024 * 1024;
+  static constexpr int kRed = 4 * 32 * (8 * kMtNb) * 4;       // [rg][lane][nb][8] floats
+  // three stages where they fit next to the metadata of up to 256 experts
+  static constexpr int kStages = (1024 + 3 * kStage + kRed + 256 + (4 * 256 + 4) * 4 <= 232448) ? 3 : 2;
+  static constexpr size_t smem(int E) {
+    return 1024 + (size_t)kStages * kStage + kRed + sizeof(MtCtl<kStages>) + (size_t)(4 * E + 4) * 4;
+  }
+};
+
+template <int G, typename XT>
+__global__ void __launch_bounds__(kMtThreads, 1)
+ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int box_chunks,
+                     const __grid_constant__ CUtensorMap s_map, int s_tma, const XT* __restrict__ x,
+                     const int32_t* __restrict__ row_token, const int32_t* __restrict__ offsets,
+                     const int32_t* __restrict__ active, const uint16_t* __restrict__ w13_s, int H, int I, int E,
+                     __nv_bfloat16* __restrict__ h_hi, __nv_bfloat16* __restrict__ h_lo) {
+  using C = MtCfg<G, XT>;
+  constexpr int S = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* red = reinterpret_cast<float*>(smem + S * C::kStage);
+  MtCtl<S>* ctl = reinterpret_cast<MtCtl<S>*>(smem + S * C::kStage + C::kRed);
+  int* mbase = reinterpret_cast<int*>(ctl + 1);
+  const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
+  volatile int* abort_flag = &ctl->abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = (I + kMtRows - 1) / kMtRows;
+  const int NG = H / G;
+  const int nkc = (H + kMtKc - 1) / kMtKc;
+  const int na = active[0];
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(&ctl->full[s]), 1 + 32);
+      mbar_init(smem_u32(&ctl->empty[s]), kMtConsumers);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(smem_u32(&ctl->red_full[i]), 1);
+      mbar_init(smem_u32(&ctl->red_empty[i]), 1);
+    }
+    ctl->abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  const int total = build_meta<kMtTok>(offsets, active, tiles, meta);
+  int q0, q1;
+  cta_range(total, q0, q1);
+  const int ntask = (q1 - q0) * nkc;
+  if (ntask == 0) return;
+
+  if (warp == kMtConsumers) {
+    // ---------------- producer warp ----------------
+    Cursor cu = cursor_at<kMtTok>(q0, na, tiles, meta);
+    auto token = [&](const Cursor& k) -> int {  // lane holds the token id of block row `lane`
+      const int rr = k.pass * kMtTok + lane;
+      return rr < meta.n[k.slot] ? __ldg(row_token + meta.row0[k.slot] + rr) : -1;
+    };
+    int tok = token(cu);
+    int issued = 0;
+    for (int t = 0; t < ntask; ++t) {
+      const int s = t % S;
+      if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
+      Cursor nx = cu;
+      cursor_next<kMtTok>(nx, tiles, nkc, meta);
+      const int tok_next = (t + 1 < ntask && nx.kc == 0) ? token(nx) : tok;
+      const int k0 = cu.kc * kMtKc;
+      const int kel = min(kMtKc, H - k0);
+      const int nt = min(kMtTok, meta.n[cu.slot] - cu.pass * kMtTok);
+      const uint32_t full = smem_u32(&ctl->full[s]);
+      uint8_t* st = smem + s * C::kStage;
+      if (lane == 0)
+        mbar_arrive_expect_tx(full, 2u * (uint32_t)(box_chunks * kMtRows * 128) + (uint32_t)(nt * kel * (int)sizeof(XT)) +
+                                        (s_tma ? 2u * kMtRows * C::kScaleRow : 0u));
+      __syncwarp();
+      const int grow = meta.e[cu.slot] * 2 * I + cu.tile * kMtRows;  // first gate row; up rows are I further
+      if (lane < 2) {
+        const uint32_t dst = smem_u32(st + C::kW + lane * C::kBlock);
+        const int row = grow + lane * I;
+        if (map3d) {
+          tma_load_3d(dst, &w13_map, 0, row, k0 / 256, full);
+        } else {
+          for (int ch = 0; ch < box_chunks; ++ch)
+            tma_load_2d(dst + ch * kMtRows * 128, &w13_map, k0 / 2 + ch * 128, row, full);
+        }
+      }
+      if (lane < nt)  // lane n < 32 holds the token id of block row n
+        bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), x + (size_t)tok * H + k0, kel * (int)sizeof(XT), full);
+      if (s_tma) {
+        if (lane == 2 || lane == 3)
+          tma_load_2d(smem_u32(st + C::kS + (lane - 2) * kMtRows * C::kScaleRow), &s_map, k0 / G,
+                      grow + (lane - 2) * I, full);
+      } else {
+        for (int q = lane; q < 2 * kMtRows * C::kPairs; q += 32) {
+          const int rr = q / C::kPairs, pp = q - rr * C::kPairs;
+          const int i = cu.tile * kMtRows + (rr & (kMtRows - 1));
+          if (pp * 2 * G < kel && i < I) {
+            const size_t srow = (size_t)grow + (rr >= kMtRows ? I : 0) + (rr & (kMtRows - 1));
+            cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + srow * NG + k0 / G + 2 * pp);
+          }
+        }
+      }
+      cp_async_arrive_noinc(full);
+      ++issued;
+      tok = tok_next;
+      cu = nx;
+    }
+    for (int t = max(0, issued - S); t < issued; ++t) {
+      const uint32_t full = smem_u32(&ctl->full[t % S]);
+      for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(full, (t / S) & 1); ++i) {
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumer warps ----------------
+  const int rg = warp & 3, kh = warp >> 2;
+  const int r = lane >> 2, c = lane & 3;
+  constexpr int kGpq = C::kGpq;
+  const int R0 = rg * 16 + r;
+  constexpr int kScH = C::kScaleRow / 2;
+  Cursor cu = cursor_at<kMtTok>(q0, na, tiles, meta);
+  float acc_g[2][kMtNb][4], acc_u[2][kMtNb][4];  // [K quarter of this half][block][fragment]
+  int item = 0;
+  for (int t = 0; t < ntask; ++t) {
+    const int s = t % S;
+    if (cu.kc == 0) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int b = 0; b < kMtNb; ++b)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) { acc_g[h][b][q] = 0.f; acc_u[h][b][q] = 0.f; }
+    }
+    const int nb = (min(kMtTok, meta.n[cu.slot] - cu.pass * kMtTok) + kTok - 1) / kTok;  // warp-uniform
+    const int ngt = min(kMtKc, H - cu.kc * kMtKc) / G;
+    if (!wait_phase(smem_u32(&ctl->full[s]), (t / S) & 1, abort_flag)) return;
+    const uint8_t* st = smem + s * C::kStage;
+    const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll 1
+      for (int j = 0; j < kGpq; ++j) {
+        const int g = (2 * kh + h) * kGpq + j;  // group within the task
+        if (g < ngt) {
+          const int kb = (G == 64) ? g * 32 + 8 * c : g * 16 + 4 * c;
+          const RowWords<G> ag0 = lds_row<G>(st + C::kW + swz_off64(R0, kb));
+          const RowWords<G> ag8 = lds_row<G>(st + C::kW + swz_off64(R0 + 8, kb));
+          const RowWords<G> au0 = lds_row<G>(st + C::kW + C::kBlock + swz_off64(R0, kb));
+          const RowWords<G> au8 = lds_row<G>(st + C::kW + C::kBlock + swz_off64(R0 + 8, kb));
+          const float sg0 = __half2float(sc[R0 * kScH + g]), sg8 = __half2float(sc[(R0 + 8) * kScH + g]);
+          const float su0 = __half2float(sc[(kMtRows + R0) * kScH + g]);
+          const float su8 = __half2float(sc[(kMtRows + R0 + 8) * kScH + g]);
+          const int ob =
+              C::kB + r * C::kBStride + g * G * (int)sizeof(XT) + (G == 64 ? 16 : 8) * c * (int)sizeof(XT);
+          gateup_group_mt<G, C::kF32, kMtNb>(ag0, ag8, au0, au8, st + ob, kTok * C::kBStride, nb, sg0, sg8, su0,
+                                             su8, acc_g[h], acc_u[h]);
+        }
+      }
+    }
+    warp_arrive(smem_u32(&ctl->empty[s]), lane);
+    if (cu.kc == nkc - 1) {
+      float4* rb = reinterpret_cast<float4*>(red) + ((size_t)rg * 32 + lane) * (2 * kMtNb);
+      if (kh == 0) {  // hands q0 + q1 to the K-half-1 warp
+        if (item > 0 && !wait_phase(smem_u32(&ctl->red_empty[rg]), (item - 1) & 1, abort_flag)) return;
+#pragma unroll
+        for (int b = 0; b < kMtNb; ++b) {
+          if (b < nb) {
+            rb[2 * b] = make_float4(acc_g[0][b][0] + acc_g[1][b][0], acc_g[0][b][1] + acc_g[1][b][1],
+                                    acc_g[0][b][2] + acc_g[1][b][2], acc_g[0][b][3] + acc_g[1][b][3]);
+            rb[2 * b + 1] = make_float4(acc_u[0][b][0] + acc_u[1][b][0], acc_u[0][b][1] + acc_u[1][b][1],
+                                        acc_u[0][b][2] + acc_u[1][b][2], acc_u[0][b][3] + acc_u[1][b][3]);
+          }
+        }
+        warp_arrive(smem_u32(&ctl->red_full[rg]), lane);
+      } else {  // ((q0 + q1) + q2) + q3, then SwiGLU
+        if (!wait_phase(smem_u32(&ctl->red_full[rg]), item & 1, abort_flag)) return;
+        const int n = meta.n[cu.slot], row0 = meta.row0[cu.slot];
+#pragma unroll
+        for (int b = 0; b < kMtNb; ++b) {
+          if (b < nb) {
+            const float4 og = rb[2 * b], ou = rb[2 * b + 1];
+            const float gs[4] = {(og.x + acc_g[0][b][0]) + acc_g[1][b][0], (og.y + acc_g[0][b][1]) + acc_g[1][b][1],
+                                 (og.z + acc_g[0][b][2]) + acc_g[1][b][2], (og.w + acc_g[0][b][3]) + acc_g[1][b][3]};
+            const float us[4] = {(ou.x + acc_u[0][b][0]) + acc_u[1][b][0], (ou.y + acc_u[0][b][1]) + acc_u[1][b][1],
+                                 (ou.z + acc_u[0][b][2]) + acc_u[1][b][2], (ou.w + acc_u[0][b][3]) + acc_u[1][b][3]};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int i = cu.tile * kMtRows + R0 + (q >= 2 ? 8 : 0);
+              const int rr = cu.pass * kMtTok + b * kTok + 2 * c + (q & 1);
+              if (rr < n && i < I) {
+                const float hv = silu_f32(gs[q]) * us[q];
+                const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
+                const __nv_bfloat16 lb = __float2bfloat16_rn(hv - __bfloat162float(hb));
+                const size_t o = (size_t)(row0 + rr) * I + i;
+                h_hi[o] = hb;
+                h_lo[o] = lb;
+              }
+            }
+          }
+        }
+        warp_arrive(smem_u32(&ctl->red_empty[rg]), lane);
+      }
+      ++item;
+    }
+    cursor_next<kMtTok>(cu, tiles, nkc, meta);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // down projection, TMA-fed form (I % 256 == 0)
 // ---------------------------------------------------------------------------
 // Item = (expert, 128 output rows, pass of 8 tokens); task = one 512-element
@@ -790,11 +1107,6 @@ struct DnCfg {
     return 1024 + (size_t)kStages * kStage + 2 * kRed + sizeof(DnCtl<kStages>) + (size_t)(4 * E + 4) * 4;
   }
 };
-
-__device__ __forceinline__ int swz_off_rows(int R, int kb, int rows) {
-  const int c0 = kb & 127;
-  return ((kb >> 7) * rows + R) * 128 + ((((c0 >> 4) ^ (R & 7)) << 4) | (c0 & 15));
-}
 
 // B words of group g (within a task) for token row r from one h plane laid
 // out [64-element block][8 rows][128 B] with 128-byte swizzle.
@@ -1012,6 +1324,40 @@ int make_w13_map(CUtensorMap* map, const uint8_t* w13_q, long long rows, int H, 
 
 constexpr size_t kMaxSmem = 227 * 1024;
 
+// Tensor map over the fp16 scales [E*2I rows][H/G] for boxes of one task's
+// groups x `rows` rows; false when the rows are not 16-byte aligned.
+bool make_scale_map(CUtensorMap* map, const uint16_t* w13_s, long long rows, int H, int G, int kc, int box_rows) {
+  if (((H / G) * 2) % 16) return false;
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)(H / G), (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)(H / G) * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)(kc / G), (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(w13_s), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int G, typename XT>
+int launch_gateup_mt(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
+                     const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
+                     __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
+  const size_t smem = MtCfg<G, XT>::smem(E);
+  if (smem > kMaxSmem) return PHMOE_ERR_UNSUPPORTED;
+  const int box_chunks = std::min(H, kMtKc) / 256;
+  alignas(64) CUtensorMap map, smap;
+  const int mode = make_w13_map(&map, w13_q, (long long)E * 2 * I, H, box_chunks, kMtRows);
+  if (mode < 0) return PHMOE_ERR_CUDA;
+  const int s_tma = make_scale_map(&smap, w13_s, (long long)E * 2 * I, H, G, kMtKc, kMtRows) ? 1 : 0;
+  if (!s_tma) memset(&smap, 0, sizeof(smap));
+  auto k = ffn_gateup_mt_kernel<G, XT>;
+  set_smem(k, smem);
+  k<<<grid, kMtThreads, smem, st>>>(map, mode, box_chunks, smap, s_tma, static_cast<const XT*>(x), row_token, offsets,
+                                    active, w13_s, H, I, E, h_hi, h_lo);
+  return PHMOE_OK;
+}
+
 template <int G, typename XT>
 int launch_gateup_rb(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
                      const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
@@ -1128,7 +1474,7 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       const int32_t* offsets, const int32_t* active, const uint8_t* w13_q,
                       const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T,
                       int H, int E, int top_k, int I, int G, float* h, float* y,
-                      cudaStream_t st, cudaEvent_t mid_event) {
+                      cudaStream_t st, cudaEvent_t mid_event, long long rows_hint) {
   const long long R = (long long)T * top_k;
   if (R == 0) return PHMOE_OK;
   if (G != 32 && G != 64) return PHMOE_ERR_UNSUPPORTED;
@@ -1136,15 +1482,32 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
   __nv_bfloat16* h_lo = h_hi + (size_t)R * I;
   const int grid = device_sm_count();
   const bool f32 = x_dtype == PHMOE_DTYPE_F32;
-  int s;
-  if (G == 64)
-    s = f32 ? launch_gateup_rb<64, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
-            : launch_gateup_rb<64, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid,
-                                                  st);
-  else
-    s = f32 ? launch_gateup_rb<32, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
-            : launch_gateup_rb<32, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid,
-                                                  st);
+  // multi-token gate/up items from kMtMinRowsPerExpert expected rows per
+  // expert (each unpacked weight then feeds two or more 8-token MMA blocks);
+  // both forms give bit-identical h, so this choice is for speed only
+  const long long rows = rows_hint >= 0 ? rows_hint : R;
+  const bool mt = rows >= (long long)kMtMinRowsPerExpert * E;
+  int s = PHMOE_ERR_UNSUPPORTED;
+  if (mt) {
+    if (G == 64)
+      s = f32 ? launch_gateup_mt<64, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
+              : launch_gateup_mt<64, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo,
+                                                    grid, st);
+    else
+      s = f32 ? launch_gateup_mt<32, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
+              : launch_gateup_mt<32, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo,
+                                                    grid, st);
+  }
+  if (s != PHMOE_OK) {  // 8-token items (small batches, or the multi-token form did not fit)
+    if (G == 64)
+      s = f32 ? launch_gateup_rb<64, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
+              : launch_gateup_rb<64, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo,
+                                                    grid, st);
+    else
+      s = f32 ? launch_gateup_rb<32, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
+              : launch_gateup_rb<32, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo,
+                                                    grid, st);
+  }
   if (s) return s;
   if (mid_event) cudaEventRecord(mid_event, st);
   const bool tma = G == 64 ? launch_down_tma<64>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st)

@@ -22,7 +22,7 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       const int32_t* offsets, const int32_t* active, const uint8_t* w13_q,
                       const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T,
                       int H, int E, int top_k, int I, int G, float* h, float* y,
-                      cudaStream_t st, cudaEvent_t mid_event = nullptr);
+                      cudaStream_t st, cudaEvent_t mid_event = nullptr, long long rows_hint = -1);
 
 // Prefill form (tcgen05 grouped GEMMs): bf16 x only; h is R*I*4 bytes of
 // scratch and y doubles as the gathered activations until the down GEMM.

@@ -149,3 +149,52 @@ def test_prefill_qwen3_and_auto_path(cuda_device, T):
     assert mx2 <= O.MAX_ABS_TOL and mr2 <= O.MEAN_REL_TOL
     if T * 8 >= 64 * 128:  # auto takes the prefill GEMMs from 64 rows per expert
         assert torch.equal(out_auto, out)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [1024, 700])
+def test_decode_multi_token_items(cuda_device, T):
+    """Decode path at 40-64 rows per expert: gate/up items of up to 32 tokens
+    (each unpacked weight feeds up to four 8-token MMA blocks), ragged last
+    blocks included."""
+    mx, mr, _ = _layer_vs_torch(cuda_device, 128, 2048, 8, 768, 64, T, 13, "decode")
+    assert mx <= O.MAX_ABS_TOL and mr <= O.MEAN_REL_TOL, (mx, mr)
+    assert pm.load_library().phmoe_device_error(1) == 0
+
+
+@pytest.mark.gpu
+def test_decode_multi_token_fp32_activations(cuda_device):
+    """fp32 activations (hi/lo bf16 split) through the multi-token items."""
+    dev = cuda_device
+    E, H, k, I, G, T = 128, 2048, 8, 768, 64, 512
+    wr, packed = _packed_layer(E, H, I, G, 17, dev)
+    wr = wr.float()
+    x = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(18))
+    out, idx, w = pm.moe_layer(x, wr, *packed, k, group_size=G, path="decode", return_routing=True)
+    offsets, row_token, inv, _ = pm.dispatch(idx, E)
+    ref = layer_torch(x, idx, w, offsets, row_token, inv, packed, G)
+    torch.cuda.synchronize()
+    mx, mr = O.parity_stats(out.cpu().numpy(), ref.cpu().numpy())
+    assert mx <= 1e-3 and mr <= 1e-4, (mx, mr)  # fp32 in, fp32 out: ~16-bit operands
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_decode_batch_invariance(cuda_device, dtype):
+    """A token's decode-path output does not depend on the batch around it:
+    the first 8 tokens of a 1024-token batch (64 rows per expert: multi-token
+    gate/up items, block router) give bit-identical rows when run alone (8-token
+    items, per-token router)."""
+    dev = cuda_device
+    E, H, k, I, G, T = 128, 2048, 8, 768, 64, 1024
+    wr, packed = _packed_layer(E, H, I, G, 23, dev)
+    x = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(24)).to(dtype)
+    wr = wr.to(dtype)
+    big, idx_big, _ = pm.moe_layer(x, wr, *packed, k, group_size=G, path="decode", return_routing=True)
+    for n in (1, 8, 37):
+        small, idx_small, _ = pm.moe_layer(x[:n], wr, *packed, k, group_size=G, path="decode",
+                                           return_routing=True)
+        torch.cuda.synchronize()
+        assert torch.equal(idx_small, idx_big[:n]), n
+        assert torch.equal(small, big[:n]), n
+    assert pm.load_library().phmoe_device_error(1) == 0
