@@ -49,9 +49,12 @@
 // intermediate h are split into bf16 hi + lo parts (two MMAs each), keeping
 // ~16 significant bits.
 //
-// Every mbarrier wait is bounded: after kSpinLimit polls a warp raises the
-// CTA's abort flag and the device error word (phmoe_device_error) and all
-// warps leave; the producer first waits (bounded) for its copies in flight.
+// Every mbarrier wait is bounded: a waiting warp sleeps inside try_wait (a
+// suspend-time hint, woken when the phase completes, so waiting warps take no
+// issue slots from computing ones); after kWaitLimitNs of %globaltimer time
+// (or kSpinLimit tries) it raises the CTA's abort flag and the device error
+// word (phmoe_device_error) and all warps leave; the producer first waits
+// (bounded) for its copies in flight.
 #include <cuda.h>  // CUtensorMap (types only; the encoder is fetched from the driver at run time)
 #include <string.h>
 
@@ -69,6 +72,8 @@ constexpr int kGuThreads = (kConsumers + 1) * 32;  // + 1 producer warp
 constexpr int kDownThreads = 16 * 32;
 constexpr int kTok = 8;                         // tokens per pass (the MMA N dimension)
 constexpr uint32_t kSpinLimit = 1u << 24;       // try_wait polls before giving up
+constexpr uint32_t kSuspendNs = 20000;            // try_wait suspend-time hint
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -102,6 +107,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "=r"(done) : "r"(bar), "r"(parity) : "memory");
   return done != 0;
 }
+// As mbar_try_wait, suspending up to suspend_ns inside the instruction (the
+// thread resumes as soon as the phase completes).
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity, uint32_t suspend_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(done) : "r"(bar), "r"(parity), "r"(suspend_ns) : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait for copies still in flight when a producer leaves.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait_suspend(bar, parity, kSuspendNs) && global_ns() - t0 <= kWaitLimitNs) {
+  }
+}
 // Arrive on `bar` once every cp.async this thread issued so far has landed.
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
@@ -126,9 +153,12 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 
 // Bounded wait on a barrier phase. Returns false when this CTA aborts.
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 255u && *abort_flag) return false;
+    if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitLimitNs) break;
   }
   *abort_flag = 1;
   atomicExch(&g_ffn_error, 1);
@@ -559,8 +589,7 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
     }
     for (int t = max(0, issued - S); t < issued; ++t) {
       const uint32_t full = smem_u32(&ctl->full[t % S]);
-      for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(full, (t / S) & 1); ++i) {
-      }
+      drain_wait(full, (t / S) & 1);
     }
     return;
   }
@@ -969,8 +998,7 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
     }
     for (int t = max(0, issued - S); t < issued; ++t) {
       const uint32_t full = smem_u32(&ctl->full[t % S]);
-      for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(full, (t / S) & 1); ++i) {
-      }
+      drain_wait(full, (t / S) & 1);
     }
     return;
   }
@@ -1205,8 +1233,7 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
     }
     for (int t = max(0, issued - S); t < issued; ++t) {
       const uint32_t full = smem_u32(&ctl->full[t % S]);
-      for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(full, (t / S) & 1); ++i) {
-      }
+      drain_wait(full, (t / S) & 1);
     }
     return;
   }

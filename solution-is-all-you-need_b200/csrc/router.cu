@@ -88,11 +88,26 @@ router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T,
   const int t0 = blockIdx.y * TT;
   const int nt = min(TT, T - t0);
   {
+    // all loads of a round are issued before its stores, so staging the tile
+    // costs one memory round trip per 8 vectors a thread, not one per vector
     constexpr int kVec = 16 / sizeof(XT);
+    constexpr int kUnroll = 8;
     const int nvec = nt * H / kVec;  // H % 8 == 0, so rows are whole vectors
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t0 * H);
     uint4* dst = reinterpret_cast<uint4*>(xs);
-    for (int i = threadIdx.x; i < nvec; i += blockDim.x) dst[i] = __ldg(src + i);
+    for (int i0 = threadIdx.x; i0 < nvec; i0 += blockDim.x * kUnroll) {
+      uint4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int i = i0 + u * blockDim.x;
+        if (i < nvec) v[u] = __ldg(src + i);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int i = i0 + u * blockDim.x;
+        if (i < nvec) dst[i] = v[u];
+      }
+    }
   }
   __syncthreads();
   if (e >= E) return;
