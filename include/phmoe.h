@@ -249,6 +249,30 @@ int phmoe_moe_layer_noalloc(const void* x, int x_dtype, const void* router_w, in
                             int32_t* topk_idx_out, float* topk_w_out, void* stream);
 
 /*
+ * MoE layer with shared experts (Qwen2-MoE's gated shared expert,
+ * transformers 5.5.0 models/qwen2_moe/modeling_qwen2_moe.py
+ * Qwen2MoeSparseMoeBlock.forward: out = routed + sigmoid(x . w_sg) * shared(x);
+ * DeepSeek-style ungated shared experts with routed_scaling_factor).
+ *
+ * The packed expert tensors hold E + num_shared experts: the E routed ones,
+ * then the shared expert split along its intermediate dimension into
+ * num_shared experts of size I (a shared expert of size m * I is the sum of
+ * those m SwiGLU experts). Every token is routed to its top_k experts
+ * (weights times routed_scale) and to all num_shared shared experts with
+ * weight sigmoid(x . shared_gate_w) (shared_gate_w: [H] in w_dtype), or 1
+ * when shared_gate_w is NULL. topk_idx_out / topk_w_out (optional, [T, top_k])
+ * receive the routed choice before scaling. Other arguments and limits as
+ * phmoe_moe_layer; workspace_bytes >= phmoe_workspace_size_shared(...).
+ */
+size_t phmoe_workspace_size_shared(int T, int H, int E, int top_k, int I, int num_shared, int path);
+int phmoe_moe_layer_shared(const void* x, int x_dtype, const void* router_w, int w_dtype,
+                           const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
+                           const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
+                           int group_size, int renormalize, int num_shared, const void* shared_gate_w,
+                           float routed_scale, int path, void* out, int32_t* topk_idx_out,
+                           float* topk_w_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Symmetric int4 group quantiser on the GPU (load-time utility; the
  * reference has no quantiser and reads pre-quantised GGUF files):
  * scale = fp16(absmax(group)/7), q = clamp(rint(w/scale), -8, 7).
@@ -256,6 +280,33 @@ int phmoe_moe_layer_noalloc(const void* x, int x_dtype, const void* router_w, in
  */
 int phmoe_quantize_int4(const void* w, int w_dtype, long long rows, int K, int group_size,
                         uint8_t* packed, uint16_t* scales, void* stream);
+
+/*
+ * GGUF importers (load-time): llama.cpp-quantised expert tensors straight
+ * into the packed layout on the GPU, without a bf16 round trip. They replace
+ * the dequantise-at-load step of the reference's GGUF loader
+ * (python/phantom/loader/gguf_loader.py:799-805 -> dequantize_tensor_cuda,
+ * gguf_loader.py:538), whose Q4_0 and Q4_K semantics they follow
+ * (gguf_loader.py:588-596 and 648-666). `blocks` holds `rows` rows of K
+ * elements each as consecutive GGUF blocks (a GGUF tensor's data as stored:
+ * K is its innermost dimension).
+ *
+ * phmoe_gguf_q4_0_to_packed: Q4_0 (18-byte blocks of 32) -> packed int4 with
+ *   group_size 32, bit-exact: the same values, nibbles re-ordered, d copied
+ *   as the fp16 group scale. K % 32 == 0; packed 16-byte aligned.
+ * phmoe_gguf_q4_k_to_packed: Q4_K (144-byte super-blocks of 256) -> each
+ *   element dequantised in fp32 as the reference does, then re-quantised with
+ *   phmoe_quantize_int4's rule (group_size 32 or 64). Q4_K is asymmetric
+ *   (scale and min per 32 elements), so this step is lossy: the error per
+ *   element is at most half a step of the new group scale. K % 256 == 0.
+ * phmoe_gguf_q4_k_dequantize: Q4_K -> fp32 values (n elements, n % 256 == 0),
+ *   the reference's dequantised weights, for checks.
+ */
+int phmoe_gguf_q4_0_to_packed(const void* blocks, long long rows, int K, uint8_t* packed,
+                              uint16_t* scales, void* stream);
+int phmoe_gguf_q4_k_to_packed(const void* blocks, long long rows, int K, int group_size,
+                              uint8_t* packed, uint16_t* scales, void* stream);
+int phmoe_gguf_q4_k_dequantize(const void* blocks, long long n, float* out, void* stream);
 
 /*
  * Instrumentation for benchmarks (no counterpart in the reference, whose

@@ -140,6 +140,42 @@ def q4_0_to_packed(raw: bytes, rows: int, K: int):
     return pack_nibbles(q), scales
 
 
+def dequantize_q4_k(raw: bytes, n_elems: int) -> np.ndarray:
+    """GGUF Q4_K super-blocks -> fp32 (restates ``dequantize_tensor_cuda``,
+    gguf_loader.py:648-666, the dequantiser the reference's model loader runs
+    at gguf_loader.py:799; that function's fp32 values before the bf16 cast).
+
+    Super-block of 256 elements, 144 bytes: fp16 d, fp16 dmin, 12 bytes of
+    packed 6-bit (scale, min) pairs for 8 sub-blocks of 32, 128 bytes of
+    nibbles; 32-byte chunk c holds sub-block 2c in its low and 2c+1 in its
+    high nibbles. value = fp32(d * sc_j) * q - fp32(dmin * m_j), each product
+    and the difference rounded to fp32. (The reference's CPU branch,
+    gguf_loader.py:453-489, orders the nibbles differently; the loader does
+    not use it for this path.)
+    """
+    nb = n_elems // 256
+    blk = np.frombuffer(raw[: nb * 144], dtype=np.uint8).reshape(nb, 144)
+    d = blk[:, 0:2].copy().view(np.float16).astype(F32)       # [nb, 1]
+    dmin = blk[:, 2:4].copy().view(np.float16).astype(F32)
+    s = blk[:, 4:16].astype(np.int32)
+    sc = np.concatenate([s[:, 0:4] & 0x3F, (s[:, 8:12] & 0x0F) | ((s[:, 0:4] >> 6) << 4)], axis=1)
+    mn = np.concatenate([s[:, 4:8] & 0x3F, (s[:, 8:12] >> 4) | ((s[:, 4:8] >> 6) << 4)], axis=1)
+    d_sc = (d * sc.astype(F32)).astype(F32)[:, :, None]       # [nb, 8, 1]
+    dm_m = (dmin * mn.astype(F32)).astype(F32)[:, :, None]
+    qs = blk[:, 16:].reshape(nb, 4, 1, 32)
+    q = np.concatenate([qs & 0x0F, qs >> 4], axis=2).reshape(nb, 8, 32).astype(F32)
+    return ((d_sc * q).astype(F32) - dm_m).astype(F32).reshape(-1)[:n_elems]
+
+
+def q4_k_to_packed(raw: bytes, rows: int, K: int, group: int = 32):
+    """Import a GGUF Q4_K [rows, K] tensor into (packed, scales): dequantise
+    as :func:`dequantize_q4_k`, then re-quantise with :func:`quantize_int4`
+    (the symmetric format cannot hold Q4_K's per-sub-block minimum, so this
+    import is lossy, unlike :func:`q4_0_to_packed`)."""
+    w = dequantize_q4_k(raw, rows * K).reshape(rows, K)
+    return quantize_int4(w, group)
+
+
 # ---------------------------------------------------------------------------
 # fixed-order fp32 arithmetic shared with the CUDA router
 # ---------------------------------------------------------------------------
@@ -385,6 +421,33 @@ def moe_layer_reference_packed(x, wr, w13_q, w13_s, w2_q, w2_s, top_k: int, grou
         d2 = dequantize_int4(w2_q[e], w2_s[e], group)
         y = expert_ffn(x[tok], d13, d2)
         out[tok] += (y * w[tok, slot][:, None]).astype(F32)
+    return out, idx, w
+
+
+def moe_layer_reference_shared(x, wr, w13_q, w13_s, w2_q, w2_s, top_k: int, num_shared: int, group: int = 64,
+                               renormalize: bool = True, shared_gate=None, routed_scale: float = 1.0,
+                               router: str = "fixed"):
+    """MoE block with shared experts on packed weights (experts E..E+m-1 are
+    the m slices of the shared expert): routed output with weights times
+    ``routed_scale``, plus g(t) * shared(x), g = sigmoid(x . shared_gate)
+    (1 when None). Restates Qwen2MoeSparseMoeBlock.forward (transformers
+    5.5.0 models/qwen2_moe/modeling_qwen2_moe.py: shared_expert_output scaled
+    by F.sigmoid(shared_expert_gate(x)) and added to the routed output);
+    DeepSeek blocks are the ungated case. Returns (out, routed idx, routed w)."""
+    x = np.asarray(x, dtype=F32)
+    T = x.shape[0]
+    route = route_fixed_order if router == "fixed" else route_reference
+    _, _, idx, w = route(x, wr, top_k, renormalize)
+    E = wr.shape[0]
+    if shared_gate is None:
+        g = np.ones((T, 1), dtype=F32)
+    else:
+        z = (x.astype(np.float64) @ np.asarray(shared_gate, dtype=np.float64).reshape(-1, 1))
+        g = (1.0 / (1.0 + np.exp(-z))).astype(F32)
+    idx2 = np.concatenate([idx, np.broadcast_to(E + np.arange(num_shared, dtype=idx.dtype), (T, num_shared))], 1)
+    w2 = np.concatenate([(w * F32(routed_scale)).astype(F32), np.repeat(g, num_shared, axis=1)], 1)
+    out, _, _ = moe_layer_reference_packed(x, wr, w13_q, w13_s, w2_q, w2_s, top_k + num_shared, group,
+                                           idx=idx2, w=w2)
     return out, idx, w
 
 

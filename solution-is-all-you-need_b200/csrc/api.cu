@@ -366,6 +366,73 @@ int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtyp
   return check_launch("combine");
 }
 
+size_t phmoe_workspace_size_shared(int T, int H, int E, int top_k, int I, int num_shared, int path) {
+  if (T < 0 || H <= 0 || E < 1 || top_k < 1 || I <= 0 || num_shared < 0) return 0;
+  if (path < PHMOE_PATH_AUTO || path > PHMOE_PATH_PREFILL) return 0;
+  // the whole layer over E + m experts and k + m slots, plus the router's [T, k] choice
+  return make_layout(T, H, E + num_shared, top_k + num_shared, I).total + round_up((size_t)T * top_k * 8, kAlign);
+}
+
+int phmoe_moe_layer_shared(const void* x, int x_dtype, const void* router_w, int w_dtype,
+                           const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
+                           const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
+                           int group_size, int renormalize, int num_shared, const void* shared_gate_w,
+                           float routed_scale, int path, void* out, int32_t* topk_idx_out,
+                           float* topk_w_out, void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (num_shared < 0 || num_shared > 32) return fail(PHMOE_ERR_INVALID_ARG, "num_shared must be in [0, 32]");
+  if (int s = check_router_dims(T, H, E, top_k)) return s;
+  if (!dtype_ok(x_dtype) || !dtype_ok(w_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  const int Et = E + num_shared, kt = top_k + num_shared;
+  if (Et > 1024) return fail(PHMOE_ERR_INVALID_ARG, "E + num_shared must be <= 1024");
+  int chosen = PHMOE_PATH_DECODE;
+  if (int s = resolve_path(path, x_dtype, T, kt, H, I, group_size, Et, &chosen)) return s;
+  if (int s = check_router_smem(H, x_dtype)) return s;
+  if (T == 0) return PHMOE_OK;
+  if (!x || !router_w || !w13_q || !w13_s || !w2_q || !w2_s || !out || !workspace)
+    return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned(x, 16) || !aligned(router_w, 16) || !aligned(w13_q, 16) || !aligned(w2_q, 16) || !aligned(out, 16) ||
+      (shared_gate_w && !aligned(shared_gate_w, 16)))
+    return fail(PHMOE_ERR_ALIGNMENT, "x, router_w, shared_gate_w, packed weights and out must be 16-byte aligned");
+  if (!aligned(w13_s, 4) || !aligned(w2_s, 4)) return fail(PHMOE_ERR_ALIGNMENT, "scales must be 4-byte aligned");
+  const Layout L = make_layout(T, H, Et, kt, I);
+  const size_t need = phmoe_workspace_size_shared(T, H, E, top_k, I, num_shared, path);
+  if (!aligned(workspace, kAlign)) return fail(PHMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  if (workspace_bytes < need) return fail(PHMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", need, workspace_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  float* logits = reinterpret_cast<float*>(ws + L.logits);  // [T, Et] >= [T, E]
+  int32_t* r_idx = topk_idx_out ? topk_idx_out : reinterpret_cast<int32_t*>(ws + L.total);
+  float* r_w = topk_w_out ? topk_w_out : reinterpret_cast<float*>(ws + L.total + (size_t)T * top_k * 4);
+  int32_t* idx = reinterpret_cast<int32_t*>(ws + L.idx);
+  float* wts = reinterpret_cast<float*>(ws + L.w);
+  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  int32_t* active = reinterpret_cast<int32_t*>(ws + L.active);
+  int32_t* row_token = reinterpret_cast<int32_t*>(ws + L.row_token);
+  int32_t* inv = reinterpret_cast<int32_t*>(ws + L.inv);
+  float* h = reinterpret_cast<float*>(ws + L.h);
+  float* y = reinterpret_cast<float*>(ws + L.y);
+
+  launch_router(x, x_dtype, router_w, w_dtype, T, H, E, top_k, renormalize, logits, nullptr, r_idx, r_w, st);
+  if (int s = check_launch("router")) return s;
+  launch_shared_slots(x, x_dtype, shared_gate_w, w_dtype, r_idx, r_w, T, H, top_k, E, num_shared, routed_scale,
+                      idx, wts, st);
+  if (int s = check_launch("shared_slots")) return s;
+  launch_dispatch(idx, T, kt, Et, offsets, row_token, inv, active, ws + L.disp, st);
+  if (int s = check_launch("dispatch")) return s;
+  if (chosen == PHMOE_PATH_PREFILL) {
+    if (int s = launch_ffn_prefill(x, row_token, offsets, active, w13_q, w13_s, w2_q, w2_s, T, H, Et, kt, I,
+                                   group_size, h, y, st, nullptr))
+      return fail(s, "prefill launch failed (tensor map or kernel attribute)");
+  } else if (int s = launch_ffn_decode(x, x_dtype, row_token, offsets, active, w13_q, w13_s, w2_q, w2_s, T, H,
+                                       Et, kt, I, group_size, h, y, st, nullptr)) {
+    return fail(s, "no decode kernel for group_size=%d", group_size);
+  }
+  if (int s = check_launch("expert_ffn")) return s;
+  launch_combine(y, inv, wts, T, kt, H, out, x_dtype, st);
+  return check_launch("combine");
+}
+
 int phmoe_quantize_int4(const void* w, int w_dtype, long long rows, int K, int group_size,
                         uint8_t* packed, uint16_t* scales, void* stream) {
   g_last_error.clear();
@@ -376,6 +443,38 @@ int phmoe_quantize_int4(const void* w, int w_dtype, long long rows, int K, int g
   if (!w || !packed || !scales) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
   launch_quantize(w, w_dtype, rows, K, group_size, packed, scales, static_cast<cudaStream_t>(stream));
   return check_launch("phmoe_quantize_int4");
+}
+
+int phmoe_gguf_q4_0_to_packed(const void* blocks, long long rows, int K, uint8_t* packed,
+                              uint16_t* scales, void* stream) {
+  g_last_error.clear();
+  if (rows < 0 || K <= 0 || K % 32) return fail(PHMOE_ERR_INVALID_ARG, "K must be a positive multiple of 32");
+  if (rows == 0) return PHMOE_OK;
+  if (!blocks || !packed || !scales) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned(blocks, 2) || !aligned(packed, 16) || !aligned(scales, 2))
+    return fail(PHMOE_ERR_ALIGNMENT, "blocks must be 2-byte, packed 16-byte and scales 2-byte aligned");
+  launch_gguf_q4_0(blocks, rows, K, packed, scales, static_cast<cudaStream_t>(stream));
+  return check_launch("phmoe_gguf_q4_0_to_packed");
+}
+
+int phmoe_gguf_q4_k_to_packed(const void* blocks, long long rows, int K, int group_size,
+                              uint8_t* packed, uint16_t* scales, void* stream) {
+  g_last_error.clear();
+  if (group_size != 32 && group_size != 64) return fail(PHMOE_ERR_UNSUPPORTED, "group_size must be 32 or 64");
+  if (rows < 0 || K <= 0 || K % 256) return fail(PHMOE_ERR_INVALID_ARG, "K must be a positive multiple of 256");
+  if (rows == 0) return PHMOE_OK;
+  if (!blocks || !packed || !scales) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  launch_gguf_q4_k(blocks, rows, K, group_size, packed, scales, static_cast<cudaStream_t>(stream));
+  return check_launch("phmoe_gguf_q4_k_to_packed");
+}
+
+int phmoe_gguf_q4_k_dequantize(const void* blocks, long long n, float* out, void* stream) {
+  g_last_error.clear();
+  if (n < 0 || n % 256) return fail(PHMOE_ERR_INVALID_ARG, "n must be a non-negative multiple of 256");
+  if (n == 0) return PHMOE_OK;
+  if (!blocks || !out) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  launch_gguf_q4_k_dequant(blocks, n, out, static_cast<cudaStream_t>(stream));
+  return check_launch("phmoe_gguf_q4_k_dequantize");
 }
 
 unsigned long long phmoe_kernel_launch_count(void) { return g_launches.load(); }

@@ -41,6 +41,13 @@ void launch_gather_rows(const void* src, long long src_rows, const int32_t* inde
 
 int launch_quantize(const void* w, int w_dtype, long long rows, int K, int G, uint8_t* packed,
                     uint16_t* scales, cudaStream_t st);
+int launch_gguf_q4_0(const void* blocks, long long rows, int K, uint8_t* packed, uint16_t* scales, cudaStream_t st);
+int launch_gguf_q4_k(const void* blocks, long long rows, int K, int G, uint8_t* packed, uint16_t* scales,
+                     cudaStream_t st);
+int launch_gguf_q4_k_dequant(const void* blocks, long long n, float* out, cudaStream_t st);
+int launch_shared_slots(const void* x, int x_dtype, const void* gate_w, int w_dtype, const int32_t* idx,
+                        const float* w, int T, int H, int k, int E, int m, float routed_scale, int32_t* idx_out,
+                        float* w_out, cudaStream_t st);
 
 int device_sm_count();
 

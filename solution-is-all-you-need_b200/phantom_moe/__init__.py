@@ -9,6 +9,8 @@ of ``include/phmoe.h``; this package validates tensors and calls it.
 """
 
 from ._lib import PhmoeError, load as load_library
+from .gguf import GGUFFile, MoeSpec, detect_moe, load_moe_layer
+from .integrate import find_moe_blocks, install_into, uninstall
 from .layer import (
     PackedExperts,
     check_expert_weights,
@@ -19,25 +21,34 @@ from .layer import (
     gather_rows,
     moe_layer,
     pack_experts,
+    pack_experts_shared,
     quantize_int4,
     router,
     workspace_bytes,
 )
 
 __all__ = [
+    "GGUFFile",
+    "MoeSpec",
     "PhmoeError",
     "PackedExperts",
     "check_expert_weights",
     "combine",
+    "detect_moe",
     "dispatch",
     "expert_ffn_decode",
+    "find_moe_blocks",
     "expert_ffn_prefill",
     "gather_rows",
+    "install_into",
     "load_library",
+    "load_moe_layer",
     "moe_layer",
     "pack_experts",
+    "pack_experts_shared",
     "quantize_int4",
     "router",
+    "uninstall",
     "workspace_bytes",
 ]
 

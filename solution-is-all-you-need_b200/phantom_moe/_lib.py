@@ -58,6 +58,12 @@ SIGNATURES = {
                              _P, _P, _P, _P, _SZ, _P]),
     "phmoe_moe_layer_noalloc": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
                                      _P, _P, _P, _P]),
+    "phmoe_workspace_size_shared": (_SZ, [_I, _I, _I, _I, _I, _I, _I]),
+    "phmoe_moe_layer_shared": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P,
+                                    ctypes.c_float, _I, _P, _P, _P, _P, _SZ, _P]),
+    "phmoe_gguf_q4_0_to_packed": (_I, [_P, _LL, _I, _P, _P, _P]),
+    "phmoe_gguf_q4_k_to_packed": (_I, [_P, _LL, _I, _I, _P, _P, _P]),
+    "phmoe_gguf_q4_k_dequantize": (_I, [_P, _LL, _P, _P]),
     "phmoe_quantize_int4": (_I, [_P, _I, _LL, _I, _I, _P, _P, _P]),
     "phmoe_kernel_launch_count": (ctypes.c_ulonglong, []),
     "phmoe_profile_begin": (_I, [_I]),

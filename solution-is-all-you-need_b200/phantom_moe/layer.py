@@ -101,6 +101,7 @@ class PackedExperts:
     w2_q: torch.Tensor
     w2_scales: torch.Tensor
     group_size: int = 64
+    num_shared: int = 0  # trailing experts that are slices of a shared expert (pack_experts_shared)
 
     @property
     def num_experts(self) -> int:
@@ -287,6 +288,30 @@ def pack_experts(gate_up_proj: torch.Tensor, down_proj: torch.Tensor, group_size
     return PackedExperts(w13_q, w13_s, w2_q, w2_s, group_size)
 
 
+def pack_experts_shared(gate_up_proj: torch.Tensor, down_proj: torch.Tensor, shared_gate_proj: torch.Tensor,
+                        shared_up_proj: torch.Tensor, shared_down_proj: torch.Tensor,
+                        group_size: int = 64) -> PackedExperts:
+    """Routed experts (``gate_up_proj [E, 2I, H]``, ``down_proj [E, H, I]``)
+    plus one shared SwiGLU expert (``gate_proj`` / ``up_proj`` weights
+    ``[Is, H]``, ``down_proj`` weight ``[H, Is]``, Qwen2MoeMLP layout) with
+    Is = m * I, packed as E + m experts: the shared expert is cut along its
+    intermediate dimension into m experts of size I, whose outputs add up to
+    the shared expert's (the int4 groups run along H for gate/up and along
+    Is for down, so no group straddles two slices)."""
+    E, two_i, H = gate_up_proj.shape
+    I = two_i // 2
+    Is = shared_gate_proj.shape[0]
+    if Is % I:
+        raise ValueError(f"shared intermediate size {Is} must be a multiple of the routed experts' {I}")
+    m = Is // I
+    dt = gate_up_proj.dtype
+    s13 = torch.cat([shared_gate_proj.reshape(m, I, H), shared_up_proj.reshape(m, I, H)], dim=1).to(dt)
+    s2 = shared_down_proj.reshape(H, m, I).permute(1, 0, 2).to(dt)
+    packed = pack_experts(torch.cat([gate_up_proj, s13], 0), torch.cat([down_proj, s2], 0), group_size)
+    packed.num_shared = m
+    return packed
+
+
 # ---------------------------------------------------------------------------
 # the layer
 # ---------------------------------------------------------------------------
@@ -316,7 +341,8 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
               w13_scales: torch.Tensor, w2_q: torch.Tensor, w2_scales: torch.Tensor, top_k: int,
               renormalize: bool = True, group_size: int = 64, ep_group=None, *,
               path: str = "auto", return_routing: bool = False, out: torch.Tensor | None = None,
-              workspace: torch.Tensor | None = None):
+              workspace: torch.Tensor | None = None, num_shared: int = 0,
+              shared_gate_weight: torch.Tensor | None = None, routed_scale: float = 1.0):
     """Sparse-MoE layer: router -> dispatch -> grouped int4 SwiGLU FFN -> combine.
 
     ``hidden_states`` is ``[T, H]`` or ``[B, S, H]`` (bf16 or fp32); the result
@@ -328,10 +354,19 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
     ``return_routing`` adds ``(topk_idx int32[T,k], topk_w fp32[T,k])``.
     ``workspace`` (uint8 CUDA tensor of at least ``workspace_bytes(...)``)
     overrides the per-stream cached scratch buffer.
+
+    Shared experts (Qwen2-MoE, DeepSeek): with ``num_shared = m > 0`` the
+    expert tensors hold E routed experts followed by the m slices of the
+    shared expert (:func:`pack_experts_shared`); the router picks among the
+    first E, every token also goes to the m slices with weight
+    ``sigmoid(x . shared_gate_weight)`` (``[H]`` or ``[1, H]``; 1 when None),
+    and the routed weights are multiplied by ``routed_scale``.
     """
     if ep_group is not None:
         from . import ep as _ep
         if _ep.ep_world_size(ep_group) > 1:
+            if num_shared:
+                raise NotImplementedError("shared experts are not supported with expert parallelism")
             return _ep.moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scales,
                                     top_k, renormalize, group_size, ep_group, path=path,
                                     return_routing=return_routing)
@@ -344,6 +379,16 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
     x = hidden_states.reshape(-1, H)
     T = x.shape[0]
     E, I = check_expert_weights(w13_q, w13_scales, w2_q, w2_scales, H, group_size)
+    if num_shared:
+        if num_shared < 0 or num_shared >= E:
+            raise ValueError("num_shared must be in [0, number of packed experts)")
+        E -= num_shared
+        if shared_gate_weight is not None:
+            _need_cuda("shared_gate_weight", shared_gate_weight)
+            if shared_gate_weight.numel() != H or shared_gate_weight.dtype != router_weight.dtype:
+                raise ValueError("shared_gate_weight must hold H values of router_weight's dtype")
+    elif shared_gate_weight is not None or routed_scale != 1.0:
+        raise ValueError("shared_gate_weight / routed_scale need num_shared > 0")
     _need_shape("router_weight", router_weight, (E, H))
     if path not in _PATHS:
         raise ValueError(f"path must be one of {list(_PATHS)}")
@@ -357,7 +402,10 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
     idx = torch.empty(T, top_k, dtype=torch.int32, device=dev) if return_routing else None
     wts = torch.empty(T, top_k, dtype=torch.float32, device=dev) if return_routing else None
     lib = _lib.load()
-    need = lib.phmoe_workspace_size(T, H, E, top_k, I, _PATHS[path])
+    if num_shared:
+        need = lib.phmoe_workspace_size_shared(T, H, E, top_k, I, num_shared, _PATHS[path])
+    else:
+        need = lib.phmoe_workspace_size(T, H, E, top_k, I, _PATHS[path])
     if workspace is None:
         ws = WORKSPACE.get(dev, need)
     else:
@@ -366,10 +414,16 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
         if workspace.numel() < need:
             raise ValueError(f"workspace needs {need} bytes (got {workspace.numel()})")
         ws = workspace
-    _lib.call("phmoe_moe_layer", _ptr(x), _DT[x.dtype], _ptr(router_weight), _DT[router_weight.dtype],
-              _ptr(w13_q), _ptr(w13_scales), _ptr(w2_q), _ptr(w2_scales), T, H, E, top_k, I, group_size,
-              int(bool(renormalize)), _PATHS[path], _ptr(out), _ptr(idx), _ptr(wts), _ptr(ws), ws.numel(),
-              _stream())
+    if num_shared:
+        _lib.call("phmoe_moe_layer_shared", _ptr(x), _DT[x.dtype], _ptr(router_weight), _DT[router_weight.dtype],
+                  _ptr(w13_q), _ptr(w13_scales), _ptr(w2_q), _ptr(w2_scales), T, H, E, top_k, I, group_size,
+                  int(bool(renormalize)), num_shared, _ptr(shared_gate_weight), float(routed_scale),
+                  _PATHS[path], _ptr(out), _ptr(idx), _ptr(wts), _ptr(ws), ws.numel(), _stream())
+    else:
+        _lib.call("phmoe_moe_layer", _ptr(x), _DT[x.dtype], _ptr(router_weight), _DT[router_weight.dtype],
+                  _ptr(w13_q), _ptr(w13_scales), _ptr(w2_q), _ptr(w2_scales), T, H, E, top_k, I, group_size,
+                  int(bool(renormalize)), _PATHS[path], _ptr(out), _ptr(idx), _ptr(wts), _ptr(ws), ws.numel(),
+                  _stream())
     out = out.reshape(shape)
     if return_routing:
         return out, idx, wts

@@ -11,6 +11,14 @@ What each fixture pins, and which reference code produced it:
   ``GGUFLoader.dequantize_tensor`` (python/phantom/loader/gguf_loader.py:362-381,
   CPU branch), on the known-answer block of tests/audit_suite.py:36-41
   (nibbles 0x88, d = 1.5 -> zeros) and on 64 seeded random blocks.
+* ``q4_k_ref.npz`` - GGUF Q4_K (and Q4_0) dequantisation by the reference's
+  ``dequantize_tensor_cuda`` (gguf_loader.py:538-666, run with device="cpu"
+  and target_dtype=float32, i.e. the fp32 values before the loader's bf16
+  cast) - the function its model loader runs (gguf_loader.py:799) - on 48
+  seeded random super-blocks; plus the same blocks through the reference's
+  CPU ``GGUFLoader.dequantize_tensor`` Q4_K branch (gguf_loader.py:453-489),
+  which orders the nibbles differently, and through the ``gguf`` package's
+  ``quants.dequantize`` (llama.cpp's layout) when that package is present.
 * ``router_phantom.npz`` - the reference's ``PhantomTopKRouter``
   (tests/test_moe_routing.py:43-72) on the shapes of its own
   ``test_router_correctness`` (x [2,4,256], 8 experts, top-2).
@@ -19,6 +27,11 @@ What each fixture pins, and which reference code produced it:
   executes, python/phantom/phantom_cli.py:1393-1430) in fp32 on CPU, with
   expert weights set to the dequantised int4 values whose packed bytes are
   stored alongside.
+* ``qwen2moe_block_small.npz`` - transformers' ``Qwen2MoeSparseMoeBlock``
+  (routed experts + a sigmoid-gated shared expert of 4x the routed
+  intermediate size, norm_topk_prob False) in fp32 on CPU, on the
+  dequantised int4 values of the packed E + 4 experts stored alongside
+  (routed experts, then the shared expert cut into 4 slices).
 * ``qwen3_cfg1.npz`` - the same Qwen3 block at BASELINE config 1 (H=2048,
   128 experts, top-8, I=768, T=16, fp32 inputs drawn from
   ``torch.Generator().manual_seed(0)``). The 320 MB of packed weights are
@@ -61,6 +74,37 @@ def import_reference(ref: Path):
     from phantom.loader.gguf_loader import GGUFLoader, GGUFQuantType  # noqa: E402
     import test_moe_routing  # noqa: E402
     return GGUFLoader, GGUFQuantType, test_moe_routing
+
+
+def make_q4_k(GGUFLoader, GGUFQuantType):
+    from phantom.loader.gguf_loader import dequantize_tensor_cuda  # noqa: E402
+    rng = np.random.default_rng(4321)
+    nsb = 48
+    d = (np.abs(rng.standard_normal(nsb)) * 2e-3).astype(np.float16)
+    dmin = (np.abs(rng.standard_normal(nsb)) * 2e-3).astype(np.float16)
+    sc = rng.integers(0, 256, size=(nsb, 12), dtype=np.uint8)
+    qs = rng.integers(0, 256, size=(nsb, 128), dtype=np.uint8)
+    raw = b"".join(d[i:i + 1].tobytes() + dmin[i:i + 1].tobytes() + sc[i].tobytes() + qs[i].tobytes()
+                   for i in range(nsb))
+    n = nsb * 256
+    exe = dequantize_tensor_cuda(raw, GGUFQuantType.Q4_K, (n,), target_dtype=torch.float32, device="cpu").numpy()
+    loader = GGUFLoader.__new__(GGUFLoader)
+    cpu = loader.dequantize_tensor(raw, GGUFQuantType.Q4_K, (n,)).float().numpy()
+    q40_d = (rng.standard_normal(32) * 0.01).astype(np.float16)
+    q40_qs = rng.integers(0, 256, size=(32, 16), dtype=np.uint8)
+    q40_raw = b"".join(q40_d[i:i + 1].tobytes() + q40_qs[i].tobytes() for i in range(32))
+    q40 = dequantize_tensor_cuda(q40_raw, GGUFQuantType.Q4_0, (32 * 32,), target_dtype=torch.float32,
+                                 device="cpu").numpy()
+    extra = {}
+    try:
+        import gguf  # llama.cpp's own Python package
+        extra["ggml"] = gguf.quants.dequantize(np.frombuffer(raw, dtype=np.uint8).reshape(nsb, 144),
+                                               gguf.GGMLQuantizationType.Q4_K).reshape(-1).astype(np.float32)
+    except Exception as e:  # pragma: no cover - optional cross-check
+        print("gguf package cross-check skipped:", e)
+    np.savez_compressed(OUT / "q4_k_ref.npz", raw=np.frombuffer(raw, dtype=np.uint8), out_f32=exe,
+                        out_cpu_branch_bf16=cpu, q4_0_raw=np.frombuffer(q40_raw, dtype=np.uint8),
+                        q4_0_out_f32=q40, **extra)
 
 
 def make_q4_0(GGUFLoader, GGUFQuantType):
@@ -143,6 +187,43 @@ def make_small_block(kind, name, T, H, E, k, I, group, seed):
                         top_k=np.int32(k), out=out, probs=probs, idx=idx, scores=scores)
 
 
+def make_qwen2moe_block(name, T, H, E, k, I, m, group, seed):
+    from transformers.models.qwen2_moe.configuration_qwen2_moe import Qwen2MoeConfig
+    from transformers.models.qwen2_moe.modeling_qwen2_moe import Qwen2MoeSparseMoeBlock
+    x, wr, w13, w2 = small_block_inputs(T, H, E, I, seed)
+    g = torch.Generator().manual_seed(seed + 1000)
+    Is = m * I
+    sgp = (torch.randn(Is, H, generator=g) * 0.02).numpy()
+    sup = (torch.randn(Is, H, generator=g) * 0.02).numpy()
+    sdp = (torch.randn(H, Is, generator=g) * 0.02).numpy()
+    sgate = (torch.randn(1, H, generator=g) * 0.05).numpy()
+    # shared expert cut into m experts of size I, after the routed ones
+    s13 = np.concatenate([sgp.reshape(m, I, H), sup.reshape(m, I, H)], axis=1)
+    s2 = sdp.reshape(H, m, I).transpose(1, 0, 2)
+    p13, q13 = O.quantize_int4(np.concatenate([w13, s13]).astype(np.float32), group)
+    p2, q2 = O.quantize_int4(np.concatenate([w2, s2]).astype(np.float32), group)
+    d13, d2 = O.dequantize_int4(p13, q13, group), O.dequantize_int4(p2, q2, group)
+    cfg = Qwen2MoeConfig(hidden_size=H, num_experts=E, num_experts_per_tok=k, moe_intermediate_size=I,
+                         shared_expert_intermediate_size=Is, norm_topk_prob=False)
+    cfg._experts_implementation = "eager"
+    blk = Qwen2MoeSparseMoeBlock(cfg).eval()
+    with torch.no_grad():
+        blk.gate.weight.copy_(torch.from_numpy(wr))
+        blk.experts.gate_up_proj.copy_(torch.from_numpy(d13[:E]))
+        blk.experts.down_proj.copy_(torch.from_numpy(d2[:E]))
+        blk.shared_expert.gate_proj.weight.copy_(torch.from_numpy(d13[E:, :I].reshape(Is, H)))
+        blk.shared_expert.up_proj.weight.copy_(torch.from_numpy(d13[E:, I:].reshape(Is, H)))
+        blk.shared_expert.down_proj.weight.copy_(torch.from_numpy(d2[E:].transpose(1, 0, 2).reshape(H, Is)))
+        blk.shared_expert_gate.weight.copy_(torch.from_numpy(sgate))
+        xt = torch.from_numpy(x)
+        _, scores, idx = blk.gate(xt)
+        out = blk(xt[None])[0]
+    np.savez_compressed(OUT / name, x=x, wr=wr, w13_q=p13, w13_s=q13, w2_q=p2, w2_s=q2, shared_gate=sgate,
+                        dims=np.array([T, H, E, I, m, seed], np.int32), group=np.int32(group),
+                        top_k=np.int32(k), out=out.numpy().astype(np.float32),
+                        idx=idx.numpy().astype(np.int32), scores=scores.numpy().astype(np.float32))
+
+
 def gen_cfg1_inputs():
     """BASELINE config 1 inputs (documented procedure; the GPU tests repeat it)."""
     g = torch.Generator().manual_seed(0)
@@ -177,13 +258,22 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     ap.add_argument("--skip-cfg1", action="store_true", help="keep the existing qwen3_cfg1.npz")
+    ap.add_argument("--only", choices=["q4_k", "qwen2moe"], help="regenerate one fixture only")
     args = ap.parse_args()
     GGUFLoader, QT, tmr = import_reference(Path(args.reference))
+    if args.only == "q4_k":
+        make_q4_k(GGUFLoader, QT)
+        return
+    if args.only == "qwen2moe":
+        make_qwen2moe_block("qwen2moe_block_small.npz", T=10, H=256, E=8, k=2, I=64, m=4, group=64, seed=14)
+        return
     make_q4_0(GGUFLoader, QT)
+    make_q4_k(GGUFLoader, QT)
     make_router_phantom(tmr)
     make_small_block("qwen3", "qwen3_block_small.npz", T=12, H=256, E=16, k=4, I=128, group=64, seed=11)
     make_small_block("qwen3", "qwen3_block_small_g32.npz", T=9, H=256, E=8, k=2, I=64, group=32, seed=12)
     make_small_block("mixtral", "mixtral_block_small.npz", T=10, H=256, E=8, k=2, I=128, group=64, seed=13)
+    make_qwen2moe_block("qwen2moe_block_small.npz", T=10, H=256, E=8, k=2, I=64, m=4, group=64, seed=14)
     if not args.skip_cfg1:
         make_cfg1()
     for p in sorted(OUT.glob("*.npz")):

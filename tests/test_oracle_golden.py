@@ -176,3 +176,18 @@ def test_torch_reference_nibble_order():
         p, s = O.quantize_int4(w, G)
         got = dequant_torch(torch.from_numpy(p), torch.from_numpy(s), G).numpy()
         assert np.array_equal(got, O.dequantize_int4(p, s, G))
+
+
+def test_qwen2moe_shared_expert_golden():
+    """transformers' Qwen2MoeSparseMoeBlock (routed + sigmoid-gated shared
+    expert, norm_topk_prob False) against the oracle's shared-expert form on
+    the same packed weights (shared expert as 4 slices after the routed
+    experts)."""
+    z = load_golden("qwen2moe_block_small.npz")
+    T, H, E, I, m, _ = (int(v) for v in z["dims"])
+    out, idx, w = O.moe_layer_reference_shared(z["x"], z["wr"], z["w13_q"], z["w13_s"], z["w2_q"], z["w2_s"],
+                                               int(z["top_k"]), m, int(z["group"]), renormalize=False,
+                                               shared_gate=z["shared_gate"])
+    assert np.array_equal(np.sort(idx, 1), np.sort(z["idx"], 1))
+    mx, mr = O.parity_stats(out, z["out"])
+    assert mx <= 1e-5 and mr <= 1e-5, (mx, mr)
