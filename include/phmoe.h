@@ -248,29 +248,53 @@ int phmoe_moe_layer_noalloc(const void* x, int x_dtype, const void* router_w, in
                             int group_size, int renormalize, int path, void* out,
                             int32_t* topk_idx_out, float* topk_w_out, void* stream);
 
+/* Router scoring functions. */
+enum { PHMOE_SCORING_SOFTMAX = 0, PHMOE_SCORING_SIGMOID = 1 };
+
 /*
- * MoE layer with shared experts (Qwen2-MoE's gated shared expert,
- * transformers 5.5.0 models/qwen2_moe/modeling_qwen2_moe.py
- * Qwen2MoeSparseMoeBlock.forward: out = routed + sigmoid(x . w_sg) * shared(x);
- * DeepSeek-style ungated shared experts with routed_scaling_factor).
- *
- * The packed expert tensors hold E + num_shared experts: the E routed ones,
- * then the shared expert split along its intermediate dimension into
- * num_shared experts of size I (a shared expert of size m * I is the sum of
- * those m SwiGLU experts). Every token is routed to its top_k experts
- * (weights times routed_scale) and to all num_shared shared experts with
- * weight sigmoid(x . shared_gate_w) (shared_gate_w: [H] in w_dtype), or 1
- * when shared_gate_w is NULL. topk_idx_out / topk_w_out (optional, [T, top_k])
- * receive the routed choice before scaling. Other arguments and limits as
- * phmoe_moe_layer; workspace_bytes >= phmoe_workspace_size_shared(...).
+ * Router with the DeepSeek-V3 selection (transformers 5.5.0
+ * models/deepseek_v3/modeling_deepseek_v3.py DeepseekV3MoE.route_tokens_to_experts):
+ * scoring PHMOE_SCORING_SIGMOID: s = sigmoid(logit) (fp32; a fixed exp
+ * routine, bit-reproducible), choice c = s + score_bias[e] (score_bias [E]
+ * fp32 or NULL); with n_group > 1 the experts form n_group groups of
+ * E/n_group (>= 2), a group scores the sum of its two largest c, only the
+ * topk_group best groups stay (the others' c become 0); the top_k largest c
+ * are picked (ties -> lower index) and weighted by s, divided by
+ * (sum + 1e-20) when renormalize, times routed_scale.
+ * scoring PHMOE_SCORING_SOFTMAX with n_group <= 1, no bias and
+ * routed_scale == 1 is phmoe_router. Logits as phmoe_router.
  */
-size_t phmoe_workspace_size_shared(int T, int H, int E, int top_k, int I, int num_shared, int path);
-int phmoe_moe_layer_shared(const void* x, int x_dtype, const void* router_w, int w_dtype,
-                           const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
-                           const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
-                           int group_size, int renormalize, int num_shared, const void* shared_gate_w,
-                           float routed_scale, int path, void* out, int32_t* topk_idx_out,
-                           float* topk_w_out, void* workspace, size_t workspace_bytes, void* stream);
+int phmoe_router_ex(const void* x, int x_dtype, const void* router_w, int w_dtype, int T, int H,
+                    int E, int top_k, int renormalize, int scoring, const float* score_bias,
+                    int n_group, int topk_group, float routed_scale, float* logits,
+                    int32_t* topk_idx, float* topk_w, void* stream);
+
+/*
+ * Extended MoE layer: shared experts and the DeepSeek-V3 router.
+ *
+ * Shared experts (Qwen2-MoE's gated shared expert, transformers 5.5.0
+ * models/qwen2_moe/modeling_qwen2_moe.py Qwen2MoeSparseMoeBlock.forward:
+ * out = routed + sigmoid(x . w_sg) * shared(x); DeepSeek's ungated ones,
+ * DeepseekV3MoE.forward): the packed expert tensors hold E + num_shared
+ * experts, the E routed ones and then the shared expert split along its
+ * intermediate dimension into num_shared experts of size I (a shared expert
+ * of size m * I is the sum of those m SwiGLU experts). Every token goes to
+ * its top_k routed experts (weights times routed_scale) and to all
+ * num_shared shared experts with weight sigmoid(x . shared_gate_w)
+ * (shared_gate_w: [H] in w_dtype), or 1 when shared_gate_w is NULL.
+ * Routing: scoring / score_bias / n_group / topk_group as phmoe_router_ex.
+ * topk_idx_out / topk_w_out (optional, [T, top_k]) receive the routed choice
+ * before routed_scale. Other arguments and limits as phmoe_moe_layer;
+ * workspace_bytes >= phmoe_workspace_size_ex(...).
+ */
+size_t phmoe_workspace_size_ex(int T, int H, int E, int top_k, int I, int num_shared, int path);
+int phmoe_moe_layer_ex(const void* x, int x_dtype, const void* router_w, int w_dtype,
+                       const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
+                       const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
+                       int group_size, int renormalize, int scoring, const float* score_bias,
+                       int n_group, int topk_group, int num_shared, const void* shared_gate_w,
+                       float routed_scale, int path, void* out, int32_t* topk_idx_out,
+                       float* topk_w_out, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Symmetric int4 group quantiser on the GPU (load-time utility; the

@@ -301,6 +301,51 @@ def route_fixed_order(x, wr, top_k: int, renormalize: bool = True):
     return logits, probs, idx, renormalise_fixed(vals, renormalize)
 
 
+def sigmoid_fixed(x: np.ndarray) -> np.ndarray:
+    """sigmoid as the CUDA router computes it: 1 / (1 + exp(-x)) for x >= 0,
+    e / (1 + e) with e = exp(x) otherwise, exp by :func:`fixed_exp`, each
+    step rounded to fp32."""
+    x = np.asarray(x, dtype=F32)
+    pos = x >= 0
+    e = fixed_exp(np.where(pos, -x, x).astype(F32))
+    den = (F32(1.0) + e).astype(F32)
+    return np.where(pos, (F32(1.0) / den).astype(F32), (e / den).astype(F32)).astype(F32)
+
+
+def route_sigmoid_grouped(x, wr, top_k: int, renormalize: bool = True, score_bias=None, n_group: int = 1,
+                          topk_group: int = 1, routed_scale: float = 1.0, logits=None):
+    """DeepSeek-V3 routing (transformers 5.5.0 models/deepseek_v3/modeling_deepseek_v3.py
+    DeepseekV3MoE.route_tokens_to_experts) as the CUDA router computes it:
+    s = sigmoid(logits); choice c = s + bias; groups of E/n_group score the
+    sum of their two largest c; the topk_group best groups stay, the rest
+    get c = 0; top_k largest c (ties -> lower index; the reference's
+    ``topk(sorted=False)`` leaves the order open); weights = s of the picks,
+    over (their sum in pick order + 1e-20) when renormalising, times
+    routed_scale. Returns (logits, s, idx, w)."""
+    if logits is None:
+        logits = logits_fixed_order(x, wr, products_exact=True)
+    logits = np.asarray(logits, dtype=F32)
+    s = sigmoid_fixed(logits)
+    c = (s + np.asarray(score_bias, dtype=F32)).astype(F32) if score_bias is not None else s.copy()
+    T, E = c.shape
+    if n_group > 1:
+        gs = E // n_group
+        top2 = -np.sort(-c.reshape(T, n_group, gs), axis=2)[:, :, :2]
+        gscore = (top2[:, :, 0] + top2[:, :, 1]).astype(F32)
+        gsel = np.argsort(-gscore, axis=1, kind="stable")[:, :topk_group]
+        keep = np.zeros((T, n_group), dtype=bool)
+        np.put_along_axis(keep, gsel, True, axis=1)
+        c = np.where(np.repeat(keep, gs, axis=1), c, F32(0.0)).astype(F32)
+    idx = np.argsort(-c, axis=1, kind="stable")[:, :top_k].astype(np.int32)
+    w = np.take_along_axis(s, idx, axis=1).astype(F32)
+    if renormalize:
+        tot = np.zeros(T, dtype=F32)
+        for j in range(top_k):
+            tot = (tot + w[:, j]).astype(F32)
+        w = (w / (tot + F32(1e-20)).astype(F32)[:, None]).astype(F32)
+    return logits, s, idx, (w * F32(routed_scale)).astype(F32)
+
+
 def route_reference(x, wr, top_k: int, renormalize: bool = True):
     """Plain fp32 router semantics (modeling_qwen3_moe.py:263-272): logits by
     float64 dot then rounded to fp32, fp32 softmax, stable top-k, renorm."""
@@ -426,18 +471,24 @@ def moe_layer_reference_packed(x, wr, w13_q, w13_s, w2_q, w2_s, top_k: int, grou
 
 def moe_layer_reference_shared(x, wr, w13_q, w13_s, w2_q, w2_s, top_k: int, num_shared: int, group: int = 64,
                                renormalize: bool = True, shared_gate=None, routed_scale: float = 1.0,
-                               router: str = "fixed"):
+                               router: str = "fixed", scoring: str = "softmax", score_bias=None,
+                               n_group: int = 1, topk_group: int = 1):
     """MoE block with shared experts on packed weights (experts E..E+m-1 are
     the m slices of the shared expert): routed output with weights times
     ``routed_scale``, plus g(t) * shared(x), g = sigmoid(x . shared_gate)
     (1 when None). Restates Qwen2MoeSparseMoeBlock.forward (transformers
     5.5.0 models/qwen2_moe/modeling_qwen2_moe.py: shared_expert_output scaled
     by F.sigmoid(shared_expert_gate(x)) and added to the routed output);
-    DeepSeek blocks are the ungated case. Returns (out, routed idx, routed w)."""
+    DeepSeek blocks are the ungated case, routed by
+    :func:`route_sigmoid_grouped` when ``scoring="sigmoid"``. Returns
+    (out, routed idx, routed w before routed_scale)."""
     x = np.asarray(x, dtype=F32)
     T = x.shape[0]
-    route = route_fixed_order if router == "fixed" else route_reference
-    _, _, idx, w = route(x, wr, top_k, renormalize)
+    if scoring == "sigmoid":
+        _, _, idx, w = route_sigmoid_grouped(x, wr, top_k, renormalize, score_bias, n_group, topk_group)
+    else:
+        route = route_fixed_order if router == "fixed" else route_reference
+        _, _, idx, w = route(x, wr, top_k, renormalize)
     E = wr.shape[0]
     if shared_gate is None:
         g = np.ones((T, 1), dtype=F32)

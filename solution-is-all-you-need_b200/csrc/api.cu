@@ -366,22 +366,69 @@ int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtyp
   return check_launch("combine");
 }
 
-size_t phmoe_workspace_size_shared(int T, int H, int E, int top_k, int I, int num_shared, int path) {
+size_t phmoe_workspace_size_ex(int T, int H, int E, int top_k, int I, int num_shared, int path) {
   if (T < 0 || H <= 0 || E < 1 || top_k < 1 || I <= 0 || num_shared < 0) return 0;
   if (path < PHMOE_PATH_AUTO || path > PHMOE_PATH_PREFILL) return 0;
   // the whole layer over E + m experts and k + m slots, plus the router's [T, k] choice
   return make_layout(T, H, E + num_shared, top_k + num_shared, I).total + round_up((size_t)T * top_k * 8, kAlign);
 }
 
-int phmoe_moe_layer_shared(const void* x, int x_dtype, const void* router_w, int w_dtype,
-                           const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
-                           const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
-                           int group_size, int renormalize, int num_shared, const void* shared_gate_w,
-                           float routed_scale, int path, void* out, int32_t* topk_idx_out,
-                           float* topk_w_out, void* workspace, size_t workspace_bytes, void* stream) {
+// Checks of the extended router options; PHMOE_OK when valid.
+int check_routing_ex(int E, int scoring, int n_group, int topk_group, float routed_scale) {
+  if (scoring != PHMOE_SCORING_SOFTMAX && scoring != PHMOE_SCORING_SIGMOID)
+    return fail(PHMOE_ERR_INVALID_ARG, "bad scoring code %d", scoring);
+  if (n_group > 1) {
+    if (scoring != PHMOE_SCORING_SIGMOID)
+      return fail(PHMOE_ERR_UNSUPPORTED, "group-limited routing is implemented for sigmoid scoring");
+    if (n_group > 32 || E % n_group || E / n_group < 2)
+      return fail(PHMOE_ERR_INVALID_ARG, "n_group must divide E into groups of >= 2 experts (n_group <= 32)");
+    if (topk_group < 1 || topk_group > n_group)
+      return fail(PHMOE_ERR_INVALID_ARG, "topk_group must be in [1, n_group]");
+  }
+  if (!(routed_scale > 0.f)) return fail(PHMOE_ERR_INVALID_ARG, "routed_scale must be > 0");
+  return PHMOE_OK;
+}
+
+void route_ex(const void* x, int x_dtype, const void* router_w, int w_dtype, int T, int H, int E, int top_k,
+              int renormalize, int scoring, const float* score_bias, int n_group, int topk_group, float scale,
+              float* logits, int32_t* idx, float* w, cudaStream_t st) {
+  if (scoring == PHMOE_SCORING_SOFTMAX && n_group <= 1 && !score_bias && scale == 1.0f)
+    launch_router(x, x_dtype, router_w, w_dtype, T, H, E, top_k, renormalize, logits, nullptr, idx, w, st);
+  else
+    launch_router_grouped(x, x_dtype, router_w, w_dtype, T, H, E, top_k, renormalize, score_bias,
+                          scoring == PHMOE_SCORING_SIGMOID ? n_group : 1, topk_group, scale, logits, idx, w, st);
+}
+
+int phmoe_router_ex(const void* x, int x_dtype, const void* router_w, int w_dtype, int T, int H,
+                    int E, int top_k, int renormalize, int scoring, const float* score_bias,
+                    int n_group, int topk_group, float routed_scale, float* logits,
+                    int32_t* topk_idx, float* topk_w, void* stream) {
+  g_last_error.clear();
+  if (int s = check_router_dims(T, H, E, top_k)) return s;
+  if (int s = check_routing_ex(E, scoring, n_group, topk_group, routed_scale)) return s;
+  if (scoring == PHMOE_SCORING_SOFTMAX && (score_bias || routed_scale != 1.0f))
+    return fail(PHMOE_ERR_UNSUPPORTED, "score_bias and routed_scale apply to sigmoid scoring");
+  if (!dtype_ok(x_dtype) || !dtype_ok(w_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  if (int s = check_router_smem(H, x_dtype)) return s;
+  if (T == 0) return PHMOE_OK;
+  if (!x || !router_w || !logits || !topk_idx || !topk_w) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned(x, 16) || !aligned(router_w, 16)) return fail(PHMOE_ERR_ALIGNMENT, "x and router_w must be 16-byte aligned");
+  route_ex(x, x_dtype, router_w, w_dtype, T, H, E, top_k, renormalize, scoring, score_bias, n_group, topk_group,
+           routed_scale, logits, topk_idx, topk_w, static_cast<cudaStream_t>(stream));
+  return check_launch("phmoe_router_ex");
+}
+
+int phmoe_moe_layer_ex(const void* x, int x_dtype, const void* router_w, int w_dtype,
+                       const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
+                       const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
+                       int group_size, int renormalize, int scoring, const float* score_bias,
+                       int n_group, int topk_group, int num_shared, const void* shared_gate_w,
+                       float routed_scale, int path, void* out, int32_t* topk_idx_out,
+                       float* topk_w_out, void* workspace, size_t workspace_bytes, void* stream) {
   g_last_error.clear();
   if (num_shared < 0 || num_shared > 32) return fail(PHMOE_ERR_INVALID_ARG, "num_shared must be in [0, 32]");
   if (int s = check_router_dims(T, H, E, top_k)) return s;
+  if (int s = check_routing_ex(E, scoring, n_group, topk_group, routed_scale)) return s;
   if (!dtype_ok(x_dtype) || !dtype_ok(w_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
   const int Et = E + num_shared, kt = top_k + num_shared;
   if (Et > 1024) return fail(PHMOE_ERR_INVALID_ARG, "E + num_shared must be <= 1024");
@@ -396,7 +443,7 @@ int phmoe_moe_layer_shared(const void* x, int x_dtype, const void* router_w, int
     return fail(PHMOE_ERR_ALIGNMENT, "x, router_w, shared_gate_w, packed weights and out must be 16-byte aligned");
   if (!aligned(w13_s, 4) || !aligned(w2_s, 4)) return fail(PHMOE_ERR_ALIGNMENT, "scales must be 4-byte aligned");
   const Layout L = make_layout(T, H, Et, kt, I);
-  const size_t need = phmoe_workspace_size_shared(T, H, E, top_k, I, num_shared, path);
+  const size_t need = phmoe_workspace_size_ex(T, H, E, top_k, I, num_shared, path);
   if (!aligned(workspace, kAlign)) return fail(PHMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   if (workspace_bytes < need) return fail(PHMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", need, workspace_bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -413,7 +460,8 @@ int phmoe_moe_layer_shared(const void* x, int x_dtype, const void* router_w, int
   float* h = reinterpret_cast<float*>(ws + L.h);
   float* y = reinterpret_cast<float*>(ws + L.y);
 
-  launch_router(x, x_dtype, router_w, w_dtype, T, H, E, top_k, renormalize, logits, nullptr, r_idx, r_w, st);
+  route_ex(x, x_dtype, router_w, w_dtype, T, H, E, top_k, renormalize, scoring, score_bias, n_group, topk_group,
+           1.0f, logits, r_idx, r_w, st);
   if (int s = check_launch("router")) return s;
   launch_shared_slots(x, x_dtype, shared_gate_w, w_dtype, r_idx, r_w, T, H, top_k, E, num_shared, routed_scale,
                       idx, wts, st);

@@ -75,6 +75,38 @@ __device__ __forceinline__ void unpack_word(uint32_t w, uint32_t (&p)[4]) {
   for (int i = 0; i < 4; ++i) p[i] = bf16x2_sub136(p[i]);
 }
 
+// One packed word -> p[i] = (e_{2i}, e_{2i+1}) as f16x2 holding nibble - 8
+// exactly. The fp16 magic 1024 (0x6400) has a 10-bit mantissa, so the
+// nibbles at bits 0-3 and at bits 4-7 of each 16-bit half both land inside
+// it, as 1024 + n and 1024 + 16n: one shift and four lop3 give the four
+// pairs, and one fma each removes the offset ((v - 1032), (v / 16 - 72)),
+// every result an exactly representable integer.
+__device__ __forceinline__ void unpack_word_f16(uint32_t w, uint32_t (&p)[4]) {
+  const uint32_t w8 = w >> 8;
+  uint32_t a, b, c, d;
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x64006400, 0xEA;" : "=r"(a) : "r"(w));
+  asm("lop3.b32 %0, %1, 0x00F000F0, 0x64006400, 0xEA;" : "=r"(b) : "r"(w));
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x64006400, 0xEA;" : "=r"(c) : "r"(w8));
+  asm("lop3.b32 %0, %1, 0x00F000F0, 0x64006400, 0xEA;" : "=r"(d) : "r"(w8));
+  const uint32_t one = 0x3C003C00u, m1032 = 0xE408E408u;       // 1.0, -1032.0
+  const uint32_t sixteenth = 0x2C002C00u, m72 = 0xD480D480u;   // 1/16, -72.0
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(p[0]) : "r"(a), "r"(one), "r"(m1032));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(p[1]) : "r"(b), "r"(sixteenth), "r"(m72));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(p[2]) : "r"(c), "r"(one), "r"(m1032));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(p[3]) : "r"(d), "r"(sixteenth), "r"(m72));
+}
+
+// D = A * B + C, m16n8k16, fp16 inputs, fp32 accumulate (register operands).
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                              const float (&c)[4]) {
+  asm(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1),
+        "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
+}
+
 // D = A * B + C, m16n8k16, bf16 inputs, fp32 accumulate (register operands).
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
                                                uint32_t b0, uint32_t b1, const float (&c)[4]) {

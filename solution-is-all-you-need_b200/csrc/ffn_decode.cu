@@ -45,9 +45,12 @@
 // order is a permutation applied to both operands, which a dot product does
 // not see.
 //
-// Precision: bf16 activations enter the MMA exactly; fp32 activations and the
-// intermediate h are split into bf16 hi + lo parts (two MMAs each), keeping
-// ~16 significant bits.
+// Precision: bf16 activations enter the gate/up MMAs exactly; fp32
+// activations are split into bf16 hi + lo parts (two MMAs each, ~16
+// significant bits). The intermediate h goes to the down projection as fp16
+// (11 significant bits; with fp32 activations as fp16 hi + lo, ~22 bits),
+// against weights unpacked exactly to fp16; an |h| above the fp16 range is
+// clamped to 65504 and raises bit 2 of the device error word.
 //
 // Every mbarrier wait is bounded: a waiting warp sleeps inside try_wait (a
 // suspend-time hint, woken when the phase completes, so waiting warps take no
@@ -326,28 +329,43 @@ __device__ __forceinline__ void gateup_group_mt(const RowWords<G>& g0, const Row
   }
 }
 
-// down partial of one group: acc += s * A.(B_hi + B_lo), A unpacked exactly.
-template <int G>
+// down partial of one group: acc += s * A.(B_hi [+ B_lo]), A unpacked exactly
+// to fp16, B the fp16 h plane(s).
+template <int G, bool kTwo>
 __device__ __forceinline__ void down_group(const RowWords<G>& a0, const RowWords<G>& a8,
                                            const BWords<G>& b, float s0, float s8, float (&acc)[4]) {
   float t[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int w = 0; w < G / 32; ++w) {
     uint32_t p0[4], p8[4];
-    unpack_word(a0.w[w], p0);
-    unpack_word(a8.w[w], p8);
+    unpack_word_f16(a0.w[w], p0);
+    unpack_word_f16(a8.w[w], p8);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int s = 2 * w + h;
       const uint32_t a[4] = {p0[2 * h], p8[2 * h], p0[2 * h + 1], p8[2 * h + 1]};
-      mma_bf16_16816(t, a, b.hi[2 * s], b.hi[2 * s + 1], t);
-      mma_bf16_16816(t, a, b.lo[2 * s], b.lo[2 * s + 1], t);
+      mma_f16_16816(t, a, b.hi[2 * s], b.hi[2 * s + 1], t);
+      if constexpr (kTwo) mma_f16_16816(t, a, b.lo[2 * s], b.lo[2 * s + 1], t);
     }
   }
   acc[0] = fmaf(s0, t[0], acc[0]);
   acc[1] = fmaf(s0, t[1], acc[1]);
   acc[2] = fmaf(s8, t[2], acc[2]);
   acc[3] = fmaf(s8, t[3], acc[3]);
+}
+
+// h as the down projection reads it: fp16, clamped to the fp16 range (a
+// clamp raises bit 2 of the device error word); with fp32 activations the
+// rounding remainder goes to a second fp16 plane.
+template <bool kTwo>
+__device__ __forceinline__ void store_h(float hv, __half* __restrict__ h_hi, __half* __restrict__ h_lo, size_t o) {
+  if (fabsf(hv) > 65504.0f) {
+    hv = copysignf(65504.0f, hv);
+    atomicOr(&g_ffn_error, 2);
+  }
+  const __half hb = __float2half_rn(hv);
+  h_hi[o] = hb;
+  if constexpr (kTwo) h_lo[o] = __float2half_rn(hv - __half2float(hb));
 }
 
 // ---------------------------------------------------------------------------
@@ -496,7 +514,7 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
                      const __grid_constant__ CUtensorMap s_map, int s_tma, const XT* __restrict__ x,
                      const int32_t* __restrict__ row_token, const int32_t* __restrict__ offsets,
                      const int32_t* __restrict__ active, const uint16_t* __restrict__ w13_s, int H, int I, int E,
-                     __nv_bfloat16* __restrict__ h_hi, __nv_bfloat16* __restrict__ h_lo) {
+                     __half* __restrict__ h_hi, __half* __restrict__ h_lo) {
   using C = RbCfg<G, XT>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -682,12 +700,7 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
           const int i = cu.tile * kRbRows + R0 + (q >= 2 ? 8 : 0);
           const int rr = cu.pass * kTok + 2 * c + (q & 1);
           if (rr < n && i < I) {
-            const float hv = silu_f32(gs[q]) * us[q];
-            const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
-            const __nv_bfloat16 lb = __float2bfloat16_rn(hv - __bfloat162float(hb));
-            const size_t o = (size_t)(row0 + rr) * I + i;
-            h_hi[o] = hb;
-            h_lo[o] = lb;
+            store_h<C::kF32>(silu_f32(gs[q]) * us[q], h_hi, h_lo, (size_t)(row0 + rr) * I + i);
           }
         }
       }
@@ -718,9 +731,9 @@ struct DownCfg {
   static constexpr int kRed = 8 * 4 * 32 * 4;
 };
 
-template <int G>
+template <int G, bool kTwo>
 __global__ void __launch_bounds__(kDownThreads, 1)
-ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __restrict__ h_lo,
+ffn_down_kernel(const __half* __restrict__ h_hi, const __half* __restrict__ h_lo,
                 const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                 const uint8_t* __restrict__ w2_q, const uint16_t* __restrict__ w2_s, int H, int I, int E,
                 float* __restrict__ y) {
@@ -762,15 +775,15 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
       if (pp * 2 * G < kel)
         cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
     }
-    // h rows of the pass (both planes), this K-chunk
+    // h rows of the pass (one fp16 plane, two with fp32 activations), this K-chunk
     const int row_p = meta.row0[cu.slot] + cu.pass * kTok;
     const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
 #pragma unroll
-    for (int q = threadIdx.x; q < 2 * kTok * C::kBch; q += kDownThreads) {
+    for (int q = threadIdx.x; q < (kTwo ? 2 : 1) * kTok * C::kBch; q += kDownThreads) {
       const int pl = q / (kTok * C::kBch);
       const int n = (q / C::kBch) % kTok, cc = q % C::kBch;
       if (n < nt && cc * 8 < kel) {
-        const __nv_bfloat16* src = (pl ? h_lo : h_hi) + (size_t)(row_p + n) * I + k0;
+        const __half* src = (pl ? h_lo : h_hi) + (size_t)(row_p + n) * I + k0;
         cp_async16(smem_u32(st + C::kB + (pl * kTok + n) * C::kBStride + cc * 16),
                    reinterpret_cast<const uint8_t*>(src) + cc * 16);
       }
@@ -814,12 +827,12 @@ ffn_down_kernel(const __nv_bfloat16* __restrict__ h_hi, const __nv_bfloat16* __r
       if (tok_ok) {
         const uint8_t* bb = st + C::kB + r * C::kBStride + g * G * 2 + b_off;
         lds_b_plane<G>(bb, b.hi);
-        lds_b_plane<G>(bb + kTok * C::kBStride, b.lo);
+        if constexpr (kTwo) lds_b_plane<G>(bb + kTok * C::kBStride, b.lo);
       } else {
 #pragma unroll
         for (int i = 0; i < G / 8; ++i) b.hi[i] = b.lo[i] = 0u;
       }
-      down_group<G>(a0, a8, b, __half2float(sc[lr0 * kScH + g]), __half2float(sc[(lr0 + 8) * kScH + g]), acc);
+      down_group<G, kTwo>(a0, a8, b, __half2float(sc[lr0 * kScH + g]), __half2float(sc[(lr0 + 8) * kScH + g]), acc);
     }
     if (cm.kc == nkc - 1) {
       if (kh == 1) {
@@ -906,7 +919,7 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
                      const __grid_constant__ CUtensorMap s_map, int s_tma, const XT* __restrict__ x,
                      const int32_t* __restrict__ row_token, const int32_t* __restrict__ offsets,
                      const int32_t* __restrict__ active, const uint16_t* __restrict__ w13_s, int H, int I, int E,
-                     __nv_bfloat16* __restrict__ h_hi, __nv_bfloat16* __restrict__ h_lo) {
+                     __half* __restrict__ h_hi, __half* __restrict__ h_lo) {
   using C = MtCfg<G, XT>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -1079,12 +1092,7 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
               const int i = cu.tile * kMtRows + R0 + (q >= 2 ? 8 : 0);
               const int rr = cu.pass * kMtTok + b * kTok + 2 * c + (q & 1);
               if (rr < n && i < I) {
-                const float hv = silu_f32(gs[q]) * us[q];
-                const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
-                const __nv_bfloat16 lb = __float2bfloat16_rn(hv - __bfloat162float(hb));
-                const size_t o = (size_t)(row0 + rr) * I + i;
-                h_hi[o] = hb;
-                h_lo[o] = lb;
+                store_h<C::kF32>(silu_f32(gs[q]) * us[q], h_hi, h_lo, (size_t)(row0 + rr) * I + i);
               }
             }
           }
@@ -1153,7 +1161,7 @@ __device__ __forceinline__ void lds_b_swz(const uint8_t* plane, int g, int r, in
   }
 }
 
-template <int G>
+template <int G, bool kTwo>
 __global__ void __launch_bounds__(kGuThreads, 1)
 ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap s_map,
                     const __grid_constant__ CUtensorMap hi_map, const __grid_constant__ CUtensorMap lo_map,
@@ -1210,11 +1218,12 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
       const int wrow = meta.e[cu.slot] * H + cu.tile * kDnRows;
       const int hrow = meta.row0[cu.slot] + cu.pass * kTok;
       const uint32_t sbytes = s_mode == 0 ? (uint32_t)kDnRows * (kDnKc / G) * 2 : (s_mode == 1 ? sbytes_block : 0u);
-      if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(2 * kDnRows * 128) + sbytes + 2u * C::kPlane);
+      if (lane == 0)
+        mbar_arrive_expect_tx(full, (uint32_t)(2 * kDnRows * 128) + sbytes + (kTwo ? 2u : 1u) * C::kPlane);
       __syncwarp();
       if (lane == 0) tma_load_3d(smem_u32(st + C::kW), &w_map, 0, wrow, k0 / 256, full);
       if (lane == 1) tma_load_3d(smem_u32(st + C::kB), &hi_map, 0, hrow, k0 / 64, full);
-      if (lane == 2) tma_load_3d(smem_u32(st + C::kB + C::kPlane), &lo_map, 0, hrow, k0 / 64, full);
+      if (kTwo && lane == 2) tma_load_3d(smem_u32(st + C::kB + C::kPlane), &lo_map, 0, hrow, k0 / 64, full);
       if (s_mode == 0) {
         if (lane == 3) tma_load_2d(smem_u32(st + C::kS), &s_map, k0 / G, wrow, full);
       } else if (s_mode == 1) {
@@ -1266,8 +1275,8 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
         const RowWords<G> a8 = lds_row<G>(st + C::kW + swz_off_rows(lr0 + 8, kb, kDnRows));
         BWords<G> b;
         lds_b_swz<G>(st + C::kB, g, r, c, b.hi);
-        lds_b_swz<G>(st + C::kB + C::kPlane, g, r, c, b.lo);
-        down_group<G>(a0, a8, b, __half2float(sc[(lr0 * srow) / 2 + goff + g]),
+        if constexpr (kTwo) lds_b_swz<G>(st + C::kB + C::kPlane, g, r, c, b.lo);
+        down_group<G, kTwo>(a0, a8, b, __half2float(sc[(lr0 * srow) / 2 + goff + g]),
                       __half2float(sc[((lr0 + 8) * srow) / 2 + goff + g]), acc);
       }
     }
@@ -1368,8 +1377,8 @@ bool make_scale_map(CUtensorMap* map, const uint16_t* w13_s, long long rows, int
 
 template <int G, typename XT>
 int launch_gateup_mt(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
-                     const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
-                     __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
+                     const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __half* h_hi,
+                     __half* h_lo, int grid, cudaStream_t st) {
   const size_t smem = MtCfg<G, XT>::smem(E);
   if (smem > kMaxSmem) return PHMOE_ERR_UNSUPPORTED;
   const int box_chunks = std::min(H, kMtKc) / 256;
@@ -1387,8 +1396,8 @@ int launch_gateup_mt(const void* x, const int32_t* row_token, const int32_t* off
 
 template <int G, typename XT>
 int launch_gateup_rb(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
-                     const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __nv_bfloat16* h_hi,
-                     __nv_bfloat16* h_lo, int grid, cudaStream_t st) {
+                     const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __half* h_hi,
+                     __half* h_lo, int grid, cudaStream_t st) {
   const int box_chunks = std::min(H, kRbKc) / 256;
   alignas(64) CUtensorMap map, smap;
   const int mode = make_w13_map(&map, w13_q, (long long)E * 2 * I, H, box_chunks, kRbRows);
@@ -1421,20 +1430,20 @@ size_t down_smem(int E) {
   return (size_t)C::kStages * C::kStage + C::kRed + (size_t)(4 * E + 4) * 4;
 }
 
-template <int G>
-void launch_down(const __nv_bfloat16* h_hi, const __nv_bfloat16* h_lo, const int32_t* offsets,
+template <int G, bool kTwo>
+void launch_down(const __half* h_hi, const __half* h_lo, const int32_t* offsets,
                  const int32_t* active, const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, float* y,
                  int grid, cudaStream_t st) {
   const size_t smem = down_smem<G>(E);
-  auto k = ffn_down_kernel<G>;
+  auto k = ffn_down_kernel<G, kTwo>;
   set_smem(k, smem);
   k<<<grid, kDownThreads, smem, st>>>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
 }
 
 // TMA-fed down projection; returns false (nothing launched) when the shape
 // or the tensor maps do not allow it.
-template <int G>
-bool launch_down_tma(const __nv_bfloat16* h_hi, const __nv_bfloat16* h_lo, long long R, const int32_t* offsets,
+template <int G, bool kTwo>
+bool launch_down_tma(const __half* h_hi, const __half* h_lo, long long R, const int32_t* offsets,
                      const int32_t* active, const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, float* y,
                      int grid, cudaStream_t st) {
   if (I % 256 || H % kDnRows || R <= 0) return false;
@@ -1453,13 +1462,13 @@ bool launch_down_tma(const __nv_bfloat16* h_hi, const __nv_bfloat16* h_lo, long 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return false;
   }
-  const __nv_bfloat16* planes[2] = {h_hi, h_lo};
+  const __half* planes[2] = {h_hi, h_lo};
   CUtensorMap* pm[2] = {&hm, &lm};
   for (int p = 0; p < 2; ++p) {
     const cuuint64_t dims[3] = {64, (cuuint64_t)R, (cuuint64_t)(I / 64)};
     const cuuint64_t strides[2] = {(cuuint64_t)I * 2, 128};
     const cuuint32_t box[3] = {64, (cuuint32_t)kTok, 8};
-    if (enc(pm[p], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<__nv_bfloat16*>(planes[p]), dims, strides, box, e3,
+    if (enc(pm[p], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<__half*>(planes[p]), dims, strides, box, e3,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return false;
@@ -1479,7 +1488,7 @@ bool launch_down_tma(const __nv_bfloat16* h_hi, const __nv_bfloat16* h_lo, long 
   if (s_mode == 2 && (size_t)kDnRows * NG * 2 <= (size_t)kDnScaleBytes &&
       (reinterpret_cast<uintptr_t>(w2_s) & 15) == 0)
     s_mode = 1;
-  auto k = ffn_down_tma_kernel<G>;
+  auto k = ffn_down_tma_kernel<G, kTwo>;
   set_smem(k, smem);
   k<<<grid, kGuThreads, smem, st>>>(wm, sm, hm, lm, s_mode, offsets, active, w2_s, H, I, E, y);
   return true;
@@ -1505,8 +1514,8 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
   const long long R = (long long)T * top_k;
   if (R == 0) return PHMOE_OK;
   if (G != 32 && G != 64) return PHMOE_ERR_UNSUPPORTED;
-  __nv_bfloat16* h_hi = reinterpret_cast<__nv_bfloat16*>(h);
-  __nv_bfloat16* h_lo = h_hi + (size_t)R * I;
+  __half* h_hi = reinterpret_cast<__half*>(h);  // fp16 planes: hi, then lo (fp32 activations only)
+  __half* h_lo = h_hi + (size_t)R * I;
   const int grid = device_sm_count();
   const bool f32 = x_dtype == PHMOE_DTYPE_F32;
   // multi-token gate/up items from kMtMinRowsPerExpert expected rows per
@@ -1537,11 +1546,18 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
   }
   if (s) return s;
   if (mid_event) cudaEventRecord(mid_event, st);
-  const bool tma = G == 64 ? launch_down_tma<64>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st)
-                           : launch_down_tma<32>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+  bool tma;
+  if (G == 64)
+    tma = f32 ? launch_down_tma<64, true>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st)
+              : launch_down_tma<64, false>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+  else
+    tma = f32 ? launch_down_tma<32, true>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st)
+              : launch_down_tma<32, false>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
   if (!tma) {
-    if (G == 64) launch_down<64>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
-    else launch_down<32>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+    if (G == 64 && f32) launch_down<64, true>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+    else if (G == 64) launch_down<64, false>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+    else if (f32) launch_down<32, true>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+    else launch_down<32, false>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
   }
   note_launches(2);
   return PHMOE_OK;

@@ -45,6 +45,9 @@ int launch_gguf_q4_0(const void* blocks, long long rows, int K, uint8_t* packed,
 int launch_gguf_q4_k(const void* blocks, long long rows, int K, int G, uint8_t* packed, uint16_t* scales,
                      cudaStream_t st);
 int launch_gguf_q4_k_dequant(const void* blocks, long long n, float* out, cudaStream_t st);
+int launch_router_grouped(const void* x, int x_dtype, const void* wr, int w_dtype, int T, int H, int E, int top_k,
+                          int renormalize, const float* bias, int n_group, int topk_group, float scale,
+                          float* logits, int32_t* topk_idx, float* topk_w, cudaStream_t st);
 int launch_shared_slots(const void* x, int x_dtype, const void* gate_w, int w_dtype, const int32_t* idx,
                         const float* w, int T, int H, int k, int E, int m, float routed_scale, int32_t* idx_out,
                         float* w_out, cudaStream_t st);

@@ -319,6 +319,109 @@ router_topk_kernel(const float* __restrict__ logits, int T, int E, int top_k, in
   }
 }
 
+// sigmoid(x) from exp_fixed (so the CPU restatement replays it bit for bit).
+__device__ __forceinline__ float sigmoid_fixed(float x) {
+  if (x >= 0.0f) return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_fixed(-x)));
+  const float e = exp_fixed(x);
+  return __fdiv_rn(e, __fadd_rn(1.0f, e));
+}
+
+// DeepSeek-V3 routing (transformers 5.5.0 models/deepseek_v3/modeling_deepseek_v3.py
+// DeepseekV3MoE.route_tokens_to_experts): s = sigmoid(logit); choice c = s +
+// bias[e]; the E experts form n_group groups of E/n_group, a group scores
+// the sum of its two largest c, the topk_group best groups stay and the
+// others' c become 0; the top_k largest c are picked and weighted by their
+// s, renormalised by (sum + 1e-20) when asked, times `scale`. Ties -> lower
+// index (groups and experts). One warp per token.
+template <int EPL>
+__global__ void __launch_bounds__(256)
+router_topk_grouped_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E,
+                           int top_k, int n_group, int topk_group, int renormalize, float scale,
+                           int32_t* __restrict__ topk_idx, float* __restrict__ topk_w) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t >= T) return;
+  const float* lrow = logits + (size_t)t * E;
+  float sc[EPL], c[EPL];
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    if (e < E) {
+      sc[i] = sigmoid_fixed(lrow[e]);
+      c[i] = bias ? __fadd_rn(sc[i], bias[e]) : sc[i];
+    } else {
+      sc[i] = 0.f;
+      c[i] = -INFINITY;
+    }
+  }
+  if (n_group > 1) {
+    const int gs = E / n_group;
+    float mine = -INFINITY;  // lane g: score of group g
+    for (int g = 0; g < n_group; ++g) {
+      float a = -INFINITY, b = -INFINITY;  // two largest c of this lane's members of group g
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E && e / gs == g) {
+          if (c[i] > a) { b = a; a = c[i]; } else if (c[i] > b) { b = c[i]; }
+        }
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, a, off), ob = __shfl_xor_sync(0xffffffffu, b, off);
+        const float na = fmaxf(a, oa);
+        b = fmaxf(fminf(a, oa), fmaxf(b, ob));
+        a = na;
+      }
+      if (lane == g) mine = __fadd_rn(a, b);
+    }
+    uint32_t keep = 0;
+    for (int r = 0; r < topk_group; ++r) {
+      float bv = (lane < n_group && !((keep >> lane) & 1u)) ? mine : -INFINITY;
+      int bi = (lane < n_group && !((keep >> lane) & 1u)) ? lane : 0x7fffffff;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      keep |= 1u << bi;
+    }
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && !((keep >> (e / gs)) & 1u)) c[i] = 0.0f;  // masked_fill(~mask, 0.0)
+    }
+  }
+  uint32_t taken = 0;
+  float my_val = 0.f, sum_sel = 0.f;
+  int my_idx = 0;
+  for (int j = 0; j < top_k; ++j) {
+    float bv = -INFINITY, bs = 0.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && !((taken >> i) & 1u) && (c[i] > bv || (c[i] == bv && e < bi))) { bv = c[i]; bi = e; bs = sc[i]; }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      const float os = __shfl_xor_sync(0xffffffffu, bs, off);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; bs = os; }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    sum_sel = __fadd_rn(sum_sel, bs);
+    if (lane == j) { my_val = bs; my_idx = bi; }
+  }
+  if (lane < top_k) {
+    const float w = renormalize ? __fdiv_rn(my_val, __fadd_rn(sum_sel, 1e-20f)) : my_val;
+    topk_idx[(size_t)t * top_k + lane] = my_idx;
+    topk_w[(size_t)t * top_k + lane] = __fmul_rn(w, scale);
+  }
+}
+
 template <typename XT, typename WT, int TT>
 void launch_logits_tt(const void* x, const void* wr, int T, int H, int E, float* logits,
                       cudaStream_t st) {
@@ -343,10 +446,9 @@ void launch_logits(const void* x, const void* wr, int T, int H, int E, float* lo
 
 }  // namespace
 
-int launch_router(const void* x, int x_dtype, const void* wr, int w_dtype, int T, int H, int E,
-                  int top_k, int renormalize, float* logits, float* probs, int32_t* topk_idx,
-                  float* topk_w, cudaStream_t st) {
-  if (T == 0) return PHMOE_OK;
+namespace {
+void launch_router_logits(const void* x, int x_dtype, const void* wr, int w_dtype, int T, int H, int E, float* logits,
+                          cudaStream_t st) {
   if (x_dtype == PHMOE_DTYPE_BF16 && w_dtype == PHMOE_DTYPE_BF16 && T >= kBlockRouterMinTokens) {
     dim3 grid((E + kBlkE * kBlkWarpsE - 1) / (kBlkE * kBlkWarpsE), (T + kBlkT * kBlkWarpsT - 1) / (kBlkT * kBlkWarpsT));
     router_logits_block_kernel<<<grid, kBlkWarpsT * kBlkWarpsE * 32, 0, st>>>(
@@ -359,6 +461,34 @@ int launch_router(const void* x, int x_dtype, const void* wr, int w_dtype, int T
     launch_logits<float, __nv_bfloat16>(x, wr, T, H, E, logits, st);
   else
     launch_logits<float, float>(x, wr, T, H, E, logits, st);
+}
+}  // namespace
+
+int launch_router_grouped(const void* x, int x_dtype, const void* wr, int w_dtype, int T, int H, int E, int top_k,
+                          int renormalize, const float* bias, int n_group, int topk_group, float scale,
+                          float* logits, int32_t* topk_idx, float* topk_w, cudaStream_t st) {
+  if (T == 0) return PHMOE_OK;
+  if (E > 1024) return PHMOE_ERR_UNSUPPORTED;
+  launch_router_logits(x, x_dtype, wr, w_dtype, T, H, E, logits, st);
+  const int grid = (T + 7) / 8;
+  if (E <= 128)
+    router_topk_grouped_kernel<4><<<grid, 256, 0, st>>>(logits, bias, T, E, top_k, n_group, topk_group, renormalize,
+                                                        scale, topk_idx, topk_w);
+  else if (E <= 256)
+    router_topk_grouped_kernel<8><<<grid, 256, 0, st>>>(logits, bias, T, E, top_k, n_group, topk_group, renormalize,
+                                                        scale, topk_idx, topk_w);
+  else
+    router_topk_grouped_kernel<32><<<grid, 256, 0, st>>>(logits, bias, T, E, top_k, n_group, topk_group, renormalize,
+                                                         scale, topk_idx, topk_w);
+  note_launches(2);
+  return PHMOE_OK;
+}
+
+int launch_router(const void* x, int x_dtype, const void* wr, int w_dtype, int T, int H, int E,
+                  int top_k, int renormalize, float* logits, float* probs, int32_t* topk_idx,
+                  float* topk_w, cudaStream_t st) {
+  if (T == 0) return PHMOE_OK;
+  launch_router_logits(x, x_dtype, wr, w_dtype, T, H, E, logits, st);
   const int grid = (T + 7) / 8;
   if (E <= 128)
     router_topk_kernel<4><<<grid, 256, 0, st>>>(logits, T, E, top_k, renormalize, probs, topk_idx, topk_w);

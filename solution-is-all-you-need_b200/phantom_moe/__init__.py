@@ -24,6 +24,7 @@ from .layer import (
     pack_experts_shared,
     quantize_int4,
     router,
+    router_ex,
     workspace_bytes,
 )
 
@@ -48,6 +49,7 @@ __all__ = [
     "pack_experts_shared",
     "quantize_int4",
     "router",
+    "router_ex",
     "uninstall",
     "workspace_bytes",
 ]

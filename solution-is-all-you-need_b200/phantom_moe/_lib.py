@@ -23,6 +23,9 @@ PHMOE_ERR_ALIGNMENT = -5
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 
+SCORING_SOFTMAX = 0
+SCORING_SIGMOID = 1
+
 PATH_AUTO = 0
 PATH_DECODE = 1
 PATH_PREFILL = 2
@@ -58,9 +61,10 @@ SIGNATURES = {
                              _P, _P, _P, _P, _SZ, _P]),
     "phmoe_moe_layer_noalloc": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
                                      _P, _P, _P, _P]),
-    "phmoe_workspace_size_shared": (_SZ, [_I, _I, _I, _I, _I, _I, _I]),
-    "phmoe_moe_layer_shared": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P,
-                                    ctypes.c_float, _I, _P, _P, _P, _P, _SZ, _P]),
+    "phmoe_router_ex": (_I, [_P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _P, _I, _I, ctypes.c_float, _P, _P, _P, _P]),
+    "phmoe_workspace_size_ex": (_SZ, [_I, _I, _I, _I, _I, _I, _I]),
+    "phmoe_moe_layer_ex": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _I, _I,
+                                _I, _P, ctypes.c_float, _I, _P, _P, _P, _P, _SZ, _P]),
     "phmoe_gguf_q4_0_to_packed": (_I, [_P, _LL, _I, _P, _P, _P]),
     "phmoe_gguf_q4_k_to_packed": (_I, [_P, _LL, _I, _I, _P, _P, _P]),
     "phmoe_gguf_q4_k_dequantize": (_I, [_P, _LL, _P, _P]),

@@ -372,7 +372,8 @@ def _detect_config(cfg: Dict[str, Any]) -> Optional[MoeSpec]:
         return MoeSpec("deepseek", E, int(cfg.get("num_experts_per_tok", 8)), H, I, L,
                        norm_topk_prob=bool(cfg.get("norm_topk_prob", True)),
                        shared_intermediate_size=int(cfg.get("n_shared_experts") or 0) * I,
-                       scoring=str(cfg.get("scoring_func", "softmax")),
+                       scoring=str(cfg.get("scoring_func", "sigmoid" if "v3" in mt or any("v3" in a for a in archs)
+                                           else "softmax")),
                        routed_scaling_factor=float(cfg.get("routed_scaling_factor", 1.0)),
                        n_group=int(cfg.get("n_group") or 1), topk_group=int(cfg.get("topk_group") or 1))
     if "mixtral" in mt or any("mixtral" in a for a in archs):

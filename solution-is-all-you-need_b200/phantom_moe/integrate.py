@@ -4,14 +4,17 @@ The MoE path PHANTOM executes is transformers' sparse-MoE block, reached from
 ``from_pretrained`` (python/phantom/phantom_cli.py:1393-1410,
 phantom_tui.py:2140-2153): ``Qwen3MoeSparseMoeBlock.forward`` (transformers
 5.5.0 models/qwen3_moe/modeling_qwen3_moe.py:281-286), and likewise
-``MixtralSparseMoeBlock`` and ``Qwen2MoeSparseMoeBlock``. ``install_into``
+``MixtralSparseMoeBlock``, ``Qwen2MoeSparseMoeBlock`` and ``DeepseekV3MoE``
+(models/deepseek_v3/modeling_deepseek_v3.py). ``install_into``
 packs each block's weights once into the int4 layout on the GPU (router
 ``gate.weight [E, H]``, ``experts.gate_up_proj [E, 2I, H]``,
 ``experts.down_proj [E, H, I]``, and for Qwen2-MoE the shared expert and its
-sigmoid gate) and replaces the block's ``forward`` with :func:`moe_layer`, so
-``model.generate`` runs the experts on this library's kernels. Routing
-semantics follow each block's router: top-k renormalisation per
-``norm_topk_prob`` (Mixtral always renormalises).
+sigmoid gate, for DeepSeek-V3 the shared experts, the score-correction bias
+and the group settings) and replaces the block's ``forward`` with
+:func:`moe_layer`, so ``model.generate`` runs the experts on this library's
+kernels. Routing semantics follow each block's router: top-k
+renormalisation per ``norm_topk_prob`` (Mixtral always renormalises);
+DeepSeek-V3's sigmoid scoring, group-limited choice and routed scaling.
 """
 
 from __future__ import annotations
@@ -24,7 +27,7 @@ import torch
 
 from .layer import PackedExperts, moe_layer, pack_experts, pack_experts_shared
 
-SUPPORTED_BLOCKS = ("Qwen3MoeSparseMoeBlock", "MixtralSparseMoeBlock", "Qwen2MoeSparseMoeBlock")
+SUPPORTED_BLOCKS = ("Qwen3MoeSparseMoeBlock", "MixtralSparseMoeBlock", "Qwen2MoeSparseMoeBlock", "DeepseekV3MoE")
 
 
 @dataclasses.dataclass
@@ -39,6 +42,7 @@ class InstalledMoe:
     shared_gate: Optional[torch.Tensor]
     original_forward: object
     dense_kept: bool
+    routing: dict = dataclasses.field(default_factory=dict)  # extra moe_layer routing arguments
 
 
 def find_moe_blocks(model: torch.nn.Module) -> List[Tuple[str, torch.nn.Module]]:
@@ -61,22 +65,32 @@ def _pack_block(blk: torch.nn.Module, group_size: int, path: str, keep_dense: bo
     rdt = _router_dtype(gate.weight)
     shared_gate = None
     with torch.no_grad():
-        if kind == "Qwen2MoeSparseMoeBlock":
-            se = blk.shared_expert
+        se = blk.shared_expert if kind == "Qwen2MoeSparseMoeBlock" else getattr(blk, "shared_experts", None)
+        if se is not None:
             packed = pack_experts_shared(gu.float(), dn.float(), se.gate_proj.weight.float(), se.up_proj.weight.float(),
                                          se.down_proj.weight.float(), group_size)
-            shared_gate = blk.shared_expert_gate.weight.detach().reshape(-1).to(rdt).contiguous()
         else:
             packed = pack_experts(gu.float(), dn.float(), group_size)
-    renorm = True if kind == "MixtralSparseMoeBlock" else bool(getattr(gate, "norm_topk_prob", True))
-    st = InstalledMoe(kind, packed, gate.weight.detach().to(rdt).contiguous(), int(gate.top_k), renorm, path,
-                      shared_gate, blk.forward, keep_dense)
+        if kind == "Qwen2MoeSparseMoeBlock":
+            shared_gate = blk.shared_expert_gate.weight.detach().reshape(-1).to(rdt).contiguous()
+    routing = {}
+    if kind == "DeepseekV3MoE":
+        renorm, top_k = bool(blk.norm_topk_prob), int(blk.top_k)
+        routing = dict(scoring="sigmoid", score_bias=gate.e_score_correction_bias.detach().float().contiguous(),
+                       n_group=int(blk.n_group), topk_group=int(blk.topk_group),
+                       routed_scale=float(blk.routed_scaling_factor))
+    else:
+        renorm = True if kind == "MixtralSparseMoeBlock" else bool(getattr(gate, "norm_topk_prob", True))
+        top_k = int(gate.top_k)
+    st = InstalledMoe(kind, packed, gate.weight.detach().to(rdt).contiguous(), top_k, renorm, path,
+                      shared_gate, blk.forward, keep_dense, routing)
     if not keep_dense:  # the packed copy replaces the dense expert weights
         empty = torch.empty(0, device=dev, dtype=gu.dtype)
         experts.gate_up_proj.data = empty
         experts.down_proj.data = empty
-        if kind == "Qwen2MoeSparseMoeBlock":
-            for lin in (blk.shared_expert.gate_proj, blk.shared_expert.up_proj, blk.shared_expert.down_proj):
+        se = blk.shared_expert if kind == "Qwen2MoeSparseMoeBlock" else getattr(blk, "shared_experts", None)
+        if se is not None:
+            for lin in (se.gate_proj, se.up_proj, se.down_proj):
                 lin.weight.data = torch.empty(0, device=dev, dtype=lin.weight.dtype)
     return st
 
@@ -91,7 +105,7 @@ def _forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
     p = st.packed
     out = moe_layer(x.contiguous(), st.router_weight, p.w13_q, p.w13_scales, p.w2_q, p.w2_scales, st.top_k,
                     renormalize=st.renormalize, group_size=p.group_size, path=st.path, num_shared=p.num_shared,
-                    shared_gate_weight=st.shared_gate)
+                    shared_gate_weight=st.shared_gate, **st.routing)
     return out.to(dt).reshape(shape)
 
 

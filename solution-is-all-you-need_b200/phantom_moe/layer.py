@@ -23,6 +23,7 @@ from . import _lib
 
 _DT = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}
 _PATHS = {"auto": _lib.PATH_AUTO, "decode": _lib.PATH_DECODE, "prefill": _lib.PATH_PREFILL}
+_SCORING = {"softmax": _lib.SCORING_SOFTMAX, "sigmoid": _lib.SCORING_SIGMOID}
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -167,6 +168,24 @@ def router(x: torch.Tensor, router_weight: torch.Tensor, top_k: int, renormalize
               _stream())
     if return_probs:
         return idx, w, logits, probs
+    return idx, w, logits
+
+
+def router_ex(x: torch.Tensor, router_weight: torch.Tensor, top_k: int, renormalize: bool = True,
+              scoring: str = "sigmoid", score_bias: torch.Tensor | None = None, n_group: int = 1,
+              topk_group: int = 1, routed_scale: float = 1.0):
+    """DeepSeek-V3 style router (``phmoe_router_ex``): returns
+    ``(topk_idx int32[T,k], topk_w fp32[T,k], logits fp32[T,E])``."""
+    _need_cuda("x", x)
+    _need_cuda("router_weight", router_weight)
+    T, H = x.shape
+    E = router_weight.shape[0]
+    logits = torch.empty(T, E, dtype=torch.float32, device=x.device)
+    idx = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
+    _lib.call("phmoe_router_ex", _ptr(x), _DT[x.dtype], _ptr(router_weight), _DT[router_weight.dtype], T, H, E,
+              top_k, int(bool(renormalize)), _SCORING[scoring], _ptr(score_bias), n_group, topk_group,
+              float(routed_scale), _ptr(logits), _ptr(idx), _ptr(w), _stream())
     return idx, w, logits
 
 
@@ -342,7 +361,9 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
               renormalize: bool = True, group_size: int = 64, ep_group=None, *,
               path: str = "auto", return_routing: bool = False, out: torch.Tensor | None = None,
               workspace: torch.Tensor | None = None, num_shared: int = 0,
-              shared_gate_weight: torch.Tensor | None = None, routed_scale: float = 1.0):
+              shared_gate_weight: torch.Tensor | None = None, routed_scale: float = 1.0,
+              scoring: str = "softmax", score_bias: torch.Tensor | None = None, n_group: int = 1,
+              topk_group: int = 1):
     """Sparse-MoE layer: router -> dispatch -> grouped int4 SwiGLU FFN -> combine.
 
     ``hidden_states`` is ``[T, H]`` or ``[B, S, H]`` (bf16 or fp32); the result
@@ -361,6 +382,11 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
     first E, every token also goes to the m slices with weight
     ``sigmoid(x . shared_gate_weight)`` (``[H]`` or ``[1, H]``; 1 when None),
     and the routed weights are multiplied by ``routed_scale``.
+
+    DeepSeek-V3 routing: ``scoring="sigmoid"`` with an optional fp32
+    ``score_bias [E]`` (``e_score_correction_bias``, used for the choice
+    only) and group-limited selection (``n_group`` groups, the
+    ``topk_group`` best kept); see ``phmoe_router_ex`` in ``phmoe.h``.
     """
     if ep_group is not None:
         from . import ep as _ep
@@ -387,8 +413,15 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
             _need_cuda("shared_gate_weight", shared_gate_weight)
             if shared_gate_weight.numel() != H or shared_gate_weight.dtype != router_weight.dtype:
                 raise ValueError("shared_gate_weight must hold H values of router_weight's dtype")
-    elif shared_gate_weight is not None or routed_scale != 1.0:
-        raise ValueError("shared_gate_weight / routed_scale need num_shared > 0")
+    elif shared_gate_weight is not None:
+        raise ValueError("shared_gate_weight needs num_shared > 0")
+    if scoring not in _SCORING:
+        raise ValueError(f"scoring must be one of {list(_SCORING)}")
+    if score_bias is not None:
+        _need_cuda("score_bias", score_bias)
+        _need_dtype("score_bias", score_bias, (torch.float32,))
+        _need_shape("score_bias", score_bias, (E,))
+    extended = bool(num_shared) or routed_scale != 1.0 or scoring != "softmax" or score_bias is not None or n_group > 1
     _need_shape("router_weight", router_weight, (E, H))
     if path not in _PATHS:
         raise ValueError(f"path must be one of {list(_PATHS)}")
@@ -402,8 +435,8 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
     idx = torch.empty(T, top_k, dtype=torch.int32, device=dev) if return_routing else None
     wts = torch.empty(T, top_k, dtype=torch.float32, device=dev) if return_routing else None
     lib = _lib.load()
-    if num_shared:
-        need = lib.phmoe_workspace_size_shared(T, H, E, top_k, I, num_shared, _PATHS[path])
+    if extended:
+        need = lib.phmoe_workspace_size_ex(T, H, E, top_k, I, num_shared, _PATHS[path])
     else:
         need = lib.phmoe_workspace_size(T, H, E, top_k, I, _PATHS[path])
     if workspace is None:
@@ -414,11 +447,12 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
         if workspace.numel() < need:
             raise ValueError(f"workspace needs {need} bytes (got {workspace.numel()})")
         ws = workspace
-    if num_shared:
-        _lib.call("phmoe_moe_layer_shared", _ptr(x), _DT[x.dtype], _ptr(router_weight), _DT[router_weight.dtype],
+    if extended:
+        _lib.call("phmoe_moe_layer_ex", _ptr(x), _DT[x.dtype], _ptr(router_weight), _DT[router_weight.dtype],
                   _ptr(w13_q), _ptr(w13_scales), _ptr(w2_q), _ptr(w2_scales), T, H, E, top_k, I, group_size,
-                  int(bool(renormalize)), num_shared, _ptr(shared_gate_weight), float(routed_scale),
-                  _PATHS[path], _ptr(out), _ptr(idx), _ptr(wts), _ptr(ws), ws.numel(), _stream())
+                  int(bool(renormalize)), _SCORING[scoring], _ptr(score_bias), n_group, topk_group, num_shared,
+                  _ptr(shared_gate_weight), float(routed_scale), _PATHS[path], _ptr(out), _ptr(idx), _ptr(wts),
+                  _ptr(ws), ws.numel(), _stream())
     else:
         _lib.call("phmoe_moe_layer", _ptr(x), _DT[x.dtype], _ptr(router_weight), _DT[router_weight.dtype],
                   _ptr(w13_q), _ptr(w13_scales), _ptr(w2_q), _ptr(w2_scales), T, H, E, top_k, I, group_size,

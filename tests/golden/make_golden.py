@@ -32,6 +32,9 @@ What each fixture pins, and which reference code produced it:
   intermediate size, norm_topk_prob False) in fp32 on CPU, on the
   dequantised int4 values of the packed E + 4 experts stored alongside
   (routed experts, then the shared expert cut into 4 slices).
+* ``deepseek_route.npz`` - transformers' ``DeepseekV3MoE.route_tokens_to_experts``
+  (sigmoid scores, e_score_correction_bias, 16 experts in 4 groups, 2 groups
+  kept, top-4, renormalised, routed_scaling_factor 2.5) on seeded fp32 logits.
 * ``qwen3_cfg1.npz`` - the same Qwen3 block at BASELINE config 1 (H=2048,
   128 experts, top-8, I=768, T=16, fp32 inputs drawn from
   ``torch.Generator().manual_seed(0)``). The 320 MB of packed weights are
@@ -224,6 +227,24 @@ def make_qwen2moe_block(name, T, H, E, k, I, m, group, seed):
                         idx=idx.numpy().astype(np.int32), scores=scores.numpy().astype(np.float32))
 
 
+def make_deepseek_route(name, T=64, E=16, n_group=4, topk_group=2, k=4, scale=2.5, seed=15):
+    from transformers.models.deepseek_v3.configuration_deepseek_v3 import DeepseekV3Config
+    from transformers.models.deepseek_v3.modeling_deepseek_v3 import DeepseekV3MoE
+    cfg = DeepseekV3Config(hidden_size=64, n_routed_experts=E, n_group=n_group, topk_group=topk_group,
+                           num_experts_per_tok=k, moe_intermediate_size=32, n_shared_experts=1,
+                           routed_scaling_factor=scale, norm_topk_prob=True)
+    moe = DeepseekV3MoE(cfg).eval()
+    g = torch.Generator().manual_seed(seed)
+    logits = torch.randn(T, E, generator=g) * 2.0
+    bias = torch.randn(E, generator=g) * 0.1
+    with torch.no_grad():
+        moe.gate.e_score_correction_bias.copy_(bias)
+        idx, w = moe.route_tokens_to_experts(logits)
+    np.savez_compressed(OUT / name, logits=logits.numpy(), bias=bias.numpy(), idx=idx.numpy().astype(np.int32),
+                        w=w.numpy().astype(np.float32), cfg=np.array([E, n_group, topk_group, k], np.int32),
+                        scale=np.float32(scale))
+
+
 def gen_cfg1_inputs():
     """BASELINE config 1 inputs (documented procedure; the GPU tests repeat it)."""
     g = torch.Generator().manual_seed(0)
@@ -258,14 +279,17 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
     ap.add_argument("--skip-cfg1", action="store_true", help="keep the existing qwen3_cfg1.npz")
-    ap.add_argument("--only", choices=["q4_k", "qwen2moe"], help="regenerate one fixture only")
+    ap.add_argument("--only", choices=["q4_k", "qwen2moe", "deepseek"], help="regenerate one fixture only")
     args = ap.parse_args()
     GGUFLoader, QT, tmr = import_reference(Path(args.reference))
     if args.only == "q4_k":
         make_q4_k(GGUFLoader, QT)
         return
+    if args.only == "deepseek":
+        make_deepseek_route("deepseek_route.npz")
+        return
     if args.only == "qwen2moe":
-        make_qwen2moe_block("qwen2moe_block_small.npz", T=10, H=256, E=8, k=2, I=64, m=4, group=64, seed=14)
+        make_qwen2moe_block("qwen2moe_block_small.npz", T=10, H=256, E=8, k=2, I=128, m=4, group=64, seed=14)
         return
     make_q4_0(GGUFLoader, QT)
     make_q4_k(GGUFLoader, QT)
@@ -273,7 +297,8 @@ def main():
     make_small_block("qwen3", "qwen3_block_small.npz", T=12, H=256, E=16, k=4, I=128, group=64, seed=11)
     make_small_block("qwen3", "qwen3_block_small_g32.npz", T=9, H=256, E=8, k=2, I=64, group=32, seed=12)
     make_small_block("mixtral", "mixtral_block_small.npz", T=10, H=256, E=8, k=2, I=128, group=64, seed=13)
-    make_qwen2moe_block("qwen2moe_block_small.npz", T=10, H=256, E=8, k=2, I=64, m=4, group=64, seed=14)
+    make_qwen2moe_block("qwen2moe_block_small.npz", T=10, H=256, E=8, k=2, I=128, m=4, group=64, seed=14)
+    make_deepseek_route("deepseek_route.npz")
     if not args.skip_cfg1:
         make_cfg1()
     for p in sorted(OUT.glob("*.npz")):

@@ -59,7 +59,8 @@ def test_gguf_layer_end_to_end(cuda_device, tmp_path, qtype):
     the file's values exactly."""
     rng = np.random.default_rng(77 + qtype)
     E, H, I, k, T = 8, 512, 256, 2, 24
-    mk = random_q4_0 if qtype == 2 else random_q4_k
+    # weights of a realistic size (|w| up to ~0.1): Q4_0 d ~ 0.01, Q4_K d, dmin ~ 1e-4 (6-bit scales up to 63)
+    mk = (lambda r, a, b: random_q4_0(r, a, b, 0.01)) if qtype == 2 else (lambda r, a, b: random_q4_k(r, a, b, 1e-4))
     gate, up, down = mk(rng, E * I, H), mk(rng, E * I, H), mk(rng, E * H, I)
     router = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
     path = tmp_path / "moe.gguf"

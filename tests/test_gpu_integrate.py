@@ -28,41 +28,43 @@ def _dequantised_copy(model, group=64):
             for p in (ex.gate_up_proj, ex.down_proj):
                 q, s = O.quantize_int4(p.detach().float().cpu().numpy(), group)
                 p.copy_(torch.from_numpy(O.dequantize_int4(q, s, group)).to(p.dtype))
-            if hasattr(blk, "shared_expert"):
-                for lin in (blk.shared_expert.gate_proj, blk.shared_expert.up_proj, blk.shared_expert.down_proj):
+            se = getattr(blk, "shared_expert", None) or getattr(blk, "shared_experts", None)
+            if se is not None:
+                for lin in (se.gate_proj, se.up_proj, se.down_proj):
                     q, s = O.quantize_int4(lin.weight.detach().float().cpu().numpy(), group)
                     lin.weight.copy_(torch.from_numpy(O.dequantize_int4(q, s, group)).to(lin.weight.dtype))
     return ref
 
 
-@pytest.mark.parametrize("kind", ["qwen3_moe", "mixtral", "qwen2_moe"])
+@pytest.mark.parametrize("kind", ["qwen3_moe", "mixtral", "qwen2_moe", "deepseek_v3"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_install_into_matches_transformers(cuda_device, kind, dtype):
+    """Each patched block against transformers' own block in fp32 on the
+    int4-dequantised weights and the same inputs; then the whole model's
+    logits. (A bf16 transformers block is no reference: it rounds the router
+    logits to bf16 before top-k and its own result carries ~1e-2 error.)"""
     model = tiny_model(kind, seed=3).to(cuda_device, dtype)
-    ref = _dequantised_copy(model)
+    ref = _dequantised_copy(model).float()
+    ref_blocks = dict(pm.find_moe_blocks(ref))
     ids = torch.randint(0, 256, (2, 24), device=cuda_device, generator=torch.Generator(device=cuda_device).manual_seed(4))
-    # block inputs/outputs of the reference model
-    seen = {}
-    hooks = [blk.register_forward_hook(lambda m, a, o, n=n: seen.__setitem__(n, (a[0].detach(), o.detach())))
-             for n, blk in pm.find_moe_blocks(ref)]
     with torch.no_grad():
         logits_ref = ref(ids).logits.float()
-    for h in hooks:
-        h.remove()
     names = pm.install_into(model, path="decode")
     assert len(names) == 2
     tol = (1e-3, 1e-4) if dtype == torch.float32 else (0.05, O.MEAN_REL_TOL)
-    blocks = dict(pm.find_moe_blocks(model))
+    gen = torch.Generator(device=cuda_device).manual_seed(5)
     with torch.no_grad():
-        for n, (xin, yout) in seen.items():  # each block on the reference's own input
-            got = blocks[n](xin)
-            mx, mr = O.parity_stats(got.float().cpu().numpy(), yout.float().cpu().numpy())
+        for n, blk in pm.find_moe_blocks(model):
+            x = torch.randn(2, 24, 256, device=cuda_device, generator=gen).to(dtype)
+            got = blk(x).float()
+            want = ref_blocks[n](x.float()).float()
+            mx, mr = O.parity_stats(got.cpu().numpy(), want.cpu().numpy())
             assert mx <= tol[0] and mr <= tol[1], (n, mx, mr)
         logits = model(ids).logits.float()
     mx, mr = O.parity_stats(logits.cpu().numpy(), logits_ref.cpu().numpy())
-    assert mr <= (1e-3 if dtype == torch.float32 else 2e-2), (mx, mr)
+    assert mr <= (1e-3 if dtype == torch.float32 else 5e-2), (mx, mr)
     # dense expert weights were released
-    assert all(b.experts.gate_up_proj.numel() == 0 for b in blocks.values())
+    assert all(b.experts.gate_up_proj.numel() == 0 for _, b in pm.find_moe_blocks(model))
 
 
 def test_generate_and_uninstall(cuda_device):

@@ -90,3 +90,61 @@ def test_pack_experts_shared_bytes(cuda_device):
     assert np.array_equal(pk.w13_scales.cpu().numpy(), q13) and np.array_equal(pk.w2_scales.cpu().numpy(), q2)
     with pytest.raises(ValueError):
         pm.pack_experts_shared(gu, dn, sg[:100], su[:100], sd[:, :100], 64)
+
+
+@pytest.mark.parametrize("E,ng,tg,k,dt", [(256, 8, 4, 8, torch.bfloat16), (16, 4, 2, 4, torch.float32),
+                                          (64, 1, 1, 6, torch.bfloat16)])
+def test_router_ex_bit_exact(cuda_device, E, ng, tg, k, dt):
+    """DeepSeek-V3 routing on the GPU against the oracle's replay: same
+    indices in the same order, weights bit-exact (DeepSeek-V3 shape H 7168,
+    256 experts in 8 groups, 4 kept, top-8)."""
+    dev = cuda_device
+    H = 7168 if E == 256 else 512
+    gen = torch.Generator(device=dev).manual_seed(E + k)
+    x = torch.randn(40, H, device=dev, generator=gen).to(dt)
+    wr = (torch.randn(E, H, device=dev, generator=gen) * 0.02).to(dt)
+    bias = torch.randn(E, device=dev, generator=gen) * 0.05
+    idx, w, logits = pm.router_ex(x, wr, k, True, "sigmoid", bias, ng, tg, 2.5)
+    lg, _, i_ref, w_ref = O.route_sigmoid_grouped(x.float().cpu().numpy(), wr.float().cpu().numpy(), k, True,
+                                                  bias.cpu().numpy(), ng, tg, 2.5)
+    assert np.array_equal(logits.cpu().numpy().view(np.uint32), lg.view(np.uint32))
+    assert np.array_equal(idx.cpu().numpy(), i_ref)
+    assert np.array_equal(w.cpu().numpy().view(np.uint32), w_ref.view(np.uint32))
+
+
+def test_router_ex_rejects(cuda_device):
+    x = torch.zeros(4, 256, device=cuda_device)
+    wr = torch.zeros(12, 256, device=cuda_device)
+    for kw in (dict(n_group=5, topk_group=1), dict(n_group=4, topk_group=5), dict(scoring="softmax", n_group=4)):
+        args = dict(renormalize=True, scoring="sigmoid", score_bias=None, topk_group=1, routed_scale=1.0)
+        args.update(kw)
+        with pytest.raises(pm.PhmoeError):
+            pm.router_ex(x, wr, 2, **args)
+
+
+@pytest.mark.parametrize("path", ["decode", "prefill"])
+def test_deepseek_layer(cuda_device, path):
+    """DeepSeek-style layer: sigmoid routing with bias over 64 experts in 8
+    groups (3 kept), top-6, 2 ungated shared experts, routed_scale 2.5."""
+    dev = cuda_device
+    H, E, k, I, m, G, T = 1024, 64, 6, 256, 2, 64, 200
+    gen = torch.Generator(device=dev).manual_seed(21)
+    gu = torch.randn(E, 2 * I, H, device=dev, generator=gen) * 0.02
+    dn = torch.randn(E, H, I, device=dev, generator=gen) * 0.02
+    sg, su = (torch.randn(m * I, H, device=dev, generator=gen) * 0.02 for _ in range(2))
+    sd = torch.randn(H, m * I, device=dev, generator=gen) * 0.02
+    pk = pm.pack_experts_shared(gu, dn, sg, su, sd, G)
+    wr = (torch.randn(E, H, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+    bias = torch.randn(E, device=dev, generator=gen) * 0.05
+    x = torch.randn(T, H, device=dev, generator=gen).to(torch.bfloat16)
+    out, idx, w = pm.moe_layer(x, wr, pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, k, group_size=G, path=path,
+                               return_routing=True, num_shared=m, routed_scale=2.5, scoring="sigmoid",
+                               score_bias=bias, n_group=8, topk_group=3)
+    host = [t.cpu().numpy() for t in (pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales)]
+    ref, i_ref, w_ref = O.moe_layer_reference_shared(x.float().cpu().numpy(), wr.float().cpu().numpy(), *host, k, m,
+                                                     G, routed_scale=2.5, scoring="sigmoid",
+                                                     score_bias=bias.cpu().numpy(), n_group=8, topk_group=3)
+    assert np.array_equal(idx.cpu().numpy(), i_ref)
+    assert np.array_equal(w.cpu().numpy(), w_ref)
+    mx, mr = O.parity_stats(out.float().cpu().numpy(), ref)
+    assert mx <= 0.05 and mr <= O.MEAN_REL_TOL, (mx, mr)

@@ -12,13 +12,15 @@ from tests.hf_models import tiny_model  # noqa: E402
 
 
 @pytest.mark.parametrize("kind,cls", [("qwen3_moe", "Qwen3MoeSparseMoeBlock"), ("mixtral", "MixtralSparseMoeBlock"),
-                                      ("qwen2_moe", "Qwen2MoeSparseMoeBlock")])
+                                      ("qwen2_moe", "Qwen2MoeSparseMoeBlock"), ("deepseek_v3", "DeepseekV3MoE")])
 def test_find_blocks(kind, cls):
     model = tiny_model(kind)
     blocks = pm.find_moe_blocks(model)
     assert len(blocks) == 2 and all(type(m).__name__ == cls for _, m in blocks)
     spec = pm.detect_moe(model.config)
-    assert spec.num_experts == 8 and spec.top_k == 2
+    assert (spec.num_experts, spec.top_k) == ((16, 4) if kind == "deepseek_v3" else (8, 2))
+    if kind == "deepseek_v3":
+        assert (spec.scoring, spec.n_group, spec.topk_group, spec.shared_intermediate_size) == ("sigmoid", 4, 2, 256)
 
 
 def test_install_refuses_cpu_model():

@@ -191,3 +191,16 @@ def test_qwen2moe_shared_expert_golden():
     assert np.array_equal(np.sort(idx, 1), np.sort(z["idx"], 1))
     mx, mr = O.parity_stats(out, z["out"])
     assert mx <= 1e-5 and mr <= 1e-5, (mx, mr)
+
+
+def test_deepseek_routing_golden():
+    """transformers' DeepseekV3MoE.route_tokens_to_experts (sigmoid, score
+    bias, 4 groups of 4 experts with 2 kept, top-4, renormalised, x2.5) on
+    the same logits: same expert sets, weights within 1e-6."""
+    z = load_golden("deepseek_route.npz")
+    E, ng, tg, k = (int(v) for v in z["cfg"])
+    _, _, idx, w = O.route_sigmoid_grouped(None, None, k, True, z["bias"], ng, tg, float(z["scale"]),
+                                           logits=z["logits"])
+    o1, o2 = np.argsort(idx, 1), np.argsort(z["idx"], 1)
+    assert np.array_equal(np.take_along_axis(idx, o1, 1), np.take_along_axis(z["idx"], o2, 1))
+    assert np.abs(np.take_along_axis(w, o1, 1) - np.take_along_axis(z["w"], o2, 1)).max() <= 1e-6
