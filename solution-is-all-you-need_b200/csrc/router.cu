@@ -23,6 +23,7 @@ namespace {
 constexpr int kRouterWarps = 8;     // experts per CTA (one warp each)
 constexpr int kRouterTokens = 8;    // tokens per CTA
 constexpr int kBlockRouterMinTokens = 256;  // from here the register-blocked kernel is used
+constexpr size_t kMaxTileBytes = 232448;    // dynamic shared memory per CTA
 
 template <typename T>
 struct Vec8;
@@ -71,10 +72,34 @@ __device__ __forceinline__ float mul_add(float acc, float x, float w) {
   else return __fadd_rn(acc, __fmul_rn(x, w));
 }
 
+// Shared-memory layout of the fp32 token tile: per token row, per 256-element
+// chunk c, the 8 elements of lane L = (h / 8) % 32 are split into two
+// 16-byte halves stored at [c][half][L] so that a warp reading one half of
+// its chunk reads 512 contiguous bytes (no bank conflicts).
+__device__ __forceinline__ int tile_pos(int c, int half, int lane) { return c * 256 + half * 128 + lane * 4; }
+
+// Stage the 16 bytes `u` holding elements h .. h + 16/sizeof(XT) - 1 of a row
+// (h a multiple of 16/sizeof(XT)) into the row's tile as fp32 (exact).
+template <typename XT>
+__device__ __forceinline__ void stage_f32(float* row, int h, const uint4& u);
+template <>
+__device__ __forceinline__ void stage_f32<__nv_bfloat16>(float* row, int h, const uint4& u) {
+  const int c = h >> 8, L = (h >> 3) & 31;
+  *reinterpret_cast<float4*>(row + tile_pos(c, 0, L)) =
+      make_float4(bf16_lo_to_f32(u.x), bf16_hi_to_f32(u.x), bf16_lo_to_f32(u.y), bf16_hi_to_f32(u.y));
+  *reinterpret_cast<float4*>(row + tile_pos(c, 1, L)) =
+      make_float4(bf16_lo_to_f32(u.z), bf16_hi_to_f32(u.z), bf16_lo_to_f32(u.w), bf16_hi_to_f32(u.w));
+}
+template <>
+__device__ __forceinline__ void stage_f32<float>(float* row, int h, const uint4& u) {
+  *reinterpret_cast<uint4*>(row + tile_pos(h >> 8, (h >> 2) & 1, (h >> 3) & 31)) = u;
+}
+
 // Grid: (ceil(E/8), ceil(T/TT)); warp w of a CTA owns expert blockIdx.x*8+w.
-// The TT-token tile of x is staged once in shared memory (one cooperative
-// round trip of 16-byte loads); router-weight chunks are loaded kBatch at a
-// time so their latencies overlap.
+// The TT-token tile of x is staged once in shared memory as fp32 (one
+// cooperative round trip of 16-byte loads, converted once per CTA rather
+// than once per expert); router-weight chunks are loaded kBatch at a time so
+// their latencies overlap.
 template <typename XT, typename WT, int TT>
 __global__ void __launch_bounds__(kRouterWarps * 32)
 router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T, int H, int E,
@@ -82,7 +107,9 @@ router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T,
   constexpr bool kExact = std::is_same<XT, __nv_bfloat16>::value && std::is_same<WT, __nv_bfloat16>::value;
   constexpr int kBatch = std::is_same<WT, float>::value ? 4 : 8;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  XT* xs = reinterpret_cast<XT*>(smem_raw);  // [TT][H]
+  float* xs = reinterpret_cast<float*>(smem_raw);  // [TT][nchunk * 256] fp32, tile_pos layout
+  const int nchunk = (H + 255) / 256;
+  const int rowf = nchunk * 256;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * kRouterWarps + warp;
   const int t0 = blockIdx.y * TT;
@@ -93,8 +120,8 @@ router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T,
     constexpr int kVec = 16 / sizeof(XT);
     constexpr int kUnroll = 8;
     const int nvec = nt * H / kVec;  // H % 8 == 0, so rows are whole vectors
+    const int vrow = H / kVec;
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t0 * H);
-    uint4* dst = reinterpret_cast<uint4*>(xs);
     for (int i0 = threadIdx.x; i0 < nvec; i0 += blockDim.x * kUnroll) {
       uint4 v[kUnroll];
 #pragma unroll
@@ -105,7 +132,10 @@ router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T,
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
         const int i = i0 + u * blockDim.x;
-        if (i < nvec) dst[i] = v[u];
+        if (i < nvec) {
+          const int t = i / vrow;
+          stage_f32<XT>(xs + (size_t)t * rowf, (i - t * vrow) * kVec, v[u]);
+        }
       }
     }
   }
@@ -114,7 +144,6 @@ router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T,
   float acc[TT];
 #pragma unroll
   for (int t = 0; t < TT; ++t) acc[t] = 0.f;
-  const int nchunk = (H + 255) / 256;
   const WT* wrow = wr + (size_t)e * H;
   for (int c0 = 0; c0 < nchunk; c0 += kBatch) {
     float w[kBatch][8];
@@ -123,20 +152,22 @@ router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T,
       const int h0 = (c0 + b) * 256 + lane * 8;
       Vec8<WT>::load(wrow + h0, c0 + b < nchunk && h0 < H, w[b]);
     }
+    // tokens innermost: the TT accumulation chains interleave; each token
+    // still adds its elements in increasing h
 #pragma unroll
-    for (int t = 0; t < TT; ++t) {
-      if (t < nt) {
+    for (int b = 0; b < kBatch; ++b) {
+      if (c0 + b < nchunk) {
+        const bool hok = (c0 + b) * 256 + lane * 8 < H;
+        const float* px = xs + tile_pos(c0 + b, 0, lane);
 #pragma unroll
-        for (int b = 0; b < kBatch; ++b) {
-          if (c0 + b < nchunk) {
-            const int h0 = (c0 + b) * 256 + lane * 8;
-            float xv[8];
-            if (h0 < H) {
-              Vec8<XT>::load_smem(xs + (size_t)t * H + h0, xv);
-            } else {
-#pragma unroll
-              for (int v = 0; v < 8; ++v) xv[v] = 0.f;
+        for (int t = 0; t < TT; ++t) {
+          if (t < nt) {
+            float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+            if (hok) {
+              lo = *reinterpret_cast<const float4*>(px + (size_t)t * rowf);
+              hi = *reinterpret_cast<const float4*>(px + (size_t)t * rowf + 128);
             }
+            const float xv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
             for (int v = 0; v < 8; ++v) acc[t] = mul_add<kExact>(acc[t], xv[v], w[b][v]);
           }
@@ -425,7 +456,7 @@ router_topk_grouped_kernel(const float* __restrict__ logits, const float* __rest
 template <typename XT, typename WT, int TT>
 void launch_logits_tt(const void* x, const void* wr, int T, int H, int E, float* logits,
                       cudaStream_t st) {
-  const size_t smem = (size_t)TT * H * sizeof(XT);
+  const size_t smem = (size_t)TT * ((H + 255) / 256 * 256) * sizeof(float);
   auto kern = router_logits_kernel<XT, WT, TT>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((E + kRouterWarps - 1) / kRouterWarps, (T + TT - 1) / TT);
@@ -438,7 +469,10 @@ void launch_logits_tt(const void* x, const void* wr, int T, int H, int E, float*
 template <typename XT, typename WT>
 void launch_logits(const void* x, const void* wr, int T, int H, int E, float* logits,
                    cudaStream_t st) {
-  if (T >= 256 && (size_t)32 * H * sizeof(XT) <= 160 * 1024)
+  const size_t row = (size_t)((H + 255) / 256 * 256) * sizeof(float);
+  if (kRouterTokens * row > kMaxTileBytes)  // very wide layers: 4-token tiles
+    launch_logits_tt<XT, WT, 4>(x, wr, T, H, E, logits, st);
+  else if (T >= 256 && 32 * row <= 160 * 1024)
     launch_logits_tt<XT, WT, 32>(x, wr, T, H, E, logits, st);
   else
     launch_logits_tt<XT, WT, kRouterTokens>(x, wr, T, H, E, logits, st);
