@@ -32,6 +32,7 @@ template <typename OT>
 __global__ void __launch_bounds__(256)
 combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv,
                const float* __restrict__ topk_w, int T, int top_k, int H, OT* __restrict__ out) {
+  pdl_begin();
   const int t = blockIdx.x;
   const int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
   if (h >= H) return;
@@ -74,10 +75,10 @@ int launch_combine(const float* y, const int32_t* inv, const float* topk_w, int 
   if (T == 0) return PHMOE_OK;
   dim3 grid(T, (H / 4 + 255) / 256);
   if (out_dtype == PHMOE_DTYPE_BF16)
-    combine_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(y, inv, topk_w, T, top_k, H,
+    launch_pdl(combine_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, st, y, inv, topk_w, T, top_k, H,
                                                          static_cast<__nv_bfloat16*>(out));
   else
-    combine_kernel<float><<<grid, 256, 0, st>>>(y, inv, topk_w, T, top_k, H, static_cast<float*>(out));
+    launch_pdl(combine_kernel<float>, dim3(grid), dim3(256), 0, st, y, inv, topk_w, T, top_k, H, static_cast<float*>(out));
   note_launches(1);
   return PHMOE_OK;
 }

@@ -123,6 +123,7 @@ __global__ void __launch_bounds__(kDispThreads)
 dispatch_single_kernel(const int32_t* __restrict__ idx, int T, int top_k, int E,
                        int32_t* __restrict__ offsets, int32_t* __restrict__ row_token,
                        int32_t* __restrict__ inv, int32_t* __restrict__ active) {
+  pdl_begin();
   extern __shared__ int smem[];
   int* cnt = smem;               // [E]
   int* base = cnt + E;           // [E]
@@ -145,6 +146,7 @@ dispatch_single_kernel(const int32_t* __restrict__ idx, int T, int top_k, int E,
 // Multi-CTA form for large T*k: count per chunk, scan, then rank per chunk.
 __global__ void __launch_bounds__(kDispThreads)
 dispatch_count_kernel(const int32_t* __restrict__ idx, int R, int E, int32_t* __restrict__ blkcnt) {
+  pdl_begin();
   extern __shared__ int cnt[];
   for (int e = threadIdx.x; e < E; e += kDispThreads) cnt[e] = 0;
   __syncthreads();
@@ -160,6 +162,7 @@ dispatch_count_kernel(const int32_t* __restrict__ idx, int R, int E, int32_t* __
 __global__ void __launch_bounds__(kDispThreads)
 dispatch_scan_kernel(int nblk, int E, int32_t* __restrict__ blkcnt, int32_t* __restrict__ offsets,
                      int32_t* __restrict__ active) {
+  pdl_begin();
   extern __shared__ int smem[];
   int* cnt = smem;            // [E]
   int* base = cnt + E;        // [E]
@@ -187,6 +190,7 @@ __global__ void __launch_bounds__(kDispThreads)
 dispatch_rank_kernel(const int32_t* __restrict__ idx, int R, int top_k, int E,
                      const int32_t* __restrict__ blkbase, int32_t* __restrict__ row_token,
                      int32_t* __restrict__ inv) {
+  pdl_begin();
   extern __shared__ int smem[];
   int* base = smem;         // [E]
   int* wcnt = base + E;     // [kDispWarps * E]
@@ -214,22 +218,22 @@ int launch_dispatch(const int32_t* topk_idx, int T, int top_k, int E, int32_t* o
       cudaFuncSetAttribute(dispatch_single_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem);
     }
-    dispatch_single_kernel<<<1, kDispThreads, smem, st>>>(topk_idx, T, top_k, E, offsets, row_token,
+    launch_pdl(dispatch_single_kernel, dim3(1), dim3(kDispThreads), smem, st, topk_idx, T, top_k, E, offsets, row_token,
                                                           inv, active);
     note_launches(1);
     return PHMOE_OK;
   }
   const int nblk = (R + kDispThreads - 1) / kDispThreads;
   int32_t* blkcnt = static_cast<int32_t*>(scratch);
-  dispatch_count_kernel<<<nblk, kDispThreads, E * sizeof(int), st>>>(topk_idx, R, E, blkcnt);
-  dispatch_scan_kernel<<<1, kDispThreads, (2 * E + 32) * sizeof(int), st>>>(nblk, E, blkcnt,
+  launch_pdl(dispatch_count_kernel, dim3(nblk), dim3(kDispThreads), E * sizeof(int), st, topk_idx, R, E, blkcnt);
+  launch_pdl(dispatch_scan_kernel, dim3(1), dim3(kDispThreads), (2 * E + 32) * sizeof(int), st, nblk, E, blkcnt,
                                                                             offsets, active);
   const size_t smem = (size_t)(E + kDispWarps * E) * sizeof(int);
   if (smem > 48 * 1024) {
     cudaFuncSetAttribute(dispatch_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
   }
-  dispatch_rank_kernel<<<nblk, kDispThreads, smem, st>>>(topk_idx, R, top_k, E, blkcnt, row_token,
+  launch_pdl(dispatch_rank_kernel, dim3(nblk), dim3(kDispThreads), smem, st, topk_idx, R, top_k, E, blkcnt, row_token,
                                                         inv);
   note_launches(3);
   return PHMOE_OK;

@@ -515,6 +515,7 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
                      const int32_t* __restrict__ row_token, const int32_t* __restrict__ offsets,
                      const int32_t* __restrict__ active, const uint16_t* __restrict__ w13_s, int H, int I, int E,
                      __half* __restrict__ h_hi, __half* __restrict__ h_lo) {
+  pdl_begin();
   using C = RbCfg<G, XT>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -737,6 +738,7 @@ ffn_down_kernel(const __half* __restrict__ h_hi, const __half* __restrict__ h_lo
                 const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                 const uint8_t* __restrict__ w2_q, const uint16_t* __restrict__ w2_s, int H, int I, int E,
                 float* __restrict__ y) {
+  pdl_begin();
   using C = DownCfg<G>;
   constexpr int S = C::kStages;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -920,6 +922,7 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
                      const int32_t* __restrict__ row_token, const int32_t* __restrict__ offsets,
                      const int32_t* __restrict__ active, const uint16_t* __restrict__ w13_s, int H, int I, int E,
                      __half* __restrict__ h_hi, __half* __restrict__ h_lo) {
+  pdl_begin();
   using C = MtCfg<G, XT>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -1167,6 +1170,7 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
                     const __grid_constant__ CUtensorMap hi_map, const __grid_constant__ CUtensorMap lo_map,
                     int s_mode, const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                     const uint16_t* __restrict__ w2_s, int H, int I, int E, float* __restrict__ y) {
+  pdl_begin();
   using C = DnCfg<G>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -1389,7 +1393,7 @@ int launch_gateup_mt(const void* x, const int32_t* row_token, const int32_t* off
   if (!s_tma) memset(&smap, 0, sizeof(smap));
   auto k = ffn_gateup_mt_kernel<G, XT>;
   set_smem(k, smem);
-  k<<<grid, kMtThreads, smem, st>>>(map, mode, box_chunks, smap, s_tma, static_cast<const XT*>(x), row_token, offsets,
+  launch_pdl(k, dim3(grid), dim3(kMtThreads), smem, st, map, mode, box_chunks, smap, s_tma, static_cast<const XT*>(x), row_token, offsets,
                                     active, w13_s, H, I, E, h_hi, h_lo);
   return PHMOE_OK;
 }
@@ -1419,7 +1423,7 @@ int launch_gateup_rb(const void* x, const int32_t* row_token, const int32_t* off
   if (smem > kMaxSmem) return PHMOE_ERR_UNSUPPORTED;
   auto k = ffn_gateup_rb_kernel<G, XT>;
   set_smem(k, smem);
-  k<<<grid, kGuThreads, smem, st>>>(map, mode, box_chunks, smap, s_tma, static_cast<const XT*>(x), row_token,
+  launch_pdl(k, dim3(grid), dim3(kGuThreads), smem, st, map, mode, box_chunks, smap, s_tma, static_cast<const XT*>(x), row_token,
                                     offsets, active, w13_s, H, I, E, h_hi, h_lo);
   return PHMOE_OK;
 }
@@ -1437,7 +1441,7 @@ void launch_down(const __half* h_hi, const __half* h_lo, const int32_t* offsets,
   const size_t smem = down_smem<G>(E);
   auto k = ffn_down_kernel<G, kTwo>;
   set_smem(k, smem);
-  k<<<grid, kDownThreads, smem, st>>>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
+  launch_pdl(k, dim3(grid), dim3(kDownThreads), smem, st, h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
 }
 
 // TMA-fed down projection; returns false (nothing launched) when the shape
@@ -1490,7 +1494,7 @@ bool launch_down_tma(const __half* h_hi, const __half* h_lo, long long R, const 
     s_mode = 1;
   auto k = ffn_down_tma_kernel<G, kTwo>;
   set_smem(k, smem);
-  k<<<grid, kGuThreads, smem, st>>>(wm, sm, hm, lm, s_mode, offsets, active, w2_s, H, I, E, y);
+  launch_pdl(k, dim3(grid), dim3(kGuThreads), smem, st, wm, sm, hm, lm, s_mode, offsets, active, w2_s, H, I, E, y);
   return true;
 }
 

@@ -104,6 +104,7 @@ template <typename XT, typename WT, int TT>
 __global__ void __launch_bounds__(kRouterWarps * 32)
 router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T, int H, int E,
                      float* __restrict__ logits) {
+  pdl_begin();
   constexpr bool kExact = std::is_same<XT, __nv_bfloat16>::value && std::is_same<WT, __nv_bfloat16>::value;
   constexpr int kBatch = std::is_same<WT, float>::value ? 4 : 8;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -200,6 +201,7 @@ constexpr int kBlkT = 8, kBlkE = 8, kBlkWarpsT = 4, kBlkWarpsE = 2;
 __global__ void __launch_bounds__(kBlkWarpsT * kBlkWarpsE * 32)
 router_logits_block_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wr, int T,
                            int H, int E, float* __restrict__ logits) {
+  pdl_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = (blockIdx.y * kBlkWarpsT + warp % kBlkWarpsT) * kBlkT;
   const int e0 = (blockIdx.x * kBlkWarpsE + warp / kBlkWarpsT) * kBlkE;
@@ -287,6 +289,7 @@ __global__ void __launch_bounds__(256)
 router_topk_kernel(const float* __restrict__ logits, int T, int E, int top_k, int renormalize,
                    float* __restrict__ probs, int32_t* __restrict__ topk_idx,
                    float* __restrict__ topk_w) {
+  pdl_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + warp;
   if (t >= T) return;
@@ -369,6 +372,7 @@ __global__ void __launch_bounds__(256)
 router_topk_grouped_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E,
                            int top_k, int n_group, int topk_group, int renormalize, float scale,
                            int32_t* __restrict__ topk_idx, float* __restrict__ topk_w) {
+  pdl_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + warp;
   if (t >= T) return;
@@ -460,7 +464,7 @@ void launch_logits_tt(const void* x, const void* wr, int T, int H, int E, float*
   auto kern = router_logits_kernel<XT, WT, TT>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((E + kRouterWarps - 1) / kRouterWarps, (T + TT - 1) / TT);
-  kern<<<grid, kRouterWarps * 32, smem, st>>>(static_cast<const XT*>(x), static_cast<const WT*>(wr),
+  launch_pdl(kern, dim3(grid), dim3(kRouterWarps * 32), smem, st, static_cast<const XT*>(x), static_cast<const WT*>(wr),
                                               T, H, E, logits);
 }
 
@@ -485,7 +489,7 @@ void launch_router_logits(const void* x, int x_dtype, const void* wr, int w_dtyp
                           cudaStream_t st) {
   if (x_dtype == PHMOE_DTYPE_BF16 && w_dtype == PHMOE_DTYPE_BF16 && T >= kBlockRouterMinTokens) {
     dim3 grid((E + kBlkE * kBlkWarpsE - 1) / (kBlkE * kBlkWarpsE), (T + kBlkT * kBlkWarpsT - 1) / (kBlkT * kBlkWarpsT));
-    router_logits_block_kernel<<<grid, kBlkWarpsT * kBlkWarpsE * 32, 0, st>>>(
+    launch_pdl(router_logits_block_kernel, dim3(grid), dim3(kBlkWarpsT * kBlkWarpsE * 32), 0, st, 
         static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(wr), T, H, E, logits);
   } else if (x_dtype == PHMOE_DTYPE_BF16 && w_dtype == PHMOE_DTYPE_BF16)
     launch_logits<__nv_bfloat16, __nv_bfloat16>(x, wr, T, H, E, logits, st);
@@ -506,13 +510,13 @@ int launch_router_grouped(const void* x, int x_dtype, const void* wr, int w_dtyp
   launch_router_logits(x, x_dtype, wr, w_dtype, T, H, E, logits, st);
   const int grid = (T + 7) / 8;
   if (E <= 128)
-    router_topk_grouped_kernel<4><<<grid, 256, 0, st>>>(logits, bias, T, E, top_k, n_group, topk_group, renormalize,
+    launch_pdl(router_topk_grouped_kernel<4>, dim3(grid), dim3(256), 0, st, logits, bias, T, E, top_k, n_group, topk_group, renormalize,
                                                         scale, topk_idx, topk_w);
   else if (E <= 256)
-    router_topk_grouped_kernel<8><<<grid, 256, 0, st>>>(logits, bias, T, E, top_k, n_group, topk_group, renormalize,
+    launch_pdl(router_topk_grouped_kernel<8>, dim3(grid), dim3(256), 0, st, logits, bias, T, E, top_k, n_group, topk_group, renormalize,
                                                         scale, topk_idx, topk_w);
   else
-    router_topk_grouped_kernel<32><<<grid, 256, 0, st>>>(logits, bias, T, E, top_k, n_group, topk_group, renormalize,
+    launch_pdl(router_topk_grouped_kernel<32>, dim3(grid), dim3(256), 0, st, logits, bias, T, E, top_k, n_group, topk_group, renormalize,
                                                          scale, topk_idx, topk_w);
   note_launches(2);
   return PHMOE_OK;
@@ -525,11 +529,11 @@ int launch_router(const void* x, int x_dtype, const void* wr, int w_dtype, int T
   launch_router_logits(x, x_dtype, wr, w_dtype, T, H, E, logits, st);
   const int grid = (T + 7) / 8;
   if (E <= 128)
-    router_topk_kernel<4><<<grid, 256, 0, st>>>(logits, T, E, top_k, renormalize, probs, topk_idx, topk_w);
+    launch_pdl(router_topk_kernel<4>, dim3(grid), dim3(256), 0, st, logits, T, E, top_k, renormalize, probs, topk_idx, topk_w);
   else if (E <= 256)
-    router_topk_kernel<8><<<grid, 256, 0, st>>>(logits, T, E, top_k, renormalize, probs, topk_idx, topk_w);
+    launch_pdl(router_topk_kernel<8>, dim3(grid), dim3(256), 0, st, logits, T, E, top_k, renormalize, probs, topk_idx, topk_w);
   else
-    router_topk_kernel<32><<<grid, 256, 0, st>>>(logits, T, E, top_k, renormalize, probs, topk_idx, topk_w);
+    launch_pdl(router_topk_kernel<32>, dim3(grid), dim3(256), 0, st, logits, T, E, top_k, renormalize, probs, topk_idx, topk_w);
   note_launches(2);
   return PHMOE_OK;
 }

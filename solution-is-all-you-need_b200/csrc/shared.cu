@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(256)
 shared_slots_kernel(const XT* __restrict__ x, const WT* __restrict__ gate_w, const int32_t* __restrict__ idx,
                     const float* __restrict__ w, int T, int H, int k, int E, int m, float routed_scale,
                     int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -78,7 +79,7 @@ shared_slots_kernel(const XT* __restrict__ x, const WT* __restrict__ gate_w, con
 template <typename XT, typename WT>
 void launch_slots(const void* x, const void* gate_w, const int32_t* idx, const float* w, int T, int H, int k,
                   int E, int m, float scale, int32_t* idx_out, float* w_out, cudaStream_t st) {
-  shared_slots_kernel<XT, WT><<<(T + 7) / 8, 256, 0, st>>>(static_cast<const XT*>(x),
+  launch_pdl(shared_slots_kernel<XT, WT>, dim3((T + 7) / 8), dim3(256), 0, st, static_cast<const XT*>(x),
                                                            static_cast<const WT*>(gate_w), idx, w, T, H, k, E, m,
                                                            scale, idx_out, w_out);
 }
