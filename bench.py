@@ -416,6 +416,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     prefill = run_prefill(args, device) if args.prefill else None
+    hf = run_hf_generate(args, device) if args.hf_generate else None
     cpu = None
     if not args.no_cpu_baseline:
         cpu = cpu_baseline(host_layer0, T, args.cpu_budget)
@@ -437,7 +438,63 @@ def run_ours(args):
         "gpu_launches": int(round(res["launches_per_step"] * args.steps)),
         "prefill": prefill,
     }
+    if hf is not None:
+        line["hf_generate"] = hf
     print(json.dumps(line), flush=True)
+
+
+def run_hf_generate(args, device):
+    """End-to-end decode through transformers' generate: a Qwen3-30B-A3B-shaped
+    model (real MoE layer shapes, ``--hf-layers`` decoder layers, random
+    weights, bf16), greedy decoding of ``--hf-new-tokens`` tokens for a batch
+    of ``--tokens`` sequences; transformers' own experts path (its default
+    ``grouped_mm`` on bf16 weights, and the per-expert ``eager`` loop) against
+    the same model after ``phantom_moe.install_into`` (int4 g64 experts on
+    this library's kernels). Timed with CUDA events around each generate."""
+    import transformers as tf
+    import phantom_moe as pm
+    B, N, P = args.tokens, args.hf_new_tokens, 16
+    cfg = tf.Qwen3MoeConfig(hidden_size=H, num_hidden_layers=args.hf_layers, num_attention_heads=32,
+                            num_key_value_heads=4, head_dim=128, vocab_size=32000, num_experts=E,
+                            num_experts_per_tok=K_TOP, moe_intermediate_size=I, norm_topk_prob=True,
+                            intermediate_size=6144, max_position_embeddings=4096)
+    torch.manual_seed(0)
+    with torch.device(device):
+        model = tf.Qwen3MoeForCausalLM(cfg).to(torch.bfloat16).eval()
+    with torch.no_grad():
+        for p in model.parameters():
+            if p.dim() >= 2:
+                p.normal_(0.0, 0.02)
+    ids = torch.randint(0, cfg.vocab_size, (B, P), device=device, generator=torch.Generator(device=device).manual_seed(1))
+
+    def timed(reps=2):
+        with torch.no_grad():
+            model.generate(ids, max_new_tokens=4, min_new_tokens=4, do_sample=False)  # warm-up
+            best = None
+            for _ in range(reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                model.generate(ids, max_new_tokens=N, min_new_tokens=N, do_sample=False)
+                e1.record()
+                e1.synchronize()
+                ms = e0.elapsed_time(e1)
+                best = ms if best is None else min(best, ms)
+        return B * N / (best / 1e3)
+
+    out = {"workload": f"qwen3-30b-a3b-shaped model, {args.hf_layers} layers, batch {B}, prompt {P}, "
+                       f"{N} new tokens, greedy", "unit": "generated tokens/s"}
+    model.config._experts_implementation = "grouped_mm"
+    out["transformers_grouped_mm_bf16"] = timed()
+    model.config._experts_implementation = "eager"
+    out["transformers_eager_loop_bf16"] = timed(reps=1)
+    model.config._experts_implementation = "grouped_mm"
+    pm.install_into(model)
+    out["phantom_moe_int4"] = timed()
+    out["speedup_vs_grouped_mm"] = out["phantom_moe_int4"] / out["transformers_grouped_mm_bf16"]
+    out["speedup_vs_eager_loop"] = out["phantom_moe_int4"] / out["transformers_eager_loop_bf16"]
+    del model
+    torch.cuda.empty_cache()
+    return out
 
 
 def _sweep_entry(v):
@@ -631,6 +688,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
     ap.add_argument("--clock-soak", type=float, default=2.0, help="seconds of sustained replay for clocks")
+    ap.add_argument("--hf-generate", action="store_true",
+                    help="also time transformers generate with and without install_into (an extra JSON object)")
+    ap.add_argument("--hf-layers", type=int, default=4)
+    ap.add_argument("--hf-new-tokens", type=int, default=32)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
