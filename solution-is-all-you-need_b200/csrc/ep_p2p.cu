@@ -8,7 +8,8 @@
 // Qwen3MoeSparseMoeBlock.forward, modeling_qwen3_moe.py:281-286) with the
 // E experts split evenly over the ranks (rank r holds [r*E/P, (r+1)*E/P)).
 //
-// Per layer on rank `me` (one stream, in order):
+// Per layer on rank `me` (one stream, in order; every kernel is launched
+// with programmatic dependent launch and waits for its predecessor first):
 //   router + dispatch over all E experts (rows come out expert-major, hence
 //     destination-major);
 //   ep_send_kernel   - row r goes to rank d = owner of its expert, slot
@@ -122,6 +123,7 @@ __device__ bool last_cta(int* counter) {
 __global__ void __launch_bounds__(kCopyThreads)
 ep_send_kernel(const char* __restrict__ x, const int32_t* __restrict__ row_token, const int32_t* __restrict__ offsets,
                int R, int T, int epr, int world, int me, int cap, int row_bytes, Peers peers, Region L, uint32_t epoch) {
+  pdl_begin();
   const int chunks = row_bytes / 16;
   const int nvalid = R > 0 ? __ldg(offsets + epr * world) : 0;
   for (int r = blockIdx.x; r < nvalid; r += gridDim.x) {
@@ -161,6 +163,7 @@ __global__ void __launch_bounds__(kPrepThreads)
 ep_prepare_kernel(const char* __restrict__ local, Region L, int world, int cap, int epr, uint32_t epoch,
                   int32_t* __restrict__ off, int32_t* __restrict__ active, int32_t* __restrict__ row_token,
                   int32_t* __restrict__ ret_src, int32_t* __restrict__ ret_row) {
+  pdl_begin();
   __shared__ int s_ok[kMaxWorld];
   extern __shared__ int sm[];
   int* cnt = sm;                           // [world][epr]
@@ -181,30 +184,49 @@ ep_prepare_kernel(const char* __restrict__ local, Region L, int world, int cap, 
     }
   }
   __syncthreads();
-  if (threadIdx.x < world) {  // per-source scan over local experts
-    const int s = threadIdx.x;
-    int run = 0;
-    for (int l = 0; l < epr; ++l) {
-      seg[s * epr + l] = run;
-      run += cnt[s * epr + l];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  if (warp < world) {  // warp s: exclusive scan of source s's counts over the local experts
+    const int s = warp;
+    int carry = 0;
+    for (int l0 = 0; l0 < epr; l0 += 32) {
+      const int l = l0 + lane;
+      const int v = l < epr ? cnt[s * epr + l] : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      if (l < epr) seg[s * epr + l] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-  }
-  if (threadIdx.x == 32) {  // scan over local experts of the per-expert totals, and the active list
-    int run = 0, na = 0;
-    for (int l = 0; l < epr; ++l) {
-      loff[l] = run;
+  } else if (warp == world) {  // per-expert totals: their exclusive scan and the active list
+    int carry = 0, na = 0;
+    for (int l0 = 0; l0 < epr; l0 += 32) {
+      const int l = l0 + lane;
       int n = 0;
-      for (int s = 0; s < world; ++s) n += cnt[s * epr + l];
-      run += n;
-      if (n) active[1 + na++] = l;
+      if (l < epr)
+        for (int s = 0; s < world; ++s) n += cnt[s * epr + l];
+      int incl = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      if (l < epr) loff[l] = carry + incl - n;
+      const unsigned m = __ballot_sync(0xffffffffu, l < epr && n > 0);
+      if (l < epr && n > 0) active[1 + na + __popc(m & ((1u << lane) - 1u))] = l;
+      na += __popc(m);
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    loff[epr] = run;
-    active[0] = na;
+    if (lane == 0) {
+      loff[epr] = carry;
+      active[0] = na;
+    }
   }
   __syncthreads();
   for (int l = threadIdx.x; l <= epr; l += blockDim.x) off[l] = loff[l];
   // rows: one warp per (expert, source) segment
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   for (int q = warp; q < epr * world; q += nwarps) {
     const int l = q / world, s = q % world;
     int p = loff[l];
@@ -222,6 +244,7 @@ __global__ void __launch_bounds__(kCopyThreads)
 ep_return_kernel(const float* __restrict__ y, const int32_t* __restrict__ off, int epr,
                  const int32_t* __restrict__ ret_src, const int32_t* __restrict__ ret_row, int world, int me, int cap,
                  int H, Peers peers, Region L, uint32_t epoch) {
+  pdl_begin();
   const int nrows = __ldg(off + epr);
   const int chunks = H * 4 / 16;
   for (int r = blockIdx.x; r < nrows; r += gridDim.x) {
@@ -238,6 +261,7 @@ ep_return_kernel(const float* __restrict__ y, const int32_t* __restrict__ off, i
 }
 
 __global__ void ep_wait_kernel(const char* __restrict__ local, Region L, int world, uint32_t epoch) {
+  pdl_begin();
   if (threadIdx.x < world) wait_flag(reinterpret_cast<const uint32_t*>(local + L.flags_back) + threadIdx.x, epoch);
 }
 
@@ -374,12 +398,12 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
   mark(1);
   if (T > 0) launch_dispatch(idx, T, k, E, offsets, row_token, inv, active, disp, st);
   const int sms = device_sm_count();
-  ep_send_kernel<<<R > 0 ? (R < sms * 4 ? R : sms * 4) : 1, kCopyThreads, 0, st>>>(
-      static_cast<const char*>(x), row_token, offsets, R, T, epr, world, c->rank, c->cap, row_bytes, c->peers, c->L,
-      epoch);
+  launch_pdl(ep_send_kernel, dim3(R > 0 ? (R < sms * 4 ? R : sms * 4) : 1), dim3(kCopyThreads), 0, st,
+             static_cast<const char*>(x), static_cast<const int32_t*>(row_token), static_cast<const int32_t*>(offsets),
+             R, T, epr, world, c->rank, c->cap, row_bytes, c->peers, c->L, epoch);
   const size_t psmem = (size_t)(2 * world * epr + world + epr + 1) * sizeof(int);
-  ep_prepare_kernel<<<1, kPrepThreads, psmem, st>>>(c->local, c->L, world, c->cap, epr, epoch, loff, lact, lrow,
-                                                    ret_src, ret_row);
+  launch_pdl(ep_prepare_kernel, dim3(1), dim3(kPrepThreads), psmem, st, static_cast<const char*>(c->local), c->L,
+             world, c->cap, epr, epoch, loff, lact, lrow, ret_src, ret_row);
   const char* recv = c->local + c->L.recv_x;
   mark(2);
   const cudaEvent_t mid = marks ? marks[3] : nullptr;
@@ -392,9 +416,10 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
                           y, st, mid, (long long)T * k);  // a rank receives about the T*k rows it sends
   if (s) return s;
   mark(4);
-  ep_return_kernel<<<sms * 4, kCopyThreads, 0, st>>>(y, loff, epr, ret_src, ret_row, world, c->rank, c->cap, c->H,
-                                                    c->peers, c->L, epoch);
-  ep_wait_kernel<<<1, 32, 0, st>>>(c->local, c->L, world, epoch);
+  launch_pdl(ep_return_kernel, dim3(sms * 4), dim3(kCopyThreads), 0, st, static_cast<const float*>(y),
+             static_cast<const int32_t*>(loff), epr, static_cast<const int32_t*>(ret_src),
+             static_cast<const int32_t*>(ret_row), world, c->rank, c->cap, c->H, c->peers, c->L, epoch);
+  launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, st, static_cast<const char*>(c->local), c->L, world, epoch);
   if (T > 0)
     launch_combine(reinterpret_cast<const float*>(c->local + c->L.y_back), inv, wts, T, k, c->H, out, x_dtype, st);
   mark(5);
