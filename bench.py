@@ -242,17 +242,19 @@ def e2e_single(args, device, layers, T):
     xh = [torch.randn(T, H, generator=g).to(torch.bfloat16).pin_memory() for _ in range(L)]
     oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
     xd = torch.empty(T, H, dtype=torch.bfloat16, device=device)
+    od = torch.empty(T, H, dtype=torch.bfloat16, device=device)
+    moe = [pm.MoeLayer(layers[l][0], *_pk(layers[l][1]), K_TOP) for l in range(L)]  # weights bound once
     st = torch.cuda.current_stream(device)
     for i in range(args.warmup):
         xd.copy_(xh[i % L], non_blocking=True)
-        out = pm.moe_layer(xd, layers[i % L][0], *_pk(layers[i % L][1]), K_TOP)
+        out = moe[i % L](xd, out=od)
         oh.copy_(out, non_blocking=True)
         st.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(st)
     for i in range(args.steps):
         xd.copy_(xh[i % L], non_blocking=True)
-        out = pm.moe_layer(xd, layers[i % L][0], *_pk(layers[i % L][1]), K_TOP)
+        out = moe[i % L](xd, out=od)
         oh.copy_(out, non_blocking=True)
         st.synchronize()
     ev1.record(st)

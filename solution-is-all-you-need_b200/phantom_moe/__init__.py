@@ -12,6 +12,7 @@ from ._lib import PhmoeError, load as load_library
 from .gguf import GGUFFile, MoeSpec, detect_moe, load_moe_layer
 from .integrate import find_moe_blocks, install_into, uninstall
 from .layer import (
+    MoeLayer,
     PackedExperts,
     check_expert_weights,
     combine,
@@ -30,6 +31,7 @@ from .layer import (
 
 __all__ = [
     "GGUFFile",
+    "MoeLayer",
     "MoeSpec",
     "PhmoeError",
     "PackedExperts",

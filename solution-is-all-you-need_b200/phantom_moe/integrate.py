@@ -25,7 +25,7 @@ from typing import List, Optional, Tuple
 
 import torch
 
-from .layer import PackedExperts, moe_layer, pack_experts, pack_experts_shared
+from .layer import MoeLayer, PackedExperts, pack_experts, pack_experts_shared
 
 SUPPORTED_BLOCKS = ("Qwen3MoeSparseMoeBlock", "MixtralSparseMoeBlock", "Qwen2MoeSparseMoeBlock", "DeepseekV3MoE")
 
@@ -43,6 +43,7 @@ class InstalledMoe:
     original_forward: object
     dense_kept: bool
     routing: dict = dataclasses.field(default_factory=dict)  # extra moe_layer routing arguments
+    layer: Optional[MoeLayer] = None  # the bound layer the patched forward calls
 
 
 def find_moe_blocks(model: torch.nn.Module) -> List[Tuple[str, torch.nn.Module]]:
@@ -84,6 +85,9 @@ def _pack_block(blk: torch.nn.Module, group_size: int, path: str, keep_dense: bo
         top_k = int(gate.top_k)
     st = InstalledMoe(kind, packed, gate.weight.detach().to(rdt).contiguous(), top_k, renorm, path,
                       shared_gate, blk.forward, keep_dense, routing)
+    p = packed
+    st.layer = MoeLayer(st.router_weight, p.w13_q, p.w13_scales, p.w2_q, p.w2_scales, top_k, renorm, p.group_size,
+                        path=path, num_shared=p.num_shared, shared_gate_weight=shared_gate, **routing)
     if not keep_dense:  # the packed copy replaces the dense expert weights
         empty = torch.empty(0, device=dev, dtype=gu.dtype)
         experts.gate_up_proj.data = empty
@@ -102,10 +106,7 @@ def _forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
     dt = x.dtype
     if dt not in (torch.bfloat16, torch.float32):
         x = x.to(torch.bfloat16)
-    p = st.packed
-    out = moe_layer(x.contiguous(), st.router_weight, p.w13_q, p.w13_scales, p.w2_q, p.w2_scales, st.top_k,
-                    renormalize=st.renormalize, group_size=p.group_size, path=st.path, num_shared=p.num_shared,
-                    shared_gate_weight=st.shared_gate, **st.routing)
+    out = st.layer(x.contiguous())
     return out.to(dt).reshape(shape)
 
 

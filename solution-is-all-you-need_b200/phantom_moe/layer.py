@@ -356,6 +356,115 @@ def workspace_bytes(T: int, H: int, E: int, top_k: int, I: int, path: str = "aut
     return int(n)
 
 
+class MoeLayer:
+    """One sparse-MoE layer bound to its weights: the weights and options are
+    validated once, and each call checks only the activations and reuses the
+    bound arguments (the per-call host work of :func:`moe_layer`, which builds
+    one of these per call, drops to one C call). Same arguments and results
+    as :func:`moe_layer` (single GPU)."""
+
+    def __init__(self, router_weight: torch.Tensor, w13_q: torch.Tensor, w13_scales: torch.Tensor,
+                 w2_q: torch.Tensor, w2_scales: torch.Tensor, top_k: int, renormalize: bool = True,
+                 group_size: int = 64, *, path: str = "auto", num_shared: int = 0,
+                 shared_gate_weight: torch.Tensor | None = None, routed_scale: float = 1.0,
+                 scoring: str = "softmax", score_bias: torch.Tensor | None = None, n_group: int = 1,
+                 topk_group: int = 1):
+        _need_cuda("router_weight", router_weight)
+        _need_dtype("router_weight", router_weight, _DT)
+        H = router_weight.shape[-1]
+        E, I = check_expert_weights(w13_q, w13_scales, w2_q, w2_scales, H, group_size)
+        if num_shared:
+            if num_shared < 0 or num_shared >= E:
+                raise ValueError("num_shared must be in [0, number of packed experts)")
+            E -= num_shared
+            if shared_gate_weight is not None:
+                _need_cuda("shared_gate_weight", shared_gate_weight)
+                if shared_gate_weight.numel() != H or shared_gate_weight.dtype != router_weight.dtype:
+                    raise ValueError("shared_gate_weight must hold H values of router_weight's dtype")
+        elif shared_gate_weight is not None:
+            raise ValueError("shared_gate_weight needs num_shared > 0")
+        if scoring not in _SCORING:
+            raise ValueError(f"scoring must be one of {list(_SCORING)}")
+        if score_bias is not None:
+            _need_cuda("score_bias", score_bias)
+            _need_dtype("score_bias", score_bias, (torch.float32,))
+            _need_shape("score_bias", score_bias, (E,))
+        _need_shape("router_weight", router_weight, (E, H))
+        if path not in _PATHS:
+            raise ValueError(f"path must be one of {list(_PATHS)}")
+        self.H, self.E, self.I, self.top_k, self.group_size = H, E, I, top_k, group_size
+        self.device = router_weight.device
+        self.num_shared = num_shared
+        # keep the tensors alive for as long as the bound pointers are used
+        self._tensors = (router_weight, w13_q, w13_scales, w2_q, w2_scales, shared_gate_weight, score_bias)
+        lib = _lib.load()
+        self._extended = (bool(num_shared) or routed_scale != 1.0 or scoring != "softmax" or score_bias is not None
+                          or n_group > 1)
+        pc = _PATHS[path]
+        head = (_ptr(router_weight), _DT[router_weight.dtype], _ptr(w13_q), _ptr(w13_scales), _ptr(w2_q),
+                _ptr(w2_scales))
+        if self._extended:
+            self._name = "phmoe_moe_layer_ex"
+            self._size = lambda T: lib.phmoe_workspace_size_ex(T, H, E, top_k, I, num_shared, pc)
+            self._tail = (H, E, top_k, I, group_size, int(bool(renormalize)), _SCORING[scoring], _ptr(score_bias),
+                          n_group, topk_group, num_shared, _ptr(shared_gate_weight), float(routed_scale), pc)
+        else:
+            self._name = "phmoe_moe_layer"
+            self._size = lambda T: lib.phmoe_workspace_size(T, H, E, top_k, I, pc)
+            self._tail = (H, E, top_k, I, group_size, int(bool(renormalize)), pc)
+        self._fn = getattr(lib, self._name)
+        self._head = head
+        self._need: dict[int, int] = {}
+
+    def workspace_bytes(self, T: int) -> int:
+        n = self._need.get(T)
+        if n is None:
+            n = self._need[T] = self._size(T)
+        return n
+
+    def __call__(self, hidden_states: torch.Tensor, out: torch.Tensor | None = None, return_routing: bool = False,
+                 workspace: torch.Tensor | None = None):
+        x = hidden_states
+        if not isinstance(x, torch.Tensor) or x.device != self.device:
+            raise ValueError(f"hidden_states must be a CUDA tensor on {self.device}; phantom_moe has no CPU path")
+        if x.dtype not in _DT:
+            raise TypeError(f"hidden_states must be bf16 or fp32 (got {x.dtype})")
+        if not x.is_contiguous():
+            raise ValueError("hidden_states must be contiguous")
+        shape = x.shape
+        H = self.H
+        if shape[-1] != H:
+            raise ValueError(f"hidden_states must end in H={H} (got {tuple(shape)})")
+        T = x.numel() // H
+        dev = x.device
+        if out is None:
+            out = torch.empty(shape, dtype=x.dtype, device=dev)
+        elif (not isinstance(out, torch.Tensor) or out.device != dev or out.dtype != x.dtype
+              or out.numel() != T * H or not out.is_contiguous()):
+            raise ValueError("out must be a contiguous CUDA tensor matching hidden_states in dtype and size")
+        idx = wts = None
+        if return_routing:
+            idx = torch.empty(T, self.top_k, dtype=torch.int32, device=dev)
+            wts = torch.empty(T, self.top_k, dtype=torch.float32, device=dev)
+        need = self.workspace_bytes(T)
+        if workspace is None:
+            ws = WORKSPACE.get(dev, need)
+        else:
+            _need_cuda("workspace", workspace)
+            _need_dtype("workspace", workspace, (torch.uint8,))
+            if workspace.numel() < need:
+                raise ValueError(f"workspace needs {need} bytes (got {workspace.numel()})")
+            ws = workspace
+        rc = self._fn(x.data_ptr(), _DT[x.dtype], *self._head, T, *self._tail, out.data_ptr(), _ptr(idx), _ptr(wts),
+                      ws.data_ptr(), ws.numel(), _stream())
+        if rc:
+            _lib.check(self._name, rc)
+        out = out.reshape(shape)
+        if return_routing:
+            return out, idx, wts
+        return out
+
+
 def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: torch.Tensor,
               w13_scales: torch.Tensor, w2_q: torch.Tensor, w2_scales: torch.Tensor, top_k: int,
               renormalize: bool = True, group_size: int = 64, ep_group=None, *,
@@ -397,68 +506,7 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
                                     top_k, renormalize, group_size, ep_group, path=path,
                                     return_routing=return_routing)
     _need_cuda("hidden_states", hidden_states)
-    _need_cuda("router_weight", router_weight)
-    _need_dtype("hidden_states", hidden_states, _DT)
-    _need_dtype("router_weight", router_weight, _DT)
-    shape = hidden_states.shape
-    H = shape[-1]
-    x = hidden_states.reshape(-1, H)
-    T = x.shape[0]
-    E, I = check_expert_weights(w13_q, w13_scales, w2_q, w2_scales, H, group_size)
-    if num_shared:
-        if num_shared < 0 or num_shared >= E:
-            raise ValueError("num_shared must be in [0, number of packed experts)")
-        E -= num_shared
-        if shared_gate_weight is not None:
-            _need_cuda("shared_gate_weight", shared_gate_weight)
-            if shared_gate_weight.numel() != H or shared_gate_weight.dtype != router_weight.dtype:
-                raise ValueError("shared_gate_weight must hold H values of router_weight's dtype")
-    elif shared_gate_weight is not None:
-        raise ValueError("shared_gate_weight needs num_shared > 0")
-    if scoring not in _SCORING:
-        raise ValueError(f"scoring must be one of {list(_SCORING)}")
-    if score_bias is not None:
-        _need_cuda("score_bias", score_bias)
-        _need_dtype("score_bias", score_bias, (torch.float32,))
-        _need_shape("score_bias", score_bias, (E,))
-    extended = bool(num_shared) or routed_scale != 1.0 or scoring != "softmax" or score_bias is not None or n_group > 1
-    _need_shape("router_weight", router_weight, (E, H))
-    if path not in _PATHS:
-        raise ValueError(f"path must be one of {list(_PATHS)}")
-    dev = x.device
-    if out is None:
-        out = torch.empty(T, H, dtype=x.dtype, device=dev)
-    else:
-        _need_cuda("out", out)
-        if out.dtype != x.dtype or out.numel() != T * H:
-            raise ValueError("out must match hidden_states in dtype and size")
-    idx = torch.empty(T, top_k, dtype=torch.int32, device=dev) if return_routing else None
-    wts = torch.empty(T, top_k, dtype=torch.float32, device=dev) if return_routing else None
-    lib = _lib.load()
-    if extended:
-        need = lib.phmoe_workspace_size_ex(T, H, E, top_k, I, num_shared, _PATHS[path])
-    else:
-        need = lib.phmoe_workspace_size(T, H, E, top_k, I, _PATHS[path])
-    if workspace is None:
-        ws = WORKSPACE.get(dev, need)
-    else:
-        _need_cuda("workspace", workspace)
-        _need_dtype("workspace", workspace, (torch.uint8,))
-        if workspace.numel() < need:
-            raise ValueError(f"workspace needs {need} bytes (got {workspace.numel()})")
-        ws = workspace
-    if extended:
-        _lib.call("phmoe_moe_layer_ex", _ptr(x), _DT[x.dtype], _ptr(router_weight), _DT[router_weight.dtype],
-                  _ptr(w13_q), _ptr(w13_scales), _ptr(w2_q), _ptr(w2_scales), T, H, E, top_k, I, group_size,
-                  int(bool(renormalize)), _SCORING[scoring], _ptr(score_bias), n_group, topk_group, num_shared,
-                  _ptr(shared_gate_weight), float(routed_scale), _PATHS[path], _ptr(out), _ptr(idx), _ptr(wts),
-                  _ptr(ws), ws.numel(), _stream())
-    else:
-        _lib.call("phmoe_moe_layer", _ptr(x), _DT[x.dtype], _ptr(router_weight), _DT[router_weight.dtype],
-                  _ptr(w13_q), _ptr(w13_scales), _ptr(w2_q), _ptr(w2_scales), T, H, E, top_k, I, group_size,
-                  int(bool(renormalize)), _PATHS[path], _ptr(out), _ptr(idx), _ptr(wts), _ptr(ws), ws.numel(),
-                  _stream())
-    out = out.reshape(shape)
-    if return_routing:
-        return out, idx, wts
-    return out
+    layer = MoeLayer(router_weight, w13_q, w13_scales, w2_q, w2_scales, top_k, renormalize, group_size, path=path,
+                     num_shared=num_shared, shared_gate_weight=shared_gate_weight, routed_scale=routed_scale,
+                     scoring=scoring, score_bias=score_bias, n_group=n_group, topk_group=topk_group)
+    return layer(hidden_states, out=out, return_routing=return_routing, workspace=workspace)

@@ -357,3 +357,34 @@ def test_stage_functions_compose(qwen3_bf16_weights):
     out = pm.combine(y, inv, w, torch.bfloat16)
     ref = pm.moe_layer(x, wr, pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, 8)
     assert torch.equal(out, ref)
+
+
+def test_moe_layer_bound_matches(cuda_device):
+    """MoeLayer (weights bound once) gives the same bits as moe_layer, for
+    plain and extended (shared experts, sigmoid routing) layers, and rejects
+    activations of the wrong device, dtype or width."""
+    import phantom_moe as pm
+    dev = cuda_device
+    E, H, I, k, G = 16, 512, 256, 4, 64
+    gen = torch.Generator(device=dev).manual_seed(31)
+    pk = pm.pack_experts(torch.randn(E, 2 * I, H, device=dev, generator=gen) * 0.02,
+                         torch.randn(E, H, I, device=dev, generator=gen) * 0.02, G)
+    wr = (torch.randn(E, H, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+    x = torch.randn(3, 7, H, device=dev, generator=gen).to(torch.bfloat16)
+    layer = pm.MoeLayer(wr, pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, k, group_size=G)
+    ref = pm.moe_layer(x, wr, pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, k, group_size=G)
+    out = torch.empty_like(x)
+    got = layer(x, out=out)
+    assert got.shape == x.shape and got.data_ptr() == out.data_ptr() and torch.equal(got, ref)
+    bias = torch.randn(E - 2, device=dev, generator=gen) * 0.05
+    kw = dict(num_shared=2, routed_scale=2.0, scoring="sigmoid", score_bias=bias, n_group=2, topk_group=1)
+    ext = pm.MoeLayer(wr[: E - 2].contiguous(), pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, k, group_size=G, **kw)
+    ref2 = pm.moe_layer(x, wr[: E - 2].contiguous(), pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, k, group_size=G,
+                        **kw)
+    assert torch.equal(ext(x), ref2)
+    with pytest.raises(ValueError):
+        layer(x.cpu())
+    with pytest.raises(TypeError):
+        layer(x.half())
+    with pytest.raises(ValueError):
+        layer(x[..., :256].contiguous())
