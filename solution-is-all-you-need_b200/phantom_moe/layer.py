@@ -464,6 +464,26 @@ class MoeLayer:
             return out, idx, wts
         return out
 
+    def graphed(self, x: torch.Tensor, out: torch.Tensor):
+        """Capture this layer on the fixed buffers ``x`` -> ``out`` into a CUDA
+        graph and return a function that replays it on the current stream (one
+        launch instead of one per kernel). Refill ``x`` in place between
+        replays; ``x`` and ``out`` must stay allocated while the graph is used."""
+        side = torch.cuda.Stream(device=x.device)
+        side.wait_stream(torch.cuda.current_stream(x.device))
+        with torch.cuda.stream(side):  # warm-up outside the capture (workspace, tensor maps)
+            self(x, out=out)
+        torch.cuda.current_stream(x.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self(x, out=out)
+        keep = (graph, x, out)
+
+        def replay():
+            keep[0].replay()
+            return keep[2]
+        return replay
+
 
 def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: torch.Tensor,
               w13_scales: torch.Tensor, w2_q: torch.Tensor, w2_scales: torch.Tensor, top_k: int,

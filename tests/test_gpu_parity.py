@@ -388,3 +388,23 @@ def test_moe_layer_bound_matches(cuda_device):
         layer(x.half())
     with pytest.raises(ValueError):
         layer(x[..., :256].contiguous())
+
+
+def test_moe_layer_graphed_replay(cuda_device):
+    """MoeLayer.graphed: replays on refilled inputs give the eager layer's bits."""
+    import phantom_moe as pm
+    dev = cuda_device
+    E, H, I, k, G, T = 32, 1024, 256, 4, 64, 48
+    gen = torch.Generator(device=dev).manual_seed(41)
+    pk = pm.pack_experts(torch.randn(E, 2 * I, H, device=dev, generator=gen) * 0.02,
+                         torch.randn(E, H, I, device=dev, generator=gen) * 0.02, G)
+    wr = (torch.randn(E, H, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+    layer = pm.MoeLayer(wr, pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, k, group_size=G)
+    x = torch.zeros(T, H, device=dev, dtype=torch.bfloat16)
+    out = torch.empty_like(x)
+    run = layer.graphed(x, out)
+    for seed in (1, 2, 3):
+        xi = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(seed)).to(torch.bfloat16)
+        x.copy_(xi)
+        got = run().clone()
+        assert torch.equal(got, layer(xi))
