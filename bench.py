@@ -398,7 +398,18 @@ def run_ours(args):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if ws > 1:
+        if args.zipf:
+            import torch.distributed as dist
+            z = run_ep_zipf(args, ws, rank, device)
+            if rank == 0:
+                print(json.dumps({"zipf": z}), flush=True)
+            dist.barrier()
+            dist.destroy_process_group()
+            return
         return run_ep(args, ws, rank, device)
+    if args.stack:
+        print(json.dumps({"stack": run_stack(args, device)}), flush=True)
+        return
     if args.prefill_only:
         print(json.dumps({"prefill": run_prefill(args, device)}), flush=True)
         return
@@ -501,6 +512,106 @@ def run_hf_generate(args, device):
     del model
     torch.cuda.empty_cache()
     return out
+
+
+def run_stack(args, device):
+    """BASELINE config 4 on one GPU: a stack of ``--stack`` Qwen3-30B-A3B-shaped
+    MoE layers (MoE FFN only, attention omitted; layer l's weights drawn from
+    seed 100 + l, int4 g64, 15.4 GB for 48 layers), decode T = ``--tokens``,
+    each layer on its own seeded input, the whole stack captured as one CUDA
+    graph per step (weights read from HBM: the stack is 120x the L2)."""
+    import phantom_moe as pm
+    Ls, T = args.stack, args.tokens
+    layers = [make_layer(100 + l, device) for l in range(Ls)]
+    g = torch.Generator(device=device).manual_seed(3000 + T)
+    xs = [torch.randn(T, H, device=device, generator=g).to(torch.bfloat16) for _ in range(Ls)]
+    outs = [torch.empty_like(x) for x in xs]
+    moe = [pm.MoeLayer(wr, *_pk(pk), K_TOP) for wr, pk in layers]
+    side = torch.cuda.Stream(device=device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for l in range(Ls):
+            moe[l](xs[l], out=outs[l])
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for l in range(Ls):
+            moe[l](xs[l], out=outs[l])
+    st = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        graph.replay()
+    st.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(st)
+    for _ in range(args.steps):
+        graph.replay()
+    ev1.record(st)
+    ev1.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    wbytes = sum(pk.w13_q.numel() + pk.w13_scales.numel() * 2 + pk.w2_q.numel() + pk.w2_scales.numel() * 2
+                 for _, pk in layers)
+    del graph, moe, layers
+    torch.cuda.empty_cache()
+    return {"workload": f"{Ls}-layer qwen3-30b-a3b MoE stack (MoE FFN only), decode T={T}, 1 GPU, CUDA graph",
+            "layers": Ls, "tokens_per_gpu": T, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
+            "us_per_layer": ms * 1e3 / Ls, "packed_weight_GB": wbytes / 1e9}
+
+
+def run_ep_zipf(args, ws, rank, device):
+    """BASELINE config 5 under expert parallelism: 8192 tokens in total
+    (8192 / N per rank), router logits biased by log of a Zipf(1.2) prior over
+    the experts (a constant input feature x[:, 0] = 1 meeting router column
+    0 = log p_i), against the same layer without the bias; reports the load
+    imbalance, every rank's received rows and the step time (max over ranks)."""
+    import torch.distributed as dist
+    import phantom_moe as pm
+    from phantom_moe import ep
+    T = 8192 // ws
+    lo, hi = ep.shard_range(E, ws, rank)
+    wr, pk = make_layer(7, device, expert_range=(lo, hi))
+    g = torch.Generator(device=device).manual_seed(4000 + 7919 * rank)
+    x = torch.randn(T, H, device=device, generator=g)
+    prior = torch.log(torch.arange(1, E + 1, device=device, dtype=torch.float32) ** -1.2)
+    wr_skew = wr.float()
+    wr_skew[:, 0] = prior
+    x_skew = x.clone()
+    x_skew[:, 0] = 1.0
+    cases = {"balanced": (x.to(torch.bfloat16), wr), "zipf": (x_skew.to(torch.bfloat16), wr_skew.to(torch.bfloat16))}
+    stream = torch.cuda.current_stream(device)
+    exchange = ep.PeerExchange(None, T, K_TOP, H, E) if args.ep_exchange == "peer" else None
+    res = {}
+    for name, (xc, wc) in cases.items():
+        st = {}
+        ep.moe_layer_ep(xc, wc, *_pk(pk), K_TOP, True, G, None, stats=st)  # row counts (NCCL path)
+        loads = torch.tensor(st["recv_rows"], device=device, dtype=torch.float32)
+        all_loads = [torch.zeros_like(loads) for _ in range(ws)]
+        dist.all_gather(all_loads, loads)
+        for _ in range(args.warmup):
+            ep.moe_layer_ep(xc, wc, *_pk(pk), K_TOP, True, G, None, exchange=exchange)
+        dist.barrier()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            ep.moe_layer_ep(xc, wc, *_pk(pk), K_TOP, True, G, None, exchange=exchange)
+        ev1.record(stream)
+        ev1.synchronize()
+        dist.barrier()
+        t = torch.tensor([ev0.elapsed_time(ev1) / args.steps], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        idx, _, _ = pm.router(xc, wc, K_TOP)
+        cnt = torch.bincount(idx.view(-1).long(), minlength=E).float()
+        dist.all_reduce(cnt)
+        recv = [float(v) for v in torch.stack(all_loads).sum(dim=1).tolist()]
+        res[name] = {"ms_per_step": ms, "tokens_per_s": 8192 / (ms / 1e3),
+                     "expert_load_max_over_mean": float(cnt.max() / cnt.mean()),
+                     "rows_received_per_rank": recv, "rank_load_max_over_mean": max(recv) / (sum(recv) / ws)}
+    res["zipf_over_balanced_time"] = res["zipf"]["ms_per_step"] / res["balanced"]["ms_per_step"]
+    if exchange is not None:
+        exchange.close()
+    return {"workload": f"config 5: 8192 tokens over {ws} GPUs, Zipf(1.2) router prior, top-8 of 128",
+            "exchange": args.ep_exchange, **res}
 
 
 def _sweep_entry(v):
@@ -696,6 +807,10 @@ def main():
     ap.add_argument("--clock-soak", type=float, default=2.0, help="seconds of sustained replay for clocks")
     ap.add_argument("--hf-generate", action="store_true",
                     help="also time transformers generate with and without install_into (an extra JSON object)")
+    ap.add_argument("--stack", type=int, default=0,
+                    help="only time a decode step through this many MoE layers (config 4 on one GPU)")
+    ap.add_argument("--zipf", action="store_true",
+                    help="N > 1: only the config-5 Zipf-skewed routing measurement (8192 tokens in total)")
     ap.add_argument("--hf-layers", type=int, default=4)
     ap.add_argument("--hf-new-tokens", type=int, default=32)
     args = ap.parse_args()
