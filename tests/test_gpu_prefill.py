@@ -198,3 +198,21 @@ def test_decode_batch_invariance(cuda_device, dtype):
         assert torch.equal(idx_small, idx_big[:n]), n
         assert torch.equal(small, big[:n]), n
     assert pm.load_library().phmoe_device_error(1) == 0
+
+
+@pytest.mark.gpu
+def test_decode_batch_invariance_few_experts(cuda_device):
+    """16 experts with ~32 rows each (the local shape of 8-way expert
+    parallelism, multi-token items): rows are bit-identical to the same
+    tokens run alone (8-token items)."""
+    dev = cuda_device
+    E, H, k, I, G, T = 16, 2048, 2, 768, 64, 256
+    wr, packed = _packed_layer(E, H, I, G, 29, dev)
+    x = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(30)).to(torch.bfloat16)
+    big = pm.moe_layer(x, wr, *packed, k, group_size=G, path="decode")
+    for n in (1, 5):
+        small = pm.moe_layer(x[:n], wr, *packed, k, group_size=G, path="decode")
+        torch.cuda.synchronize()
+        assert torch.equal(small, big[:n]), n
+    mx, mr, _ = _layer_vs_torch(dev, E, H, k, I, G, T, 31, "decode")
+    assert mx <= O.MAX_ABS_TOL and mr <= O.MEAN_REL_TOL, (mx, mr)
