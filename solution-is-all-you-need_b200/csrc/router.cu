@@ -474,12 +474,20 @@ template <typename XT, typename WT>
 void launch_logits(const void* x, const void* wr, int T, int H, int E, float* logits,
                    cudaStream_t st) {
   const size_t row = (size_t)((H + 255) / 256 * 256) * sizeof(float);
+  // CTAs for a token tile of tt rows; small batches take smaller tiles so
+  // that there are at least two CTAs per SM to hide the accumulation chains
+  const long long eblk = (E + kRouterWarps - 1) / kRouterWarps, want = 2LL * device_sm_count();
+  auto ctas = [&](int tt) { return eblk * ((T + tt - 1) / tt); };
   if (kRouterTokens * row > kMaxTileBytes)  // very wide layers: 4-token tiles
     launch_logits_tt<XT, WT, 4>(x, wr, T, H, E, logits, st);
   else if (T >= 256 && 32 * row <= 160 * 1024)
     launch_logits_tt<XT, WT, 32>(x, wr, T, H, E, logits, st);
-  else
+  else if (ctas(kRouterTokens) >= want || T <= 1)
     launch_logits_tt<XT, WT, kRouterTokens>(x, wr, T, H, E, logits, st);
+  else if (ctas(4) >= want)
+    launch_logits_tt<XT, WT, 4>(x, wr, T, H, E, logits, st);
+  else
+    launch_logits_tt<XT, WT, 2>(x, wr, T, H, E, logits, st);
 }
 
 }  // namespace
