@@ -277,7 +277,7 @@ def make_cfg1():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--skip-cfg1", action="store_true", help="keep the existing qwen3_cfg1.npz")
     ap.add_argument("--only", choices=["q4_k", "qwen2moe", "deepseek"], help="regenerate one fixture only")
     args = ap.parse_args()
