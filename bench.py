@@ -11,9 +11,12 @@ L2); no explicit flush is needed.
 
 * ``value``: tokens/s over K steps replayed from CUDA graphs, inputs resident
   in HBM, timed with CUDA events; max over ranks for N > 1.
-* ``e2e``: the same through the public API ``phantom_moe.moe_layer`` per
-  step, with the step's activations copied host->device from pinned memory
-  and the output copied back and synchronised, timed with CUDA events.
+* ``e2e``: the same through the public API (``phantom_moe.HostPipeline``
+  over ``MoeLayer``s), every step copying its activations host->device from
+  pinned memory and its output back, the copies on their own streams
+  (overlapping the neighbouring steps' layers), timed with CUDA events from
+  before the first copy in to after the last copy out; ``e2e.sync`` is the
+  same with one stream and a host synchronisation per step.
 * ``roofline``: the dominant kernel (FFN gate/up) timed by CUDA events the
   library records between its stages; algorithmic bytes = packed int4
   weights + fp16 scales of every expert hit + activations in + h out.
@@ -235,37 +238,59 @@ def profile_stages(pm, lib, layers, xs, outs, stream, n_calls):
 
 
 def e2e_single(args, device, layers, T):
-    """Public-API path with host<->device copies inside the timed region."""
+    """Public-API path with host<->device copies inside the timed region.
+
+    ``phantom_moe.HostPipeline`` over the bench's layers: every step copies
+    its tokens host->device from pinned memory, runs the layer (a CUDA graph
+    per layer and device slot) and copies its output device->host; the
+    copies run on their own streams, so those of neighbouring steps overlap
+    the layer. ``sync`` is the same steps issued on one stream with a host
+    synchronisation after each."""
     import phantom_moe as pm
     L = len(layers)
     g = torch.Generator().manual_seed(2000 + T)
     xh = [torch.randn(T, H, generator=g).to(torch.bfloat16).pin_memory() for _ in range(L)]
-    oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    oh = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    moe = [pm.MoeLayer(layers[l][0], *_pk(layers[l][1]), K_TOP) for l in range(L)]
+    pipe = pm.HostPipeline(moe, T, H, device=device, depth=2)
+    for i in range(args.warmup):
+        pipe.submit(xh[i % L], oh[i % 2])
+    pipe.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(pipe.copy_in)
+    for i in range(args.steps):
+        pipe.submit(xh[i % L], oh[i % 2])
+    ev1.record(pipe.copy_out)
+    ev1.synchronize()
+    pipe.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    # the same steps, synchronous: copy in, replay, copy out, wait
     xd = torch.empty(T, H, dtype=torch.bfloat16, device=device)
     od = torch.empty(T, H, dtype=torch.bfloat16, device=device)
-    # each layer bound to its weights once and captured on the fixed device buffers (one graph launch per
-    # call); every step still copies its input in and its result out
-    moe = [pm.MoeLayer(layers[l][0], *_pk(layers[l][1]), K_TOP).graphed(xd, od) for l in range(L)]
+    run = [m.graphed(xd, od) for m in moe]
     st = torch.cuda.current_stream(device)
     for i in range(args.warmup):
         xd.copy_(xh[i % L], non_blocking=True)
-        out = moe[i % L]()
-        oh.copy_(out, non_blocking=True)
+        oh[0].copy_(run[i % L](), non_blocking=True)
         st.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(st)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(st)
     for i in range(args.steps):
         xd.copy_(xh[i % L], non_blocking=True)
-        out = moe[i % L]()
-        oh.copy_(out, non_blocking=True)
+        oh[0].copy_(run[i % L](), non_blocking=True)
         st.synchronize()
-    ev1.record(st)
-    ev1.synchronize()
-    ms = ev0.elapsed_time(ev1) / args.steps
+    s1.record(st)
+    s1.synchronize()
+    ms_sync = s0.elapsed_time(s1) / args.steps
     return {"value": T / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
             "d2h_bytes_per_step": T * H * 2, "ms_per_step": ms,
-            "api": "phantom_moe.MoeLayer(...).graphed(x, out) replayed per step; pinned host -> device copy of "
-                   "the step's tokens before and device -> host copy of its output after, stream synchronised"}
+            "api": "phantom_moe.HostPipeline(MoeLayer per layer).submit(x_host, out_host) per step: pinned host -> "
+                   "device copy of the step's tokens, the layer (CUDA graph), device -> host copy of its output, "
+                   "each on its own stream ordered by events; timed from before the first copy in to after the "
+                   "last copy out",
+            "sync": {"value": T / (ms_sync / 1e3), "ms_per_step": ms_sync,
+                     "api": "MoeLayer(...).graphed(x, out) per step on one stream, copies in and out, "
+                            "host synchronised after every step"}}
 
 
 def cpu_baseline(layers_host_fn, T, budget_s):

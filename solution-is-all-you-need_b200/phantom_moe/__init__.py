@@ -11,6 +11,7 @@ of ``include/phmoe.h``; this package validates tensors and calls it.
 from ._lib import PhmoeError, load as load_library
 from .gguf import GGUFFile, MoeSpec, detect_moe, load_moe_layer
 from .integrate import find_moe_blocks, install_into, uninstall
+from .pipeline import HostPipeline
 from .layer import (
     MoeLayer,
     PackedExperts,
@@ -31,6 +32,7 @@ from .layer import (
 
 __all__ = [
     "GGUFFile",
+    "HostPipeline",
     "MoeLayer",
     "MoeSpec",
     "PhmoeError",

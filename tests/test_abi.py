@@ -116,6 +116,15 @@ def test_python_layer_rejects_cpu_tensors():
         phantom_moe.router(x, x[:8], 2)
 
 
+def test_host_pipeline_argument_checks():
+    with pytest.raises(ValueError, match="at least one layer"):
+        phantom_moe.HostPipeline([], 4, 256, device="cuda")
+    with pytest.raises(ValueError, match="depth"):
+        phantom_moe.HostPipeline([lambda x, out: None], 4, 256, device="cuda", depth=0)
+    with pytest.raises(ValueError, match="CUDA device"):
+        phantom_moe.HostPipeline([lambda x, out: None], 4, 256, device="cpu")
+
+
 def test_prefill_rejects_fp32_and_bad_dims(lib):
     args = [None, None, None, None, None, None, None, 4, 4096, 8, 2]
     assert lib.phmoe_expert_ffn_prefill(None, 0, *args, 14336, 64, None, None, None) == _lib.PHMOE_ERR_UNSUPPORTED
