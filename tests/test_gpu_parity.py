@@ -276,7 +276,7 @@ def qwen3_bf16_weights(cuda_device):
     return wr, pk, host
 
 
-@pytest.mark.parametrize("T", [1, 4, 16, 64, 256])
+@pytest.mark.parametrize("T", [1, 4, 16, 64, 128, 129, 256])  # 128: largest fused top-k + dispatch batch
 def test_cfg2_layer_bf16_sweep(qwen3_bf16_weights, T):
     import phantom_moe as pm
     wr, pk, host = qwen3_bf16_weights
