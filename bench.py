@@ -582,6 +582,61 @@ def run_stack(args, device):
             "us_per_layer": ms * 1e3 / Ls, "packed_weight_GB": wbytes / 1e9}
 
 
+def run_ep_prefill(args, ws, rank, device):
+    """BASELINE config 3 under expert parallelism: the Mixtral-8x7B-shaped
+    layer (H 4096, 8 experts, top-2, I 14336, int4 g64) with its experts
+    sharded 8/N per rank and --prefill-tokens tokens in total (strong scaling:
+    4096/N per rank, seed 2, the same draw on every rank), through the peer
+    exchange and the tcgen05 prefill GEMMs. Max over ranks."""
+    import torch.distributed as dist
+    import phantom_moe as pm
+    from phantom_moe import ep
+    Hm, Em, km, Im, Tt = 4096, 8, 2, 14336, args.prefill_tokens
+    T = Tt // ws
+    lo, hi = ep.shard_range(Em, ws, rank)
+    g = torch.Generator(device=device).manual_seed(2)
+    x = torch.randn(Tt, Hm, device=device, generator=g).to(torch.bfloat16)[rank * T:(rank + 1) * T].contiguous()
+    wr = (torch.randn(Em, Hm, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    w13 = torch.randn(Em, 2 * Im, Hm, device=device, generator=g) * 0.02
+    p13 = pm.quantize_int4(w13[lo:hi].contiguous(), G)
+    del w13
+    w2 = torch.randn(Em, Hm, Im, device=device, generator=g) * 0.02
+    p2 = pm.quantize_int4(w2[lo:hi].contiguous(), G)
+    del w2
+    torch.cuda.empty_cache()
+    wts = (p13[0], p13[1], p2[0], p2[1])
+    exchange = ep.PeerExchange(None, T, km, Hm, Em) if args.ep_exchange == "peer" else None
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        return ep.moe_layer_ep(x, wr, *wts, km, True, G, None, path="prefill", exchange=exchange)
+
+    for _ in range(3):
+        step()
+    dist.barrier()
+    torch.cuda.synchronize()
+    steps = max(5, min(args.steps, 20))
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        step()
+    ev1.record(stream)
+    ev1.synchronize()
+    dist.barrier()
+    t = torch.tensor([ev0.elapsed_time(ev1) / steps], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    if exchange is not None:
+        exchange.close()
+    del x, wr, wts, p13, p2
+    torch.cuda.empty_cache()
+    flops = 2.0 * 3 * Hm * Im * km * Tt
+    return {"workload": f"config 3: mixtral-8x7b moe layer prefill, {Tt} tokens over {ws} GPUs "
+                        f"({T} per GPU), {Em // ws} experts per GPU, strong scaling",
+            "exchange": args.ep_exchange, "tokens_per_s": Tt / (ms / 1e3), "ms_per_step": ms, "steps": steps,
+            "tflops_all_gpus": flops / (ms / 1e3) / 1e12}
+
+
 def run_ep_zipf(args, ws, rank, device):
     """BASELINE config 5 under expert parallelism: 8192 tokens in total
     (8192 / N per rank), router logits biased by log of a Zipf(1.2) prior over
@@ -648,8 +703,11 @@ def _sweep_entry(v):
 
 def run_ep(args, ws, rank, device):
     """N > 1: experts sharded E/N per rank, each rank routes its own
-    ``--tokens`` tokens (weak scaling), NCCL all-to-all dispatch and return.
-    Every rank runs the same collectives in the same order."""
+    ``--tokens`` tokens (weak scaling); rows move through peer memory
+    (``--ep-exchange nccl``: NCCL all-to-alls). Unless ``--no-ep-extras``,
+    BASELINE configs 5 (Zipf skew) and 3 (Mixtral prefill) are measured at
+    this N too and reported in the same line. Every rank runs the same
+    collectives in the same order."""
     import torch.distributed as dist
     import phantom_moe as pm
     from phantom_moe import ep
@@ -718,7 +776,28 @@ def run_ep(args, ws, rank, device):
         oh.copy_(out, non_blocking=True)
         stream.synchronize()
 
-    ms_e2e = timed(e2e_step, args.steps, args.warmup)
+    ms_e2e_sync = timed(e2e_step, args.steps, args.warmup)
+    # the same through HostPipeline: copies on their own streams, the layer
+    # (eager, with its peer exchange) on the pipeline's compute stream
+    pipe = pm.HostPipeline([lambda xx, out, l=l: out.copy_(step(l, x=xx)) for l in range(L)], T, H, device=device)
+    ohp = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    for i in range(args.warmup):
+        pipe.submit(xh[i % L], ohp[i % 2])
+    pipe.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(pipe.copy_in)
+    for i in range(args.steps):
+        pipe.submit(xh[i % L], ohp[i % 2])
+    p1.record(pipe.copy_out)
+    p1.synchronize()
+    pipe.synchronize()
+    dist.barrier()
+    t = torch.tensor([p0.elapsed_time(p1) / args.steps], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_e2e = float(t.item())
+    del pipe
     # per-stage device time on this rank (events the library records inside the layer)
     from phantom_moe import _lib
     import ctypes
@@ -763,12 +842,26 @@ def run_ep(args, ws, rank, device):
                          "algorithmic_bytes_per_launch": bytes_gpu},
             "cpu_baseline": None,
             "e2e": {"value": ws * T / (ms_e2e / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
-                    "d2h_bytes_per_step": T * H * 2, "ms_per_step": ms_e2e},
+                    "d2h_bytes_per_step": T * H * 2, "ms_per_step": ms_e2e,
+                    "api": "phantom_moe.HostPipeline over moe_layer_ep (peer exchange) per step on every rank: "
+                           "pinned host -> device copy of the rank's tokens, the layer, device -> host copy of "
+                           "its output, copies on their own streams; max over ranks",
+                    "sync": {"value": ws * T / (ms_e2e_sync / 1e3), "ms_per_step": ms_e2e_sync,
+                             "api": "the same on one stream, host synchronised after every step"}},
             "clocks": clocks, "gpu_launches": int(launches * args.steps // (args.steps + args.warmup)),
         }
-        print(json.dumps(line), flush=True)
     if exchange is not None:
         exchange.close()
+    # BASELINE configs 5 and 3 at this N (every rank runs both; rank 0 reports)
+    extras = {}
+    if args.ep_extras:
+        del layers
+        torch.cuda.empty_cache()
+        extras["config5_zipf"] = run_ep_zipf(args, ws, rank, device)
+        extras["config3_prefill_ep"] = run_ep_prefill(args, ws, rank, device)
+    if rank == 0:
+        line.update(extras)
+        print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -834,6 +927,8 @@ def main():
                     help="also time transformers generate with and without install_into (an extra JSON object)")
     ap.add_argument("--stack", type=int, default=0,
                     help="only time a decode step through this many MoE layers (config 4 on one GPU)")
+    ap.add_argument("--no-ep-extras", dest="ep_extras", action="store_false",
+                    help="N > 1: skip the config-5 (Zipf) and config-3 (expert-parallel prefill) legs")
     ap.add_argument("--zipf", action="store_true",
                     help="N > 1: only the config-5 Zipf-skewed routing measurement (8192 tokens in total)")
     ap.add_argument("--hf-layers", type=int, default=4)
