@@ -61,6 +61,127 @@ def shard_range(num_experts: int, world: int, rank: int) -> tuple[int, int]:
     return rank * per, (rank + 1) * per
 
 
+@dataclass
+class Placement:
+    """Which global experts each rank holds, replicas of hot experts included.
+
+    ``slots[r]`` lists rank r's experts (its home shard first, then the
+    copies it hosts); every rank is padded to ``S = max len(slots[r])`` local
+    slots, so local slot j of rank r is the virtual expert ``r * S + j``.
+    Each source rank sends all its rows for expert e to one copy
+    (:meth:`copy_for`): its own copy when it holds one (no NVLink traffic),
+    otherwise the copies in turn over the sources that hold none, starting
+    after the home copy. The rows are then dispatched by virtual expert,
+    which keeps them destination-rank-major, so the exchange is unchanged. A
+    row's result does not depend on which copy computes it, so the layer
+    output is the same bit for bit."""
+    slots: list
+    num_experts: int
+
+    def __post_init__(self):
+        held = sorted({e for s in self.slots for e in s})
+        if held != list(range(self.num_experts)):
+            raise ValueError("every expert must be held by at least one rank")
+        for s in self.slots:
+            if len(set(s)) != len(s):
+                raise ValueError("a rank holds an expert at most once")
+        self._copies = {e: [] for e in range(self.num_experts)}
+        for r, s in enumerate(self.slots):
+            for j, e in enumerate(s):
+                self._copies[e].append((r, j))
+
+    @property
+    def world(self) -> int:
+        return len(self.slots)
+
+    @property
+    def slots_per_rank(self) -> int:
+        return max(len(s) for s in self.slots)
+
+    def copies(self, e: int) -> list:
+        """(rank, slot) of every copy of expert e, in rank order."""
+        return list(self._copies[e])
+
+    def copy_for(self, e: int, source_rank: int) -> tuple:
+        """(rank, slot) of the copy of expert e that ``source_rank`` uses."""
+        c = self._copies[e]
+        for r, j in c:
+            if r == source_rank:
+                return r, j
+        holders = {r for r, _ in c}
+        others = [q for q in range(self.world) if q not in holders]
+        return c[(others.index(source_rank) + 1) % len(c)]
+
+    def virtual_map(self, source_rank: int) -> torch.Tensor:
+        """int32 [E]: the virtual expert that ``source_rank`` sends expert e's rows to."""
+        S = self.slots_per_rank
+        vm = []
+        for e in range(self.num_experts):
+            r, j = self.copy_for(e, source_rank)
+            vm.append(r * S + j)
+        return torch.tensor(vm, dtype=torch.int32)
+
+    def local_experts(self, rank: int) -> list:
+        """Global expert of each of rank's S local slots (padding repeats the
+        rank's last expert; padded slots never receive rows)."""
+        s = list(self.slots[rank])
+        return s + [s[-1]] * (self.slots_per_rank - len(s))
+
+    def local_weights(self, rank: int, *tensors):
+        """Rank's slot-stacked copies of full per-expert tensors ``[E, ...]``."""
+        idx = torch.tensor(self.local_experts(rank), dtype=torch.long)
+        return tuple(t.index_select(0, idx.to(t.device)).contiguous() for t in tensors)
+
+    def rank_loads(self, expert_load) -> list:
+        """Rows each rank receives when expert e receives expert_load[e] rows
+        spread evenly over the source ranks."""
+        P = self.world
+        load = [0.0] * P
+        for e in range(self.num_experts):
+            for s in range(P):
+                load[self.copy_for(e, s)[0]] += float(expert_load[e]) / P
+        return load
+
+
+def home_placement(num_experts: int, world: int) -> Placement:
+    """No replicas: rank r holds :func:`shard_range`'s experts."""
+    return Placement([list(range(*shard_range(num_experts, world, r))) for r in range(world)], num_experts)
+
+
+def plan_replicas(expert_load, world: int, extra_slots: int) -> Placement:
+    """Greedy replication of hot experts: starting from the home shards, up to
+    ``extra_slots`` copies per rank are added, each time copying the expert
+    whose copies carry the most rows onto the least-loaded rank that has room
+    and does not hold it yet, while that improves the rank loads sorted from
+    the busiest down (compared in that order, so ties at the top still make
+    progress). ``expert_load[e]``: rows routed to expert e (e.g. counted over
+    a batch)."""
+    E = len(expert_load)
+    pl = home_placement(E, world)
+    base = len(pl.slots[0])
+
+    def key(p):
+        return [round(v, 6) for v in sorted(p.rank_loads(expert_load), reverse=True)]
+
+    while True:
+        loads = pl.rank_loads(expert_load)
+        cur = key(pl)
+        best = None
+        for e in sorted(range(E), key=lambda q: -float(expert_load[q]) / len(pl.copies(q))):
+            holders = {r for r, _ in pl.copies(e)}
+            room = [r for r in range(world) if r not in holders and len(pl.slots[r]) < base + extra_slots]
+            if not room:
+                continue
+            r = min(room, key=lambda q: (loads[q], q))
+            trial = Placement([list(s) + ([e] if i == r else []) for i, s in enumerate(pl.slots)], E)
+            if key(trial) < cur:
+                best = trial
+                break
+        if best is None:
+            return pl
+        pl = best
+
+
 class CudaOps:
     """The product's compute steps: the libphmoe CUDA kernels."""
 
@@ -101,10 +222,17 @@ class Routed:
     counts: torch.Tensor     # int32 [E], rows per expert = per (destination rank, local expert)
 
 
-def route_local(x, router_weight, top_k, renormalize, ops) -> Routed:
+def route_local(x, router_weight, top_k, renormalize, ops, vmap=None, num_virtual=None) -> Routed:
+    """Router + dispatch of this rank's tokens. With ``vmap`` (int32 [E],
+    :meth:`Placement.virtual_map`) the rows are grouped by virtual expert
+    (``num_virtual`` = ranks x slots) instead of by expert."""
     E = router_weight.shape[0]
     idx, w = ops.router(x, router_weight, top_k, renormalize)
-    offsets, row_token, inv, _ = ops.dispatch(idx, E)
+    if vmap is None:
+        offsets, row_token, inv, _ = ops.dispatch(idx, E)
+    else:
+        vidx = vmap.to(idx.device)[idx.long()].to(torch.int32)
+        offsets, row_token, inv, _ = ops.dispatch(vidx, num_virtual)
     counts = (offsets[1:] - offsets[:-1]).to(torch.int32)
     return Routed(idx, w, offsets, row_token, inv, counts)
 
@@ -199,7 +327,7 @@ class PeerExchange:
 def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scales, top_k: int,
                  renormalize: bool = True, group_size: int = 64, ep_group=None, *, path: str = "auto",
                  return_routing: bool = False, ops=None, stats: dict | None = None,
-                 exchange: PeerExchange | None = None):
+                 exchange: PeerExchange | None = None, placement: Placement | None = None):
     """The MoE layer with this rank's expert shard (``w13_q`` etc. hold
     ``E/P`` experts, ``router_weight`` all ``E``). Same result as
     :func:`phantom_moe.moe_layer` on the full layer for this rank's tokens.
@@ -213,8 +341,16 @@ def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scale
     move through peer memory inside one library call; otherwise through
     ``torch.distributed.all_to_all_single`` (any backend, the checker's
     ``ops`` included; one device-to-host copy of the counts per call).
+
+    With ``placement`` (a :class:`Placement` over the group's ranks, hot
+    experts replicated) the expert tensors hold this rank's
+    ``placement.slots_per_rank`` local slots (:meth:`Placement.local_weights`)
+    and every rank sends each expert's rows to the copy the placement assigns
+    it; the all-to-all exchange only.
     """
     import torch.distributed as dist
+    if placement is not None and exchange is not None:
+        raise NotImplementedError("replicated placements use the all-to-all exchange (exchange=None)")
     if exchange is not None:
         _layer._need_cuda("hidden_states", hidden_states)
         shape = hidden_states.shape
@@ -230,15 +366,26 @@ def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scale
     H = shape[-1]
     x = hidden_states.reshape(-1, H)
     E = router_weight.shape[0]
-    if w13_q.shape[0] * world != E:
-        raise ValueError(f"this rank holds {w13_q.shape[0]} experts; {E} experts over {world} ranks "
-                         f"needs {E // max(world, 1)} per rank")
-    rt = route_local(x, router_weight, top_k, renormalize, ops)
+    if placement is None:
+        if w13_q.shape[0] * world != E:
+            raise ValueError(f"this rank holds {w13_q.shape[0]} experts; {E} experts over {world} ranks "
+                             f"needs {E // max(world, 1)} per rank")
+        rt = route_local(x, router_weight, top_k, renormalize, ops)
+    else:
+        S = placement.slots_per_rank
+        if placement.world != world or placement.num_experts != E:
+            raise ValueError(f"placement is for {placement.num_experts} experts over {placement.world} ranks; "
+                             f"this layer has {E} experts over {world} ranks")
+        if w13_q.shape[0] != S:
+            raise ValueError(f"this rank holds {w13_q.shape[0]} expert slots; the placement has {S} per rank")
+        rank = dist.get_rank(ep_group)
+        rt = route_local(x, router_weight, top_k, renormalize, ops, placement.virtual_map(rank), world * S)
+    V = rt.counts.numel()  # experts (or virtual experts) over all ranks
     recv_counts = torch.empty_like(rt.counts)
     dist.all_to_all_single(recv_counts, rt.counts, group=ep_group)
     both = torch.cat([rt.counts, recv_counts]).cpu()
-    send_rows = rows_per_rank(both[:E], world)
-    recv_rows = rows_per_rank(both[E:], world)
+    send_rows = rows_per_rank(both[:V], world)
+    recv_rows = rows_per_rank(both[V:], world)
     send_x = ops.gather(x, rt.row_token)
     recv_x = x.new_empty((sum(recv_rows), H))
     dist.all_to_all_single(recv_x, send_x, recv_rows, send_rows, group=ep_group)
@@ -250,7 +397,7 @@ def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scale
     if stats is not None:
         stats["send_rows"] = send_rows
         stats["recv_rows"] = recv_rows
-        stats["local_experts_hit"] = int((both[E:].view(world, -1).sum(0) > 0).sum())
+        stats["local_experts_hit"] = int((both[V:].view(world, -1).sum(0) > 0).sum())
     if return_routing:
         return out, rt.idx, rt.w
     return out

@@ -88,7 +88,17 @@ def make_case(case: str, world: int):
     return xs, wr, (torch.from_numpy(p13), torch.from_numpy(s13), torch.from_numpy(p2), torch.from_numpy(s2))
 
 
-def gloo_worker(rank: int, world: int, port: int, case: str, out_dir: str):
+def replica_plan(xs, wr, world: int):
+    """The replicated placement every rank derives from the routing of all
+    tokens (one extra slot per rank for each home expert)."""
+    from phantom_moe import ep
+    H, E, k, I, G = DIMS
+    idx, _ = OracleOps().router(torch.cat(xs), wr, k, True)
+    load = np.bincount(idx.numpy().reshape(-1), minlength=E)
+    return ep.plan_replicas(load.tolist(), world, E // world)
+
+
+def gloo_worker(rank: int, world: int, port: int, case: str, out_dir: str, replicate: bool = False):
     import torch.distributed as dist
     from phantom_moe import ep
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -97,10 +107,16 @@ def gloo_worker(rank: int, world: int, port: int, case: str, out_dir: str):
     try:
         H, E, k, I, G = DIMS
         xs, wr, (p13, s13, p2, s2) = make_case(case, world)
-        lo, hi = ep.shard_range(E, world, rank)
         stats = {}
-        out, idx, w = ep.moe_layer_ep(xs[rank], wr, p13[lo:hi], s13[lo:hi], p2[lo:hi], s2[lo:hi], k, True, G,
-                                      None, return_routing=True, ops=OracleOps(), stats=stats)
+        if replicate:
+            pl = replica_plan(xs, wr, world)
+            local = pl.local_weights(rank, p13, s13, p2, s2)
+            out, idx, w = ep.moe_layer_ep(xs[rank], wr, *local, k, True, G, None, return_routing=True,
+                                          ops=OracleOps(), stats=stats, placement=pl)
+        else:
+            lo, hi = ep.shard_range(E, world, rank)
+            out, idx, w = ep.moe_layer_ep(xs[rank], wr, p13[lo:hi], s13[lo:hi], p2[lo:hi], s2[lo:hi], k, True, G,
+                                          None, return_routing=True, ops=OracleOps(), stats=stats)
         np.savez(Path(out_dir) / f"rank{rank}.npz", out=out.numpy(), idx=idx.numpy(), w=w.numpy(),
                  send=np.array(stats["send_rows"]), recv=np.array(stats["recv_rows"]))
     finally:
