@@ -641,14 +641,18 @@ def run_ep_zipf(args, ws, rank, device):
     """BASELINE config 5 under expert parallelism: 8192 tokens in total
     (8192 / N per rank), router logits biased by log of a Zipf(1.2) prior over
     the experts (a constant input feature x[:, 0] = 1 meeting router column
-    0 = log p_i), against the same layer without the bias; reports the load
+    0 = log p_i), against the same layer without the bias, and with hot
+    experts replicated (``phantom_moe.ep.plan_replicas`` over the Zipf case's
+    expert loads, ``--replica-slots`` extra slots per rank); reports the load
     imbalance, every rank's received rows and the step time (max over ranks)."""
     import torch.distributed as dist
     import phantom_moe as pm
     from phantom_moe import ep
     T = 8192 // ws
     lo, hi = ep.shard_range(E, ws, rank)
-    wr, pk = make_layer(7, device, expert_range=(lo, hi))
+    wr, pk_full = make_layer(7, device)
+    full = _pk(pk_full)
+    shard = tuple(t[lo:hi] for t in full)
     g = torch.Generator(device=device).manual_seed(4000 + 7919 * rank)
     x = torch.randn(T, H, device=device, generator=g)
     prior = torch.log(torch.arange(1, E + 1, device=device, dtype=torch.float32) ** -1.2)
@@ -656,24 +660,34 @@ def run_ep_zipf(args, ws, rank, device):
     wr_skew[:, 0] = prior
     x_skew = x.clone()
     x_skew[:, 0] = 1.0
-    cases = {"balanced": (x.to(torch.bfloat16), wr), "zipf": (x_skew.to(torch.bfloat16), wr_skew.to(torch.bfloat16))}
+    cases = {"balanced": (x.to(torch.bfloat16), wr), "zipf": (x_skew.to(torch.bfloat16), wr_skew.to(torch.bfloat16)),
+             "zipf_replicated": None}
     stream = torch.cuda.current_stream(device)
-    exchange = ep.PeerExchange(None, T, K_TOP, H, E) if args.ep_exchange == "peer" else None
     res = {}
-    for name, (xc, wc) in cases.items():
+    for name in cases:
+        placement = None
+        if name == "zipf_replicated":
+            xc, wc = cases["zipf"]
+            placement = ep.plan_replicas(res["zipf"]["expert_rows"], ws, args.replica_slots)
+            weights = placement.local_weights(rank, *full)
+        else:
+            xc, wc = cases[name]
+            weights = shard
+        exchange = (ep.PeerExchange(None, T, K_TOP, H, E, placement=placement)
+                    if args.ep_exchange == "peer" else None)
         st = {}
-        ep.moe_layer_ep(xc, wc, *_pk(pk), K_TOP, True, G, None, stats=st)  # row counts (NCCL path)
+        ep.moe_layer_ep(xc, wc, *weights, K_TOP, True, G, None, stats=st, placement=placement)  # row counts
         loads = torch.tensor(st["recv_rows"], device=device, dtype=torch.float32)
         all_loads = [torch.zeros_like(loads) for _ in range(ws)]
         dist.all_gather(all_loads, loads)
         for _ in range(args.warmup):
-            ep.moe_layer_ep(xc, wc, *_pk(pk), K_TOP, True, G, None, exchange=exchange)
+            ep.moe_layer_ep(xc, wc, *weights, K_TOP, True, G, None, exchange=exchange, placement=placement)
         dist.barrier()
         torch.cuda.synchronize()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
         for _ in range(args.steps):
-            ep.moe_layer_ep(xc, wc, *_pk(pk), K_TOP, True, G, None, exchange=exchange)
+            ep.moe_layer_ep(xc, wc, *weights, K_TOP, True, G, None, exchange=exchange, placement=placement)
         ev1.record(stream)
         ev1.synchronize()
         dist.barrier()
@@ -686,10 +700,20 @@ def run_ep_zipf(args, ws, rank, device):
         recv = [float(v) for v in torch.stack(all_loads).sum(dim=1).tolist()]
         res[name] = {"ms_per_step": ms, "tokens_per_s": 8192 / (ms / 1e3),
                      "expert_load_max_over_mean": float(cnt.max() / cnt.mean()),
-                     "rows_received_per_rank": recv, "rank_load_max_over_mean": max(recv) / (sum(recv) / ws)}
+                     "rows_received_per_rank": recv, "rank_load_max_over_mean": max(recv) / (sum(recv) / ws),
+                     "expert_rows": [int(v) for v in cnt.tolist()]}
+        if placement is not None:
+            res[name]["slots_per_rank"] = placement.slots_per_rank
+            res[name]["copies_of_hottest"] = len(placement.copies(int(cnt.argmax())))
+        if exchange is not None:
+            exchange.close()
+        del weights
+    for v in res.values():
+        del v["expert_rows"]
     res["zipf_over_balanced_time"] = res["zipf"]["ms_per_step"] / res["balanced"]["ms_per_step"]
-    if exchange is not None:
-        exchange.close()
+    res["zipf_replicated_over_balanced_time"] = res["zipf_replicated"]["ms_per_step"] / res["balanced"]["ms_per_step"]
+    del full, shard, pk_full
+    torch.cuda.empty_cache()
     return {"workload": f"config 5: 8192 tokens over {ws} GPUs, Zipf(1.2) router prior, top-8 of 128",
             "exchange": args.ep_exchange, **res}
 
@@ -929,6 +953,8 @@ def main():
                     help="only time a decode step through this many MoE layers (config 4 on one GPU)")
     ap.add_argument("--no-ep-extras", dest="ep_extras", action="store_false",
                     help="N > 1: skip the config-5 (Zipf) and config-3 (expert-parallel prefill) legs")
+    ap.add_argument("--replica-slots", type=int, default=8,
+                    help="N > 1, config 5: extra expert slots per rank for copies of hot experts")
     ap.add_argument("--zipf", action="store_true",
                     help="N > 1: only the config-5 Zipf-skewed routing measurement (8192 tokens in total)")
     ap.add_argument("--hf-layers", type=int, default=4)

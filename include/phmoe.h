@@ -209,6 +209,27 @@ int phmoe_ep_layer(void* ctx, const void* x, int x_dtype, const void* router_w, 
                    size_t workspace_bytes, void* stream);
 
 /*
+ * Replicated placements (hot experts copied onto several ranks, to even out
+ * skewed routing). phmoe_ep_create_ex sizes every rank for slots_per_rank
+ * local expert slots (>= E/world; 0 means E/world; world * slots <= 1024);
+ * rank r's slot j is the virtual expert r * slots + j. phmoe_ep_layer_ex
+ * takes this rank's map vmap [E] int32 (device memory): the virtual expert
+ * each of its expert ids is sent to, i.e. the copy it uses; w13_q etc. hold
+ * the rank's `slots` local experts (padding slots may repeat any expert; they
+ * receive no rows). Rows with a map entry outside [0, world * slots) are
+ * dropped. With vmap = NULL it is phmoe_ep_layer (home placement only). Every
+ * row's result is the same whichever copy computes it, so the output equals
+ * phmoe_ep_layer's.
+ */
+int phmoe_ep_create_ex(int rank, int world, int max_tokens, int top_k, int H, int E, int slots_per_rank,
+                       int x_dtype, void** ctx, void* ipc_handle_out);
+int phmoe_ep_layer_ex(void* ctx, const void* x, int x_dtype, const void* router_w, int w_dtype,
+                      const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T,
+                      int I, int group_size, int renormalize, int path, const int32_t* vmap, void* out,
+                      int32_t* topk_idx_out, float* topk_w_out, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/*
  * The whole layer (Qwen3MoeSparseMoeBlock.forward, modeling_qwen3_moe.py:281-286,
  * on [T, H] rows): router -> dispatch -> grouped FFN -> combine, all
  * stream-ordered, no host synchronisation, no allocation.

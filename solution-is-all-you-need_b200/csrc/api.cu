@@ -538,8 +538,8 @@ int phmoe_device_error(int reset) {
 
 // ---- expert parallelism in peer memory ----
 
-int phmoe_ep_create(int rank, int world, int max_tokens, int top_k, int H, int E, int x_dtype, void** ctx,
-                    void* ipc_handle_out) {
+int phmoe_ep_create_ex(int rank, int world, int max_tokens, int top_k, int H, int E, int slots_per_rank,
+                       int x_dtype, void** ctx, void* ipc_handle_out) {
   g_last_error.clear();
   if (!ctx || !ipc_handle_out) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
   *ctx = nullptr;
@@ -549,12 +549,21 @@ int phmoe_ep_create(int rank, int world, int max_tokens, int top_k, int H, int E
   if (E < 1 || E > 1024 || E % world) return fail(PHMOE_ERR_INVALID_ARG, "E=%d must split evenly over %d ranks", E, world);
   if (max_tokens < 1 || top_k < 1 || top_k > E || top_k > 32 || H <= 0 || H % 8)
     return fail(PHMOE_ERR_INVALID_ARG, "bad dims max_tokens=%d top_k=%d H=%d", max_tokens, top_k, H);
+  const int slots = slots_per_rank ? slots_per_rank : E / world;
+  if (slots < E / world || (long long)slots * world > 1024)
+    return fail(PHMOE_ERR_INVALID_ARG, "slots_per_rank=%d must be >= E/world=%d with world*slots <= 1024",
+                slots_per_rank, E / world);
   EpContext* c = nullptr;
-  const int s = ep_create(rank, world, max_tokens, top_k, H, E, x_dtype == PHMOE_DTYPE_F32 ? 4 : 2, &c,
+  const int s = ep_create(rank, world, max_tokens, top_k, H, E, slots, x_dtype == PHMOE_DTYPE_F32 ? 4 : 2, &c,
                           ipc_handle_out);
   if (s) return fail(s, "could not allocate or export the exchange region (%s)", cudaGetErrorString(cudaGetLastError()));
   *ctx = c;
   return PHMOE_OK;
+}
+
+int phmoe_ep_create(int rank, int world, int max_tokens, int top_k, int H, int E, int x_dtype, void** ctx,
+                    void* ipc_handle_out) {
+  return phmoe_ep_create_ex(rank, world, max_tokens, top_k, H, E, 0, x_dtype, ctx, ipc_handle_out);
 }
 
 int phmoe_ep_connect(void* ctx, const void* ipc_handles) {
@@ -576,22 +585,28 @@ size_t phmoe_ep_workspace_size(const void* ctx, int I) {
   return ep_workspace_bytes(static_cast<const EpContext*>(ctx), I);
 }
 
-int phmoe_ep_layer(void* ctx, const void* x, int x_dtype, const void* router_w, int w_dtype, const uint8_t* w13_q,
-                   const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T, int I, int group_size,
-                   int renormalize, int path, void* out, int32_t* topk_idx_out, float* topk_w_out, void* workspace,
-                   size_t workspace_bytes, void* stream) {
+int phmoe_ep_layer_ex(void* ctx, const void* x, int x_dtype, const void* router_w, int w_dtype,
+                      const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T,
+                      int I, int group_size, int renormalize, int path, const int32_t* vmap, void* out,
+                      int32_t* topk_idx_out, float* topk_w_out, void* workspace, size_t workspace_bytes,
+                      void* stream) {
   g_last_error.clear();
   if (!ctx) return fail(PHMOE_ERR_INVALID_ARG, "null context");
   EpContext* c = static_cast<EpContext*>(ctx);
   int rank, world, max_tokens, top_k, H, E;
   if (!ep_info(c, &rank, &world, &max_tokens, &top_k, &H, &E))
     return fail(PHMOE_ERR_INVALID_ARG, "context not connected (phmoe_ep_connect)");
+  const int slots = ep_slots(c);
+  if (!vmap && slots != E / world)
+    return fail(PHMOE_ERR_INVALID_ARG, "a context with %d slots per rank (E/world = %d) needs the expert map",
+                slots, E / world);
+  if (vmap && !aligned(vmap, 4)) return fail(PHMOE_ERR_ALIGNMENT, "vmap must be 4-byte aligned");
   if (T < 0 || T > max_tokens) return fail(PHMOE_ERR_INVALID_ARG, "T=%d outside [0, %d]", T, max_tokens);
   if (!dtype_ok(x_dtype) || !dtype_ok(w_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
   if (int s = check_router_smem(H, x_dtype)) return s;
-  // the path is chosen for the rows a rank expects (T*k over E/world experts)
+  // the path is chosen for the rows a rank expects (T*k over its local slots)
   int chosen = PHMOE_PATH_DECODE;
-  if (int s = resolve_path(path, x_dtype, T > 0 ? T : 1, top_k, H, I, group_size, E / world, &chosen)) return s;
+  if (int s = resolve_path(path, x_dtype, T > 0 ? T : 1, top_k, H, I, group_size, slots, &chosen)) return s;
   if ((T > 0 && (!x || !router_w || !out)) || !w13_q || !w13_s || !w2_q || !w2_s || !workspace)
     return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
   if (!aligned(x, 16) || !aligned(router_w, 16) || !aligned(w13_q, 16) || !aligned(w2_q, 16) || !aligned(out, 16))
@@ -607,10 +622,19 @@ int phmoe_ep_layer(void* ctx, const void* x, int x_dtype, const void* router_w, 
     for (int b = 0; b <= PHMOE_NUM_STAGES; ++b) marks[b] = prof_event(g_prof.calls, b);
   const int s = ep_layer(c, x, x_dtype, router_w, w_dtype, w13_q, w13_s, w2_q, w2_s, T, I, group_size, renormalize,
                          chosen, out, topk_idx_out, topk_w_out, workspace, static_cast<cudaStream_t>(stream),
-                         prof ? marks : nullptr);
+                         prof ? marks : nullptr, vmap);
   if (prof) g_prof.calls++;
   if (s) return fail(s, "expert FFN launch failed");
   return check_launch("phmoe_ep_layer");
+}
+
+int phmoe_ep_layer(void* ctx, const void* x, int x_dtype, const void* router_w, int w_dtype, const uint8_t* w13_q,
+                   const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T, int I, int group_size,
+                   int renormalize, int path, void* out, int32_t* topk_idx_out, float* topk_w_out, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  return phmoe_ep_layer_ex(ctx, x, x_dtype, router_w, w_dtype, w13_q, w13_s, w2_q, w2_s, T, I, group_size,
+                           renormalize, path, nullptr, out, topk_idx_out, topk_w_out, workspace, workspace_bytes,
+                           stream);
 }
 
 int phmoe_profile_begin(int max_calls) {

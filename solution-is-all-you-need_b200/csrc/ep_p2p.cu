@@ -25,6 +25,11 @@
 //     return buffer at that row; the last CTA raises the return flags;
 //   ep_wait_kernel   - waits (bounded) for every destination's return flag;
 //   combine over the returned rows in slot order.
+// Replicated placements (hot experts copied onto several ranks): every rank
+// holds S >= E/P local slots and the layer takes this rank's map from expert
+// to virtual expert (rank * S + slot of the copy it sends to); the router's
+// ids are remapped to virtual ids before the dispatch, so the rows still come
+// out destination-major and every step below runs with S in place of E/P.
 // Reusing the single receive/return buffers is safe without further
 // handshakes: a source writes epoch e+1 rows only after its combine of epoch
 // e, which waited for this rank's return of epoch e, which came after this
@@ -260,6 +265,19 @@ ep_return_kernel(const float* __restrict__ y, const int32_t* __restrict__ off, i
     st_release_sys(reinterpret_cast<uint32_t*>(peers.base[threadIdx.x] + L.flags_back) + me, epoch);
 }
 
+// vidx[i] = vmap[idx[i]]: expert ids to virtual experts (-1, i.e. dropped
+// by the dispatch, for ids outside [0, E) or maps outside [0, V)).
+__global__ void __launch_bounds__(kCopyThreads)
+ep_remap_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ vmap, int R, int E, int V,
+                int32_t* __restrict__ vidx) {
+  pdl_begin();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < R; i += gridDim.x * blockDim.x) {
+    const int e = __ldg(idx + i);
+    const int v = (unsigned)e < (unsigned)E ? __ldg(vmap + e) : -1;
+    vidx[i] = (unsigned)v < (unsigned)V ? v : -1;
+  }
+}
+
 __global__ void ep_wait_kernel(const char* __restrict__ local, Region L, int world, uint32_t epoch) {
   pdl_begin();
   if (threadIdx.x < world) wait_flag(reinterpret_cast<const uint32_t*>(local + L.flags_back) + threadIdx.x, epoch);
@@ -268,7 +286,8 @@ __global__ void ep_wait_kernel(const char* __restrict__ local, Region L, int wor
 }  // namespace
 
 struct EpContext {
-  int rank = 0, world = 1, max_tokens = 0, top_k = 1, H = 0, E = 0, epr = 0, elt = 2, cap = 0, device = 0;
+  // epr: local expert slots per rank (E/world, more with replicas); V = world * epr virtual experts
+  int rank = 0, world = 1, max_tokens = 0, top_k = 1, H = 0, E = 0, epr = 0, V = 0, elt = 2, cap = 0, device = 0;
   Region L{};
   char* local = nullptr;
   Peers peers{};
@@ -287,10 +306,10 @@ int ep_device_error(bool reset) {
   return v;
 }
 
-int ep_create(int rank, int world, int max_tokens, int top_k, int H, int E, int x_elt, EpContext** out,
+int ep_create(int rank, int world, int max_tokens, int top_k, int H, int E, int slots, int x_elt, EpContext** out,
               void* handle_out) {
   if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || E % world || max_tokens < 1 || top_k < 1 ||
-      H <= 0 || (H * x_elt) % 16)
+      H <= 0 || (H * x_elt) % 16 || (slots != 0 && slots < E / world))
     return PHMOE_ERR_INVALID_ARG;
   EpContext* c = new EpContext();
   c->rank = rank;
@@ -299,7 +318,8 @@ int ep_create(int rank, int world, int max_tokens, int top_k, int H, int E, int 
   c->top_k = top_k;
   c->H = H;
   c->E = E;
-  c->epr = E / world;
+  c->epr = slots ? slots : E / world;
+  c->V = world * c->epr;
   c->elt = x_elt;
   c->cap = max_tokens * top_k;
   c->L = region_layout(world, c->cap, c->epr, H, x_elt);
@@ -350,11 +370,12 @@ size_t ep_workspace_bytes(const EpContext* c, int I) {
   take((size_t)c->max_tokens * c->E * 4);               // logits
   take((size_t)c->cap * 4);                             // idx
   take((size_t)c->cap * 4);                             // w
-  take((size_t)(c->E + 1) * 4);                         // offsets
-  take((size_t)(c->E + 1) * 4);                         // active
+  take((size_t)(c->V + 1) * 4);                         // offsets (per virtual expert)
+  take((size_t)(c->V + 1) * 4);                         // active
   take((size_t)c->cap * 4);                             // row_token
   take((size_t)c->cap * 4);                             // inv
-  take(dispatch_scratch_bytes(c->max_tokens, c->top_k, c->E));
+  take((size_t)c->cap * 4);                             // virtual expert ids
+  take(dispatch_scratch_bytes(c->max_tokens, c->top_k, c->V));
   take((size_t)(c->epr + 1) * 4 * 2);                   // local offsets, active
   take(capr * 4 * 3);                                   // local row_token, ret_src, ret_row
   take(capr * (size_t)I * 4);                           // h
@@ -365,8 +386,8 @@ size_t ep_workspace_bytes(const EpContext* c, int I) {
 int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int w_dtype, const uint8_t* w13_q,
              const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T, int I, int G, int renormalize,
              int path, void* out, int32_t* topk_idx_out, float* topk_w_out, void* workspace, cudaStream_t st,
-             const cudaEvent_t* marks) {
-  const int E = c->E, k = c->top_k, epr = c->epr, world = c->world;
+             const cudaEvent_t* marks, const int32_t* vmap) {
+  const int E = c->E, V = c->V, k = c->top_k, epr = c->epr, world = c->world;
   auto mark = [&](int b) { if (marks) cudaEventRecord(marks[b], st); };
   const size_t capr = (size_t)world * c->cap;
   char* ws = static_cast<char*>(workspace);
@@ -375,11 +396,12 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
   float* logits = reinterpret_cast<float*>(take((size_t)c->max_tokens * E * 4));
   int32_t* idx = reinterpret_cast<int32_t*>(take((size_t)c->cap * 4));
   float* wts = reinterpret_cast<float*>(take((size_t)c->cap * 4));
-  int32_t* offsets = reinterpret_cast<int32_t*>(take((size_t)(E + 1) * 4));
-  int32_t* active = reinterpret_cast<int32_t*>(take((size_t)(E + 1) * 4));
+  int32_t* offsets = reinterpret_cast<int32_t*>(take((size_t)(V + 1) * 4));
+  int32_t* active = reinterpret_cast<int32_t*>(take((size_t)(V + 1) * 4));
   int32_t* row_token = reinterpret_cast<int32_t*>(take((size_t)c->cap * 4));
   int32_t* inv = reinterpret_cast<int32_t*>(take((size_t)c->cap * 4));
-  void* disp = take(dispatch_scratch_bytes(c->max_tokens, k, E));
+  int32_t* vidx = reinterpret_cast<int32_t*>(take((size_t)c->cap * 4));
+  void* disp = take(dispatch_scratch_bytes(c->max_tokens, k, V));
   int32_t* loff = reinterpret_cast<int32_t*>(take((size_t)(epr + 1) * 4 * 2));
   int32_t* lact = loff + (epr + 1);
   int32_t* lrow = reinterpret_cast<int32_t*>(take(capr * 4 * 3));
@@ -396,8 +418,15 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
   mark(0);
   if (T > 0) launch_router(x, x_dtype, router_w, w_dtype, T, c->H, E, k, renormalize, logits, nullptr, idx, wts, st);
   mark(1);
-  if (T > 0) launch_dispatch(idx, T, k, E, offsets, row_token, inv, active, disp, st);
   const int sms = device_sm_count();
+  if (T > 0 && vmap) {  // replicated placement: dispatch by virtual expert
+    launch_pdl(ep_remap_kernel, dim3(R < sms * 4 * kCopyThreads ? (R + kCopyThreads - 1) / kCopyThreads : sms * 4),
+               dim3(kCopyThreads), 0, st, static_cast<const int32_t*>(idx), vmap, R, E, V, vidx);
+    note_launches(1);
+    launch_dispatch(vidx, T, k, V, offsets, row_token, inv, active, disp, st);
+  } else if (T > 0) {
+    launch_dispatch(idx, T, k, E, offsets, row_token, inv, active, disp, st);
+  }
   launch_pdl(ep_send_kernel, dim3(R > 0 ? (R < sms * 4 ? R : sms * 4) : 1), dim3(kCopyThreads), 0, st,
              static_cast<const char*>(x), static_cast<const int32_t*>(row_token), static_cast<const int32_t*>(offsets),
              R, T, epr, world, c->rank, c->cap, row_bytes, c->peers, c->L, epoch);
@@ -426,6 +455,8 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
   note_launches(4 + (T > 0 ? 3 : 0));
   return PHMOE_OK;
 }
+
+int ep_slots(const EpContext* c) { return c->epr; }
 
 int ep_info(const EpContext* c, int* rank, int* world, int* max_tokens, int* top_k, int* H, int* E) {
   *rank = c->rank;

@@ -65,7 +65,8 @@ int record_error(int status, const char* msg);
 
 // Expert-parallel exchange in peer memory (ep_p2p.cu).
 struct EpContext;
-int ep_create(int rank, int world, int max_tokens, int top_k, int H, int E, int x_elt, EpContext** out,
+// slots: local expert slots per rank (0: E/world; more for replicated placements)
+int ep_create(int rank, int world, int max_tokens, int top_k, int H, int E, int slots, int x_elt, EpContext** out,
               void* handle_out);
 int ep_connect(EpContext* c, const void* handles);
 void ep_destroy(EpContext* c);
@@ -73,8 +74,10 @@ size_t ep_workspace_bytes(const EpContext* c, int I);
 int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int w_dtype, const uint8_t* w13_q,
              const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T, int I, int G, int renormalize,
              int path, void* out, int32_t* topk_idx_out, float* topk_w_out, void* workspace, cudaStream_t st,
-             const cudaEvent_t* marks);  // marks: PHMOE_NUM_STAGES + 1 events, or null
+             const cudaEvent_t* marks,   // PHMOE_NUM_STAGES + 1 events, or null
+             const int32_t* vmap);       // [E] expert -> virtual expert (device), or null for the home placement
 int ep_info(const EpContext* c, int* rank, int* world, int* max_tokens, int* top_k, int* H, int* E);
+int ep_slots(const EpContext* c);
 int ep_device_error(bool reset);
 
 }  // namespace phmoe

@@ -53,10 +53,13 @@ SIGNATURES = {
     "phmoe_combine": (_I, [_P, _P, _P, _I, _I, _I, _P, _I, _P]),
     "phmoe_gather_rows": (_I, [_P, _LL, _P, _I, _LL, _P, _P]),
     "phmoe_ep_create": (_I, [_I, _I, _I, _I, _I, _I, _I, _P, _P]),
+    "phmoe_ep_create_ex": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "phmoe_ep_connect": (_I, [_P, _P]),
     "phmoe_ep_destroy": (_I, [_P]),
     "phmoe_ep_workspace_size": (_SZ, [_P, _I]),
     "phmoe_ep_layer": (_I, [_P, _P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P]),
+    "phmoe_ep_layer_ex": (_I, [_P, _P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _SZ,
+                               _P]),
     "phmoe_moe_layer": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,
                              _P, _P, _P, _P, _SZ, _P]),
     "phmoe_moe_layer_noalloc": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I,

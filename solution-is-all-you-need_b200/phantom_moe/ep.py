@@ -272,19 +272,31 @@ class PeerExchange:
 
     All ranks must create it together, call the layer the same number of
     times, and :meth:`close` it together (the group is used for the handle
-    exchange and for barriers only, so gloo or NCCL both work)."""
+    exchange and for barriers only, so gloo or NCCL both work).
+
+    With ``placement`` (a :class:`Placement`, the same on every rank) each
+    rank is sized for ``placement.slots_per_rank`` local expert slots and the
+    layer sends every row to the copy the placement assigns
+    (``phmoe_ep_create_ex`` / ``phmoe_ep_layer_ex``); the expert tensors then
+    hold the rank's slots (:meth:`Placement.local_weights`)."""
 
     def __init__(self, group, max_tokens: int, top_k: int, hidden_size: int, num_experts: int,
-                 dtype: torch.dtype = torch.bfloat16):
+                 dtype: torch.dtype = torch.bfloat16, placement: Placement | None = None):
         import torch.distributed as dist
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.max_tokens, self.top_k, self.hidden_size, self.num_experts = max_tokens, top_k, hidden_size, num_experts
         self.dtype = dtype
+        self.placement = placement
+        if placement is not None and (placement.world != self.world or placement.num_experts != num_experts):
+            raise ValueError(f"placement is for {placement.num_experts} experts over {placement.world} ranks; "
+                             f"the exchange has {num_experts} over {self.world}")
+        self._vmap = {}
         self._ctx = ctypes.c_void_p()
         handle = (ctypes.c_char * _lib.EP_HANDLE_BYTES)()
-        _lib.call("phmoe_ep_create", self.rank, self.world, max_tokens, top_k, hidden_size, num_experts,
+        slots = placement.slots_per_rank if placement is not None else 0
+        _lib.call("phmoe_ep_create_ex", self.rank, self.world, max_tokens, top_k, hidden_size, num_experts, slots,
                   _layer._DT[dtype], ctypes.byref(self._ctx), handle)
         handles = [None] * self.world
         dist.all_gather_object(handles, bytes(handle), group=group)
@@ -307,11 +319,19 @@ class PeerExchange:
         idx = torch.empty(T, self.top_k, dtype=torch.int32, device=x.device) if return_routing else None
         w = torch.empty(T, self.top_k, dtype=torch.float32, device=x.device) if return_routing else None
         ws = self.workspace(x.device, I)
-        _lib.call("phmoe_ep_layer", self._ctx, _layer._ptr(x), _layer._DT[x.dtype], _layer._ptr(router_weight),
+        vmap = None
+        if self.placement is not None:
+            if w13_q.shape[0] != self.placement.slots_per_rank:
+                raise ValueError(f"this rank holds {w13_q.shape[0]} expert slots; the placement has "
+                                 f"{self.placement.slots_per_rank} per rank")
+            if x.device.index not in self._vmap:
+                self._vmap[x.device.index] = self.placement.virtual_map(self.rank).to(x.device)
+            vmap = self._vmap[x.device.index]
+        _lib.call("phmoe_ep_layer_ex", self._ctx, _layer._ptr(x), _layer._DT[x.dtype], _layer._ptr(router_weight),
                   _layer._DT[router_weight.dtype], _layer._ptr(w13_q), _layer._ptr(w13_scales), _layer._ptr(w2_q),
                   _layer._ptr(w2_scales), T, I, group_size, int(bool(renormalize)), _layer._PATHS[path],
-                  _layer._ptr(out), _layer._ptr(idx), _layer._ptr(w), _layer._ptr(ws), ws.numel(),
-                  _layer._stream())
+                  _layer._ptr(vmap), _layer._ptr(out), _layer._ptr(idx), _layer._ptr(w), _layer._ptr(ws),
+                  ws.numel(), _layer._stream())
         return (out, idx, w) if return_routing else out
 
     def close(self):
@@ -346,11 +366,12 @@ def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scale
     experts replicated) the expert tensors hold this rank's
     ``placement.slots_per_rank`` local slots (:meth:`Placement.local_weights`)
     and every rank sends each expert's rows to the copy the placement assigns
-    it; the all-to-all exchange only.
+    it; with ``exchange`` the placement is the one the exchange was created
+    with.
     """
     import torch.distributed as dist
-    if placement is not None and exchange is not None:
-        raise NotImplementedError("replicated placements use the all-to-all exchange (exchange=None)")
+    if exchange is not None and placement is not None and exchange.placement is not placement:
+        raise ValueError("pass the placement the PeerExchange was created with")
     if exchange is not None:
         _layer._need_cuda("hidden_states", hidden_states)
         shape = hidden_states.shape

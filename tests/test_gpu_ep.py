@@ -170,6 +170,26 @@ def _peer_worker(rank, world, port, out_dir, case):
             ok = ok and torch.equal(out, ref[t0:t0 + tokens[rank]])
             ex2.close()
             result = {"ok": ok, "err": lib.phmoe_device_error(1)}
+        elif case == "replicated":
+            # a load that makes rank 0's experts hot, so the planner copies them
+            # onto the other ranks; every rank derives the same placement
+            load = [100 if e < E // world else 1 for e in range(E)]
+            pl = ep.plan_replicas(load, world, E // world)
+            local = pl.local_weights(rank, *packed)
+            ok = pl.slots_per_rank > E // world and local[0].shape[0] == pl.slots_per_rank
+            ex = ep.PeerExchange(None, max_tokens=64, top_k=K, hidden_size=H, num_experts=E, placement=pl)
+            tokens = [64, 40, 0, 64, 17, 64, 5, 33][:world]
+            t0 = sum(tokens[:rank])
+            for it in range(2):  # consecutive calls reuse the exchange buffers
+                g = torch.Generator(device=dev).manual_seed(90 + it)
+                xs = [torch.randn(t, H, device=dev, generator=g).to(torch.bfloat16) for t in tokens]
+                out = ep.moe_layer_ep(xs[rank], wr, *local, K, True, G, None, path="decode", exchange=ex,
+                                      placement=pl)
+                ref = pm.moe_layer(torch.cat(xs), wr, *packed, K, path="decode")
+                torch.cuda.synchronize()
+                ok = ok and torch.equal(out, ref[t0:t0 + tokens[rank]])
+            ex.close()
+            result = {"ok": ok, "err": lib.phmoe_device_error(1)}
         else:  # "timeout": rank 1 never calls the layer, so rank 0's flags never arrive
             ex = ep.PeerExchange(None, max_tokens=8, top_k=K, hidden_size=H, num_experts=E)
             if rank == 0:
@@ -199,6 +219,16 @@ def test_ep_peer_exchange_equals_single_gpu(cuda_device, tmp_path):
     path): three consecutive decode calls with ragged and empty ranks, then a
     prefill call, each equal to the single-GPU layer bit for bit."""
     res = _run_peer("layer", tmp_path)
+    assert all(bool(r[0]) for r in res)
+    assert all(int(r[1]) == 0 for r in res)
+
+
+@pytest.mark.gpu
+def test_ep_peer_exchange_replicated_placement(cuda_device, tmp_path):
+    """Hot experts copied onto other ranks (phmoe_ep_create_ex / _layer_ex):
+    every row goes to the copy its source is assigned, and the output still
+    equals the single-GPU layer bit for bit."""
+    res = _run_peer("replicated", tmp_path)
     assert all(bool(r[0]) for r in res)
     assert all(int(r[1]) == 0 for r in res)
 
