@@ -637,7 +637,7 @@ def run_ep_prefill(args, ws, rank, device):
             "tflops_all_gpus": flops / (ms / 1e3) / 1e12}
 
 
-def run_ep_zipf(args, ws, rank, device):
+def run_ep_zipf(args, ws, rank, device, replicate=True):
     """BASELINE config 5 under expert parallelism: 8192 tokens in total
     (8192 / N per rank), router logits biased by log of a Zipf(1.2) prior over
     the experts (a constant input feature x[:, 0] = 1 meeting router column
@@ -660,8 +660,9 @@ def run_ep_zipf(args, ws, rank, device):
     wr_skew[:, 0] = prior
     x_skew = x.clone()
     x_skew[:, 0] = 1.0
-    cases = {"balanced": (x.to(torch.bfloat16), wr), "zipf": (x_skew.to(torch.bfloat16), wr_skew.to(torch.bfloat16)),
-             "zipf_replicated": None}
+    cases = {"balanced": (x.to(torch.bfloat16), wr), "zipf": (x_skew.to(torch.bfloat16), wr_skew.to(torch.bfloat16))}
+    if replicate:
+        cases["zipf_replicated"] = None
     stream = torch.cuda.current_stream(device)
     res = {}
     for name in cases:
@@ -711,7 +712,9 @@ def run_ep_zipf(args, ws, rank, device):
     for v in res.values():
         del v["expert_rows"]
     res["zipf_over_balanced_time"] = res["zipf"]["ms_per_step"] / res["balanced"]["ms_per_step"]
-    res["zipf_replicated_over_balanced_time"] = res["zipf_replicated"]["ms_per_step"] / res["balanced"]["ms_per_step"]
+    if replicate:
+        res["zipf_replicated_over_balanced_time"] = (res["zipf_replicated"]["ms_per_step"] /
+                                                     res["balanced"]["ms_per_step"])
     del full, shard, pk_full
     torch.cuda.empty_cache()
     return {"workload": f"config 5: 8192 tokens over {ws} GPUs, Zipf(1.2) router prior, top-8 of 128",
@@ -881,7 +884,7 @@ def run_ep(args, ws, rank, device):
     if args.ep_extras:
         del layers
         torch.cuda.empty_cache()
-        extras["config5_zipf"] = run_ep_zipf(args, ws, rank, device)
+        extras["config5_zipf"] = run_ep_zipf(args, ws, rank, device, replicate=args.ep_extras_replicate)
         extras["config3_prefill_ep"] = run_ep_prefill(args, ws, rank, device)
     if rank == 0:
         line.update(extras)
@@ -953,6 +956,8 @@ def main():
                     help="only time a decode step through this many MoE layers (config 4 on one GPU)")
     ap.add_argument("--no-ep-extras", dest="ep_extras", action="store_false",
                     help="N > 1: skip the config-5 (Zipf) and config-3 (expert-parallel prefill) legs")
+    ap.add_argument("--ep-extras-replicate", action="store_true",
+                    help="N > 1: the default line's config-5 leg also times hot-expert replication")
     ap.add_argument("--replica-slots", type=int, default=8,
                     help="N > 1, config 5: extra expert slots per rank for copies of hot experts")
     ap.add_argument("--zipf", action="store_true",
