@@ -425,17 +425,23 @@ def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scale
 
 
 def moe_layer_ep_emulated(xs, router_weight, shards, top_k: int, renormalize: bool = True,
-                          group_size: int = 64, ops=None, path: str = "auto"):
+                          group_size: int = 64, ops=None, path: str = "auto", placement: Placement | None = None):
     """Expert-parallel layer for P ranks emulated in one process (one device):
     ``xs[r]`` are rank r's tokens and ``shards[r]`` its ``(w13_q, w13_scales,
-    w2_q, w2_scales)``. The all-to-alls become concatenations, so the steps
-    and data movement of :func:`moe_layer_ep` can be checked on one GPU.
-    Returns each rank's output."""
+    w2_q, w2_scales)`` (with ``placement``: its slot-stacked local experts).
+    The all-to-alls become concatenations, so the steps and data movement of
+    :func:`moe_layer_ep` can be checked on one GPU. Returns each rank's
+    output."""
     ops = _CUDA_OPS if ops is None else ops
     world = len(xs)
     E = router_weight.shape[0]
-    per = E // world
-    rts = [route_local(x, router_weight, top_k, renormalize, ops) for x in xs]
+    if placement is None:
+        per = E // world
+        rts = [route_local(x, router_weight, top_k, renormalize, ops) for x in xs]
+    else:
+        per = placement.slots_per_rank
+        rts = [route_local(x, router_weight, top_k, renormalize, ops, placement.virtual_map(s), world * per)
+               for s, x in enumerate(xs)]
     counts = [rt.counts.cpu() for rt in rts]
     send_rows = [rows_per_rank(c, world) for c in counts]              # [src][dst]
     packed = [ops.gather(x, rt.row_token) for x, rt in zip(xs, rts)]

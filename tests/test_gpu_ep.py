@@ -66,6 +66,28 @@ def test_ep_emulated_equals_single_gpu(cuda_device, world, tokens):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_emulated_replicated_equals_single_gpu(cuda_device, world):
+    """Hot experts copied onto other ranks (plan_replicas), ranks emulated on
+    one GPU with the CUDA kernels: the same output bit for bit."""
+    dev = cuda_device
+    wr, packed = _layer(63, dev)
+    load = [200.0 / (e + 1) for e in range(E)]  # the low (rank 0) experts hot
+    pl = ep.plan_replicas(load, world, 4)
+    assert pl.slots_per_rank > E // world
+    tokens = [64, 5, 0, 40, 64, 17, 9, 33][:world]
+    g = torch.Generator(device=dev).manual_seed(64 + world)
+    xs = [torch.randn(t, H, device=dev, generator=g).to(torch.bfloat16) for t in tokens]
+    shards = [pl.local_weights(r, *packed) for r in range(world)]
+    outs = ep.moe_layer_ep_emulated(xs, wr, shards, K, True, G, path="decode", placement=pl)
+    ref = pm.moe_layer(torch.cat(xs), wr, *packed, K, path="decode")
+    t0 = 0
+    for r, t in enumerate(tokens):
+        assert torch.equal(outs[r], ref[t0:t0 + t]), r
+        t0 += t
+
+
+@pytest.mark.gpu
 def test_ep_emulated_zipf_skew(cuda_device):
     """BASELINE config 5 shape: 8192 tokens, router logits biased by log of a
     Zipf(1.2) prior (folded into the router weight through a constant input
