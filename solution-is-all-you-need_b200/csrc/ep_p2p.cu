@@ -42,6 +42,7 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "pipeline.cuh"
 #include "launch.h"
 
 namespace phmoe {
@@ -86,11 +87,6 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
-}
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
 }
 // Bounded wait for *flag == epoch; false (and the error bit) on timeout.
 __device__ bool wait_flag(const uint32_t* flag, uint32_t epoch) {
