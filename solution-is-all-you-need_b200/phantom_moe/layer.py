@@ -468,7 +468,10 @@ class MoeLayer:
         """Capture this layer on the fixed buffers ``x`` -> ``out`` into a CUDA
         graph and return a function that replays it on the current stream (one
         launch instead of one per kernel). Refill ``x`` in place between
-        replays; ``x`` and ``out`` must stay allocated while the graph is used."""
+        replays; ``x`` and ``out`` must stay allocated while the graph is used.
+        The capture first runs the layer once on ``x``'s current contents, so
+        ``x`` should hold valid activations (zeros will do), not uninitialised
+        memory."""
         side = torch.cuda.Stream(device=x.device)
         side.wait_stream(torch.cuda.current_stream(x.device))
         with torch.cuda.stream(side):  # warm-up outside the capture (workspace, tensor maps)

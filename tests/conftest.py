@@ -43,3 +43,16 @@ def cuda_device():
     import phantom_moe
     phantom_moe.load_library()  # raises if the library is missing: no silent fallback
     return torch.device("cuda", 0)
+
+
+@pytest.fixture(autouse=True)
+def _clear_device_error(request):
+    """The library's device error word (phmoe_device_error) accumulates until
+    it is read with reset; clear it before each GPU test so a test that checks
+    it sees only what its own calls raised."""
+    if request.node.get_closest_marker("gpu") is not None:
+        import torch
+        if torch.cuda.is_available():
+            import phantom_moe
+            phantom_moe.load_library().phmoe_device_error(1)
+    yield
