@@ -141,6 +141,22 @@ class ClockSampler:
                 "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()), default=None)}
 
 
+def bench_config(ws: int, T: int, args) -> dict:
+    """The workload description both arms print as ``config`` (identical for
+    the same N and flags): what is computed, not what was measured."""
+    cfg = {"workload": f"qwen3-30b-a3b moe layer decode T={T}" + (" per GPU, expert-parallel" if ws > 1 else ""),
+           "hidden": H, "experts": E, "top_k": K_TOP, "intermediate": I, "group_size": G, "tokens_per_gpu": T,
+           "global_batch": ws * T, "parallelism": f"ep{ws}" if ws > 1 else "single-gpu",
+           "l2": f"inputs larger than L2: {args.layers} layers' weights cycled per step",
+           "graph": "CUDA graph per layer" if ws == 1 else "eager layer calls (peer exchange inside)"}
+    if ws > 1:
+        cfg["experts_per_gpu"] = E // ws
+        cfg["exchange"] = ("peer-memory stores over NVLink with epoch flags (phmoe_ep_layer)"
+                           if args.ep_exchange == "peer" else
+                           "NCCL all_to_all_single: counts, bf16 rows out, fp32 rows back")
+    return cfg
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -314,13 +330,19 @@ def cpu_baseline(layers_host_fn, T, budget_s):
                       f"T={T}, {n} forwards in {el:.1f}s, torch threads={threads}, cpu={tf_ref.cpu_model()}"}
 
 
-def host_layer0():
-    """Layer-0 weights (seed 1) on the host, packed by the CUDA quantiser when
-    a GPU is present (identical bytes to the oracle's quantiser)."""
-    if torch.cuda.is_available():
-        wr, pk = make_layer(1, torch.device("cuda", torch.cuda.current_device()))
-        return (wr.float().cpu().numpy(), pk.w13_q.cpu().numpy(), pk.w13_scales.cpu().numpy(),
-                pk.w2_q.cpu().numpy(), pk.w2_scales.cpu().numpy())
+def host_layer0_gpu():
+    """Layer-0 weights (seed 1) packed by this library's CUDA quantiser and
+    copied to the host (our arm's CPU-baseline leg; the bytes equal
+    :func:`host_layer0_cpu`'s, as the GPU parity tests check)."""
+    wr, pk = make_layer(1, torch.device("cuda", torch.cuda.current_device()))
+    return (wr.float().cpu().numpy(), pk.w13_q.cpu().numpy(), pk.w13_scales.cpu().numpy(),
+            pk.w2_q.cpu().numpy(), pk.w2_scales.cpu().numpy())
+
+
+def host_layer0_cpu():
+    """Layer-0 weights (seed 1): the same torch draw as :func:`make_layer`,
+    quantised on the host by the oracle's quantiser. The reference arm uses
+    this so that it never loads this library."""
     from oracle import moe_oracle as O
     g = torch.Generator().manual_seed(1)
     wr = (torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16).float().numpy()
@@ -461,17 +483,14 @@ def run_ours(args):
     hf = run_hf_generate(args, device) if args.hf_generate else None
     cpu = None
     if not args.no_cpu_baseline:
-        cpu = cpu_baseline(host_layer0, T, args.cpu_budget)
+        cpu = cpu_baseline(host_layer0_gpu, T, args.cpu_budget)
     line = {
         "metric": METRIC, "value": res["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights, int4 g64)",
-        "config": {"workload": f"qwen3-30b-a3b moe layer decode T={T}", "hidden": H, "experts": E,
-                   "top_k": K_TOP, "intermediate": I, "group_size": G, "tokens_per_gpu": T,
-                   "global_batch": T, "parallelism": "single-gpu",
-                   "l2": f"inputs larger than L2: {args.layers} layers' weights cycled per step",
-                   "graph": "CUDA graph per layer", "sweep": {str(k): _sweep_entry(v) for k, v in results.items()}},
+        "config": bench_config(1, T, args),
+        "sweep": {str(k): _sweep_entry(v) for k, v in results.items()},
         "roofline": {"kernel": "ffn_gateup", "bound": "hbm", "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": load_traffic(T), "algorithmic_bytes_per_launch": gateup_bytes,
@@ -854,16 +873,9 @@ def run_ep(args, ws, rank, device):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights, int4 g64)",
-            "config": {"workload": f"qwen3-30b-a3b moe layer decode T={T} per GPU, expert-parallel",
-                       "hidden": H, "experts": E, "top_k": K_TOP, "intermediate": I, "group_size": G,
-                       "tokens_per_gpu": T, "global_batch": ws * T, "parallelism": f"ep{ws}",
-                       "experts_per_gpu": E // ws,
-                       "l2": f"inputs larger than L2: {L} layers' weights cycled per step",
-                       "exchange": ("peer-memory stores over NVLink with epoch flags (phmoe_ep_layer)"
-                                    if exchange is not None else
-                                    "NCCL all_to_all_single: counts, bf16 rows out, fp32 rows back"),
-                       "local_experts_hit_mean": g_hit, "recv_rows_max_over_ranks": max(recv_all),
-                       "recv_rows_mean": recv_mean, "stage_us_rank0": stage_us},
+            "config": bench_config(ws, T, args),
+            "ep_stats": {"local_experts_hit_mean": g_hit, "recv_rows_max_over_ranks": max(recv_all),
+                         "recv_rows_mean": recv_mean, "stage_us_rank0": stage_us},
             "roofline": {"kernel": "layer (per GPU)", "bound": "hbm", "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
                          "algorithmic_bytes_per_launch": bytes_gpu},
@@ -898,18 +910,22 @@ def run_ep(args, ws, rank, device):
 # ---------------------------------------------------------------------------
 
 def run_reference(args):
+    """The reference's MoE path (transformers' Qwen3MoeSparseMoeBlock in fp32,
+    the code PHANTOM runs) on the host cores, on the global batch our arm
+    processes at this N. Runs on rank 0 only, never touches a GPU and never
+    imports this library: the weights are drawn and quantised on the host."""
     ws, rank, local = dist_info()
     if rank != 0:
         return
     from oracle import tf_ref
     T = args.tokens
+    Tg = ws * T
     threads = tf_ref.host_threads()
     torch.set_num_threads(threads)
-    if torch.cuda.is_available():
-        torch.cuda.set_device(local)
-    wr, w13_q, w13_s, w2_q, w2_s = host_layer0()
+    wr, w13_q, w13_s, w2_q, w2_s = host_layer0_cpu()
     blk = tf_ref.build_block("qwen3", wr, w13_q, w13_s, w2_q, w2_s, K_TOP, G)
-    x = torch.randn(T, H, generator=torch.Generator().manual_seed(3000 + T)).to(torch.bfloat16).float().numpy()
+    del w13_q, w13_s, w2_q, w2_s
+    x = torch.randn(Tg, H, generator=torch.Generator().manual_seed(3000 + T)).to(torch.bfloat16).float().numpy()
     for _ in range(max(1, args.warmup)):
         tf_ref.forward(blk, x)
     steps = max(1, args.steps)
@@ -917,21 +933,20 @@ def run_reference(args):
     for _ in range(steps):
         tf_ref.forward(blk, x)
     el = time.perf_counter() - t0
-    v = steps * T / el
+    v = steps * Tg / el
     sample = (f"transformers 5.5.0 Qwen3MoeSparseMoeBlock fp32 on the host (the MoE code PHANTOM runs), "
-              f"T={T}, {steps} forwards, torch threads={threads}, cpu={tf_ref.cpu_model()}")
+              f"{Tg} tokens per forward, {steps} forwards, torch threads={threads}, cpu={tf_ref.cpu_model()}")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": ws,
         "steps": steps, "warmup": args.warmup, "ms_per_step": el / steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"qwen3-30b-a3b moe layer decode T={T}", "hidden": H, "experts": E,
-                   "top_k": K_TOP, "intermediate": I, "group_size": G, "tokens_per_gpu": T},
+        "config": bench_config(ws, T, args),
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "reference", "sample": sample},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
-def main():
+def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -964,7 +979,11 @@ def main():
                     help="N > 1: only the config-5 Zipf-skewed routing measurement (8192 tokens in total)")
     ap.add_argument("--hf-layers", type=int, default=4)
     ap.add_argument("--hf-new-tokens", type=int, default=32)
-    args = ap.parse_args()
+    return ap
+
+
+def main():
+    args = build_parser().parse_args()
     if args.warmup < 3:
         args.warmup = 3
     ws, rank, local = dist_info()

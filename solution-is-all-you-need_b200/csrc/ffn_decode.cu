@@ -67,7 +67,11 @@
 
 namespace phmoe {
 
-__device__ int g_ffn_error;  // 0 = ok, 1 = a pipeline wait timed out
+// Error bits raised by the decode FFN kernels (read by phmoe_device_error;
+// every writer ORs its bit in, so several conditions of one call all show):
+//   1  a pipeline wait timed out and its CTA abandoned its work
+//   2  a SwiGLU value was clamped to the fp16 range
+__device__ int g_ffn_error;
 
 namespace {
 
@@ -111,7 +115,7 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volati
     if (global_ns() - t0 > kWaitLimitNs) break;
   }
   *abort_flag = 1;
-  atomicExch(&g_ffn_error, 1);
+  atomicOr(&g_ffn_error, 1);
   return false;
 }
 

@@ -53,7 +53,11 @@
 
 namespace phmoe {
 
-__device__ int g_prefill_error;  // 0 = ok, 1 = a pipeline wait timed out
+// Error bits raised by the prefill kernels (read by phmoe_device_error;
+// every writer ORs its bit in):
+//   1  a pipeline wait timed out and its CTA abandoned its work
+//   2  an activation or SwiGLU value was clamped to the fp16 range
+__device__ int g_prefill_error;
 
 namespace {
 
@@ -180,7 +184,7 @@ __device__ __forceinline__ bool lane_wait(uint32_t bar, uint32_t parity, volatil
     if (global_ns() - t0 > kWaitLimitNs) break;
   }
   *abort_flag = 1;
-  atomicExch(&g_prefill_error, 1);
+  atomicOr(&g_prefill_error, 1);
   return false;
 }
 // Warp form: lane 0 waits, the result is the same for the whole warp.

@@ -13,8 +13,11 @@ from .gguf import GGUFFile, MoeSpec, detect_moe, load_moe_layer
 from .integrate import find_moe_blocks, install_into, uninstall
 from .pipeline import HostPipeline
 from .layer import (
+    DEVICE_ERROR_BITS,
+    DeviceError,
     MoeLayer,
     PackedExperts,
+    check_device_errors,
     check_expert_weights,
     combine,
     dispatch,
@@ -31,12 +34,15 @@ from .layer import (
 )
 
 __all__ = [
+    "DEVICE_ERROR_BITS",
+    "DeviceError",
     "GGUFFile",
     "HostPipeline",
     "MoeLayer",
     "MoeSpec",
     "PhmoeError",
     "PackedExperts",
+    "check_device_errors",
     "check_expert_weights",
     "combine",
     "detect_moe",

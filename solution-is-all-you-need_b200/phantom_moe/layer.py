@@ -88,6 +88,36 @@ class _Workspace:
 WORKSPACE = _Workspace()
 
 
+class DeviceError(RuntimeError):
+    """A kernel of this library raised a bit of the device error word
+    (``phmoe_device_error``). ``bits`` holds the word; see
+    :data:`DEVICE_ERROR_BITS` for the meanings."""
+
+    def __init__(self, bits: int):
+        self.bits = bits
+        names = [txt for b, txt in DEVICE_ERROR_BITS.items() if bits & b] or [f"unknown bits {bits:#x}"]
+        super().__init__("phantom_moe device error: " + "; ".join(names))
+
+
+DEVICE_ERROR_BITS = {
+    1: "an FFN pipeline wait timed out (its CTA abandoned its work; results are incomplete)",
+    2: "a value left the fp16 range of the FFN operands (activations or SwiGLU output) and was clamped",
+    4: "an expert-parallel peer flag did not arrive within 2 s (a peer stopped calling the layer)",
+}
+
+
+def check_device_errors(reset: bool = True) -> None:
+    """Raise :class:`DeviceError` if any kernel of this library raised a bit
+    of the current device's error word since it was last cleared (``reset``
+    clears it). Waits for the device (``cudaMemcpyFromSymbol``): call it
+    between steps, not on a latency-critical path."""
+    bits = _lib.load().phmoe_device_error(int(bool(reset)))
+    if bits < 0:
+        raise RuntimeError("phmoe_device_error: reading the device error word failed")
+    if bits:
+        raise DeviceError(bits)
+
+
 @dataclass
 class PackedExperts:
     """Packed int4 expert weights for one layer.
@@ -368,7 +398,7 @@ class MoeLayer:
                  group_size: int = 64, *, path: str = "auto", num_shared: int = 0,
                  shared_gate_weight: torch.Tensor | None = None, routed_scale: float = 1.0,
                  scoring: str = "softmax", score_bias: torch.Tensor | None = None, n_group: int = 1,
-                 topk_group: int = 1):
+                 topk_group: int = 1, check_errors: bool = False):
         _need_cuda("router_weight", router_weight)
         _need_dtype("router_weight", router_weight, _DT)
         H = router_weight.shape[-1]
@@ -415,6 +445,10 @@ class MoeLayer:
         self._fn = getattr(lib, self._name)
         self._head = head
         self._need: dict[int, int] = {}
+        # check_errors: after every call wait for the device and raise
+        # DeviceError if a kernel raised the device error word (a debugging
+        # aid: it synchronises, and does not work inside stream capture)
+        self.check_errors = bool(check_errors)
 
     def workspace_bytes(self, T: int) -> int:
         n = self._need.get(T)
@@ -459,6 +493,8 @@ class MoeLayer:
                       ws.data_ptr(), ws.numel(), _stream())
         if rc:
             _lib.check(self._name, rc)
+        if self.check_errors:
+            check_device_errors()
         out = out.reshape(shape)
         if return_routing:
             return out, idx, wts
@@ -495,7 +531,7 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
               workspace: torch.Tensor | None = None, num_shared: int = 0,
               shared_gate_weight: torch.Tensor | None = None, routed_scale: float = 1.0,
               scoring: str = "softmax", score_bias: torch.Tensor | None = None, n_group: int = 1,
-              topk_group: int = 1):
+              topk_group: int = 1, check_errors: bool = False):
     """Sparse-MoE layer: router -> dispatch -> grouped int4 SwiGLU FFN -> combine.
 
     ``hidden_states`` is ``[T, H]`` or ``[B, S, H]`` (bf16 or fp32); the result
@@ -519,6 +555,10 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
     ``score_bias [E]`` (``e_score_correction_bias``, used for the choice
     only) and group-limited selection (``n_group`` groups, the
     ``topk_group`` best kept); see ``phmoe_router_ex`` in ``phmoe.h``.
+
+    ``check_errors``: wait for the device after the call and raise
+    :class:`DeviceError` if a kernel raised the device error word (see
+    :func:`check_device_errors`).
     """
     if ep_group is not None:
         from . import ep as _ep
@@ -531,5 +571,6 @@ def moe_layer(hidden_states: torch.Tensor, router_weight: torch.Tensor, w13_q: t
     _need_cuda("hidden_states", hidden_states)
     layer = MoeLayer(router_weight, w13_q, w13_scales, w2_q, w2_scales, top_k, renormalize, group_size, path=path,
                      num_shared=num_shared, shared_gate_weight=shared_gate_weight, routed_scale=routed_scale,
-                     scoring=scoring, score_bias=score_bias, n_group=n_group, topk_group=topk_group)
+                     scoring=scoring, score_bias=score_bias, n_group=n_group, topk_group=topk_group,
+                     check_errors=check_errors)
     return layer(hidden_states, out=out, return_routing=return_routing, workspace=workspace)

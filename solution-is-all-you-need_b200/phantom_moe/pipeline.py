@@ -48,9 +48,10 @@ class HostPipeline:
     ``submit(x_host, out_host, layer=None)`` enqueues one step: layer
     ``layer`` (default: steps cycle through ``layers``) on ``x_host``
     (pinned ``[T, H]``), the result landing in ``out_host`` (pinned
-    ``[T, H]``). It returns the event recorded after the result's copy; the
-    caller may reuse ``x_host`` and read ``out_host`` once that event has
-    completed (or after :meth:`synchronize`).
+    ``[T, H]``). It returns an event of its own for this step, recorded
+    after the result's copy; the caller may reuse ``x_host`` and read
+    ``out_host`` once that event has completed (or after
+    :meth:`synchronize`). The event stays valid however many steps follow.
     """
 
     def __init__(self, layers: Sequence[LayerLike], T: int, H: int, dtype: torch.dtype = torch.bfloat16,
@@ -113,9 +114,11 @@ class HostPipeline:
         with torch.cuda.stream(self.copy_out):
             out_host.copy_(self.out[s], non_blocking=True)
             self.copied[s].record(self.copy_out)
+            done = torch.cuda.Event()
+            done.record(self.copy_out)
         self._used[s] = True
         self._step += 1
-        return self.copied[s]
+        return done
 
     def synchronize(self) -> None:
         for st in (self.copy_in, self.compute, self.copy_out):

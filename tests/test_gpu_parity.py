@@ -67,9 +67,20 @@ def test_router_cfg2_bf16_bitexact(cuda_device, T):
     wr = (torch.randn(128, 2048, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
     idx, probs = _check_router(x, wr, 8)
     # same experts as the plain fp32 semantics wherever the k-th/k+1-th gap is resolvable
-    _, _, i_plain, _ = O.route_reference(bf16_np(x), bf16_np(wr), 8)
-    safe = O.topk_margin(probs, 8) > 1e-5
+    _, p_plain, i_plain, _ = O.route_reference(bf16_np(x), bf16_np(wr), 8)
+    margin = O.topk_margin(probs, 8)
+    safe = margin > 1e-5
     assert np.array_equal(np.sort(idx[safe], 1), np.sort(i_plain[safe], 1))
+    # near ties (k-th and k+1-th probabilities within 1e-5): counted and
+    # reported; the two selections may differ only by experts whose plain
+    # probability lies within that gap of the plain k-th largest
+    near = np.flatnonzero(~safe)
+    print(f"T={T}: {near.size} near-tie tokens excluded of {T}; smallest k/k+1 gap {margin.min():.3e}")
+    assert near.size <= max(1, T // 50), near.size
+    for t in near:
+        kth = np.sort(p_plain[t])[::-1][7]
+        for e in set(idx[t].tolist()) ^ set(i_plain[t].tolist()):
+            assert abs(p_plain[t, e] - kth) <= 1e-5, (t, e)
 
 
 def test_router_cfg1_fp32_matches_transformers(cuda_device):

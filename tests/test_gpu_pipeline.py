@@ -53,6 +53,26 @@ def test_pipeline_reused_host_buffers_and_eager_callables(cuda_device):
         assert torch.equal(oh, layer(x.to(dev)).cpu())
 
 
+def test_pipeline_step_events_stay_valid(cuda_device):
+    """The event submit() returns belongs to its step: waiting on it after
+    later steps have reused the same device slot still means that step's
+    result is on the host."""
+    import phantom_moe as pm
+    dev, T, H, depth = cuda_device, 16, 1024, 2
+    layers = _layers(dev, 1)
+    pipe = pm.HostPipeline(layers, T, H, device=dev, depth=depth)
+    g = torch.Generator().manual_seed(13)
+    steps = 2 * depth + 1
+    xh = [torch.randn(T, H, generator=g).to(torch.bfloat16).pin_memory() for _ in range(steps)]
+    oh = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(steps)]
+    evs = [pipe.submit(xh[i], oh[i]) for i in range(steps)]
+    assert len({id(e) for e in evs}) == steps
+    evs[0].synchronize()
+    assert torch.equal(oh[0], layers[0](xh[0].to(dev)).cpu())
+    pipe.synchronize()
+    assert all(e.query() for e in evs)
+
+
 def test_pipeline_rejects_bad_buffers(cuda_device):
     import phantom_moe as pm
     dev = cuda_device

@@ -25,10 +25,10 @@ def _ptr(t):
 
 
 def _weights(E, H, I, G, seed, dev):
-    g = torch.Generator(device="cpu").manual_seed(seed)
-    wr = (torch.randn(E, H, generator=g) * 0.02).to(dev)
-    w13 = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(dev)
-    w2 = (torch.randn(E, H, I, generator=g) * 0.02).to(dev)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    wr = torch.randn(E, H, generator=g, device=dev) * 0.02
+    w13 = torch.randn(E, 2 * I, H, generator=g, device=dev) * 0.02
+    w2 = torch.randn(E, H, I, generator=g, device=dev) * 0.02
     w13_q, w13_s = phantom_moe.quantize_int4(w13, G)
     w2_q, w2_s = phantom_moe.quantize_int4(w2, G)
     return wr, w13_q, w13_s, w2_q, w2_s
@@ -55,6 +55,37 @@ def test_noalloc_rejects_sizes_beyond_static_scratch():
     assert lib.phmoe_workspace_size(185, H, E, k, I, 0) > STATIC_SCRATCH_BYTES
 
 
+def _run_pair(lib, x, wr, w13_q, w13_s, w2_q, w2_s, k, I, G, stream):
+    """One call through phmoe_moe_layer with a fresh workspace and one through
+    phmoe_moe_layer_noalloc; returns both results (out, idx, wts)."""
+    T, H = x.shape
+    E = wr.shape[0]
+    dev = x.device
+    ws = torch.empty(lib.phmoe_workspace_size(T, H, E, k, I, 0), dtype=torch.uint8, device=dev)
+    assert ws.numel() <= STATIC_SCRATCH_BYTES
+    ref = (torch.empty_like(x), torch.empty(T, k, dtype=torch.int32, device=dev),
+           torch.empty(T, k, dtype=torch.float32, device=dev))
+    _lib.call("phmoe_moe_layer", *_layer_args(x, wr, w13_q, w13_s, w2_q, w2_s, k, I, G, *ref),
+              _ptr(ws), ctypes.c_size_t(ws.numel()), stream)
+    got = (torch.full_like(x, float("nan")), torch.full((T, k), -7, dtype=torch.int32, device=dev),
+           torch.full((T, k), float("nan"), dtype=torch.float32, device=dev))
+    _lib.call("phmoe_moe_layer_noalloc", *_layer_args(x, wr, w13_q, w13_s, w2_q, w2_s, k, I, G, *got), stream)
+    torch.cuda.synchronize(dev)
+    return ref, got
+
+
+def _assert_same(ref, got, what):
+    """Both entries run the same kernels on the same inputs, and the layer is
+    deterministic: every output bit must agree (a scratch-aliasing bug that
+    changes a few rows would show here)."""
+    (ro, ri, rw), (go, gi, gw) = ref, got
+    assert torch.equal(gi, ri), what
+    assert torch.equal(gw, rw), what
+    assert torch.equal(go, ro), (what, int((go != ro).sum()))
+    mx, mr = O.parity_stats(go.float().cpu().numpy(), ro.float().cpu().numpy())
+    assert np.isfinite(mx) and mx <= O.MAX_ABS_TOL and mr <= O.MEAN_REL_TOL, (what, mx, mr)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("T,H,E,k,I,G,dtype", [
     (64, 2048, 128, 8, 768, 64, torch.bfloat16),   # Qwen3-30B-A3B shape, decode
@@ -66,25 +97,27 @@ def test_noalloc_matches_workspace_entry_two_calls(cuda_device, T, H, E, k, I, G
     wr, w13_q, w13_s, w2_q, w2_s = _weights(E, H, I, G, 5, dev)
     wr = wr.to(dtype)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    ws = torch.empty(lib.phmoe_workspace_size(T, H, E, k, I, 0), dtype=torch.uint8, device=dev)
-    assert ws.numel() <= STATIC_SCRATCH_BYTES
     for call in range(2):  # two calls in a row: the second runs over the first's leftovers
         gx = torch.Generator(device="cpu").manual_seed(100 + call)
         x = torch.randn(T, H, generator=gx).to(dtype).to(dev)
-        ref_out = torch.empty_like(x)
-        ref_idx = torch.empty(T, k, dtype=torch.int32, device=dev)
-        ref_w = torch.empty(T, k, dtype=torch.float32, device=dev)
-        _lib.call("phmoe_moe_layer",
-                  *_layer_args(x, wr, w13_q, w13_s, w2_q, w2_s, k, I, G, ref_out, ref_idx, ref_w),
-                  _ptr(ws), ctypes.c_size_t(ws.numel()), stream)
-        out = torch.full_like(x, float("nan"))
-        idx = torch.full((T, k), -7, dtype=torch.int32, device=dev)
-        wts = torch.full((T, k), float("nan"), dtype=torch.float32, device=dev)
-        _lib.call("phmoe_moe_layer_noalloc",
-                  *_layer_args(x, wr, w13_q, w13_s, w2_q, w2_s, k, I, G, out, idx, wts), stream)
-        torch.cuda.synchronize(dev)
-        assert torch.equal(idx, ref_idx)
-        assert torch.equal(wts, ref_w)
-        mx, mr = O.parity_stats(out.float().cpu().numpy(), ref_out.float().cpu().numpy())
-        assert np.isfinite(mx) and mx <= O.MAX_ABS_TOL and mr <= O.MEAN_REL_TOL, (call, mx, mr)
+        _assert_same(*_run_pair(lib, x, wr, w13_q, w13_s, w2_q, w2_s, k, I, G, stream), f"call {call}")
+    assert lib.phmoe_device_error(1) == 0
+
+
+@pytest.mark.gpu
+def test_noalloc_layout_changes_between_calls(cuda_device):
+    """A call that fills the scratch almost to its limit (184 tokens at the
+    Qwen3 shape), then smaller calls with other T, E and k: each sub-buffer
+    moves between calls and sits over the previous call's leftovers, which
+    nothing may depend on."""
+    dev = cuda_device
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    shapes = [(184, 2048, 128, 8, 768, 64, 11), (37, 2048, 64, 6, 768, 64, 12), (5, 1024, 16, 2, 512, 32, 13),
+              (184, 2048, 128, 8, 768, 64, 14)]
+    for n, (T, H, E, k, I, G, seed) in enumerate(shapes):
+        wr, w13_q, w13_s, w2_q, w2_s = _weights(E, H, I, G, seed, dev)
+        wr = wr.to(torch.bfloat16)
+        x = torch.randn(T, H, generator=torch.Generator().manual_seed(200 + n)).to(torch.bfloat16).to(dev)
+        _assert_same(*_run_pair(lib, x, wr, w13_q, w13_s, w2_q, w2_s, k, I, G, stream), (T, E, k))
     assert lib.phmoe_device_error(1) == 0
