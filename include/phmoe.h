@@ -107,15 +107,19 @@ int phmoe_dispatch(const int32_t* topk_idx, int T, int top_k, int E, int32_t* ex
                    size_t scratch_bytes, void* stream);
 
 /*
- * Grouped SwiGLU expert FFN over dispatched rows, decode form: int4 weights
- * are dequantised in registers straight into mma.sync A fragments (weights
- * never pass through shared memory). Replaces Qwen3MoeExperts.forward's
- * per-expert loop body (modeling_qwen3_moe.py:245-247).
+ * Grouped SwiGLU expert FFN over dispatched rows, decode form: exact integer
+ * dot products on the int8 tensor cores. The activations and the SwiGLU
+ * output h are encoded as fixed-point rows (phmoe_fx_rows); the int4
+ * nibbles enter the MMAs as unsigned bytes, the group sums are exact int32,
+ * and the fp16 group scales and fp32 accumulation are applied per group.
+ * Replaces Qwen3MoeExperts.forward's per-expert loop body
+ * (modeling_qwen3_moe.py:245-247).
  *   x        [T, H] x_dtype, gathered through row_token
  *   w13_q    [E, 2I, H/2] uint8 (gate rows 0..I-1, up rows I..2I-1)
  *   w13_s    [E, 2I, H/G] fp16        w2_q [E, H, I/2] uint8   w2_s [E, H, I/G] fp16
- *   h        scratch of T*k*I*4 bytes (bf16 hi and lo planes of the SwiGLU output)
- *   y        [T*k, H] fp32 output (permuted rows)
+ *   h        scratch of T*k*I*4 bytes (fixed-point rows of the SwiGLU output)
+ *   y        [T*k, H] fp32 output (permuted rows); also holds the encoded
+ *            activations until the down projection writes it
  * Limits: G in {32, 64}; H % 256 == 0 (gate/up weight tiles are copied by TMA
  * in 128-byte rows); I % 16 == 0 and I % (2G) == 0; w13_s and w2_s 4-byte
  * aligned; w13_q 16-byte aligned.
@@ -146,6 +150,25 @@ int phmoe_expert_ffn_prefill(const void* x, int x_dtype, const int32_t* row_toke
                              const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q,
                              const uint16_t* w2_s, int T, int H, int E, int top_k, int I,
                              int group_size, float* h, float* y, void* stream);
+
+/*
+ * Fixed-point rows, the operand format of the decode FFN (no counterpart in
+ * the reference, which multiplies in fp32). Each group of G consecutive
+ * elements of a row gets an exponent e (the group's largest |value| scaled
+ * into [4096, 8191] for G = 64, [8192, 16383] for G = 32; |value| below
+ * ~1e34) and integers A = rint(v * 2^-e). Layout of `out`
+ * (phmoe_fx_rows_size bytes, 256-byte aligned):
+ *   q       [rows][K*2 bytes]: per 8-element word 16 bytes, the high bytes
+ *           A >> 8 (signed) then the low bytes A & 255, each in element
+ *           order 0, 4, 1, 5, 2, 6, 3, 7;
+ *   consts  [rows][K/G] int32 pairs {C0, M} at byte offset
+ *           phmoe_fx_rows_size - rows*(K/G)*8: M = bits of the float
+ *           1.5 * 2^(23+e), C0 = M - 8 * sum(A).
+ * Values beyond the range, infinities and NaNs are clamped and raise bit
+ * value 2 of phmoe_device_error.
+ */
+size_t phmoe_fx_rows_size(long long rows, int K, int group_size);
+int phmoe_fx_rows(const void* x, int x_dtype, long long rows, int K, int group_size, void* out, void* stream);
 
 /*
  * Combine: out[t] = sum_j topk_w[t,j] * y[inv[t,j]] in slot order j = 0..k-1
@@ -375,9 +398,11 @@ int phmoe_gguf_q4_k_dequantize(const void* blocks, long long n, float* out, void
 /*
  * Device-side error bits of the current device: 0 when all is well; bit 0
  * (1) when a pipeline wait of an FFN kernel timed out (its CTA abandoned its
- * work after a bounded wait instead of hanging); bit 1 (2) when the prefill
- * path clamped an activation or SwiGLU value to the fp16 range (+-65504);
- * bit 2 (4) when an expert-parallel peer flag did not arrive within 2 s.
+ * work after a bounded wait instead of hanging); bit 1 (2) when an
+ * activation or SwiGLU value could not be held and was clamped (the prefill
+ * path's fp16 operands: beyond +-65504; the decode path's fixed-point rows:
+ * beyond ~1e34, infinite or NaN); bit 2 (4) when an expert-parallel peer
+ * flag did not arrive within 2 s.
  * Synchronous; reset != 0 clears it. Not part of the hot path.
  */
 int phmoe_device_error(int reset);

@@ -370,6 +370,108 @@ def topk_margin(probs: np.ndarray, k: int) -> np.ndarray:
 
 
 # ---------------------------------------------------------------------------
+# fixed-point rows: the operand format of the decode FFN
+# ---------------------------------------------------------------------------
+#
+# The CUDA decode FFN multiplies the int4 nibbles with activations and SwiGLU
+# outputs held as exact integers (build-defined; the reference multiplies in
+# fp32, modeling_qwen3_moe.py:245-247, on weights dequantised as
+# (nibble - 8) * scale, gguf_loader.py:372-378):
+#   per row and group of G elements, e = the exponent that scales the group's
+#   largest |value| m into [2^12, 8191] (G = 64) or [2^13, 16383] (G = 32),
+#   clamped to [-137, 100]; A = rint(v * 2^-e), |A| <= 8191 (16383);
+#   bytes of each 8-element word: the high bytes A >> 8 (two's complement)
+#   then the low bytes A & 255, each in element order 0, 4, 1, 5, 2, 6, 3, 7;
+#   constants {C0, M}: M = the int32 bits of the float 1.5 * 2^(23 + e),
+#   C0 = M - 8 * sum(A).
+# For nibbles n the group sum v = sum((n - 8) * A) is an exact integer with
+# |v| < 2^22, so the int32 M + v, read as a float, minus the float of M is
+# v * 2^e with no rounding (fx_group_dot replays this).
+
+FX_MAGIC = 0x4B400000
+FX_MIN_EXP, FX_MAX_EXP = -137, 100
+_FX_SLOT_ELEM = np.array([0, 4, 1, 5, 2, 6, 3, 7])  # element held by byte slot j of a plane
+
+
+def fx_limits(group: int):
+    """(amax, shift, limit) of the fixed-point groups of size ``group``."""
+    return (8191, 12, 8191.5) if group == 64 else (16383, 13, 16383.5)
+
+
+def fx_exponents(v: np.ndarray, group: int):
+    """Per-group exponents of ``v [..., K]`` (fp32 values) and a flag per
+    group that holds a value it cannot represent (beyond the range, infinite
+    or NaN; the kernels raise device error bit value 2 for it). As in the
+    kernels, the group maximum ignores NaNs (fmaxf) and a maximum above
+    3e38 takes the largest exponent."""
+    _, shift, lim = fx_limits(group)
+    v = np.asarray(v, dtype=F32)
+    vg = np.abs(v.reshape(*v.shape[:-1], v.shape[-1] // group, group).astype(np.float64))
+    big = float(F32(3.0e38))
+    with np.errstate(invalid="ignore"):
+        flag = ~np.all(vg <= big, axis=-1)
+        m = np.where(np.isnan(vg), 0.0, vg).max(axis=-1)
+        top = ~(m <= big)
+        _, p = np.frexp(np.where(top, 1.0, m))  # m = f * 2^p, f in [0.5, 1): floor(log2 m) = p - 1
+    e = (p - 1 - shift).astype(np.int64)
+    e = np.where(m * np.exp2(-e.astype(np.float64)) >= lim, e + 1, e)
+    e = np.where(m == 0, 0, e)
+    e = np.maximum(e, FX_MIN_EXP)
+    over = e > FX_MAX_EXP
+    e = np.where(top | over, FX_MAX_EXP, e)
+    return e, flag | over
+
+
+def fx_encode_rows(v: np.ndarray, group: int):
+    """Fixed-point rows of ``v [rows, K]`` (fp32): returns ``(A int32 [rows,
+    K], e int64 [rows, K/G], q uint8 [rows, 2K], consts int32 [rows, K/G, 2],
+    bad bool [rows, K/G])`` with the byte layout and constants the CUDA
+    encoder writes (``phmoe_fx_rows``)."""
+    amax, _, _ = fx_limits(group)
+    v = np.asarray(v, dtype=F32)
+    rows, K = v.shape
+    e, bad = fx_exponents(v, group)
+    scaled = v.astype(np.float64).reshape(rows, K // group, group) * np.exp2(-e.astype(np.float64))[..., None]
+    with np.errstate(invalid="ignore"):
+        a = np.where(np.isnan(scaled), 0.0, np.clip(np.rint(scaled), -amax, amax))
+    A = a.astype(np.int64).reshape(rows, K)
+    hi = ((A >> 8) & 255).astype(np.uint8).reshape(rows, K // 8, 8)[..., _FX_SLOT_ELEM]
+    lo = (A & 255).astype(np.uint8).reshape(rows, K // 8, 8)[..., _FX_SLOT_ELEM]
+    q = np.concatenate([hi, lo], axis=-1).reshape(rows, 2 * K)
+    M = FX_MAGIC + e * (1 << 23)
+    S = A.reshape(rows, K // group, group).sum(-1)
+    consts = np.stack([M - 8 * S, M], axis=-1).astype(np.int32)
+    return A.astype(np.int32), e, q, consts, bad
+
+
+def fx_decode_q(q: np.ndarray) -> np.ndarray:
+    """The integers A of fixed-point row bytes ``q [rows, 2K]``."""
+    rows, K2 = q.shape
+    w = q.reshape(rows, K2 // 16, 2, 8)
+    hi = w[:, :, 0, :].astype(np.int8).astype(np.int64)
+    lo = w[:, :, 1, :].astype(np.int64)
+    A = np.empty((rows, K2 // 16, 8), dtype=np.int64)
+    A[..., _FX_SLOT_ELEM] = hi * 256 + lo
+    return A.reshape(rows, K2 // 2)
+
+
+def fx_group_dot(nibbles: np.ndarray, A: np.ndarray, consts: np.ndarray) -> np.ndarray:
+    """One group's dot product the way the tensor-core kernels form it:
+    i_lo = C0 + sum(n * lo), i_hi = sum(n * hi) (exact int32), i = 256 * i_hi
+    + i_lo, then float32(bits i) - float32(bits M). ``nibbles [G]`` (0..15),
+    ``A [..., G]``, ``consts [..., 2]``; returns fp32 ``[...]`` equal to
+    sum((n - 8) * A) * 2^e."""
+    n = np.asarray(nibbles, dtype=np.int64)
+    A = np.asarray(A, dtype=np.int64)
+    hi, lo = A >> 8, A & 255
+    i = 256 * (hi * n).sum(-1) + consts[..., 0].astype(np.int64) + (lo * n).sum(-1)
+    assert np.all((i >= 0) & (i < 2 ** 31)), "int32 range"
+    f = i.astype(np.uint32).view(F32)
+    m = consts[..., 1].astype(np.uint32).view(F32)
+    return (f - m).astype(F32)
+
+
+# ---------------------------------------------------------------------------
 # dispatch / FFN / combine
 # ---------------------------------------------------------------------------
 
@@ -513,3 +615,8 @@ def parity_stats(got: np.ndarray, ref: np.ndarray):
 
 MAX_ABS_TOL = 2e-2
 MEAN_REL_TOL = 5e-3
+# Tighter bound the decode path meets on fp32 inputs (below the contract's
+# MEAN_REL_TOL): its fixed-point operands hold every activation and SwiGLU
+# value to 2^-13 of its group's largest |value|, which leaves ~3e-4 mean
+# relative error against an fp32 computation.
+DECODE_FP32_MEAN_REL = 1e-3

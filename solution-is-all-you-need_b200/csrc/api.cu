@@ -281,6 +281,28 @@ int phmoe_expert_ffn_prefill(const void* x, int x_dtype, const int32_t* row_toke
   return check_launch("phmoe_expert_ffn_prefill");
 }
 
+size_t phmoe_fx_rows_size(long long rows, int K, int group_size) {
+  if (rows < 0 || K <= 0 || (group_size != 32 && group_size != 64) || K % group_size) return 0;
+  return fx_rows_bytes(rows, K, group_size);
+}
+
+int phmoe_fx_rows(const void* x, int x_dtype, long long rows, int K, int group_size, void* out, void* stream) {
+  g_last_error.clear();
+  if (!dtype_ok(x_dtype)) return fail(PHMOE_ERR_INVALID_ARG, "bad dtype code");
+  if (group_size != 32 && group_size != 64) return fail(PHMOE_ERR_UNSUPPORTED, "group_size must be 32 or 64");
+  if (rows < 0 || K <= 0 || K % group_size)
+    return fail(PHMOE_ERR_INVALID_ARG, "K must be a positive multiple of group_size (got %d)", K);
+  if (rows == 0) return PHMOE_OK;
+  if (!x || !out) return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned(x, 16) || !aligned(out, 256)) return fail(PHMOE_ERR_ALIGNMENT, "x must be 16- and out 256-byte aligned");
+  uint8_t* q = static_cast<uint8_t*>(out);
+  int2* consts = reinterpret_cast<int2*>(q + (fx_rows_bytes(rows, K, group_size) - (size_t)rows * (K / group_size) * 8));
+  if (int st = launch_fx_rows(x, x_dtype, rows, K, group_size, nullptr, nullptr, q, consts,
+                              static_cast<cudaStream_t>(stream)))
+    return fail(st, "fx row encoding not built for these arguments");
+  return check_launch("phmoe_fx_rows");
+}
+
 int phmoe_combine(const float* y, const int32_t* inv, const float* topk_w, int T, int top_k,
                   int H, void* out, int out_dtype, void* stream) {
   g_last_error.clear();

@@ -148,4 +148,110 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
 
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
 
+// ---------------------------------------------------------------------------
+// Integer tensor-core path of the decode FFN
+// ---------------------------------------------------------------------------
+// D = A * B + C, m16n8k32, A unsigned 8-bit (int4 nibbles 0..15), B signed /
+// unsigned 8-bit, exact int32 accumulation (register operands).
+__device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_u8u8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// One packed word (elements e0..e7, packed layout above) as two registers of
+// unsigned bytes: lo = (e0, e4, e1, e5), hi = (e2, e6, e3, e7). One AND and
+// one shift + AND: the whole int4 -> int8 unpack of 8 weights.
+__device__ __forceinline__ void nib_bytes(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  lo = w & 0x0F0F0F0Fu;
+  hi = (w >> 4) & 0x0F0F0F0Fu;
+}
+
+// Fixed-point rows ("fx rows"): the decode FFN's activations (x) and SwiGLU
+// output (h) as exact integers for the int8 tensor cores.
+//  * Per row and group of G elements: an exponent e with A = rint(v * 2^-e)
+//    and |A| <= kFxAmax(G) (8191 for G = 64, 16383 for G = 32; the largest
+//    element of the group lands in the top two binades, so every element is
+//    held to 2^-13 of the group's maximum or better).
+//  * A = 256 * hi + lo with hi = A >> 8 (signed byte) and lo = A & 255
+//    (unsigned byte). Each 8-element word of a row is 16 bytes: 8 hi bytes
+//    then 8 lo bytes, each in element order (0, 4, 1, 5, 2, 6, 3, 7) - the
+//    order nib_bytes gives the weight bytes, so one 16-byte load per word
+//    yields matching B fragments for the hi and the lo plane.
+//  * Per row and group, two int32 constants {C0, M}: M = the bits of the
+//    float 1.5 * 2^(23 + e) and C0 = M - 8 * sum(A). For int4 nibbles n the
+//    group's dot product sum((n - 8) * A) = v is exact in int32 and, since
+//    |v| < 2^22, the int32 M + v read as a float is 1.5 * 2^(23 + e) + v * 2^e
+//    exactly: float(M + v) - float(M) = v * 2^e with no conversion
+//    instruction (I2F runs on a quarter-rate pipe).
+// The dot product of one group is then: i_lo = C0 + sum(n * lo) and i_hi =
+// sum(n * hi) by the tensor cores, i = 256 * i_hi + i_lo (one IMAD), and
+// __int_as_float(i) - __int_as_float(M) = v * 2^e.
+constexpr int kFxMagic = 0x4B400000;  // float 1.5 * 2^23
+constexpr int kFxMinExp = -137;       // keeps M + v a normal float
+constexpr int kFxMaxExp = 100;        // keeps M + v below 2^31
+template <int G>
+struct FxLimits {
+  static constexpr int kAmax = G == 64 ? 8191 : 16383;  // G * 8 * kAmax < 2^22
+  static constexpr int kShift = G == 64 ? 12 : 13;
+  static constexpr float kLim = G == 64 ? 8191.5f : 16383.5f;
+};
+
+// floor(log2(m)) for a finite m > 0 (normal or subnormal).
+__device__ __forceinline__ int ilog2_f32(float m) {
+  const int b = __float_as_int(m);
+  const int ex = (b >> 23) & 255;
+  return ex ? ex - 127 : -149 + (31 - __clz(b));
+}
+
+// The exponent of a group whose largest |value| is m. `bad` is set when the
+// group cannot be held (m beyond 2^(kFxMaxExp + 13), infinite or NaN): its
+// values are then clamped.
+template <int G>
+__device__ __forceinline__ int fx_exponent(float m, bool& bad) {
+  bad = !(m <= 3.0e38f);  // NaN or infinite
+  if (bad) return kFxMaxExp;
+  if (m == 0.0f) return 0;
+  int e = ilog2_f32(m) - FxLimits<G>::kShift;
+  if (ldexpf(m, -e) >= FxLimits<G>::kLim) ++e;
+  if (e < kFxMinExp) e = kFxMinExp;
+  if (e > kFxMaxExp) {
+    e = kFxMaxExp;
+    bad = true;
+  }
+  return e;
+}
+
+template <int G>
+__device__ __forceinline__ int fx_encode(float v, int e) {
+  int a = __float2int_rn(ldexpf(v, -e));
+  return max(-FxLimits<G>::kAmax, min(FxLimits<G>::kAmax, a));
+}
+
+__device__ __forceinline__ int fx_magic(int e) { return kFxMagic + e * (1 << 23); }
+
+// Byte slot of element p (0..7) inside its word's 8-byte plane.
+__device__ __forceinline__ int fx_slot(int p) { return (p & 3) * 2 + (p >> 2); }
+
+// The 16 bytes of one word from its 8 integers A[0..7].
+__device__ __forceinline__ uint4 fx_word(const int (&a)[8]) {
+  auto hb = [&](int i) { return (uint32_t)((a[i] >> 8) & 255); };
+  auto lb = [&](int i) { return (uint32_t)(a[i] & 255); };
+  uint4 r;
+  r.x = hb(0) | (hb(4) << 8) | (hb(1) << 16) | (hb(5) << 24);
+  r.y = hb(2) | (hb(6) << 8) | (hb(3) << 16) | (hb(7) << 24);
+  r.z = lb(0) | (lb(4) << 8) | (lb(1) << 16) | (lb(5) << 24);
+  r.w = lb(2) | (lb(6) << 8) | (lb(3) << 16) | (lb(7) << 24);
+  return r;
+}
+
 }  // namespace phmoe

@@ -7,57 +7,63 @@
 // on weights dequantised as (nibble - 8) * scale (gguf_loader.py:372-378).
 //
 // At decode sizes the layer streams ~2.5 MB of packed weights per expert hit
-// and does a few FMAs per weight: the bound is HBM. Both kernels are
-// persistent (one CTA per SM, a contiguous range of work items each) and
-// stream "tasks" (a work item's K-chunk) through a ring of shared-memory
-// stages; from shared memory each lane reads the int4 words of its A
-// fragments and turns each 32-bit word (8 consecutive weights) into four
-// bf16x2 pairs with one lop3 each (packed layout in phmoe.h); the pairs feed
-// mma.sync m16n8k16 directly, with the 8 tokens of a pass as the N side.
-// Dequantised weights are never written back to shared memory (bf16 would
-// be 4x the int4 bytes).
+// and does a few multiply-adds per weight: the bound is HBM, and the kernels
+// are built to spend as few instructions per weight byte as possible.
 //
-// gate/up kernel (the larger half of the bytes): warp-specialised.
-//  * item = (expert, 64 gate rows and the 64 matching up rows, pass of 8
-//    tokens); task = one 512-element K chunk of an item (32 KB of weights).
-//    Items are ordered (expert, row block, pass) so extra passes re-read
-//    weights still in L2.
-//  * A producer warp issues, per task, two TMA tensor copies of weights (a
-//    64-row x 2 x 128-byte box of gate rows and one of up rows, 128-byte
-//    swizzled so the fragment reads are nearly conflict free), two TMA copies
-//    of the matching fp16 scale slices, and one bulk copy per activation row;
-//    all complete on the stage's "full" mbarrier.
-//  * Consumer warp w owns 16-row group w%4 and K quarter w/4 of every task,
-//    waits on "full", computes and releases "empty" (one arrival per warp);
-//    its accumulators cover the item's whole K, so the only cross-warp step
-//    is a 4-way sum (fixed order) at the item's end, after which the
-//    quarter-0 warp applies SwiGLU and stores h as bf16 hi/lo planes. The
-//    unpacked weights are 128 + nibble: the +136 offset is removed after the
-//    MMA with one extra MMA per K step against an all-ones A (it yields
-//    sum_k x_k), and the fp16 group scale multiplies the fp32 partial of
-//    each group.
-// down kernel: 16 warps copy each task (128 rows x 512 K) with 16-byte
-//  cp.async into padded rows and compute it between two CTA barriers; warp w
-//  owns rows 16(w%8)..+15 and half of each K-chunk (w/8).
+// Numerics: exact integer dot products on the int8 tensor cores.
+//  * The activations of the rows and the SwiGLU output h are "fx rows"
+//    (common.cuh): per row and group of G elements a power-of-two exponent
+//    and integers |A| <= 8191 (16383 for G = 32) split into a signed high
+//    byte and an unsigned low byte. fx_rows_kernel encodes x; the gate/up
+//    epilogue encodes h.
+//  * A weight word (8 nibbles) becomes two registers of unsigned bytes with
+//    one AND and one shift + AND (nib_bytes); mma.sync m16n8k32 u8 x s8 and
+//    u8 x u8 give the exact int32 sums sum(n * hi) and C0 + sum(n * lo) per
+//    group; one IMAD joins them, and the result read as a float minus the
+//    group's magic constant is sum((n - 8) * A) * 2^e exactly (no int-to-float
+//    conversion). The fp16 weight scale multiplies it and fp32 accumulates
+//    over the groups.
+//  * Every group's dot product is exact: the only roundings are the
+//    encodings of x and h (to 2^-13 of the group's largest |value| or
+//    better) and the fp32 accumulation. The exponent adapts per group, so any
+//    finite value below ~1e34 is held; larger or non-finite values are
+//    clamped and raise bit value 2 of the device error word.
 //
-// Lane c of a quad holds K elements 16c..16c+15 of a 64-group (8c..8c+7 of a
-// 32-group) for A and reads the same activations for B; inside one MMA the K
-// order is a permutation applied to both operands, which a dot product does
-// not see.
+// gate/up kernels (persistent, one CTA per SM, warp-specialised):
+//  * row-block form: item = (expert, 64 gate rows and the 64 matching up rows,
+//    pass of 8 tokens); task = one 512-element K chunk of an item (32 KB of
+//    weights). A producer warp issues per task two TMA tensor copies of
+//    weights (128-byte swizzle), two TMA copies of the fp16 scale slices, one
+//    bulk copy per token of its fx row slice, and 8-byte async copies of the
+//    fx constants (transposed to [group][token] so a lane reads its two
+//    tokens' constants with one 16-byte load); all complete on the stage's
+//    "full" mbarrier. Consumer warp w owns 16-row group w%4 and K quarter w/4
+//    of every task; its accumulators cover the item's whole K, and the item
+//    ends with a 4-way sum in fixed order ((q0 + q1) + q2) + q3.
+//  * multi-token form (from ~20 rows per expert): items of up to 32 tokens
+//    of one expert; each lane unpacks its weight bytes once per group and
+//    feeds up to four 8-token column blocks. Both forms sum in the same
+//    order, so h is bit-identical whichever runs.
+//  * epilogue (the four warps that hold an item's 64 I rows after the K sum):
+//    h = silu(gate) * up in fp32, then the fx encoding of h per (row, group):
+//    the group's |max| and sum of integers are exchanged between the warps
+//    holding the group's rows (mbarriers with bounded waits), the bytes are
+//    staged in shared memory and stored as 16-byte words.
+// down kernel (TMA-fed for I % 256 == 0, else an all-thread cp.async form):
+//  item = (expert, 128 output rows, pass of 8 tokens), 8 row groups x 2 K
+//  halves, the same integer dot products against the fx h rows, fp32 y.
 //
-// Precision: bf16 activations enter the gate/up MMAs exactly; fp32
-// activations are split into bf16 hi + lo parts (two MMAs each, ~16
-// significant bits). The intermediate h goes to the down projection as fp16
-// (11 significant bits; with fp32 activations as fp16 hi + lo, ~22 bits),
-// against weights unpacked exactly to fp16; an |h| above the fp16 range is
-// clamped to 65504 and raises bit 2 of the device error word.
+// Fragment layout of one m16n8k32 step: lane (r, c) holds for weight rows r
+// and r+8 one packed word each (its bytes are K slots 4c..4c+3 and
+// 16+4c..16+4c+3), and the fx word of token r for the same 8 K elements;
+// inside one MMA the K order is a permutation applied to both operands,
+// which a dot product does not see.
 //
 // Every mbarrier wait is bounded: a waiting warp sleeps inside try_wait (a
-// suspend-time hint, woken when the phase completes, so waiting warps take no
-// issue slots from computing ones); after kWaitLimitNs of %globaltimer time
-// (or kSpinLimit tries) it raises the CTA's abort flag and the device error
-// word (phmoe_device_error) and all warps leave; the producer first waits
-// (bounded) for its copies in flight.
+// suspend-time hint, woken when the phase completes); after kWaitLimitNs of
+// %globaltimer time (or kSpinLimit tries) it raises the CTA's abort flag and
+// the device error word (phmoe_device_error) and all warps leave; the
+// producer first waits (bounded) for its copies in flight.
 #include <cuda.h>  // CUtensorMap (types only; the encoder is fetched from the driver at run time)
 #include <string.h>
 
@@ -70,7 +76,8 @@ namespace phmoe {
 // Error bits raised by the decode FFN kernels (read by phmoe_device_error;
 // every writer ORs its bit in, so several conditions of one call all show):
 //   1  a pipeline wait timed out and its CTA abandoned its work
-//   2  a SwiGLU value was clamped to the fp16 range
+//   2  an activation or SwiGLU value was beyond the fixed-point range (about
+//      1e34) or not finite, and was clamped
 __device__ int g_ffn_error;
 
 namespace {
@@ -80,11 +87,14 @@ constexpr int kGuThreads = (kConsumers + 1) * 32;  // + 1 producer warp
 constexpr int kDownThreads = 16 * 32;
 constexpr int kTok = 8;                         // tokens per pass (the MMA N dimension)
 constexpr uint32_t kSpinLimit = 1u << 24;       // try_wait polls before giving up
-constexpr uint32_t kSuspendNs = 20000;            // try_wait suspend-time hint
+constexpr uint32_t kSuspendNs = 20000;          // try_wait suspend-time hint
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ void cp_async4(uint32_t saddr, const void* g) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(saddr), "l"(g) : "memory");
 }
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(g) : "memory");
@@ -124,23 +134,83 @@ __device__ __forceinline__ void warp_arrive(uint32_t bar, int lane) {
   if (lane == 0) mbar_arrive(bar);
 }
 
-// Control block of the row-block gate/up kernel: stage ring plus
-// double-buffered reduction barriers for each of the four row groups.
-template <int S>
-struct RbCtl {
-  uint64_t full[S];
-  uint64_t empty[S];
-  uint64_t red_full[8];   // [buf][rg]: the three kq > 0 warps have written
-  uint64_t red_empty[8];  // [buf][rg]: the kq = 0 warp has read
-  int abort_flag;
-};
-
+// ---------------------------------------------------------------------------
+// fixed-point encoding of activation rows
+// ---------------------------------------------------------------------------
+// One thread per 8-element word, G/8 threads per group. Rows 0..rows-1 of x,
+// or (index != null) rows index[i] for i < *count (the rows a caller wants
+// encoded out of a larger buffer). q [rows][K * 2 bytes], consts [rows][K/G].
+template <typename XT, int G>
+__global__ void __launch_bounds__(256)
+fx_rows_kernel(const XT* __restrict__ x, int K, long long rows, const int32_t* __restrict__ index,
+               const int32_t* __restrict__ count, uint8_t* __restrict__ q, int2* __restrict__ consts) {
+  pdl_begin();
+  constexpr int kTpg = G / 8;
+  const int wpr = K / 8;
+  const long long n = count ? (long long)*count : rows;
+  const long long nw = n * wpr;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long w0 = (long long)blockIdx.x * blockDim.x; w0 < nw; w0 += stride) {
+    const long long w = w0 + threadIdx.x;
+    const bool ok = w < nw;
+    long long row = 0;
+    int wi = 0;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = 0.f;
+    if (ok) {
+      const long long i = w / wpr;
+      wi = (int)(w - i * wpr);
+      row = index ? (long long)__ldg(index + i) : i;
+      const XT* p = x + row * K + (long long)wi * 8;
+      if constexpr (std::is_same<XT, float>::value) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+        v[0] = bf16_lo_to_f32(u.x); v[1] = bf16_hi_to_f32(u.x); v[2] = bf16_lo_to_f32(u.y);
+        v[3] = bf16_hi_to_f32(u.y); v[4] = bf16_lo_to_f32(u.z); v[5] = bf16_hi_to_f32(u.z);
+        v[6] = bf16_lo_to_f32(u.w); v[7] = bf16_hi_to_f32(u.w);
+      }
+    }
+    float m = 0.f;
+    bool nonfinite = false;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float a = fabsf(v[j]);
+      nonfinite |= !(a <= 3.0e38f);
+      m = fmaxf(m, a);
+    }
+#pragma unroll
+    for (int off = 1; off < kTpg; off <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    bool bad;
+    const int e = fx_exponent<G>(m, bad);
+    int a[8];
+    int s = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      a[j] = fx_encode<G>(v[j], e);
+      s += a[j];
+    }
+#pragma unroll
+    for (int off = 1; off < kTpg; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (ok) {
+      *reinterpret_cast<uint4*>(q + ((size_t)row * wpr + wi) * 16) = fx_word(a);
+      if ((threadIdx.x & (kTpg - 1)) == 0) {
+        const int M = fx_magic(e);
+        consts[(size_t)row * (K / G) + wi / kTpg] = make_int2(M - 8 * s, M);
+      }
+      if (bad || nonfinite) atomicOr(&g_ffn_error, 2);
+    }
+  }
+}
 
 // ---------------------------------------------------------------------------
-// fragments
+// fragments and group dot products
 // ---------------------------------------------------------------------------
 
-// A words of one row and one group for this lane (G/32 words).
+// Packed weight words of one row and one group for this lane (G/32 words).
 template <int G>
 struct RowWords {
   uint32_t w[G / 32];
@@ -158,165 +228,72 @@ __device__ __forceinline__ RowWords<G> lds_row(const uint8_t* p) {
   return r;
 }
 
-// B words of one group for this lane: bf16 pairs of its G/4 elements.
+// fx words of one group for this lane (one per m16n8k32 step): .x .y = the
+// high-byte B fragment, .z .w = the low-byte one.
 template <int G>
-struct BWords {
-  uint32_t hi[G / 8];
-  uint32_t lo[G / 8];
+struct FxB {
+  uint4 s[G / 32];
 };
 
 template <int G>
-__device__ __forceinline__ void lds_b_plane(const uint8_t* p, uint32_t (&d)[G / 8]) {
-  const uint4 a = *reinterpret_cast<const uint4*>(p);
-  d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w;
-  if constexpr (G == 64) {
-    const uint4 b = *reinterpret_cast<const uint4*>(p + 16);
-    d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
-  }
+__device__ __forceinline__ FxB<G> lds_fxb(const uint8_t* p) {
+  FxB<G> b;
+#pragma unroll
+  for (int i = 0; i < G / 32; ++i) b.s[i] = reinterpret_cast<const uint4*>(p)[i];
+  return b;
 }
 
-__device__ __forceinline__ void split4(const float4 v, uint32_t& h0, uint32_t& h1, uint32_t& l0,
-                                       uint32_t& l1) {
-  split_bf16x2(v.x, v.y, h0, l0);
-  split_bf16x2(v.z, v.w, h1, l1);
-}
-
+// One group's contribution for weight rows (r, r+8) of one tile and the 8
+// tokens of a pass: acc += s_row * (sum((n - 8) * A) * 2^e). cc: the fx
+// constants {C0, M} of tokens 2c (columns 0, 2) and 2c+1 (columns 1, 3).
 template <int G>
-__device__ __forceinline__ void lds_b_f32(const uint8_t* p, BWords<G>& b) {
+__device__ __forceinline__ void fx_group_tile(const RowWords<G>& w0, const RowWords<G>& w8, const FxB<G>& b,
+                                              const int4& cc, float s0, float s8, float (&acc)[4]) {
+  int lo[4] = {cc.x, cc.z, cc.x, cc.z};
+  int hi[4] = {0, 0, 0, 0};
 #pragma unroll
-  for (int i = 0; i < G / 16; ++i)
-    split4(reinterpret_cast<const float4*>(p)[i], b.hi[2 * i], b.hi[2 * i + 1], b.lo[2 * i], b.lo[2 * i + 1]);
-}
-
-// gate/up partial of one group: acc_g/acc_u += s * (A.B - 136 * sum(B)) for
-// rows (r, r+8) of the gate and up tiles. A is unpacked biased (128 + n).
-template <int G, bool kTwo>
-__device__ __forceinline__ void gateup_group(const RowWords<G>& g0, const RowWords<G>& g8,
-                                             const RowWords<G>& u0, const RowWords<G>& u8,
-                                             const BWords<G>& b, float sg0, float sg8, float su0,
-                                             float su8, float (&acc_g)[4], float (&acc_u)[4]) {
-  float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f}, td[4] = {0.f, 0.f, 0.f, 0.f};
-  const uint32_t ones[4] = {kBf16x2One, kBf16x2One, kBf16x2One, kBf16x2One};
-#pragma unroll
-  for (int w = 0; w < G / 32; ++w) {
-    uint32_t pg0[4], pg8[4], pu0[4], pu8[4];
-    unpack_word_biased(g0.w[w], pg0);
-    unpack_word_biased(g8.w[w], pg8);
-    unpack_word_biased(u0.w[w], pu0);
-    unpack_word_biased(u8.w[w], pu8);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {  // two MMA steps per word
-      const int s = 2 * w + h;
-      const uint32_t ag[4] = {pg0[2 * h], pg8[2 * h], pg0[2 * h + 1], pg8[2 * h + 1]};
-      const uint32_t au[4] = {pu0[2 * h], pu8[2 * h], pu0[2 * h + 1], pu8[2 * h + 1]};
-      mma_bf16_16816(tg, ag, b.hi[2 * s], b.hi[2 * s + 1], tg);
-      mma_bf16_16816(tu, au, b.hi[2 * s], b.hi[2 * s + 1], tu);
-      mma_bf16_16816(td, ones, b.hi[2 * s], b.hi[2 * s + 1], td);
-      if constexpr (kTwo) {
-        mma_bf16_16816(tg, ag, b.lo[2 * s], b.lo[2 * s + 1], tg);
-        mma_bf16_16816(tu, au, b.lo[2 * s], b.lo[2 * s + 1], tu);
-        mma_bf16_16816(td, ones, b.lo[2 * s], b.lo[2 * s + 1], td);
-      }
-    }
+  for (int s = 0; s < G / 32; ++s) {
+    uint32_t a[4];
+    nib_bytes(w0.w[s], a[0], a[2]);
+    nib_bytes(w8.w[s], a[1], a[3]);
+    mma_u8u8_16832(lo, a, b.s[s].z, b.s[s].w);
+    mma_u8s8_16832(hi, a, b.s[s].x, b.s[s].y);
   }
+  const float m0 = __int_as_float(cc.y), m1 = __int_as_float(cc.w);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const float d = -136.0f * td[q];  // td = sum of this group's activations (per token)
-    const float sg = q < 2 ? sg0 : sg8, su = q < 2 ? su0 : su8;
-    acc_g[q] = fmaf(sg, tg[q] + d, acc_g[q]);
-    acc_u[q] = fmaf(su, tu[q] + d, acc_u[q]);
+    const float f = __fsub_rn(__int_as_float(hi[q] * 256 + lo[q]), (q & 1) ? m1 : m0);
+    acc[q] = fmaf(q < 2 ? s0 : s8, f, acc[q]);
   }
 }
 
-// gateup_group for up to NB 8-token column blocks: the A fragments are
-// unpacked once and reused for every block b < nb (B of block b at
-// b_base + b * b_stride).
-template <int G, bool kTwo, int NB>
-__device__ __forceinline__ void gateup_group_mt(const RowWords<G>& g0, const RowWords<G>& g8,
-                                                const RowWords<G>& u0, const RowWords<G>& u8,
-                                                const uint8_t* b_base, int b_stride, int nb, float sg0, float sg8,
-                                                float su0, float su8, float (&acc_g)[NB][4], float (&acc_u)[NB][4]) {
-  uint32_t pg0[G / 32][4], pg8[G / 32][4], pu0[G / 32][4], pu8[G / 32][4];
+// gate and up tiles of one group, sharing the B words and constants.
+template <int G>
+__device__ __forceinline__ void gateup_group_fx(const RowWords<G>& g0, const RowWords<G>& g8,
+                                                const RowWords<G>& u0, const RowWords<G>& u8, const FxB<G>& b,
+                                                const int4& cc, float sg0, float sg8, float su0, float su8,
+                                                float (&acc_g)[4], float (&acc_u)[4]) {
+  int gl[4] = {cc.x, cc.z, cc.x, cc.z}, ul[4] = {cc.x, cc.z, cc.x, cc.z};
+  int gh[4] = {0, 0, 0, 0}, uh[4] = {0, 0, 0, 0};
 #pragma unroll
-  for (int w = 0; w < G / 32; ++w) {
-    unpack_word_biased(g0.w[w], pg0[w]);
-    unpack_word_biased(g8.w[w], pg8[w]);
-    unpack_word_biased(u0.w[w], pu0[w]);
-    unpack_word_biased(u8.w[w], pu8[w]);
+  for (int s = 0; s < G / 32; ++s) {
+    uint32_t ag[4], au[4];
+    nib_bytes(g0.w[s], ag[0], ag[2]);
+    nib_bytes(g8.w[s], ag[1], ag[3]);
+    nib_bytes(u0.w[s], au[0], au[2]);
+    nib_bytes(u8.w[s], au[1], au[3]);
+    mma_u8u8_16832(gl, ag, b.s[s].z, b.s[s].w);
+    mma_u8s8_16832(gh, ag, b.s[s].x, b.s[s].y);
+    mma_u8u8_16832(ul, au, b.s[s].z, b.s[s].w);
+    mma_u8s8_16832(uh, au, b.s[s].x, b.s[s].y);
   }
-  const uint32_t ones[4] = {kBf16x2One, kBf16x2One, kBf16x2One, kBf16x2One};
+  const float m0 = __int_as_float(cc.y), m1 = __int_as_float(cc.w);
 #pragma unroll
-  for (int b = 0; b < NB; ++b) {
-    if (b < nb) {
-      BWords<G> bw;
-      if constexpr (kTwo) lds_b_f32<G>(b_base + b * b_stride, bw);
-      else lds_b_plane<G>(b_base + b * b_stride, bw.hi);
-      float tg[4] = {0.f, 0.f, 0.f, 0.f}, tu[4] = {0.f, 0.f, 0.f, 0.f}, td[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int w = 0; w < G / 32; ++w) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int s = 2 * w + h;
-          const uint32_t ag[4] = {pg0[w][2 * h], pg8[w][2 * h], pg0[w][2 * h + 1], pg8[w][2 * h + 1]};
-          const uint32_t au[4] = {pu0[w][2 * h], pu8[w][2 * h], pu0[w][2 * h + 1], pu8[w][2 * h + 1]};
-          mma_bf16_16816(tg, ag, bw.hi[2 * s], bw.hi[2 * s + 1], tg);
-          mma_bf16_16816(tu, au, bw.hi[2 * s], bw.hi[2 * s + 1], tu);
-          mma_bf16_16816(td, ones, bw.hi[2 * s], bw.hi[2 * s + 1], td);
-          if constexpr (kTwo) {
-            mma_bf16_16816(tg, ag, bw.lo[2 * s], bw.lo[2 * s + 1], tg);
-            mma_bf16_16816(tu, au, bw.lo[2 * s], bw.lo[2 * s + 1], tu);
-            mma_bf16_16816(td, ones, bw.lo[2 * s], bw.lo[2 * s + 1], td);
-          }
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float d = -136.0f * td[q];
-        const float sg = q < 2 ? sg0 : sg8, su = q < 2 ? su0 : su8;
-        acc_g[b][q] = fmaf(sg, tg[q] + d, acc_g[b][q]);
-        acc_u[b][q] = fmaf(su, tu[q] + d, acc_u[b][q]);
-      }
-    }
+  for (int q = 0; q < 4; ++q) {
+    const float m = (q & 1) ? m1 : m0;
+    acc_g[q] = fmaf(q < 2 ? sg0 : sg8, __fsub_rn(__int_as_float(gh[q] * 256 + gl[q]), m), acc_g[q]);
+    acc_u[q] = fmaf(q < 2 ? su0 : su8, __fsub_rn(__int_as_float(uh[q] * 256 + ul[q]), m), acc_u[q]);
   }
-}
-
-// down partial of one group: acc += s * A.(B_hi [+ B_lo]), A unpacked exactly
-// to fp16, B the fp16 h plane(s).
-template <int G, bool kTwo>
-__device__ __forceinline__ void down_group(const RowWords<G>& a0, const RowWords<G>& a8,
-                                           const BWords<G>& b, float s0, float s8, float (&acc)[4]) {
-  float t[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int w = 0; w < G / 32; ++w) {
-    uint32_t p0[4], p8[4];
-    unpack_word_f16(a0.w[w], p0);
-    unpack_word_f16(a8.w[w], p8);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int s = 2 * w + h;
-      const uint32_t a[4] = {p0[2 * h], p8[2 * h], p0[2 * h + 1], p8[2 * h + 1]};
-      mma_f16_16816(t, a, b.hi[2 * s], b.hi[2 * s + 1], t);
-      if constexpr (kTwo) mma_f16_16816(t, a, b.lo[2 * s], b.lo[2 * s + 1], t);
-    }
-  }
-  acc[0] = fmaf(s0, t[0], acc[0]);
-  acc[1] = fmaf(s0, t[1], acc[1]);
-  acc[2] = fmaf(s8, t[2], acc[2]);
-  acc[3] = fmaf(s8, t[3], acc[3]);
-}
-
-// h as the down projection reads it: fp16, clamped to the fp16 range (a
-// clamp raises bit 2 of the device error word); with fp32 activations the
-// rounding remainder goes to a second fp16 plane.
-template <bool kTwo>
-__device__ __forceinline__ void store_h(float hv, __half* __restrict__ h_hi, __half* __restrict__ h_lo, size_t o) {
-  if (fabsf(hv) > 65504.0f) {
-    hv = copysignf(65504.0f, hv);
-    atomicOr(&g_ffn_error, 2);
-  }
-  const __half hb = __float2half_rn(hv);
-  h_hi[o] = hb;
-  if constexpr (kTwo) h_lo[o] = __float2half_rn(hv - __half2float(hb));
 }
 
 // ---------------------------------------------------------------------------
@@ -325,7 +302,7 @@ __device__ __forceinline__ void store_h(float hv, __half* __restrict__ h_hi, __h
 
 // Per active slot s: expert id, first row, row count, and the prefix
 // table[s] of items before slot s (an expert with n rows has
-// tiles * ceil(n / 8) items). Every CTA builds the same copy in shared memory.
+// tiles * ceil(n / TB) items). Every CTA builds the same copy in shared memory.
 struct Meta {
   int* e;
   int* row0;
@@ -412,40 +389,6 @@ __device__ __forceinline__ void cta_range(int total, int& q0, int& q1) {
   q1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
 }
 
-// ---------------------------------------------------------------------------
-// gate/up + SwiGLU, row-block form
-// ---------------------------------------------------------------------------
-// Item = (expert, 64-row block of gate rows and the matching up rows, pass of
-// 8 tokens); task = one 512-element K chunk of the item (32 KB of weights).
-// Consumer warp w owns 16-row group rg = w % 4 and K quarter kq = w / 4 of
-// every task, so its accumulators run over the whole K range of the item and
-// the only cross-warp step is a 4-way sum (fixed order kq 0, 1, 2, 3) at the
-// end of each item, after which the kq = 0 warp applies SwiGLU. Scales arrive
-// with the weights (4-byte async copies) and are read as fp16 pairs.
-constexpr int kRbRows = 64;   // gate rows per item (and as many up rows)
-constexpr int kRbKc = 512;    // K elements per task
-
-template <int G, typename XT>
-struct RbCfg {
-  static constexpr bool kF32 = std::is_same<XT, float>::value;
-  static constexpr int kGpq = 128 / G;                       // groups per consumer warp per task
-  static constexpr int kBlock = 2 * kRbRows * 128;           // one 64-row box of 2 K-chunks (16 KB)
-  static constexpr int kScaleRow = kRbKc / G * 2;            // bytes of scales per row per task
-  static constexpr int kPairs = kRbKc / G / 2;
-  static constexpr int kBRowBytes = kRbKc * (int)sizeof(XT);
-  static constexpr int kBPad = (G == 32 && !kF32) ? 64 : 16;
-  static constexpr int kBStride = kBRowBytes + kBPad;
-  static constexpr int kW = 0;                                // [gate box][up box]
-  static constexpr int kS = 2 * kBlock;                       // [128 rows][kScaleRow]
-  static constexpr int kB = kS + 2 * kRbRows * kScaleRow;     // [8 tokens][kBStride]
-  static constexpr int kStage = (kB + kTok * kBStride + 1023) / 1024 * 1024;
-  static constexpr int kStages = kF32 ? 3 : 4;
-  static constexpr int kRed = 4 * 3 * 32 * 8 * 4;             // [rg][kq-1][lane][8] floats
-  static constexpr size_t smem(int E) {
-    return 1024 + (size_t)kStages * kStage + 2 * kRed + sizeof(RbCtl<kStages>) + (size_t)(4 * E + 4) * 4;
-  }
-};
-
 // Byte offset of (row R of a `rows`-row box of 128-byte K-chunks, byte kb of
 // the task's K slice) as TMA writes it with the 128-byte swizzle.
 __device__ __forceinline__ int swz_off_rows(int R, int kb, int rows) {
@@ -453,31 +396,173 @@ __device__ __forceinline__ int swz_off_rows(int R, int kb, int rows) {
   return ((kb >> 7) * rows + R) * 128 + ((((c0 >> 4) ^ (R & 7)) << 4) | (c0 & 15));
 }
 
-// Byte offset of (row R of a 64-row box, byte kb of the task's K slice).
-__device__ __forceinline__ int swz_off64(int R, int kb) {
-  const int c0 = kb & 127;
-  return ((kb >> 7) * kRbRows + R) * 128 + ((((c0 >> 4) ^ (R & 7)) << 4) | (c0 & 15));
+// ---------------------------------------------------------------------------
+// gate/up epilogue: SwiGLU output -> fx rows
+// ---------------------------------------------------------------------------
+// Run by the four warps (rg = 0..3) that hold an item's 64 I rows after the
+// K sum: lane (r, c) of warp rg holds for token columns tb + 2c + (q & 1) the
+// I rows tile * 64 + rg * 16 + r (+ 8 for q >= 2), i.e. element r of words
+// 2 rg and 2 rg + 1 of the item's 8 words. With G = 64 the item is one group
+// (all four warps), with G = 32 two (warps 0-1 and 2-3). One buffer per item
+// parity holds the exchange of per-warp maxima and integer sums and the byte
+// staging of the item's rows.
+template <int TB>
+struct EpiBuf {
+  float xm[4][TB];
+  int xs[4][TB];
+  uint8_t hs[TB][128];
+};
+
+// Per-warp |max| of token columns tb + 2c, tb + 2c + 1 into xm.
+template <int TB>
+__device__ __forceinline__ void epi_block_max(EpiBuf<TB>* eb, int rg, int lane, int tb, const float (&hv)[4]) {
+  const int r = lane >> 2, c = lane & 3;
+  float m0 = fmaxf(fabsf(hv[0]), fabsf(hv[2])), m1 = fmaxf(fabsf(hv[1]), fabsf(hv[3]));
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, off));
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, off));
+  }
+  if (r == 0) {
+    eb->xm[rg][tb + 2 * c] = m0;
+    eb->xm[rg][tb + 2 * c + 1] = m1;
+  }
 }
 
-template <int G, typename XT>
+// After the max exchange: the group exponents of this lane's two token
+// columns (e[]), the integers of its four values, the per-warp integer sums
+// into xs and the bytes into the staging rows.
+template <int G, int TB>
+__device__ __forceinline__ void epi_block_encode(EpiBuf<TB>* eb, int rg, int lane, int tb, const float (&hv)[4],
+                                                 bool any_valid, int (&e)[2]) {
+  const int r = lane >> 2, c = lane & 3;
+  const int w0 = (G == 64) ? 0 : (rg & 2), nw = (G == 64) ? 4 : 2;  // warps holding this group's rows
+  float M0 = 0.f, M1 = 0.f;
+  for (int w = w0; w < w0 + nw; ++w) {
+    M0 = fmaxf(M0, eb->xm[w][tb + 2 * c]);
+    M1 = fmaxf(M1, eb->xm[w][tb + 2 * c + 1]);
+  }
+  bool bad0, bad1;
+  e[0] = fx_exponent<G>(M0, bad0);
+  e[1] = fx_exponent<G>(M1, bad1);
+  int a[4];
+  a[0] = fx_encode<G>(hv[0], e[0]);
+  a[1] = fx_encode<G>(hv[1], e[1]);
+  a[2] = fx_encode<G>(hv[2], e[0]);
+  a[3] = fx_encode<G>(hv[3], e[1]);
+  int s0 = a[0] + a[2], s1 = a[1] + a[3];
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    s0 += __shfl_xor_sync(0xffffffffu, s0, off);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+  }
+  if (r == 0) {
+    eb->xs[rg][tb + 2 * c] = s0;
+    eb->xs[rg][tb + 2 * c + 1] = s1;
+  }
+  const int slot = fx_slot(r);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint8_t* p = &eb->hs[tb + 2 * c + (q & 1)][(2 * rg + (q >> 1)) * 16 + slot];
+    p[0] = (uint8_t)((a[q] >> 8) & 255);
+    p[8] = (uint8_t)(a[q] & 255);
+  }
+  if ((bad0 || bad1) && any_valid) atomicOr(&g_ffn_error, 2);
+}
+
+// After the sum exchange: the group constants (one writer lane per token
+// column and group) and the 16-byte word stores of the 8 staged rows of
+// block tb. Rows at or beyond n (the expert's row count) are not stored.
+template <int G, int TB>
+__device__ __forceinline__ void epi_block_store(EpiBuf<TB>* eb, int rg, int lane, int tb, const int (&e)[2],
+                                                int tile, int prow0, int n, int row0, int I,
+                                                uint8_t* __restrict__ hq, int2* __restrict__ hc) {
+  const int r = lane >> 2, c = lane & 3;
+  const bool writer = (G == 64) ? rg == 0 : (rg & 1) == 0;
+  if (writer && r == 0) {
+    const int w0 = (G == 64) ? 0 : (rg & 2), nw = (G == 64) ? 4 : 2;
+    const int grp = (G == 64) ? tile : 2 * tile + (rg >> 1);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int t = tb + 2 * c + j;
+      const int rr = prow0 + t;
+      if (rr < n) {
+        int S = 0;
+        for (int w = w0; w < w0 + nw; ++w) S += eb->xs[w][t];
+        const int M = fx_magic(e[j]);
+        hc[(size_t)(row0 + rr) * (I / G) + grp] = make_int2(M - 8 * S, M);
+      }
+    }
+  }
+  const int tid = rg * 32 + lane;  // the four warps store the block's 8 rows x 8 words
+  if (tid < 64) {
+    const int t = tb + (tid >> 3), w = tid & 7;
+    const int rr = prow0 + t;
+    if (rr < n)
+      *reinterpret_cast<uint4*>(hq + (size_t)(row0 + rr) * I * 2 + (size_t)(tile * 8 + w) * 16) =
+          *reinterpret_cast<const uint4*>(&eb->hs[t][w * 16]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// gate/up + SwiGLU, row-block form
+// ---------------------------------------------------------------------------
+constexpr int kRbRows = 64;   // gate rows per item (and as many up rows)
+constexpr int kRbKc = 512;    // K elements per task
+
+template <int S>
+struct RbCtl {
+  uint64_t full[S];
+  uint64_t empty[S];
+  uint64_t red_full[8];   // [buf][rg]: the three kq > 0 warps have written
+  uint64_t red_empty[8];  // [buf][rg]: the kq = 0 warp has read
+  uint64_t epi[4];        // [buf][2]: the epilogue's max and sum exchanges
+  int abort_flag;
+};
+
+template <int G>
+struct RbCfg {
+  static constexpr int kGpq = 128 / G;                       // groups per consumer warp per task
+  static constexpr int kCg = kRbKc / G;                      // groups per task
+  static constexpr int kBlock = 2 * kRbRows * 128;           // one 64-row box of 2 K-chunks (16 KB)
+  static constexpr int kScaleRow = kRbKc / G * 2;            // bytes of scales per row per task
+  static constexpr int kPairs = kRbKc / G / 2;
+  static constexpr int kBStride = kRbKc * 2 + 16;            // fx row slice + pad
+  static constexpr int kW = 0;                                // [gate box][up box]
+  static constexpr int kS = 2 * kBlock;                       // [128 rows][kScaleRow]
+  static constexpr int kB = kS + 2 * kRbRows * kScaleRow;     // [8 tokens][kBStride]
+  static constexpr int kC = kB + kTok * kBStride;             // [kCg groups][8 tokens] int2
+  static constexpr int kStage = (kC + kCg * kTok * 8 + 1023) / 1024 * 1024;
+  static constexpr int kStages = 4;
+  static constexpr int kRed = 4 * 3 * 32 * 8 * 4;             // [rg][kq-1][lane][8] floats
+  static constexpr int kEpi = (int)sizeof(EpiBuf<kTok>);
+  static constexpr size_t smem(int E) {
+    return 1024 + (size_t)kStages * kStage + 2 * kRed + 2 * kEpi + sizeof(RbCtl<kStages>) +
+           (size_t)(4 * E + 4) * 4;
+  }
+};
+
+template <int G>
 __global__ void __launch_bounds__(kGuThreads, 1)
 ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int box_chunks,
-                     const __grid_constant__ CUtensorMap s_map, int s_tma, const XT* __restrict__ x,
-                     const int32_t* __restrict__ row_token, const int32_t* __restrict__ offsets,
-                     const int32_t* __restrict__ active, const uint16_t* __restrict__ w13_s, int H, int I, int E,
-                     __half* __restrict__ h_hi, __half* __restrict__ h_lo) {
+                     const __grid_constant__ CUtensorMap s_map, int s_tma, const uint8_t* __restrict__ xq,
+                     const int2* __restrict__ xc, const int32_t* __restrict__ row_token,
+                     const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
+                     const uint16_t* __restrict__ w13_s, int H, int I, int E, uint8_t* __restrict__ hq,
+                     int2* __restrict__ hc) {
   pdl_begin();
-  using C = RbCfg<G, XT>;
+  using C = RbCfg<G>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [2][rg][kq-1][lane][8]
-  RbCtl<S>* ctl = reinterpret_cast<RbCtl<S>*>(smem + S * C::kStage + 2 * C::kRed);
+  EpiBuf<kTok>* epib = reinterpret_cast<EpiBuf<kTok>*>(smem + S * C::kStage + 2 * C::kRed);
+  RbCtl<S>* ctl = reinterpret_cast<RbCtl<S>*>(smem + S * C::kStage + 2 * C::kRed + 2 * C::kEpi);
   int* mbase = reinterpret_cast<int*>(ctl + 1);
   const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
   volatile int* abort_flag = &ctl->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles = (I + kRbRows - 1) / kRbRows;
+  const int tiles = I / kRbRows;
   const int NG = H / G;
   const int nkc = (H + kRbKc - 1) / kRbKc;
   const int na = active[0];
@@ -491,6 +576,7 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
       mbar_init(smem_u32(&ctl->red_full[i]), 3);
       mbar_init(smem_u32(&ctl->red_empty[i]), 1);
     }
+    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&ctl->epi[i]), 4);
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
@@ -521,7 +607,7 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
       const uint32_t full = smem_u32(&ctl->full[s]);
       uint8_t* st = smem + s * C::kStage;
       if (lane == 0)
-        mbar_arrive_expect_tx(full, 2u * (uint32_t)(box_chunks * kRbRows * 128) + (uint32_t)(nt * kel * (int)sizeof(XT)) +
+        mbar_arrive_expect_tx(full, 2u * (uint32_t)(box_chunks * kRbRows * 128) + (uint32_t)(nt * kel * 2) +
                                         (s_tma ? 2u * kRbRows * C::kScaleRow : 0u));
       __syncwarp();
       const int grow = meta.e[cu.slot] * 2 * I + cu.tile * kRbRows;  // first gate row; up rows are I further
@@ -536,7 +622,15 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
         }
       }
       if (lane < nt)  // lane n < 8 holds the token id of pass row n
-        bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), x + (size_t)tok * H + k0, kel * (int)sizeof(XT), full);
+        bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), xq + (size_t)tok * H * 2 + (size_t)k0 * 2, kel * 2,
+                 full);
+      // fx constants of the task's groups, transposed to [group][token]
+      // (lane L copies for pass row L % 8, whose token id it holds)
+      for (int q = lane; q < C::kCg * kTok; q += 32) {
+        const int tt = q & (kTok - 1), j = q >> 3;
+        if (tt < nt && j * G < kel)
+          cp_async8(smem_u32(st + C::kC + (j * kTok + tt) * 8), xc + (size_t)tok * NG + k0 / G + j);
+      }
       // scales: 64 gate rows then 64 up rows, kel/G groups each: two TMA boxes
       // when the scale rows are 16-byte aligned, else pairs of groups by
       // 4-byte async copies
@@ -546,8 +640,7 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
                       grow + (lane - 2) * I, full);
       } else for (int q = lane; q < 2 * kRbRows * C::kPairs; q += 32) {
         const int rr = q / C::kPairs, pp = q - rr * C::kPairs;
-        const int i = cu.tile * kRbRows + (rr & (kRbRows - 1));
-        if (pp * 2 * G < kel && i < I) {
+        if (pp * 2 * G < kel) {
           const size_t srow = (size_t)grow + (rr >= kRbRows ? I : 0) + (rr & (kRbRows - 1));
           cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + srow * NG + k0 / G + 2 * pp);
         }
@@ -574,9 +667,9 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
   for (int j = 0; j < kGpq; ++j) {
     const int g = kq * kGpq + j;  // group within the task
     const int kb = (G == 64) ? g * 32 + 8 * c : g * 16 + 4 * c;
-    o0[j] = C::kW + swz_off64(R0, kb);
-    o8[j] = C::kW + swz_off64(R0 + 8, kb);
-    ob[j] = C::kB + r * C::kBStride + g * G * (int)sizeof(XT) + (G == 64 ? 16 : 8) * c * (int)sizeof(XT);
+    o0[j] = C::kW + swz_off_rows(R0, kb, kRbRows);
+    o8[j] = C::kW + swz_off_rows(R0 + 8, kb, kRbRows);
+    ob[j] = C::kB + r * C::kBStride + g * G * 2 + (G == 64 ? 32 : 16) * c;
   }
   // scales of this warp's groups for gate rows R0, R0+8 and up rows R0, R0+8
   const int osg0 = C::kS + R0 * C::kScaleRow + kq * kGpq * 2;
@@ -606,21 +699,20 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
     }
 #pragma unroll
     for (int j = 0; j < kGpq; ++j) {
-      if (kq * kGpq + j < ngt) {
+      const int g = kq * kGpq + j;
+      if (g < ngt) {
         const RowWords<G> ag0 = lds_row<G>(st + o0[j]);
         const RowWords<G> ag8 = lds_row<G>(st + o8[j]);
         const RowWords<G> au0 = lds_row<G>(st + o0[j] + C::kBlock);
         const RowWords<G> au8 = lds_row<G>(st + o8[j] + C::kBlock);
-        BWords<G> b;
-        if constexpr (C::kF32) lds_b_f32<G>(st + ob[j], b);
-        else lds_b_plane<G>(st + ob[j], b.hi);
+        const FxB<G> b = lds_fxb<G>(st + ob[j]);
+        const int4 cc = *reinterpret_cast<const int4*>(st + C::kC + (g * kTok + 2 * c) * 8);
         const int p = j >> 1;
         const bool hi = j & 1;
-        gateup_group<G, C::kF32>(ag0, ag8, au0, au8, b,
-                                 hi ? __high2float(sg0[p]) : __low2float(sg0[p]),
-                                 hi ? __high2float(sg8[p]) : __low2float(sg8[p]),
-                                 hi ? __high2float(su0[p]) : __low2float(su0[p]),
-                                 hi ? __high2float(su8[p]) : __low2float(su8[p]), acc_g, acc_u);
+        gateup_group_fx<G>(ag0, ag8, au0, au8, b, cc, hi ? __high2float(sg0[p]) : __low2float(sg0[p]),
+                           hi ? __high2float(sg8[p]) : __low2float(sg8[p]),
+                           hi ? __high2float(su0[p]) : __low2float(su0[p]),
+                           hi ? __high2float(su8[p]) : __low2float(su8[p]), acc_g, acc_u);
       }
     }
     warp_arrive(smem_u32(&ctl->empty[s]), lane);  // this warp is done with the stage
@@ -647,14 +739,24 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
         }
         warp_arrive(smem_u32(&ctl->red_empty[bi]), lane);
         const int n = meta.n[cu.slot], row0 = meta.row0[cu.slot];
+        const int prow0 = cu.pass * kTok;
+        float hv[4];
+        bool any = false;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const int i = cu.tile * kRbRows + R0 + (q >= 2 ? 8 : 0);
-          const int rr = cu.pass * kTok + 2 * c + (q & 1);
-          if (rr < n && i < I) {
-            store_h<C::kF32>(silu_f32(gs[q]) * us[q], h_hi, h_lo, (size_t)(row0 + rr) * I + i);
-          }
+          const bool ok = prow0 + 2 * c + (q & 1) < n;
+          hv[q] = ok ? silu_f32(gs[q]) * us[q] : 0.f;
+          any |= ok;
         }
+        EpiBuf<kTok>* eb = epib + buf;
+        epi_block_max<kTok>(eb, rg, lane, 0, hv);
+        warp_arrive(smem_u32(&ctl->epi[buf * 2]), lane);
+        if (!wait_phase(smem_u32(&ctl->epi[buf * 2]), use & 1, abort_flag)) return;
+        int e[2];
+        epi_block_encode<G, kTok>(eb, rg, lane, 0, hv, any, e);
+        warp_arrive(smem_u32(&ctl->epi[buf * 2 + 1]), lane);
+        if (!wait_phase(smem_u32(&ctl->epi[buf * 2 + 1]), use & 1, abort_flag)) return;
+        epi_block_store<G, kTok>(eb, rg, lane, 0, e, cu.tile, prow0, n, row0, I, hq, hc);
       }
       ++item;
     }
@@ -662,167 +764,16 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
   }
 }
 
-// down projection
 // ---------------------------------------------------------------------------
-template <int G>
-struct DownCfg {
-  static constexpr int kStages = 3;
-  static constexpr int kRows = 128;
-  static constexpr int kKch = 512;
-  static constexpr int kWch = kKch / 32;
-  static constexpr int kPairs = kKch / G / 2;
-  static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);
-  static constexpr int kScaleRow = kKch / G * 2;
-  static constexpr int kBRowBytes = kKch * 2;  // one bf16 plane
-  static constexpr int kBch = kBRowBytes / 16;
-  static constexpr int kBStride = kBRowBytes + (G == 64 ? 16 : 64);
-  static constexpr int kW = 0;
-  static constexpr int kS = kRows * kWStride;
-  static constexpr int kB = kS + kRows * kScaleRow;             // [2 planes][kTok][kBStride]
-  static constexpr int kStage = (kB + 2 * kTok * kBStride + 127) / 128 * 128;
-  static constexpr int kRed = 8 * 4 * 32 * 4;
-};
-
-template <int G, bool kTwo>
-__global__ void __launch_bounds__(kDownThreads, 1)
-ffn_down_kernel(const __half* __restrict__ h_hi, const __half* __restrict__ h_lo,
-                const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
-                const uint8_t* __restrict__ w2_q, const uint16_t* __restrict__ w2_s, int H, int I, int E,
-                float* __restrict__ y) {
-  pdl_begin();
-  using C = DownCfg<G>;
-  constexpr int S = C::kStages;
-  extern __shared__ __align__(128) uint8_t smem[];
-  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [8][4][32]
-  int* mbase = reinterpret_cast<int*>(smem + S * C::kStage + C::kRed);
-  const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = lane >> 2, c = lane & 3;
-  const int rb = warp & 7, kh = warp >> 3;  // row block, K half
-  const int tiles = H / C::kRows;
-  const int NG = I / G;
-  const int nkc = (I + C::kKch - 1) / C::kKch;
-  const size_t row_bytes = (size_t)I / 2;
-  const int na = active[0];
-
-  const int total = build_meta(offsets, active, tiles, meta);
-  int q0, q1;
-  cta_range(total, q0, q1);
-  const int ntask = (q1 - q0) * nkc;
-  if (ntask == 0) return;
-
-  auto issue = [&](const Cursor& cu, int task) {
-    uint8_t* st = smem + (task % S) * C::kStage;
-    const int k0 = cu.kc * C::kKch;
-    const int kel = min(C::kKch, I - k0);
-    const size_t rbase = (size_t)meta.e[cu.slot] * H + (size_t)cu.tile * C::kRows;
-#pragma unroll
-    for (int q = threadIdx.x; q < C::kRows * C::kWch; q += kDownThreads) {
-      const int rr = q / C::kWch, cc = q % C::kWch;
-      if (cc * 32 < kel)
-        cp_async16(smem_u32(st + C::kW + rr * C::kWStride + cc * 16), w2_q + (rbase + rr) * row_bytes + k0 / 2 + cc * 16);
-    }
-#pragma unroll
-    for (int q = threadIdx.x; q < C::kRows * C::kPairs; q += kDownThreads) {
-      const int rr = q / C::kPairs, pp = q % C::kPairs;
-      if (pp * 2 * G < kel)
-        cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
-    }
-    // h rows of the pass (one fp16 plane, two with fp32 activations), this K-chunk
-    const int row_p = meta.row0[cu.slot] + cu.pass * kTok;
-    const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
-#pragma unroll
-    for (int q = threadIdx.x; q < (kTwo ? 2 : 1) * kTok * C::kBch; q += kDownThreads) {
-      const int pl = q / (kTok * C::kBch);
-      const int n = (q / C::kBch) % kTok, cc = q % C::kBch;
-      if (n < nt && cc * 8 < kel) {
-        const __half* src = (pl ? h_lo : h_hi) + (size_t)(row_p + n) * I + k0;
-        cp_async16(smem_u32(st + C::kB + (pl * kTok + n) * C::kBStride + cc * 16),
-                   reinterpret_cast<const uint8_t*>(src) + cc * 16);
-      }
-    }
-  };
-
-  Cursor ci = cursor_at(q0, na, tiles, meta);
-  for (int s = 0; s < S - 1; ++s) {
-    if (s < ntask) issue(ci, s);
-    cp_async_commit();
-    cursor_next(ci, tiles, nkc, meta);
-  }
-  Cursor cm = cursor_at(q0, na, tiles, meta);
-
-  float acc[4];
-  const int lr0 = rb * 16 + r;
-  const int a_off = (G == 64) ? 8 * c : 4 * c;
-  const int b_off = (G == 64 ? 32 : 16) * c;
-  for (int task = 0; task < ntask; ++task) {
-    if (task + S - 1 < ntask) issue(ci, task + S - 1);
-    cp_async_commit();
-    cursor_next(ci, tiles, nkc, meta);
-    if (cm.kc == 0) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) acc[q] = 0.f;
-    }
-    const int ngt = min(C::kKch, I - cm.kc * C::kKch) / G;
-    const int n = meta.n[cm.slot], p0 = cm.pass * kTok;
-    const bool tok_ok = p0 + r < n;  // B rows beyond the pass hold stale data: use zeros
-    cp_async_wait<S - 1>();
-    __syncthreads();
-    const uint8_t* st = smem + (task % S) * C::kStage;
-    const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
-    constexpr int kScH = C::kScaleRow / 2;
-#pragma unroll 2
-    for (int g = kh; g < ngt; g += 2) {
-      const uint8_t* ab = st + C::kW + g * (G / 2) + a_off;
-      const RowWords<G> a0 = lds_row<G>(ab + lr0 * C::kWStride);
-      const RowWords<G> a8 = lds_row<G>(ab + (lr0 + 8) * C::kWStride);
-      BWords<G> b;
-      if (tok_ok) {
-        const uint8_t* bb = st + C::kB + r * C::kBStride + g * G * 2 + b_off;
-        lds_b_plane<G>(bb, b.hi);
-        if constexpr (kTwo) lds_b_plane<G>(bb + kTok * C::kBStride, b.lo);
-      } else {
-#pragma unroll
-        for (int i = 0; i < G / 8; ++i) b.hi[i] = b.lo[i] = 0u;
-      }
-      down_group<G, kTwo>(a0, a8, b, __half2float(sc[lr0 * kScH + g]), __half2float(sc[(lr0 + 8) * kScH + g]), acc);
-    }
-    if (cm.kc == nkc - 1) {
-      if (kh == 1) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) red[(rb * 4 + q) * 32 + lane] = acc[q];
-      }
-      __syncthreads();
-      if (kh == 0) {
-        const int row0 = meta.row0[cm.slot];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float v = acc[q] + red[(rb * 4 + q) * 32 + lane];
-          const int hrow = cm.tile * C::kRows + lr0 + (q >= 2 ? 8 : 0);
-          const int rr = p0 + 2 * c + (q & 1);
-          if (rr < n) y[(size_t)(row0 + rr) * H + hrow] = v;
-        }
-      }
-    }
-    cursor_next(cm, tiles, nkc, meta);
-    __syncthreads();  // stage (task % S) and `red` are free again
-  }
-  cp_async_wait<0>();
-}
-
-// ---------------------------------------------------------------------------
-// gate/up + SwiGLU, multi-token form (batches with >= ~12 rows per expert)
+// gate/up + SwiGLU, multi-token form (batches with ~20 or more rows per expert)
 // ---------------------------------------------------------------------------
 // As the row-block form, but an item covers up to 32 tokens of one expert:
-// each lane unpacks its A fragments once per group and applies them to every
-// 8-token column block of the item (up to four mma.sync per fragment and row
-// pair), so the unpack cost is shared by up to 32 tokens. Item = (expert, 64
-// gate rows + the 64 matching up rows, block of up to 32 tokens); task = one
-// 512-element K chunk. Eight consumer warps = 4 row groups x 2 K halves (288
-// threads leave registers for the accumulators). Each warp keeps one
-// accumulator per 128-element K quarter of the task, and the item's end sum
-// is ((q0 + q1) + q2) + q3 like the row-block form's, so both forms give
-// bit-identical h for every row: which one runs never changes the result.
+// each lane unpacks its weight bytes once per group and applies them to every
+// 8-token column block of the item (up to four sets of m16n8k32 per group),
+// so the unpack cost is shared by up to 32 tokens. Eight consumer warps = 4
+// row groups x 2 K halves. Each warp keeps one accumulator per 128-element K
+// quarter of the task, and the item's end sum is ((q0 + q1) + q2) + q3 like
+// the row-block form's, so both forms give bit-identical h for every row.
 constexpr int kMtConsumers = 8;
 constexpr int kMtThreads = (kMtConsumers + 1) * 32;
 constexpr int kMtRows = 64;
@@ -839,52 +790,58 @@ template <int S>
 struct MtCtl {
   uint64_t full[S];
   uint64_t empty[S];
-  uint64_t red_full[4];   // [rg]: the K-half-1 warp has written its partials
-  uint64_t red_empty[4];  // [rg]: the K-half-0 warp has read them
+  uint64_t red_full[4];   // [rg]: the K-half-0 warp has written its partials
+  uint64_t red_empty[4];  // [rg]: the K-half-1 warp has read them
+  uint64_t epi[4];        // [buf][2]: the epilogue's max and sum exchanges
   int abort_flag;
 };
 
-template <int G, typename XT>
+template <int G>
 struct MtCfg {
-  static constexpr bool kF32 = std::is_same<XT, float>::value;
   static constexpr int kGpq = 128 / G;                        // groups per K quarter per task
+  static constexpr int kCg = kMtKc / G;                       // groups per task
   static constexpr int kBlock = 2 * kMtRows * 128;            // one 64-row box of 2 K-chunks (16 KB)
   static constexpr int kScaleRow = kMtKc / G * 2;
   static constexpr int kPairs = kMtKc / G / 2;
-  static constexpr int kBRowBytes = kMtKc * (int)sizeof(XT);
-  static constexpr int kBPad = (G == 32 && !kF32) ? 64 : 16;
-  static constexpr int kBStride = kBRowBytes + kBPad;
+  static constexpr int kBStride = kMtKc * 2 + 16;
   static constexpr int kW = 0;                                // [gate box][up box]
   static constexpr int kS = 2 * kBlock;                       // [128 rows][kScaleRow]
   static constexpr int kB = kS + 2 * kMtRows * kScaleRow;     // [32 tokens][kBStride]
-  static constexpr int kStage = (kB + kMtTok * kBStride + 1023) / 1024 * 1024;
+  static constexpr int kC = kB + kMtTok * kBStride;           // [kCg groups][32 tokens] int2
+  static constexpr int kStage = (kC + kCg * kMtTok * 8 + 1023) / 1024 * 1024;
   static constexpr int kRed = 4 * 32 * (8 * kMtNb) * 4;       // [rg][lane][nb][8] floats
+  static constexpr int kEpi = (int)sizeof(EpiBuf<kMtTok>);
+  static constexpr size_t fixed_bytes(int S) {
+    return 1024 + (size_t)S * kStage + kRed + 2 * kEpi + sizeof(MtCtl<3>);
+  }
   // three stages where they fit next to the metadata of up to 256 experts
-  static constexpr int kStages = (1024 + 3 * kStage + kRed + 256 + (4 * 256 + 4) * 4 <= 232448) ? 3 : 2;
+  static constexpr int kStages = fixed_bytes(3) + (4 * 256 + 4) * 4 <= 232448 ? 3 : 2;
   static constexpr size_t smem(int E) {
-    return 1024 + (size_t)kStages * kStage + kRed + sizeof(MtCtl<kStages>) + (size_t)(4 * E + 4) * 4;
+    return 1024 + (size_t)kStages * kStage + kRed + 2 * kEpi + sizeof(MtCtl<kStages>) + (size_t)(4 * E + 4) * 4;
   }
 };
 
-template <int G, typename XT>
+template <int G>
 __global__ void __launch_bounds__(kMtThreads, 1)
 ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int box_chunks,
-                     const __grid_constant__ CUtensorMap s_map, int s_tma, const XT* __restrict__ x,
-                     const int32_t* __restrict__ row_token, const int32_t* __restrict__ offsets,
-                     const int32_t* __restrict__ active, const uint16_t* __restrict__ w13_s, int H, int I, int E,
-                     __half* __restrict__ h_hi, __half* __restrict__ h_lo) {
+                     const __grid_constant__ CUtensorMap s_map, int s_tma, const uint8_t* __restrict__ xq,
+                     const int2* __restrict__ xc, const int32_t* __restrict__ row_token,
+                     const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
+                     const uint16_t* __restrict__ w13_s, int H, int I, int E, uint8_t* __restrict__ hq,
+                     int2* __restrict__ hc) {
   pdl_begin();
-  using C = MtCfg<G, XT>;
+  using C = MtCfg<G>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* red = reinterpret_cast<float*>(smem + S * C::kStage);
-  MtCtl<S>* ctl = reinterpret_cast<MtCtl<S>*>(smem + S * C::kStage + C::kRed);
+  EpiBuf<kMtTok>* epib = reinterpret_cast<EpiBuf<kMtTok>*>(smem + S * C::kStage + C::kRed);
+  MtCtl<S>* ctl = reinterpret_cast<MtCtl<S>*>(smem + S * C::kStage + C::kRed + 2 * C::kEpi);
   int* mbase = reinterpret_cast<int*>(ctl + 1);
   const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
   volatile int* abort_flag = &ctl->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles = (I + kMtRows - 1) / kMtRows;
+  const int tiles = I / kMtRows;
   const int NG = H / G;
   const int nkc = (H + kMtKc - 1) / kMtKc;
   const int na = active[0];
@@ -897,6 +854,7 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
     for (int i = 0; i < 4; ++i) {
       mbar_init(smem_u32(&ctl->red_full[i]), 1);
       mbar_init(smem_u32(&ctl->red_empty[i]), 1);
+      mbar_init(smem_u32(&ctl->epi[i]), 4);
     }
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -928,7 +886,7 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
       const uint32_t full = smem_u32(&ctl->full[s]);
       uint8_t* st = smem + s * C::kStage;
       if (lane == 0)
-        mbar_arrive_expect_tx(full, 2u * (uint32_t)(box_chunks * kMtRows * 128) + (uint32_t)(nt * kel * (int)sizeof(XT)) +
+        mbar_arrive_expect_tx(full, 2u * (uint32_t)(box_chunks * kMtRows * 128) + (uint32_t)(nt * kel * 2) +
                                         (s_tma ? 2u * kMtRows * C::kScaleRow : 0u));
       __syncwarp();
       const int grow = meta.e[cu.slot] * 2 * I + cu.tile * kMtRows;  // first gate row; up rows are I further
@@ -942,8 +900,12 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
             tma_load_2d(dst + ch * kMtRows * 128, &w13_map, k0 / 2 + ch * 128, row, full);
         }
       }
-      if (lane < nt)  // lane n < 32 holds the token id of block row n
-        bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), x + (size_t)tok * H + k0, kel * (int)sizeof(XT), full);
+      if (lane < nt) {  // lane n < 32 holds the token id of block row n
+        bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), xq + (size_t)tok * H * 2 + (size_t)k0 * 2, kel * 2,
+                 full);
+        for (int j = 0; j * G < kel; ++j)
+          cp_async8(smem_u32(st + C::kC + (j * kMtTok + lane) * 8), xc + (size_t)tok * NG + k0 / G + j);
+      }
       if (s_tma) {
         if (lane == 2 || lane == 3)
           tma_load_2d(smem_u32(st + C::kS + (lane - 2) * kMtRows * C::kScaleRow), &s_map, k0 / G,
@@ -951,8 +913,7 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
       } else {
         for (int q = lane; q < 2 * kMtRows * C::kPairs; q += 32) {
           const int rr = q / C::kPairs, pp = q - rr * C::kPairs;
-          const int i = cu.tile * kMtRows + (rr & (kMtRows - 1));
-          if (pp * 2 * G < kel && i < I) {
+          if (pp * 2 * G < kel) {
             const size_t srow = (size_t)grow + (rr >= kMtRows ? I : 0) + (rr & (kMtRows - 1));
             cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + srow * NG + k0 / G + 2 * pp);
           }
@@ -1001,17 +962,48 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
         const int g = (2 * kh + h) * kGpq + j;  // group within the task
         if (g < ngt) {
           const int kb = (G == 64) ? g * 32 + 8 * c : g * 16 + 4 * c;
-          const RowWords<G> ag0 = lds_row<G>(st + C::kW + swz_off64(R0, kb));
-          const RowWords<G> ag8 = lds_row<G>(st + C::kW + swz_off64(R0 + 8, kb));
-          const RowWords<G> au0 = lds_row<G>(st + C::kW + C::kBlock + swz_off64(R0, kb));
-          const RowWords<G> au8 = lds_row<G>(st + C::kW + C::kBlock + swz_off64(R0 + 8, kb));
+          const RowWords<G> g0 = lds_row<G>(st + C::kW + swz_off_rows(R0, kb, kMtRows));
+          const RowWords<G> g8 = lds_row<G>(st + C::kW + swz_off_rows(R0 + 8, kb, kMtRows));
+          const RowWords<G> u0 = lds_row<G>(st + C::kW + C::kBlock + swz_off_rows(R0, kb, kMtRows));
+          const RowWords<G> u8 = lds_row<G>(st + C::kW + C::kBlock + swz_off_rows(R0 + 8, kb, kMtRows));
           const float sg0 = __half2float(sc[R0 * kScH + g]), sg8 = __half2float(sc[(R0 + 8) * kScH + g]);
           const float su0 = __half2float(sc[(kMtRows + R0) * kScH + g]);
           const float su8 = __half2float(sc[(kMtRows + R0 + 8) * kScH + g]);
-          const int ob =
-              C::kB + r * C::kBStride + g * G * (int)sizeof(XT) + (G == 64 ? 16 : 8) * c * (int)sizeof(XT);
-          gateup_group_mt<G, C::kF32, kMtNb>(ag0, ag8, au0, au8, st + ob, kTok * C::kBStride, nb, sg0, sg8, su0,
-                                             su8, acc_g[h], acc_u[h]);
+          uint32_t ag[G / 32][4], au[G / 32][4];
+#pragma unroll
+          for (int w = 0; w < G / 32; ++w) {
+            nib_bytes(g0.w[w], ag[w][0], ag[w][2]);
+            nib_bytes(g8.w[w], ag[w][1], ag[w][3]);
+            nib_bytes(u0.w[w], au[w][0], au[w][2]);
+            nib_bytes(u8.w[w], au[w][1], au[w][3]);
+          }
+          const uint8_t* bb = st + C::kB + r * C::kBStride + g * G * 2 + (G == 64 ? 32 : 16) * c;
+          const uint8_t* cb = st + C::kC + (g * kMtTok + 2 * c) * 8;
+#pragma unroll
+          for (int b = 0; b < kMtNb; ++b) {
+            if (b < nb) {
+              const FxB<G> bw = lds_fxb<G>(bb + b * kTok * C::kBStride);
+              const int4 cc = *reinterpret_cast<const int4*>(cb + b * kTok * 8);
+              int gl[4] = {cc.x, cc.z, cc.x, cc.z}, ul[4] = {cc.x, cc.z, cc.x, cc.z};
+              int gh[4] = {0, 0, 0, 0}, uh[4] = {0, 0, 0, 0};
+#pragma unroll
+              for (int w = 0; w < G / 32; ++w) {
+                mma_u8u8_16832(gl, ag[w], bw.s[w].z, bw.s[w].w);
+                mma_u8s8_16832(gh, ag[w], bw.s[w].x, bw.s[w].y);
+                mma_u8u8_16832(ul, au[w], bw.s[w].z, bw.s[w].w);
+                mma_u8s8_16832(uh, au[w], bw.s[w].x, bw.s[w].y);
+              }
+              const float m0 = __int_as_float(cc.y), m1 = __int_as_float(cc.w);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float m = (q & 1) ? m1 : m0;
+                acc_g[h][b][q] = fmaf(q < 2 ? sg0 : sg8, __fsub_rn(__int_as_float(gh[q] * 256 + gl[q]), m),
+                                      acc_g[h][b][q]);
+                acc_u[h][b][q] = fmaf(q < 2 ? su0 : su8, __fsub_rn(__int_as_float(uh[q] * 256 + ul[q]), m),
+                                      acc_u[h][b][q]);
+              }
+            }
+          }
         }
       }
     }
@@ -1030,11 +1022,17 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
           }
         }
         warp_arrive(smem_u32(&ctl->red_full[rg]), lane);
-      } else {  // ((q0 + q1) + q2) + q3, then SwiGLU
+      } else {  // ((q0 + q1) + q2) + q3, then SwiGLU and the fx encoding of h
         if (!wait_phase(smem_u32(&ctl->red_full[rg]), item & 1, abort_flag)) return;
         const int n = meta.n[cu.slot], row0 = meta.row0[cu.slot];
+        const int prow0 = cu.pass * kMtTok;
+        float hv[kMtNb][4];
+        bool any[kMtNb];
 #pragma unroll
         for (int b = 0; b < kMtNb; ++b) {
+          any[b] = false;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) hv[b][q] = 0.f;
           if (b < nb) {
             const float4 og = rb[2 * b], ou = rb[2 * b + 1];
             const float gs[4] = {(og.x + acc_g[0][b][0]) + acc_g[1][b][0], (og.y + acc_g[0][b][1]) + acc_g[1][b][1],
@@ -1043,15 +1041,27 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
                                  (ou.z + acc_u[0][b][2]) + acc_u[1][b][2], (ou.w + acc_u[0][b][3]) + acc_u[1][b][3]};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const int i = cu.tile * kMtRows + R0 + (q >= 2 ? 8 : 0);
-              const int rr = cu.pass * kMtTok + b * kTok + 2 * c + (q & 1);
-              if (rr < n && i < I) {
-                store_h<C::kF32>(silu_f32(gs[q]) * us[q], h_hi, h_lo, (size_t)(row0 + rr) * I + i);
-              }
+              const bool ok = prow0 + b * kTok + 2 * c + (q & 1) < n;
+              hv[b][q] = ok ? silu_f32(gs[q]) * us[q] : 0.f;
+              any[b] |= ok;
             }
           }
         }
         warp_arrive(smem_u32(&ctl->red_empty[rg]), lane);
+        const int buf = item & 1, use = item >> 1;
+        EpiBuf<kMtTok>* eb = epib + buf;
+#pragma unroll
+        for (int b = 0; b < kMtNb; ++b) epi_block_max<kMtTok>(eb, rg, lane, b * kTok, hv[b]);
+        warp_arrive(smem_u32(&ctl->epi[buf * 2]), lane);
+        if (!wait_phase(smem_u32(&ctl->epi[buf * 2]), use & 1, abort_flag)) return;
+        int e[kMtNb][2];
+#pragma unroll
+        for (int b = 0; b < kMtNb; ++b) epi_block_encode<G, kMtTok>(eb, rg, lane, b * kTok, hv[b], any[b], e[b]);
+        warp_arrive(smem_u32(&ctl->epi[buf * 2 + 1]), lane);
+        if (!wait_phase(smem_u32(&ctl->epi[buf * 2 + 1]), use & 1, abort_flag)) return;
+#pragma unroll
+        for (int b = 0; b < kMtNb; ++b)
+          if (b < nb) epi_block_store<G, kMtTok>(eb, rg, lane, b * kTok, e[b], cu.tile, prow0, n, row0, I, hq, hc);
       }
       ++item;
     }
@@ -1066,10 +1076,11 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
 // K chunk. A producer warp copies per task one TMA box of weights (128 rows x
 // 2 x 128 bytes, 128-byte swizzle), the matching scales (a TMA box when the
 // scale rows are 16-byte aligned, else one bulk copy of the block's
-// contiguous scale rows, else 4-byte async copies) and the two h planes of
-// the pass (one TMA box each: 8 groups x 8 rows x 64 elements, 128-byte
-// swizzle). Consumer warp w owns 16-row group w%8 and K half w/8; the two
-// halves are summed (fixed order) at the item's end.
+// contiguous scale rows, else 4-byte async copies), the fx h rows of the
+// pass (one TMA box: 8 blocks of 64 elements x 8 rows, 128-byte swizzle) and
+// their fx constants (8-byte async copies into [group][token]). Consumer
+// warp w owns 16-row group w%8 and K half w/8; the two halves are summed
+// (fixed order) at the item's end.
 constexpr int kDnRows = 128;
 constexpr int kDnKc = 512;
 constexpr int kDnScaleBytes = 4096;  // scale region of a stage
@@ -1086,11 +1097,15 @@ struct DnCtl {
 template <int G>
 struct DnCfg {
   static constexpr int kGph = 256 / G;                 // groups per consumer warp per task
+  static constexpr int kCg = kDnKc / G;                // groups per task
   static constexpr int kW = 0;                         // [2 chunks][128 rows][128 B]
   static constexpr int kS = 2 * kDnRows * 128;         // scales
-  static constexpr int kB = kS + kDnScaleBytes;        // [2 planes][8 groups][8 rows][128 B]
+  static constexpr int kB = kS + kDnScaleBytes;        // [8 blocks of 64][8 rows][128 B]
   static constexpr int kPlane = 8 * kTok * 128;
-  static constexpr int kStage = kB + 2 * kPlane;
+  static constexpr int kC = kB + kPlane;               // [kCg groups][8 tokens] int2
+  // stages start on 1024-byte boundaries: the 128-byte swizzle of the TMA
+  // boxes (weights, h) is a function of the shared-memory address bits 7-9
+  static constexpr int kStage = (kC + kCg * kTok * 8 + 1023) / 1024 * 1024;
   static constexpr int kStages = 4;
   static constexpr int kRed = 8 * 32 * 16;             // [rg][lane][4 floats]
   static constexpr size_t smem(int E) {
@@ -1098,28 +1113,27 @@ struct DnCfg {
   }
 };
 
-// B words of group g (within a task) for token row r from one h plane laid
+// fx words of group g (within a task) for token row r from the h box laid
 // out [64-element block][8 rows][128 B] with 128-byte swizzle.
 template <int G>
-__device__ __forceinline__ void lds_b_swz(const uint8_t* plane, int g, int r, int c, uint32_t (&d)[G / 8]) {
+__device__ __forceinline__ FxB<G> lds_fxb_swz(const uint8_t* plane, int g, int r, int c) {
+  FxB<G> b;
   if constexpr (G == 64) {
     const uint8_t* row = plane + g * (kTok * 128) + r * 128;
-    const uint4 a = *reinterpret_cast<const uint4*>(row + (((2 * c) ^ (r & 7)) << 4));
-    const uint4 b = *reinterpret_cast<const uint4*>(row + (((2 * c + 1) ^ (r & 7)) << 4));
-    d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w;
-    d[4] = b.x; d[5] = b.y; d[6] = b.z; d[7] = b.w;
+    b.s[0] = *reinterpret_cast<const uint4*>(row + (((2 * c) ^ (r & 7)) << 4));
+    b.s[1] = *reinterpret_cast<const uint4*>(row + (((2 * c + 1) ^ (r & 7)) << 4));
   } else {
     const uint8_t* row = plane + (g >> 1) * (kTok * 128) + r * 128;
-    const uint4 a = *reinterpret_cast<const uint4*>(row + ((((g & 1) * 4 + c) ^ (r & 7)) << 4));
-    d[0] = a.x; d[1] = a.y; d[2] = a.z; d[3] = a.w;
+    b.s[0] = *reinterpret_cast<const uint4*>(row + ((((g & 1) * 4 + c) ^ (r & 7)) << 4));
   }
+  return b;
 }
 
-template <int G, bool kTwo>
+template <int G>
 __global__ void __launch_bounds__(kGuThreads, 1)
 ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap s_map,
-                    const __grid_constant__ CUtensorMap hi_map, const __grid_constant__ CUtensorMap lo_map,
-                    int s_mode, const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
+                    const __grid_constant__ CUtensorMap h_map, int s_mode, const int2* __restrict__ hc, int R,
+                    const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
                     const uint16_t* __restrict__ w2_s, int H, int I, int E, float* __restrict__ y) {
   pdl_begin();
   using C = DnCfg<G>;
@@ -1173,12 +1187,10 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
       const int wrow = meta.e[cu.slot] * H + cu.tile * kDnRows;
       const int hrow = meta.row0[cu.slot] + cu.pass * kTok;
       const uint32_t sbytes = s_mode == 0 ? (uint32_t)kDnRows * (kDnKc / G) * 2 : (s_mode == 1 ? sbytes_block : 0u);
-      if (lane == 0)
-        mbar_arrive_expect_tx(full, (uint32_t)(2 * kDnRows * 128) + sbytes + (kTwo ? 2u : 1u) * C::kPlane);
+      if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(2 * kDnRows * 128) + sbytes + (uint32_t)C::kPlane);
       __syncwarp();
       if (lane == 0) tma_load_3d(smem_u32(st + C::kW), &w_map, 0, wrow, k0 / 256, full);
-      if (lane == 1) tma_load_3d(smem_u32(st + C::kB), &hi_map, 0, hrow, k0 / 64, full);
-      if (kTwo && lane == 2) tma_load_3d(smem_u32(st + C::kB + C::kPlane), &lo_map, 0, hrow, k0 / 64, full);
+      if (lane == 1) tma_load_3d(smem_u32(st + C::kB), &h_map, 0, hrow, k0 / 64, full);
       if (s_mode == 0) {
         if (lane == 3) tma_load_2d(smem_u32(st + C::kS), &s_map, k0 / G, wrow, full);
       } else if (s_mode == 1) {
@@ -1190,6 +1202,11 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
           if (pp * 2 * G < kel)
             cp_async4(smem_u32(st + C::kS + rr * srow + pp * 4), w2_s + (size_t)(wrow + rr) * NG + k0 / G + 2 * pp);
         }
+      }
+      for (int q = lane; q < C::kCg * kTok; q += 32) {  // fx constants, transposed to [group][token]
+        const int tt = q & (kTok - 1), j = q >> 3;
+        if (hrow + tt < R && j * G < kel)
+          cp_async8(smem_u32(st + C::kC + (j * kTok + tt) * 8), hc + (size_t)(hrow + tt) * NG + k0 / G + j);
       }
       cp_async_arrive_noinc(full);
       ++issued;
@@ -1228,11 +1245,10 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
         const int kb = g * (G / 2) + a_off;
         const RowWords<G> a0 = lds_row<G>(st + C::kW + swz_off_rows(lr0, kb, kDnRows));
         const RowWords<G> a8 = lds_row<G>(st + C::kW + swz_off_rows(lr0 + 8, kb, kDnRows));
-        BWords<G> b;
-        lds_b_swz<G>(st + C::kB, g, r, c, b.hi);
-        if constexpr (kTwo) lds_b_swz<G>(st + C::kB + C::kPlane, g, r, c, b.lo);
-        down_group<G, kTwo>(a0, a8, b, __half2float(sc[(lr0 * srow) / 2 + goff + g]),
-                      __half2float(sc[((lr0 + 8) * srow) / 2 + goff + g]), acc);
+        const FxB<G> b = lds_fxb_swz<G>(st + C::kB, g, r, c);
+        const int4 cc = *reinterpret_cast<const int4*>(st + C::kC + (g * kTok + 2 * c) * 8);
+        fx_group_tile<G>(a0, a8, b, cc, __half2float(sc[(lr0 * srow) / 2 + goff + g]),
+                         __half2float(sc[((lr0 + 8) * srow) / 2 + goff + g]), acc);
       }
     }
     warp_arrive(smem_u32(&ctl->empty[s]), lane);
@@ -1263,6 +1279,158 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
   }
 }
 
+// ---------------------------------------------------------------------------
+// down projection, all-thread form (I % 256 != 0)
+// ---------------------------------------------------------------------------
+// 16 warps copy each task (128 rows x up to 512 K) with cp.async into padded
+// rows and compute it between two CTA barriers; warp w owns rows 16(w%8)..+15
+// and every other group of the task (w/8).
+template <int G>
+struct DownCfg {
+  static constexpr int kStages = 3;
+  static constexpr int kRows = 128;
+  static constexpr int kKch = 512;
+  static constexpr int kWch = kKch / 32;
+  static constexpr int kPairs = kKch / G / 2;
+  static constexpr int kCg = kKch / G;
+  static constexpr int kWStride = kKch / 2 + (G == 64 ? 32 : 16);
+  static constexpr int kScaleRow = kKch / G * 2;
+  static constexpr int kBRowBytes = kKch * 2;  // fx row slice
+  static constexpr int kBch = kBRowBytes / 16;
+  static constexpr int kBStride = kBRowBytes + 16;
+  static constexpr int kW = 0;
+  static constexpr int kS = kRows * kWStride;
+  static constexpr int kB = kS + kRows * kScaleRow;             // [kTok][kBStride]
+  static constexpr int kC = kB + kTok * kBStride;               // [kCg][kTok] int2
+  static constexpr int kStage = (kC + kCg * kTok * 8 + 127) / 128 * 128;
+  static constexpr int kRed = 8 * 4 * 32 * 4;
+};
+
+template <int G>
+__global__ void __launch_bounds__(kDownThreads, 1)
+ffn_down_kernel(const uint8_t* __restrict__ hq, const int2* __restrict__ hc, const int32_t* __restrict__ offsets,
+                const int32_t* __restrict__ active, const uint8_t* __restrict__ w2_q,
+                const uint16_t* __restrict__ w2_s, int H, int I, int E, float* __restrict__ y) {
+  pdl_begin();
+  using C = DownCfg<G>;
+  constexpr int S = C::kStages;
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [8][4][32]
+  int* mbase = reinterpret_cast<int*>(smem + S * C::kStage + C::kRed);
+  const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, c = lane & 3;
+  const int rb = warp & 7, kh = warp >> 3;  // row block, K half
+  const int tiles = H / C::kRows;
+  const int NG = I / G;
+  const int nkc = (I + C::kKch - 1) / C::kKch;
+  const size_t row_bytes = (size_t)I / 2;
+  const int na = active[0];
+
+  const int total = build_meta(offsets, active, tiles, meta);
+  int q0, q1;
+  cta_range(total, q0, q1);
+  const int ntask = (q1 - q0) * nkc;
+  if (ntask == 0) return;
+
+  auto issue = [&](const Cursor& cu, int task) {
+    uint8_t* st = smem + (task % S) * C::kStage;
+    const int k0 = cu.kc * C::kKch;
+    const int kel = min(C::kKch, I - k0);
+    const size_t rbase = (size_t)meta.e[cu.slot] * H + (size_t)cu.tile * C::kRows;
+#pragma unroll
+    for (int q = threadIdx.x; q < C::kRows * C::kWch; q += kDownThreads) {
+      const int rr = q / C::kWch, cc = q % C::kWch;
+      if (cc * 32 < kel)
+        cp_async16(smem_u32(st + C::kW + rr * C::kWStride + cc * 16), w2_q + (rbase + rr) * row_bytes + k0 / 2 + cc * 16);
+    }
+#pragma unroll
+    for (int q = threadIdx.x; q < C::kRows * C::kPairs; q += kDownThreads) {
+      const int rr = q / C::kPairs, pp = q % C::kPairs;
+      if (pp * 2 * G < kel)
+        cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w2_s + (rbase + rr) * NG + k0 / G + 2 * pp);
+    }
+    // fx h rows of the pass and their constants, this K-chunk
+    const int row_p = meta.row0[cu.slot] + cu.pass * kTok;
+    const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
+#pragma unroll
+    for (int q = threadIdx.x; q < kTok * C::kBch; q += kDownThreads) {
+      const int n = q / C::kBch, cc = q % C::kBch;
+      if (n < nt && cc * 8 < kel)
+        cp_async16(smem_u32(st + C::kB + n * C::kBStride + cc * 16),
+                   hq + (size_t)(row_p + n) * I * 2 + (size_t)k0 * 2 + cc * 16);
+    }
+    for (int q = threadIdx.x; q < C::kCg * kTok; q += kDownThreads) {
+      const int tt = q & (kTok - 1), j = q >> 3;
+      if (tt < nt && j * G < kel)
+        cp_async8(smem_u32(st + C::kC + (j * kTok + tt) * 8), hc + (size_t)(row_p + tt) * NG + k0 / G + j);
+    }
+  };
+
+  Cursor ci = cursor_at(q0, na, tiles, meta);
+  for (int s = 0; s < S - 1; ++s) {
+    if (s < ntask) issue(ci, s);
+    cp_async_commit();
+    cursor_next(ci, tiles, nkc, meta);
+  }
+  Cursor cm = cursor_at(q0, na, tiles, meta);
+
+  float acc[4];
+  const int lr0 = rb * 16 + r;
+  const int a_off = (G == 64) ? 8 * c : 4 * c;
+  const int b_off = (G == 64 ? 32 : 16) * c;
+  for (int task = 0; task < ntask; ++task) {
+    if (task + S - 1 < ntask) issue(ci, task + S - 1);
+    cp_async_commit();
+    cursor_next(ci, tiles, nkc, meta);
+    if (cm.kc == 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] = 0.f;
+    }
+    const int ngt = min(C::kKch, I - cm.kc * C::kKch) / G;
+    const int n = meta.n[cm.slot], p0 = cm.pass * kTok;
+    cp_async_wait<S - 1>();
+    __syncthreads();
+    const uint8_t* st = smem + (task % S) * C::kStage;
+    const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
+    constexpr int kScH = C::kScaleRow / 2;
+#pragma unroll 2
+    for (int g = kh; g < ngt; g += 2) {
+      const uint8_t* ab = st + C::kW + g * (G / 2) + a_off;
+      const RowWords<G> a0 = lds_row<G>(ab + lr0 * C::kWStride);
+      const RowWords<G> a8 = lds_row<G>(ab + (lr0 + 8) * C::kWStride);
+      const FxB<G> b = lds_fxb<G>(st + C::kB + r * C::kBStride + g * G * 2 + b_off);
+      const int4 cc = *reinterpret_cast<const int4*>(st + C::kC + (g * kTok + 2 * c) * 8);
+      fx_group_tile<G>(a0, a8, b, cc, __half2float(sc[lr0 * kScH + g]), __half2float(sc[(lr0 + 8) * kScH + g]),
+                       acc);
+    }
+    if (cm.kc == nkc - 1) {
+      if (kh == 1) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) red[(rb * 4 + q) * 32 + lane] = acc[q];
+      }
+      __syncthreads();
+      if (kh == 0) {
+        const int row0 = meta.row0[cm.slot];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float v = acc[q] + red[(rb * 4 + q) * 32 + lane];
+          const int hrow = cm.tile * C::kRows + lr0 + (q >= 2 ? 8 : 0);
+          const int rr = p0 + 2 * c + (q & 1);
+          if (rr < n) y[(size_t)(row0 + rr) * H + hrow] = v;
+        }
+      }
+    }
+    cursor_next(cm, tiles, nkc, meta);
+    __syncthreads();  // stage (task % S) and `red` are free again
+  }
+  cp_async_wait<0>();
+}
+
+// ---------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------
+
 template <typename K>
 void set_smem(K kern, size_t bytes) {
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
@@ -1284,12 +1452,12 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Tensor map over w13_q viewed as [rows = E*2I][K bytes = H/2], for 16-row
-// boxes of `box_chunks` 128-byte K-chunks with 128-byte swizzle. First choice:
-// a 3-D view (128 B, rows, K-chunks) so one copy moves the whole box; if the
-// driver rejects it, a 2-D view copied one 128-byte chunk at a time (same
-// shared-memory layout). Returns 0 (2-D), 1 (3-D) or -1 (no map).
-int make_w13_map(CUtensorMap* map, const uint8_t* w13_q, long long rows, int H, int box_chunks, int box_rows = 16) {
+// Tensor map over w13_q viewed as [rows = E*2I][K bytes = H/2], for boxes of
+// `box_rows` rows x `box_chunks` 128-byte K-chunks with 128-byte swizzle.
+// First choice: a 3-D view (128 B, rows, K-chunks) so one copy moves the
+// whole box; if the driver rejects it, a 2-D view copied one 128-byte chunk
+// at a time (same shared-memory layout). Returns 0 (2-D), 1 (3-D) or -1.
+int make_w13_map(CUtensorMap* map, const uint8_t* w13_q, long long rows, int H, int box_chunks, int box_rows) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return -1;
   {
@@ -1315,8 +1483,8 @@ int make_w13_map(CUtensorMap* map, const uint8_t* w13_q, long long rows, int H, 
 
 constexpr size_t kMaxSmem = 227 * 1024;
 
-// Tensor map over the fp16 scales [E*2I rows][H/G] for boxes of one task's
-// groups x `rows` rows; false when the rows are not 16-byte aligned.
+// Tensor map over the fp16 scales [rows][H/G] for boxes of one task's
+// groups x `box_rows` rows; false when the rows are not 16-byte aligned.
 bool make_scale_map(CUtensorMap* map, const uint16_t* w13_s, long long rows, int H, int G, int kc, int box_rows) {
   if (((H / G) * 2) % 16) return false;
   EncodeTiledFn enc = encode_fn();
@@ -1330,83 +1498,46 @@ bool make_scale_map(CUtensorMap* map, const uint16_t* w13_s, long long rows, int
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int G, typename XT>
-int launch_gateup_mt(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
-                     const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __half* h_hi,
-                     __half* h_lo, int grid, cudaStream_t st) {
-  const size_t smem = MtCfg<G, XT>::smem(E);
-  if (smem > kMaxSmem) return PHMOE_ERR_UNSUPPORTED;
-  const int box_chunks = std::min(H, kMtKc) / 256;
-  alignas(64) CUtensorMap map, smap;
-  const int mode = make_w13_map(&map, w13_q, (long long)E * 2 * I, H, box_chunks, kMtRows);
-  if (mode < 0) return PHMOE_ERR_CUDA;
-  const int s_tma = make_scale_map(&smap, w13_s, (long long)E * 2 * I, H, G, kMtKc, kMtRows) ? 1 : 0;
-  if (!s_tma) memset(&smap, 0, sizeof(smap));
-  auto k = ffn_gateup_mt_kernel<G, XT>;
-  set_smem(k, smem);
-  launch_pdl(k, dim3(grid), dim3(kMtThreads), smem, st, map, mode, box_chunks, smap, s_tma, static_cast<const XT*>(x), row_token, offsets,
-                                    active, w13_s, H, I, E, h_hi, h_lo);
-  return PHMOE_OK;
-}
-
-template <int G, typename XT>
-int launch_gateup_rb(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
-                     const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E, __half* h_hi,
-                     __half* h_lo, int grid, cudaStream_t st) {
-  const int box_chunks = std::min(H, kRbKc) / 256;
-  alignas(64) CUtensorMap map, smap;
-  const int mode = make_w13_map(&map, w13_q, (long long)E * 2 * I, H, box_chunks, kRbRows);
-  if (mode < 0) return PHMOE_ERR_CUDA;
-  // scales as a 2-D fp16 tensor [E*2I rows][H/G]: boxes of one task's groups x 64 rows
-  int s_tma = 0;
-  if (((H / G) * 2) % 16 == 0) {
-    EncodeTiledFn enc = encode_fn();
-    const cuuint64_t dims[2] = {(cuuint64_t)(H / G), (cuuint64_t)E * 2 * I};
-    const cuuint64_t strides[1] = {(cuuint64_t)(H / G) * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)(kRbKc / G), (cuuint32_t)kRbRows};
-    const cuuint32_t estr[2] = {1, 1};
-    s_tma = enc && enc(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(w13_s), dims, strides, box,
-                       estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-  }
-  if (!s_tma) memset(&smap, 0, sizeof(smap));
-  const size_t smem = RbCfg<G, XT>::smem(E);
-  if (smem > kMaxSmem) return PHMOE_ERR_UNSUPPORTED;
-  auto k = ffn_gateup_rb_kernel<G, XT>;
-  set_smem(k, smem);
-  launch_pdl(k, dim3(grid), dim3(kGuThreads), smem, st, map, mode, box_chunks, smap, s_tma, static_cast<const XT*>(x), row_token,
-                                    offsets, active, w13_s, H, I, E, h_hi, h_lo);
-  return PHMOE_OK;
-}
-
 template <int G>
-size_t down_smem(int E) {
-  using C = DownCfg<G>;
-  return (size_t)C::kStages * C::kStage + C::kRed + (size_t)(4 * E + 4) * 4;
-}
-
-template <int G, bool kTwo>
-void launch_down(const __half* h_hi, const __half* h_lo, const int32_t* offsets,
-                 const int32_t* active, const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, float* y,
-                 int grid, cudaStream_t st) {
-  const size_t smem = down_smem<G>(E);
-  auto k = ffn_down_kernel<G, kTwo>;
-  set_smem(k, smem);
-  launch_pdl(k, dim3(grid), dim3(kDownThreads), smem, st, h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y);
+int launch_gateup(bool mt, const uint8_t* xq, const int2* xc, const int32_t* row_token, const int32_t* offsets,
+                  const int32_t* active, const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E,
+                  uint8_t* hq, int2* hc, int grid, cudaStream_t st) {
+  const int rows = mt ? kMtRows : kRbRows;
+  const int kc = mt ? kMtKc : kRbKc;
+  const size_t smem = mt ? MtCfg<G>::smem(E) : RbCfg<G>::smem(E);
+  if (smem > kMaxSmem) return PHMOE_ERR_UNSUPPORTED;
+  const int box_chunks = std::min(H, kc) / 256;
+  alignas(64) CUtensorMap map, smap;
+  const int mode = make_w13_map(&map, w13_q, (long long)E * 2 * I, H, box_chunks, rows);
+  if (mode < 0) return PHMOE_ERR_CUDA;
+  const int s_tma = make_scale_map(&smap, w13_s, (long long)E * 2 * I, H, G, kc, rows) ? 1 : 0;
+  if (!s_tma) memset(&smap, 0, sizeof(smap));
+  if (mt) {
+    auto k = ffn_gateup_mt_kernel<G>;
+    set_smem(k, smem);
+    launch_pdl(k, dim3(grid), dim3(kMtThreads), smem, st, map, mode, box_chunks, smap, s_tma, xq, xc, row_token,
+               offsets, active, w13_s, H, I, E, hq, hc);
+  } else {
+    auto k = ffn_gateup_rb_kernel<G>;
+    set_smem(k, smem);
+    launch_pdl(k, dim3(grid), dim3(kGuThreads), smem, st, map, mode, box_chunks, smap, s_tma, xq, xc, row_token,
+               offsets, active, w13_s, H, I, E, hq, hc);
+  }
+  return PHMOE_OK;
 }
 
 // TMA-fed down projection; returns false (nothing launched) when the shape
 // or the tensor maps do not allow it.
-template <int G, bool kTwo>
-bool launch_down_tma(const __half* h_hi, const __half* h_lo, long long R, const int32_t* offsets,
-                     const int32_t* active, const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, float* y,
-                     int grid, cudaStream_t st) {
-  if (I % 256 || H % kDnRows || R <= 0) return false;
+template <int G>
+bool launch_down_tma(const uint8_t* hq, const int2* hc, long long R, const int32_t* offsets, const int32_t* active,
+                     const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, float* y, int grid,
+                     cudaStream_t st) {
+  if (I % 256 || H % kDnRows || R <= 0 || R > (1LL << 30)) return false;
   const size_t smem = DnCfg<G>::smem(E);
   if (smem > kMaxSmem) return false;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
-  alignas(64) CUtensorMap wm, sm, hm, lm;
+  alignas(64) CUtensorMap wm, sm, hm;
   const cuuint32_t e3[3] = {1, 1, 1}, e2[2] = {1, 1};
   {
     const cuuint64_t dims[3] = {128, (cuuint64_t)E * H, (cuuint64_t)(I / 256)};
@@ -1417,13 +1548,11 @@ bool launch_down_tma(const __half* h_hi, const __half* h_lo, long long R, const 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return false;
   }
-  const __half* planes[2] = {h_hi, h_lo};
-  CUtensorMap* pm[2] = {&hm, &lm};
-  for (int p = 0; p < 2; ++p) {
+  {  // fx h rows viewed as 16-bit elements: [I/64 blocks][R rows][64]
     const cuuint64_t dims[3] = {64, (cuuint64_t)R, (cuuint64_t)(I / 64)};
     const cuuint64_t strides[2] = {(cuuint64_t)I * 2, 128};
     const cuuint32_t box[3] = {64, (cuuint32_t)kTok, 8};
-    if (enc(pm[p], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<__half*>(planes[p]), dims, strides, box, e3,
+    if (enc(&hm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint8_t*>(hq), dims, strides, box, e3,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return false;
@@ -1443,11 +1572,25 @@ bool launch_down_tma(const __half* h_hi, const __half* h_lo, long long R, const 
   if (s_mode == 2 && (size_t)kDnRows * NG * 2 <= (size_t)kDnScaleBytes &&
       (reinterpret_cast<uintptr_t>(w2_s) & 15) == 0)
     s_mode = 1;
-  auto k = ffn_down_tma_kernel<G, kTwo>;
+  auto k = ffn_down_tma_kernel<G>;
   set_smem(k, smem);
-  launch_pdl(k, dim3(grid), dim3(kGuThreads), smem, st, wm, sm, hm, lm, s_mode, offsets, active, w2_s, H, I, E, y);
+  launch_pdl(k, dim3(grid), dim3(kGuThreads), smem, st, wm, sm, hm, s_mode, hc, (int)R, offsets, active, w2_s, H, I,
+             E, y);
   return true;
 }
+
+template <int G>
+void launch_down(const uint8_t* hq, const int2* hc, const int32_t* offsets, const int32_t* active,
+                 const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, float* y, int grid,
+                 cudaStream_t st) {
+  using C = DownCfg<G>;
+  const size_t smem = (size_t)C::kStages * C::kStage + C::kRed + (size_t)(4 * E + 4) * 4;
+  auto k = ffn_down_kernel<G>;
+  set_smem(k, smem);
+  launch_pdl(k, dim3(grid), dim3(kDownThreads), smem, st, hq, hc, offsets, active, w2_q, w2_s, H, I, E, y);
+}
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 }  // namespace
 
@@ -1461,58 +1604,73 @@ int ffn_device_error(bool reset) {
   return v;
 }
 
+size_t fx_rows_bytes(long long rows, int K, int G) {
+  return align256((size_t)rows * K * 2) + (size_t)rows * (K / G) * 8;
+}
+
+int launch_fx_rows(const void* x, int x_dtype, long long rows, int K, int G, const int32_t* index,
+                   const int32_t* count, uint8_t* q, int2* consts, cudaStream_t st) {
+  if (rows <= 0) return PHMOE_OK;
+  if ((G != 32 && G != 64) || K % G) return PHMOE_ERR_UNSUPPORTED;
+  const long long words = rows * (K / 8);
+  const long long want = (words + 255) / 256;
+  const int grid = (int)std::min<long long>(want, 8LL * device_sm_count());
+  const bool f32 = x_dtype == PHMOE_DTYPE_F32;
+  if (G == 64) {
+    if (f32)
+      launch_pdl(fx_rows_kernel<float, 64>, dim3(grid), dim3(256), 0, st, static_cast<const float*>(x), K, rows,
+                 index, count, q, consts);
+    else
+      launch_pdl(fx_rows_kernel<__nv_bfloat16, 64>, dim3(grid), dim3(256), 0, st,
+                 static_cast<const __nv_bfloat16*>(x), K, rows, index, count, q, consts);
+  } else {
+    if (f32)
+      launch_pdl(fx_rows_kernel<float, 32>, dim3(grid), dim3(256), 0, st, static_cast<const float*>(x), K, rows,
+                 index, count, q, consts);
+    else
+      launch_pdl(fx_rows_kernel<__nv_bfloat16, 32>, dim3(grid), dim3(256), 0, st,
+                 static_cast<const __nv_bfloat16*>(x), K, rows, index, count, q, consts);
+  }
+  note_launches(1);
+  return PHMOE_OK;
+}
+
 int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       const int32_t* offsets, const int32_t* active, const uint8_t* w13_q,
                       const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T,
                       int H, int E, int top_k, int I, int G, float* h, float* y,
-                      cudaStream_t st, cudaEvent_t mid_event, long long rows_hint) {
+                      cudaStream_t st, cudaEvent_t mid_event, long long rows_hint, const int32_t* enc_index,
+                      const int32_t* enc_count) {
   const long long R = (long long)T * top_k;
   if (R == 0) return PHMOE_OK;
   if (G != 32 && G != 64) return PHMOE_ERR_UNSUPPORTED;
-  __half* h_hi = reinterpret_cast<__half*>(h);  // fp16 planes: hi, then lo (fp32 activations only)
-  __half* h_lo = h_hi + (size_t)R * I;
+  // fx rows of x in y's memory (the down kernel writes y only after gate/up
+  // has read them), fx rows of h in h's
+  uint8_t* xq = reinterpret_cast<uint8_t*>(y);
+  int2* xc = reinterpret_cast<int2*>(xq + align256((size_t)T * H * 2));
+  uint8_t* hq = reinterpret_cast<uint8_t*>(h);
+  int2* hc = reinterpret_cast<int2*>(hq + align256((size_t)R * I * 2));
+  if (int s = launch_fx_rows(x, x_dtype, T, H, G, enc_index, enc_count, xq, xc, st)) return s;
   const int grid = device_sm_count();
-  const bool f32 = x_dtype == PHMOE_DTYPE_F32;
   // multi-token gate/up items from kMtMinRowsPerExpert expected rows per
   // expert (each unpacked weight then feeds two or more 8-token MMA blocks);
   // both forms give bit-identical h, so this choice is for speed only
   const long long rows = rows_hint >= 0 ? rows_hint : R;
   const bool mt = rows >= (long long)kMtMinRowsPerExpert * E;
   int s = PHMOE_ERR_UNSUPPORTED;
-  if (mt) {
-    if (G == 64)
-      s = f32 ? launch_gateup_mt<64, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
-              : launch_gateup_mt<64, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo,
-                                                    grid, st);
-    else
-      s = f32 ? launch_gateup_mt<32, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
-              : launch_gateup_mt<32, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo,
-                                                    grid, st);
-  }
-  if (s != PHMOE_OK) {  // 8-token items (small batches, or the multi-token form did not fit)
-    if (G == 64)
-      s = f32 ? launch_gateup_rb<64, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
-              : launch_gateup_rb<64, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo,
-                                                    grid, st);
-    else
-      s = f32 ? launch_gateup_rb<32, float>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo, grid, st)
-              : launch_gateup_rb<32, __nv_bfloat16>(x, row_token, offsets, active, w13_q, w13_s, H, I, E, h_hi, h_lo,
-                                                    grid, st);
-  }
+  if (mt)
+    s = G == 64 ? launch_gateup<64>(true, xq, xc, row_token, offsets, active, w13_q, w13_s, H, I, E, hq, hc, grid, st)
+                : launch_gateup<32>(true, xq, xc, row_token, offsets, active, w13_q, w13_s, H, I, E, hq, hc, grid, st);
+  if (s != PHMOE_OK)  // 8-token items (small batches, or the multi-token form did not fit)
+    s = G == 64 ? launch_gateup<64>(false, xq, xc, row_token, offsets, active, w13_q, w13_s, H, I, E, hq, hc, grid, st)
+                : launch_gateup<32>(false, xq, xc, row_token, offsets, active, w13_q, w13_s, H, I, E, hq, hc, grid, st);
   if (s) return s;
   if (mid_event) cudaEventRecord(mid_event, st);
-  bool tma;
-  if (G == 64)
-    tma = f32 ? launch_down_tma<64, true>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st)
-              : launch_down_tma<64, false>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
-  else
-    tma = f32 ? launch_down_tma<32, true>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st)
-              : launch_down_tma<32, false>(h_hi, h_lo, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+  const bool tma = G == 64 ? launch_down_tma<64>(hq, hc, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st)
+                           : launch_down_tma<32>(hq, hc, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
   if (!tma) {
-    if (G == 64 && f32) launch_down<64, true>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
-    else if (G == 64) launch_down<64, false>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
-    else if (f32) launch_down<32, true>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
-    else launch_down<32, false>(h_hi, h_lo, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+    if (G == 64) launch_down<64>(hq, hc, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+    else launch_down<32>(hq, hc, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
   }
   note_launches(2);
   return PHMOE_OK;

@@ -17,12 +17,25 @@ int launch_dispatch(const int32_t* topk_idx, int T, int top_k, int E, int32_t* o
                     int32_t* row_token, int32_t* inv, int32_t* active, void* scratch,
                     cudaStream_t st);
 
+// Decode FFN over dispatched rows (exact integer tensor-core dot products on
+// fixed-point rows, ffn_decode.cu). The activation rows of x are encoded
+// first: all T rows, or (enc_index != null) rows enc_index[i] for
+// i < *enc_count (device memory), e.g. the rows that arrived from peers in a
+// receive buffer of T rows. h is scratch of T*k*I*4 bytes; y ([T*k, H]
+// fp32) also holds the encoded activations until the down kernel writes it.
 // mid_event (may be null) is recorded between the gate/up and down kernels.
 int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       const int32_t* offsets, const int32_t* active, const uint8_t* w13_q,
                       const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T,
                       int H, int E, int top_k, int I, int G, float* h, float* y,
-                      cudaStream_t st, cudaEvent_t mid_event = nullptr, long long rows_hint = -1);
+                      cudaStream_t st, cudaEvent_t mid_event = nullptr, long long rows_hint = -1,
+                      const int32_t* enc_index = nullptr, const int32_t* enc_count = nullptr);
+
+// Fixed-point rows (common.cuh) of `rows` rows of K elements (or of rows
+// index[i], i < *count): q [rows][K*2 bytes], consts [rows][K/G] {C0, M}.
+size_t fx_rows_bytes(long long rows, int K, int G);
+int launch_fx_rows(const void* x, int x_dtype, long long rows, int K, int G, const int32_t* index,
+                   const int32_t* count, uint8_t* q, int2* consts, cudaStream_t st);
 
 // Prefill form (tcgen05 grouped GEMMs): bf16 x only; h is R*I*4 bytes of
 // scratch and y doubles as the gathered activations until the down GEMM.

@@ -51,6 +51,8 @@ SIGNATURES = {
     "phmoe_expert_ffn_prefill": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _P,
                                       _I, _I, _I, _I, _I, _I, _P, _P, _P]),
     "phmoe_combine": (_I, [_P, _P, _P, _I, _I, _I, _P, _I, _P]),
+    "phmoe_fx_rows_size": (_SZ, [_LL, _I, _I]),
+    "phmoe_fx_rows": (_I, [_P, _I, _LL, _I, _I, _P, _P]),
     "phmoe_gather_rows": (_I, [_P, _LL, _P, _I, _LL, _P, _P]),
     "phmoe_ep_create": (_I, [_I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "phmoe_ep_create_ex": (_I, [_I, _I, _I, _I, _I, _I, _I, _I, _P, _P]),

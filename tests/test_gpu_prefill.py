@@ -164,7 +164,7 @@ def test_decode_multi_token_items(cuda_device, T):
 
 @pytest.mark.gpu
 def test_decode_multi_token_fp32_activations(cuda_device):
-    """fp32 activations (hi/lo bf16 split) through the multi-token items."""
+    """fp32 activations through the multi-token items."""
     dev = cuda_device
     E, H, k, I, G, T = 128, 2048, 8, 768, 64, 512
     wr, packed = _packed_layer(E, H, I, G, 17, dev)
@@ -175,7 +175,7 @@ def test_decode_multi_token_fp32_activations(cuda_device):
     ref = layer_torch(x, idx, w, offsets, row_token, inv, packed, G)
     torch.cuda.synchronize()
     mx, mr = O.parity_stats(out.cpu().numpy(), ref.cpu().numpy())
-    assert mx <= 1e-3 and mr <= 1e-4, (mx, mr)  # fp32 in, fp32 out: ~16-bit operands
+    assert mx <= 1e-3 and mr <= O.DECODE_FP32_MEAN_REL, (mx, mr)  # fp32 in, fp32 out: 14-bit operands
 
 
 @pytest.mark.gpu

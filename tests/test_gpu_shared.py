@@ -40,7 +40,7 @@ def test_qwen2moe_golden(cuda_device, path):
     assert mx <= O.MAX_ABS_TOL and mr <= O.MEAN_REL_TOL, (mx, mr)
     if dt == torch.float32:  # fp32 end to end: also the transformers block itself
         mx, mr = O.parity_stats(out.cpu().numpy(), z["out"])
-        assert mx <= 1e-3 and mr <= 1e-4, (mx, mr)
+        assert mx <= 1e-3 and mr <= O.DECODE_FP32_MEAN_REL, (mx, mr)
 
 
 @pytest.mark.parametrize("T,path,gated,scale", [(3, "decode", True, 1.0), (64, "decode", False, 2.5),
