@@ -379,7 +379,7 @@ def topk_margin(probs: np.ndarray, k: int) -> np.ndarray:
 # (nibble - 8) * scale, gguf_loader.py:372-378):
 #   per row and group of G elements, e = the exponent that scales the group's
 #   largest |value| m into [2^12, 8191] (G = 64) or [2^13, 16383] (G = 32),
-#   clamped to [-137, 100]; A = rint(v * 2^-e), |A| <= 8191 (16383);
+#   clamped to [-126, 100]; A = rint(v * 2^-e), |A| <= 8191 (16383);
 #   bytes of each 8-element word: the high bytes A >> 8 (two's complement)
 #   then the low bytes A & 255, each in element order 0, 4, 1, 5, 2, 6, 3, 7;
 #   constants {C0, M}: M = the int32 bits of the float 1.5 * 2^(23 + e),
@@ -389,7 +389,7 @@ def topk_margin(probs: np.ndarray, k: int) -> np.ndarray:
 # v * 2^e with no rounding (fx_group_dot replays this).
 
 FX_MAGIC = 0x4B400000
-FX_MIN_EXP, FX_MAX_EXP = -137, 100
+FX_MIN_EXP, FX_MAX_EXP = -126, 100
 _FX_SLOT_ELEM = np.array([0, 4, 1, 5, 2, 6, 3, 7])  # element held by byte slot j of a plane
 
 
@@ -413,10 +413,10 @@ def fx_exponents(v: np.ndarray, group: int):
         m = np.where(np.isnan(vg), 0.0, vg).max(axis=-1)
         top = ~(m <= big)
         _, p = np.frexp(np.where(top, 1.0, m))  # m = f * 2^p, f in [0.5, 1): floor(log2 m) = p - 1
-    e = (p - 1 - shift).astype(np.int64)
-    e = np.where(m * np.exp2(-e.astype(np.float64)) >= lim, e + 1, e)
+    e0 = (p - 1 - shift).astype(np.int64)
+    e = np.where(m * np.exp2(-e0.astype(np.float64)) >= lim, e0 + 1, e0)
+    e = np.where(e0 < FX_MIN_EXP, FX_MIN_EXP, e)   # tiny groups: the smallest exponent, no rounding up
     e = np.where(m == 0, 0, e)
-    e = np.maximum(e, FX_MIN_EXP)
     over = e > FX_MAX_EXP
     e = np.where(top | over, FX_MAX_EXP, e)
     return e, flag | over

@@ -367,7 +367,11 @@ int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtyp
   auto mark = [&](int b) { if (prof) cudaEventRecord(prof_event(pc, b), st); };
 
   mark(0);
-  launch_router(x, x_dtype, router_w, w_dtype, T, H, E, top_k, renormalize, logits, nullptr, idx, wts, st);
+  const bool decode = chosen != PHMOE_PATH_PREFILL;
+  const bool x_encoded =
+      launch_router(x, x_dtype, router_w, w_dtype, T, H, E, top_k, renormalize, logits, nullptr, idx, wts, st,
+                    group_size, decode ? ffn_decode_xq(y) : nullptr, decode ? ffn_decode_xc(y, T, H) : nullptr) ==
+      kRouterEncodedX;
   if (int s = check_launch("router")) return s;
   mark(1);
   launch_dispatch(idx, T, top_k, E, offsets, row_token, inv, active, ws + L.disp, st);
@@ -378,7 +382,8 @@ int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtyp
                                    group_size, h, y, st, prof ? prof_event(pc, 3) : nullptr))
       return fail(s, "prefill launch failed (tensor map or kernel attribute)");
   } else if (int s = launch_ffn_decode(x, x_dtype, row_token, offsets, active, w13_q, w13_s, w2_q, w2_s, T, H,
-                                       E, top_k, I, group_size, h, y, st, prof ? prof_event(pc, 3) : nullptr)) {
+                                       E, top_k, I, group_size, h, y, st, prof ? prof_event(pc, 3) : nullptr, -1,
+                                       nullptr, nullptr, x_encoded)) {
     return fail(s, "no decode kernel for group_size=%d", group_size);
   }
   if (int s = check_launch("expert_ffn")) return s;
@@ -554,8 +559,9 @@ int phmoe_device_error(int reset) {
   const int a = ffn_device_error(reset != 0);
   const int b = prefill_device_error(reset != 0);
   const int c = ep_device_error(reset != 0);
-  if (a < 0 || b < 0 || c < 0) return -1;
-  return a | b | c;
+  const int d = router_device_error(reset != 0);
+  if (a < 0 || b < 0 || c < 0 || d < 0) return -1;
+  return a | b | c | d;
 }
 
 // ---- expert parallelism in peer memory ----

@@ -135,6 +135,28 @@ inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// launch_pdl with a thread-block cluster of `cluster` CTAs (grid dimensions
+// must be multiples of it).
+template <typename... KArgs, typename... Args>
+inline void launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, dim3 cluster, size_t smem,
+                               cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster.x;
+  attr[1].val.clusterDim.y = cluster.y;
+  attr[1].val.clusterDim.z = cluster.z;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // D = A * B + C, m16n8k16, bf16 inputs, fp32 accumulate (register operands).
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
                                                uint32_t b0, uint32_t b1, const float (&c)[4]) {
@@ -147,6 +169,10 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
 }
 
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
+// SiLU from the hardware exp2 approximation and a fast reciprocal (a few
+// ulp; the decode FFN's h is then held to 2^-13 of its group maximum, far
+// coarser). For g below ~-88, e^-g is infinite and the result is -0.
+__device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 // ---------------------------------------------------------------------------
 // Integer tensor-core path of the decode FFN
@@ -166,6 +192,26 @@ __device__ __forceinline__ void mma_u8u8_16832(int (&d)[4], const uint32_t (&a)[
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// First step of a chain: D = A * B + C with C = (c0, c1, c0, c1) given as
+// plain inputs (the constants of the pass's two token columns, or zeros),
+// so no register copies are needed to seed the accumulators.
+__device__ __forceinline__ void mma_u8s8_16832_first(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                                     int c0, int c1) {
+  asm(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+}
+__device__ __forceinline__ void mma_u8u8_16832_first(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                                     int c0, int c1) {
+  asm(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
 }
 
 // One packed word (elements e0..e7, packed layout above) as two registers of
@@ -197,7 +243,7 @@ __device__ __forceinline__ void nib_bytes(uint32_t w, uint32_t& lo, uint32_t& hi
 // sum(n * hi) by the tensor cores, i = 256 * i_hi + i_lo (one IMAD), and
 // __int_as_float(i) - __int_as_float(M) = v * 2^e.
 constexpr int kFxMagic = 0x4B400000;  // float 1.5 * 2^23
-constexpr int kFxMinExp = -137;       // keeps M + v a normal float
+constexpr int kFxMinExp = -126;       // 2^-e stays a normal float (and M + v one too)
 constexpr int kFxMaxExp = 100;        // keeps M + v below 2^31
 template <int G>
 struct FxLimits {
@@ -213,27 +259,31 @@ __device__ __forceinline__ int ilog2_f32(float m) {
   return ex ? ex - 127 : -149 + (31 - __clz(b));
 }
 
+// 2^-e as a float, for e in [kFxMinExp, kFxMaxExp] (a normal power of two,
+// so multiplying by it is exact unless the product underflows).
+__device__ __forceinline__ float fx_pow2_neg(int e) { return __int_as_float((127 - e) << 23); }
+
 // The exponent of a group whose largest |value| is m. `bad` is set when the
 // group cannot be held (m beyond 2^(kFxMaxExp + 13), infinite or NaN): its
-// values are then clamped.
+// values are then clamped. Groups below 2^(kFxMinExp + 12) take kFxMinExp.
 template <int G>
 __device__ __forceinline__ int fx_exponent(float m, bool& bad) {
   bad = !(m <= 3.0e38f);  // NaN or infinite
   if (bad) return kFxMaxExp;
   if (m == 0.0f) return 0;
   int e = ilog2_f32(m) - FxLimits<G>::kShift;
-  if (ldexpf(m, -e) >= FxLimits<G>::kLim) ++e;
-  if (e < kFxMinExp) e = kFxMinExp;
-  if (e > kFxMaxExp) {
-    e = kFxMaxExp;
-    bad = true;
+  if (e < kFxMinExp) return kFxMinExp;
+  if (e >= kFxMaxExp) {
+    if (e > kFxMaxExp || m * fx_pow2_neg(e) >= FxLimits<G>::kLim) bad = true;
+    return kFxMaxExp;
   }
+  if (m * fx_pow2_neg(e) >= FxLimits<G>::kLim) ++e;
   return e;
 }
 
 template <int G>
 __device__ __forceinline__ int fx_encode(float v, int e) {
-  int a = __float2int_rn(ldexpf(v, -e));
+  int a = __float2int_rn(v * fx_pow2_neg(e));
   return max(-FxLimits<G>::kAmax, min(FxLimits<G>::kAmax, a));
 }
 

@@ -82,8 +82,10 @@ __device__ int g_ffn_error;
 
 namespace {
 
-constexpr int kConsumers = 16;                  // gate/up consumer warps
-constexpr int kGuThreads = (kConsumers + 1) * 32;  // + 1 producer warp
+constexpr int kConsumers = 16;                  // consumer (MMA) warps
+constexpr int kGuThreads = (kConsumers + 1) * 32;  // + 1 producer warp (down kernel)
+constexpr int kEpiWarps = 4;                    // gate/up epilogue warps (one per 16-row group)
+constexpr int kRbThreads = (kConsumers + kEpiWarps + 1) * 32;  // gate/up row-block kernel
 constexpr int kDownThreads = 16 * 32;
 constexpr int kTok = 8;                         // tokens per pass (the MMA N dimension)
 constexpr uint32_t kSpinLimit = 1u << 24;       // try_wait polls before giving up
@@ -249,15 +251,19 @@ __device__ __forceinline__ FxB<G> lds_fxb(const uint8_t* p) {
 template <int G>
 __device__ __forceinline__ void fx_group_tile(const RowWords<G>& w0, const RowWords<G>& w8, const FxB<G>& b,
                                               const int4& cc, float s0, float s8, float (&acc)[4]) {
-  int lo[4] = {cc.x, cc.z, cc.x, cc.z};
-  int hi[4] = {0, 0, 0, 0};
+  int lo[4], hi[4];
 #pragma unroll
   for (int s = 0; s < G / 32; ++s) {
     uint32_t a[4];
     nib_bytes(w0.w[s], a[0], a[2]);
     nib_bytes(w8.w[s], a[1], a[3]);
-    mma_u8u8_16832(lo, a, b.s[s].z, b.s[s].w);
-    mma_u8s8_16832(hi, a, b.s[s].x, b.s[s].y);
+    if (s == 0) {
+      mma_u8u8_16832_first(lo, a, b.s[s].z, b.s[s].w, cc.x, cc.z);
+      mma_u8s8_16832_first(hi, a, b.s[s].x, b.s[s].y, 0, 0);
+    } else {
+      mma_u8u8_16832(lo, a, b.s[s].z, b.s[s].w);
+      mma_u8s8_16832(hi, a, b.s[s].x, b.s[s].y);
+    }
   }
   const float m0 = __int_as_float(cc.y), m1 = __int_as_float(cc.w);
 #pragma unroll
@@ -273,8 +279,7 @@ __device__ __forceinline__ void gateup_group_fx(const RowWords<G>& g0, const Row
                                                 const RowWords<G>& u0, const RowWords<G>& u8, const FxB<G>& b,
                                                 const int4& cc, float sg0, float sg8, float su0, float su8,
                                                 float (&acc_g)[4], float (&acc_u)[4]) {
-  int gl[4] = {cc.x, cc.z, cc.x, cc.z}, ul[4] = {cc.x, cc.z, cc.x, cc.z};
-  int gh[4] = {0, 0, 0, 0}, uh[4] = {0, 0, 0, 0};
+  int gl[4], ul[4], gh[4], uh[4];
 #pragma unroll
   for (int s = 0; s < G / 32; ++s) {
     uint32_t ag[4], au[4];
@@ -282,10 +287,17 @@ __device__ __forceinline__ void gateup_group_fx(const RowWords<G>& g0, const Row
     nib_bytes(g8.w[s], ag[1], ag[3]);
     nib_bytes(u0.w[s], au[0], au[2]);
     nib_bytes(u8.w[s], au[1], au[3]);
-    mma_u8u8_16832(gl, ag, b.s[s].z, b.s[s].w);
-    mma_u8s8_16832(gh, ag, b.s[s].x, b.s[s].y);
-    mma_u8u8_16832(ul, au, b.s[s].z, b.s[s].w);
-    mma_u8s8_16832(uh, au, b.s[s].x, b.s[s].y);
+    if (s == 0) {
+      mma_u8u8_16832_first(gl, ag, b.s[s].z, b.s[s].w, cc.x, cc.z);
+      mma_u8s8_16832_first(gh, ag, b.s[s].x, b.s[s].y, 0, 0);
+      mma_u8u8_16832_first(ul, au, b.s[s].z, b.s[s].w, cc.x, cc.z);
+      mma_u8s8_16832_first(uh, au, b.s[s].x, b.s[s].y, 0, 0);
+    } else {
+      mma_u8u8_16832(gl, ag, b.s[s].z, b.s[s].w);
+      mma_u8s8_16832(gh, ag, b.s[s].x, b.s[s].y);
+      mma_u8u8_16832(ul, au, b.s[s].z, b.s[s].w);
+      mma_u8s8_16832(uh, au, b.s[s].x, b.s[s].y);
+    }
   }
   const float m0 = __int_as_float(cc.y), m1 = __int_as_float(cc.w);
 #pragma unroll
@@ -514,13 +526,13 @@ template <int S>
 struct RbCtl {
   uint64_t full[S];
   uint64_t empty[S];
-  uint64_t red_full[8];   // [buf][rg]: the three kq > 0 warps have written
-  uint64_t red_empty[8];  // [buf][rg]: the kq = 0 warp has read
-  uint64_t epi[4];        // [buf][2]: the epilogue's max and sum exchanges
+  uint64_t red_full[8];   // [buf][rg]: the four K-quarter warps have written their partials
+  uint64_t red_empty[8];  // [buf][rg]: the epilogue warp has read them
+  uint64_t epi[4];        // [buf][2]: the epilogue warps' max and sum exchanges
   int abort_flag;
 };
 
-template <int G>
+template <int G, int NS = 4>
 struct RbCfg {
   static constexpr int kGpq = 128 / G;                       // groups per consumer warp per task
   static constexpr int kCg = kRbKc / G;                      // groups per task
@@ -533,8 +545,8 @@ struct RbCfg {
   static constexpr int kB = kS + 2 * kRbRows * kScaleRow;     // [8 tokens][kBStride]
   static constexpr int kC = kB + kTok * kBStride;             // [kCg groups][8 tokens] int2
   static constexpr int kStage = (kC + kCg * kTok * 8 + 1023) / 1024 * 1024;
-  static constexpr int kStages = 4;
-  static constexpr int kRed = 4 * 3 * 32 * 8 * 4;             // [rg][kq-1][lane][8] floats
+  static constexpr int kStages = NS;
+  static constexpr int kRed = 4 * 4 * 32 * 8 * 4;             // [rg][kq][lane][8] floats
   static constexpr int kEpi = (int)sizeof(EpiBuf<kTok>);
   static constexpr size_t smem(int E) {
     return 1024 + (size_t)kStages * kStage + 2 * kRed + 2 * kEpi + sizeof(RbCtl<kStages>) +
@@ -542,8 +554,8 @@ struct RbCfg {
   }
 };
 
-template <int G>
-__global__ void __launch_bounds__(kGuThreads, 1)
+template <int G, int NS>
+__global__ void __launch_bounds__(kRbThreads, 1)
 ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int box_chunks,
                      const __grid_constant__ CUtensorMap s_map, int s_tma, const uint8_t* __restrict__ xq,
                      const int2* __restrict__ xc, const int32_t* __restrict__ row_token,
@@ -551,11 +563,11 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
                      const uint16_t* __restrict__ w13_s, int H, int I, int E, uint8_t* __restrict__ hq,
                      int2* __restrict__ hc) {
   pdl_begin();
-  using C = RbCfg<G>;
+  using C = RbCfg<G, NS>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [2][rg][kq-1][lane][8]
+  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [2][rg][kq][lane][8]
   EpiBuf<kTok>* epib = reinterpret_cast<EpiBuf<kTok>*>(smem + S * C::kStage + 2 * C::kRed);
   RbCtl<S>* ctl = reinterpret_cast<RbCtl<S>*>(smem + S * C::kStage + 2 * C::kRed + 2 * C::kEpi);
   int* mbase = reinterpret_cast<int*>(ctl + 1);
@@ -573,10 +585,10 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
       mbar_init(smem_u32(&ctl->empty[s]), kConsumers);
     }
     for (int i = 0; i < 8; ++i) {
-      mbar_init(smem_u32(&ctl->red_full[i]), 3);
+      mbar_init(smem_u32(&ctl->red_full[i]), 4);
       mbar_init(smem_u32(&ctl->red_empty[i]), 1);
     }
-    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&ctl->epi[i]), 4);
+    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&ctl->epi[i]), kEpiWarps);
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
@@ -586,7 +598,58 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
   const int ntask = (q1 - q0) * nkc;
   if (ntask == 0) return;
 
-  if (warp == kConsumers) {
+  if (warp >= kConsumers && warp < kConsumers + kEpiWarps) {
+    // ---------------- epilogue warps ----------------
+    // Warp rg finishes the I rows rg*16..rg*16+15 of every item: the sum of
+    // the four K-quarter partials in fixed order ((q0 + q1) + q2) + q3, the
+    // SwiGLU, and with the other three the fx encoding of h.
+    const int rg = warp - kConsumers;
+    const int c = lane & 3;
+    Cursor ci = cursor_at(q0, na, tiles, meta);
+    for (int it = 0; it < q1 - q0; ++it) {
+      const int buf = it & 1, use = it >> 1;
+      const int bi = buf * 4 + rg;
+      if (!wait_phase(smem_u32(&ctl->red_full[bi]), use & 1, abort_flag)) return;
+      const float* rb = red + (size_t)buf * (C::kRed / 4) + (size_t)rg * 4 * 32 * 8 + lane * 8;
+      float gs[4], us[4];
+      {
+        const float4 a = reinterpret_cast<const float4*>(rb)[0], b = reinterpret_cast<const float4*>(rb)[1];
+        gs[0] = a.x; gs[1] = a.y; gs[2] = a.z; gs[3] = a.w;
+        us[0] = b.x; us[1] = b.y; us[2] = b.z; us[3] = b.w;
+      }
+#pragma unroll
+      for (int w = 1; w < 4; ++w) {
+        const float4 a = reinterpret_cast<const float4*>(rb + w * 32 * 8)[0];
+        const float4 b = reinterpret_cast<const float4*>(rb + w * 32 * 8)[1];
+        gs[0] += a.x; gs[1] += a.y; gs[2] += a.z; gs[3] += a.w;
+        us[0] += b.x; us[1] += b.y; us[2] += b.z; us[3] += b.w;
+      }
+      warp_arrive(smem_u32(&ctl->red_empty[bi]), lane);
+      const int n = meta.n[ci.slot], row0 = meta.row0[ci.slot];
+      const int prow0 = ci.pass * kTok;
+      float hv[4];
+      bool any = false;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const bool ok = prow0 + 2 * c + (q & 1) < n;
+        hv[q] = ok ? silu_fast(gs[q]) * us[q] : 0.f;
+        any |= ok;
+      }
+      EpiBuf<kTok>* eb = epib + buf;
+      epi_block_max<kTok>(eb, rg, lane, 0, hv);
+      warp_arrive(smem_u32(&ctl->epi[buf * 2]), lane);
+      if (!wait_phase(smem_u32(&ctl->epi[buf * 2]), use & 1, abort_flag)) return;
+      int e[2];
+      epi_block_encode<G, kTok>(eb, rg, lane, 0, hv, any, e);
+      warp_arrive(smem_u32(&ctl->epi[buf * 2 + 1]), lane);
+      if (!wait_phase(smem_u32(&ctl->epi[buf * 2 + 1]), use & 1, abort_flag)) return;
+      epi_block_store<G, kTok>(eb, rg, lane, 0, e, ci.tile, prow0, n, row0, I, hq, hc);
+      cursor_next(ci, tiles, 1, meta);
+    }
+    return;
+  }
+
+  if (warp == kConsumers + kEpiWarps) {
     // ---------------- producer warp ----------------
     Cursor cu = cursor_at(q0, na, tiles, meta);
     auto token = [&](const Cursor& k) -> int {  // lane holds the token id of pass row lane % 8
@@ -716,48 +779,14 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
       }
     }
     warp_arrive(smem_u32(&ctl->empty[s]), lane);  // this warp is done with the stage
-    if (cu.kc == nkc - 1) {
+    if (cu.kc == nkc - 1) {  // hand this K quarter's partials to the epilogue warp
       const int buf = item & 1, use = item >> 1;
       const int bi = buf * 4 + rg;  // barrier index
-      float* rb = red + (size_t)buf * (C::kRed / 4) + (size_t)rg * 3 * 32 * 8;
-      if (kq > 0) {
-        if (use > 0 && !wait_phase(smem_u32(&ctl->red_empty[bi]), (use - 1) & 1, abort_flag)) return;
-        float4* dst = reinterpret_cast<float4*>(rb + ((kq - 1) * 32 + lane) * 8);
-        dst[0] = make_float4(acc_g[0], acc_g[1], acc_g[2], acc_g[3]);
-        dst[1] = make_float4(acc_u[0], acc_u[1], acc_u[2], acc_u[3]);
-        warp_arrive(smem_u32(&ctl->red_full[bi]), lane);
-      } else {
-        if (!wait_phase(smem_u32(&ctl->red_full[bi]), use & 1, abort_flag)) return;
-        float gs[4] = {acc_g[0], acc_g[1], acc_g[2], acc_g[3]};
-        float us[4] = {acc_u[0], acc_u[1], acc_u[2], acc_u[3]};
-#pragma unroll
-        for (int w = 0; w < 3; ++w) {
-          const float4* src = reinterpret_cast<const float4*>(rb + (w * 32 + lane) * 8);
-          const float4 a = src[0], b = src[1];
-          gs[0] += a.x; gs[1] += a.y; gs[2] += a.z; gs[3] += a.w;
-          us[0] += b.x; us[1] += b.y; us[2] += b.z; us[3] += b.w;
-        }
-        warp_arrive(smem_u32(&ctl->red_empty[bi]), lane);
-        const int n = meta.n[cu.slot], row0 = meta.row0[cu.slot];
-        const int prow0 = cu.pass * kTok;
-        float hv[4];
-        bool any = false;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const bool ok = prow0 + 2 * c + (q & 1) < n;
-          hv[q] = ok ? silu_f32(gs[q]) * us[q] : 0.f;
-          any |= ok;
-        }
-        EpiBuf<kTok>* eb = epib + buf;
-        epi_block_max<kTok>(eb, rg, lane, 0, hv);
-        warp_arrive(smem_u32(&ctl->epi[buf * 2]), lane);
-        if (!wait_phase(smem_u32(&ctl->epi[buf * 2]), use & 1, abort_flag)) return;
-        int e[2];
-        epi_block_encode<G, kTok>(eb, rg, lane, 0, hv, any, e);
-        warp_arrive(smem_u32(&ctl->epi[buf * 2 + 1]), lane);
-        if (!wait_phase(smem_u32(&ctl->epi[buf * 2 + 1]), use & 1, abort_flag)) return;
-        epi_block_store<G, kTok>(eb, rg, lane, 0, e, cu.tile, prow0, n, row0, I, hq, hc);
-      }
+      if (use > 0 && !wait_phase(smem_u32(&ctl->red_empty[bi]), (use - 1) & 1, abort_flag)) return;
+      float4* dst = reinterpret_cast<float4*>(red + (size_t)buf * (C::kRed / 4) + ((size_t)(rg * 4 + kq) * 32 + lane) * 8);
+      dst[0] = make_float4(acc_g[0], acc_g[1], acc_g[2], acc_g[3]);
+      dst[1] = make_float4(acc_u[0], acc_u[1], acc_u[2], acc_u[3]);
+      warp_arrive(smem_u32(&ctl->red_full[bi]), lane);
       ++item;
     }
     cursor_next(cu, tiles, nkc, meta);
@@ -984,14 +1013,20 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
             if (b < nb) {
               const FxB<G> bw = lds_fxb<G>(bb + b * kTok * C::kBStride);
               const int4 cc = *reinterpret_cast<const int4*>(cb + b * kTok * 8);
-              int gl[4] = {cc.x, cc.z, cc.x, cc.z}, ul[4] = {cc.x, cc.z, cc.x, cc.z};
-              int gh[4] = {0, 0, 0, 0}, uh[4] = {0, 0, 0, 0};
+              int gl[4], ul[4], gh[4], uh[4];
 #pragma unroll
               for (int w = 0; w < G / 32; ++w) {
-                mma_u8u8_16832(gl, ag[w], bw.s[w].z, bw.s[w].w);
-                mma_u8s8_16832(gh, ag[w], bw.s[w].x, bw.s[w].y);
-                mma_u8u8_16832(ul, au[w], bw.s[w].z, bw.s[w].w);
-                mma_u8s8_16832(uh, au[w], bw.s[w].x, bw.s[w].y);
+                if (w == 0) {
+                  mma_u8u8_16832_first(gl, ag[w], bw.s[w].z, bw.s[w].w, cc.x, cc.z);
+                  mma_u8s8_16832_first(gh, ag[w], bw.s[w].x, bw.s[w].y, 0, 0);
+                  mma_u8u8_16832_first(ul, au[w], bw.s[w].z, bw.s[w].w, cc.x, cc.z);
+                  mma_u8s8_16832_first(uh, au[w], bw.s[w].x, bw.s[w].y, 0, 0);
+                } else {
+                  mma_u8u8_16832(gl, ag[w], bw.s[w].z, bw.s[w].w);
+                  mma_u8s8_16832(gh, ag[w], bw.s[w].x, bw.s[w].y);
+                  mma_u8u8_16832(ul, au[w], bw.s[w].z, bw.s[w].w);
+                  mma_u8s8_16832(uh, au[w], bw.s[w].x, bw.s[w].y);
+                }
               }
               const float m0 = __int_as_float(cc.y), m1 = __int_as_float(cc.w);
 #pragma unroll
@@ -1042,7 +1077,7 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const bool ok = prow0 + b * kTok + 2 * c + (q & 1) < n;
-              hv[b][q] = ok ? silu_f32(gs[q]) * us[q] : 0.f;
+              hv[b][q] = ok ? silu_fast(gs[q]) * us[q] : 0.f;
               any[b] |= ok;
             }
           }
@@ -1504,7 +1539,8 @@ int launch_gateup(bool mt, const uint8_t* xq, const int2* xc, const int32_t* row
                   uint8_t* hq, int2* hc, int grid, cudaStream_t st) {
   const int rows = mt ? kMtRows : kRbRows;
   const int kc = mt ? kMtKc : kRbKc;
-  const size_t smem = mt ? MtCfg<G>::smem(E) : RbCfg<G>::smem(E);
+  const bool rb4 = RbCfg<G, 4>::smem(E) <= kMaxSmem;  // four stages where they fit, else three
+  const size_t smem = mt ? MtCfg<G>::smem(E) : (rb4 ? RbCfg<G, 4>::smem(E) : RbCfg<G, 3>::smem(E));
   if (smem > kMaxSmem) return PHMOE_ERR_UNSUPPORTED;
   const int box_chunks = std::min(H, kc) / 256;
   alignas(64) CUtensorMap map, smap;
@@ -1518,9 +1554,9 @@ int launch_gateup(bool mt, const uint8_t* xq, const int2* xc, const int32_t* row
     launch_pdl(k, dim3(grid), dim3(kMtThreads), smem, st, map, mode, box_chunks, smap, s_tma, xq, xc, row_token,
                offsets, active, w13_s, H, I, E, hq, hc);
   } else {
-    auto k = ffn_gateup_rb_kernel<G>;
+    auto k = rb4 ? ffn_gateup_rb_kernel<G, 4> : ffn_gateup_rb_kernel<G, 3>;
     set_smem(k, smem);
-    launch_pdl(k, dim3(grid), dim3(kGuThreads), smem, st, map, mode, box_chunks, smap, s_tma, xq, xc, row_token,
+    launch_pdl(k, dim3(grid), dim3(kRbThreads), smem, st, map, mode, box_chunks, smap, s_tma, xq, xc, row_token,
                offsets, active, w13_s, H, I, E, hq, hc);
   }
   return PHMOE_OK;
@@ -1604,6 +1640,11 @@ int ffn_device_error(bool reset) {
   return v;
 }
 
+uint8_t* ffn_decode_xq(float* y) { return reinterpret_cast<uint8_t*>(y); }
+int2* ffn_decode_xc(float* y, int T, int H) {
+  return reinterpret_cast<int2*>(reinterpret_cast<uint8_t*>(y) + align256((size_t)T * H * 2));
+}
+
 size_t fx_rows_bytes(long long rows, int K, int G) {
   return align256((size_t)rows * K * 2) + (size_t)rows * (K / G) * 8;
 }
@@ -1640,17 +1681,18 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T,
                       int H, int E, int top_k, int I, int G, float* h, float* y,
                       cudaStream_t st, cudaEvent_t mid_event, long long rows_hint, const int32_t* enc_index,
-                      const int32_t* enc_count) {
+                      const int32_t* enc_count, bool x_encoded) {
   const long long R = (long long)T * top_k;
   if (R == 0) return PHMOE_OK;
   if (G != 32 && G != 64) return PHMOE_ERR_UNSUPPORTED;
   // fx rows of x in y's memory (the down kernel writes y only after gate/up
   // has read them), fx rows of h in h's
-  uint8_t* xq = reinterpret_cast<uint8_t*>(y);
-  int2* xc = reinterpret_cast<int2*>(xq + align256((size_t)T * H * 2));
+  uint8_t* xq = ffn_decode_xq(y);
+  int2* xc = ffn_decode_xc(y, T, H);
   uint8_t* hq = reinterpret_cast<uint8_t*>(h);
   int2* hc = reinterpret_cast<int2*>(hq + align256((size_t)R * I * 2));
-  if (int s = launch_fx_rows(x, x_dtype, T, H, G, enc_index, enc_count, xq, xc, st)) return s;
+  if (!x_encoded)
+    if (int s = launch_fx_rows(x, x_dtype, T, H, G, enc_index, enc_count, xq, xc, st)) return s;
   const int grid = device_sm_count();
   // multi-token gate/up items from kMtMinRowsPerExpert expected rows per
   // expert (each unpacked weight then feeds two or more 8-token MMA blocks);

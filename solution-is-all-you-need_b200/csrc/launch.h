@@ -8,9 +8,17 @@
 
 namespace phmoe {
 
+// Router. With xq != null and a batch the fused single-launch router takes
+// (router_fused_supported), it also writes the fixed-point rows of x for the
+// decode FFN (group size G) to xq / xc and returns kRouterEncodedX; callers
+// then pass x_encoded to launch_ffn_decode. Otherwise returns PHMOE_OK and
+// writes nothing there.
+constexpr int kRouterEncodedX = 1;
+bool router_fused_supported(int T, int H, int E);
 int launch_router(const void* x, int x_dtype, const void* wr, int w_dtype, int T, int H, int E,
                   int top_k, int renormalize, float* logits, float* probs, int32_t* topk_idx,
-                  float* topk_w, cudaStream_t st);
+                  float* topk_w, cudaStream_t st, int G = 0, uint8_t* xq = nullptr, int2* xc = nullptr);
+int router_device_error(bool reset);
 
 size_t dispatch_scratch_bytes(int T, int top_k, int E);
 int launch_dispatch(const int32_t* topk_idx, int T, int top_k, int E, int32_t* offsets,
@@ -29,7 +37,12 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T,
                       int H, int E, int top_k, int I, int G, float* h, float* y,
                       cudaStream_t st, cudaEvent_t mid_event = nullptr, long long rows_hint = -1,
-                      const int32_t* enc_index = nullptr, const int32_t* enc_count = nullptr);
+                      const int32_t* enc_index = nullptr, const int32_t* enc_count = nullptr,
+                      bool x_encoded = false);
+// Where launch_ffn_decode keeps the fixed-point rows of x inside y (the
+// router may write them there first).
+uint8_t* ffn_decode_xq(float* y);
+int2* ffn_decode_xc(float* y, int T, int H);
 
 // Fixed-point rows (common.cuh) of `rows` rows of K elements (or of rows
 // index[i], i < *count): q [rows][K*2 bytes], consts [rows][K/G] {C0, M}.

@@ -13,12 +13,23 @@
 //   logit(t,e): element h goes to lane (h/8)%32; each lane adds its products
 //   in increasing h; lanes are combined by an xor butterfly 16,8,4,2,1.
 //   softmax: expert e on lane e%32, lane sums in increasing e, xor butterfly.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "launch.h"
 
+namespace cg = cooperative_groups;
+
 namespace phmoe {
 
+// Error bit the fused router raises (read by phmoe_device_error): 2 when a
+// value of x could not be held by the decode FFN's fixed-point rows (about
+// 1e34 or beyond, infinite or NaN) and was clamped.
+__device__ int g_router_error;
+
 namespace {
+
+__device__ __forceinline__ void fx_flag_bad() { atomicOr(&g_router_error, 2); }
 
 constexpr int kRouterWarps = 8;     // experts per CTA (one warp each)
 constexpr int kRouterTokens = 8;    // tokens per CTA
@@ -95,57 +106,45 @@ __device__ __forceinline__ void stage_f32<float>(float* row, int h, const uint4&
   *reinterpret_cast<uint4*>(row + tile_pos(h >> 8, (h >> 2) & 1, (h >> 3) & 31)) = u;
 }
 
-// Grid: (ceil(E/8), ceil(T/TT)); warp w of a CTA owns expert blockIdx.x*8+w.
-// The TT-token tile of x is staged once in shared memory as fp32 (one
-// cooperative round trip of 16-byte loads, converted once per CTA rather
-// than once per expert); router-weight chunks are loaded kBatch at a time so
-// their latencies overlap.
-template <typename XT, typename WT, int TT>
-__global__ void __launch_bounds__(kRouterWarps * 32)
-router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T, int H, int E,
-                     float* __restrict__ logits) {
-  pdl_begin();
-  constexpr bool kExact = std::is_same<XT, __nv_bfloat16>::value && std::is_same<WT, __nv_bfloat16>::value;
-  constexpr int kBatch = std::is_same<WT, float>::value ? 4 : 8;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  float* xs = reinterpret_cast<float*>(smem_raw);  // [TT][nchunk * 256] fp32, tile_pos layout
-  const int nchunk = (H + 255) / 256;
-  const int rowf = nchunk * 256;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * kRouterWarps + warp;
-  const int t0 = blockIdx.y * TT;
-  const int nt = min(TT, T - t0);
-  {
-    // all loads of a round are issued before its stores, so staging the tile
-    // costs one memory round trip per 8 vectors a thread, not one per vector
-    constexpr int kVec = 16 / sizeof(XT);
-    constexpr int kUnroll = 8;
-    const int nvec = nt * H / kVec;  // H % 8 == 0, so rows are whole vectors
-    const int vrow = H / kVec;
-    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t0 * H);
-    for (int i0 = threadIdx.x; i0 < nvec; i0 += blockDim.x * kUnroll) {
-      uint4 v[kUnroll];
+// Stage nt rows of x (H elements each) into xs as fp32 in the tile_pos
+// layout (row stride rowf). All loads of a round are issued before its
+// stores, so staging costs one memory round trip per 8 vectors a thread.
+template <typename XT>
+__device__ __forceinline__ void stage_tile(const XT* __restrict__ x, int nt, int H, int rowf, float* xs) {
+  constexpr int kVec = 16 / sizeof(XT);
+  constexpr int kUnroll = 8;
+  const int nvec = nt * H / kVec;  // H % 8 == 0, so rows are whole vectors
+  const int vrow = H / kVec;
+  const uint4* src = reinterpret_cast<const uint4*>(x);
+  for (int i0 = threadIdx.x; i0 < nvec; i0 += blockDim.x * kUnroll) {
+    uint4 v[kUnroll];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int i = i0 + u * blockDim.x;
-        if (i < nvec) v[u] = __ldg(src + i);
-      }
+    for (int u = 0; u < kUnroll; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < nvec) v[u] = __ldg(src + i);
+    }
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int i = i0 + u * blockDim.x;
-        if (i < nvec) {
-          const int t = i / vrow;
-          stage_f32<XT>(xs + (size_t)t * rowf, (i - t * vrow) * kVec, v[u]);
-        }
+    for (int u = 0; u < kUnroll; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < nvec) {
+        const int t = i / vrow;
+        stage_f32<XT>(xs + (size_t)t * rowf, (i - t * vrow) * kVec, v[u]);
       }
     }
   }
-  __syncthreads();
-  if (e >= E) return;
-  float acc[TT];
+}
+
+// The x tile of TT tokens (fp32, tile_pos layout) against one router-weight
+// row: acc[t] = the fixed-order logit of token t, returned on every lane.
+// Lane L owns the elements h with (h/8) % 32 == L, adds its products in
+// increasing h, and the 32 lane sums are combined by an xor butterfly.
+template <typename XT, typename WT, int TT>
+__device__ __forceinline__ void expert_logits(const float* xs, int rowf, int nchunk, const WT* __restrict__ wrow,
+                                              int H, int nt, int lane, float (&acc)[TT]) {
+  constexpr bool kExact = std::is_same<XT, __nv_bfloat16>::value && std::is_same<WT, __nv_bfloat16>::value;
+  constexpr int kBatch = std::is_same<WT, float>::value ? 4 : 8;
 #pragma unroll
   for (int t = 0; t < TT; ++t) acc[t] = 0.f;
-  const WT* wrow = wr + (size_t)e * H;
   for (int c0 = 0; c0 < nchunk; c0 += kBatch) {
     float w[kBatch][8];
 #pragma unroll
@@ -182,6 +181,31 @@ router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T,
     for (int off = 16; off >= 1; off >>= 1)
       acc[t] = __fadd_rn(acc[t], __shfl_xor_sync(0xffffffffu, acc[t], off));
   }
+}
+
+// Grid: (ceil(E/8), ceil(T/TT)); warp w of a CTA owns expert blockIdx.x*8+w.
+// The TT-token tile of x is staged once in shared memory as fp32 (one
+// cooperative round trip of 16-byte loads, converted once per CTA rather
+// than once per expert); router-weight chunks are loaded kBatch at a time so
+// their latencies overlap.
+template <typename XT, typename WT, int TT>
+__global__ void __launch_bounds__(kRouterWarps * 32)
+router_logits_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T, int H, int E,
+                     float* __restrict__ logits) {
+  pdl_begin();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* xs = reinterpret_cast<float*>(smem_raw);  // [TT][nchunk * 256] fp32, tile_pos layout
+  const int nchunk = (H + 255) / 256;
+  const int rowf = nchunk * 256;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * kRouterWarps + warp;
+  const int t0 = blockIdx.y * TT;
+  const int nt = min(TT, T - t0);
+  stage_tile<XT>(x + (size_t)t0 * H, nt, H, rowf, xs);
+  __syncthreads();
+  if (e >= E) return;
+  float acc[TT];
+  expert_logits<XT, WT, TT>(xs, rowf, nchunk, wr + (size_t)e * H, H, nt, lane, acc);
   if (lane == 0) {
 #pragma unroll
     for (int t = 0; t < TT; ++t)
@@ -283,23 +307,19 @@ __device__ __forceinline__ float exp_fixed(float x) {
   return x < -87.0f ? 0.0f : out;
 }
 
-// One warp per token. EPL = experts held per lane (E <= 32*EPL).
+// softmax (fp32, exp_fixed), top-k (ties -> lower index) and
+// renormalisation of one token held by one warp: v[i] is the logit of
+// expert lane + 32 i (entries at or beyond E are ignored). Writes probs (when
+// non-null), topk_idx and topk_w of token t.
 template <int EPL>
-__global__ void __launch_bounds__(256)
-router_topk_kernel(const float* __restrict__ logits, int T, int E, int top_k, int renormalize,
-                   float* __restrict__ probs, int32_t* __restrict__ topk_idx,
-                   float* __restrict__ topk_w) {
-  pdl_begin();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (t >= T) return;
-  const float* lrow = logits + (size_t)t * E;
-  float v[EPL];
+__device__ __forceinline__ void softmax_topk_warp(float (&v)[EPL], int lane, int t, int E, int top_k,
+                                                  int renormalize, float* __restrict__ probs,
+                                                  int32_t* __restrict__ topk_idx, float* __restrict__ topk_w) {
   float m = -INFINITY;
 #pragma unroll
   for (int i = 0; i < EPL; ++i) {
     const int e = lane + 32 * i;
-    v[i] = e < E ? lrow[e] : -INFINITY;
+    if (e >= E) v[i] = -INFINITY;
     m = fmaxf(m, v[i]);
   }
 #pragma unroll
@@ -351,6 +371,155 @@ router_topk_kernel(const float* __restrict__ logits, int T, int E, int top_k, in
     topk_idx[(size_t)t * top_k + lane] = my_idx;
     topk_w[(size_t)t * top_k + lane] = renormalize ? __fdiv_rn(my_val, sum_sel) : my_val;
   }
+}
+
+// One warp per token. EPL = experts held per lane (E <= 32*EPL).
+template <int EPL>
+__global__ void __launch_bounds__(256)
+router_topk_kernel(const float* __restrict__ logits, int T, int E, int top_k, int renormalize,
+                   float* __restrict__ probs, int32_t* __restrict__ topk_idx,
+                   float* __restrict__ topk_w) {
+  pdl_begin();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t >= T) return;
+  const float* lrow = logits + (size_t)t * E;
+  float v[EPL];
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? lrow[e] : -INFINITY;
+  }
+  softmax_topk_warp<EPL>(v, lane, t, E, top_k, renormalize, probs, topk_idx, topk_w);
+}
+
+// Fused router for decode batches (T < 256, E <= 256): logits, softmax,
+// top-k and, optionally, the fixed-point encoding of x for the decode FFN, in
+// one launch. A cluster of 8 CTAs shares a tile of TT tokens: CTA q stages
+// the tile as fp32 and computes the logits of experts q*EC .. q*EC+EC-1
+// (EC = ceil(E/8), warp w taking experts w, w+8, ... of them) with the same
+// fixed reduction order as router_logits_kernel; the logits go to global
+// memory and to the CTA's shared memory. CTA q also encodes the groups
+// g = q, q+8, ... of every token of the tile (fx rows, as fx_rows_kernel).
+// After a cluster barrier, token t of the tile is taken by warp t/8 of CTA
+// t%8, which reads all E logits through distributed shared memory and runs
+// softmax_topk_warp. A second cluster barrier keeps every CTA's shared
+// memory alive until all reads are done. No CTA leaves before either
+// barrier, so the barriers always complete.
+constexpr int kFusedCluster = 8;
+
+template <int G>
+__device__ __forceinline__ void encode_tile_groups(const float* xs, int rowf, int nt, int H, int q, int t0,
+                                                   uint8_t* __restrict__ xq, int2* __restrict__ xc) {
+  constexpr int kTpg = G / 8;                  // threads per group (one word each)
+  constexpr int kGroupsPerRound = 256 / kTpg;
+  const int NG = H / G;
+  const int ngc = (NG + kFusedCluster - 1) / kFusedCluster;  // groups of a token handled by this CTA
+  const int units = nt * ngc;
+  for (int u0 = 0; u0 < units; u0 += kGroupsPerRound) {
+    const int u = u0 + (int)threadIdx.x / kTpg;
+    const int t = u / ngc;
+    const int g = q + kFusedCluster * (u - t * ngc);
+    const bool ok = u < units && g < NG;
+    const int w = (ok ? g : 0) * kTpg + (int)(threadIdx.x % kTpg);  // word index in the row
+    float v[8];
+    if (ok) {
+      const int h = w * 8, c = h >> 8, L = (h >> 3) & 31;
+      const float4 lo = *reinterpret_cast<const float4*>(xs + (size_t)t * rowf + tile_pos(c, 0, L));
+      const float4 hi = *reinterpret_cast<const float4*>(xs + (size_t)t * rowf + tile_pos(c, 1, L));
+      v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w; v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = 0.f;
+    }
+    float m = 0.f;
+    bool nonfinite = false;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float a = fabsf(v[j]);
+      nonfinite |= !(a <= 3.0e38f);
+      m = fmaxf(m, a);
+    }
+#pragma unroll
+    for (int off = 1; off < kTpg; off <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    bool bad;
+    const int e = fx_exponent<G>(m, bad);
+    int a[8];
+    int s = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      a[j] = fx_encode<G>(v[j], e);
+      s += a[j];
+    }
+#pragma unroll
+    for (int off = 1; off < kTpg; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (ok) {
+      const size_t row = (size_t)(t0 + t);
+      *reinterpret_cast<uint4*>(xq + (row * (H / 8) + w) * 16) = fx_word(a);
+      if ((threadIdx.x % kTpg) == 0) {
+        const int M = fx_magic(e);
+        xc[row * NG + g] = make_int2(M - 8 * s, M);
+      }
+      if (bad || nonfinite) fx_flag_bad();
+    }
+  }
+}
+
+template <typename XT, typename WT, int TT>
+__global__ void __launch_bounds__(kRouterWarps * 32)
+router_fused_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T, int H, int E, int top_k,
+                    int renormalize, float* __restrict__ logits, float* __restrict__ probs,
+                    int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, int G, uint8_t* __restrict__ xq,
+                    int2* __restrict__ xc) {
+  pdl_begin();
+  cg::cluster_group cluster = cg::this_cluster();
+  const int q = (int)cluster.block_rank();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int nchunk = (H + 255) / 256;
+  const int rowf = nchunk * 256;
+  const int EC = (E + kFusedCluster - 1) / kFusedCluster;
+  float* xs = reinterpret_cast<float*>(smem_raw);  // [TT][rowf]
+  float* lg = xs + (size_t)TT * rowf;              // [TT][EC] this CTA's logits
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.y * TT;
+  const int nt = min(TT, T - t0);
+  stage_tile<XT>(x + (size_t)t0 * H, nt, H, rowf, xs);
+  __syncthreads();
+  for (int el = warp; el < EC; el += kRouterWarps) {
+    const int e = q * EC + el;
+    if (e >= E) break;
+    float acc[TT];
+    expert_logits<XT, WT, TT>(xs, rowf, nchunk, wr + (size_t)e * H, H, nt, lane, acc);
+    if (lane == 0) {
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
+        if (t < nt) {
+          logits[(size_t)(t0 + t) * E + e] = acc[t];
+          lg[t * EC + el] = acc[t];
+        }
+      }
+    }
+  }
+  if (xq != nullptr) {
+    if (G == 64) encode_tile_groups<64>(xs, rowf, nt, H, q, t0, xq, xc);
+    else encode_tile_groups<32>(xs, rowf, nt, H, q, t0, xq, xc);
+  }
+  cluster.sync();
+  for (int t = q + kFusedCluster * warp; t < nt; t += kFusedCluster * kRouterWarps) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E) {
+        const float* remote = cluster.map_shared_rank(lg, e / EC);
+        v[i] = remote[t * EC + e % EC];
+      } else {
+        v[i] = -INFINITY;
+      }
+    }
+    softmax_topk_warp<8>(v, lane, t0 + t, E, top_k, renormalize, probs, topk_idx, topk_w);
+  }
+  cluster.sync();
 }
 
 // sigmoid(x) from exp_fixed (so the CPU restatement replays it bit for bit).
@@ -530,10 +699,67 @@ int launch_router_grouped(const void* x, int x_dtype, const void* wr, int w_dtyp
   return PHMOE_OK;
 }
 
+namespace {
+template <typename XT, typename WT, int TT>
+void launch_fused_tt(const void* x, const void* wr, int T, int H, int E, int top_k, int renormalize, float* logits,
+                     float* probs, int32_t* topk_idx, float* topk_w, int G, uint8_t* xq, int2* xc,
+                     cudaStream_t st) {
+  const int EC = (E + kFusedCluster - 1) / kFusedCluster;
+  const size_t smem = ((size_t)TT * ((H + 255) / 256 * 256) + (size_t)TT * EC) * sizeof(float);
+  auto kern = router_fused_kernel<XT, WT, TT>;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_pdl_cluster(kern, dim3(kFusedCluster, (T + TT - 1) / TT), dim3(kRouterWarps * 32), dim3(kFusedCluster, 1, 1),
+                     smem, st, static_cast<const XT*>(x), static_cast<const WT*>(wr), T, H, E, top_k, renormalize,
+                     logits, probs, topk_idx, topk_w, G, xq, xc);
+}
+
+template <typename XT, typename WT>
+void launch_fused(const void* x, const void* wr, int T, int H, int E, int top_k, int renormalize, float* logits,
+                  float* probs, int32_t* topk_idx, float* topk_w, int G, uint8_t* xq, int2* xc, cudaStream_t st) {
+  // token tiles: at least ~one CTA per SM where the batch allows
+  if (T <= 16)
+    launch_fused_tt<XT, WT, 1>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq, xc, st);
+  else if (T <= 128)
+    launch_fused_tt<XT, WT, 2>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq, xc, st);
+  else
+    launch_fused_tt<XT, WT, 4>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq, xc, st);
+}
+}  // namespace
+
+int router_device_error(bool reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_router_error, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_router_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+bool router_fused_supported(int T, int H, int E) {
+  return T > 0 && T < kBlockRouterMinTokens && E <= 256 && (size_t)4 * ((H + 255) / 256 * 256) * 4 <= kMaxTileBytes;
+}
+
 int launch_router(const void* x, int x_dtype, const void* wr, int w_dtype, int T, int H, int E,
                   int top_k, int renormalize, float* logits, float* probs, int32_t* topk_idx,
-                  float* topk_w, cudaStream_t st) {
+                  float* topk_w, cudaStream_t st, int G, uint8_t* xq, int2* xc) {
   if (T == 0) return PHMOE_OK;
+  if (router_fused_supported(T, H, E)) {
+    const bool xb = x_dtype == PHMOE_DTYPE_BF16, wb = w_dtype == PHMOE_DTYPE_BF16;
+    if (xb && wb)
+      launch_fused<__nv_bfloat16, __nv_bfloat16>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w,
+                                                 G, xq, xc, st);
+    else if (xb)
+      launch_fused<__nv_bfloat16, float>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq,
+                                         xc, st);
+    else if (wb)
+      launch_fused<float, __nv_bfloat16>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq,
+                                         xc, st);
+    else
+      launch_fused<float, float>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq, xc, st);
+    note_launches(1);
+    return xq ? kRouterEncodedX : PHMOE_OK;
+  }
   launch_router_logits(x, x_dtype, wr, w_dtype, T, H, E, logits, st);
   const int grid = (T + 7) / 8;
   if (E <= 128)
