@@ -630,6 +630,19 @@ def run_ep_prefill(args, ws, rank, device):
     def step():
         return ep.moe_layer_ep(x, wr, *wts, km, True, G, None, path="prefill", exchange=exchange)
 
+    # parity of the first call against the single-GPU prefill layer (all experts)
+    gg = torch.Generator(device=device).manual_seed(2)
+    torch.randn(Tt, Hm, device=device, generator=gg)
+    torch.randn(Em, Hm, device=device, generator=gg)
+    full13 = pm.quantize_int4(torch.randn(Em, 2 * Im, Hm, device=device, generator=gg) * 0.02, G)
+    full2 = pm.quantize_int4(torch.randn(Em, Hm, Im, device=device, generator=gg) * 0.02, G)
+    torch.cuda.empty_cache()
+    ref = pm.moe_layer(x, wr, full13[0], full13[1], full2[0], full2[1], km, path="prefill")
+    got = step()
+    mism = torch.tensor([int((got != ref).sum().item()), ref.numel()], device=device, dtype=torch.int64)
+    dist.all_reduce(mism)
+    del full13, full2, ref, got
+    torch.cuda.empty_cache()
     for _ in range(3):
         step()
     dist.barrier()
@@ -653,7 +666,59 @@ def run_ep_prefill(args, ws, rank, device):
     return {"workload": f"config 3: mixtral-8x7b moe layer prefill, {Tt} tokens over {ws} GPUs "
                         f"({T} per GPU), {Em // ws} experts per GPU, strong scaling",
             "exchange": args.ep_exchange, "tokens_per_s": Tt / (ms / 1e3), "ms_per_step": ms, "steps": steps,
-            "tflops_all_gpus": flops / (ms / 1e3) / 1e12}
+            "tflops_all_gpus": flops / (ms / 1e3) / 1e12,
+            "ep_parity": {"compared": "first call, every rank's tokens, EP prefill layer vs single-GPU prefill layer",
+                          "elements": int(mism[1].item()), "mismatches": int(mism[0].item()),
+                          "result": "bit-exact" if int(mism[0].item()) == 0 else "MISMATCH"}}
+
+
+def run_ep_stack(args, ws, rank, device):
+    """BASELINE config 4 under expert parallelism: ``--stack-ep`` (default 48)
+    Qwen3-30B-A3B-shaped MoE layers (attention omitted), 128/N experts of each
+    layer per GPU, ``--tokens`` decode tokens per GPU, the peer-memory
+    exchange in every layer; a step is one pass through the whole stack. Max
+    over ranks."""
+    import torch.distributed as dist
+    import phantom_moe as pm
+    from phantom_moe import ep
+    Ls, T = args.stack_ep, args.tokens
+    lo, hi = ep.shard_range(E, ws, rank)
+    layers = [make_layer(100 + l, device, expert_range=(lo, hi)) for l in range(Ls)]
+    g = torch.Generator(device=device).manual_seed(3000 + T + 7919 * rank)
+    x0 = torch.randn(T, H, device=device, generator=g).to(torch.bfloat16)
+    exchange = ep.PeerExchange(None, T, K_TOP, H, E)
+    stream = torch.cuda.current_stream(device)
+
+    def run_stack():
+        h = x0
+        for wr, pk in layers:
+            h = ep.moe_layer_ep(h, wr, *_pk(pk), K_TOP, True, G, None, exchange=exchange)
+        return h
+
+    for _ in range(2):
+        run_stack()
+    dist.barrier()
+    torch.cuda.synchronize()
+    steps = max(3, min(args.steps, 10))
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        run_stack()
+    ev1.record(stream)
+    ev1.synchronize()
+    dist.barrier()
+    t = torch.tensor([ev0.elapsed_time(ev1) / steps], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    exchange.close()
+    wbytes = sum(pk.w13_q.numel() + pk.w13_scales.numel() * 2 + pk.w2_q.numel() + pk.w2_scales.numel() * 2
+                 for _, pk in layers)
+    del layers
+    torch.cuda.empty_cache()
+    return {"workload": f"config 4: {Ls}-layer qwen3-30b-a3b MoE stack (MoE FFN only), decode T={T} per GPU, "
+                        f"{E // ws} experts per GPU per layer, peer exchange per layer",
+            "layers": Ls, "ms_per_step": ms, "tokens_per_s": ws * T / (ms / 1e3), "us_per_layer": ms * 1e3 / Ls,
+            "steps": steps, "packed_weight_GB_per_gpu": wbytes / 1e9}
 
 
 def run_ep_zipf(args, ws, rank, device, replicate=True):
@@ -772,6 +837,20 @@ def run_ep(args, ws, rank, device):
         return ep.moe_layer_ep(xs[l] if x is None else x, layers[l][0], *_pk(layers[l][1]), K_TOP, True, G,
                                None, stats=stats, exchange=None if stats is not None else exchange)
 
+    # parity: the first step's output on every rank against the single-GPU
+    # layer (all 128 experts) on the same tokens; the exchange returns fp32
+    # rows and every row's result is independent of its batch, so the two
+    # must agree bit for bit
+    wr0, pk0 = make_layer(1, device)
+    ref0 = pm.moe_layer(xs[0], wr0, *_pk(pk0), K_TOP, path="decode")
+    got0 = step(0)
+    mism = torch.tensor([int((got0 != ref0).sum().item()), ref0.numel()], device=device, dtype=torch.int64)
+    dist.all_reduce(mism)
+    parity = {"compared": "first step, every rank's T tokens, EP layer vs single-GPU phmoe_moe_layer with all "
+                          f"{E} experts", "elements": int(mism[1].item()), "mismatches": int(mism[0].item()),
+              "result": "bit-exact" if int(mism[0].item()) == 0 else "MISMATCH"}
+    del wr0, pk0, ref0, got0
+    torch.cuda.empty_cache()
     # imbalance and local experts hit, per layer (outside the timed region)
     hit, recv = [], []
     for l in range(L):
@@ -888,9 +967,31 @@ def run_ep(args, ws, rank, device):
                     "sync": {"value": ws * T / (ms_e2e_sync / 1e3), "ms_per_step": ms_e2e_sync,
                              "api": "the same on one stream, host synchronised after every step"}},
             "clocks": clocks, "gpu_launches": int(launches * args.steps // (args.steps + args.warmup)),
+            "ep_parity": parity,
         }
     if exchange is not None:
         exchange.close()
+    # the same layer with the token exchange as NCCL all-to-alls: split sizes
+    # read on the host every layer, and equal fixed-capacity blocks (T * k rows
+    # per rank pair, no host synchronisation)
+    nccl = None
+    if args.ep_extras and args.ep_exchange == "peer":
+        def nccl_step(i, cap=None):
+            l = i % L
+            return ep.moe_layer_ep(xs[l], layers[l][0], *_pk(layers[l][1]), K_TOP, True, G, None, path="decode",
+                                   fixed_capacity=cap)
+        ms_hc = timed(nccl_step, args.steps, args.warmup)
+        ms_fc = timed(lambda i: nccl_step(i, T * K_TOP), args.steps, args.warmup)
+        row_in, row_out = H * 2, H * 4  # bf16 rows out, fp32 results back
+        nccl = {"host_counted": {"ms_per_step": ms_hc, "tokens_per_s": ws * T / (ms_hc / 1e3),
+                                 "bytes_per_rank_per_step": int(T * K_TOP * (row_in + row_out)),
+                                 "note": "all_to_all_single with split sizes copied to the host every layer "
+                                         "(one device synchronisation per layer)"},
+                "fixed_capacity": {"ms_per_step": ms_fc, "tokens_per_s": ws * T / (ms_fc / 1e3),
+                                   "bytes_per_rank_per_step": int(ws * T * K_TOP * (row_in + row_out)),
+                                   "note": f"equal splits of T*k = {T * K_TOP} rows per rank pair, no host "
+                                           "synchronisation; the padded blocks move world x more bytes"},
+                "peer_memory_ms_per_step": ms}
     # BASELINE configs 5 and 3 at this N (every rank runs both; rank 0 reports)
     extras = {}
     if args.ep_extras:
@@ -898,11 +999,19 @@ def run_ep(args, ws, rank, device):
         torch.cuda.empty_cache()
         extras["config5_zipf"] = run_ep_zipf(args, ws, rank, device, replicate=args.ep_extras_replicate)
         extras["config3_prefill_ep"] = run_ep_prefill(args, ws, rank, device)
+        extras["config4_stack_ep"] = run_ep_stack(args, ws, rank, device)
     if rank == 0:
+        if nccl is not None:
+            line["nccl_exchange"] = nccl
         line.update(extras)
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
+    # a result that differs from the single-GPU layer is not a valid measurement
+    bad = parity["mismatches"] + extras.get("config3_prefill_ep", {}).get("ep_parity", {}).get("mismatches", 0)
+    if bad:
+        log(f"[bench] expert-parallel output differs from the single-GPU layer in {bad} elements")
+        raise SystemExit(3)
 
 
 # ---------------------------------------------------------------------------
@@ -967,12 +1076,14 @@ def build_parser() -> argparse.ArgumentParser:
     ap.add_argument("--clock-soak", type=float, default=2.0, help="seconds of sustained replay for clocks")
     ap.add_argument("--hf-generate", action="store_true",
                     help="also time transformers generate with and without install_into (an extra JSON object)")
+    ap.add_argument("--stack-ep", type=int, default=48,
+                    help="N > 1: layers of the config-4 stack leg in the default line")
     ap.add_argument("--stack", type=int, default=0,
                     help="only time a decode step through this many MoE layers (config 4 on one GPU)")
     ap.add_argument("--no-ep-extras", dest="ep_extras", action="store_false",
                     help="N > 1: skip the config-5 (Zipf) and config-3 (expert-parallel prefill) legs")
-    ap.add_argument("--ep-extras-replicate", action="store_true",
-                    help="N > 1: the default line's config-5 leg also times hot-expert replication")
+    ap.add_argument("--no-ep-extras-replicate", dest="ep_extras_replicate", action="store_false",
+                    help="N > 1: the default line's config-5 leg skips the hot-expert replication case")
     ap.add_argument("--replica-slots", type=int, default=8,
                     help="N > 1, config 5: extra expert slots per rank for copies of hot experts")
     ap.add_argument("--zipf", action="store_true",

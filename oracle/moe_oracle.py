@@ -491,16 +491,20 @@ def dispatch(idx: np.ndarray, num_experts: int):
     idx = np.asarray(idx, dtype=np.int64)
     T, k = idx.shape
     flat = idx.reshape(-1)
-    counts = np.bincount(flat, minlength=num_experts).astype(np.int32)
+    # an expert id outside [0, E) is dropped, as the CUDA dispatch drops it:
+    # no row, inverse -1 (R = the valid assignments)
+    valid = (flat >= 0) & (flat < num_experts)
+    a = np.nonzero(valid)[0]
+    counts = np.bincount(flat[a], minlength=num_experts).astype(np.int32)
     offsets = np.zeros(num_experts + 1, dtype=np.int32)
     offsets[1:] = np.cumsum(counts)
-    tok = np.repeat(np.arange(T), k)
-    slot = np.tile(np.arange(k), T)
-    order = np.lexsort((tok, flat))  # by expert, then token
+    tok = np.repeat(np.arange(T), k)[a]
+    slot = np.tile(np.arange(k), T)[a]
+    order = np.lexsort((tok, flat[a]))  # by expert, then token
     row_token = tok[order].astype(np.int32)
     row_slot = slot[order].astype(np.int32)
-    inv = np.empty(T * k, dtype=np.int32)
-    inv[order] = np.arange(T * k, dtype=np.int32)
+    inv = np.full(T * k, -1, dtype=np.int32)
+    inv[a[order]] = np.arange(a.size, dtype=np.int32)
     return counts, offsets, row_token, row_slot, inv.reshape(T, k)
 
 

@@ -344,10 +344,51 @@ class PeerExchange:
             dist.barrier(group=self.group)
 
 
+def _exchange_fixed(x, rt: Routed, recv_counts, world: int, C: int, w13_q, w13_scales, w2_q, w2_scales,
+                    group_size: int, ops, path: str, ep_group):
+    """The row exchange with equal split sizes: every rank sends every rank a
+    block of C rows (its rows for that rank's experts, then zero rows) and
+    gets C fp32 result rows back per block, so the all-to-alls need no split
+    sizes from the host and the layer no host synchronisation. C must be at
+    least the rows any rank sends to one rank (T * k always is). The padded
+    blocks carry world * C rows each way instead of the rows routed."""
+    import torch.distributed as dist
+    dev = x.device
+    per = recv_counts.numel() // world
+    off = rt.offsets.to(torch.int64)
+    starts = off[0:world * per:per]                                  # first row of each destination block
+    ends = off[per:world * per + 1:per]
+    pos = torch.arange(world * C, device=dev, dtype=torch.int64)
+    d, i = pos // C, pos % C
+    src = starts[d] + i
+    valid = src < ends[d]
+    index = torch.where(valid, rt.row_token.to(torch.int64)[src.clamp(max=max(rt.row_token.numel() - 1, 0))],
+                        torch.full_like(src, -1)).to(torch.int32) if rt.row_token.numel() else \
+        torch.full((world * C,), -1, dtype=torch.int32, device=dev)
+    send_x = ops.gather(x, index)
+    recv_x = torch.empty_like(send_x)
+    dist.all_to_all_single(recv_x, send_x, group=ep_group)
+    # local expert of every arrived row; padding rows get id `per` (dropped by the dispatch)
+    rc = recv_counts.view(world, per).to(torch.int64)
+    cum = rc.cumsum(1)                                               # [src, per]
+    eid = torch.searchsorted(cum, i.view(world, C), right=True).view(-1).to(torch.int32)
+    offsets, row_token, inv, active = ops.dispatch(eid.view(world * C, 1), per)
+    y = ops.ffn(recv_x, row_token, offsets, active, w13_q, w13_scales, w2_q, w2_scales, group_size, path)
+    y_arrived = ops.gather(y, inv.view(-1))                          # arrival order; padding rows zero
+    y_back = torch.empty_like(y_arrived)
+    dist.all_to_all_single(y_back, y_arrived, group=ep_group)
+    # assignment a's row: block of its destination, position inside the block
+    rows = rt.inv.to(torch.int64)
+    dblk = torch.searchsorted(ends, rows.view(-1), right=True).view_as(rows)
+    inv2 = torch.where(rows >= 0, dblk * C + rows - starts[dblk.clamp(max=world - 1)], torch.full_like(rows, -1))
+    return ops.combine(y_back, inv2.to(torch.int32), rt.w, x.dtype)
+
+
 def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scales, top_k: int,
                  renormalize: bool = True, group_size: int = 64, ep_group=None, *, path: str = "auto",
                  return_routing: bool = False, ops=None, stats: dict | None = None,
-                 exchange: PeerExchange | None = None, placement: Placement | None = None):
+                 exchange: PeerExchange | None = None, placement: Placement | None = None,
+                 fixed_capacity: int | None = None):
     """The MoE layer with this rank's expert shard (``w13_q`` etc. hold
     ``E/P`` experts, ``router_weight`` all ``E``). Same result as
     :func:`phantom_moe.moe_layer` on the full layer for this rank's tokens.
@@ -368,6 +409,13 @@ def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scale
     and every rank sends each expert's rows to the copy the placement assigns
     it; with ``exchange`` the placement is the one the exchange was created
     with.
+
+    ``fixed_capacity`` (all-to-all path only): exchange blocks of that many
+    rows per rank pair, with equal split sizes, so nothing is copied to the
+    host and the layer never synchronises; it must be at least the rows any
+    rank sends to one rank (``T * top_k`` of the largest rank batch always
+    is, the same value on every rank). The padded blocks move
+    ``world * fixed_capacity`` rows each way.
     """
     import torch.distributed as dist
     if exchange is not None and placement is not None and exchange.placement is not placement:
@@ -404,6 +452,17 @@ def moe_layer_ep(hidden_states, router_weight, w13_q, w13_scales, w2_q, w2_scale
     V = rt.counts.numel()  # experts (or virtual experts) over all ranks
     recv_counts = torch.empty_like(rt.counts)
     dist.all_to_all_single(recv_counts, rt.counts, group=ep_group)
+    if fixed_capacity is not None:
+        out = _exchange_fixed(x, rt, recv_counts, world, int(fixed_capacity), w13_q, w13_scales, w2_q, w2_scales,
+                              group_size, ops, path, ep_group).reshape(shape)
+        if stats is not None:  # (reads the counts on the host: outside any timed loop)
+            both = torch.cat([rt.counts, recv_counts]).cpu()
+            stats["send_rows"] = rows_per_rank(both[:V], world)
+            stats["recv_rows"] = rows_per_rank(both[V:], world)
+            stats["local_experts_hit"] = int((both[V:].view(world, -1).sum(0) > 0).sum())
+        if return_routing:
+            return out, rt.idx, rt.w
+        return out
     both = torch.cat([rt.counts, recv_counts]).cpu()
     send_rows = rows_per_rank(both[:V], world)
     recv_rows = rows_per_rank(both[V:], world)

@@ -98,7 +98,8 @@ def replica_plan(xs, wr, world: int):
     return ep.plan_replicas(load.tolist(), world, E // world)
 
 
-def gloo_worker(rank: int, world: int, port: int, case: str, out_dir: str, replicate: bool = False):
+def gloo_worker(rank: int, world: int, port: int, case: str, out_dir: str, replicate: bool = False,
+                fixed: bool = False):
     import torch.distributed as dist
     from phantom_moe import ep
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -115,8 +116,10 @@ def gloo_worker(rank: int, world: int, port: int, case: str, out_dir: str, repli
                                           ops=OracleOps(), stats=stats, placement=pl)
         else:
             lo, hi = ep.shard_range(E, world, rank)
+            cap = max(x.shape[0] for x in xs) * k if fixed else None  # the same on every rank
             out, idx, w = ep.moe_layer_ep(xs[rank], wr, p13[lo:hi], s13[lo:hi], p2[lo:hi], s2[lo:hi], k, True, G,
-                                          None, return_routing=True, ops=OracleOps(), stats=stats)
+                                          None, return_routing=True, ops=OracleOps(), stats=stats,
+                                          fixed_capacity=cap)
         np.savez(Path(out_dir) / f"rank{rank}.npz", out=out.numpy(), idx=idx.numpy(), w=w.numpy(),
                  send=np.array(stats["send_rows"]), recv=np.array(stats["recv_rows"]))
     finally:

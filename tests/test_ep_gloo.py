@@ -30,9 +30,12 @@ def _single_process(xs, wr, packed):
     return ops.combine(y, inv, w, torch.float32).numpy(), idx.numpy()
 
 
-@pytest.mark.parametrize("world,case", [(2, "ragged"), (4, "ragged"), (2, "skew"), (4, "skew")])
-def test_ep_gloo_matches_single_process(tmp_path, world, case):
-    torch.multiprocessing.start_processes(gloo_worker, args=(world, _free_port(), case, str(tmp_path)),
+@pytest.mark.parametrize("world,case,fixed", [(2, "ragged", False), (4, "ragged", False), (2, "skew", False),
+                                              (4, "skew", False), (2, "ragged", True), (4, "skew", True)])
+def test_ep_gloo_matches_single_process(tmp_path, world, case, fixed):
+    """fixed: the equal-split all-to-all (fixed_capacity) instead of the
+    host-counted one; the same output bit for bit."""
+    torch.multiprocessing.start_processes(gloo_worker, args=(world, _free_port(), case, str(tmp_path), False, fixed),
                                           nprocs=world, join=True, start_method="spawn")
     H, E, k, I, G = DIMS
     xs, wr, packed = make_case(case, world)
