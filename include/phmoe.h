@@ -137,11 +137,16 @@ int phmoe_expert_ffn_decode(const void* x, int x_dtype, const int32_t* row_token
  * the bf16 rows convert to fp16 exactly, the int4 weights are dequantised per
  * tile in shared memory to fp16_rn((nibble - 8) * scale) (the semantics of
  * gguf_loader.py:362-381 with 11 significant bits), and the SwiGLU output h
- * is rounded to fp16 between the two GEMMs. Values beyond the fp16 range
- * are clamped and reported by phmoe_device_error (bit 1). Replaces the same
- * loop as phmoe_expert_ffn_decode, for batches where every expert sees many
- * rows. Same arguments; x must be bf16; h is scratch of T*k*I*4 bytes (the
- * fp16 h uses half); y doubles as the gathered rows until the down GEMM.
+ * is rounded to fp16 between the two GEMMs. Rows of x beyond the fp16 range
+ * are stored with a power-of-two row exponent, 128-column blocks of h with a
+ * power-of-two block exponent (a short fixup pass brings a row's blocks to
+ * one exponent), and the fp32 epilogues undo both exactly, so values up to
+ * the bf16/fp32 range keep their magnitude; rows inside the fp16 range are
+ * computed exactly as without them. Replaces the same loop as
+ * phmoe_expert_ffn_decode, for batches where every expert sees many rows.
+ * Same arguments; x must be bf16; h is scratch of T*k*I*4 bytes (the fp16 h
+ * uses half, the exponents part of the rest); y doubles as the gathered rows
+ * until the down GEMM.
  * Limits: G in {32, 64}; H % 256 == 0; I % 128 == 0; E such that the tile
  * table fits in shared memory (E <= 1024).
  */
@@ -399,9 +404,9 @@ int phmoe_gguf_q4_k_dequantize(const void* blocks, long long n, float* out, void
  * Device-side error bits of the current device: 0 when all is well; bit 0
  * (1) when a pipeline wait of an FFN kernel timed out (its CTA abandoned its
  * work after a bounded wait instead of hanging); bit 1 (2) when an
- * activation or SwiGLU value could not be held and was clamped (the prefill
- * path's fp16 operands: beyond +-65504; the decode path's fixed-point rows:
- * beyond ~1e34, infinite or NaN); bit 2 (4) when an expert-parallel peer
+ * activation or SwiGLU value could not be held and was clamped (the decode
+ * path's fixed-point rows: beyond ~1e34, infinite or NaN; the prefill path
+ * has no such limit below the fp32 range); bit 2 (4) when an expert-parallel peer
  * flag did not arrive within 2 s.
  * Synchronous; reset != 0 clears it. Not part of the hot path.
  */

@@ -16,8 +16,18 @@
 // f16x2 multiply of the fp16 scale, it carries 11 significant bits instead of
 // 8 (at Mixtral's I = 14336 bf16 weights and h alone put the layer ~0.05 off
 // the fp32 result), and bf16 activations convert to fp16 exactly inside the
-// fp16 range. Activations or h beyond +-65504 are clamped to it and flagged
-// in the device error word (value 2).
+// fp16 range. Values beyond the fp16 range keep their magnitude through
+// power-of-two exponents (multiplying by 2^n is exact, so rows that stay in
+// range are untouched - exponent 0, factor 1.0):
+//   * gather: a row of x with |x| > 65504 is stored as x * 2^-sx[r] (its
+//     largest finite |x| brought into [2^15, 2^16)); the gate/up epilogue
+//     multiplies the accumulators by 2^sx[r];
+//   * gate/up: a 128-column block of h with |h| > 65504 is stored as
+//     h * 2^-eb[r, b] and raises the row's exponent er[r] (atomicMax);
+//   * fixup: blocks of a row with eb[r, b] < er[r] are rescaled to er[r]
+//     (a short kernel that reads er[] and leaves at once when all are 0);
+//   * down: the epilogue multiplies row r of y by 2^er[r].
+// Infinite and NaN inputs propagate as they would in fp32.
 //
 // Tile: 256 rows (two M=128 MMAs sharing one dequantised B tile) x 256
 // output columns (N=256: a 128x128 MMA keeps the tensor core only about half
@@ -47,6 +57,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "pipeline.cuh"
 #include "launch.h"
@@ -56,7 +68,6 @@ namespace phmoe {
 // Error bits raised by the prefill kernels (read by phmoe_device_error;
 // every writer ORs its bit in):
 //   1  a pipeline wait timed out and its CTA abandoned its work
-//   2  an activation or SwiGLU value was clamped to the fp16 range
 __device__ int g_prefill_error;
 
 namespace {
@@ -152,14 +163,17 @@ __device__ __forceinline__ void dequant_word_f16(uint32_t w, uint32_t s2, uint32
     asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[i]) : "r"(t), "r"(s2));
   }
 }
-// fp32 pair -> fp16x2, clamped to the fp16 range (flag set when clamped;
-// NaN stays NaN).
-__device__ __forceinline__ uint32_t pack_f16x2_clamped(float a, float b, bool& clamped) {
-  if (fabsf(a) > kF16Max) { a = copysignf(kF16Max, a); clamped = true; }
-  if (fabsf(b) > kF16Max) { b = copysignf(kF16Max, b); clamped = true; }
+// fp32 pair -> fp16x2 (round to nearest even); `over` is set when either
+// value lies beyond the fp16 range (and so rounds to infinity).
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b, bool& over) {
+  over |= fabsf(a) > kF16Max || fabsf(b) > kF16Max;
   const __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
+// 2^e as fp32 for e in [-126, 127] (exact).
+__device__ __forceinline__ float pow2i(int e) { return __int_as_float((127 + e) << 23); }
+// Unbiased exponent of a positive finite or infinite fp32 (128 for inf).
+__device__ __forceinline__ int exponent_of(float m) { return (int)((__float_as_uint(m) >> 23) & 0xFFu) - 127; }
 
 struct Ctl {
   uint64_t full[kLoadStages];   // A rows + raw weights landed (TMA transaction bytes)
@@ -246,6 +260,50 @@ __device__ __forceinline__ Tile tile_at(int t, int na, const int* prefix, const 
   return Tile{e, r0, n, (local % mt) * kTileM, local / mt};
 }
 
+// The SwiGLU block of one row (128 columns: gate accumulators at taddr,
+// up at taddr + 128) when some |h| exceeds the fp16 range: one pass finds
+// the largest |h|, a second stores h * 2^-eb with that value in
+// [2^14, 2^15); returns eb (0 for lanes with `over` false, which store
+// nothing). Warp-collective (tcgen05.ld).
+__device__ __noinline__ int swiglu_block_rescaled(uint32_t taddr, float rs, bool over, __half* dst_row) {
+  constexpr int kHalfN = kBN / 2;
+  float m = 0.0f;
+#pragma unroll 1
+  for (int c = 0; c < kHalfN; c += 32) {
+    uint32_t g[32], u[32];
+    tmem_ld32(taddr + c, g);
+    tmem_ld32(taddr + kHalfN + c, u);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      m = fmaxf(m, fabsf(silu_f32(__uint_as_float(g[i]) * rs) * (__uint_as_float(u[i]) * rs)));
+  }
+  const int eb = over ? exponent_of(m) - 14 : 0;
+  const float hs = pow2i(-eb);
+#pragma unroll 1
+  for (int c = 0; c < kHalfN; c += 32) {
+    uint32_t g[32], u[32];
+    tmem_ld32(taddr + c, g);
+    tmem_ld32(taddr + kHalfN + c, u);
+    tmem_ld_wait();
+    uint32_t packed[16];
+    bool unused = false;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float h0 = silu_f32(__uint_as_float(g[2 * i]) * rs) * (__uint_as_float(u[2 * i]) * rs);
+      const float h1 = silu_f32(__uint_as_float(g[2 * i + 1]) * rs) * (__uint_as_float(u[2 * i + 1]) * rs);
+      packed[i] = pack_f16x2(h0 * hs, h1 * hs, unused);
+    }
+    if (over) {
+      uint4* dst = reinterpret_cast<uint4*>(dst_row + c);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+    }
+  }
+  return eb;
+}
+
 // kGateUp: B rows of a tile are gate rows col*64.. and up rows I+col*64..
 // (wrows = 2I per expert), output h = SwiGLU as fp16 [R, n_out = I].
 // Otherwise B rows are col*128.. of [E*H, K/2] (wrows = H) and the output is
@@ -255,7 +313,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 prefill_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap w_map,
                     const uint16_t* __restrict__ w_s, const int32_t* __restrict__ offsets,
                     const int32_t* __restrict__ active, int K, int n_out, int wrows, int G,
-                    __half* __restrict__ h_out, float* __restrict__ y_out) {
+                    __half* __restrict__ h_out, float* __restrict__ y_out, const int32_t* __restrict__ row_exp,
+                    int32_t* __restrict__ h_row_exp, uint8_t* __restrict__ h_blk_exp) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Ctl* ctl = reinterpret_cast<Ctl*>(smem + kCtlOffset);
@@ -427,8 +486,17 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
         const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * kBN);
         const bool valid = tl.m0 + lrow < tl.n;
         const size_t row = (size_t)(tl.row0 + tl.m0 + lrow);
+        // row_exp[row]: 2^row_exp undoes the power-of-two scaling of this
+        // GEMM's A row (x for gate/up, h for down); 0 for rows in range.
+        const float rs = valid ? pow2i(__ldg(row_exp + row)) : 1.0f;
         if (kGateUp) {
           constexpr int kHalfN = kBN / 2;  // gate columns, then as many up columns
+          // h is stored as fp16; a row whose block went beyond the fp16
+          // range is redone by swiglu_block_rescaled (the accumulators stay
+          // in TMEM until acc_empty; tcgen05.ld is warp-collective, so the
+          // whole warp takes that call).
+          bool over = false;
+          int eb = 0;
 #pragma unroll 1
           for (int c = 0; c < kHalfN; c += 32) {
             uint32_t g[32], u[32];
@@ -436,15 +504,13 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
             tmem_ld32(taddr + kHalfN + c, u);
             tmem_ld_wait();
             uint32_t packed[16];
-            bool clamped = false;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
-              const float h0 = silu_f32(g0) * __uint_as_float(u[2 * i]);
-              const float h1 = silu_f32(g1) * __uint_as_float(u[2 * i + 1]);
-              packed[i] = pack_f16x2_clamped(h0, h1, clamped);
+              const float g0 = __uint_as_float(g[2 * i]) * rs, g1 = __uint_as_float(g[2 * i + 1]) * rs;
+              const float h0 = silu_f32(g0) * (__uint_as_float(u[2 * i]) * rs);
+              const float h1 = silu_f32(g1) * (__uint_as_float(u[2 * i + 1]) * rs);
+              packed[i] = pack_f16x2(h0, h1, over);
             }
-            if (clamped && valid) atomicOr(&g_prefill_error, 2);
             if (valid) {
               uint4* dst = reinterpret_cast<uint4*>(h_out + row * n_out + tl.col * kHalfN + c);
 #pragma unroll
@@ -452,12 +518,23 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap a_map, const __grid_cons
                 dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
             }
           }
+          over = over && valid;
+          if (__any_sync(0xffffffffu, over))
+            eb = swiglu_block_rescaled(taddr, rs, over, h_out + row * n_out + tl.col * kHalfN);
+          if (valid) {
+            h_blk_exp[row * (size_t)(n_out / kHalfN) + tl.col] = (uint8_t)eb;
+            if (eb) atomicMax(h_row_exp + row, eb);
+          }
         } else {
 #pragma unroll 1
           for (int c = 0; c < kBN; c += 32) {
             uint32_t v[32];
             tmem_ld32(taddr + c, v);
             tmem_ld_wait();
+            if (rs != 1.0f) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * rs);
+            }
             if (valid) {
               uint4* dst = reinterpret_cast<uint4*>(y_out + row * n_out + tl.col * kBN + c);
 #pragma unroll
@@ -516,13 +593,13 @@ bool make_map(CUtensorMap* map, CUtensorMapDataType dt, size_t elt, const void* 
 template <bool kGateUp>
 int launch_gemm(const CUtensorMap& a_map, const CUtensorMap& w_map, const uint16_t* w_s, const int32_t* offsets,
                 const int32_t* active, int K, int n_out, int wrows, int G, int E, __half* h_out,
-                float* y_out, cudaStream_t st) {
+                float* y_out, const int32_t* row_exp, int32_t* h_row_exp, uint8_t* h_blk_exp, cudaStream_t st) {
   auto k = prefill_gemm_kernel<kGateUp>;
   const size_t smem = prefill_smem(E);
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return PHMOE_ERR_CUDA;
   k<<<device_sm_count(), kThreads, smem, st>>>(a_map, w_map, w_s, offsets, active, K, n_out, wrows, G, h_out,
-                                               y_out);
+                                               y_out, row_exp, h_row_exp, h_blk_exp);
   note_launches(1);
   return PHMOE_OK;
 }
@@ -547,34 +624,104 @@ bool prefill_supported(int H, int I, int G, int E) {
 namespace {
 
 constexpr int kGatherThreads = 128;
+constexpr int kFixupWarps = 8;
 
-// X[r] = fp16(x[row_token[r]]) for the rows of experts (r < offsets[E]);
-// bf16 -> fp16 is exact inside the fp16 range, values beyond it are clamped
-// and flagged (device error word, value 2). One CTA per row.
+// X[r] = fp16(x[row_token[r]] * 2^-sx[r]) for the rows of experts
+// (r < offsets[E]). bf16 -> fp16 is exact inside the fp16 range, where
+// sx[r] = 0; a row with |x| > 65504 gets sx[r] = (exponent of its largest
+// finite |x|) - 15, which brings that value into [2^15, 2^16) where every
+// bf16 value is an fp16 value. Also zeroes er[r], the row's h exponent that
+// the gate/up epilogue raises. One CTA per row.
 __global__ void __launch_bounds__(kGatherThreads)
 gather_to_f16_kernel(const __nv_bfloat16* __restrict__ x, int T, const int32_t* __restrict__ row_token,
-                     const int32_t* __restrict__ offsets, int E, int H, __half* __restrict__ xg) {
+                     const int32_t* __restrict__ offsets, int E, int H, __half* __restrict__ xg,
+                     int32_t* __restrict__ sx, int32_t* __restrict__ er) {
+  __shared__ uint32_t warp_max[kGatherThreads / 32];
   const int r = blockIdx.x;
   if (r >= __ldg(offsets + E)) return;
   const int t = __ldg(row_token + r);
-  if (t < 0 || t >= T) return;
+  if (t < 0 || t >= T) {
+    if (threadIdx.x == 0) sx[r] = er[r] = 0;
+    return;
+  }
   const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)t * H);
   uint4* dst = reinterpret_cast<uint4*>(xg + (size_t)r * H);
-  bool clamped = false;
+  bool over = false;
+  uint32_t mag = 0;  // largest finite |x| of this thread, as bf16 bits (they order like the values)
   for (int c = threadIdx.x; c < H / 8; c += kGatherThreads) {
     const uint4 v = __ldg(src + c);
     const uint32_t in[4] = {v.x, v.y, v.z, v.w};
     uint32_t out[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) out[i] = pack_f16x2_clamped(bf16_lo_to_f32(in[i]), bf16_hi_to_f32(in[i]), clamped);
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t a = in[i] & 0x7FFFu, b = (in[i] >> 16) & 0x7FFFu;
+      if (a < 0x7F80u) mag = max(mag, a);
+      if (b < 0x7F80u) mag = max(mag, b);
+      out[i] = pack_f16x2(bf16_lo_to_f32(in[i]), bf16_hi_to_f32(in[i]), over);
+    }
     dst[c] = make_uint4(out[0], out[1], out[2], out[3]);
   }
-  if (clamped) atomicOr(&g_prefill_error, 2);
+  int e = 0;
+  if (__syncthreads_or(over)) {
+    mag = __reduce_max_sync(0xffffffffu, mag);
+    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = mag;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kGatherThreads / 32; ++w) mag = max(mag, warp_max[w]);
+    e = max(0, (int)(mag >> 7) - 127 - 15);
+    const float s = pow2i(-e);
+    bool unused = false;
+    for (int c = threadIdx.x; c < H / 8; c += kGatherThreads) {
+      const uint4 v = __ldg(src + c);
+      const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+      uint32_t out[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) out[i] = pack_f16x2(bf16_lo_to_f32(in[i]) * s, bf16_hi_to_f32(in[i]) * s, unused);
+      dst[c] = make_uint4(out[0], out[1], out[2], out[3]);
+    }
+  }
+  if (threadIdx.x == 0) {
+    sx[r] = e;
+    er[r] = 0;
+  }
+}
+
+// Rows whose 128-column blocks of h were stored with different exponents:
+// block b of row r holds h * 2^-eb[r, b]; rescale the blocks below the row's
+// exponent er[r] to it (exact unless a value falls into the fp16 subnormals).
+// One warp per row, 4 halves per lane per block; rows with er[r] = 0 - all
+// of them unless something exceeded the fp16 range - cost one load.
+__global__ void __launch_bounds__(kFixupWarps * 32)
+h_fixup_kernel(const int32_t* __restrict__ offsets, int E, const int32_t* __restrict__ er,
+               const uint8_t* __restrict__ eb, int I, __half* __restrict__ h) {
+  const int rows = __ldg(offsets + E);
+  const int nblk = I / (kBN / 2);
+  const int lane = threadIdx.x & 31;
+  for (int r = blockIdx.x * kFixupWarps + (threadIdx.x >> 5); r < rows; r += gridDim.x * kFixupWarps) {
+    const int e = __ldg(er + r);
+    if (e == 0) continue;
+    for (int b = 0; b < nblk; ++b) {
+      const int d = e - (int)__ldg(eb + (size_t)r * nblk + b);
+      if (d <= 0) continue;
+      const float s = pow2i(-d);
+      uint2* p = reinterpret_cast<uint2*>(h + (size_t)r * I + b * (kBN / 2)) + lane;
+      uint2 v = *p;
+      __half2* hv = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float2 f = __half22float2(hv[i]);
+        hv[i] = __floats2half2_rn(f.x * s, f.y * s);
+      }
+      *p = v;
+    }
+  }
 }
 
 }  // namespace
 
-// x is bf16 [T, H]; h is scratch of R*I*4 bytes (fp16 h uses the first half);
+// x is bf16 [T, H]; h is scratch of R*I*4 bytes: the fp16 h [R, I], then the
+// row exponents sx[R] and er[R] (int32) and the block exponents
+// eb[R, I/128] (uint8), which need 8 + I/128 <= 2*I bytes per row;
 // y [R, H] fp32 doubles as the gathered fp16 activation rows until the down GEMM.
 int launch_ffn_prefill(const void* x, const int32_t* row_token, const int32_t* offsets, const int32_t* active,
                        const uint8_t* w13_q, const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s,
@@ -584,8 +731,11 @@ int launch_ffn_prefill(const void* x, const int32_t* row_token, const int32_t* o
   if (R == 0) return PHMOE_OK;
   __half* xg = reinterpret_cast<__half*>(y);
   __half* hb = reinterpret_cast<__half*>(h);
+  int32_t* sx = reinterpret_cast<int32_t*>(hb + (size_t)R * I);
+  int32_t* er = sx + R;
+  uint8_t* eb = reinterpret_cast<uint8_t*>(er + R);
   gather_to_f16_kernel<<<R, kGatherThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), T, row_token, offsets, E,
-                                                      H, xg);
+                                                      H, xg, sx, er);
   note_launches(1);
   CUtensorMap a1, w1, a2, w2;
   if (!make_map(&a1, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xg, H, R, kBK, kTileM, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -595,9 +745,13 @@ int launch_ffn_prefill(const void* x, const int32_t* row_token, const int32_t* o
       !make_map(&w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w2_q, I / 2, (uint64_t)E * H, kBK / 2, kBN,
                 CU_TENSOR_MAP_SWIZZLE_NONE))
     return PHMOE_ERR_CUDA;
-  if (int s = launch_gemm<true>(a1, w1, w13_s, offsets, active, H, I, 2 * I, G, E, hb, nullptr, st)) return s;
+  if (int s = launch_gemm<true>(a1, w1, w13_s, offsets, active, H, I, 2 * I, G, E, hb, nullptr, sx, er, eb, st))
+    return s;
+  const int fixup_ctas = std::min((R + kFixupWarps - 1) / kFixupWarps, device_sm_count() * 8);
+  h_fixup_kernel<<<fixup_ctas, kFixupWarps * 32, 0, st>>>(offsets, E, er, eb, I, hb);
+  note_launches(1);
   if (mid_event) cudaEventRecord(mid_event, st);
-  return launch_gemm<false>(a2, w2, w2_s, offsets, active, I, H, H, G, E, nullptr, y, st);
+  return launch_gemm<false>(a2, w2, w2_s, offsets, active, I, H, H, G, E, nullptr, y, er, nullptr, nullptr, st);
 }
 
 }  // namespace phmoe

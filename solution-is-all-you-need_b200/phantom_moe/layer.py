@@ -101,7 +101,7 @@ class DeviceError(RuntimeError):
 
 DEVICE_ERROR_BITS = {
     1: "an FFN pipeline wait timed out (its CTA abandoned its work; results are incomplete)",
-    2: "a value left the fp16 range of the FFN operands (activations or SwiGLU output) and was clamped",
+    2: "an activation could not be held by the decode FFN's fixed-point rows (beyond ~1e34, inf or NaN)",
     4: "an expert-parallel peer flag did not arrive within 2 s (a peer stopped calling the layer)",
 }
 

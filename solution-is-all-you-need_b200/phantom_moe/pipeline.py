@@ -65,8 +65,8 @@ class HostPipeline:
             raise ValueError(f"HostPipeline runs on a CUDA device (got {dev})")
         self.T, self.H, self.dtype, self.device, self.depth = T, H, dtype, dev, depth
         # zeroed: capturing a slot's graph runs the layer once on the slot, and
-        # uninitialised memory can hold values beyond the fp16 range, which the
-        # layer clamps and reports in the device error word
+        # uninitialised memory can hold inf or NaN, which the decode layer
+        # reports in the device error word
         self.x = [torch.zeros(T, H, dtype=dtype, device=dev) for _ in range(depth)]
         self.out = [torch.zeros(T, H, dtype=dtype, device=dev) for _ in range(depth)]
         self.copy_in = torch.cuda.Stream(device=dev)

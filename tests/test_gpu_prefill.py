@@ -216,3 +216,75 @@ def test_decode_batch_invariance_few_experts(cuda_device):
         assert torch.equal(small, big[:n]), n
     mx, mr, _ = _layer_vs_torch(dev, E, H, k, I, G, T, 31, "decode")
     assert mx <= O.MAX_ABS_TOL and mr <= O.MEAN_REL_TOL, (mx, mr)
+
+
+def _row_scaled_parity(got, ref):
+    """parity_stats with every row divided by its own largest |reference|:
+    rows of very different magnitude are each held to the contract."""
+    s = np.maximum(np.abs(ref).max(axis=1, keepdims=True), 1e-30)
+    return O.parity_stats(got / s, ref / s)
+
+
+def _large_layer(dev, E=32, H=1024, I=512, G=64, seed=11):
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    wr = (torch.randn(E, H, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+    pk = pm.pack_experts(torch.randn(E, 2 * I, H, device=dev, generator=gen) * 0.02,
+                         torch.randn(E, H, I, device=dev, generator=gen) * 0.02, G)
+    return wr, pk, gen
+
+
+def _prefill_vs_oracle(x, wr, pk, k, G):
+    out, idx, _ = pm.moe_layer(x, wr, pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, k, group_size=G,
+                               path="prefill", return_routing=True, check_errors=True)
+    host = [t.cpu().numpy() for t in (pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales)]
+    ref, i_ref, _ = O.moe_layer_reference_packed(x.float().cpu().numpy(), wr.float().cpu().numpy(), *host, k, G)
+    assert np.array_equal(idx.cpu().numpy(), i_ref)
+    got = out.float().cpu().numpy()
+    assert np.all(np.isfinite(got))
+    return got, ref
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("scale", [1e3, 1e5, 1e6])
+def test_prefill_layer_activations_beyond_fp16(cuda_device, scale):
+    """At 1e3 the activations fit fp16 but the SwiGLU output (~1e5) does not;
+    at 1e5-1e6 both are beyond it (h ~1e9-1e11). Rows of x and 128-column
+    blocks of h take power-of-two exponents, so the prefill layer matches the
+    fp32 oracle within the contract tolerance taken relative to each row's
+    scale, and no device error bit is raised."""
+    dev = cuda_device
+    T, k, G = 300, 4, 64
+    wr, pk, gen = _large_layer(dev, G=G)
+    x = (torch.randn(T, 1024, device=dev, generator=gen) * scale).to(torch.bfloat16)
+    got, ref = _prefill_vs_oracle(x, wr, pk, k, G)
+    mx, mr = _row_scaled_parity(got, ref)
+    assert mx <= O.MAX_ABS_TOL and mr <= O.MEAN_REL_TOL, (mx, mr)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("G", [32, 64])
+def test_prefill_outlier_rows_and_features(cuda_device, G):
+    """A batch of ordinary rows with outliers mixed in: 8 rows scaled by 1e5,
+    8 by 2e3 (h alone beyond fp16), and 6 rows with one feature at 3e5 (a
+    "massive activation"). Within a row the h blocks then need different
+    exponents, which the fixup pass brings to the row's largest. Ordinary rows
+    give bit-identical output to the same rows run without the outliers."""
+    dev = cuda_device
+    T, k = 257, 4
+    wr, pk, gen = _large_layer(dev, G=G, seed=5)
+    base = torch.randn(T, 1024, device=dev, generator=gen)
+    x = base.clone()
+    x[3:11] *= 1e5
+    x[40:48] *= 2e3
+    x[100:106, 17] = 3e5
+    x = x.to(torch.bfloat16)
+    got, ref = _prefill_vs_oracle(x, wr, pk, k, G)
+    mx, mr = _row_scaled_parity(got, ref)
+    assert mx <= O.MAX_ABS_TOL and mr <= O.MEAN_REL_TOL, (mx, mr)
+    plain = pm.moe_layer(base.to(torch.bfloat16), wr, pk.w13_q, pk.w13_scales, pk.w2_q, pk.w2_scales, k,
+                         group_size=G, path="prefill", check_errors=True).float().cpu().numpy()
+    keep = np.ones(T, dtype=bool)
+    keep[3:11] = keep[40:48] = keep[100:106] = False
+    # routing of a row depends only on that row; the FFN rows of other tokens
+    # share tiles but not accumulators
+    assert np.array_equal(got[keep], plain[keep])
