@@ -639,6 +639,7 @@ int phmoe_ep_layer_ex(void* ctx, const void* x, int x_dtype, const void* router_
     return fail(PHMOE_ERR_INVALID_ARG, "null pointer argument");
   if (!aligned(x, 16) || !aligned(router_w, 16) || !aligned(w13_q, 16) || !aligned(w2_q, 16) || !aligned(out, 16))
     return fail(PHMOE_ERR_ALIGNMENT, "x, router_w, packed weights and out must be 16-byte aligned");
+  if (!aligned(w13_s, 4) || !aligned(w2_s, 4)) return fail(PHMOE_ERR_ALIGNMENT, "scales must be 4-byte aligned");
   if (!aligned(workspace, kAlign)) return fail(PHMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   const size_t need = ep_workspace_bytes(c, I);
   if (workspace_bytes < need) return fail(PHMOE_ERR_WORKSPACE, "workspace needs %zu bytes (got %zu)", need, workspace_bytes);

@@ -1105,47 +1105,44 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
 }
 
 // ---------------------------------------------------------------------------
-// down projection, TMA-fed form (I % 256 == 0)
+// down projection, TMA-fed form (I % 256 == 0, H % 256 == 0)
 // ---------------------------------------------------------------------------
-// Item = (expert, 128 output rows, pass of 8 tokens); task = one 512-element
-// K chunk. A producer warp copies per task one TMA box of weights (128 rows x
-// 2 x 128 bytes, 128-byte swizzle), the matching scales (a TMA box when the
-// scale rows are 16-byte aligned, else one bulk copy of the block's
-// contiguous scale rows, else 4-byte async copies), the fx h rows of the
-// pass (one TMA box: 8 blocks of 64 elements x 8 rows, 128-byte swizzle) and
-// their fx constants (8-byte async copies into [group][token]). Consumer
-// warp w owns 16-row group w%8 and K half w/8; the two halves are summed
-// (fixed order) at the item's end.
-constexpr int kDnRows = 128;
-constexpr int kDnKc = 512;
-constexpr int kDnScaleBytes = 4096;  // scale region of a stage
+// Item = (expert, 256 output rows, pass of 8 tokens); task = one 256-element
+// K chunk (one 128-byte chunk of every weight row, 32 KB). A producer warp
+// copies per task one TMA box of weights (256 rows x 128 bytes, 128-byte
+// swizzle), the fx h rows of the pass (one TMA box: 4 blocks of 64 elements
+// x 8 rows, 128-byte swizzle), the rows' scale slices (8- or 16-byte async
+// copies, one per weight row) and the fx constants (8-byte async copies into
+// [group][token]). Consumer warp w owns output rows 16w..16w+15 and every
+// group of the task, so all 16 warps do equal work for any I that is a
+// multiple of 256, and each warp's accumulators hold its rows' whole K: the
+// item ends with a plain store, no cross-warp sum.
+constexpr int kDnRows = 256;
+constexpr int kDnKc = 256;
 
 template <int S>
 struct DnCtl {
   uint64_t full[S];
   uint64_t empty[S];
-  uint64_t red_full[16];   // [buf][rg]
-  uint64_t red_empty[16];
   int abort_flag;
 };
 
-template <int G>
+template <int G, int NS>
 struct DnCfg {
-  static constexpr int kGph = 256 / G;                 // groups per consumer warp per task
-  static constexpr int kCg = kDnKc / G;                // groups per task
-  static constexpr int kW = 0;                         // [2 chunks][128 rows][128 B]
-  static constexpr int kS = 2 * kDnRows * 128;         // scales
-  static constexpr int kB = kS + kDnScaleBytes;        // [8 blocks of 64][8 rows][128 B]
-  static constexpr int kPlane = 8 * kTok * 128;
-  static constexpr int kC = kB + kPlane;               // [kCg groups][8 tokens] int2
+  static constexpr int kGt = kDnKc / G;                // groups per task
+  static constexpr int kW = 0;                         // [256 rows][128 B]
+  static constexpr int kS = kDnRows * 128;             // [256 rows][kGt] fp16 scales
+  static constexpr int kB = kS + kDnRows * kGt * 2;    // [4 blocks of 64][8 rows][128 B]
+  static constexpr int kPlane = (kDnKc / 64) * kTok * 128;
+  static constexpr int kC = kB + kPlane;               // [kGt groups][8 tokens] int2
   // stages start on 1024-byte boundaries: the 128-byte swizzle of the TMA
   // boxes (weights, h) is a function of the shared-memory address bits 7-9
-  static constexpr int kStage = (kC + kCg * kTok * 8 + 1023) / 1024 * 1024;
-  static constexpr int kStages = 4;
-  static constexpr int kRed = 8 * 32 * 16;             // [rg][lane][4 floats]
+  static constexpr int kStage = (kC + kGt * kTok * 8 + 1023) / 1024 * 1024;
+  static constexpr int kStages = NS;
   static constexpr size_t smem(int E) {
-    return 1024 + (size_t)kStages * kStage + 2 * kRed + sizeof(DnCtl<kStages>) + (size_t)(4 * E + 4) * 4;
+    return 1024 + (size_t)kStages * kStage + sizeof(DnCtl<kStages>) + (size_t)(4 * E + 4) * 4;
   }
+  static_assert(kS % 1024 == 0 && kB % 1024 == 0, "TMA destinations must keep the swizzle phase");
 };
 
 // fx words of group g (within a task) for token row r from the h box laid
@@ -1164,39 +1161,35 @@ __device__ __forceinline__ FxB<G> lds_fxb_swz(const uint8_t* plane, int g, int r
   return b;
 }
 
-template <int G>
+// s_vec: the scale slice of a row for one task (kGt halves: 8 bytes for
+// G = 64, 16 for G = 32) is copied with one async copy when w2_s and the
+// scale rows allow it, else as 4-byte pairs.
+template <int G, int NS>
 __global__ void __launch_bounds__(kGuThreads, 1)
-ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap s_map,
-                    const __grid_constant__ CUtensorMap h_map, int s_mode, const int2* __restrict__ hc, int R,
-                    const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
-                    const uint16_t* __restrict__ w2_s, int H, int I, int E, float* __restrict__ y) {
+ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap h_map,
+                    int s_vec, const int2* __restrict__ hc, int R, const int32_t* __restrict__ offsets,
+                    const int32_t* __restrict__ active, const uint16_t* __restrict__ w2_s, int H, int I, int E,
+                    float* __restrict__ y) {
   pdl_begin();
-  using C = DnCfg<G>;
+  using C = DnCfg<G, NS>;
   constexpr int S = C::kStages;
+  constexpr int kGt = C::kGt;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* red = reinterpret_cast<float*>(smem + S * C::kStage);  // [2][rg][lane][4]
-  DnCtl<S>* ctl = reinterpret_cast<DnCtl<S>*>(smem + S * C::kStage + 2 * C::kRed);
+  DnCtl<S>* ctl = reinterpret_cast<DnCtl<S>*>(smem + S * C::kStage);
   int* mbase = reinterpret_cast<int*>(ctl + 1);
   const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
   volatile int* abort_flag = &ctl->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles = H / kDnRows;
   const int NG = I / G;
-  const int nkc = (I + kDnKc - 1) / kDnKc;
+  const int nkc = I / kDnKc;
   const int na = active[0];
-  // scale rows in shared memory: s_mode 0 = TMA box / async copies of the
-  // task's groups; 1 = every group of the block (one bulk copy)
-  const int srow = s_mode == 1 ? NG * 2 : (kDnKc / G) * 2;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_u32(&ctl->full[s]), 1 + 32);
       mbar_init(smem_u32(&ctl->empty[s]), kConsumers);
-    }
-    for (int i = 0; i < 16; ++i) {
-      mbar_init(smem_u32(&ctl->red_full[i]), 1);
-      mbar_init(smem_u32(&ctl->red_empty[i]), 1);
     }
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -1211,36 +1204,35 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
     // ---------------- producer warp ----------------
     Cursor cu = cursor_at(q0, na, tiles, meta);
     int issued = 0;
-    const uint32_t sbytes_block = (uint32_t)kDnRows * (uint32_t)NG * 2;
     for (int t = 0; t < ntask; ++t) {
       const int s = t % S;
       if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
       const int k0 = cu.kc * kDnKc;
-      const int kel = min(kDnKc, I - k0);
       const uint32_t full = smem_u32(&ctl->full[s]);
       uint8_t* st = smem + s * C::kStage;
       const int wrow = meta.e[cu.slot] * H + cu.tile * kDnRows;
       const int hrow = meta.row0[cu.slot] + cu.pass * kTok;
-      const uint32_t sbytes = s_mode == 0 ? (uint32_t)kDnRows * (kDnKc / G) * 2 : (s_mode == 1 ? sbytes_block : 0u);
-      if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(2 * kDnRows * 128) + sbytes + (uint32_t)C::kPlane);
+      if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(kDnRows * 128 + C::kPlane));
       __syncwarp();
-      if (lane == 0) tma_load_3d(smem_u32(st + C::kW), &w_map, 0, wrow, k0 / 256, full);
+      if (lane == 0) tma_load_3d(smem_u32(st + C::kW), &w_map, 0, wrow, cu.kc, full);
       if (lane == 1) tma_load_3d(smem_u32(st + C::kB), &h_map, 0, hrow, k0 / 64, full);
-      if (s_mode == 0) {
-        if (lane == 3) tma_load_2d(smem_u32(st + C::kS), &s_map, k0 / G, wrow, full);
-      } else if (s_mode == 1) {
-        if (lane == 3) bulk_g2s(smem_u32(st + C::kS), w2_s + (size_t)wrow * NG, sbytes_block, full);
+      const uint16_t* sbase = w2_s + (size_t)wrow * NG + k0 / G;
+      if (s_vec) {
+#pragma unroll
+        for (int rr = lane; rr < kDnRows; rr += 32) {
+          const uint32_t dst = smem_u32(st + C::kS + rr * kGt * 2);
+          if constexpr (G == 64) cp_async8(dst, sbase + (size_t)rr * NG);
+          else cp_async16(dst, sbase + (size_t)rr * NG);
+        }
       } else {
-        constexpr int kPairs = kDnKc / G / 2;
-        for (int q = lane; q < kDnRows * kPairs; q += 32) {
-          const int rr = q / kPairs, pp = q - rr * kPairs;
-          if (pp * 2 * G < kel)
-            cp_async4(smem_u32(st + C::kS + rr * srow + pp * 4), w2_s + (size_t)(wrow + rr) * NG + k0 / G + 2 * pp);
+        for (int q = lane; q < kDnRows * (kGt / 2); q += 32) {
+          const int rr = q / (kGt / 2), pp = q - rr * (kGt / 2);
+          cp_async4(smem_u32(st + C::kS + rr * kGt * 2 + pp * 4), sbase + (size_t)rr * NG + 2 * pp);
         }
       }
-      for (int q = lane; q < C::kCg * kTok; q += 32) {  // fx constants, transposed to [group][token]
+      for (int q = lane; q < kGt * kTok; q += 32) {  // fx constants, transposed to [group][token]
         const int tt = q & (kTok - 1), j = q >> 3;
-        if (hrow + tt < R && j * G < kel)
+        if (hrow + tt < R)
           cp_async8(smem_u32(st + C::kC + (j * kTok + tt) * 8), hc + (size_t)(hrow + tt) * NG + k0 / G + j);
       }
       cp_async_arrive_noinc(full);
@@ -1255,60 +1247,41 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
   }
 
   // ---------------- consumer warps ----------------
-  const int rg = warp & 7, kh = warp >> 3;
   const int r = lane >> 2, c = lane & 3;
-  const int lr0 = rg * 16 + r;
+  const int lr0 = warp * 16 + r;
   const int a_off = (G == 64) ? 8 * c : 4 * c;
+  // row lr0 + 8 has the swizzle phase of row lr0 and lies 8 x 128 bytes further
+  int ow0[kGt];
+#pragma unroll
+  for (int g = 0; g < kGt; ++g) ow0[g] = C::kW + swz_off_rows(lr0, g * (G / 2) + a_off, kDnRows);
   Cursor cu = cursor_at(q0, na, tiles, meta);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  int item = 0;
   for (int t = 0; t < ntask; ++t) {
     const int s = t % S;
     if (cu.kc == 0) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[q] = 0.f;
     }
-    const int ngt = min(kDnKc, I - cu.kc * kDnKc) / G;
     if (!wait_phase(smem_u32(&ctl->full[s]), (t / S) & 1, abort_flag)) return;
     const uint8_t* st = smem + s * C::kStage;
     const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
-    const int goff = s_mode == 1 ? cu.kc * (kDnKc / G) : 0;
 #pragma unroll
-    for (int j = 0; j < C::kGph; ++j) {
-      const int g = kh * C::kGph + j;
-      if (g < ngt) {
-        const int kb = g * (G / 2) + a_off;
-        const RowWords<G> a0 = lds_row<G>(st + C::kW + swz_off_rows(lr0, kb, kDnRows));
-        const RowWords<G> a8 = lds_row<G>(st + C::kW + swz_off_rows(lr0 + 8, kb, kDnRows));
-        const FxB<G> b = lds_fxb_swz<G>(st + C::kB, g, r, c);
-        const int4 cc = *reinterpret_cast<const int4*>(st + C::kC + (g * kTok + 2 * c) * 8);
-        fx_group_tile<G>(a0, a8, b, cc, __half2float(sc[(lr0 * srow) / 2 + goff + g]),
-                         __half2float(sc[((lr0 + 8) * srow) / 2 + goff + g]), acc);
-      }
+    for (int g = 0; g < kGt; ++g) {
+      const RowWords<G> a0 = lds_row<G>(st + ow0[g]);
+      const RowWords<G> a8 = lds_row<G>(st + ow0[g] + 8 * 128);
+      const FxB<G> b = lds_fxb_swz<G>(st + C::kB, g, r, c);
+      const int4 cc = *reinterpret_cast<const int4*>(st + C::kC + (g * kTok + 2 * c) * 8);
+      fx_group_tile<G>(a0, a8, b, cc, __half2float(sc[lr0 * kGt + g]), __half2float(sc[(lr0 + 8) * kGt + g]), acc);
     }
     warp_arrive(smem_u32(&ctl->empty[s]), lane);
     if (cu.kc == nkc - 1) {
-      const int buf = item & 1, use = item >> 1;
-      const int bi = buf * 8 + rg;
-      float4* rb = reinterpret_cast<float4*>(red + (size_t)buf * (C::kRed / 4)) + rg * 32 + lane;
-      if (kh == 1) {
-        if (use > 0 && !wait_phase(smem_u32(&ctl->red_empty[bi]), (use - 1) & 1, abort_flag)) return;
-        *rb = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        warp_arrive(smem_u32(&ctl->red_full[bi]), lane);
-      } else {
-        if (!wait_phase(smem_u32(&ctl->red_full[bi]), use & 1, abort_flag)) return;
-        const float4 o = *rb;
-        warp_arrive(smem_u32(&ctl->red_empty[bi]), lane);
-        const float v[4] = {acc[0] + o.x, acc[1] + o.y, acc[2] + o.z, acc[3] + o.w};
-        const int n = meta.n[cu.slot], row0 = meta.row0[cu.slot];
+      const int n = meta.n[cu.slot], row0 = meta.row0[cu.slot];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int hr = cu.tile * kDnRows + lr0 + (q >= 2 ? 8 : 0);
-          const int rr = cu.pass * kTok + 2 * c + (q & 1);
-          if (rr < n) y[(size_t)(row0 + rr) * H + hr] = v[q];
-        }
+      for (int q = 0; q < 4; ++q) {
+        const int hr = cu.tile * kDnRows + lr0 + (q >= 2 ? 8 : 0);
+        const int rr = cu.pass * kTok + 2 * c + (q & 1);
+        if (rr < n) y[(size_t)(row0 + rr) * H + hr] = acc[q];
       }
-      ++item;
     }
     cursor_next(cu, tiles, nkc, meta);
   }
@@ -1568,17 +1541,18 @@ template <int G>
 bool launch_down_tma(const uint8_t* hq, const int2* hc, long long R, const int32_t* offsets, const int32_t* active,
                      const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, float* y, int grid,
                      cudaStream_t st) {
-  if (I % 256 || H % kDnRows || R <= 0 || R > (1LL << 30)) return false;
-  const size_t smem = DnCfg<G>::smem(E);
+  if (I % kDnKc || H % kDnRows || R <= 0 || R > (1LL << 30)) return false;
+  const bool five = DnCfg<G, 5>::smem(E) <= kMaxSmem;  // five stages where they fit, else four
+  const size_t smem = five ? DnCfg<G, 5>::smem(E) : DnCfg<G, 4>::smem(E);
   if (smem > kMaxSmem) return false;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return false;
-  alignas(64) CUtensorMap wm, sm, hm;
-  const cuuint32_t e3[3] = {1, 1, 1}, e2[2] = {1, 1};
-  {
+  alignas(64) CUtensorMap wm, hm;
+  const cuuint32_t e3[3] = {1, 1, 1};
+  {  // weights as [I/256 chunks][E*H rows][128 bytes]
     const cuuint64_t dims[3] = {128, (cuuint64_t)E * H, (cuuint64_t)(I / 256)};
     const cuuint64_t strides[2] = {(cuuint64_t)(I / 2), 128};
-    const cuuint32_t box[3] = {128, (cuuint32_t)kDnRows, 2};
+    const cuuint32_t box[3] = {128, (cuuint32_t)kDnRows, 1};
     if (enc(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(w2_q), dims, strides, box, e3,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -1587,31 +1561,27 @@ bool launch_down_tma(const uint8_t* hq, const int2* hc, long long R, const int32
   {  // fx h rows viewed as 16-bit elements: [I/64 blocks][R rows][64]
     const cuuint64_t dims[3] = {64, (cuuint64_t)R, (cuuint64_t)(I / 64)};
     const cuuint64_t strides[2] = {(cuuint64_t)I * 2, 128};
-    const cuuint32_t box[3] = {64, (cuuint32_t)kTok, 8};
+    const cuuint32_t box[3] = {64, (cuuint32_t)kTok, (cuuint32_t)(kDnKc / 64)};
     if (enc(&hm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint8_t*>(hq), dims, strides, box, e3,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return false;
   }
-  const int NG = I / G;
-  int s_mode = 2;
-  memset(&sm, 0, sizeof(sm));
-  if ((NG * 2) % 16 == 0) {
-    const cuuint64_t dims[2] = {(cuuint64_t)NG, (cuuint64_t)E * H};
-    const cuuint64_t strides[1] = {(cuuint64_t)NG * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)(kDnKc / G), (cuuint32_t)kDnRows};
-    if (enc(&sm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(w2_s), dims, strides, box, e2,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
-      s_mode = 0;
+  // one 8- (G = 64) or 16-byte (G = 32) copy per row's scale slice: the
+  // slice starts at (row * I/G + k0/G) * 2 bytes, a multiple of the copy size
+  // when w2_s is 16-byte aligned (I % 256 == 0 makes I/G a multiple of 4 or 8)
+  const int s_vec = (reinterpret_cast<uintptr_t>(w2_s) & 15) == 0 ? 1 : 0;
+  if (five) {
+    auto k = ffn_down_tma_kernel<G, 5>;
+    set_smem(k, smem);
+    launch_pdl(k, dim3(grid), dim3(kGuThreads), smem, st, wm, hm, s_vec, hc, (int)R, offsets, active, w2_s, H, I,
+               E, y);
+  } else {
+    auto k = ffn_down_tma_kernel<G, 4>;
+    set_smem(k, smem);
+    launch_pdl(k, dim3(grid), dim3(kGuThreads), smem, st, wm, hm, s_vec, hc, (int)R, offsets, active, w2_s, H, I,
+               E, y);
   }
-  if (s_mode == 2 && (size_t)kDnRows * NG * 2 <= (size_t)kDnScaleBytes &&
-      (reinterpret_cast<uintptr_t>(w2_s) & 15) == 0)
-    s_mode = 1;
-  auto k = ffn_down_tma_kernel<G>;
-  set_smem(k, smem);
-  launch_pdl(k, dim3(grid), dim3(kGuThreads), smem, st, wm, sm, hm, s_mode, hc, (int)R, offsets, active, w2_s, H, I,
-             E, y);
   return true;
 }
 

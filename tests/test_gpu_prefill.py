@@ -163,6 +163,16 @@ def test_decode_multi_token_items(cuda_device, T):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("T,I", [(5, 768), (64, 512), (64, 768)])
+def test_decode_group32(cuda_device, T, I):
+    """Decode path with 32-element scale groups at Qwen3's hidden size: the
+    down projection's 256-element K tasks hold 8 groups, and I = 768 takes
+    three tasks per item."""
+    mx, mr, _ = _layer_vs_torch(cuda_device, 32, 2048, 4, I, 32, T, 21, "decode")
+    assert mx <= O.MAX_ABS_TOL and mr <= O.MEAN_REL_TOL, (mx, mr)
+
+
+@pytest.mark.gpu
 def test_decode_multi_token_fp32_activations(cuda_device):
     """fp32 activations through the multi-token items."""
     dev = cuda_device
