@@ -85,7 +85,8 @@ namespace {
 constexpr int kConsumers = 16;                  // consumer (MMA) warps
 constexpr int kGuThreads = (kConsumers + 1) * 32;  // + 1 producer warp (down kernel)
 constexpr int kEpiWarps = 4;                    // gate/up epilogue warps (one per 16-row group)
-constexpr int kRbThreads = (kConsumers + kEpiWarps + 1) * 32;  // gate/up row-block kernel
+constexpr int kRbProducers = 3;                // gate/up row-block kernel: weights+scales, x rows, constants
+constexpr int kRbThreads = (kConsumers + kEpiWarps + kRbProducers) * 32;
 constexpr int kDownThreads = 16 * 32;
 constexpr int kTok = 8;                         // tokens per pass (the MMA N dimension)
 constexpr uint32_t kSpinLimit = 1u << 24;       // try_wait polls before giving up
@@ -581,7 +582,9 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&ctl->full[s]), 1 + 32);  // expect_tx arrival + one cp.async arrival per lane
+      // expect_tx arrivals of the weight and x producers + one cp.async
+      // arrival per lane of the constants producer
+      mbar_init(smem_u32(&ctl->full[s]), 2 + 32);
       mbar_init(smem_u32(&ctl->empty[s]), kConsumers);
     }
     for (int i = 0; i < 8; ++i) {
@@ -649,66 +652,78 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
     return;
   }
 
-  if (warp == kConsumers + kEpiWarps) {
-    // ---------------- producer warp ----------------
+  if (warp >= kConsumers + kEpiWarps) {
+    // ---------------- producer warps ----------------
+    // Issuing a copy waits behind the consumers' shared-memory loads (about
+    // 150 cycles per TMA or bulk instruction at full load), so the copies of
+    // a task are split over three warps that issue side by side: role 0 the
+    // weight and scale boxes, role 1 the fx rows of x, role 2 the fx
+    // constants (and the scales when they go by 4-byte async copies).
+    const int role = warp - kConsumers - kEpiWarps;
     Cursor cu = cursor_at(q0, na, tiles, meta);
     auto token = [&](const Cursor& k) -> int {  // lane holds the token id of pass row lane % 8
       const int rr = k.pass * kTok + (lane & (kTok - 1));
       return rr < meta.n[k.slot] ? __ldg(row_token + meta.row0[k.slot] + rr) : -1;
     };
-    int tok = token(cu);
+    int tok = role != 0 ? token(cu) : -1;
     int issued = 0;
     for (int t = 0; t < ntask; ++t) {
       const int s = t % S;
       if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
       Cursor nx = cu;
       cursor_next(nx, tiles, nkc, meta);
-      const int tok_next = (t + 1 < ntask && nx.kc == 0) ? token(nx) : tok;
+      const int tok_next = (role != 0 && t + 1 < ntask && nx.kc == 0) ? token(nx) : tok;
       const int k0 = cu.kc * kRbKc;
       const int kel = min(kRbKc, H - k0);
       const int nt = min(kTok, meta.n[cu.slot] - cu.pass * kTok);
       const uint32_t full = smem_u32(&ctl->full[s]);
       uint8_t* st = smem + s * C::kStage;
-      if (lane == 0)
-        mbar_arrive_expect_tx(full, 2u * (uint32_t)(box_chunks * kRbRows * 128) + (uint32_t)(nt * kel * 2) +
-                                        (s_tma ? 2u * kRbRows * C::kScaleRow : 0u));
-      __syncwarp();
       const int grow = meta.e[cu.slot] * 2 * I + cu.tile * kRbRows;  // first gate row; up rows are I further
-      if (lane < 2) {
-        const uint32_t dst = smem_u32(st + C::kW + lane * C::kBlock);
-        const int row = grow + lane * I;
-        if (map3d) {
-          tma_load_3d(dst, &w13_map, 0, row, k0 / 256, full);
-        } else {
-          for (int ch = 0; ch < box_chunks; ++ch)
-            tma_load_2d(dst + ch * kRbRows * 128, &w13_map, k0 / 2 + ch * 128, row, full);
+      if (role == 0) {
+        if (lane == 0)
+          mbar_arrive_expect_tx(full, 2u * (uint32_t)(box_chunks * kRbRows * 128) +
+                                          (s_tma ? 2u * kRbRows * C::kScaleRow : 0u));
+        __syncwarp();
+        if (lane < 2) {
+          const uint32_t dst = smem_u32(st + C::kW + lane * C::kBlock);
+          const int row = grow + lane * I;
+          if (map3d) {
+            tma_load_3d(dst, &w13_map, 0, row, k0 / 256, full);
+          } else {
+            for (int ch = 0; ch < box_chunks; ++ch)
+              tma_load_2d(dst + ch * kRbRows * 128, &w13_map, k0 / 2 + ch * 128, row, full);
+          }
         }
-      }
-      if (lane < nt)  // lane n < 8 holds the token id of pass row n
-        bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), xq + (size_t)tok * H * 2 + (size_t)k0 * 2, kel * 2,
-                 full);
-      // fx constants of the task's groups, transposed to [group][token]
-      // (lane L copies for pass row L % 8, whose token id it holds)
-      for (int q = lane; q < C::kCg * kTok; q += 32) {
-        const int tt = q & (kTok - 1), j = q >> 3;
-        if (tt < nt && j * G < kel)
-          cp_async8(smem_u32(st + C::kC + (j * kTok + tt) * 8), xc + (size_t)tok * NG + k0 / G + j);
-      }
-      // scales: 64 gate rows then 64 up rows, kel/G groups each: two TMA boxes
-      // when the scale rows are 16-byte aligned, else pairs of groups by
-      // 4-byte async copies
-      if (s_tma) {
-        if (lane == 2 || lane == 3)
+        // scales: 64 gate rows then 64 up rows, kel/G groups each (two TMA
+        // boxes when the scale rows are 16-byte aligned; role 2 otherwise)
+        if (s_tma && (lane == 2 || lane == 3))
           tma_load_2d(smem_u32(st + C::kS + (lane - 2) * kRbRows * C::kScaleRow), &s_map, k0 / G,
                       grow + (lane - 2) * I, full);
-      } else for (int q = lane; q < 2 * kRbRows * C::kPairs; q += 32) {
-        const int rr = q / C::kPairs, pp = q - rr * C::kPairs;
-        if (pp * 2 * G < kel) {
-          const size_t srow = (size_t)grow + (rr >= kRbRows ? I : 0) + (rr & (kRbRows - 1));
-          cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + srow * NG + k0 / G + 2 * pp);
+      } else if (role == 1) {
+        if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(nt * kel * 2));
+        __syncwarp();
+        if (lane < nt)  // lane n < 8 holds the token id of pass row n
+          bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), xq + (size_t)tok * H * 2 + (size_t)k0 * 2, kel * 2,
+                   full);
+      } else {
+        // fx constants of the task's groups, transposed to [group][token]
+        // (lane L copies for pass row L % 8, whose token id it holds)
+        for (int q = lane; q < C::kCg * kTok; q += 32) {
+          const int tt = q & (kTok - 1), j = q >> 3;
+          if (tt < nt && j * G < kel)
+            cp_async8(smem_u32(st + C::kC + (j * kTok + tt) * 8), xc + (size_t)tok * NG + k0 / G + j);
         }
+        if (!s_tma) {  // scales as pairs of groups by 4-byte async copies
+          for (int q = lane; q < 2 * kRbRows * C::kPairs; q += 32) {
+            const int rr = q / C::kPairs, pp = q - rr * C::kPairs;
+            if (pp * 2 * G < kel) {
+              const size_t srow = (size_t)grow + (rr >= kRbRows ? I : 0) + (rr & (kRbRows - 1));
+              cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + srow * NG + k0 / G + 2 * pp);
+            }
+          }
+        }
+        cp_async_arrive_noinc(full);
       }
-      cp_async_arrive_noinc(full);
       ++issued;
       tok = tok_next;
       cu = nx;
