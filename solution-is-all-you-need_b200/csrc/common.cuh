@@ -118,6 +118,13 @@ __device__ __forceinline__ void pdl_begin() {
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
+// The two halves of pdl_begin, for a kernel that starts work which does not
+// depend on the previous kernel before it waits. Every kernel of the chain
+// waits before it triggers, so a kernel scheduled early may already read
+// what the kernels before its predecessor wrote: its predecessor's blocks
+// triggered only after those had finished.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 
 template <typename... KArgs, typename... Args>
 inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,

@@ -83,7 +83,6 @@ __device__ int g_ffn_error;
 namespace {
 
 constexpr int kConsumers = 16;                  // consumer (MMA) warps
-constexpr int kGuThreads = (kConsumers + 1) * 32;  // + 1 producer warp (down kernel)
 constexpr int kEpiWarps = 4;                    // gate/up epilogue warps (one per 16-row group)
 constexpr int kRbProducers = 3;                // gate/up row-block kernel: weights+scales, x rows, constants
 constexpr int kRbThreads = (kConsumers + kEpiWarps + kRbProducers) * 32;
@@ -819,7 +818,8 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
 // quarter of the task, and the item's end sum is ((q0 + q1) + q2) + q3 like
 // the row-block form's, so both forms give bit-identical h for every row.
 constexpr int kMtConsumers = 8;
-constexpr int kMtThreads = (kMtConsumers + 1) * 32;
+constexpr int kMtProducers = 3;  // weights+scales, x rows, constants (as the row-block form)
+constexpr int kMtThreads = (kMtConsumers + kMtProducers) * 32;
 constexpr int kMtRows = 64;
 constexpr int kMtKc = 512;
 constexpr int kMtTok = 32;
@@ -892,7 +892,7 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&ctl->full[s]), 1 + 32);
+      mbar_init(smem_u32(&ctl->full[s]), 2 + 32);  // two expect_tx arrivals + one cp.async arrival per lane
       mbar_init(smem_u32(&ctl->empty[s]), kMtConsumers);
     }
     for (int i = 0; i < 4; ++i) {
@@ -909,61 +909,69 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
   const int ntask = (q1 - q0) * nkc;
   if (ntask == 0) return;
 
-  if (warp == kMtConsumers) {
-    // ---------------- producer warp ----------------
+  if (warp >= kMtConsumers) {
+    // ---------------- producer warps ----------------
+    // role 0: weight and scale boxes; role 1: fx rows of x; role 2: fx
+    // constants (and scales by 4-byte async copies when not by TMA)
+    const int role = warp - kMtConsumers;
     Cursor cu = cursor_at<kMtTok>(q0, na, tiles, meta);
     auto token = [&](const Cursor& k) -> int {  // lane holds the token id of block row `lane`
       const int rr = k.pass * kMtTok + lane;
       return rr < meta.n[k.slot] ? __ldg(row_token + meta.row0[k.slot] + rr) : -1;
     };
-    int tok = token(cu);
+    int tok = role != 0 ? token(cu) : -1;
     int issued = 0;
     for (int t = 0; t < ntask; ++t) {
       const int s = t % S;
       if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
       Cursor nx = cu;
       cursor_next<kMtTok>(nx, tiles, nkc, meta);
-      const int tok_next = (t + 1 < ntask && nx.kc == 0) ? token(nx) : tok;
+      const int tok_next = (role != 0 && t + 1 < ntask && nx.kc == 0) ? token(nx) : tok;
       const int k0 = cu.kc * kMtKc;
       const int kel = min(kMtKc, H - k0);
       const int nt = min(kMtTok, meta.n[cu.slot] - cu.pass * kMtTok);
       const uint32_t full = smem_u32(&ctl->full[s]);
       uint8_t* st = smem + s * C::kStage;
-      if (lane == 0)
-        mbar_arrive_expect_tx(full, 2u * (uint32_t)(box_chunks * kMtRows * 128) + (uint32_t)(nt * kel * 2) +
-                                        (s_tma ? 2u * kMtRows * C::kScaleRow : 0u));
-      __syncwarp();
       const int grow = meta.e[cu.slot] * 2 * I + cu.tile * kMtRows;  // first gate row; up rows are I further
-      if (lane < 2) {
-        const uint32_t dst = smem_u32(st + C::kW + lane * C::kBlock);
-        const int row = grow + lane * I;
-        if (map3d) {
-          tma_load_3d(dst, &w13_map, 0, row, k0 / 256, full);
-        } else {
-          for (int ch = 0; ch < box_chunks; ++ch)
-            tma_load_2d(dst + ch * kMtRows * 128, &w13_map, k0 / 2 + ch * 128, row, full);
-        }
-      }
-      if (lane < nt) {  // lane n < 32 holds the token id of block row n
-        bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), xq + (size_t)tok * H * 2 + (size_t)k0 * 2, kel * 2,
-                 full);
-        for (int j = 0; j * G < kel; ++j)
-          cp_async8(smem_u32(st + C::kC + (j * kMtTok + lane) * 8), xc + (size_t)tok * NG + k0 / G + j);
-      }
-      if (s_tma) {
-        if (lane == 2 || lane == 3)
-          tma_load_2d(smem_u32(st + C::kS + (lane - 2) * kMtRows * C::kScaleRow), &s_map, k0 / G,
-                      grow + (lane - 2) * I, full);
-      } else {
-        for (int q = lane; q < 2 * kMtRows * C::kPairs; q += 32) {
-          const int rr = q / C::kPairs, pp = q - rr * C::kPairs;
-          if (pp * 2 * G < kel) {
-            const size_t srow = (size_t)grow + (rr >= kMtRows ? I : 0) + (rr & (kMtRows - 1));
-            cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + srow * NG + k0 / G + 2 * pp);
+      if (role == 0) {
+        if (lane == 0)
+          mbar_arrive_expect_tx(full, 2u * (uint32_t)(box_chunks * kMtRows * 128) +
+                                          (s_tma ? 2u * kMtRows * C::kScaleRow : 0u));
+        __syncwarp();
+        if (lane < 2) {
+          const uint32_t dst = smem_u32(st + C::kW + lane * C::kBlock);
+          const int row = grow + lane * I;
+          if (map3d) {
+            tma_load_3d(dst, &w13_map, 0, row, k0 / 256, full);
+          } else {
+            for (int ch = 0; ch < box_chunks; ++ch)
+              tma_load_2d(dst + ch * kMtRows * 128, &w13_map, k0 / 2 + ch * 128, row, full);
           }
         }
+        if (s_tma && (lane == 2 || lane == 3))
+          tma_load_2d(smem_u32(st + C::kS + (lane - 2) * kMtRows * C::kScaleRow), &s_map, k0 / G,
+                      grow + (lane - 2) * I, full);
+      } else if (role == 1) {
+        if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(nt * kel * 2));
+        __syncwarp();
+        if (lane < nt)  // lane n < 32 holds the token id of block row n
+          bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), xq + (size_t)tok * H * 2 + (size_t)k0 * 2, kel * 2,
+                   full);
+      } else {
+        if (lane < nt)
+          for (int j = 0; j * G < kel; ++j)
+            cp_async8(smem_u32(st + C::kC + (j * kMtTok + lane) * 8), xc + (size_t)tok * NG + k0 / G + j);
+        if (!s_tma) {
+          for (int q = lane; q < 2 * kMtRows * C::kPairs; q += 32) {
+            const int rr = q / C::kPairs, pp = q - rr * C::kPairs;
+            if (pp * 2 * G < kel) {
+              const size_t srow = (size_t)grow + (rr >= kMtRows ? I : 0) + (rr & (kMtRows - 1));
+              cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + srow * NG + k0 / G + 2 * pp);
+            }
+          }
+        }
+        cp_async_arrive_noinc(full);
       }
-      cp_async_arrive_noinc(full);
       ++issued;
       tok = tok_next;
       cu = nx;
@@ -1134,6 +1142,7 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
 // item ends with a plain store, no cross-warp sum.
 constexpr int kDnRows = 256;
 constexpr int kDnKc = 256;
+constexpr int kDnThreads = (kConsumers + 2) * 32;  // 16 consumer + 2 producer warps
 
 template <int S>
 struct DnCtl {
@@ -1180,12 +1189,15 @@ __device__ __forceinline__ FxB<G> lds_fxb_swz(const uint8_t* plane, int g, int r
 // G = 64, 16 for G = 32) is copied with one async copy when w2_s and the
 // scale rows allow it, else as 4-byte pairs.
 template <int G, int NS>
-__global__ void __launch_bounds__(kGuThreads, 1)
+__global__ void __launch_bounds__(kDnThreads, 1)
 ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap h_map,
                     int s_vec, const int2* __restrict__ hc, int R, const int32_t* __restrict__ offsets,
                     const int32_t* __restrict__ active, const uint16_t* __restrict__ w2_s, int H, int I, int E,
                     float* __restrict__ y) {
-  pdl_begin();
+  // No wait here: the item table comes from the dispatch, which ran before
+  // the gate/up kernel (see pdl_wait), and the weights and scales do not
+  // change; the producers wait for the gate/up kernel only before they copy
+  // its h rows.
   using C = DnCfg<G, NS>;
   constexpr int S = C::kStages;
   constexpr int kGt = C::kGt;
@@ -1203,7 +1215,7 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&ctl->full[s]), 1 + 32);
+      mbar_init(smem_u32(&ctl->full[s]), 1 + 32);  // TMA warp's expect_tx + one cp.async arrival per lane
       mbar_init(smem_u32(&ctl->empty[s]), kConsumers);
     }
     ctl->abort_flag = 0;
@@ -1215,42 +1227,73 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
   const int ntask = (q1 - q0) * nkc;
   if (ntask == 0) return;
 
-  if (warp == kConsumers) {
-    // ---------------- producer warp ----------------
-    Cursor cu = cursor_at(q0, na, tiles, meta);
-    int issued = 0;
-    for (int t = 0; t < ntask; ++t) {
-      const int s = t % S;
-      if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
-      const int k0 = cu.kc * kDnKc;
-      const uint32_t full = smem_u32(&ctl->full[s]);
-      uint8_t* st = smem + s * C::kStage;
-      const int wrow = meta.e[cu.slot] * H + cu.tile * kDnRows;
-      const int hrow = meta.row0[cu.slot] + cu.pass * kTok;
-      if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(kDnRows * 128 + C::kPlane));
-      __syncwarp();
-      if (lane == 0) tma_load_3d(smem_u32(st + C::kW), &w_map, 0, wrow, cu.kc, full);
-      if (lane == 1) tma_load_3d(smem_u32(st + C::kB), &h_map, 0, hrow, k0 / 64, full);
-      const uint16_t* sbase = w2_s + (size_t)wrow * NG + k0 / G;
-      if (s_vec) {
-#pragma unroll
-        for (int rr = lane; rr < kDnRows; rr += 32) {
-          const uint32_t dst = smem_u32(st + C::kS + rr * kGt * 2);
-          if constexpr (G == 64) cp_async8(dst, sbase + (size_t)rr * NG);
-          else cp_async16(dst, sbase + (size_t)rr * NG);
+  if (warp >= kConsumers) {
+    // ---------------- producer warps ----------------
+    // role 0: the weight and h boxes (TMA); role 1: the scale slices and the
+    // fx constants (async copies). Two warps issue side by side: each copy
+    // instruction waits behind the consumers' shared-memory loads. The first
+    // stages' weights and scales go out before griddepcontrol.wait, while
+    // the gate/up kernel finishes; h and its constants after it.
+    const int role = warp - kConsumers;
+    const uint16_t* s_all = w2_s;
+    auto issue_static = [&](const Cursor& c, int t) {
+      const uint32_t full = smem_u32(&ctl->full[t % S]);
+      uint8_t* st = smem + (t % S) * C::kStage;
+      const int wrow = meta.e[c.slot] * H + c.tile * kDnRows;
+      if (role == 0) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(full, (uint32_t)(kDnRows * 128 + C::kPlane));  // weights now, h later
+          tma_load_3d(smem_u32(st + C::kW), &w_map, 0, wrow, c.kc, full);
         }
       } else {
-        for (int q = lane; q < kDnRows * (kGt / 2); q += 32) {
-          const int rr = q / (kGt / 2), pp = q - rr * (kGt / 2);
-          cp_async4(smem_u32(st + C::kS + rr * kGt * 2 + pp * 4), sbase + (size_t)rr * NG + 2 * pp);
+        const uint16_t* sbase = s_all + (size_t)wrow * NG + c.kc * kGt;
+        if (s_vec) {
+#pragma unroll
+          for (int rr = lane; rr < kDnRows; rr += 32) {
+            const uint32_t dst = smem_u32(st + C::kS + rr * kGt * 2);
+            if constexpr (G == 64) cp_async8(dst, sbase + (size_t)rr * NG);
+            else cp_async16(dst, sbase + (size_t)rr * NG);
+          }
+        } else {
+          for (int q = lane; q < kDnRows * (kGt / 2); q += 32) {
+            const int rr = q / (kGt / 2), pp = q - rr * (kGt / 2);
+            cp_async4(smem_u32(st + C::kS + rr * kGt * 2 + pp * 4), sbase + (size_t)rr * NG + 2 * pp);
+          }
         }
       }
-      for (int q = lane; q < kGt * kTok; q += 32) {  // fx constants, transposed to [group][token]
-        const int tt = q & (kTok - 1), j = q >> 3;
-        if (hrow + tt < R)
-          cp_async8(smem_u32(st + C::kC + (j * kTok + tt) * 8), hc + (size_t)(hrow + tt) * NG + k0 / G + j);
+    };
+    auto issue_dynamic = [&](const Cursor& c, int t) {
+      const uint32_t full = smem_u32(&ctl->full[t % S]);
+      uint8_t* st = smem + (t % S) * C::kStage;
+      const int hrow = meta.row0[c.slot] + c.pass * kTok;
+      if (role == 0) {
+        if (lane == 0) tma_load_3d(smem_u32(st + C::kB), &h_map, 0, hrow, c.kc * (kDnKc / 64), full);
+      } else {
+        for (int q = lane; q < kGt * kTok; q += 32) {  // fx constants, transposed to [group][token]
+          const int tt = q & (kTok - 1), j = q >> 3;
+          if (hrow + tt < R)
+            cp_async8(smem_u32(st + C::kC + (j * kTok + tt) * 8), hc + (size_t)(hrow + tt) * NG + c.kc * kGt + j);
+        }
+        cp_async_arrive_noinc(full);
       }
-      cp_async_arrive_noinc(full);
+    };
+    Cursor cu = cursor_at(q0, na, tiles, meta);
+    {
+      Cursor c = cu;
+      for (int t = 0; t < min(S, ntask); ++t) {
+        issue_static(c, t);
+        cursor_next(c, tiles, nkc, meta);
+      }
+    }
+    pdl_wait();  // the gate/up kernel's h rows and constants are complete and visible
+    if (role == 0) pdl_trigger();
+    int issued = 0;
+    for (int t = 0; t < ntask; ++t) {
+      if (t >= S) {
+        if (!wait_phase(smem_u32(&ctl->empty[t % S]), (t / S - 1) & 1, abort_flag)) break;
+        issue_static(cu, t);
+      }
+      issue_dynamic(cu, t);
       ++issued;
       cursor_next(cu, tiles, nkc, meta);
     }
@@ -1589,12 +1632,12 @@ bool launch_down_tma(const uint8_t* hq, const int2* hc, long long R, const int32
   if (five) {
     auto k = ffn_down_tma_kernel<G, 5>;
     set_smem(k, smem);
-    launch_pdl(k, dim3(grid), dim3(kGuThreads), smem, st, wm, hm, s_vec, hc, (int)R, offsets, active, w2_s, H, I,
+    launch_pdl(k, dim3(grid), dim3(kDnThreads), smem, st, wm, hm, s_vec, hc, (int)R, offsets, active, w2_s, H, I,
                E, y);
   } else {
     auto k = ffn_down_tma_kernel<G, 4>;
     set_smem(k, smem);
-    launch_pdl(k, dim3(grid), dim3(kGuThreads), smem, st, wm, hm, s_vec, hc, (int)R, offsets, active, w2_s, H, I,
+    launch_pdl(k, dim3(grid), dim3(kDnThreads), smem, st, wm, hm, s_vec, hc, (int)R, offsets, active, w2_s, H, I,
                E, y);
   }
   return true;
