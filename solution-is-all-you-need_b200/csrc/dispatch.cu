@@ -21,9 +21,16 @@ namespace {
 constexpr int kDispThreads = 1024;
 constexpr int kDispWarps = kDispThreads / 32;
 constexpr int kSingleCtaMaxRows = 16384;
+// Decode batches (up to kSmallRows assignments) take a 256-thread CTA: the
+// same algorithm with a quarter of the barrier participants and an
+// 8-warp (instead of 32-warp) per-expert prefix.
+constexpr int kSmallThreads = 256;
+constexpr int kSmallRows = 2048;
 
-// Exclusive scan of one int per thread over a 1024-thread block.
+// Exclusive scan of one int per thread over a kThreads-thread block.
+template <int kThreads = kDispThreads>
 __device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+  constexpr int kWarps = kThreads / 32;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int incl = v;
 #pragma unroll
@@ -34,32 +41,33 @@ __device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
   if (lane == 31) warp_sums[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    int s = warp_sums[lane];
+    int s = lane < kWarps ? warp_sums[lane] : 0;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
       const int n = __shfl_up_sync(0xffffffffu, s, off);
       if (lane >= off) s += n;
     }
-    warp_sums[lane] = s;
+    if (lane < kWarps) warp_sums[lane] = s;
   }
   __syncthreads();
   const int prefix = warp > 0 ? warp_sums[warp - 1] : 0;
-  *total = warp_sums[31];
+  *total = warp_sums[kWarps - 1];
   __syncthreads();
   return prefix + incl - v;
 }
 
 // Offsets + active list from per-expert totals held in smem `cnt[E]`.
 // Writes offsets[E+1], active[E+1] and leaves base[e] = offsets[e] in smem.
+template <int kThreads = kDispThreads>
 __device__ void scan_experts(const int* cnt, int E, int* base, int32_t* offsets, int32_t* active,
                              int* warp_sums) {
   int carry = 0, carry_act = 0;
-  for (int e0 = 0; e0 < E; e0 += kDispThreads) {
+  for (int e0 = 0; e0 < E; e0 += kThreads) {
     const int e = e0 + threadIdx.x;
     const int c = e < E ? cnt[e] : 0;
     int tot, tot_act;
-    const int ex = block_exclusive_scan(c, warp_sums, &tot);
-    const int ex_act = block_exclusive_scan(c > 0 ? 1 : 0, warp_sums, &tot_act);
+    const int ex = block_exclusive_scan<kThreads>(c, warp_sums, &tot);
+    const int ex_act = block_exclusive_scan<kThreads>(c > 0 ? 1 : 0, warp_sums, &tot_act);
     if (e < E) {
       base[e] = carry + ex;
       offsets[e] = carry + ex;
@@ -74,11 +82,14 @@ __device__ void scan_experts(const int* cnt, int E, int* base, int32_t* offsets,
   }
 }
 
-// Rank the assignments [a0, a0+1024) and write their permuted rows.
+// Rank the assignments [a0, a0 + kThreads) and write their permuted rows.
 // `base[e]` (smem) is the first free row of expert e and is advanced.
-// `wcnt` is smem [kDispWarps][E].
+// `wcnt` is smem [kThreads / 32][E].
+template <int kThreads = kDispThreads>
 __device__ void rank_chunk(const int32_t* __restrict__ idx, int R, int top_k, int E, int a0,
                            int* base, int* wcnt, int32_t* row_token, int32_t* inv) {
+  constexpr int kDispWarps = kThreads / 32;
+  constexpr int kDispThreads = kThreads;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int a = a0 + threadIdx.x;
   const int e_raw = a < R ? idx[a] : 0;
@@ -119,6 +130,7 @@ __device__ void rank_chunk(const int32_t* __restrict__ idx, int R, int top_k, in
   __syncthreads();
 }
 
+template <int kDispThreads>
 __global__ void __launch_bounds__(kDispThreads)
 dispatch_single_kernel(const int32_t* __restrict__ idx, int T, int top_k, int E,
                        int32_t* __restrict__ offsets, int32_t* __restrict__ row_token,
@@ -137,10 +149,10 @@ dispatch_single_kernel(const int32_t* __restrict__ idx, int T, int top_k, int E,
     if ((unsigned)e < (unsigned)E) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  scan_experts(cnt, E, base, offsets, active, warp_sums);
+  scan_experts<kDispThreads>(cnt, E, base, offsets, active, warp_sums);
   __syncthreads();
   for (int a0 = 0; a0 < R; a0 += kDispThreads)
-    rank_chunk(idx, R, top_k, E, a0, base, wcnt, row_token, inv);
+    rank_chunk<kDispThreads>(idx, R, top_k, E, a0, base, wcnt, row_token, inv);
 }
 
 // Multi-CTA form for large T*k: count per chunk, scan, then rank per chunk.
@@ -212,14 +224,19 @@ int launch_dispatch(const int32_t* topk_idx, int T, int top_k, int E, int32_t* o
                     int32_t* row_token, int32_t* inv, int32_t* active, void* scratch,
                     cudaStream_t st) {
   const int R = T * top_k;
+  if (R <= kSmallRows) {
+    auto k = dispatch_single_kernel<kSmallThreads>;
+    const size_t smem = (size_t)(2 * E + 32 + (kSmallThreads / 32) * E) * sizeof(int);
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    launch_pdl(k, dim3(1), dim3(kSmallThreads), smem, st, topk_idx, T, top_k, E, offsets, row_token, inv, active);
+    note_launches(1);
+    return PHMOE_OK;
+  }
   if (R <= kSingleCtaMaxRows) {
+    auto k = dispatch_single_kernel<kDispThreads>;
     const size_t smem = (size_t)(2 * E + 32 + kDispWarps * E) * sizeof(int);
-    if (smem > 48 * 1024) {
-      cudaFuncSetAttribute(dispatch_single_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-    }
-    launch_pdl(dispatch_single_kernel, dim3(1), dim3(kDispThreads), smem, st, topk_idx, T, top_k, E, offsets, row_token,
-                                                          inv, active);
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    launch_pdl(k, dim3(1), dim3(kDispThreads), smem, st, topk_idx, T, top_k, E, offsets, row_token, inv, active);
     note_launches(1);
     return PHMOE_OK;
   }

@@ -323,15 +323,46 @@ struct Meta {
 };
 
 template <int TB = kTok>  // tokens per item
-__device__ int build_meta(const int32_t* __restrict__ offsets, const int32_t* __restrict__ active, int tiles,
+__device__ int build_meta(const int32_t* __restrict__ offsets, const int32_t* __restrict__ active, int E, int tiles,
                           Meta m) {
-  const int na = active[0];
-  for (int s = threadIdx.x; s < na; s += blockDim.x) {
-    const int e = active[1 + s];
-    const int r0 = offsets[e];
-    m.e[s] = e;
-    m.row0[s] = r0;
-    m.n[s] = offsets[e + 1] - r0;
+  // active[0..E] and offsets[0..E] are loaded side by side (one round trip
+  // to memory instead of three dependent ones) into table and n, then
+  // reordered by active slot in shared memory.
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+    m.table[i] = __ldg(active + i);
+    m.n[i] = __ldg(offsets + i);
+  }
+  __syncthreads();
+  const int na = m.table[0];
+  constexpr int kPer = 4;  // slots per thread held in registers across the barrier
+  int nreg[kPer];
+  if (na <= kPer * (int)blockDim.x) {
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int s = threadIdx.x + i * blockDim.x;
+      if (s < na) {
+        const int e = m.table[1 + s];
+        const int r0 = m.n[e];
+        m.e[s] = e;
+        m.row0[s] = r0;
+        nreg[i] = m.n[e + 1] - r0;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int s = threadIdx.x + i * blockDim.x;
+      if (s < na) m.n[s] = nreg[i];
+    }
+  } else {  // more active experts than kPer per thread: reload from global memory
+    __syncthreads();
+    for (int s = threadIdx.x; s < na; s += blockDim.x) {
+      const int e = __ldg(active + 1 + s);
+      const int r0 = __ldg(offsets + e);
+      m.e[s] = e;
+      m.row0[s] = r0;
+      m.n[s] = __ldg(offsets + e + 1) - r0;
+    }
   }
   __syncthreads();
   if (threadIdx.x < 32) {
@@ -594,7 +625,7 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  const int total = build_meta(offsets, active, tiles, meta);  // its barriers publish the init too
+  const int total = build_meta(offsets, active, E, tiles, meta);  // its barriers publish the init too
   int q0, q1;
   cta_range(total, q0, q1);
   const int ntask = (q1 - q0) * nkc;
@@ -903,7 +934,7 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  const int total = build_meta<kMtTok>(offsets, active, tiles, meta);
+  const int total = build_meta<kMtTok>(offsets, active, E, tiles, meta);
   int q0, q1;
   cta_range(total, q0, q1);
   const int ntask = (q1 - q0) * nkc;
@@ -1221,7 +1252,7 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
     ctl->abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  const int total = build_meta(offsets, active, tiles, meta);
+  const int total = build_meta(offsets, active, E, tiles, meta);
   int q0, q1;
   cta_range(total, q0, q1);
   const int ntask = (q1 - q0) * nkc;
@@ -1393,7 +1424,7 @@ ffn_down_kernel(const uint8_t* __restrict__ hq, const int2* __restrict__ hc, con
   const size_t row_bytes = (size_t)I / 2;
   const int na = active[0];
 
-  const int total = build_meta(offsets, active, tiles, meta);
+  const int total = build_meta(offsets, active, E, tiles, meta);
   int q0, q1;
   cta_range(total, q0, q1);
   const int ntask = (q1 - q0) * nkc;

@@ -36,42 +36,37 @@ constexpr int kRouterTokens = 8;    // tokens per CTA
 constexpr int kBlockRouterMinTokens = 256;  // from here the register-blocked kernel is used
 constexpr size_t kMaxTileBytes = 232448;    // dynamic shared memory per CTA
 
+// One lane's 8 router-weight elements in their stored form: a batch of
+// loads is kept in flight unconverted, and converted one chunk at a time.
 template <typename T>
-struct Vec8;
-
+struct RawW8;
 template <>
-struct Vec8<__nv_bfloat16> {
-  static __device__ __forceinline__ void load(const __nv_bfloat16* p, bool ok, float (&v)[8]) {
-    uint4 u = ok ? __ldg(reinterpret_cast<const uint4*>(p)) : make_uint4(0, 0, 0, 0);
-    v[0] = bf16_lo_to_f32(u.x); v[1] = bf16_hi_to_f32(u.x);
-    v[2] = bf16_lo_to_f32(u.y); v[3] = bf16_hi_to_f32(u.y);
-    v[4] = bf16_lo_to_f32(u.z); v[5] = bf16_hi_to_f32(u.z);
-    v[6] = bf16_lo_to_f32(u.w); v[7] = bf16_hi_to_f32(u.w);
+struct RawW8<__nv_bfloat16> {
+  uint4 u;
+  __device__ __forceinline__ void load(const __nv_bfloat16* p, bool ok) {
+    u = ok ? __ldg(reinterpret_cast<const uint4*>(p)) : make_uint4(0, 0, 0, 0);
   }
-  static __device__ __forceinline__ void load_smem(const __nv_bfloat16* p, float (&v)[8]) {
-    const uint4 u = *reinterpret_cast<const uint4*>(p);
+  __device__ __forceinline__ void to_f32(float (&v)[8]) const {
     v[0] = bf16_lo_to_f32(u.x); v[1] = bf16_hi_to_f32(u.x);
     v[2] = bf16_lo_to_f32(u.y); v[3] = bf16_hi_to_f32(u.y);
     v[4] = bf16_lo_to_f32(u.z); v[5] = bf16_hi_to_f32(u.z);
     v[6] = bf16_lo_to_f32(u.w); v[7] = bf16_hi_to_f32(u.w);
   }
 };
-
 template <>
-struct Vec8<float> {
-  static __device__ __forceinline__ void load(const float* p, bool ok, float (&v)[8]) {
-    float4 a = ok ? __ldg(reinterpret_cast<const float4*>(p)) : make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 b = ok ? __ldg(reinterpret_cast<const float4*>(p) + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+struct RawW8<float> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const float* p, bool ok) {
+    a = ok ? __ldg(reinterpret_cast<const float4*>(p)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    b = ok ? __ldg(reinterpret_cast<const float4*>(p) + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  static __device__ __forceinline__ void load_smem(const float* p, float (&v)[8]) {
-    const float4 a = reinterpret_cast<const float4*>(p)[0];
-    const float4 b = reinterpret_cast<const float4*>(p)[1];
+  __device__ __forceinline__ void to_f32(float (&v)[8]) const {
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   }
 };
+template <typename WT>
+constexpr int kWBatch = std::is_same<WT, float>::value ? 4 : 8;  // 16-byte chunk loads in flight per lane
 
 // acc + x*w as one rounded operation sequence matching the CPU replay
 // (rounded product, then rounded add). When both operands are bf16 the fp32
@@ -142,21 +137,24 @@ template <typename XT, typename WT, int TT>
 __device__ __forceinline__ void expert_logits(const float* xs, int rowf, int nchunk, const WT* __restrict__ wrow,
                                               int H, int nt, int lane, float (&acc)[TT]) {
   constexpr bool kExact = std::is_same<XT, __nv_bfloat16>::value && std::is_same<WT, __nv_bfloat16>::value;
-  constexpr int kBatch = std::is_same<WT, float>::value ? 4 : 8;
+  constexpr int kBatch = kWBatch<WT>;
 #pragma unroll
   for (int t = 0; t < TT; ++t) acc[t] = 0.f;
   for (int c0 = 0; c0 < nchunk; c0 += kBatch) {
-    float w[kBatch][8];
+    // a batch of loads in flight, held in stored form (converted per chunk)
+    RawW8<WT> raw[kBatch];
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
       const int h0 = (c0 + b) * 256 + lane * 8;
-      Vec8<WT>::load(wrow + h0, c0 + b < nchunk && h0 < H, w[b]);
+      raw[b].load(wrow + h0, c0 + b < nchunk && h0 < H);
     }
     // tokens innermost: the TT accumulation chains interleave; each token
     // still adds its elements in increasing h
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
       if (c0 + b < nchunk) {
+        float w[1][8];
+        raw[b].to_f32(w[0]);
         const bool hok = (c0 + b) * 256 + lane * 8 < H;
         const float* px = xs + tile_pos(c0 + b, 0, lane);
 #pragma unroll
@@ -169,7 +167,7 @@ __device__ __forceinline__ void expert_logits(const float* xs, int rowf, int nch
             }
             const float xv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
-            for (int v = 0; v < 8; ++v) acc[t] = mul_add<kExact>(acc[t], xv[v], w[b][v]);
+            for (int v = 0; v < 8; ++v) acc[t] = mul_add<kExact>(acc[t], xv[v], w[0][v]);
           }
         }
       }
@@ -181,6 +179,16 @@ __device__ __forceinline__ void expert_logits(const float* xs, int rowf, int nch
     for (int off = 16; off >= 1; off >>= 1)
       acc[t] = __fadd_rn(acc[t], __shfl_xor_sync(0xffffffffu, acc[t], off));
   }
+}
+
+// Ask L2 for a router-weight row (H elements): lane L touches every 32nd
+// 128-byte line.
+template <typename WT>
+__device__ __forceinline__ void prefetch_row_l2(const WT* __restrict__ wrow, int H, int lane) {
+  const char* p = reinterpret_cast<const char*>(wrow);
+  const int bytes = H * (int)sizeof(WT);
+  for (int off = lane * 128; off < bytes; off += 32 * 128)
+    asm volatile("prefetch.global.L2 [%0];\n" ::"l"(p + off));
 }
 
 // Grid: (ceil(E/8), ceil(T/TT)); warp w of a CTA owns expert blockIdx.x*8+w.
@@ -407,12 +415,108 @@ router_topk_kernel(const float* __restrict__ logits, int T, int E, int top_k, in
 // memory alive until all reads are done. No CTA leaves before either
 // barrier, so the barriers always complete.
 constexpr int kFusedCluster = 8;
+constexpr int kFusedWarps = 16;  // one expert per warp for E <= 128
+constexpr int kTopkScratch = 8 + 8 + 256 + 32 + 32 + 4;  // words of shared memory for softmax_topk_group
+
+// Softmax and top-k of one token by the nw = ceil(E/32) warps wl = 0..nw-1
+// of a group (named barrier bar_id), one expert per lane (e = 32 wl + lane),
+// with results bit-identical to softmax_topk_warp<8>:
+//  * the maximum and exp_fixed(v - max) as there;
+//  * the sum in the same order: "lane" L adds e = L, L+32, ... (L + 224) to
+//    0, then the xor butterfly 16..1 (run by warp 0 over the exps in shared
+//    memory; terms with e >= E are 0 there and change nothing);
+//  * the same division; and instead of k rounds of warp argmax, the rank of
+//    each probability among all E (larger first, equal -> lower index), the
+//    order in which those rounds pick. A NaN is never picked; when fewer
+//    than k values can be (non-finite logits), the remaining picks are the
+//    padding slots e = E, E+1, ... < 256 with value -1, then (0x7fffffff,
+//    -2), exactly as the rounds would make them. The selected values are
+//    summed in pick order.
+__device__ void softmax_topk_group(float v, int wl, int nw, int lane, int bar_id, int t, int E, int top_k,
+                                   int renormalize, float* __restrict__ probs, int32_t* __restrict__ topk_idx,
+                                   float* __restrict__ topk_w, float* scr) {
+  float* wmax = scr;                                  // [8]
+  int* wnan = reinterpret_cast<int*>(scr + 8);         // [8]
+  float* ps = scr + 16;                               // [256]
+  float* selv = ps + 256;                             // [32]
+  int* seli = reinterpret_cast<int*>(selv + 32);      // [32]
+  float* ssum = reinterpret_cast<float*>(seli + 32);  // [2]
+  const int nthreads = nw * 32;
+  const int e = wl * 32 + lane;
+  auto gsync = [&]() { asm volatile("bar.sync %0, %1;\n" ::"r"(bar_id), "r"(nthreads) : "memory"); };
+  if (e >= E) v = -INFINITY;
+  float m = v;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if (lane == 0) wmax[wl] = m;
+  gsync();
+  m = wmax[0];
+  for (int i = 1; i < nw; ++i) m = fmaxf(m, wmax[i]);
+  const float pe = e < E ? exp_fixed(__fsub_rn(v, m)) : 0.f;
+  ps[e] = pe;
+  gsync();
+  if (wl == 0) {
+    float sm = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int ee = lane + 32 * i;
+      if (ee < E) sm = __fadd_rn(sm, ps[ee]);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, off));
+    if (lane == 0) ssum[0] = sm;
+  }
+  gsync();  // also: warp 0 has read every exp before ps is overwritten below
+  const float s = ssum[0];
+  float q = -1.0f;
+  if (e < E) {
+    q = __fdiv_rn(pe, s);
+    if (probs) probs[(size_t)t * E + e] = q;
+  }
+  ps[e] = q;
+  const bool is_nan = e < E && q != q;
+  const unsigned nb = __ballot_sync(0xffffffffu, is_nan);
+  if (lane == 0) wnan[wl] = __popc(nb);
+  gsync();
+  if (e < E && !is_nan) {
+    int rank = 0;
+    const int E4 = E & ~3;
+    for (int j = 0; j < E4; j += 4) {
+      const float4 o = *reinterpret_cast<const float4*>(ps + j);
+      rank += (o.x > q || (o.x == q && j < e)) + (o.y > q || (o.y == q && j + 1 < e)) +
+              (o.z > q || (o.z == q && j + 2 < e)) + (o.w > q || (o.w == q && j + 3 < e));
+    }
+    for (int j = E4; j < E; ++j) rank += (ps[j] > q || (ps[j] == q && j < e));
+    if (rank < top_k) {
+      selv[rank] = q;
+      seli[rank] = e;
+    }
+  }
+  gsync();
+  if (wl == 0 && lane == 0) {
+    int valid = E;
+    for (int i = 0; i < nw; ++i) valid -= wnan[i];
+    for (int r = valid; r < top_k; ++r) {
+      const int ep = E + (r - valid);
+      selv[r] = ep < 256 ? -1.0f : -2.0f;
+      seli[r] = ep < 256 ? ep : 0x7fffffff;
+    }
+    float ss = 0.f;
+    for (int r = 0; r < top_k; ++r) ss = __fadd_rn(ss, selv[r]);
+    ssum[1] = ss;
+  }
+  gsync();
+  if (e < top_k) {
+    topk_idx[(size_t)t * top_k + e] = seli[e];
+    topk_w[(size_t)t * top_k + e] = renormalize ? __fdiv_rn(selv[e], ssum[1]) : selv[e];
+  }
+}
 
 template <int G>
 __device__ __forceinline__ void encode_tile_groups(const float* xs, int rowf, int nt, int H, int q, int t0,
                                                    uint8_t* __restrict__ xq, int2* __restrict__ xc) {
   constexpr int kTpg = G / 8;                  // threads per group (one word each)
-  constexpr int kGroupsPerRound = 256 / kTpg;
+  constexpr int kGroupsPerRound = kFusedWarps * 32 / kTpg;
   const int NG = H / G;
   const int ngc = (NG + kFusedCluster - 1) / kFusedCluster;  // groups of a token handled by this CTA
   const int units = nt * ngc;
@@ -466,12 +570,11 @@ __device__ __forceinline__ void encode_tile_groups(const float* xs, int rowf, in
 }
 
 template <typename XT, typename WT, int TT>
-__global__ void __launch_bounds__(kRouterWarps * 32)
+__global__ void __launch_bounds__(kFusedWarps * 32, 2)  // two CTAs per SM: a 32-cluster batch fits one wave
 router_fused_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T, int H, int E, int top_k,
                     int renormalize, float* __restrict__ logits, float* __restrict__ probs,
                     int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, int G, uint8_t* __restrict__ xq,
                     int2* __restrict__ xc) {
-  pdl_begin();
   cg::cluster_group cluster = cg::this_cluster();
   const int q = (int)cluster.block_rank();
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -480,12 +583,20 @@ router_fused_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T, 
   const int EC = (E + kFusedCluster - 1) / kFusedCluster;
   float* xs = reinterpret_cast<float*>(smem_raw);  // [TT][rowf]
   float* lg = xs + (size_t)TT * rowf;              // [TT][EC] this CTA's logits
+  float* scr = lg + ((size_t)TT * EC + 3) / 4 * 4;  // [kTopkScratch] top-k scratch
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.y * TT;
   const int nt = min(TT, T - t0);
+  // The router weights are constant: each warp asks L2 for its experts'
+  // rows before waiting for the previous kernel, so the fetch from HBM
+  // overlaps that kernel's tail and the staging of x.
+  for (int el = warp; el < EC && q * EC + el < E; el += kFusedWarps)
+    prefetch_row_l2<WT>(wr + (size_t)(q * EC + el) * H, H, lane);
+  pdl_wait();
+  pdl_trigger();
   stage_tile<XT>(x + (size_t)t0 * H, nt, H, rowf, xs);
   __syncthreads();
-  for (int el = warp; el < EC; el += kRouterWarps) {
+  for (int el = warp; el < EC; el += kFusedWarps) {
     const int e = q * EC + el;
     if (e >= E) break;
     float acc[TT];
@@ -505,19 +616,20 @@ router_fused_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T, 
     else encode_tile_groups<32>(xs, rowf, nt, H, q, t0, xq, xc);
   }
   cluster.sync();
-  for (int t = q + kFusedCluster * warp; t < nt; t += kFusedCluster * kRouterWarps) {
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int e = lane + 32 * i;
+  // token t of the tile: CTA t % 8, warps 0 .. ceil(E/32)-1 (TT <= 8: one
+  // token per CTA), every logit read through distributed shared memory
+  {
+    const int nw = (E + 31) / 32;
+    const int t = q;
+    if (t < nt && warp < nw) {
+      const int e = warp * 32 + lane;
+      float v = -INFINITY;
       if (e < E) {
         const float* remote = cluster.map_shared_rank(lg, e / EC);
-        v[i] = remote[t * EC + e % EC];
-      } else {
-        v[i] = -INFINITY;
+        v = remote[t * EC + e % EC];
       }
+      softmax_topk_group(v, warp, nw, lane, 1, t0 + t, E, top_k, renormalize, probs, topk_idx, topk_w, scr);
     }
-    softmax_topk_warp<8>(v, lane, t0 + t, E, top_k, renormalize, probs, topk_idx, topk_w);
   }
   cluster.sync();
 }
@@ -705,10 +817,12 @@ void launch_fused_tt(const void* x, const void* wr, int T, int H, int E, int top
                      float* probs, int32_t* topk_idx, float* topk_w, int G, uint8_t* xq, int2* xc,
                      cudaStream_t st) {
   const int EC = (E + kFusedCluster - 1) / kFusedCluster;
-  const size_t smem = ((size_t)TT * ((H + 255) / 256 * 256) + (size_t)TT * EC) * sizeof(float);
+  const size_t smem =
+      ((size_t)TT * ((H + 255) / 256 * 256) + ((size_t)TT * EC + 3) / 4 * 4 + kTopkScratch) * sizeof(float);
+  static_assert(TT <= kFusedCluster, "one token per CTA in the top-k step");
   auto kern = router_fused_kernel<XT, WT, TT>;
   if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_pdl_cluster(kern, dim3(kFusedCluster, (T + TT - 1) / TT), dim3(kRouterWarps * 32), dim3(kFusedCluster, 1, 1),
+  launch_pdl_cluster(kern, dim3(kFusedCluster, (T + TT - 1) / TT), dim3(kFusedWarps * 32), dim3(kFusedCluster, 1, 1),
                      smem, st, static_cast<const XT*>(x), static_cast<const WT*>(wr), T, H, E, top_k, renormalize,
                      logits, probs, topk_idx, topk_w, G, xq, xc);
 }
@@ -737,7 +851,9 @@ int router_device_error(bool reset) {
 }
 
 bool router_fused_supported(int T, int H, int E) {
-  return T > 0 && T < kBlockRouterMinTokens && E <= 256 && (size_t)4 * ((H + 255) / 256 * 256) * 4 <= kMaxTileBytes;
+  // shared memory of the largest tile (4 tokens): x tile, logits, top-k scratch
+  const size_t bytes = ((size_t)4 * ((H + 255) / 256 * 256) + 4 * 32 + kTopkScratch) * 4;
+  return T > 0 && T < kBlockRouterMinTokens && E <= 256 && bytes <= kMaxTileBytes;
 }
 
 int launch_router(const void* x, int x_dtype, const void* wr, int w_dtype, int T, int H, int E,
