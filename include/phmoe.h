@@ -163,9 +163,10 @@ int phmoe_expert_ffn_prefill(const void* x, int x_dtype, const int32_t* row_toke
  * into [4096, 8191] for G = 64, [8192, 16383] for G = 32; |value| below
  * ~1e34) and integers A = rint(v * 2^-e). Layout of `out`
  * (phmoe_fx_rows_size bytes, 256-byte aligned):
- *   q       [rows][K*2 bytes]: per 8-element word 16 bytes, the high bytes
- *           A >> 8 (signed) then the low bytes A & 255, each in element
- *           order 0, 4, 1, 5, 2, 6, 3, 7;
+ *   q       [rows][K*2 bytes]: A = 256 * hi + lo with hi = (A + 128) >> 8
+ *           and lo = A - 256 * hi (both signed bytes); per 8-element word
+ *           16 bytes, the high bytes then the low bytes (the low byte is
+ *           A & 255), each in element order 0, 4, 1, 5, 2, 6, 3, 7;
  *   consts  [rows][K/G] int32 pairs {C0, M} at byte offset
  *           phmoe_fx_rows_size - rows*(K/G)*8: M = bits of the float
  *           1.5 * 2^(23+e), C0 = M - 8 * sum(A).

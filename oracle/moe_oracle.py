@@ -380,8 +380,10 @@ def topk_margin(probs: np.ndarray, k: int) -> np.ndarray:
 #   per row and group of G elements, e = the exponent that scales the group's
 #   largest |value| m into [2^12, 8191] (G = 64) or [2^13, 16383] (G = 32),
 #   clamped to [-126, 100]; A = rint(v * 2^-e), |A| <= 8191 (16383);
-#   bytes of each 8-element word: the high bytes A >> 8 (two's complement)
-#   then the low bytes A & 255, each in element order 0, 4, 1, 5, 2, 6, 3, 7;
+#   A = 256 * hi + lo with hi = (A + 128) >> 8 and lo = A - 256 * hi, both
+#   signed bytes; bytes of each 8-element word: the 8 high bytes then the 8
+#   low bytes (two's complement; the low byte is A & 255), each in element
+#   order 0, 4, 1, 5, 2, 6, 3, 7;
 #   constants {C0, M}: M = the int32 bits of the float 1.5 * 2^(23 + e),
 #   C0 = M - 8 * sum(A).
 # For nibbles n the group sum v = sum((n - 8) * A) is an exact integer with
@@ -435,7 +437,7 @@ def fx_encode_rows(v: np.ndarray, group: int):
     with np.errstate(invalid="ignore"):
         a = np.where(np.isnan(scaled), 0.0, np.clip(np.rint(scaled), -amax, amax))
     A = a.astype(np.int64).reshape(rows, K)
-    hi = ((A >> 8) & 255).astype(np.uint8).reshape(rows, K // 8, 8)[..., _FX_SLOT_ELEM]
+    hi = (((A + 128) >> 8) & 255).astype(np.uint8).reshape(rows, K // 8, 8)[..., _FX_SLOT_ELEM]
     lo = (A & 255).astype(np.uint8).reshape(rows, K // 8, 8)[..., _FX_SLOT_ELEM]
     q = np.concatenate([hi, lo], axis=-1).reshape(rows, 2 * K)
     M = FX_MAGIC + e * (1 << 23)
@@ -449,7 +451,7 @@ def fx_decode_q(q: np.ndarray) -> np.ndarray:
     rows, K2 = q.shape
     w = q.reshape(rows, K2 // 16, 2, 8)
     hi = w[:, :, 0, :].astype(np.int8).astype(np.int64)
-    lo = w[:, :, 1, :].astype(np.int64)
+    lo = w[:, :, 1, :].astype(np.int8).astype(np.int64)
     A = np.empty((rows, K2 // 16, 8), dtype=np.int64)
     A[..., _FX_SLOT_ELEM] = hi * 256 + lo
     return A.reshape(rows, K2 // 2)
@@ -457,13 +459,15 @@ def fx_decode_q(q: np.ndarray) -> np.ndarray:
 
 def fx_group_dot(nibbles: np.ndarray, A: np.ndarray, consts: np.ndarray) -> np.ndarray:
     """One group's dot product the way the tensor-core kernels form it:
-    i_lo = C0 + sum(n * lo), i_hi = sum(n * hi) (exact int32), i = 256 * i_hi
+    i_lo = C0 + sum(n * lo), i_hi = sum(n * hi) (exact int32; hi = (A + 128)
+    >> 8 and lo = A - 256 * hi, both signed bytes), i = 256 * i_hi
     + i_lo, then float32(bits i) - float32(bits M). ``nibbles [G]`` (0..15),
     ``A [..., G]``, ``consts [..., 2]``; returns fp32 ``[...]`` equal to
     sum((n - 8) * A) * 2^e."""
     n = np.asarray(nibbles, dtype=np.int64)
     A = np.asarray(A, dtype=np.int64)
-    hi, lo = A >> 8, A & 255
+    hi = (A + 128) >> 8
+    lo = A - 256 * hi
     i = 256 * (hi * n).sum(-1) + consts[..., 0].astype(np.int64) + (lo * n).sum(-1)
     assert np.all((i >= 0) & (i < 2 ** 31)), "int32 range"
     f = i.astype(np.uint32).view(F32)

@@ -184,8 +184,8 @@ __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f 
 // ---------------------------------------------------------------------------
 // Integer tensor-core path of the decode FFN
 // ---------------------------------------------------------------------------
-// D = A * B + C, m16n8k32, A unsigned 8-bit (int4 nibbles 0..15), B signed /
-// unsigned 8-bit, exact int32 accumulation (register operands).
+// D = A * B + C, m16n8k32, A unsigned 8-bit (int4 nibbles 0..15), B signed
+// 8-bit (the hi and lo bytes of fx rows), exact int32 accumulation.
 __device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
@@ -193,14 +193,6 @@ __device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ void mma_u8u8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm(
-      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
 // First step of a chain: D = A * B + C with C = (c0, c1, c0, c1) given as
 // plain inputs (the constants of the pass's two token columns, or zeros),
 // so no register copies are needed to seed the accumulators.
@@ -212,15 +204,6 @@ __device__ __forceinline__ void mma_u8s8_16832_first(int (&d)[4], const uint32_t
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
 }
-__device__ __forceinline__ void mma_u8u8_16832_first(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
-                                                     int c0, int c1) {
-  asm(
-      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};\n"
-      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
-}
-
 // One packed word (elements e0..e7, packed layout above) as two registers of
 // unsigned bytes: lo = (e0, e4, e1, e5), hi = (e2, e6, e3, e7). One AND and
 // one shift + AND: the whole int4 -> int8 unpack of 8 weights.
@@ -235,11 +218,12 @@ __device__ __forceinline__ void nib_bytes(uint32_t w, uint32_t& lo, uint32_t& hi
 //    and |A| <= kFxAmax(G) (8191 for G = 64, 16383 for G = 32; the largest
 //    element of the group lands in the top two binades, so every element is
 //    held to 2^-13 of the group's maximum or better).
-//  * A = 256 * hi + lo with hi = A >> 8 (signed byte) and lo = A & 255
-//    (unsigned byte). Each 8-element word of a row is 16 bytes: 8 hi bytes
-//    then 8 lo bytes, each in element order (0, 4, 1, 5, 2, 6, 3, 7) - the
-//    order nib_bytes gives the weight bytes, so one 16-byte load per word
-//    yields matching B fragments for the hi and the lo plane.
+//  * A = 256 * hi + lo with hi = (A + 128) >> 8 and lo = A - 256 * hi, both
+//    signed bytes (lo in [-128, 127]; its byte is A & 255), so both planes
+//    enter the MMAs as s8 (one MMA type). Each 8-element word of a row is 16
+//    bytes: 8 hi bytes then 8 lo bytes, each in element order
+//    (0, 4, 1, 5, 2, 6, 3, 7) - the order nib_bytes gives the weight bytes,
+//    so one load per word yields matching B fragments.
 //  * Per row and group, two int32 constants {C0, M}: M = the bits of the
 //    float 1.5 * 2^(23 + e) and C0 = M - 8 * sum(A). For int4 nibbles n the
 //    group's dot product sum((n - 8) * A) = v is exact in int32 and, since
@@ -247,7 +231,7 @@ __device__ __forceinline__ void nib_bytes(uint32_t w, uint32_t& lo, uint32_t& hi
 //    exactly: float(M + v) - float(M) = v * 2^e with no conversion
 //    instruction (I2F runs on a quarter-rate pipe).
 // The dot product of one group is then: i_lo = C0 + sum(n * lo) and i_hi =
-// sum(n * hi) by the tensor cores, i = 256 * i_hi + i_lo (one IMAD), and
+// sum(n * hi) by the tensor cores (u8 x s8), i = 256 * i_hi + i_lo (one IMAD), and
 // __int_as_float(i) - __int_as_float(M) = v * 2^e.
 constexpr int kFxMagic = 0x4B400000;  // float 1.5 * 2^23
 constexpr int kFxMinExp = -126;       // 2^-e stays a normal float (and M + v one too)
@@ -301,7 +285,7 @@ __device__ __forceinline__ int fx_slot(int p) { return (p & 3) * 2 + (p >> 2); }
 
 // The 16 bytes of one word from its 8 integers A[0..7].
 __device__ __forceinline__ uint4 fx_word(const int (&a)[8]) {
-  auto hb = [&](int i) { return (uint32_t)((a[i] >> 8) & 255); };
+  auto hb = [&](int i) { return (uint32_t)(((a[i] + 128) >> 8) & 255); };
   auto lb = [&](int i) { return (uint32_t)(a[i] & 255); };
   uint4 r;
   r.x = hb(0) | (hb(4) << 8) | (hb(1) << 16) | (hb(5) << 24);

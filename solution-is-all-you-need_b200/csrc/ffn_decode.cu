@@ -13,16 +13,16 @@
 // Numerics: exact integer dot products on the int8 tensor cores.
 //  * The activations of the rows and the SwiGLU output h are "fx rows"
 //    (common.cuh): per row and group of G elements a power-of-two exponent
-//    and integers |A| <= 8191 (16383 for G = 32) split into a signed high
-//    byte and an unsigned low byte. fx_rows_kernel encodes x; the gate/up
-//    epilogue encodes h.
+//    and integers |A| <= 8191 (16383 for G = 32) split into two signed
+//    bytes, A = 256 hi + lo. fx_rows_kernel encodes x; the gate/up epilogue
+//    encodes h.
 //  * A weight word (8 nibbles) becomes two registers of unsigned bytes with
-//    one AND and one shift + AND (nib_bytes); mma.sync m16n8k32 u8 x s8 and
-//    u8 x u8 give the exact int32 sums sum(n * hi) and C0 + sum(n * lo) per
-//    group; one IMAD joins them, and the result read as a float minus the
-//    group's magic constant is sum((n - 8) * A) * 2^e exactly (no int-to-float
-//    conversion). The fp16 weight scale multiplies it and fp32 accumulates
-//    over the groups.
+//    one AND and one shift + AND (nib_bytes); mma.sync m16n8k32 u8 x s8
+//    gives the exact int32 sums sum(n * hi) and C0 + sum(n * lo) per group
+//    (one MMA type for both planes); one IMAD joins them, and the result
+//    read as a float minus the group's magic constant is
+//    sum((n - 8) * A) * 2^e exactly (no int-to-float conversion). The fp16
+//    weight scale multiplies it and fp32 accumulates over the groups.
 //  * Every group's dot product is exact: the only roundings are the
 //    encodings of x and h (to 2^-13 of the group's largest |value| or
 //    better) and the fp32 accumulation. The exponent adapts per group, so any
@@ -258,10 +258,10 @@ __device__ __forceinline__ void fx_group_tile(const RowWords<G>& w0, const RowWo
     nib_bytes(w0.w[s], a[0], a[2]);
     nib_bytes(w8.w[s], a[1], a[3]);
     if (s == 0) {
-      mma_u8u8_16832_first(lo, a, b.s[s].z, b.s[s].w, cc.x, cc.z);
+      mma_u8s8_16832_first(lo, a, b.s[s].z, b.s[s].w, cc.x, cc.z);
       mma_u8s8_16832_first(hi, a, b.s[s].x, b.s[s].y, 0, 0);
     } else {
-      mma_u8u8_16832(lo, a, b.s[s].z, b.s[s].w);
+      mma_u8s8_16832(lo, a, b.s[s].z, b.s[s].w);
       mma_u8s8_16832(hi, a, b.s[s].x, b.s[s].y);
     }
   }
@@ -288,14 +288,14 @@ __device__ __forceinline__ void gateup_group_fx(const RowWords<G>& g0, const Row
     nib_bytes(u0.w[s], au[0], au[2]);
     nib_bytes(u8.w[s], au[1], au[3]);
     if (s == 0) {
-      mma_u8u8_16832_first(gl, ag, b.s[s].z, b.s[s].w, cc.x, cc.z);
+      mma_u8s8_16832_first(gl, ag, b.s[s].z, b.s[s].w, cc.x, cc.z);
       mma_u8s8_16832_first(gh, ag, b.s[s].x, b.s[s].y, 0, 0);
-      mma_u8u8_16832_first(ul, au, b.s[s].z, b.s[s].w, cc.x, cc.z);
+      mma_u8s8_16832_first(ul, au, b.s[s].z, b.s[s].w, cc.x, cc.z);
       mma_u8s8_16832_first(uh, au, b.s[s].x, b.s[s].y, 0, 0);
     } else {
-      mma_u8u8_16832(gl, ag, b.s[s].z, b.s[s].w);
+      mma_u8s8_16832(gl, ag, b.s[s].z, b.s[s].w);
       mma_u8s8_16832(gh, ag, b.s[s].x, b.s[s].y);
-      mma_u8u8_16832(ul, au, b.s[s].z, b.s[s].w);
+      mma_u8s8_16832(ul, au, b.s[s].z, b.s[s].w);
       mma_u8s8_16832(uh, au, b.s[s].x, b.s[s].y);
     }
   }
@@ -307,6 +307,7 @@ __device__ __forceinline__ void gateup_group_fx(const RowWords<G>& g0, const Row
     acc_u[q] = fmaf(q < 2 ? su0 : su8, __fsub_rn(__int_as_float(uh[q] * 256 + ul[q]), m), acc_u[q]);
   }
 }
+
 
 // ---------------------------------------------------------------------------
 // work items
@@ -507,7 +508,7 @@ __device__ __forceinline__ void epi_block_encode(EpiBuf<TB>* eb, int rg, int lan
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint8_t* p = &eb->hs[tb + 2 * c + (q & 1)][(2 * rg + (q >> 1)) * 16 + slot];
-    p[0] = (uint8_t)((a[q] >> 8) & 255);
+    p[0] = (uint8_t)(((a[q] + 128) >> 8) & 255);
     p[8] = (uint8_t)(a[q] & 255);
   }
   if ((bad0 || bad1) && any_valid) atomicOr(&g_ffn_error, 2);
@@ -813,14 +814,15 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
         const RowWords<G> ag8 = lds_row<G>(st + o8[j]);
         const RowWords<G> au0 = lds_row<G>(st + o0[j] + C::kBlock);
         const RowWords<G> au8 = lds_row<G>(st + o8[j] + C::kBlock);
-        const FxB<G> b = lds_fxb<G>(st + ob[j]);
-        const int4 cc = *reinterpret_cast<const int4*>(st + C::kC + (g * kTok + 2 * c) * 8);
         const int p = j >> 1;
         const bool hi = j & 1;
-        gateup_group_fx<G>(ag0, ag8, au0, au8, b, cc, hi ? __high2float(sg0[p]) : __low2float(sg0[p]),
-                           hi ? __high2float(sg8[p]) : __low2float(sg8[p]),
-                           hi ? __high2float(su0[p]) : __low2float(su0[p]),
-                           hi ? __high2float(su8[p]) : __low2float(su8[p]), acc_g, acc_u);
+        const float fsg0 = hi ? __high2float(sg0[p]) : __low2float(sg0[p]);
+        const float fsg8 = hi ? __high2float(sg8[p]) : __low2float(sg8[p]);
+        const float fsu0 = hi ? __high2float(su0[p]) : __low2float(su0[p]);
+        const float fsu8 = hi ? __high2float(su8[p]) : __low2float(su8[p]);
+        const FxB<G> b = lds_fxb<G>(st + ob[j]);
+        const int4 cc = *reinterpret_cast<const int4*>(st + C::kC + (g * kTok + 2 * c) * 8);
+        gateup_group_fx<G>(ag0, ag8, au0, au8, b, cc, fsg0, fsg8, fsu0, fsu8, acc_g, acc_u);
       }
     }
     warp_arrive(smem_u32(&ctl->empty[s]), lane);  // this warp is done with the stage
@@ -1071,14 +1073,14 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
 #pragma unroll
               for (int w = 0; w < G / 32; ++w) {
                 if (w == 0) {
-                  mma_u8u8_16832_first(gl, ag[w], bw.s[w].z, bw.s[w].w, cc.x, cc.z);
+                  mma_u8s8_16832_first(gl, ag[w], bw.s[w].z, bw.s[w].w, cc.x, cc.z);
                   mma_u8s8_16832_first(gh, ag[w], bw.s[w].x, bw.s[w].y, 0, 0);
-                  mma_u8u8_16832_first(ul, au[w], bw.s[w].z, bw.s[w].w, cc.x, cc.z);
+                  mma_u8s8_16832_first(ul, au[w], bw.s[w].z, bw.s[w].w, cc.x, cc.z);
                   mma_u8s8_16832_first(uh, au[w], bw.s[w].x, bw.s[w].y, 0, 0);
                 } else {
-                  mma_u8u8_16832(gl, ag[w], bw.s[w].z, bw.s[w].w);
+                  mma_u8s8_16832(gl, ag[w], bw.s[w].z, bw.s[w].w);
                   mma_u8s8_16832(gh, ag[w], bw.s[w].x, bw.s[w].y);
-                  mma_u8u8_16832(ul, au[w], bw.s[w].z, bw.s[w].w);
+                  mma_u8s8_16832(ul, au[w], bw.s[w].z, bw.s[w].w);
                   mma_u8s8_16832(uh, au[w], bw.s[w].x, bw.s[w].y);
                 }
               }
@@ -1358,9 +1360,10 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
     for (int g = 0; g < kGt; ++g) {
       const RowWords<G> a0 = lds_row<G>(st + ow0[g]);
       const RowWords<G> a8 = lds_row<G>(st + ow0[g] + 8 * 128);
+      const float s0 = __half2float(sc[lr0 * kGt + g]), s8 = __half2float(sc[(lr0 + 8) * kGt + g]);
       const FxB<G> b = lds_fxb_swz<G>(st + C::kB, g, r, c);
       const int4 cc = *reinterpret_cast<const int4*>(st + C::kC + (g * kTok + 2 * c) * 8);
-      fx_group_tile<G>(a0, a8, b, cc, __half2float(sc[lr0 * kGt + g]), __half2float(sc[(lr0 + 8) * kGt + g]), acc);
+      fx_group_tile<G>(a0, a8, b, cc, s0, s8, acc);
     }
     warp_arrive(smem_u32(&ctl->empty[s]), lane);
     if (cu.kc == nkc - 1) {
