@@ -17,9 +17,15 @@ L2); no explicit flush is needed.
   (overlapping the neighbouring steps' layers), timed with CUDA events from
   before the first copy in to after the last copy out; ``e2e.sync`` is the
   same with one stream and a host synchronisation per step.
-* ``roofline``: the dominant kernel (FFN gate/up) timed by CUDA events the
-  library records between its stages; algorithmic bytes = packed int4
-  weights + fp16 scales of every expert hit + activations in + h out.
+* ``roofline``: the dominant kernels, the decode expert FFN (fixed-point
+  encoding of x, gate/up, down), called back to back over the cycled layers
+  inside one CUDA graph and timed with CUDA events around the replays (per
+  call: device time of the three kernels, programmatic launch between them
+  as in the layer); algorithmic bytes = packed int4 weights + fp16 scales
+  of every expert hit + x fx rows read + h written and read + y written.
+  The per-stage times of the layer (CUDA events the library records between
+  its kernels, which also stop the kernels' launch overlap) are in
+  ``stages``.
 * ``cpu_baseline``: transformers' Qwen3MoeSparseMoeBlock (the MoE code
   PHANTOM runs) in fp32 on the host cores, same layer and batch.
 
@@ -364,13 +370,65 @@ def load_peaks():
 
 
 def load_traffic(T):
+    """DRAM bytes (read + write) per call of the decode FFN's two weight
+    kernels at batch T, from the ncu capture summarised in profiles/."""
     p = ROOT / "profiles" / "traffic.json"
     if p.exists():
         d = json.loads(p.read_text())
-        v = d.get(f"ffn_gateup_T{T}")
-        if v is not None:
-            return float(v)
+        g, dn = d.get(f"ffn_gateup_T{T}"), d.get(f"ffn_down_T{T}")
+        if g is not None and dn is not None:
+            return float(g) + float(dn)
     return None
+
+
+def ffn_chain_timing(pm, layers, T, device, calls=64, replays=8):
+    """The decode expert FFN alone (phmoe_expert_ffn_decode: fx encoding of
+    x, gate/up, down) over the cycled layers, `calls` back-to-back calls
+    captured in one CUDA graph on fixed dispatched rows; returns (us per
+    call, algorithmic bytes per call)."""
+    from phantom_moe import _lib
+    L = len(layers)
+    g = torch.Generator(device=device).manual_seed(4242 + T)
+    R = T * K_TOP
+    ins, us = [], []
+    for l in range(L):
+        x = torch.randn(T, H, device=device, generator=g).to(torch.bfloat16)
+        idx, _, _ = pm.router(x, layers[l][0], K_TOP)
+        offsets, row_token, _, active = pm.dispatch(idx, E)
+        h = torch.empty(R * I, dtype=torch.float32, device=device)
+        y = torch.empty(R, H, dtype=torch.float32, device=device)
+        ins.append((x, row_token, offsets, active, h, y) + tuple(_pk(layers[l][1])))
+        us.append(int(torch.unique(idx).numel()))
+    stream = torch.cuda.Stream(device)
+
+    def call(i):
+        x, rt, off, act, h, y, w13q, w13s, w2q, w2s = ins[i % L]
+        _lib.call("phmoe_expert_ffn_decode", x.data_ptr(), 1, rt.data_ptr(), off.data_ptr(), act.data_ptr(),
+                  w13q.data_ptr(), w13s.data_ptr(), w2q.data_ptr(), w2s.data_ptr(), T, H, E, K_TOP, I, G,
+                  h.data_ptr(), y.data_ptr(), stream.cuda_stream)
+
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(L):
+            call(i)
+        stream.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for i in range(calls):
+                call(i)
+        gr.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(replays):
+            gr.replay()
+        e1.record(stream)
+        e1.synchronize()
+    per_call_us = e0.elapsed_time(e1) * 1e3 / (replays * calls)
+    mean_u = float(np.mean(us))
+    nbytes = mean_u * EXPERT_BYTES + R * H * 2 + 2 * R * I * 2 + R * H * 4
+    del gr
+    return per_call_us, nbytes
 
 
 def run_prefill(args, device):
@@ -475,7 +533,10 @@ def run_ours(args):
     res = results[T]
     peak, peak_kind = load_peaks()
     gateup_bytes = hl["gateup_bytes"]
-    achieved = gateup_bytes / (res["stage_ms"]["ffn_gateup"] / 1e3) / 1e9
+    import phantom_moe as pm
+    ffn_us, ffn_bytes = ffn_chain_timing(pm, layers, T, device)
+    achieved = ffn_bytes / (ffn_us / 1e6) / 1e9
+    log(f"[bench] decode FFN alone at T={T}: {ffn_us:.1f} us per call, {achieved:.0f} GB/s")
     del layers, hl
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
@@ -491,10 +552,16 @@ def run_ours(args):
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights, int4 g64)",
         "config": bench_config(1, T, args),
         "sweep": {str(k): _sweep_entry(v) for k, v in results.items()},
-        "roofline": {"kernel": "ffn_gateup", "bound": "hbm", "achieved": achieved, "peak": peak,
+        "roofline": {"kernel": "decode expert FFN (fx encode + ffn_gateup + ffn_down), back-to-back calls "
+                               "in a CUDA graph", "bound": "hbm", "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": load_traffic(T), "algorithmic_bytes_per_launch": gateup_bytes,
-                     "ffn_achieved": res["ffn_GBps"], "ffn_frac": res["ffn_GBps"] / peak},
+                     "traffic": load_traffic(T), "algorithmic_bytes_per_launch": ffn_bytes,
+                     "us_per_call": ffn_us,
+                     "stage_events": {"note": "per-stage CUDA events inside the layer call (they also stop "
+                                              "the launch overlap between kernels, so each stage includes "
+                                              "its kernel's launch and drain)",
+                                      "ffn_gateup_GBps": gateup_bytes / (res["stage_ms"]["ffn_gateup"] / 1e3) / 1e9,
+                                      "ffn_GBps": res["ffn_GBps"]}},
         "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
         "gpu_launches": int(round(res["launches_per_step"] * args.steps)),
         "prefill": prefill,
