@@ -433,6 +433,16 @@ __device__ __forceinline__ void cta_range(int total, int& q0, int& q1) {
   q1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
 }
 
+// Weight row (within an 8-row block) of MMA row r of a lane's tile. A lane
+// (r, c) loads 8 bytes of rows r and r + 8 at K byte 8c (+ 32 per group); in
+// the 128-byte swizzle rows r and r ^ 1 at K halves c >> 1 = 0 and 1 share a
+// 16-byte bank slot, so with rows in order each half-warp (MMA rows 0-3,
+// 4-7) took two passes. Rows 0, 2, 4, 6 for MMA rows 0-3 and 1, 3, 5, 7 for
+// 4-7 give every lane of a half-warp its own slot. The dot products do not
+// depend on which MMA row holds a weight row; the scales, the h slot and
+// the output row follow the same map.
+__device__ __forceinline__ int mma_row(int r) { return 2 * (r & 3) + (r >> 2); }
+
 // Byte offset of (row R of a `rows`-row box of 128-byte K-chunks, byte kb of
 // the task's K slice) as TMA writes it with the 128-byte swizzle.
 __device__ __forceinline__ int swz_off_rows(int R, int kb, int rows) {
@@ -504,7 +514,7 @@ __device__ __forceinline__ void epi_block_encode(EpiBuf<TB>* eb, int rg, int lan
     eb->xs[rg][tb + 2 * c] = s0;
     eb->xs[rg][tb + 2 * c + 1] = s1;
   }
-  const int slot = fx_slot(r);
+  const int slot = fx_slot(mma_row(r));  // this lane holds I rows rg*16 + mma_row(r) (+ 8)
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint8_t* p = &eb->hs[tb + 2 * c + (q & 1)][(2 * rg + (q >> 1)) * 16 + slot];
@@ -770,7 +780,7 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
   const int rg = warp & 3, kq = warp >> 2;
   const int r = lane >> 2, c = lane & 3;
   constexpr int kGpq = C::kGpq;
-  const int R0 = rg * 16 + r;
+  const int R0 = rg * 16 + mma_row(r);
   int o0[kGpq], o8[kGpq], ob[kGpq];
 #pragma unroll
   for (int j = 0; j < kGpq; ++j) {
@@ -1020,7 +1030,7 @@ ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
   const int rg = warp & 3, kh = warp >> 2;
   const int r = lane >> 2, c = lane & 3;
   constexpr int kGpq = C::kGpq;
-  const int R0 = rg * 16 + r;
+  const int R0 = rg * 16 + mma_row(r);
   constexpr int kScH = C::kScaleRow / 2;
   Cursor cu = cursor_at<kMtTok>(q0, na, tiles, meta);
   float acc_g[2][kMtNb][4], acc_u[2][kMtNb][4];  // [K quarter of this half][block][fragment]
@@ -1339,7 +1349,7 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
 
   // ---------------- consumer warps ----------------
   const int r = lane >> 2, c = lane & 3;
-  const int lr0 = warp * 16 + r;
+  const int lr0 = warp * 16 + mma_row(r);
   const int a_off = (G == 64) ? 8 * c : 4 * c;
   // row lr0 + 8 has the swizzle phase of row lr0 and lies 8 x 128 bytes further
   int ow0[kGt];
