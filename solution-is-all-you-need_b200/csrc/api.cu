@@ -382,7 +382,7 @@ int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtyp
                                    group_size, h, y, st, prof ? prof_event(pc, 3) : nullptr))
       return fail(s, "prefill launch failed (tensor map or kernel attribute)");
   } else if (int s = launch_ffn_decode(x, x_dtype, row_token, offsets, active, w13_q, w13_s, w2_q, w2_s, T, H,
-                                       E, top_k, I, group_size, h, y, st, prof ? prof_event(pc, 3) : nullptr, -1,
+                                       E, top_k, I, group_size, h, y, st, prof ? prof_event(pc, 3) : nullptr,
                                        nullptr, nullptr, x_encoded)) {
     return fail(s, "no decode kernel for group_size=%d", group_size);
   }

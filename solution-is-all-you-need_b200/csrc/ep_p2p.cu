@@ -438,8 +438,7 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
                            mid);
   else
     s = launch_ffn_decode(recv, x_dtype, lrow, loff, lact, w13_q, w13_s, w2_q, w2_s, (int)capr, c->H, epr, 1, I, G, h,
-                          y, st, mid, (long long)T * k,  // a rank receives about the T*k rows it sends
-                          lrow, loff + epr);             // encode only the rows that arrived
+                          y, st, mid, lrow, loff + epr);  // encode only the rows that arrived
   if (s) return s;
   mark(4);
   launch_pdl(ep_return_kernel, dim3(sms * 4), dim3(kCopyThreads), 0, st, static_cast<const float*>(y),

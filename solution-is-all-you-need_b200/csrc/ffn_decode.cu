@@ -29,35 +29,36 @@
 //    finite value below ~1e34 is held; larger or non-finite values are
 //    clamped and raise bit value 2 of the device error word.
 //
-// gate/up kernels (persistent, one CTA per SM, warp-specialised):
-//  * row-block form: item = (expert, 64 gate rows and the 64 matching up rows,
-//    pass of 8 tokens); task = one 512-element K chunk of an item (32 KB of
-//    weights). A producer warp issues per task two TMA tensor copies of
-//    weights (128-byte swizzle), two TMA copies of the fp16 scale slices, one
-//    bulk copy per token of its fx row slice, and 8-byte async copies of the
-//    fx constants (transposed to [group][token] so a lane reads its two
-//    tokens' constants with one 16-byte load); all complete on the stage's
-//    "full" mbarrier. Consumer warp w owns 16-row group w%4 and K quarter w/4
-//    of every task; its accumulators cover the item's whole K, and the item
-//    ends with a 4-way sum in fixed order ((q0 + q1) + q2) + q3.
-//  * multi-token form (from ~20 rows per expert): items of up to 32 tokens
-//    of one expert; each lane unpacks its weight bytes once per group and
-//    feeds up to four 8-token column blocks. Both forms sum in the same
-//    order, so h is bit-identical whichever runs.
-//  * epilogue (the four warps that hold an item's 64 I rows after the K sum):
-//    h = silu(gate) * up in fp32, then the fx encoding of h per (row, group):
-//    the group's |max| and sum of integers are exchanged between the warps
-//    holding the group's rows (mbarriers with bounded waits), the bytes are
-//    staged in shared memory and stored as 16-byte words.
-// down kernel (TMA-fed for I % 256 == 0, else an all-thread cp.async form):
-//  item = (expert, 128 output rows, pass of 8 tokens), 8 row groups x 2 K
-//  halves, the same integer dot products against the fx h rows, fp32 y.
+// gate/up kernel (persistent, one CTA per SM, warp-specialised):
+//  * item = (expert, 64 gate rows and the 64 matching up rows, pass of 8
+//    tokens); task = one 512-element K chunk of an item (32 KB of weights).
+//    Three producer warps issue side by side (each copy instruction waits
+//    behind the consumers' shared-memory loads): two TMA tensor copies of
+//    weights (128-byte swizzle) and two of the fp16 scale slices; one bulk
+//    copy per token of its fx row slice; 8-byte async copies of the fx
+//    constants (transposed to [group][token] so a lane reads its two tokens'
+//    constants with one 16-byte load). All complete on the stage's "full"
+//    mbarrier. Consumer warp w owns 16-row group w%4 and K quarter w/4 of
+//    every task; its accumulators cover the item's whole K. An expert with
+//    more than 8 rows takes one pass per 8 of them (its weights come from L2
+//    after the first). (A form that unpacked each weight once for up to 32
+//    tokens was slower at every batch once the producers were split.)
+//  * epilogue (4 warps, one per 16-row group): the four K-quarter partials
+//    summed in fixed order ((q0 + q1) + q2) + q3, h = silu(gate) * up in
+//    fp32, then the fx encoding of h per (row, group): the group's |max| and
+//    sum of integers are exchanged between the warps holding the group's rows
+//    (mbarriers with bounded waits), the bytes are staged in shared memory
+//    and stored as 16-byte words.
+// down kernel (TMA-fed for I % 256 == 0 and H % 256 == 0, else an
+//  all-thread cp.async form): item = (expert, 256 output rows, pass of 8
+//  tokens), tasks of 256 K elements, 16 warps of 16 output rows each over
+//  the whole K, the same integer dot products against the fx h rows, fp32 y.
 //
-// Fragment layout of one m16n8k32 step: lane (r, c) holds for weight rows r
-// and r+8 one packed word each (its bytes are K slots 4c..4c+3 and
-// 16+4c..16+4c+3), and the fx word of token r for the same 8 K elements;
-// inside one MMA the K order is a permutation applied to both operands,
-// which a dot product does not see.
+// Fragment layout of one m16n8k32 step: lane (r, c) holds for weight rows
+// mma_row(r) and mma_row(r) + 8 of its 16-row tile one packed word each (its
+// bytes are K slots 4c..4c+3 and 16+4c..16+4c+3), and the fx word of token r
+// for the same 8 K elements; inside one MMA the K order is a permutation
+// applied to both operands, which a dot product does not see.
 //
 // Every mbarrier wait is bounded: a waiting warp sleeps inside try_wait (a
 // suspend-time hint, woken when the phase completes); after kWaitLimitNs of
@@ -851,326 +852,6 @@ ffn_gateup_rb_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int
 }
 
 // ---------------------------------------------------------------------------
-// gate/up + SwiGLU, multi-token form (batches with ~20 or more rows per expert)
-// ---------------------------------------------------------------------------
-// As the row-block form, but an item covers up to 32 tokens of one expert:
-// each lane unpacks its weight bytes once per group and applies them to every
-// 8-token column block of the item (up to four sets of m16n8k32 per group),
-// so the unpack cost is shared by up to 32 tokens. Eight consumer warps = 4
-// row groups x 2 K halves. Each warp keeps one accumulator per 128-element K
-// quarter of the task, and the item's end sum is ((q0 + q1) + q2) + q3 like
-// the row-block form's, so both forms give bit-identical h for every row.
-constexpr int kMtConsumers = 8;
-constexpr int kMtProducers = 3;  // weights+scales, x rows, constants (as the row-block form)
-constexpr int kMtThreads = (kMtConsumers + kMtProducers) * 32;
-constexpr int kMtRows = 64;
-constexpr int kMtKc = 512;
-constexpr int kMtTok = 32;
-constexpr int kMtNb = kMtTok / kTok;  // 8-token column blocks per item
-// expected rows per expert from which a launch takes the multi-token form
-#ifndef PHMOE_DECODE_MT_MIN_ROWS
-#define PHMOE_DECODE_MT_MIN_ROWS 20
-#endif
-constexpr int kMtMinRowsPerExpert = PHMOE_DECODE_MT_MIN_ROWS;
-
-template <int S>
-struct MtCtl {
-  uint64_t full[S];
-  uint64_t empty[S];
-  uint64_t red_full[4];   // [rg]: the K-half-0 warp has written its partials
-  uint64_t red_empty[4];  // [rg]: the K-half-1 warp has read them
-  uint64_t epi[4];        // [buf][2]: the epilogue's max and sum exchanges
-  int abort_flag;
-};
-
-template <int G>
-struct MtCfg {
-  static constexpr int kGpq = 128 / G;                        // groups per K quarter per task
-  static constexpr int kCg = kMtKc / G;                       // groups per task
-  static constexpr int kBlock = 2 * kMtRows * 128;            // one 64-row box of 2 K-chunks (16 KB)
-  static constexpr int kScaleRow = kMtKc / G * 2;
-  static constexpr int kPairs = kMtKc / G / 2;
-  static constexpr int kBStride = kMtKc * 2 + 16;
-  static constexpr int kW = 0;                                // [gate box][up box]
-  static constexpr int kS = 2 * kBlock;                       // [128 rows][kScaleRow]
-  static constexpr int kB = kS + 2 * kMtRows * kScaleRow;     // [32 tokens][kBStride]
-  static constexpr int kC = kB + kMtTok * kBStride;           // [kCg groups][32 tokens] int2
-  static constexpr int kStage = (kC + kCg * kMtTok * 8 + 1023) / 1024 * 1024;
-  static constexpr int kRed = 4 * 32 * (8 * kMtNb) * 4;       // [rg][lane][nb][8] floats
-  static constexpr int kEpi = (int)sizeof(EpiBuf<kMtTok>);
-  static constexpr size_t fixed_bytes(int S) {
-    return 1024 + (size_t)S * kStage + kRed + 2 * kEpi + sizeof(MtCtl<3>);
-  }
-  // three stages where they fit next to the metadata of up to 256 experts
-  static constexpr int kStages = fixed_bytes(3) + (4 * 256 + 4) * 4 <= 232448 ? 3 : 2;
-  static constexpr size_t smem(int E) {
-    return 1024 + (size_t)kStages * kStage + kRed + 2 * kEpi + sizeof(MtCtl<kStages>) + (size_t)(4 * E + 4) * 4;
-  }
-};
-
-template <int G>
-__global__ void __launch_bounds__(kMtThreads, 1)
-ffn_gateup_mt_kernel(const __grid_constant__ CUtensorMap w13_map, int map3d, int box_chunks,
-                     const __grid_constant__ CUtensorMap s_map, int s_tma, const uint8_t* __restrict__ xq,
-                     const int2* __restrict__ xc, const int32_t* __restrict__ row_token,
-                     const int32_t* __restrict__ offsets, const int32_t* __restrict__ active,
-                     const uint16_t* __restrict__ w13_s, int H, int I, int E, uint8_t* __restrict__ hq,
-                     int2* __restrict__ hc) {
-  pdl_begin();
-  using C = MtCfg<G>;
-  constexpr int S = C::kStages;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* red = reinterpret_cast<float*>(smem + S * C::kStage);
-  EpiBuf<kMtTok>* epib = reinterpret_cast<EpiBuf<kMtTok>*>(smem + S * C::kStage + C::kRed);
-  MtCtl<S>* ctl = reinterpret_cast<MtCtl<S>*>(smem + S * C::kStage + C::kRed + 2 * C::kEpi);
-  int* mbase = reinterpret_cast<int*>(ctl + 1);
-  const Meta meta{mbase, mbase + (E + 1), mbase + 2 * (E + 1), mbase + 3 * (E + 1)};
-  volatile int* abort_flag = &ctl->abort_flag;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles = I / kMtRows;
-  const int NG = H / G;
-  const int nkc = (H + kMtKc - 1) / kMtKc;
-  const int na = active[0];
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(smem_u32(&ctl->full[s]), 2 + 32);  // two expect_tx arrivals + one cp.async arrival per lane
-      mbar_init(smem_u32(&ctl->empty[s]), kMtConsumers);
-    }
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(smem_u32(&ctl->red_full[i]), 1);
-      mbar_init(smem_u32(&ctl->red_empty[i]), 1);
-      mbar_init(smem_u32(&ctl->epi[i]), 4);
-    }
-    ctl->abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-  }
-  const int total = build_meta<kMtTok>(offsets, active, E, tiles, meta);
-  int q0, q1;
-  cta_range(total, q0, q1);
-  const int ntask = (q1 - q0) * nkc;
-  if (ntask == 0) return;
-
-  if (warp >= kMtConsumers) {
-    // ---------------- producer warps ----------------
-    // role 0: weight and scale boxes; role 1: fx rows of x; role 2: fx
-    // constants (and scales by 4-byte async copies when not by TMA)
-    const int role = warp - kMtConsumers;
-    Cursor cu = cursor_at<kMtTok>(q0, na, tiles, meta);
-    auto token = [&](const Cursor& k) -> int {  // lane holds the token id of block row `lane`
-      const int rr = k.pass * kMtTok + lane;
-      return rr < meta.n[k.slot] ? __ldg(row_token + meta.row0[k.slot] + rr) : -1;
-    };
-    int tok = role != 0 ? token(cu) : -1;
-    int issued = 0;
-    for (int t = 0; t < ntask; ++t) {
-      const int s = t % S;
-      if (t >= S && !wait_phase(smem_u32(&ctl->empty[s]), (t / S - 1) & 1, abort_flag)) break;
-      Cursor nx = cu;
-      cursor_next<kMtTok>(nx, tiles, nkc, meta);
-      const int tok_next = (role != 0 && t + 1 < ntask && nx.kc == 0) ? token(nx) : tok;
-      const int k0 = cu.kc * kMtKc;
-      const int kel = min(kMtKc, H - k0);
-      const int nt = min(kMtTok, meta.n[cu.slot] - cu.pass * kMtTok);
-      const uint32_t full = smem_u32(&ctl->full[s]);
-      uint8_t* st = smem + s * C::kStage;
-      const int grow = meta.e[cu.slot] * 2 * I + cu.tile * kMtRows;  // first gate row; up rows are I further
-      if (role == 0) {
-        if (lane == 0)
-          mbar_arrive_expect_tx(full, 2u * (uint32_t)(box_chunks * kMtRows * 128) +
-                                          (s_tma ? 2u * kMtRows * C::kScaleRow : 0u));
-        __syncwarp();
-        if (lane < 2) {
-          const uint32_t dst = smem_u32(st + C::kW + lane * C::kBlock);
-          const int row = grow + lane * I;
-          if (map3d) {
-            tma_load_3d(dst, &w13_map, 0, row, k0 / 256, full);
-          } else {
-            for (int ch = 0; ch < box_chunks; ++ch)
-              tma_load_2d(dst + ch * kMtRows * 128, &w13_map, k0 / 2 + ch * 128, row, full);
-          }
-        }
-        if (s_tma && (lane == 2 || lane == 3))
-          tma_load_2d(smem_u32(st + C::kS + (lane - 2) * kMtRows * C::kScaleRow), &s_map, k0 / G,
-                      grow + (lane - 2) * I, full);
-      } else if (role == 1) {
-        if (lane == 0) mbar_arrive_expect_tx(full, (uint32_t)(nt * kel * 2));
-        __syncwarp();
-        if (lane < nt)  // lane n < 32 holds the token id of block row n
-          bulk_g2s(smem_u32(st + C::kB + lane * C::kBStride), xq + (size_t)tok * H * 2 + (size_t)k0 * 2, kel * 2,
-                   full);
-      } else {
-        if (lane < nt)
-          for (int j = 0; j * G < kel; ++j)
-            cp_async8(smem_u32(st + C::kC + (j * kMtTok + lane) * 8), xc + (size_t)tok * NG + k0 / G + j);
-        if (!s_tma) {
-          for (int q = lane; q < 2 * kMtRows * C::kPairs; q += 32) {
-            const int rr = q / C::kPairs, pp = q - rr * C::kPairs;
-            if (pp * 2 * G < kel) {
-              const size_t srow = (size_t)grow + (rr >= kMtRows ? I : 0) + (rr & (kMtRows - 1));
-              cp_async4(smem_u32(st + C::kS + rr * C::kScaleRow + pp * 4), w13_s + srow * NG + k0 / G + 2 * pp);
-            }
-          }
-        }
-        cp_async_arrive_noinc(full);
-      }
-      ++issued;
-      tok = tok_next;
-      cu = nx;
-    }
-    for (int t = max(0, issued - S); t < issued; ++t) {
-      const uint32_t full = smem_u32(&ctl->full[t % S]);
-      drain_wait(full, (t / S) & 1);
-    }
-    return;
-  }
-
-  // ---------------- consumer warps ----------------
-  const int rg = warp & 3, kh = warp >> 2;
-  const int r = lane >> 2, c = lane & 3;
-  constexpr int kGpq = C::kGpq;
-  const int R0 = rg * 16 + mma_row(r);
-  constexpr int kScH = C::kScaleRow / 2;
-  Cursor cu = cursor_at<kMtTok>(q0, na, tiles, meta);
-  float acc_g[2][kMtNb][4], acc_u[2][kMtNb][4];  // [K quarter of this half][block][fragment]
-  int item = 0;
-  for (int t = 0; t < ntask; ++t) {
-    const int s = t % S;
-    if (cu.kc == 0) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int b = 0; b < kMtNb; ++b)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) { acc_g[h][b][q] = 0.f; acc_u[h][b][q] = 0.f; }
-    }
-    const int nb = (min(kMtTok, meta.n[cu.slot] - cu.pass * kMtTok) + kTok - 1) / kTok;  // warp-uniform
-    const int ngt = min(kMtKc, H - cu.kc * kMtKc) / G;
-    if (!wait_phase(smem_u32(&ctl->full[s]), (t / S) & 1, abort_flag)) return;
-    const uint8_t* st = smem + s * C::kStage;
-    const __half* sc = reinterpret_cast<const __half*>(st + C::kS);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-#pragma unroll 1
-      for (int j = 0; j < kGpq; ++j) {
-        const int g = (2 * kh + h) * kGpq + j;  // group within the task
-        if (g < ngt) {
-          const int kb = (G == 64) ? g * 32 + 8 * c : g * 16 + 4 * c;
-          const RowWords<G> g0 = lds_row<G>(st + C::kW + swz_off_rows(R0, kb, kMtRows));
-          const RowWords<G> g8 = lds_row<G>(st + C::kW + swz_off_rows(R0 + 8, kb, kMtRows));
-          const RowWords<G> u0 = lds_row<G>(st + C::kW + C::kBlock + swz_off_rows(R0, kb, kMtRows));
-          const RowWords<G> u8 = lds_row<G>(st + C::kW + C::kBlock + swz_off_rows(R0 + 8, kb, kMtRows));
-          const float sg0 = __half2float(sc[R0 * kScH + g]), sg8 = __half2float(sc[(R0 + 8) * kScH + g]);
-          const float su0 = __half2float(sc[(kMtRows + R0) * kScH + g]);
-          const float su8 = __half2float(sc[(kMtRows + R0 + 8) * kScH + g]);
-          uint32_t ag[G / 32][4], au[G / 32][4];
-#pragma unroll
-          for (int w = 0; w < G / 32; ++w) {
-            nib_bytes(g0.w[w], ag[w][0], ag[w][2]);
-            nib_bytes(g8.w[w], ag[w][1], ag[w][3]);
-            nib_bytes(u0.w[w], au[w][0], au[w][2]);
-            nib_bytes(u8.w[w], au[w][1], au[w][3]);
-          }
-          const uint8_t* bb = st + C::kB + r * C::kBStride + g * G * 2 + (G == 64 ? 32 : 16) * c;
-          const uint8_t* cb = st + C::kC + (g * kMtTok + 2 * c) * 8;
-#pragma unroll
-          for (int b = 0; b < kMtNb; ++b) {
-            if (b < nb) {
-              const FxB<G> bw = lds_fxb<G>(bb + b * kTok * C::kBStride);
-              const int4 cc = *reinterpret_cast<const int4*>(cb + b * kTok * 8);
-              int gl[4], ul[4], gh[4], uh[4];
-#pragma unroll
-              for (int w = 0; w < G / 32; ++w) {
-                if (w == 0) {
-                  mma_u8s8_16832_first(gl, ag[w], bw.s[w].z, bw.s[w].w, cc.x, cc.z);
-                  mma_u8s8_16832_first(gh, ag[w], bw.s[w].x, bw.s[w].y, 0, 0);
-                  mma_u8s8_16832_first(ul, au[w], bw.s[w].z, bw.s[w].w, cc.x, cc.z);
-                  mma_u8s8_16832_first(uh, au[w], bw.s[w].x, bw.s[w].y, 0, 0);
-                } else {
-                  mma_u8s8_16832(gl, ag[w], bw.s[w].z, bw.s[w].w);
-                  mma_u8s8_16832(gh, ag[w], bw.s[w].x, bw.s[w].y);
-                  mma_u8s8_16832(ul, au[w], bw.s[w].z, bw.s[w].w);
-                  mma_u8s8_16832(uh, au[w], bw.s[w].x, bw.s[w].y);
-                }
-              }
-              const float m0 = __int_as_float(cc.y), m1 = __int_as_float(cc.w);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const float m = (q & 1) ? m1 : m0;
-                acc_g[h][b][q] = fmaf(q < 2 ? sg0 : sg8, __fsub_rn(__int_as_float(gh[q] * 256 + gl[q]), m),
-                                      acc_g[h][b][q]);
-                acc_u[h][b][q] = fmaf(q < 2 ? su0 : su8, __fsub_rn(__int_as_float(uh[q] * 256 + ul[q]), m),
-                                      acc_u[h][b][q]);
-              }
-            }
-          }
-        }
-      }
-    }
-    warp_arrive(smem_u32(&ctl->empty[s]), lane);
-    if (cu.kc == nkc - 1) {
-      float4* rb = reinterpret_cast<float4*>(red) + ((size_t)rg * 32 + lane) * (2 * kMtNb);
-      if (kh == 0) {  // hands q0 + q1 to the K-half-1 warp
-        if (item > 0 && !wait_phase(smem_u32(&ctl->red_empty[rg]), (item - 1) & 1, abort_flag)) return;
-#pragma unroll
-        for (int b = 0; b < kMtNb; ++b) {
-          if (b < nb) {
-            rb[2 * b] = make_float4(acc_g[0][b][0] + acc_g[1][b][0], acc_g[0][b][1] + acc_g[1][b][1],
-                                    acc_g[0][b][2] + acc_g[1][b][2], acc_g[0][b][3] + acc_g[1][b][3]);
-            rb[2 * b + 1] = make_float4(acc_u[0][b][0] + acc_u[1][b][0], acc_u[0][b][1] + acc_u[1][b][1],
-                                        acc_u[0][b][2] + acc_u[1][b][2], acc_u[0][b][3] + acc_u[1][b][3]);
-          }
-        }
-        warp_arrive(smem_u32(&ctl->red_full[rg]), lane);
-      } else {  // ((q0 + q1) + q2) + q3, then SwiGLU and the fx encoding of h
-        if (!wait_phase(smem_u32(&ctl->red_full[rg]), item & 1, abort_flag)) return;
-        const int n = meta.n[cu.slot], row0 = meta.row0[cu.slot];
-        const int prow0 = cu.pass * kMtTok;
-        float hv[kMtNb][4];
-        bool any[kMtNb];
-#pragma unroll
-        for (int b = 0; b < kMtNb; ++b) {
-          any[b] = false;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) hv[b][q] = 0.f;
-          if (b < nb) {
-            const float4 og = rb[2 * b], ou = rb[2 * b + 1];
-            const float gs[4] = {(og.x + acc_g[0][b][0]) + acc_g[1][b][0], (og.y + acc_g[0][b][1]) + acc_g[1][b][1],
-                                 (og.z + acc_g[0][b][2]) + acc_g[1][b][2], (og.w + acc_g[0][b][3]) + acc_g[1][b][3]};
-            const float us[4] = {(ou.x + acc_u[0][b][0]) + acc_u[1][b][0], (ou.y + acc_u[0][b][1]) + acc_u[1][b][1],
-                                 (ou.z + acc_u[0][b][2]) + acc_u[1][b][2], (ou.w + acc_u[0][b][3]) + acc_u[1][b][3]};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const bool ok = prow0 + b * kTok + 2 * c + (q & 1) < n;
-              hv[b][q] = ok ? silu_fast(gs[q]) * us[q] : 0.f;
-              any[b] |= ok;
-            }
-          }
-        }
-        warp_arrive(smem_u32(&ctl->red_empty[rg]), lane);
-        const int buf = item & 1, use = item >> 1;
-        EpiBuf<kMtTok>* eb = epib + buf;
-#pragma unroll
-        for (int b = 0; b < kMtNb; ++b) epi_block_max<kMtTok>(eb, rg, lane, b * kTok, hv[b]);
-        warp_arrive(smem_u32(&ctl->epi[buf * 2]), lane);
-        if (!wait_phase(smem_u32(&ctl->epi[buf * 2]), use & 1, abort_flag)) return;
-        int e[kMtNb][2];
-#pragma unroll
-        for (int b = 0; b < kMtNb; ++b) epi_block_encode<G, kMtTok>(eb, rg, lane, b * kTok, hv[b], any[b], e[b]);
-        warp_arrive(smem_u32(&ctl->epi[buf * 2 + 1]), lane);
-        if (!wait_phase(smem_u32(&ctl->epi[buf * 2 + 1]), use & 1, abort_flag)) return;
-#pragma unroll
-        for (int b = 0; b < kMtNb; ++b)
-          if (b < nb) epi_block_store<G, kMtTok>(eb, rg, lane, b * kTok, e[b], cu.tile, prow0, n, row0, I, hq, hc);
-      }
-      ++item;
-    }
-    cursor_next<kMtTok>(cu, tiles, nkc, meta);
-  }
-}
-
-// ---------------------------------------------------------------------------
 // down projection, TMA-fed form (I % 256 == 0, H % 256 == 0)
 // ---------------------------------------------------------------------------
 // Item = (expert, 256 output rows, pass of 8 tokens); task = one 256-element
@@ -1609,13 +1290,13 @@ bool make_scale_map(CUtensorMap* map, const uint16_t* w13_s, long long rows, int
 }
 
 template <int G>
-int launch_gateup(bool mt, const uint8_t* xq, const int2* xc, const int32_t* row_token, const int32_t* offsets,
+int launch_gateup(const uint8_t* xq, const int2* xc, const int32_t* row_token, const int32_t* offsets,
                   const int32_t* active, const uint8_t* w13_q, const uint16_t* w13_s, int H, int I, int E,
                   uint8_t* hq, int2* hc, int grid, cudaStream_t st) {
-  const int rows = mt ? kMtRows : kRbRows;
-  const int kc = mt ? kMtKc : kRbKc;
+  const int rows = kRbRows;
+  const int kc = kRbKc;
   const bool rb4 = RbCfg<G, 4>::smem(E) <= kMaxSmem;  // four stages where they fit, else three
-  const size_t smem = mt ? MtCfg<G>::smem(E) : (rb4 ? RbCfg<G, 4>::smem(E) : RbCfg<G, 3>::smem(E));
+  const size_t smem = rb4 ? RbCfg<G, 4>::smem(E) : RbCfg<G, 3>::smem(E);
   if (smem > kMaxSmem) return PHMOE_ERR_UNSUPPORTED;
   const int box_chunks = std::min(H, kc) / 256;
   alignas(64) CUtensorMap map, smap;
@@ -1623,17 +1304,10 @@ int launch_gateup(bool mt, const uint8_t* xq, const int2* xc, const int32_t* row
   if (mode < 0) return PHMOE_ERR_CUDA;
   const int s_tma = make_scale_map(&smap, w13_s, (long long)E * 2 * I, H, G, kc, rows) ? 1 : 0;
   if (!s_tma) memset(&smap, 0, sizeof(smap));
-  if (mt) {
-    auto k = ffn_gateup_mt_kernel<G>;
-    set_smem(k, smem);
-    launch_pdl(k, dim3(grid), dim3(kMtThreads), smem, st, map, mode, box_chunks, smap, s_tma, xq, xc, row_token,
-               offsets, active, w13_s, H, I, E, hq, hc);
-  } else {
-    auto k = rb4 ? ffn_gateup_rb_kernel<G, 4> : ffn_gateup_rb_kernel<G, 3>;
-    set_smem(k, smem);
-    launch_pdl(k, dim3(grid), dim3(kRbThreads), smem, st, map, mode, box_chunks, smap, s_tma, xq, xc, row_token,
-               offsets, active, w13_s, H, I, E, hq, hc);
-  }
+  auto k = rb4 ? ffn_gateup_rb_kernel<G, 4> : ffn_gateup_rb_kernel<G, 3>;
+  set_smem(k, smem);
+  launch_pdl(k, dim3(grid), dim3(kRbThreads), smem, st, map, mode, box_chunks, smap, s_tma, xq, xc, row_token,
+             offsets, active, w13_s, H, I, E, hq, hc);
   return PHMOE_OK;
 }
 
@@ -1752,7 +1426,7 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       const int32_t* offsets, const int32_t* active, const uint8_t* w13_q,
                       const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T,
                       int H, int E, int top_k, int I, int G, float* h, float* y,
-                      cudaStream_t st, cudaEvent_t mid_event, long long rows_hint, const int32_t* enc_index,
+                      cudaStream_t st, cudaEvent_t mid_event, const int32_t* enc_index,
                       const int32_t* enc_count, bool x_encoded) {
   const long long R = (long long)T * top_k;
   if (R == 0) return PHMOE_OK;
@@ -1766,18 +1440,8 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
   if (!x_encoded)
     if (int s = launch_fx_rows(x, x_dtype, T, H, G, enc_index, enc_count, xq, xc, st)) return s;
   const int grid = device_sm_count();
-  // multi-token gate/up items from kMtMinRowsPerExpert expected rows per
-  // expert (each unpacked weight then feeds two or more 8-token MMA blocks);
-  // both forms give bit-identical h, so this choice is for speed only
-  const long long rows = rows_hint >= 0 ? rows_hint : R;
-  const bool mt = rows >= (long long)kMtMinRowsPerExpert * E;
-  int s = PHMOE_ERR_UNSUPPORTED;
-  if (mt)
-    s = G == 64 ? launch_gateup<64>(true, xq, xc, row_token, offsets, active, w13_q, w13_s, H, I, E, hq, hc, grid, st)
-                : launch_gateup<32>(true, xq, xc, row_token, offsets, active, w13_q, w13_s, H, I, E, hq, hc, grid, st);
-  if (s != PHMOE_OK)  // 8-token items (small batches, or the multi-token form did not fit)
-    s = G == 64 ? launch_gateup<64>(false, xq, xc, row_token, offsets, active, w13_q, w13_s, H, I, E, hq, hc, grid, st)
-                : launch_gateup<32>(false, xq, xc, row_token, offsets, active, w13_q, w13_s, H, I, E, hq, hc, grid, st);
+  const int s = G == 64 ? launch_gateup<64>(xq, xc, row_token, offsets, active, w13_q, w13_s, H, I, E, hq, hc, grid, st)
+                        : launch_gateup<32>(xq, xc, row_token, offsets, active, w13_q, w13_s, H, I, E, hq, hc, grid, st);
   if (s) return s;
   if (mid_event) cudaEventRecord(mid_event, st);
   const bool tma = G == 64 ? launch_down_tma<64>(hq, hc, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st)

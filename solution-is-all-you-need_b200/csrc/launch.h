@@ -36,7 +36,7 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       const int32_t* offsets, const int32_t* active, const uint8_t* w13_q,
                       const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T,
                       int H, int E, int top_k, int I, int G, float* h, float* y,
-                      cudaStream_t st, cudaEvent_t mid_event = nullptr, long long rows_hint = -1,
+                      cudaStream_t st, cudaEvent_t mid_event = nullptr,
                       const int32_t* enc_index = nullptr, const int32_t* enc_count = nullptr,
                       bool x_encoded = false);
 // Where launch_ffn_decode keeps the fixed-point rows of x inside y (the

@@ -153,10 +153,9 @@ def test_prefill_qwen3_and_auto_path(cuda_device, T):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("T", [1024, 700])
-def test_decode_multi_token_items(cuda_device, T):
-    """Decode path at 40-64 rows per expert: gate/up items of up to 32 tokens
-    (each unpacked weight feeds up to four 8-token MMA blocks), ragged last
-    blocks included."""
+def test_decode_many_rows_per_expert(cuda_device, T):
+    """Decode path at 40-64 rows per expert: 5-8 passes of 8 tokens per row
+    tile of every expert, ragged last passes included."""
     mx, mr, _ = _layer_vs_torch(cuda_device, 128, 2048, 8, 768, 64, T, 13, "decode")
     assert mx <= O.MAX_ABS_TOL and mr <= O.MEAN_REL_TOL, (mx, mr)
     assert pm.load_library().phmoe_device_error(1) == 0
@@ -173,8 +172,8 @@ def test_decode_group32(cuda_device, T, I):
 
 
 @pytest.mark.gpu
-def test_decode_multi_token_fp32_activations(cuda_device):
-    """fp32 activations through the multi-token items."""
+def test_decode_many_rows_fp32_activations(cuda_device):
+    """fp32 activations at 32 rows per expert (four passes per row tile)."""
     dev = cuda_device
     E, H, k, I, G, T = 128, 2048, 8, 768, 64, 512
     wr, packed = _packed_layer(E, H, I, G, 17, dev)
@@ -192,9 +191,9 @@ def test_decode_multi_token_fp32_activations(cuda_device):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_decode_batch_invariance(cuda_device, dtype):
     """A token's decode-path output does not depend on the batch around it:
-    the first 8 tokens of a 1024-token batch (64 rows per expert: multi-token
-    gate/up items, block router) give bit-identical rows when run alone (8-token
-    items, per-token router)."""
+    the first 8 tokens of a 1024-token batch (64 rows per expert: eight passes
+    per row tile, block router) give bit-identical rows when run alone (one
+    pass, per-token router)."""
     dev = cuda_device
     E, H, k, I, G, T = 128, 2048, 8, 768, 64, 1024
     wr, packed = _packed_layer(E, H, I, G, 23, dev)
@@ -213,8 +212,7 @@ def test_decode_batch_invariance(cuda_device, dtype):
 @pytest.mark.gpu
 def test_decode_batch_invariance_few_experts(cuda_device):
     """16 experts with ~32 rows each (the local shape of 8-way expert
-    parallelism, multi-token items): rows are bit-identical to the same
-    tokens run alone (8-token items)."""
+    parallelism): rows are bit-identical to the same tokens run alone."""
     dev = cuda_device
     E, H, k, I, G, T = 16, 2048, 2, 768, 64, 256
     wr, packed = _packed_layer(E, H, I, G, 29, dev)
