@@ -154,7 +154,8 @@ def bench_config(ws: int, T: int, args) -> dict:
            "hidden": H, "experts": E, "top_k": K_TOP, "intermediate": I, "group_size": G, "tokens_per_gpu": T,
            "global_batch": ws * T, "parallelism": f"ep{ws}" if ws > 1 else "single-gpu",
            "l2": f"inputs larger than L2: {args.layers} layers' weights cycled per step",
-           "graph": "CUDA graph per layer" if ws == 1 else "eager layer calls (peer exchange inside)"}
+           "graph": ("CUDA graph per layer" if ws == 1 or getattr(args, "ep_exchange", "peer") == "peer"
+                     else "eager layer calls (NCCL all-to-alls)")}
     if ws > 1:
         cfg["experts_per_gpu"] = E // ws
         cfg["exchange"] = ("peer-memory stores over NVLink with epoch flags (phmoe_ep_layer)"
@@ -926,6 +927,29 @@ def run_ep(args, ws, rank, device):
         hit.append(st["local_experts_hit"])
         recv.append(sum(st["recv_rows"]))
     stream = torch.cuda.current_stream(device)
+    # the peer-exchange layer as one CUDA graph per layer (its epoch lives in
+    # device memory, so replays stay in step across ranks: every rank warms
+    # up, captures and replays the same sequence)
+    graphs, gouts = [], []
+    if exchange is not None:
+        gstream = torch.cuda.Stream(device)
+        with torch.cuda.stream(gstream):
+            for l in range(L):
+                step(l)
+            gstream.synchronize()
+            for l in range(L):
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=gstream):
+                    gouts.append(step(l))
+                graphs.append(gr)
+        torch.cuda.synchronize()
+        dist.barrier()
+
+    def run_step(i):
+        if graphs:
+            graphs[i % L].replay()
+        else:
+            step(i)
 
     def timed(fn, K, W):
         for i in range(W):
@@ -946,14 +970,14 @@ def run_ep(args, ws, rank, device):
 
     n0 = lib.phmoe_kernel_launch_count()
     with ClockSampler(torch.cuda.current_device()) as clk:
-        ms = timed(step, args.steps, args.warmup)
+        ms = timed(run_step, args.steps, args.warmup)
         launches = lib.phmoe_kernel_launch_count() - n0
         # sustained steps while the sampler runs (same count on every rank)
         n_soak = int(args.clock_soak / max(ms / 1e3, 1e-6))
         n_soak = torch.tensor([n_soak], device=device)
         dist.all_reduce(n_soak, op=dist.ReduceOp.MIN)
         for i in range(int(n_soak.item())):
-            step(i)
+            run_step(i)
         torch.cuda.synchronize()
     clocks = clk.summary()
     # end to end: pinned host tokens in, output back to the host, every step
@@ -962,16 +986,26 @@ def run_ep(args, ws, rank, device):
     oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
     xd = torch.empty(T, H, dtype=torch.bfloat16, device=device)
 
+    def layer_on(i, xx):
+        """The layer on input xx: the captured graph of layer i % L (its
+        input buffer refilled first), or an eager call."""
+        l = i % L
+        if graphs:
+            xs[l].copy_(xx, non_blocking=True)
+            graphs[l].replay()
+            return gouts[l]
+        return step(i, x=xx)
+
     def e2e_step(i):
         xd.copy_(xh[i % L], non_blocking=True)
-        out = step(i, x=xd)
+        out = layer_on(i, xd)
         oh.copy_(out, non_blocking=True)
         stream.synchronize()
 
     ms_e2e_sync = timed(e2e_step, args.steps, args.warmup)
     # the same through HostPipeline: copies on their own streams, the layer
     # (eager, with its peer exchange) on the pipeline's compute stream
-    pipe = pm.HostPipeline([lambda xx, out, l=l: out.copy_(step(l, x=xx)) for l in range(L)], T, H, device=device)
+    pipe = pm.HostPipeline([lambda xx, out, l=l: out.copy_(layer_on(l, xx)) for l in range(L)], T, H, device=device)
     ohp = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     for i in range(args.warmup):
         pipe.submit(xh[i % L], ohp[i % 2])

@@ -61,7 +61,7 @@ struct Peers {
 
 // Byte offsets inside a rank's region (identical on every rank).
 struct Region {
-  size_t flags_in, flags_back, counts_in, recv_x, y_back, done, total;
+  size_t flags_in, flags_back, counts_in, recv_x, y_back, done, epoch, total;
 };
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -74,6 +74,7 @@ Region region_layout(int world, int cap, int epr, int H, int elt) {
   L.flags_back = take(kMaxWorld * 4);
   L.counts_in = take((size_t)kMaxWorld * (epr + 1) * 4);  // per source: epr counts, then its base row
   L.done = take(2 * 4);                                     // last-CTA counters (send, return)
+  L.epoch = take(4);                                        // the current layer call's epoch (from 1)
   L.recv_x = take((size_t)world * cap * H * elt);
   L.y_back = take((size_t)cap * H * 4);
   L.total = off;
@@ -106,6 +107,15 @@ __device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* _
   for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = __ldg(src + c);
 }
 
+// The epoch of the current layer call: a word of this rank's region, set to
+// 1 at creation and advanced by the call's last exchange kernel
+// (ep_wait_kernel), so the layer can be captured in a CUDA graph and
+// replayed. Read after the kernel's programmatic-launch wait, i.e. after the
+// previous call's advance.
+__device__ __forceinline__ uint32_t call_epoch(const char* region, const Region& L) {
+  return *reinterpret_cast<const volatile uint32_t*>(region + L.epoch);
+}
+
 // True for the one CTA that finishes last (every CTA fences its writes to
 // system scope first); that CTA resets the counter for the next layer.
 __device__ bool last_cta(int* counter) {
@@ -123,8 +133,9 @@ __device__ bool last_cta(int* counter) {
 
 __global__ void __launch_bounds__(kCopyThreads)
 ep_send_kernel(const char* __restrict__ x, const int32_t* __restrict__ row_token, const int32_t* __restrict__ offsets,
-               int R, int T, int epr, int world, int me, int cap, int row_bytes, Peers peers, Region L, uint32_t epoch) {
+               int R, int T, int epr, int world, int me, int cap, int row_bytes, Peers peers, Region L) {
   pdl_begin();
+  const uint32_t epoch = call_epoch(peers.base[me], L);
   const int chunks = row_bytes / 16;
   const int nvalid = R > 0 ? __ldg(offsets + epr * world) : 0;
   for (int r = blockIdx.x; r < nvalid; r += gridDim.x) {
@@ -161,10 +172,11 @@ constexpr int kPrepThreads = 1024;
 // off[epr+1], active[epr+1], row_token (index into the receive buffer),
 // ret_src / ret_row (where each local row goes back).
 __global__ void __launch_bounds__(kPrepThreads)
-ep_prepare_kernel(const char* __restrict__ local, Region L, int world, int cap, int epr, uint32_t epoch,
+ep_prepare_kernel(const char* __restrict__ local, Region L, int world, int cap, int epr,
                   int32_t* __restrict__ off, int32_t* __restrict__ active, int32_t* __restrict__ row_token,
                   int32_t* __restrict__ ret_src, int32_t* __restrict__ ret_row) {
   pdl_begin();
+  const uint32_t epoch = call_epoch(local, L);
   __shared__ int s_ok[kMaxWorld];
   extern __shared__ int sm[];
   int* cnt = sm;                           // [world][epr]
@@ -244,8 +256,9 @@ ep_prepare_kernel(const char* __restrict__ local, Region L, int world, int cap, 
 __global__ void __launch_bounds__(kCopyThreads)
 ep_return_kernel(const float* __restrict__ y, const int32_t* __restrict__ off, int epr,
                  const int32_t* __restrict__ ret_src, const int32_t* __restrict__ ret_row, int world, int me, int cap,
-                 int H, Peers peers, Region L, uint32_t epoch) {
+                 int H, Peers peers, Region L) {
   pdl_begin();
+  const uint32_t epoch = call_epoch(peers.base[me], L);
   const int nrows = __ldg(off + epr);
   const int chunks = H * 4 / 16;
   for (int r = blockIdx.x; r < nrows; r += gridDim.x) {
@@ -274,9 +287,15 @@ ep_remap_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ vma
   }
 }
 
-__global__ void ep_wait_kernel(const char* __restrict__ local, Region L, int world, uint32_t epoch) {
+// Waits for the return flags, then advances the epoch word for the next
+// layer call (every rank advances its own in step: one per call).
+__global__ void ep_wait_kernel(char* __restrict__ local, Region L, int world) {
   pdl_begin();
+  const uint32_t epoch = call_epoch(local, L);
+  __syncthreads();  // every thread has read this call's epoch
   if (threadIdx.x < world) wait_flag(reinterpret_cast<const uint32_t*>(local + L.flags_back) + threadIdx.x, epoch);
+  __syncthreads();
+  if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(local + L.epoch) = epoch + 1;
 }
 
 }  // namespace
@@ -289,7 +308,6 @@ struct EpContext {
   Peers peers{};
   bool opened[kMaxWorld] = {};
   bool connected = false;
-  uint32_t epoch = 0;
 };
 
 int ep_device_error(bool reset) {
@@ -319,8 +337,10 @@ int ep_create(int rank, int world, int max_tokens, int top_k, int H, int E, int 
   c->elt = x_elt;
   c->cap = max_tokens * top_k;
   c->L = region_layout(world, c->cap, c->epr, H, x_elt);
+  const uint32_t first_epoch = 1;
   if (cudaGetDevice(&c->device) != cudaSuccess || cudaMalloc(&c->local, c->L.total) != cudaSuccess ||
-      cudaMemset(c->local, 0, c->L.total) != cudaSuccess) {
+      cudaMemset(c->local, 0, c->L.total) != cudaSuccess ||
+      cudaMemcpy(c->local + c->L.epoch, &first_epoch, 4, cudaMemcpyHostToDevice) != cudaSuccess) {
     if (c->local) cudaFree(c->local);
     delete c;
     return PHMOE_ERR_CUDA;
@@ -408,7 +428,6 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
   if (topk_idx_out) idx = topk_idx_out;
   if (topk_w_out) wts = topk_w_out;
 
-  const uint32_t epoch = ++c->epoch;
   const int R = T * k;
   const int row_bytes = c->H * c->elt;
   mark(0);
@@ -425,10 +444,10 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
   }
   launch_pdl(ep_send_kernel, dim3(R > 0 ? (R < sms * 4 ? R : sms * 4) : 1), dim3(kCopyThreads), 0, st,
              static_cast<const char*>(x), static_cast<const int32_t*>(row_token), static_cast<const int32_t*>(offsets),
-             R, T, epr, world, c->rank, c->cap, row_bytes, c->peers, c->L, epoch);
+             R, T, epr, world, c->rank, c->cap, row_bytes, c->peers, c->L);
   const size_t psmem = (size_t)(2 * world * epr + world + epr + 1) * sizeof(int);
   launch_pdl(ep_prepare_kernel, dim3(1), dim3(kPrepThreads), psmem, st, static_cast<const char*>(c->local), c->L,
-             world, c->cap, epr, epoch, loff, lact, lrow, ret_src, ret_row);
+             world, c->cap, epr, loff, lact, lrow, ret_src, ret_row);
   const char* recv = c->local + c->L.recv_x;
   mark(2);
   const cudaEvent_t mid = marks ? marks[3] : nullptr;
@@ -443,8 +462,8 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
   mark(4);
   launch_pdl(ep_return_kernel, dim3(sms * 4), dim3(kCopyThreads), 0, st, static_cast<const float*>(y),
              static_cast<const int32_t*>(loff), epr, static_cast<const int32_t*>(ret_src),
-             static_cast<const int32_t*>(ret_row), world, c->rank, c->cap, c->H, c->peers, c->L, epoch);
-  launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, st, static_cast<const char*>(c->local), c->L, world, epoch);
+             static_cast<const int32_t*>(ret_row), world, c->rank, c->cap, c->H, c->peers, c->L);
+  launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, st, c->local, c->L, world);
   if (T > 0)
     launch_combine(reinterpret_cast<const float*>(c->local + c->L.y_back), inv, wts, T, k, c->H, out, x_dtype, st);
   mark(5);

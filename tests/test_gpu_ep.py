@@ -212,6 +212,39 @@ def _peer_worker(rank, world, port, out_dir, case):
                 ok = ok and torch.equal(out, ref[t0:t0 + tokens[rank]])
             ex.close()
             result = {"ok": ok, "err": lib.phmoe_device_error(1)}
+        elif case == "graphed":
+            # the layer captured in CUDA graphs: its epoch is a device word
+            # advanced by every call, so replays keep the ranks in step
+            ex = ep.PeerExchange(None, max_tokens=64, top_k=K, hidden_size=H, num_experts=E)
+            tokens = [64, 3, 0, 40, 64, 1, 17, 9][:world]
+            t0 = sum(tokens[:rank])
+            inputs, refs = [], []
+            for l in range(3):
+                g = torch.Generator(device=dev).manual_seed(100 + l)
+                xs = [torch.randn(t, H, device=dev, generator=g).to(torch.bfloat16) for t in tokens]
+                inputs.append(xs[rank].clone())
+                refs.append(pm.moe_layer(torch.cat(xs), wr, *packed, K, path="decode")[t0:t0 + tokens[rank]])
+            s = torch.cuda.Stream(dev)
+            graphs, outs = [], []
+            with torch.cuda.stream(s):
+                for l in range(3):  # eager warm-up, the same number of calls on every rank
+                    ep.moe_layer_ep(inputs[l], wr, *shard, K, True, G, None, path="decode", exchange=ex)
+                s.synchronize()
+                for l in range(3):
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr, stream=s):
+                        outs.append(ep.moe_layer_ep(inputs[l], wr, *shard, K, True, G, None, path="decode",
+                                                    exchange=ex))
+                    graphs.append(gr)
+            torch.cuda.synchronize()
+            ok = True
+            for l in (0, 1, 2, 2, 0, 1):  # out of order, same order on every rank
+                graphs[l].replay()
+                torch.cuda.synchronize()
+                ok = ok and torch.equal(outs[l], refs[l])
+            del graphs
+            ex.close()
+            result = {"ok": ok, "err": lib.phmoe_device_error(1)}
         else:  # "timeout": rank 1 never calls the layer, so rank 0's flags never arrive
             ex = ep.PeerExchange(None, max_tokens=8, top_k=K, hidden_size=H, num_experts=E)
             if rank == 0:
@@ -251,6 +284,16 @@ def test_ep_peer_exchange_replicated_placement(cuda_device, tmp_path):
     every row goes to the copy its source is assigned, and the output still
     equals the single-GPU layer bit for bit."""
     res = _run_peer("replicated", tmp_path)
+    assert all(bool(r[0]) for r in res)
+    assert all(int(r[1]) == 0 for r in res)
+
+
+@pytest.mark.gpu
+def test_ep_peer_exchange_in_cuda_graph(cuda_device, tmp_path):
+    """The peer-exchange layer captured in CUDA graphs (the exchange's epoch
+    is a device word every call advances) and replayed out of order: every
+    replay equals the single-GPU layer bit for bit."""
+    res = _run_peer("graphed", tmp_path)
     assert all(bool(r[0]) for r in res)
     assert all(int(r[1]) == 0 for r in res)
 
