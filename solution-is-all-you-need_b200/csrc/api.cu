@@ -368,13 +368,14 @@ int phmoe_moe_layer(const void* x, int x_dtype, const void* router_w, int w_dtyp
 
   mark(0);
   const bool decode = chosen != PHMOE_PATH_PREFILL;
-  const bool x_encoded =
+  const DispatchOut disp{offsets, row_token, inv, active};
+  const int rflags =
       launch_router(x, x_dtype, router_w, w_dtype, T, H, E, top_k, renormalize, logits, nullptr, idx, wts, st,
-                    group_size, decode ? ffn_decode_xq(y) : nullptr, decode ? ffn_decode_xc(y, T, H) : nullptr) ==
-      kRouterEncodedX;
+                    group_size, decode ? ffn_decode_xq(y) : nullptr, decode ? ffn_decode_xc(y, T, H) : nullptr, &disp);
+  const bool x_encoded = (rflags & kRouterEncodedX) != 0;
   if (int s = check_launch("router")) return s;
   mark(1);
-  launch_dispatch(idx, T, top_k, E, offsets, row_token, inv, active, ws + L.disp, st);
+  if (!(rflags & kRouterDispatched)) launch_dispatch(idx, T, top_k, E, offsets, row_token, inv, active, ws + L.disp, st);
   if (int s = check_launch("dispatch")) return s;
   mark(2);
   if (chosen == PHMOE_PATH_PREFILL) {

@@ -10,14 +10,24 @@ namespace phmoe {
 
 // Router. With xq != null and a batch the fused single-launch router takes
 // (router_fused_supported), it also writes the fixed-point rows of x for the
-// decode FFN (group size G) to xq / xc and returns kRouterEncodedX; callers
-// then pass x_encoded to launch_ffn_decode. Otherwise returns PHMOE_OK and
-// writes nothing there.
+// decode FFN (group size G) to xq / xc and sets kRouterEncodedX in its
+// result; callers then pass x_encoded to launch_ffn_decode. With disp !=
+// null and a one-token batch it also writes launch_dispatch's outputs (the
+// token's k rows in expert order) and sets kRouterDispatched; callers then
+// skip launch_dispatch. The result is 0 when it did neither.
 constexpr int kRouterEncodedX = 1;
+constexpr int kRouterDispatched = 2;
+struct DispatchOut {
+  int32_t* offsets;    // [E+1]
+  int32_t* row_token;  // [T*k]
+  int32_t* inv;        // [T, k]
+  int32_t* active;     // [E+1]
+};
 bool router_fused_supported(int T, int H, int E);
 int launch_router(const void* x, int x_dtype, const void* wr, int w_dtype, int T, int H, int E,
                   int top_k, int renormalize, float* logits, float* probs, int32_t* topk_idx,
-                  float* topk_w, cudaStream_t st, int G = 0, uint8_t* xq = nullptr, int2* xc = nullptr);
+                  float* topk_w, cudaStream_t st, int G = 0, uint8_t* xq = nullptr, int2* xc = nullptr,
+                  const DispatchOut* disp = nullptr);
 int router_device_error(bool reset);
 
 size_t dispatch_scratch_bytes(int T, int top_k, int E);

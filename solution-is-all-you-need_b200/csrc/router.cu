@@ -512,6 +512,39 @@ __device__ void softmax_topk_group(float v, int wl, int nw, int lane, int bar_id
   }
 }
 
+// The dispatch of a one-token batch from its picks (softmax_topk_group's
+// scratch, after it returns), with launch_dispatch's results: row r of the
+// k valid picks is the r-th smallest expert id (one token: rows in expert
+// order), offsets[e] = the valid picks below e, active = the picked experts
+// ascending, row_token = 0, inv = the pick's row (-1 for an id outside
+// [0, E), which launch_dispatch drops too). The picks are distinct experts.
+__device__ void dispatch_one_token(const float* scr, int wl, int nw, int lane, int E, int top_k,
+                                   const DispatchOut& disp) {
+  const int* seli = reinterpret_cast<const int*>(scr + 16 + 256 + 32);
+  const int tid = wl * 32 + lane;
+  for (int e = tid; e <= E; e += nw * 32) {
+    int c = 0;
+    for (int j = 0; j < top_k; ++j) c += (unsigned)seli[j] < (unsigned)E && seli[j] < e;
+    disp.offsets[e] = c;
+  }
+  if (tid < top_k) {
+    const int ej = seli[tid];
+    const bool ok = (unsigned)ej < (unsigned)E;
+    int rank = 0;
+    for (int j = 0; j < top_k; ++j) rank += (unsigned)seli[j] < (unsigned)E && seli[j] < ej;
+    disp.inv[tid] = ok ? rank : -1;
+    if (ok) {
+      disp.row_token[rank] = 0;
+      disp.active[1 + rank] = ej;
+    }
+  }
+  if (tid == 0) {
+    int nv = 0;
+    for (int j = 0; j < top_k; ++j) nv += (unsigned)seli[j] < (unsigned)E;
+    disp.active[0] = nv;
+  }
+}
+
 template <int G>
 __device__ __forceinline__ void encode_tile_groups(const float* xs, int rowf, int nt, int H, int q, int t0,
                                                    uint8_t* __restrict__ xq, int2* __restrict__ xc) {
@@ -574,7 +607,7 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 2)  // two CTAs per SM: a 32
 router_fused_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T, int H, int E, int top_k,
                     int renormalize, float* __restrict__ logits, float* __restrict__ probs,
                     int32_t* __restrict__ topk_idx, float* __restrict__ topk_w, int G, uint8_t* __restrict__ xq,
-                    int2* __restrict__ xc) {
+                    int2* __restrict__ xc, DispatchOut disp) {
   cg::cluster_group cluster = cg::this_cluster();
   const int q = (int)cluster.block_rank();
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -629,6 +662,7 @@ router_fused_kernel(const XT* __restrict__ x, const WT* __restrict__ wr, int T, 
         v = remote[t * EC + e % EC];
       }
       softmax_topk_group(v, warp, nw, lane, 1, t0 + t, E, top_k, renormalize, probs, topk_idx, topk_w, scr);
+      if (disp.offsets != nullptr && T == 1) dispatch_one_token(scr, warp, nw, lane, E, top_k, disp);
     }
   }
   cluster.sync();
@@ -815,7 +849,7 @@ namespace {
 template <typename XT, typename WT, int TT>
 void launch_fused_tt(const void* x, const void* wr, int T, int H, int E, int top_k, int renormalize, float* logits,
                      float* probs, int32_t* topk_idx, float* topk_w, int G, uint8_t* xq, int2* xc,
-                     cudaStream_t st) {
+                     const DispatchOut& disp, cudaStream_t st) {
   const int EC = (E + kFusedCluster - 1) / kFusedCluster;
   const size_t smem =
       ((size_t)TT * ((H + 255) / 256 * 256) + ((size_t)TT * EC + 3) / 4 * 4 + kTopkScratch) * sizeof(float);
@@ -824,19 +858,23 @@ void launch_fused_tt(const void* x, const void* wr, int T, int H, int E, int top
   if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   launch_pdl_cluster(kern, dim3(kFusedCluster, (T + TT - 1) / TT), dim3(kFusedWarps * 32), dim3(kFusedCluster, 1, 1),
                      smem, st, static_cast<const XT*>(x), static_cast<const WT*>(wr), T, H, E, top_k, renormalize,
-                     logits, probs, topk_idx, topk_w, G, xq, xc);
+                     logits, probs, topk_idx, topk_w, G, xq, xc, disp);
 }
 
 template <typename XT, typename WT>
 void launch_fused(const void* x, const void* wr, int T, int H, int E, int top_k, int renormalize, float* logits,
-                  float* probs, int32_t* topk_idx, float* topk_w, int G, uint8_t* xq, int2* xc, cudaStream_t st) {
+                  float* probs, int32_t* topk_idx, float* topk_w, int G, uint8_t* xq, int2* xc,
+                  const DispatchOut& disp, cudaStream_t st) {
   // token tiles: at least ~one CTA per SM where the batch allows
   if (T <= 16)
-    launch_fused_tt<XT, WT, 1>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq, xc, st);
+    launch_fused_tt<XT, WT, 1>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq, xc, disp,
+                               st);
   else if (T <= 128)
-    launch_fused_tt<XT, WT, 2>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq, xc, st);
+    launch_fused_tt<XT, WT, 2>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq, xc, disp,
+                               st);
   else
-    launch_fused_tt<XT, WT, 4>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq, xc, st);
+    launch_fused_tt<XT, WT, 4>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq, xc, disp,
+                               st);
 }
 }  // namespace
 
@@ -858,23 +896,26 @@ bool router_fused_supported(int T, int H, int E) {
 
 int launch_router(const void* x, int x_dtype, const void* wr, int w_dtype, int T, int H, int E,
                   int top_k, int renormalize, float* logits, float* probs, int32_t* topk_idx,
-                  float* topk_w, cudaStream_t st, int G, uint8_t* xq, int2* xc) {
+                  float* topk_w, cudaStream_t st, int G, uint8_t* xq, int2* xc, const DispatchOut* disp) {
   if (T == 0) return PHMOE_OK;
   if (router_fused_supported(T, H, E)) {
+    // the one-token dispatch rides along (the batch is one cluster)
+    const DispatchOut d = (disp != nullptr && T == 1) ? *disp : DispatchOut{nullptr, nullptr, nullptr, nullptr};
     const bool xb = x_dtype == PHMOE_DTYPE_BF16, wb = w_dtype == PHMOE_DTYPE_BF16;
     if (xb && wb)
       launch_fused<__nv_bfloat16, __nv_bfloat16>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w,
-                                                 G, xq, xc, st);
+                                                 G, xq, xc, d, st);
     else if (xb)
       launch_fused<__nv_bfloat16, float>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq,
-                                         xc, st);
+                                         xc, d, st);
     else if (wb)
       launch_fused<float, __nv_bfloat16>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq,
-                                         xc, st);
+                                         xc, d, st);
     else
-      launch_fused<float, float>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq, xc, st);
+      launch_fused<float, float>(x, wr, T, H, E, top_k, renormalize, logits, probs, topk_idx, topk_w, G, xq, xc, d,
+                                 st);
     note_launches(1);
-    return xq ? kRouterEncodedX : PHMOE_OK;
+    return (xq ? kRouterEncodedX : 0) | (d.offsets ? kRouterDispatched : 0);
   }
   launch_router_logits(x, x_dtype, wr, w_dtype, T, H, E, logits, st);
   const int grid = (T + 7) / 8;
