@@ -53,6 +53,11 @@ namespace {
 
 constexpr int kMaxWorld = 8;
 constexpr int kCopyThreads = 256;
+// The row exchange kernels run one CTA of kXferThreads per SM: every thread
+// ends with a system-scope fence (its peer stores acknowledged) before the
+// last-CTA count, so all fences overlap in one wave instead of queueing over
+// several waves of small CTAs.
+constexpr int kXferThreads = 1024;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
 struct Peers {
@@ -103,8 +108,38 @@ __device__ bool wait_flag(const uint32_t* flag, uint32_t epoch) {
   return true;
 }
 
-__device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int chunks) {
-  for (int c = threadIdx.x; c < chunks; c += blockDim.x) dst[c] = __ldg(src + c);
+// Copies this CTA's rows, r = blockIdx.x + j * gridDim.x < n: the (row,
+// 16-byte chunk) pairs are spread over all threads, four loads in flight per
+// thread. row(r) gives a row's source and destination (dst null: the row is
+// not copied).
+struct RowCopy {
+  const uint4* src;
+  uint4* dst;
+};
+template <typename RowFn>
+__device__ __forceinline__ void copy_rows(int n, int chunks, RowFn row) {
+  const int mine = (int)blockIdx.x < n ? (n - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int total = mine * chunks;
+  for (int q0 = threadIdx.x; q0 < total; q0 += 4 * blockDim.x) {
+    uint4 v[4];
+    uint4* d[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int q = q0 + u * blockDim.x;
+      d[u] = nullptr;
+      if (q < total) {
+        const int j = q / chunks, c = q - j * chunks;
+        const RowCopy rc = row((int)blockIdx.x + j * (int)gridDim.x);
+        if (rc.dst != nullptr) {
+          v[u] = __ldg(rc.src + c);
+          d[u] = rc.dst + c;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (d[u] != nullptr) *d[u] = v[u];
+  }
 }
 
 // The epoch of the current layer call: a word of this rank's region, set to
@@ -116,38 +151,43 @@ __device__ __forceinline__ uint32_t call_epoch(const char* region, const Region&
   return *reinterpret_cast<const volatile uint32_t*>(region + L.epoch);
 }
 
-// True for the one CTA that finishes last (every CTA fences its writes to
-// system scope first); that CTA resets the counter for the next layer.
+// True for the one CTA that finishes last; that CTA resets the counter for
+// the next layer. The CTA barrier orders every thread's stores before
+// thread 0's system-scope fence, which is cumulative: the CTA's stores (to
+// peers too) are visible system-wide before its count, and the last CTA's
+// fence after reading the count orders them all before its flag stores.
+// (One fence per CTA instead of one per thread: a fence in every thread cost
+// ~2.4 us more per copy kernel of a 148 x 1024 grid.)
 __device__ bool last_cta(int* counter) {
   __shared__ bool last;
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     last = atomicAdd(counter, 1) == (int)(gridDim.x - 1);
     if (last) *counter = 0;
+    if (last) __threadfence_system();
   }
   __syncthreads();
-  if (last) __threadfence_system();
   return last;
 }
 
-__global__ void __launch_bounds__(kCopyThreads)
+__global__ void __launch_bounds__(kXferThreads)
 ep_send_kernel(const char* __restrict__ x, const int32_t* __restrict__ row_token, const int32_t* __restrict__ offsets,
-               int R, int T, int epr, int world, int me, int cap, int row_bytes, Peers peers, Region L) {
+               int R, int T, int epr, int world, int me, int cap, int row_bytes, const __grid_constant__ Peers peers,
+               Region L) {
   pdl_begin();
   const uint32_t epoch = call_epoch(peers.base[me], L);
   const int chunks = row_bytes / 16;
   const int nvalid = R > 0 ? __ldg(offsets + epr * world) : 0;
-  for (int r = blockIdx.x; r < nvalid; r += gridDim.x) {
+  copy_rows(nvalid, chunks, [&](int r) -> RowCopy {
     int d = 0;
     while (d + 1 < world && __ldg(offsets + (d + 1) * epr) <= r) ++d;
     const int i = r - __ldg(offsets + d * epr);
     const int t = __ldg(row_token + r);
-    if (i < cap && t >= 0 && t < T) {
-      uint4* dst = reinterpret_cast<uint4*>(peers.base[d] + L.recv_x + ((size_t)me * cap + i) * row_bytes);
-      copy_row(dst, reinterpret_cast<const uint4*>(x + (size_t)t * row_bytes), chunks);
-    }
-  }
+    if (i >= cap || t < 0 || t >= T) return RowCopy{nullptr, nullptr};
+    return RowCopy{reinterpret_cast<const uint4*>(x + (size_t)t * row_bytes),
+                   reinterpret_cast<uint4*>(peers.base[d] + L.recv_x + ((size_t)me * cap + i) * row_bytes)};
+  });
   int* done = reinterpret_cast<int*>(peers.base[me] + L.done);
   if (!last_cta(done)) return;
   // counts and base row for each destination, then its flag
@@ -253,21 +293,20 @@ ep_prepare_kernel(const char* __restrict__ local, Region L, int world, int cap, 
   }
 }
 
-__global__ void __launch_bounds__(kCopyThreads)
+__global__ void __launch_bounds__(kXferThreads)
 ep_return_kernel(const float* __restrict__ y, const int32_t* __restrict__ off, int epr,
                  const int32_t* __restrict__ ret_src, const int32_t* __restrict__ ret_row, int world, int me, int cap,
-                 int H, Peers peers, Region L) {
+                 int H, const __grid_constant__ Peers peers, Region L) {
   pdl_begin();
   const uint32_t epoch = call_epoch(peers.base[me], L);
   const int nrows = __ldg(off + epr);
   const int chunks = H * 4 / 16;
-  for (int r = blockIdx.x; r < nrows; r += gridDim.x) {
+  copy_rows(nrows, chunks, [&](int r) -> RowCopy {
     const int s = __ldg(ret_src + r), row = __ldg(ret_row + r);
-    if (s >= 0 && s < world && row >= 0 && row < cap) {
-      uint4* dst = reinterpret_cast<uint4*>(peers.base[s] + L.y_back + (size_t)row * H * 4);
-      copy_row(dst, reinterpret_cast<const uint4*>(y + (size_t)r * H), chunks);
-    }
-  }
+    if (s < 0 || s >= world || row < 0 || row >= cap) return RowCopy{nullptr, nullptr};
+    return RowCopy{reinterpret_cast<const uint4*>(y + (size_t)r * H),
+                   reinterpret_cast<uint4*>(peers.base[s] + L.y_back + (size_t)row * H * 4)};
+  });
   int* done = reinterpret_cast<int*>(peers.base[me] + L.done) + 1;
   if (!last_cta(done)) return;
   if (threadIdx.x < world)
@@ -442,7 +481,7 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
   } else if (T > 0) {
     launch_dispatch(idx, T, k, E, offsets, row_token, inv, active, disp, st);
   }
-  launch_pdl(ep_send_kernel, dim3(R > 0 ? (R < sms * 4 ? R : sms * 4) : 1), dim3(kCopyThreads), 0, st,
+  launch_pdl(ep_send_kernel, dim3(R > 0 ? (R < sms ? R : sms) : 1), dim3(kXferThreads), 0, st,
              static_cast<const char*>(x), static_cast<const int32_t*>(row_token), static_cast<const int32_t*>(offsets),
              R, T, epr, world, c->rank, c->cap, row_bytes, c->peers, c->L);
   const size_t psmem = (size_t)(2 * world * epr + world + epr + 1) * sizeof(int);
@@ -460,7 +499,7 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
                           y, st, mid, lrow, loff + epr);  // encode only the rows that arrived
   if (s) return s;
   mark(4);
-  launch_pdl(ep_return_kernel, dim3(sms * 4), dim3(kCopyThreads), 0, st, static_cast<const float*>(y),
+  launch_pdl(ep_return_kernel, dim3(sms), dim3(kXferThreads), 0, st, static_cast<const float*>(y),
              static_cast<const int32_t*>(loff), epr, static_cast<const int32_t*>(ret_src),
              static_cast<const int32_t*>(ret_row), world, c->rank, c->cap, c->H, c->peers, c->L);
   launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, st, c->local, c->L, world);
