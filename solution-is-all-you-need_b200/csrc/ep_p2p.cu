@@ -326,6 +326,19 @@ ep_remap_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ vma
   }
 }
 
+// The return flags when the down projection stored its rows straight into
+// the sources' return buffers (RowScatter): after the down kernel (the
+// programmatic-launch wait makes its stores visible to this grid), one
+// system-scope fence orders them before each source's flag.
+__global__ void ep_flag_kernel(const __grid_constant__ Peers peers, Region L, int world, int me) {
+  pdl_begin();
+  const uint32_t epoch = call_epoch(peers.base[me], L);
+  if (threadIdx.x < world) {
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<uint32_t*>(peers.base[threadIdx.x] + L.flags_back) + me, epoch);
+  }
+}
+
 // Waits for the return flags, then advances the epoch word for the next
 // layer call (every rank advances its own in step: one per call).
 __global__ void ep_wait_kernel(char* __restrict__ local, Region L, int world) {
@@ -490,18 +503,31 @@ int ep_layer(EpContext* c, const void* x, int x_dtype, const void* router_w, int
   const char* recv = c->local + c->L.recv_x;
   mark(2);
   const cudaEvent_t mid = marks ? marks[3] : nullptr;
+  // the decode down kernel stores each row straight into its source's
+  // return buffer (no separate return copy)
+  RowScatter scatter{};
+  for (int r = 0; r < world; ++r) scatter.base[r] = reinterpret_cast<float*>(c->peers.base[r] + c->L.y_back);
+  scatter.src = ret_src;
+  scatter.row = ret_row;
+  scatter.nbase = world;
+  scatter.cap = c->cap;
+  bool scattered = false;
   int s;
   if (path == PHMOE_PATH_PREFILL)
     s = launch_ffn_prefill(recv, lrow, loff, lact, w13_q, w13_s, w2_q, w2_s, (int)capr, c->H, epr, 1, I, G, h, y, st,
                            mid);
   else
     s = launch_ffn_decode(recv, x_dtype, lrow, loff, lact, w13_q, w13_s, w2_q, w2_s, (int)capr, c->H, epr, 1, I, G, h,
-                          y, st, mid, lrow, loff + epr);  // encode only the rows that arrived
+                          y, st, mid, lrow, loff + epr,  // encode only the rows that arrived
+                          false, &scatter, &scattered);
   if (s) return s;
   mark(4);
-  launch_pdl(ep_return_kernel, dim3(sms), dim3(kXferThreads), 0, st, static_cast<const float*>(y),
-             static_cast<const int32_t*>(loff), epr, static_cast<const int32_t*>(ret_src),
-             static_cast<const int32_t*>(ret_row), world, c->rank, c->cap, c->H, c->peers, c->L);
+  if (scattered)
+    launch_pdl(ep_flag_kernel, dim3(1), dim3(32), 0, st, c->peers, c->L, world, c->rank);
+  else
+    launch_pdl(ep_return_kernel, dim3(sms), dim3(kXferThreads), 0, st, static_cast<const float*>(y),
+               static_cast<const int32_t*>(loff), epr, static_cast<const int32_t*>(ret_src),
+               static_cast<const int32_t*>(ret_row), world, c->rank, c->cap, c->H, c->peers, c->L);
   launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, st, c->local, c->L, world);
   if (T > 0)
     launch_combine(reinterpret_cast<const float*>(c->local + c->L.y_back), inv, wts, T, k, c->H, out, x_dtype, st);

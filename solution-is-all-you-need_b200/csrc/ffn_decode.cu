@@ -917,7 +917,7 @@ __global__ void __launch_bounds__(kDnThreads, 1)
 ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap h_map,
                     int s_vec, const int2* __restrict__ hc, int R, const int32_t* __restrict__ offsets,
                     const int32_t* __restrict__ active, const uint16_t* __restrict__ w2_s, int H, int I, int E,
-                    float* __restrict__ y) {
+                    float* __restrict__ y, const __grid_constant__ RowScatter scat) {
   // No wait here: the item table comes from the dispatch, which ran before
   // the gate/up kernel (see pdl_wait), and the weights and scales do not
   // change; the producers wait for the gate/up kernel only before they copy
@@ -1059,11 +1059,25 @@ ffn_down_tma_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_cons
     warp_arrive(smem_u32(&ctl->empty[s]), lane);
     if (cu.kc == nkc - 1) {
       const int n = meta.n[cu.slot], row0 = meta.row0[cu.slot];
+      float* dst[2];  // this lane's two output rows (token columns 2c, 2c + 1)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int rr = cu.pass * kTok + 2 * c + j;
+        dst[j] = nullptr;
+        if (rr < n) {
+          const int row = row0 + rr;
+          if (scat.src == nullptr) {
+            dst[j] = y + (size_t)row * H;
+          } else {
+            const int s = __ldg(scat.src + row), d = __ldg(scat.row + row);
+            if (s >= 0 && s < scat.nbase && d >= 0 && d < scat.cap) dst[j] = scat.base[s] + (size_t)d * H;
+          }
+        }
+      }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int hr = cu.tile * kDnRows + lr0 + (q >= 2 ? 8 : 0);
-        const int rr = cu.pass * kTok + 2 * c + (q & 1);
-        if (rr < n) y[(size_t)(row0 + rr) * H + hr] = acc[q];
+        if (dst[q & 1] != nullptr) dst[q & 1][hr] = acc[q];
       }
     }
     cursor_next(cu, tiles, nkc, meta);
@@ -1316,7 +1330,7 @@ int launch_gateup(const uint8_t* xq, const int2* xc, const int32_t* row_token, c
 template <int G>
 bool launch_down_tma(const uint8_t* hq, const int2* hc, long long R, const int32_t* offsets, const int32_t* active,
                      const uint8_t* w2_q, const uint16_t* w2_s, int H, int I, int E, float* y, int grid,
-                     cudaStream_t st) {
+                     cudaStream_t st, const RowScatter& sc) {
   if (I % kDnKc || H % kDnRows || R <= 0 || R > (1LL << 30)) return false;
   const bool five = DnCfg<G, 5>::smem(E) <= kMaxSmem;  // five stages where they fit, else four
   const size_t smem = five ? DnCfg<G, 5>::smem(E) : DnCfg<G, 4>::smem(E);
@@ -1351,12 +1365,12 @@ bool launch_down_tma(const uint8_t* hq, const int2* hc, long long R, const int32
     auto k = ffn_down_tma_kernel<G, 5>;
     set_smem(k, smem);
     launch_pdl(k, dim3(grid), dim3(kDnThreads), smem, st, wm, hm, s_vec, hc, (int)R, offsets, active, w2_s, H, I,
-               E, y);
+               E, y, sc);
   } else {
     auto k = ffn_down_tma_kernel<G, 4>;
     set_smem(k, smem);
     launch_pdl(k, dim3(grid), dim3(kDnThreads), smem, st, wm, hm, s_vec, hc, (int)R, offsets, active, w2_s, H, I,
-               E, y);
+               E, y, sc);
   }
   return true;
 }
@@ -1427,7 +1441,7 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       const uint16_t* w13_s, const uint8_t* w2_q, const uint16_t* w2_s, int T,
                       int H, int E, int top_k, int I, int G, float* h, float* y,
                       cudaStream_t st, cudaEvent_t mid_event, const int32_t* enc_index,
-                      const int32_t* enc_count, bool x_encoded) {
+                      const int32_t* enc_count, bool x_encoded, const RowScatter* scatter, bool* scattered) {
   const long long R = (long long)T * top_k;
   if (R == 0) return PHMOE_OK;
   if (G != 32 && G != 64) return PHMOE_ERR_UNSUPPORTED;
@@ -1444,8 +1458,11 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                         : launch_gateup<32>(xq, xc, row_token, offsets, active, w13_q, w13_s, H, I, E, hq, hc, grid, st);
   if (s) return s;
   if (mid_event) cudaEventRecord(mid_event, st);
-  const bool tma = G == 64 ? launch_down_tma<64>(hq, hc, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st)
-                           : launch_down_tma<32>(hq, hc, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
+  RowScatter sc{};
+  if (scatter != nullptr) sc = *scatter;
+  const bool tma = G == 64 ? launch_down_tma<64>(hq, hc, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st, sc)
+                           : launch_down_tma<32>(hq, hc, R, offsets, active, w2_q, w2_s, H, I, E, y, grid, st, sc);
+  if (scattered != nullptr) *scattered = tma && sc.src != nullptr;
   if (!tma) {
     if (G == 64) launch_down<64>(hq, hc, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);
     else launch_down<32>(hq, hc, offsets, active, w2_q, w2_s, H, I, E, y, grid, st);

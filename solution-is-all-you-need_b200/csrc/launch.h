@@ -48,7 +48,21 @@ int launch_ffn_decode(const void* x, int x_dtype, const int32_t* row_token,
                       int H, int E, int top_k, int I, int G, float* h, float* y,
                       cudaStream_t st, cudaEvent_t mid_event = nullptr,
                       const int32_t* enc_index = nullptr, const int32_t* enc_count = nullptr,
-                      bool x_encoded = false);
+                      bool x_encoded = false, const struct RowScatter* scatter = nullptr,
+                      bool* scattered = nullptr);
+// Where the decode down projection stores its output rows (expert
+// parallelism: straight into the source ranks' return buffers): row r of y
+// goes to base[src[r]] + row[r] * H instead of y + r * H; a row whose src is
+// outside [0, nbase) or whose row is outside [0, cap) is not stored.
+// launch_ffn_decode sets *scattered when its down kernel did this (the TMA
+// form); otherwise the rows are in y as usual.
+struct RowScatter {
+  float* base[8];
+  const int32_t* src;
+  const int32_t* row;
+  int nbase;
+  int cap;
+};
 // Where launch_ffn_decode keeps the fixed-point rows of x inside y (the
 // router may write them there first).
 uint8_t* ffn_decode_xq(float* y);
