@@ -151,21 +151,27 @@ __device__ __forceinline__ uint32_t call_epoch(const char* region, const Region&
   return *reinterpret_cast<const volatile uint32_t*>(region + L.epoch);
 }
 
+// System-scope acquire-release fence (the count hand-offs below need no
+// sequentially consistent fence; fence.sc.sys measured ~3-4 us per step of
+// the exchange's chain).
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 // True for the one CTA that finishes last; that CTA resets the counter for
 // the next layer. The CTA barrier orders every thread's stores before
 // thread 0's system-scope fence, which is cumulative: the CTA's stores (to
-// peers too) are visible system-wide before its count, and the last CTA's
-// fence after reading the count orders them all before its flag stores.
+// peers too) are visible system-wide before its count (release), and the
+// last CTA's fence after reading the count (acquire) orders them all before
+// the release stores of its flags.
 // (One fence per CTA instead of one per thread: a fence in every thread cost
 // ~2.4 us more per copy kernel of a 148 x 1024 grid.)
 __device__ bool last_cta(int* counter) {
   __shared__ bool last;
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    fence_acq_rel_sys();
     last = atomicAdd(counter, 1) == (int)(gridDim.x - 1);
     if (last) *counter = 0;
-    if (last) __threadfence_system();
+    if (last) fence_acq_rel_sys();
   }
   __syncthreads();
   return last;
@@ -179,6 +185,19 @@ ep_send_kernel(const char* __restrict__ x, const int32_t* __restrict__ row_token
   const uint32_t epoch = call_epoch(peers.base[me], L);
   const int chunks = row_bytes / 16;
   const int nvalid = R > 0 ? __ldg(offsets + epr * world) : 0;
+  if (blockIdx.x == 0) {
+    // counts and base row for each destination (they depend on the dispatch
+    // only): written first, so CTA 0's release before its count covers them
+    for (int d = 0; d < world; ++d) {
+      int32_t* cnt = reinterpret_cast<int32_t*>(peers.base[d] + L.counts_in) + (size_t)me * (epr + 1);
+      for (int l = threadIdx.x; l <= epr; l += blockDim.x) {
+        int32_t v = 0;
+        if (R > 0)
+          v = l < epr ? __ldg(offsets + d * epr + l + 1) - __ldg(offsets + d * epr + l) : __ldg(offsets + d * epr);
+        cnt[l] = v;
+      }
+    }
+  }
   copy_rows(nvalid, chunks, [&](int r) -> RowCopy {
     int d = 0;
     while (d + 1 < world && __ldg(offsets + (d + 1) * epr) <= r) ++d;
@@ -190,17 +209,7 @@ ep_send_kernel(const char* __restrict__ x, const int32_t* __restrict__ row_token
   });
   int* done = reinterpret_cast<int*>(peers.base[me] + L.done);
   if (!last_cta(done)) return;
-  // counts and base row for each destination, then its flag
-  for (int d = 0; d < world; ++d) {
-    int32_t* cnt = reinterpret_cast<int32_t*>(peers.base[d] + L.counts_in) + (size_t)me * (epr + 1);
-    for (int l = threadIdx.x; l <= epr; l += blockDim.x) {
-      int32_t v = 0;
-      if (R > 0) v = l < epr ? __ldg(offsets + d * epr + l + 1) - __ldg(offsets + d * epr + l) : __ldg(offsets + d * epr);
-      cnt[l] = v;
-    }
-  }
-  __threadfence_system();
-  __syncthreads();
+  // every CTA's rows (and CTA 0's counts) are ordered before these
   if (threadIdx.x < world)
     st_release_sys(reinterpret_cast<uint32_t*>(peers.base[threadIdx.x] + L.flags_in) + me, epoch);
 }
@@ -328,13 +337,13 @@ ep_remap_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ vma
 
 // The return flags when the down projection stored its rows straight into
 // the sources' return buffers (RowScatter): after the down kernel (the
-// programmatic-launch wait makes its stores visible to this grid), one
-// system-scope fence orders them before each source's flag.
+// programmatic-launch wait makes its stores visible to this grid), a
+// system-scope acquire-release fence orders them before each source's flag.
 __global__ void ep_flag_kernel(const __grid_constant__ Peers peers, Region L, int world, int me) {
   pdl_begin();
   const uint32_t epoch = call_epoch(peers.base[me], L);
   if (threadIdx.x < world) {
-    __threadfence_system();
+    fence_acq_rel_sys();
     st_release_sys(reinterpret_cast<uint32_t*>(peers.base[threadIdx.x] + L.flags_back) + me, epoch);
   }
 }
