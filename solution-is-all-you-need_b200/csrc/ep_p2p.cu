@@ -13,16 +13,19 @@
 //   router + dispatch over all E experts (rows come out expert-major, hence
 //     destination-major);
 //   ep_send_kernel   - row r goes to rank d = owner of its expert, slot
-//     i = r - offsets[d*Epr] of d's receive block for `me`; the last CTA to
-//     finish (after a system fence by every CTA) stores `me`'s per-expert
-//     counts for d and then d's arrival flag for `me` = epoch;
+//     i = r - offsets[d*Epr] of d's receive block for `me`; the first CTA
+//     also stores `me`'s per-expert counts for every d; the last CTA to
+//     count (each CTA releases its stores with one system fence) stores d's
+//     arrival flag for `me` = epoch;
 //   ep_prepare_kernel - waits (bounded) for every source's flag, then builds
 //     the local expert grouping of the arrived rows (per local expert: source
 //     by source, each source's rows in its own order) and, per local row, the
 //     source rank and its row in the source's dispatch order;
-//   grouped FFN (decode or prefill kernels) over the arrived rows;
-//   ep_return_kernel - each fp32 expert-output row goes back to its source's
-//     return buffer at that row; the last CTA raises the return flags;
+//   grouped FFN (decode or prefill kernels) over the arrived rows; the
+//     decode down kernel stores each fp32 output row straight into its
+//     source's return buffer at that row (RowScatter) and ep_flag_kernel
+//     then raises the return flags; after the prefill kernels,
+//     ep_return_kernel copies the rows back and its last CTA raises them;
 //   ep_wait_kernel   - waits (bounded) for every destination's return flag;
 //   combine over the returned rows in slot order.
 // Replicated placements (hot experts copied onto several ranks): every rank
